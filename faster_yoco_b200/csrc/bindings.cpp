@@ -1,0 +1,78 @@
+// Python bindings of the sm_100a extension (faster_yoco_b200._C).
+#include <torch/extension.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common/host.h"
+
+namespace fyb {
+
+void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
+          const c10::optional<at::Tensor>& R);
+std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps);
+std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const c10::optional<at::Tensor>& w,
+                                     const at::Tensor& rstd);
+std::vector<at::Tensor> subln_swiglu_fwd(const at::Tensor& o, const at::Tensor& g, double eps, int64_t D);
+std::vector<at::Tensor> subln_swiglu_bwd(const at::Tensor& dout, const at::Tensor& o, const at::Tensor& g,
+                                         const at::Tensor& rstd, int64_t D);
+at::Tensor swiglu_fwd(const at::Tensor& x, const at::Tensor& y);
+std::vector<at::Tensor> swiglu_bwd(const at::Tensor& x, const at::Tensor& y, const at::Tensor& g);
+at::Tensor rope_fwd(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t, bool conj);
+at::Tensor embedding_fwd(const at::Tensor& tok, const at::Tensor& w, double scale);
+at::Tensor embedding_bwd(const at::Tensor& tok, const at::Tensor& dy, int64_t V, double scale,
+                         const c10::optional<at::Tensor>& out);
+std::vector<at::Tensor> ce_fwd(const at::Tensor& logits, const at::Tensor& target, int64_t ignore);
+at::Tensor ce_bwd(const at::Tensor& logits, const at::Tensor& target, const at::Tensor& lse, const at::Tensor& grad,
+                  int64_t ignore, const c10::optional<at::Tensor>& out);
+void adam_step(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor& v, at::Tensor& p16,
+               const at::Tensor& hyper, const at::Tensor& factor, double b1, double b2, double eps, double wd,
+               bool adamw);
+at::Tensor sq_norm(const at::Tensor& x);
+
+// one status word per device, allocated once (zero = ok)
+int* status_ptr() {
+  static std::mutex mu;
+  static std::unordered_map<int, int*> ptrs;
+  int dev;
+  FYB_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = ptrs.find(dev);
+  if (it != ptrs.end()) return it->second;
+  int* p = nullptr;
+  FYB_CUDA(cudaMalloc(&p, 4 * sizeof(int)));
+  FYB_CUDA(cudaMemset(p, 0, 4 * sizeof(int)));
+  ptrs[dev] = p;
+  return p;
+}
+
+at::Tensor status_tensor() {
+  int dev;
+  FYB_CUDA(cudaGetDevice(&dev));
+  auto opts = at::TensorOptions().dtype(at::kInt).device(at::kCUDA, dev);
+  return at::from_blob(status_ptr(), {4}, opts);
+}
+
+}  // namespace fyb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "faster_yoco_b200 sm_100a kernels";
+  m.def("gemm", &fyb::gemm, "C = A @ B^T on tcgen05 (operands K-major or MN-major)", py::arg("A"), py::arg("B"),
+        py::arg("C"), py::arg("a_mn_major"), py::arg("b_mn_major"), py::arg("residual") = py::none());
+  m.def("rms_norm_fwd", &fyb::rms_norm_fwd);
+  m.def("rms_norm_bwd", &fyb::rms_norm_bwd);
+  m.def("subln_swiglu_fwd", &fyb::subln_swiglu_fwd);
+  m.def("subln_swiglu_bwd", &fyb::subln_swiglu_bwd);
+  m.def("swiglu_fwd", &fyb::swiglu_fwd);
+  m.def("swiglu_bwd", &fyb::swiglu_bwd);
+  m.def("rope_fwd", &fyb::rope_fwd);
+  m.def("embedding_fwd", &fyb::embedding_fwd);
+  m.def("embedding_bwd", &fyb::embedding_bwd, py::arg("tok"), py::arg("dy"), py::arg("V"), py::arg("scale"),
+        py::arg("out") = py::none());
+  m.def("ce_fwd", &fyb::ce_fwd);
+  m.def("ce_bwd", &fyb::ce_bwd, py::arg("logits"), py::arg("target"), py::arg("lse"), py::arg("grad"),
+        py::arg("ignore"), py::arg("out") = py::none());
+  m.def("adam_step", &fyb::adam_step);
+  m.def("sq_norm", &fyb::sq_norm);
+  m.def("status", &fyb::status_tensor, "device status word of the kernels with bounded waits");
+}

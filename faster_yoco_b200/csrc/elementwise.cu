@@ -1,0 +1,529 @@
+// Memory-bound kernels: SwiGLU, rotary embedding, scaled embedding gather / scatter-sum, cross-entropy over the
+// vocabulary, the sharded Adam step and the gradient sum of squares.
+//
+// References: SwiGLU kernel/swiglu.py:4-17 (silu of the first operand); rotary kernel/rotary.py:20-141
+// (interleaved pairs, fp32 math, conjugate rotation for the backward); fused CE tasks/fused_ce.py:23-59 (online
+// log-sum-exp over bf16 logits, bf16 gradient (softmax - onehot) * g, 0 for padding targets); fused Adam
+// tasks/fused_adam_cast.py:19-45 (apex AdamFunctor: fma for m and v, IEEE division and square root, host bias
+// corrections, bf16 copy of the new master); owner embedding gradient models/decoder/layer_graphs.py:68-105.
+#include <ATen/ATen.h>
+#include <c10/util/Optional.h>
+
+#include "common/host.h"
+#include "common/ptx.cuh"
+
+namespace fyb {
+namespace {
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = unpack_bf16(w[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
+  *reinterpret_cast<uint4*>(p) =
+      make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]), pack_bf16(f[6], f[7]));
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+
+// ------------------------------------------------------------------------------------------------------------------
+// SwiGLU on [M, N] views with row strides (N % 8 == 0)
+
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ y,
+                                  int64_t ldy, __nv_bfloat16* __restrict__ out, int64_t M, int N) {
+  const int per_row = N / 8;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= M * per_row) return;
+  const int64_t r = i / per_row;
+  const int c = static_cast<int>(i % per_row) * 8;
+  float a[8], b[8], o[8];
+  load8(x + r * ldx + c, a);
+  load8(y + r * ldy + c, b);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) o[k] = a[k] * b[k] * sigmoidf_(a[k]);
+  store8(out + r * N + c, o);
+}
+
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ y,
+                                  int64_t ldy, const __nv_bfloat16* __restrict__ g, __nv_bfloat16* __restrict__ dx,
+                                  __nv_bfloat16* __restrict__ dy, int64_t M, int N) {
+  const int per_row = N / 8;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= M * per_row) return;
+  const int64_t r = i / per_row;
+  const int c = static_cast<int>(i % per_row) * 8;
+  float a[8], b[8], gg[8], da[8], db[8];
+  load8(x + r * ldx + c, a);
+  load8(y + r * ldy + c, b);
+  load8(g + r * N + c, gg);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float s = sigmoidf_(a[k]);
+    da[k] = s * (1.0f + a[k] * (1.0f - s)) * gg[k] * b[k];
+    db[k] = a[k] * s * gg[k];
+  }
+  store8(dx + r * N + c, da);
+  store8(dy + r * N + c, db);
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// rotary embedding, interleaved pairs. x: [B, L, H, D] strided (last dim contiguous); out contiguous.
+
+__global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, int64_t sb, int64_t sl, int64_t sh,
+                            const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t,
+                            __nv_bfloat16* __restrict__ out, int B, int L, int H, int D, float sign) {
+  const int per = D / 8;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t total = static_cast<int64_t>(B) * L * H * per;
+  if (i >= total) return;
+  const int c8 = static_cast<int>(i % per) * 8;
+  int64_t rest = i / per;
+  const int h = static_cast<int>(rest % H);
+  rest /= H;
+  const int l = static_cast<int>(rest % L);
+  const int b = static_cast<int>(rest / L);
+  float f[8], o[8];
+  load8(x + b * sb + l * sl + h * sh + c8, f);
+  const __nv_bfloat16* cp = cos_t + static_cast<int64_t>(l) * (D / 2) + c8 / 2;
+  const __nv_bfloat16* spp = sin_t + static_cast<int64_t>(l) * (D / 2) + c8 / 2;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float cs = __bfloat162float(cp[k]);
+    const float sn = sign * __bfloat162float(spp[k]);
+    const float x0 = f[2 * k], x1 = f[2 * k + 1];
+    o[2 * k] = x0 * cs - x1 * sn;
+    o[2 * k + 1] = x0 * sn + x1 * cs;
+  }
+  store8(out + ((static_cast<int64_t>(b) * L + l) * H + h) * D + c8, o);
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// embedding: out[i] = bf16(w[tok[i]] * scale)
+
+__global__ void embed_fwd_kernel(const int64_t* __restrict__ tok, const __nv_bfloat16* __restrict__ w,
+                                 __nv_bfloat16* __restrict__ out, int64_t M, int N, float scale, int64_t V,
+                                 int* status) {
+  const int per = N / 8;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= M * per) return;
+  const int64_t r = i / per;
+  const int c = static_cast<int>(i % per) * 8;
+  int64_t t = tok[r];
+  if (t < 0 || t >= V) {
+    record_status(status, kBounds, 100);
+    t = 0;
+  }
+  float f[8];
+  load8(w + t * N + c, f);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) f[k] *= scale;
+  store8(out + r * N + c, f);
+}
+
+// Deterministic embedding gradient: block j handles the FIRST occurrence of token tok[j] and sums, in position
+// order, bf16(dy[i] * scale) over every position i with the same token (fp32 accumulation). Rows of tokens that do
+// not occur must be zero beforehand.
+__global__ void embed_bwd_kernel(const int64_t* __restrict__ tok, const __nv_bfloat16* __restrict__ dy,
+                                 __nv_bfloat16* __restrict__ dw, int M, int N, float scale, int64_t V) {
+  extern __shared__ int stok[];
+  for (int i = threadIdx.x; i < M; i += blockDim.x) stok[i] = static_cast<int>(tok[i]);
+  __syncthreads();
+  const int j = blockIdx.x;
+  const int t = stok[j];
+  if (t < 0 || t >= V) return;
+  for (int i = 0; i < j; ++i)
+    if (stok[i] == t) return;   // not the first occurrence
+  for (int c = threadIdx.x * 8; c < N; c += blockDim.x * 8) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int i = j; i < M; ++i) {
+      if (stok[i] != t) continue;
+      float f[8];
+      load8(dy + static_cast<int64_t>(i) * N + c, f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] += bf16_round(f[k] * scale);
+    }
+    store8(dw + static_cast<int64_t>(t) * N + c, acc);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// cross-entropy over bf16 logits [M, V] (row stride ld), one CTA per row
+
+constexpr int kCeThreads = 512;
+
+__device__ __forceinline__ void online_merge(float& m, float& s, float m2, float s2) {
+  const float mn = fmaxf(m, m2);
+  if (mn == -INFINITY) return;
+  s = s * __expf(m - mn) + s2 * __expf(m2 - mn);
+  m = mn;
+}
+
+__global__ void __launch_bounds__(kCeThreads) ce_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld,
+                                                            const int64_t* __restrict__ tgt, float* __restrict__ loss,
+                                                            float* __restrict__ lse_out, int V, int64_t ignore) {
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * ld;
+  float m = -INFINITY, s = 0.f;
+  const bool vec = (V % 8 == 0) && (ld % 8 == 0);
+  if (vec) {
+    for (int c = threadIdx.x * 8; c < V; c += kCeThreads * 8) {
+      float f[8];
+      load8(xr + c, f);
+      float mx = f[0];
+#pragma unroll
+      for (int k = 1; k < 8; ++k) mx = fmaxf(mx, f[k]);
+      const float mn = fmaxf(m, mx);
+      float acc = s * __expf(m - mn);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc += __expf(f[k] - mn);
+      s = acc;
+      m = mn;
+    }
+  } else {
+    for (int c = threadIdx.x; c < V; c += kCeThreads) {
+      const float f = __bfloat162float(xr[c]);
+      const float mn = fmaxf(m, f);
+      s = s * __expf(m - mn) + __expf(f - mn);
+      m = mn;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    online_merge(m, s, m2, s2);
+  }
+  __shared__ float sm[32], ss[32];
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    sm[w] = m;
+    ss[w] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M_ = sm[0], S_ = ss[0];
+    for (int i = 1; i < kCeThreads / 32; ++i) online_merge(M_, S_, sm[i], ss[i]);
+    const float lse = M_ + logf(S_);
+    const int64_t t = tgt[row];
+    lse_out[row] = lse;
+    loss[row] = (t == ignore || t < 0 || t >= V) ? 0.f : lse - __bfloat162float(xr[t]);
+  }
+}
+
+__global__ void __launch_bounds__(kCeThreads) ce_bwd_kernel(const __nv_bfloat16* x, int64_t ld,
+                                                            const int64_t* __restrict__ tgt,
+                                                            const float* __restrict__ lse_in,
+                                                            const float* __restrict__ grad, __nv_bfloat16* dx,
+                                                            int64_t ldd, int V, int64_t ignore) {
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * ld;
+  __nv_bfloat16* dr = dx + row * ldd;
+  const int64_t t = tgt[row];
+  const float lse = lse_in[row];
+  const float g = (t == ignore) ? 0.f : grad[0];
+  const bool vec = (V % 8 == 0) && (ld % 8 == 0) && (ldd % 8 == 0);
+  if (vec) {
+    for (int c = threadIdx.x * 8; c < V; c += kCeThreads * 8) {
+      float f[8];
+      load8(xr + c, f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float p = __expf(f[k] - lse);
+        if (c + k == t) p -= 1.0f;
+        f[k] = p * g;
+      }
+      store8(dr + c, f);
+    }
+  } else {
+    for (int c = threadIdx.x; c < V; c += kCeThreads) {
+      float p = __expf(__bfloat162float(xr[c]) - lse);
+      if (c == t) p -= 1.0f;
+      dr[c] = __float2bfloat16_rn(p * g);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// Adam (apex AdamFunctor expression), 4 elements per thread. hyper = [lr, bias_corr1, bias_corr2, step].
+
+__device__ __forceinline__ void adam_elem(float& p, float& m, float& v, float g, float lr, float b1, float b2,
+                                          float eps, float wd, float bc1, float bc2, bool adamw) {
+  if (!adamw) g = g + wd * p;
+  m = fmaf(b1, m, (1.0f - b1) * g);
+  v = fmaf(b2, v, ((1.0f - b2) * g) * g);
+  const float mh = __fdiv_rn(m, bc1);
+  const float vh = __fdiv_rn(v, bc2);
+  const float denom = __fadd_rn(__fsqrt_rn(vh), eps);
+  float upd = __fdiv_rn(mh, denom);
+  if (adamw) upd = upd + wd * p;
+  p = p - lr * upd;
+}
+
+__global__ void adam_kernel(float* __restrict__ p32, const __nv_bfloat16* __restrict__ g16, float* __restrict__ m,
+                            float* __restrict__ v, __nv_bfloat16* __restrict__ p16, const float* __restrict__ hyper,
+                            const float* __restrict__ factor, int64_t n, float b1, float b2, float eps, float wd,
+                            bool adamw) {
+  const float lr = hyper[0], bc1 = hyper[1], bc2 = hyper[2];
+  const float f = factor[0];
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 4;
+  for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < n; i += stride) {
+    if (i + 4 <= n) {
+      float4 P = *reinterpret_cast<float4*>(p32 + i);
+      float4 Mv = *reinterpret_cast<float4*>(m + i);
+      float4 Vv = *reinterpret_cast<float4*>(v + i);
+      const uint2 gu = *reinterpret_cast<const uint2*>(g16 + i);
+      const float2 g01 = unpack_bf16(gu.x), g23 = unpack_bf16(gu.y);
+      adam_elem(P.x, Mv.x, Vv.x, g01.x * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
+      adam_elem(P.y, Mv.y, Vv.y, g01.y * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
+      adam_elem(P.z, Mv.z, Vv.z, g23.x * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
+      adam_elem(P.w, Mv.w, Vv.w, g23.y * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
+      *reinterpret_cast<float4*>(p32 + i) = P;
+      *reinterpret_cast<float4*>(m + i) = Mv;
+      *reinterpret_cast<float4*>(v + i) = Vv;
+      *reinterpret_cast<uint2*>(p16 + i) = make_uint2(pack_bf16(P.x, P.y), pack_bf16(P.z, P.w));
+    } else {
+      for (int64_t j = i; j < n; ++j) {
+        float P = p32[j], Mv = m[j], Vv = v[j];
+        adam_elem(P, Mv, Vv, __bfloat162float(g16[j]) * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
+        p32[j] = P;
+        m[j] = Mv;
+        v[j] = Vv;
+        p16[j] = __float2bfloat16_rn(P);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// sum of squares of a bf16 vector: per-CTA fp32 partials, then one CTA sums them in a fixed order
+
+constexpr int kSqThreads = 512;
+
+__global__ void sq_partial_kernel(const __nv_bfloat16* __restrict__ x, int64_t n, float* __restrict__ part) {
+  float s = 0.f;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 8;
+  for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < n; i += stride) {
+    if (i + 8 <= n) {
+      float f[8];
+      load8(x + i, f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s += f[k] * f[k];
+    } else {
+      for (int64_t j = i; j < n; ++j) {
+        const float f = __bfloat162float(x[j]);
+        s += f * f;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < kSqThreads / 32; ++i) t += red[i];
+    part[blockIdx.x] = t;
+  }
+}
+
+__global__ void sq_final_kernel(const float* __restrict__ part, int P, float* __restrict__ out) {
+  __shared__ float red[1024];
+  float s = 0.f;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) s += part[i];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out[0] = red[0];
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------------------------
+// host entry points
+
+at::Tensor swiglu_fwd(const at::Tensor& x, const at::Tensor& y) {
+  FYB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16 && x.dim() == 2 &&
+                x.sizes() == y.sizes() && x.stride(1) == 1 && y.stride(1) == 1,
+            "swiglu_fwd: bf16 [M, N] views with contiguous rows expected");
+  const int64_t M = x.size(0), N = x.size(1);
+  FYB_CHECK(N % 8 == 0 && x.stride(0) % 8 == 0 && y.stride(0) % 8 == 0, "swiglu_fwd: alignment");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto out = at::empty({M, N}, x.options());
+  const int64_t n = M * (N / 8);
+  if (n > 0)
+    swiglu_fwd_kernel<<<(n + 255) / 256, 256, 0, cur_stream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
+        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), M, (int)N);
+  check_launch("swiglu_fwd");
+  return out;
+}
+
+std::vector<at::Tensor> swiglu_bwd(const at::Tensor& x, const at::Tensor& y, const at::Tensor& g) {
+  const int64_t M = x.size(0), N = x.size(1);
+  FYB_CHECK(g.is_contiguous() && g.size(0) == M && g.size(1) == N, "swiglu_bwd: grad");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto dx = at::empty({M, N}, x.options());
+  auto dy = at::empty({M, N}, x.options());
+  const int64_t n = M * (N / 8);
+  if (n > 0)
+    swiglu_bwd_kernel<<<(n + 255) / 256, 256, 0, cur_stream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()), M, (int)N);
+  check_launch("swiglu_bwd");
+  return {dx, dy};
+}
+
+at::Tensor rope_fwd(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t, bool conj) {
+  FYB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 4 && x.stride(3) == 1,
+            "rope: bf16 [B, L, H, D] with contiguous last dim expected");
+  const int B = (int)x.size(0), L = (int)x.size(1), H = (int)x.size(2), D = (int)x.size(3);
+  FYB_CHECK(D % 8 == 0 && x.stride(0) % 8 == 0 && x.stride(1) % 8 == 0 && x.stride(2) % 8 == 0,
+            "rope: alignment (strides multiple of 8 elements)");
+  FYB_CHECK(cos_t.is_contiguous() && sin_t.is_contiguous() && cos_t.size(0) >= L && cos_t.size(1) == D / 2 &&
+                cos_t.scalar_type() == at::kBFloat16 && sin_t.scalar_type() == at::kBFloat16,
+            "rope: cos/sin must be contiguous bf16 [L, D/2]");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto out = at::empty({B, L, H, D}, x.options());
+  const int64_t n = static_cast<int64_t>(B) * L * H * (D / 8);
+  if (n > 0)
+    rope_kernel<<<(n + 255) / 256, 256, 0, cur_stream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), x.stride(1), x.stride(2),
+        reinterpret_cast<const __nv_bfloat16*>(cos_t.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(sin_t.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), B, L, H, D, conj ? -1.f : 1.f);
+  check_launch("rope");
+  return out;
+}
+
+at::Tensor embedding_fwd(const at::Tensor& tok, const at::Tensor& w, double scale) {
+  FYB_CHECK(tok.is_cuda() && tok.scalar_type() == at::kLong && tok.dim() == 1 && tok.is_contiguous(),
+            "embedding_fwd: int64 token vector expected");
+  FYB_CHECK(w.scalar_type() == at::kBFloat16 && w.dim() == 2 && w.is_contiguous() && w.size(1) % 8 == 0,
+            "embedding_fwd: contiguous bf16 [V, N] with N % 8 == 0");
+  c10::cuda::CUDAGuard guard(w.device());
+  const int64_t M = tok.size(0), N = w.size(1);
+  auto out = at::empty({M, N}, w.options());
+  const int64_t n = M * (N / 8);
+  if (n > 0)
+    embed_fwd_kernel<<<(n + 255) / 256, 256, 0, cur_stream()>>>(
+        tok.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), M, (int)N, (float)scale, w.size(0), status_ptr());
+  check_launch("embedding_fwd");
+  return out;
+}
+
+at::Tensor embedding_bwd(const at::Tensor& tok, const at::Tensor& dy, int64_t V, double scale,
+                         const c10::optional<at::Tensor>& out_opt) {
+  FYB_CHECK(dy.is_contiguous() && dy.dim() == 2 && dy.size(1) % 8 == 0 && dy.size(0) == tok.size(0),
+            "embedding_bwd: dy");
+  const int64_t M = tok.size(0), N = dy.size(1);
+  FYB_CHECK(M <= 16384, "embedding_bwd: at most 16384 positions per call");
+  c10::cuda::CUDAGuard guard(dy.device());
+  at::Tensor dw;
+  if (out_opt.has_value() && out_opt->defined()) {
+    dw = *out_opt;
+    FYB_CHECK(dw.is_contiguous() && dw.size(0) == V && dw.size(1) == N && dw.scalar_type() == at::kBFloat16,
+              "embedding_bwd: out");
+  } else {
+    dw = at::empty({V, N}, dy.options());
+  }
+  FYB_CUDA(cudaMemsetAsync(dw.data_ptr(), 0, dw.numel() * 2, cur_stream()));
+  if (M > 0)
+    embed_bwd_kernel<<<M, 128, M * sizeof(int), cur_stream()>>>(
+        tok.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(dw.data_ptr()), (int)M, (int)N, (float)scale, V);
+  check_launch("embedding_bwd");
+  return dw;
+}
+
+std::vector<at::Tensor> ce_fwd(const at::Tensor& logits, const at::Tensor& target, int64_t ignore) {
+  FYB_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 && logits.stride(1) == 1,
+            "ce_fwd: bf16 [M, V] logits with contiguous rows expected");
+  FYB_CHECK(target.scalar_type() == at::kLong && target.is_contiguous() && target.numel() == logits.size(0),
+            "ce_fwd: int64 target [M]");
+  c10::cuda::CUDAGuard guard(logits.device());
+  const int64_t M = logits.size(0), V = logits.size(1);
+  auto loss = at::empty({M}, logits.options().dtype(at::kFloat));
+  auto lse = at::empty({M}, logits.options().dtype(at::kFloat));
+  if (M > 0)
+    ce_fwd_kernel<<<M, kCeThreads, 0, cur_stream()>>>(reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()),
+                                                      logits.stride(0), target.data_ptr<int64_t>(),
+                                                      loss.data_ptr<float>(), lse.data_ptr<float>(), (int)V, ignore);
+  check_launch("ce_fwd");
+  return {loss, lse};
+}
+
+at::Tensor ce_bwd(const at::Tensor& logits, const at::Tensor& target, const at::Tensor& lse, const at::Tensor& grad,
+                  int64_t ignore, const c10::optional<at::Tensor>& out_opt) {
+  c10::cuda::CUDAGuard guard(logits.device());
+  const int64_t M = logits.size(0), V = logits.size(1);
+  at::Tensor dx = (out_opt.has_value() && out_opt->defined()) ? *out_opt : at::empty_like(logits);
+  FYB_CHECK(dx.sizes() == logits.sizes() && dx.stride(1) == 1 && dx.scalar_type() == at::kBFloat16, "ce_bwd: out");
+  FYB_CHECK(grad.scalar_type() == at::kFloat && grad.numel() == 1, "ce_bwd: grad must be one fp32 value");
+  if (M > 0)
+    ce_bwd_kernel<<<M, kCeThreads, 0, cur_stream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), logits.stride(0), target.data_ptr<int64_t>(),
+        lse.data_ptr<float>(), grad.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dx.stride(0),
+        (int)V, ignore);
+  check_launch("ce_bwd");
+  return dx;
+}
+
+void adam_step(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor& v, at::Tensor& p16,
+               const at::Tensor& hyper, const at::Tensor& factor, double b1, double b2, double eps, double wd,
+               bool adamw) {
+  const int64_t n = p32.numel();
+  FYB_CHECK(p32.is_contiguous() && m.is_contiguous() && v.is_contiguous() && g16.is_contiguous() &&
+                p16.is_contiguous() && g16.numel() == n && m.numel() == n && v.numel() == n && p16.numel() == n,
+            "adam_step: contiguous tensors of equal size expected");
+  FYB_CHECK(p32.scalar_type() == at::kFloat && g16.scalar_type() == at::kBFloat16 &&
+                p16.scalar_type() == at::kBFloat16,
+            "adam_step: fp32 master / bf16 grad / bf16 param");
+  FYB_CHECK(reinterpret_cast<uintptr_t>(g16.data_ptr()) % 8 == 0 && reinterpret_cast<uintptr_t>(p16.data_ptr()) % 8 == 0,
+            "adam_step: bf16 buffers must be 8-byte aligned");
+  c10::cuda::CUDAGuard guard(p32.device());
+  if (n == 0) return;
+  const int blocks = static_cast<int>(std::min<int64_t>((n / 4 + 255) / 256 + 1, num_sms() * 8));
+  adam_kernel<<<blocks, 256, 0, cur_stream()>>>(
+      p32.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(g16.data_ptr()), m.data_ptr<float>(),
+      v.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(p16.data_ptr()), hyper.data_ptr<float>(),
+      factor.data_ptr<float>(), n, (float)b1, (float)b2, (float)eps, (float)wd, adamw);
+  check_launch("adam");
+}
+
+int sq_norm_ctas(int64_t n) { return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n + 4095) / 4096, 1024))); }
+
+void sq_norm_into(const at::Tensor& x, float* part, int P, float* out) {
+  sq_partial_kernel<<<P, kSqThreads, 0, cur_stream()>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                                                        x.numel(), part);
+  check_launch("sq_partial");
+  sq_final_kernel<<<1, 1024, 0, cur_stream()>>>(part, P, out);
+  check_launch("sq_final");
+}
+
+at::Tensor sq_norm(const at::Tensor& x) {
+  FYB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() &&
+                reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+            "sq_norm: contiguous 16-byte aligned bf16 expected");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int P = sq_norm_ctas(x.numel());
+  auto part = at::empty({P}, x.options().dtype(at::kFloat));
+  auto out = at::empty({1}, x.options().dtype(at::kFloat));
+  sq_norm_into(x, part.data_ptr<float>(), P, out.data_ptr<float>());
+  return out;
+}
+
+}  // namespace fyb

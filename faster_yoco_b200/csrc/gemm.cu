@@ -1,0 +1,365 @@
+// Persistent tcgen05 GEMM for sm_100a: C[M,N] = sum_k A(m,k) * B(n,k)  (+ R[M,N])
+//
+// The reference runs every projection through cuBLAS (F.linear: yoco/models/decoder/gate_retention.py:64-72,108,
+// feedforward_network.py:31, cross_attention.py:38,45, yoco.py:235,320). Here one kernel family covers the forward
+// (A, B both K-major), the input gradient (B MN-major) and the weight gradient (A, B both MN-major) without any
+// transposed copies: the MN-major operands are described to the tensor core by the UMMA descriptor's major bit.
+//
+// CTA = 6 warps, one CTA per SM, persistent over output tiles of 128 x BN:
+//   warp 0      : TMA producer (one lane) -- STAGES-deep ring of (A 128x64, B BNx64) bf16 tiles, 128B swizzle
+//   warp 1      : TMEM allocator + UMMA issuer (one lane): 4 x tcgen05.mma (M=128, N=BN, K=16) per stage
+//   warps 2..5  : epilogue -- tcgen05.ld of the fp32 accumulator, bf16 convert (+ residual), global store
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of tile i overlaps the MMAs of i+1.
+// No TMA multicast anywhere (this kernel also runs on operands that other ranks wrote).
+#include <ATen/ATen.h>
+#include <c10/util/Optional.h>
+
+#include "common/host.h"
+#include "common/ptx.cuh"
+
+namespace fyb {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+
+enum Epi : int { kEpiBf16 = 0, kEpiBf16Res = 1, kEpiF32 = 2 };
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int TOTAL = BAR_OFF + 256 + 1024;   // barriers + slack for 1024-byte alignment
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
+  constexpr int GROUP_M = 16;
+  const int per_group = GROUP_M * num_n;
+  const int g = t / per_group;
+  const int first_m = g * GROUP_M;
+  const int gm = min(num_m - first_m, GROUP_M);
+  const int r = t - g * per_group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* Cv,
+                        const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, int* status) {
+  using S = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_k = (K + BK - 1) / BK;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t IDESC = idesc_bf16(BM, BN, A_MN, B_MN);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, status, 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * S::STAGE_BYTES;
+          uint8_t* sb = sa + S::A_BYTES;
+          mbar_arrive_expect_tx(&full[s], S::STAGE_BYTES);
+          if (!A_MN) {
+            tma_load_2d(sa, &tmA, &full[s], kb * BK, mb * BM);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(sa + j * 8192, &tmA, &full[s], mb * BM + 64 * j, kb * BK);
+          }
+          if (!B_MN) {
+            tma_load_2d(sb, &tmB, &full[s], kb * BK, nb * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, &tmB, &full[s], nb * BN + 64 * j, kb * BK);
+          }
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // drain: every issued stage must have landed before the CTA may exit
+      for (int i = 0; i < STAGES; ++i) {
+        mbar_wait(&empty[s], ph ^ 1u, nullptr, status, 11);
+        if (++s == STAGES) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------------------------------- UMMA issuer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_ph ^ 1u, abort_flag, status, 2)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag, status, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + s * S::STAGE_BYTES);
+          const uint32_t b0 = a0 + S::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sw128_desc(a0 + k * 2048, 8192, 1024) : sw128_desc(a0 + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sw128_desc(b0 + k * 2048, 8192, 1024) : sw128_desc(b0 + k * 32, 16, 1024);
+            umma_bf16(d, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);   // frees the smem stage once these MMAs have read it
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);   // accumulator ready for the epilogue
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1u;
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------------------------------- epilogue
+    const int q = warp & 3;   // TMEM lane quadrant this warp may access
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, num_m, num_n, mb, nb);
+      if (!mbar_wait(&tfull[acc], acc_ph, abort_flag, status, 4)) break;
+      tc_fence_after();
+      const int row = mb * BM + q * 32 + lane;
+      const uint32_t tb = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tb + c * 32, r);
+        tmem_ld_wait();
+        const int col = nb * BN + c * 32;
+        if (row < M && col < N) {
+          if (EPI == kEpiF32) {
+            float* C = reinterpret_cast<float*>(Cv) + static_cast<int64_t>(row) * ldc + col;
+            if (col + 32 <= N && (ldc % 4) == 0) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(C + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                                __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col + j < N) C[j] = __uint_as_float(r[j]);
+            }
+          } else {
+            __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(Cv) + static_cast<int64_t>(row) * ldc + col;
+            uint32_t p[16];
+            if (EPI == kEpiBf16Res) {
+              const __nv_bfloat16* Rr = R + static_cast<int64_t>(row) * ldr + col;
+              if (col + 32 <= N && (ldr % 8) == 0) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const uint4 rv = *reinterpret_cast<const uint4*>(Rr + 8 * j);
+                  const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                  for (int h = 0; h < 4; ++h) {
+                    const float2 res = unpack_bf16(rw[h]);
+                    const int e = 8 * j + 2 * h;
+                    p[4 * j + h] = pack_bf16(bf16_round(__uint_as_float(r[e])) + res.x,
+                                             bf16_round(__uint_as_float(r[e + 1])) + res.y);
+                  }
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const int e = 2 * j;
+                  const float r0 = col + e < N ? __bfloat162float(Rr[e]) : 0.f;
+                  const float r1 = col + e + 1 < N ? __bfloat162float(Rr[e + 1]) : 0.f;
+                  p[j] = pack_bf16(bf16_round(__uint_as_float(r[e])) + r0, bf16_round(__uint_as_float(r[e + 1])) + r1);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) p[j] = pack_bf16(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+            }
+            if (col + 32 <= N && (ldc % 8) == 0) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                *reinterpret_cast<uint4*>(C + 8 * j) = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (col + j < N) {
+                  const uint16_t h = (j & 1) ? static_cast<uint16_t>(p[j >> 1] >> 16)
+                                             : static_cast<uint16_t>(p[j >> 1] & 0xffffu);
+                  C[j] = __ushort_as_bfloat16(h);
+                }
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_ph ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const __nv_bfloat16* R, int M, int N, int K,
+            int64_t ldc, int64_t ldr, cudaStream_t stream) {
+  using S = GemmSmem<BN, STAGES>;
+  auto kern = gemm_tcgen05_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    FYB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
+    attr_set = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int grid = std::min(tiles, num_sms());
+  kern<<<grid, kThreads, S::TOTAL, stream>>>(ta, tb, C, R, M, N, K, ldc, ldr, status_ptr());
+  check_launch("gemm_tcgen05");
+}
+
+template <int BN, int STAGES, int EPI>
+void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, void* C,
+                    const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, cudaStream_t st) {
+  if (!a_mn && !b_mn) launch<BN, STAGES, false, false, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
+  else if (!a_mn && b_mn) launch<BN, STAGES, false, true, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
+  else if (a_mn && b_mn) launch<BN, STAGES, true, true, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
+  else launch<BN, STAGES, true, false, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
+}
+
+// Pick the tile width whose last wave wastes the least of the machine (ties: the wider tile).
+int pick_bn(int M, int N) {
+  const int sms = num_sms();
+  const int tm = (M + BM - 1) / BM;
+  auto cost = [&](int bn) {
+    const long tiles = static_cast<long>(tm) * ((N + bn - 1) / bn);
+    const long waves = (tiles + sms - 1) / sms;
+    return waves * bn;   // time ~ waves x per-tile work (per-tile work ~ bn)
+  };
+  return cost(128) < cost(256) ? 128 : 256;
+}
+
+}  // namespace
+
+// C = A @ B^T in the operand conventions above. C: bf16 or fp32 [M, N] (any row stride); R: optional bf16 residual.
+void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
+          const c10::optional<at::Tensor>& R) {
+  FYB_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm: CUDA tensors expected");
+  FYB_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
+  FYB_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm: 2-D tensors expected");
+  FYB_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm: last dimension must be contiguous");
+  const int64_t M = a_mn ? A.size(1) : A.size(0);
+  const int64_t K = a_mn ? A.size(0) : A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0);
+  const int64_t Kb = b_mn ? B.size(0) : B.size(1);
+  FYB_CHECK(K == Kb, "gemm: inner dimensions differ");
+  FYB_CHECK(C.size(0) == M && C.size(1) == N, "gemm: output shape mismatch");
+  FYB_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm: dimension too large");
+  const bool f32 = C.scalar_type() == at::kFloat;
+  FYB_CHECK(f32 || C.scalar_type() == at::kBFloat16, "gemm: output must be bf16 or fp32");
+  const __nv_bfloat16* Rp = nullptr;
+  int64_t ldr = 0;
+  if (R.has_value() && R->defined()) {
+    FYB_CHECK(!f32, "gemm: residual needs a bf16 output");
+    FYB_CHECK(R->scalar_type() == at::kBFloat16 && R->dim() == 2 && R->size(0) == M && R->size(1) == N &&
+                  R->stride(1) == 1,
+              "gemm: residual must be bf16 [M, N] with contiguous rows");
+    Rp = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr());
+    ldr = R->stride(0);
+  }
+  if (M == 0 || N == 0) return;
+  c10::cuda::CUDAGuard guard(A.device());
+  cudaStream_t st = cur_stream();
+  if (K == 0) {
+    if (Rp != nullptr) C.copy_(*R);
+    else C.zero_();
+    return;
+  }
+  const int bn = pick_bn(static_cast<int>(M), static_cast<int>(N));
+  const CUtensorMap ta = a_mn ? make_tmap_2d(A.data_ptr(), K, M, A.stride(0), 64)
+                              : make_tmap_2d(A.data_ptr(), M, K, A.stride(0), BM);
+  const CUtensorMap tb = b_mn ? make_tmap_2d(B.data_ptr(), K, N, B.stride(0), 64)
+                              : make_tmap_2d(B.data_ptr(), N, K, B.stride(0), bn);
+  void* Cp = C.data_ptr();
+  const int epi = f32 ? kEpiF32 : (Rp != nullptr ? kEpiBf16Res : kEpiBf16);
+  const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
+  const int64_t ldc = C.stride(0);
+  if (bn == 256) {
+    if (epi == kEpiBf16) dispatch_major<256, 4, kEpiBf16>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
+    else if (epi == kEpiBf16Res) dispatch_major<256, 4, kEpiBf16Res>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
+    else dispatch_major<256, 4, kEpiF32>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
+  } else {
+    if (epi == kEpiBf16) dispatch_major<128, 6, kEpiBf16>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
+    else if (epi == kEpiBf16Res) dispatch_major<128, 6, kEpiBf16Res>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
+    else dispatch_major<128, 6, kEpiF32>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
+  }
+}
+
+}  // namespace fyb

@@ -1,0 +1,360 @@
+// RMSNorm forward / backward and the per-head weightless RMSNorm fused with the retention output gate.
+//
+// Numerics follow the reference's RMSNorm (yoco/models/decoder/rms_norm.py:34-46): statistics in fp32,
+// n = bf16(x * rsqrt(mean(x^2) + eps)), y = bf16(n * w) -- two bf16 roundings, as the upstream expression and its
+// Triton port (yoco/models/decoder/rms_triton.py:19-63) produce. The weight gradient is reduced deterministically
+// from per-CTA fp32 partials (no atomics), like the Triton kernel's per-program partials (:102).
+//
+// subln_swiglu: the retention output o [T, H*D] is normalised per head without weight (n16 = bf16(o * rstd_h)),
+// then gated: out = bf16(g * n16 * sigmoid(g)) (gate_retention.py:101-107 with kernel/swiglu.py:4-9).
+#include <ATen/ATen.h>
+#include <c10/util/Optional.h>
+
+#include "common/host.h"
+#include "common/ptx.cuh"
+
+namespace fyb {
+namespace {
+
+constexpr int kNormThreads = 256;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  const int nw = blockDim.x >> 5;
+  for (int i = 0; i < nw; ++i) t += red[i];
+  return t;
+}
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = unpack_bf16(w[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
+  *reinterpret_cast<uint4*>(p) =
+      make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]), pack_bf16(f[6], f[7]));
+}
+
+// one CTA per row; N % 8 == 0
+__global__ void rms_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                               __nv_bfloat16* __restrict__ y, float* __restrict__ rstd, int N, float eps) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * N;
+  float ss = 0.f;
+  for (int c = threadIdx.x * 8; c < N; c += blockDim.x * 8) {
+    float f[8];
+    load8(xr + c, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+  }
+  ss = block_sum(ss, red);
+  const float r = rsqrtf(ss / static_cast<float>(N) + eps);
+  if (threadIdx.x == 0) rstd[row] = r;
+  for (int c = threadIdx.x * 8; c < N; c += blockDim.x * 8) {
+    float f[8], o[8];
+    load8(xr + c, f);
+    if (w != nullptr) {
+      float wf[8];
+      load8(w + c, wf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = bf16_round(f[i] * r) * wf[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = f[i] * r;
+    }
+    store8(y + row * N + c, o);
+  }
+}
+
+// rows [row0, row1) per CTA; dx per row; dw partial (fp32) per CTA in part[blockIdx.x, N]
+__global__ void rms_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                               const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
+                               __nv_bfloat16* __restrict__ dx, float* __restrict__ part, int M, int N,
+                               int rows_per_cta) {
+  __shared__ float red[32];
+  extern __shared__ float dw_acc[];   // N floats (only when w != nullptr)
+  if (w != nullptr)
+    for (int c = threadIdx.x; c < N; c += blockDim.x) dw_acc[c] = 0.f;
+  __syncthreads();
+  const int row0 = blockIdx.x * rows_per_cta;
+  const int row1 = min(M, row0 + rows_per_cta);
+  for (int row = row0; row < row1; ++row) {
+    const int64_t off = static_cast<int64_t>(row) * N;
+    const float r = rstd[row];
+    float dot = 0.f;
+    for (int c = threadIdx.x * 8; c < N; c += blockDim.x * 8) {
+      float g[8], f[8];
+      load8(dy + off + c, g);
+      load8(x + off + c, f);
+      if (w != nullptr) {
+        float wf[8];
+        load8(w + c, wf);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float n = f[i] * r;
+          const float dn = bf16_round(g[i] * wf[i]);
+          dot += dn * n;
+          dw_acc[c + i] += g[i] * bf16_round(n);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dot += g[i] * f[i] * r;
+      }
+    }
+    dot = block_sum(dot, red) / static_cast<float>(N);
+    for (int c = threadIdx.x * 8; c < N; c += blockDim.x * 8) {
+      float g[8], f[8], o[8];
+      load8(dy + off + c, g);
+      load8(x + off + c, f);
+      if (w != nullptr) {
+        float wf[8];
+        load8(w + c, wf);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = r * (bf16_round(g[i] * wf[i]) - f[i] * r * dot);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = r * (g[i] - f[i] * r * dot);
+      }
+      store8(dx + off + c, o);
+    }
+  }
+  if (w != nullptr) {
+    __syncthreads();
+    for (int c = threadIdx.x; c < N; c += blockDim.x) part[static_cast<int64_t>(blockIdx.x) * N + c] = dw_acc[c];
+  }
+}
+
+// dw[c] = bf16(sum_p part[p, c]) in a fixed order
+__global__ void col_sum_kernel(const float* __restrict__ part, __nv_bfloat16* __restrict__ dw, int P, int N) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= N) return;
+  float s = 0.f;
+  for (int p = 0; p < P; ++p) s += part[static_cast<int64_t>(p) * N + c];
+  dw[c] = __float2bfloat16_rn(s);
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// subln (per-head RMSNorm, no weight) + swiglu(g, .)
+// D/8 threads per (token, head) row; each thread 8 contiguous elements.
+
+template <int D>
+__global__ void subln_swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ g,
+                                        int64_t ldg, __nv_bfloat16* __restrict__ out, float* __restrict__ rstd,
+                                        int T, int H, float eps) {
+  constexpr int TPR = D / 8;   // threads per head row
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t hrow = gid / TPR;   // (t, h) flattened
+  const int sub = static_cast<int>(gid % TPR);
+  const bool valid = hrow < static_cast<int64_t>(T) * H;
+  const int64_t t = valid ? hrow / H : 0;
+  const int h = valid ? static_cast<int>(hrow % H) : 0;
+  float f[8];
+  float ss = 0.f;
+  if (valid) {
+    load8(o + t * (static_cast<int64_t>(H) * D) + h * D + sub * 8, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+  }
+#pragma unroll
+  for (int s = TPR / 2; s > 0; s >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, s);
+  if (!valid) return;
+  const float r = rsqrtf(ss / static_cast<float>(D) + eps);
+  if (sub == 0) rstd[hrow] = r;
+  float gv[8], res[8];
+  load8(g + t * ldg + h * D + sub * 8, gv);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float n16 = bf16_round(f[i] * r);
+    res[i] = gv[i] * n16 / (1.0f + __expf(-gv[i]));
+  }
+  store8(out + t * (static_cast<int64_t>(H) * D) + h * D + sub * 8, res);
+}
+
+template <int D>
+__global__ void subln_swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ o,
+                                        const __nv_bfloat16* __restrict__ g, int64_t ldg,
+                                        const float* __restrict__ rstd, __nv_bfloat16* __restrict__ d_o,
+                                        __nv_bfloat16* __restrict__ dg, int T, int H) {
+  constexpr int TPR = D / 8;
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t hrow = gid / TPR;
+  const int sub = static_cast<int>(gid % TPR);
+  const bool valid = hrow < static_cast<int64_t>(T) * H;
+  const int64_t t = valid ? hrow / H : 0;
+  const int h = valid ? static_cast<int>(hrow % H) : 0;
+  const int64_t ooff = t * (static_cast<int64_t>(H) * D) + h * D + sub * 8;
+  const int64_t goff = t * ldg + h * D + sub * 8;
+  float f[8], gv[8], dv[8], dn[8];
+  float dot = 0.f;
+  float r = 0.f;
+  if (valid) {
+    r = rstd[hrow];
+    load8(o + ooff, f);
+    load8(g + goff, gv);
+    load8(dout + ooff, dv);
+    float dgo[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float n16 = bf16_round(f[i] * r);
+      const float s = 1.0f / (1.0f + __expf(-gv[i]));
+      dgo[i] = s * (1.0f + gv[i] * (1.0f - s)) * dv[i] * n16;
+      dn[i] = bf16_round(gv[i] * s * dv[i]);
+      dot += dn[i] * f[i] * r;
+    }
+    store8(dg + goff, dgo);
+  }
+#pragma unroll
+  for (int s = TPR / 2; s > 0; s >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, s);
+  if (!valid) return;
+  dot /= static_cast<float>(D);
+  float res[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) res[i] = r * (dn[i] - f[i] * r * dot);
+  store8(d_o + ooff, res);
+}
+
+}  // namespace
+
+std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps) {
+  FYB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.is_contiguous(),
+            "rms_norm_fwd: contiguous bf16 [M, N] expected");
+  const int64_t M = x.size(0), N = x.size(1);
+  FYB_CHECK(N % 8 == 0, "rms_norm_fwd: N must be a multiple of 8");
+  const __nv_bfloat16* wp = nullptr;
+  if (w.has_value() && w->defined()) {
+    FYB_CHECK(w->scalar_type() == at::kBFloat16 && w->numel() == N && w->is_contiguous(), "rms_norm_fwd: weight");
+    wp = reinterpret_cast<const __nv_bfloat16*>(w->data_ptr());
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  auto y = at::empty_like(x);
+  auto rstd = at::empty({M}, x.options().dtype(at::kFloat));
+  if (M > 0)
+    rms_fwd_kernel<<<M, N >= 2048 ? kNormThreads : 128, 0, cur_stream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), wp, reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
+        rstd.data_ptr<float>(), static_cast<int>(N), static_cast<float>(eps));
+  check_launch("rms_fwd");
+  return {y, rstd};
+}
+
+// Gradient of RMSNorm. The weight gradient's per-CTA partials live in `part` (P x N fp32); pass an empty tensor to
+// have it allocated here.
+std::vector<at::Tensor> rms_norm_bwd_impl(const at::Tensor& dy, const at::Tensor& x, const c10::optional<at::Tensor>& w,
+                                          const at::Tensor& rstd, float* part, int P) {
+  const int64_t M = x.size(0), N = x.size(1);
+  const bool has_w = w.has_value() && w->defined();
+  auto dx = at::empty_like(x);
+  at::Tensor dw;
+  if (has_w) dw = at::empty({N}, x.options());
+  if (M == 0) {
+    if (has_w) dw.zero_();
+    return {dx, has_w ? dw : at::Tensor()};
+  }
+  const int rows_per = static_cast<int>((M + P - 1) / P);
+  const int grid = static_cast<int>((M + rows_per - 1) / rows_per);
+  const size_t shm = has_w ? N * sizeof(float) : 0;
+  auto kern = rms_bwd_kernel;
+  if (shm > 48 * 1024) FYB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm));
+  kern<<<grid, kNormThreads, shm, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+      has_w ? reinterpret_cast<const __nv_bfloat16*>(w->data_ptr()) : nullptr, rstd.data_ptr<float>(),
+      reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), part, static_cast<int>(M), static_cast<int>(N), rows_per);
+  check_launch("rms_bwd");
+  if (has_w) {
+    col_sum_kernel<<<(N + 255) / 256, 256, 0, cur_stream()>>>(part, reinterpret_cast<__nv_bfloat16*>(dw.data_ptr()),
+                                                             grid, static_cast<int>(N));
+    check_launch("rms_bwd_colsum");
+  }
+  return {dx, has_w ? dw : at::Tensor()};
+}
+
+int rms_bwd_ctas(int64_t M) { return static_cast<int>(std::min<int64_t>(M, 2 * num_sms())); }
+
+std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const c10::optional<at::Tensor>& w,
+                                     const at::Tensor& rstd) {
+  FYB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.is_contiguous() &&
+                dy.is_contiguous() && dy.sizes() == x.sizes() && dy.scalar_type() == at::kBFloat16,
+            "rms_norm_bwd: contiguous bf16 [M, N] expected");
+  FYB_CHECK(x.size(1) % 8 == 0, "rms_norm_bwd: N must be a multiple of 8");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int P = std::max(rms_bwd_ctas(x.size(0)), 1);
+  const bool has_w = w.has_value() && w->defined();
+  at::Tensor part;
+  if (has_w) part = at::empty({P, x.size(1)}, x.options().dtype(at::kFloat));
+  return rms_norm_bwd_impl(dy, x, w, rstd, has_w ? part.data_ptr<float>() : nullptr, P);
+}
+
+std::vector<at::Tensor> subln_swiglu_fwd(const at::Tensor& o, const at::Tensor& g, double eps, int64_t D) {
+  FYB_CHECK(o.is_cuda() && o.scalar_type() == at::kBFloat16 && o.dim() == 2 && o.is_contiguous(),
+            "subln_swiglu_fwd: o must be contiguous bf16 [T, H*D]");
+  FYB_CHECK(g.scalar_type() == at::kBFloat16 && g.dim() == 2 && g.stride(1) == 1 && g.sizes() == o.sizes() &&
+                g.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(g.data_ptr()) % 16 == 0,
+            "subln_swiglu_fwd: g must be bf16 [T, H*D] with 16-byte aligned rows");
+  const int64_t T = o.size(0), HD = o.size(1);
+  FYB_CHECK(D == 64 || D == 128, "subln_swiglu: head_dim 64 or 128");
+  const int H = static_cast<int>(HD / D);
+  c10::cuda::CUDAGuard guard(o.device());
+  auto out = at::empty_like(o);
+  auto rstd = at::empty({T, H}, o.options().dtype(at::kFloat));
+  const int64_t threads = T * H * (D / 8);
+  const int blocks = static_cast<int>((threads + 255) / 256);
+  if (T > 0) {
+    if (D == 128)
+      subln_swiglu_fwd_kernel<128><<<blocks, 256, 0, cur_stream()>>>(
+          reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()),
+          g.stride(0), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rstd.data_ptr<float>(), (int)T, H, (float)eps);
+    else
+      subln_swiglu_fwd_kernel<64><<<blocks, 256, 0, cur_stream()>>>(
+          reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()),
+          g.stride(0), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rstd.data_ptr<float>(), (int)T, H, (float)eps);
+  }
+  check_launch("subln_swiglu_fwd");
+  return {out, rstd};
+}
+
+std::vector<at::Tensor> subln_swiglu_bwd(const at::Tensor& dout, const at::Tensor& o, const at::Tensor& g,
+                                         const at::Tensor& rstd, int64_t D) {
+  FYB_CHECK(dout.is_contiguous() && dout.sizes() == o.sizes(), "subln_swiglu_bwd: dout");
+  const int64_t T = o.size(0), HD = o.size(1);
+  const int H = static_cast<int>(HD / D);
+  c10::cuda::CUDAGuard guard(o.device());
+  auto d_o = at::empty_like(o);
+  auto dg = at::empty({T, HD}, o.options());
+  const int64_t threads = T * H * (D / 8);
+  const int blocks = static_cast<int>((threads + 255) / 256);
+  if (T > 0) {
+    if (D == 128)
+      subln_swiglu_bwd_kernel<128><<<blocks, 256, 0, cur_stream()>>>(
+          reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+          reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()),
+          g.stride(0), rstd.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(d_o.data_ptr()),
+          reinterpret_cast<__nv_bfloat16*>(dg.data_ptr()), (int)T, H);
+    else
+      subln_swiglu_bwd_kernel<64><<<blocks, 256, 0, cur_stream()>>>(
+          reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+          reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()),
+          g.stride(0), rstd.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(d_o.data_ptr()),
+          reinterpret_cast<__nv_bfloat16*>(dg.data_ptr()), (int)T, H);
+  }
+  check_launch("subln_swiglu_bwd");
+  return {d_o, dg};
+}
+
+}  // namespace fyb

@@ -1,0 +1,249 @@
+"""Building blocks of the YOCO decoder: RMSNorm, the three token mixers and the SwiGLU FFN.
+
+Layout decisions (B200-first, not the reference's): the projections that read the same input are ONE parameter,
+physically contiguous, so each is one GEMM with no per-step ``torch.cat`` (the reference concatenates the q/k/v/g
+weights every forward under YOCO_FUSE_QKVG, yoco/models/decoder/gate_retention.py:61-66):
+
+* gated retention: ``qkvg_proj`` = rows [q | k | v | g | gt | zero pad to a multiple of 8]
+* sliding-window attention: ``qkv_proj`` = [q | k | v]
+* FFN: ``fc1_gate`` = [fc1 | gate]
+* cross-decoder shared KV: ``kv_proj`` = [k | v]
+
+State dicts are written and read with the reference's per-projection names (``mixer.q_proj.weight`` ...) by the
+hooks in :mod:`faster_yoco_b200.models.yoco`.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from .. import ops
+from . import init as I
+
+
+def _round8(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
+class RMSNorm(nn.Module):
+    """x * rsqrt(mean(x^2) + eps) in fp32, cast back, times weight (yoco/models/decoder/rms_norm.py:23-49)."""
+
+    def __init__(self, dim: int, eps: float = 1e-6, elementwise_affine: bool = True):
+        super().__init__()
+        self.dim, self.eps, self.elementwise_affine = dim, eps, elementwise_affine
+        if elementwise_affine:
+            self.weight = nn.Parameter(torch.ones(dim))
+        else:
+            self.register_parameter("weight", None)
+
+    def forward(self, x):
+        return ops.rms_norm(x, self.weight, self.eps)
+
+    def extra_repr(self):
+        return f"dim={self.dim}, eps={self.eps}, elementwise_affine={self.elementwise_affine}"
+
+
+class MergedLinear(nn.Module):
+    """One weight [sum(parts) (+pad), in] whose row blocks are the logical projections ``names``."""
+
+    def __init__(self, in_features: int, parts, names, inits, pad_to8: bool = False):
+        super().__init__()
+        self.in_features = in_features
+        self.parts = list(parts)
+        self.names = list(names)
+        rows = sum(self.parts)
+        self.rows = _round8(rows) if pad_to8 else rows
+        self.weight = nn.Parameter(torch.empty(self.rows, in_features))
+        self._inits = list(inits)
+        self.reset_parameters()
+
+    def reset_parameters(self, init_override=None):
+        with torch.no_grad():
+            self.weight.zero_()
+            off = 0
+            for n, f in zip(self.parts, self._inits):
+                (init_override or f)(self.weight[off:off + n])
+                off += n
+
+    def offsets(self):
+        off, out = 0, []
+        for n in self.parts:
+            out.append((off, n))
+            off += n
+        return out
+
+    def forward(self, x, residual=None):
+        return ops.linear(x, self.weight, residual)
+
+
+class Linear(nn.Module):
+    def __init__(self, in_features: int, out_features: int, init=I.init_method):
+        super().__init__()
+        self.in_features, self.out_features = in_features, out_features
+        self.weight = nn.Parameter(torch.empty(out_features, in_features))
+        self._init = init
+        self.reset_parameters()
+
+    def reset_parameters(self, init_override=None):
+        with torch.no_grad():
+            (init_override or self._init)(self.weight)
+
+    def forward(self, x, residual=None):
+        return ops.linear(x, self.weight, residual)
+
+
+class FeedForwardNetwork(nn.Module):
+    """fc2(swiglu(fc1 x, gate x)) with silu on fc1 (yoco/models/decoder/feedforward_network.py:15-33)."""
+
+    def __init__(self, embed_dim: int, ffn_dim: int):
+        super().__init__()
+        self.embed_dim, self.ffn_dim = embed_dim, ffn_dim
+        self.fc1_gate = MergedLinear(embed_dim, [ffn_dim, ffn_dim], ["fc1", "gate"], [I.init_method, I.init_method])
+        self.fc2 = Linear(ffn_dim, embed_dim, I.init_method)
+
+    def forward(self, x, residual=None):
+        h = self.fc1_gate(x)
+        f = self.ffn_dim
+        a = ops.swiglu(h[..., :f], h[..., f:])
+        return self.fc2(a, residual)
+
+
+class GateRetention(nn.Module):
+    """Gated retention mixer (yoco/models/decoder/gate_retention.py:27-109).
+
+    q/k/v/g: d -> d, gt: d -> n_heads; RoPE (interleaved) on q and k; gt = logsigmoid(gt) / 16; keys scaled by
+    head_dim^-0.5 inside the retention op; weightless per-head RMSNorm (subln) of the output, then swiglu(g, o), then
+    out_proj."""
+
+    def __init__(self, args):
+        super().__init__()
+        self.args = args
+        self.embed_dim = args.dim
+        self.num_heads = args.n_self_heads // args.model_parallel_size
+        self.head_dim = args.dim // args.n_self_heads
+        d = args.dim
+        self.qkvg_proj = MergedLinear(d, [d, d, d, d, args.n_self_heads], ["q_proj", "k_proj", "v_proj", "g_proj",
+                                                                           "gt_proj"],
+                                      [I.qkvg_init_method] * 5, pad_to8=True)
+        self.out_proj = Linear(d, d, I.out_init_method)
+        self.subln_eps = args.norm_eps
+        self.gate_logit_normalizer = args.gate_logit_normalizer
+
+    def project(self, x):
+        B, L, _ = x.shape
+        d, H, D = self.embed_dim, self.num_heads, self.head_dim
+        y = self.qkvg_proj(x)
+        q = y[..., 0 * d:1 * d].view(B, L, H, D)
+        k = y[..., 1 * d:2 * d].view(B, L, H, D)
+        v = y[..., 2 * d:3 * d].view(B, L, H, D)
+        g = y[..., 3 * d:4 * d]
+        gt = y[..., 4 * d:4 * d + H]
+        return q, k, v, g, gt
+
+    def forward(self, x, rel_pos, incremental_state=None, is_prefilling=False, residual=None):
+        B, L, _ = x.shape
+        H, D = self.num_heads, self.head_dim
+        q, k, v, g, gt = self.project(x)
+        cos, sin = rel_pos
+        q = ops.rope(q, cos, sin)
+        k = ops.rope(k, cos, sin)
+        gt = ops.gate_logsigmoid(gt, self.gate_logit_normalizer)            # [B, L, H]
+        if incremental_state is not None and not is_prefilling:
+            o = self._decode(q, k, v, gt, incremental_state)
+        elif incremental_state is not None:
+            o = self._prefill(q, k, v, gt, incremental_state)
+        else:
+            o = ops.retention(q, k, v, gt, chunk_size=self.args.chunk_size)      # [B, L, H, D]
+        o = ops.subln_swiglu(o.reshape(B * L, H * D), g.reshape(B * L, H * D), self.subln_eps, D)
+        o = o.view(B, L, H * D)
+        return self.out_proj(o, residual)
+
+    # inference paths (yoco/models/decoder/gate_retention.py:83-97); PyTorch expressions of the reference
+    def _decode(self, q, k, v, gt, st):
+        qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+        o, st["last_hidden_state"] = ops.ref.recurrent_gate_retention(qh, kh, vh, gt.transpose(1, 2),
+                                                                       st.get("last_hidden_state"))
+        return o.transpose(1, 2)
+
+    def _prefill(self, q, k, v, gt, st):
+        qh, kh, vh, gh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), gt.transpose(1, 2)
+        index_mask = st.get("index_mask")
+        last = st.get("last_hidden_state")
+        st["last_hidden_state"] = ops.ref.retention_prefill_state(kh, vh, gh, index_mask, last)
+        L = qh.shape[2]
+        cs = self.args.chunk_size
+        if L % cs == 0:
+            o = ops.ref.chunk_gate_retention(qh, kh, vh, gh, chunk_size=cs, last_hidden_state=last)
+        else:
+            o = ops.ref.parallel_gate_retention(qh, kh, vh, gh)
+            if last is not None:
+                G = gh.float().cumsum(-1)
+                o = o + (qh * G[..., None].exp().to(qh.dtype)) @ last
+        return o.transpose(1, 2)
+
+
+class SlidingWindowAttention(nn.Module):
+    """Causal attention over the last ``window`` keys (yoco/models/decoder/sliding_window_attention.py:15-69)."""
+
+    def __init__(self, args):
+        super().__init__()
+        self.args = args
+        self.embed_dim = args.dim
+        self.num_heads = args.n_self_heads // args.model_parallel_size
+        self.window_size = args.sliding_window
+        self.head_dim = args.dim // args.n_self_heads
+        d = args.dim
+        self.qkv_proj = MergedLinear(d, [d, d, d], ["q_proj", "k_proj", "v_proj"], [I.init_method] * 3)
+        self.out_proj = Linear(d, d, I.init_method)
+
+    def forward(self, x, rel_pos, start_pos=0, incremental_state=None, residual=None):
+        B, L, _ = x.shape
+        d, H, D = self.embed_dim, self.num_heads, self.head_dim
+        y = self.qkv_proj(x)
+        q = ops.rope(y[..., :d].view(B, L, H, D), *rel_pos)
+        k = ops.rope(y[..., d:2 * d].view(B, L, H, D), *rel_pos)
+        v = y[..., 2 * d:].view(B, L, H, D)
+        if incremental_state is not None:
+            st = incremental_state
+            w = self.window_size
+            if "prev_key" not in st:
+                st["prev_key"] = torch.empty(max(self.args.max_batch_size, B), w, H, D, device=x.device, dtype=x.dtype)
+                st["prev_value"] = torch.empty_like(st["prev_key"])
+                st["filled"] = 0
+            filled = st["filled"]
+            key = torch.cat([st["prev_key"][:B, :filled], k], dim=1)
+            value = torch.cat([st["prev_value"][:B, :filled], v], dim=1)
+            keep = min(w, key.shape[1])
+            st["prev_key"][:B, :keep] = key[:, -keep:]
+            st["prev_value"][:B, :keep] = value[:, -keep:]
+            st["filled"] = keep
+            o = ops.ref.attention(q, key, value, causal=True, window=w, q_offset=key.shape[1] - L)
+        else:
+            o = ops.attention(q, k, v, causal=True, window=self.window_size)
+        return self.out_proj(o.reshape(B, L, H * D), residual)
+
+
+class CrossAttention(nn.Module):
+    """q_proj + RoPE, causal GQA attention on the shared K/V, out_proj (yoco/models/decoder/cross_attention.py)."""
+
+    def __init__(self, args):
+        super().__init__()
+        self.args = args
+        self.embed_dim = args.dim
+        self.num_heads = args.n_attn_heads // args.model_parallel_size
+        self.num_kv_heads = args.n_attn_kv_heads // args.model_parallel_size
+        self.head_dim = args.dim // args.n_attn_heads
+        self.q_proj = Linear(args.dim, args.dim, I.init_method)
+        self.out_proj = Linear(args.dim, args.dim, I.init_method)
+
+    def forward(self, x, key, value, rel_pos, residual=None, q_offset: Optional[int] = None):
+        B, L, _ = x.shape
+        q = ops.rope(self.q_proj(x).view(B, L, self.num_heads, self.head_dim), *rel_pos)
+        if key.shape[1] != L:
+            off = key.shape[1] - L if q_offset is None else q_offset
+            o = ops.ref.attention(q, key, value, causal=True, q_offset=off)
+        else:
+            o = ops.attention(q, key, value, causal=True)
+        return self.out_proj(o.reshape(B, L, self.num_heads * self.head_dim), residual)

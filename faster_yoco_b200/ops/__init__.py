@@ -1,0 +1,379 @@
+"""Public op API of the framework.
+
+Every op has two implementations behind one signature:
+
+* ``native`` (default on CUDA tensors): the sm_100a kernels of ``faster_yoco_b200/csrc`` through the in-tree
+  extension. A missing extension raises; there is no silent fallback on a GPU.
+* ``torch``: the reference expressions of :mod:`faster_yoco_b200.ops.reference` run by PyTorch (cuBLAS GEMMs,
+  flash-attn / SDPA attention). This is the in-repo baseline that the native path is compared with, and the path
+  every op takes on CPU tensors.
+
+The backend is a process-wide setting (``set_backend``), not a per-call dispatch.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import reference as ref
+from . import _native
+
+_BACKEND = "native"
+
+
+def set_backend(name: str):
+    global _BACKEND
+    if name not in ("native", "torch"):
+        raise ValueError(name)
+    _BACKEND = name
+
+
+def get_backend() -> str:
+    return _BACKEND
+
+
+def native_on(t: torch.Tensor) -> bool:
+    return t.is_cuda and _BACKEND == "native"
+
+
+def _C():
+    return _native.lib()
+
+
+def _grad_slot(p):
+    """(slot, accumulate) when p lives in a flat ZeRO buffer that takes gradients directly, else (None, False)."""
+    fp = getattr(p, "_fyb_flat", None)
+    if fp is None or not fp.direct_grads:
+        return None, False
+    return fp.claim_grad(p)
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# GEMM: y = x @ w.T (+ residual)
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn_major: bool = False, b_mn_major: bool = False,
+         out: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
+         out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """C[M,N] = sum_k A(m,k) B(n,k) on the tcgen05 GEMM.
+
+    A is stored [M,K] (K-major) or [K,M] (``a_mn_major``); B is stored [N,K] or [K,N] (``b_mn_major``)."""
+    M = a.shape[1] if a_mn_major else a.shape[0]
+    N = b.shape[1] if b_mn_major else b.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=out_dtype or a.dtype, device=a.device)
+    _C().gemm(a, b, out, a_mn_major, b_mn_major, residual)
+    return out
+
+
+class _NativeLinear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, residual):
+        shp = x.shape
+        x2 = x.reshape(-1, shp[-1])
+        r2 = residual.reshape(-1, w.shape[0]) if residual is not None else None
+        y = gemm(x2, w, residual=r2)
+        ctx.save_for_backward(x2, w)
+        ctx.shp = shp
+        ctx.has_res = residual is not None
+        return y.view(*shp[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w = ctx.saved_tensors
+        dy2 = dy.reshape(-1, w.shape[0])
+        if not dy2.is_contiguous():
+            dy2 = dy2.contiguous()
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm(dy2, w, b_mn_major=True).view(ctx.shp)
+        if ctx.needs_input_grad[1]:
+            slot, acc = _grad_slot(w)
+            if slot is not None:
+                # the weight gradient lands in the flat gradient buffer; autograd sees no gradient for w
+                gemm(dy2, x2, a_mn_major=True, b_mn_major=True, out=slot, residual=slot if acc else None)
+            else:
+                dw = gemm(dy2, x2, a_mn_major=True, b_mn_major=True)
+        return dx, dw, (dy if ctx.has_res else None)
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if native_on(x):
+        return _NativeLinear.apply(x, w, residual)
+    y = F.linear(x, w)
+    return y + residual if residual is not None else y
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# RMSNorm
+
+
+class _NativeRMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        shp = x.shape
+        x2 = x.reshape(-1, shp[-1])
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        y, rstd = _C().rms_norm_fwd(x2, w, float(eps))
+        ctx.save_for_backward(x2, w, rstd)
+        ctx.shp = shp
+        return y.view(shp)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w, rstd = ctx.saved_tensors
+        dy2 = dy.reshape(x2.shape)
+        if not dy2.is_contiguous():
+            dy2 = dy2.contiguous()
+        dx, dw = _C().rms_norm_bwd(dy2, x2, w, rstd)
+        if w is not None:
+            slot, acc = _grad_slot(w)
+            if slot is not None:
+                slot.add_(dw) if acc else slot.copy_(dw)
+                dw = None
+        return dx.view(ctx.shp), (dw if w is not None else None), None
+
+
+def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float) -> torch.Tensor:
+    if native_on(x):
+        return _NativeRMSNorm.apply(x, weight, eps)
+    return ref.rms_norm(x, weight, eps)
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# SwiGLU
+
+
+class _NativeSwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, y):
+        out = _C().swiglu_fwd(x, y)
+        ctx.save_for_backward(x, y)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        x, y = ctx.saved_tensors
+        dx, dy = _C().swiglu_bwd(x, y, dout.contiguous())
+        return dx, dy
+
+
+def swiglu(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """x * y * sigmoid(x) (silu on the FIRST argument, as the reference's kernel/swiglu.py)."""
+    if native_on(x):
+        shp = x.shape
+        return _NativeSwiGLU.apply(x.reshape(-1, shp[-1]), y.reshape(-1, shp[-1])).view(shp)
+    return ref.swiglu(x, y)
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# rotary embedding (interleaved)
+
+
+class _NativeRope(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, cos, sin):
+        ctx.save_for_backward(cos, sin)
+        return _C().rope_fwd(x, cos, sin, False)
+
+    @staticmethod
+    def backward(ctx, dy):
+        cos, sin = ctx.saved_tensors
+        return _C().rope_fwd(dy, cos, sin, True), None, None
+
+
+def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """x: [B, L, H, D] (any strides with a contiguous last dim); returns a contiguous [B, L, H, D]."""
+    if native_on(x):
+        return _NativeRope.apply(x, cos, sin)
+    return ref.apply_rope(x, cos, sin)
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# per-head weightless RMSNorm (subln) fused with the output gate swiglu(g, .)
+
+
+class _NativeSublnSwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, o, g, eps, head_dim):
+        out, rstd = _C().subln_swiglu_fwd(o, g, float(eps), int(head_dim))
+        ctx.save_for_backward(o, g, rstd)
+        ctx.head_dim = head_dim
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        o, g, rstd = ctx.saved_tensors
+        do, dg = _C().subln_swiglu_bwd(dout.contiguous(), o, g, rstd, int(ctx.head_dim))
+        return do, dg, None, None
+
+
+def subln_swiglu(o: torch.Tensor, g: torch.Tensor, eps: float, head_dim: int) -> torch.Tensor:
+    """o: [T, H*D] retention output (token-major); g: [T, H*D]. Returns swiglu(g, rmsnorm_per_head(o))."""
+    if native_on(o):
+        return _NativeSublnSwiGLU.apply(o, g, eps, head_dim)
+    T, HD = o.shape
+    on = ref.rms_norm(o.view(T, HD // head_dim, head_dim), None, eps).view(T, HD)
+    return ref.swiglu(g, on)
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# gated retention
+
+
+def gate_logsigmoid(gt: torch.Tensor, normalizer: float) -> torch.Tensor:
+    return F.logsigmoid(gt) / normalizer
+
+
+class _NativeRetention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, gcum):
+        o = _C().retention_fwd(q, k, v, gcum)
+        ctx.save_for_backward(q, k, v, gcum)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, gcum = ctx.saved_tensors
+        dq, dk, dv, dg = _C().retention_bwd(do.contiguous(), q, k, v, gcum)
+        return dq, dk, dv, dg
+
+
+def retention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, gt: torch.Tensor,
+              chunk_size: int = 256) -> torch.Tensor:
+    """Gated retention over a full sequence (training path).
+
+    q, k, v: [B, L, H, D] (token-major, any strides with a contiguous last dim); gt: [B, L, H] per-step log decay
+    (logsigmoid / normalizer, any float dtype). Returns o: [B, L, H, D] contiguous."""
+    B, L, H, D = q.shape
+    if native_on(q) and _native.has("retention_fwd"):
+        gcum = gt.float().transpose(1, 2).cumsum(-1).contiguous()      # [B, H, L] fp32
+        return _NativeRetention.apply(q, k, v, gcum)
+    qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    gh = gt.transpose(1, 2)
+    if L % chunk_size == 0:
+        o = ref.chunk_gate_retention(qh, kh, vh, gh, chunk_size=chunk_size)
+    else:
+        o = ref.parallel_gate_retention(qh, kh, vh, gh)
+    return o.transpose(1, 2).contiguous()
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# attention (causal / sliding window, GQA)
+
+
+class _NativeAttention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, causal, window, scale):
+        o, lse = _C().attention_fwd(q, k, v, bool(causal), int(window or 0), float(scale))
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.cfg = (bool(causal), int(window or 0), float(scale))
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse = ctx.saved_tensors
+        causal, window, scale = ctx.cfg
+        dq, dk, dv = _C().attention_bwd(do.contiguous(), q, k, v, o, lse, causal, window, scale)
+        return dq, dk, dv, None, None, None
+
+
+_flash_attn_func = None
+
+
+def _flash():
+    global _flash_attn_func
+    if _flash_attn_func is None:
+        try:
+            from flash_attn import flash_attn_func
+            _flash_attn_func = flash_attn_func
+        except Exception:
+            _flash_attn_func = False
+    return _flash_attn_func
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
+              window: Optional[int] = None) -> torch.Tensor:
+    """q: [B, Lq, Hq, D], k/v: [B, Lk, Hk, D] -> [B, Lq, Hq, D]; scale 1/sqrt(D); window as flash-attn (w-1, 0)."""
+    scale = q.shape[-1] ** -0.5
+    if native_on(q) and _native.has("attention_fwd"):
+        return _NativeAttention.apply(q, k, v, causal, window, scale)
+    if q.is_cuda and _flash():
+        ws = (window - 1, 0) if window is not None else (-1, -1)
+        return _flash()(q, k, v, causal=causal, window_size=ws)
+    return ref.attention(q, k, v, causal=causal, window=window, q_offset=k.shape[1] - q.shape[1])
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# token embedding (x scale)
+
+
+class _NativeEmbedding(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, tokens, w, scale):
+        out = _C().embedding_fwd(tokens, w, float(scale))
+        ctx.save_for_backward(tokens)
+        ctx.vshape = w.shape
+        ctx.scale = scale
+        ctx.param = w
+        return out
+
+    @staticmethod
+    def backward(ctx, dy):
+        (tokens,) = ctx.saved_tensors
+        slot, acc = _grad_slot(ctx.param)
+        dy2 = dy.reshape(-1, ctx.vshape[1]).contiguous()
+        if slot is not None and not acc:
+            _C().embedding_bwd(tokens, dy2, int(ctx.vshape[0]), float(ctx.scale), slot)
+            return None, None, None
+        dw = _C().embedding_bwd(tokens, dy2, int(ctx.vshape[0]), float(ctx.scale), None)
+        if slot is not None:
+            slot.add_(dw)
+            return None, None, None
+        return None, dw, None
+
+
+def embedding(tokens: torch.Tensor, w: torch.Tensor, scale: float) -> torch.Tensor:
+    if native_on(w):
+        shp = tokens.shape
+        return _NativeEmbedding.apply(tokens.reshape(-1), w, scale).view(*shp, w.shape[1])
+    return scale * F.embedding(tokens, w)
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# cross-entropy over the vocabulary
+
+
+class _NativeCE(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, logits, target, ignore_index):
+        loss_rows, lse = _C().ce_fwd(logits, target, int(ignore_index))
+        ctx.save_for_backward(logits, target, lse)
+        ctx.ignore = int(ignore_index)
+        return loss_rows.sum()
+
+    @staticmethod
+    def backward(ctx, grad):
+        logits, target, lse = ctx.saved_tensors
+        g = grad.reshape(1).float().contiguous()
+        # the logits are not needed after this: the gradient overwrites them in place
+        dx = _C().ce_bwd(logits, target, lse, g, ctx.ignore, logits)
+        return dx, None, None
+
+
+def cross_entropy(logits: torch.Tensor, target: torch.Tensor, ignore_index: int) -> torch.Tensor:
+    """fp32 sum over non-ignored rows of lse - logit[target]. logits [N, V] (bf16), target [N] int64."""
+    if native_on(logits):
+        return _NativeCE.apply(logits, target, ignore_index)
+    lp = F.log_softmax(logits.float(), dim=-1)
+    return F.nll_loss(lp, target, ignore_index=ignore_index, reduction="sum")
+
+
+__all__ = [
+    "set_backend", "get_backend", "gemm", "linear", "rms_norm", "swiglu", "rope", "subln_swiglu", "gate_logsigmoid",
+    "retention", "attention", "embedding", "cross_entropy", "ref",
+]

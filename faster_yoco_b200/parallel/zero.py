@@ -1,0 +1,282 @@
+"""ZeRO-1 / ZeRO-2 data parallelism over one flat, owner-partitioned parameter buffer.
+
+Partition: fairscale OSS's greedy rule -- parameters in model order, each to the rank with the smallest running
+element total (yoco/tasks/zero1_fast.py:52-75 replicates it for the reference's fast path). Every rank holds the same
+layout: ``flat[r*seg:(r+1)*seg]`` is owner r's segment, each parameter a view at a 128-byte aligned offset. Gradients
+live in a second buffer with the same layout, so "reduce to owner" is a reduce-scatter of equal segments, and the
+parameter exchange after the step is an all-gather of equal segments (in place).
+
+Per update (reference call stack yoco/tasks/trainer_nosync.py:219-305 and zero1_fast.py:139-235):
+
+1. gradients are reduced to their owner, averaged over ranks, BF16 (comm backend ``nccl``: reduce-scatter; ``fused``:
+   the P2P reduce kernel of :mod:`faster_yoco_b200.parallel.p2p`, FP32 rank-order sum);
+2. ``factor = world / sample_size``; grad norm = factor * sqrt(sum over owners of ||g_owned||^2) (one scalar
+   all-reduce); ``factor *= min(1, clip / (norm + 1e-6))``;
+3. the owner runs Adam on its FP32 master shard with ``g32 = float(g16) * factor`` and writes the BF16 parameter into
+   its segment;
+4. every rank receives every segment (all-gather).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence
+
+import torch
+import torch.distributed as dist
+
+from . import dist as D
+
+ALIGN = 64          # elements (128 bytes of bf16): every parameter view starts 128-byte aligned
+
+
+def greedy_partition(sizes: Sequence[int], world: int) -> List[int]:
+    """Owner of each parameter: next parameter to the rank with the smallest running total (ties: lowest rank)."""
+    totals = [0] * world
+    owners = []
+    for n in sizes:
+        r = totals.index(min(totals))
+        owners.append(r)
+        totals[r] += n
+    return owners
+
+
+def _round_up(n: int, a: int) -> int:
+    return (n + a - 1) // a * a
+
+
+@dataclass
+class Entry:
+    param: torch.nn.Parameter
+    name: str
+    owner: int
+    offset: int        # element offset into the flat buffer (global, includes owner * seg)
+    numel: int
+    shape: torch.Size
+
+
+class FlatParams:
+    """The flat BF16 parameter buffer + flat gradient buffer; model parameters become views of it."""
+
+    def __init__(self, named_params, world: int, rank: int, device, dtype=torch.bfloat16):
+        named = [(n, p) for n, p in named_params if p.requires_grad]
+        self.world, self.rank, self.device, self.dtype = world, rank, torch.device(device), dtype
+        owners = greedy_partition([p.numel() for _, p in named], world)
+        fill = [0] * world
+        placed = []
+        for (name, p), r in zip(named, owners):
+            placed.append((name, p, r, fill[r]))
+            fill[r] = _round_up(fill[r] + p.numel(), ALIGN)
+        self.seg = max(_round_up(max(fill), 1024), 1024)
+        self.used = fill                                     # used (aligned) length of each owner's segment
+        self.flat = torch.zeros(world * self.seg, dtype=dtype, device=self.device)
+        self.grad_flat = torch.zeros(world * self.seg, dtype=dtype, device=self.device)
+        self.entries: List[Entry] = []
+        self.by_param: Dict[int, Entry] = {}
+        with torch.no_grad():
+            for name, p, r, off in placed:
+                g_off = r * self.seg + off
+                view = self.flat[g_off:g_off + p.numel()].view_as(p)
+                view.copy_(p.data.to(dtype))
+                p.data = view
+                e = Entry(p, name, r, g_off, p.numel(), p.shape)
+                self.entries.append(e)
+                self.by_param[id(p)] = e
+        for e in self.entries:
+            e.param._fyb_flat = self                                  # lets ops find the gradient slot
+        self.buckets: List[List[Entry]] = []
+        self.direct_grads = False          # native ops write weight gradients straight into their slots
+        self.accumulate = False            # later micro-batches of an update add into the slots
+        self._written = set()
+
+    # ---------------------------------------------------------------------------------------------------------
+    def owned(self, rank: Optional[int] = None) -> slice:
+        r = self.rank if rank is None else rank
+        return slice(r * self.seg, r * self.seg + self.seg)
+
+    def param_segment(self, rank: Optional[int] = None) -> torch.Tensor:
+        return self.flat[self.owned(rank)]
+
+    def grad_segment(self, rank: Optional[int] = None) -> torch.Tensor:
+        return self.grad_flat[self.owned(rank)]
+
+    def grad_view(self, p) -> torch.Tensor:
+        """A fresh view of p's gradient slot (fresh so autograd's AccumulateGrad adopts it without a copy)."""
+        e = self.by_param[id(p)]
+        return self.grad_flat[e.offset:e.offset + e.numel].view(e.shape)
+
+    def claim_grad(self, p):
+        """Slot for p's weight gradient from a native backward: (view, accumulate-into-it)."""
+        acc = self.accumulate or id(p) in self._written
+        self._written.add(id(p))
+        return self.grad_view(p), acc
+
+    def begin_update(self):
+        self.accumulate = False
+        self._written.clear()
+
+    def begin_microbatch(self, first: bool):
+        self.accumulate = not first
+
+    def collect_grads(self):
+        """Move every p.grad into its slot and clear p.grad; slots that no gradient reached this update are zeroed."""
+        with torch.no_grad():
+            for e in self.entries:
+                g = e.param.grad
+                slot = self.grad_flat[e.offset:e.offset + e.numel]
+                written = id(e.param) in self._written
+                if g is None:
+                    if not written and not self.accumulate:
+                        slot.zero_()
+                elif g.data_ptr() != slot.data_ptr():
+                    if written or self.accumulate:
+                        slot.view(e.shape).add_(g)
+                    else:
+                        slot.view(e.shape).copy_(g)
+                    self._written.add(id(e.param))
+                e.param.grad = None
+
+    def make_buckets(self, module_groups: Sequence[Sequence[torch.nn.Parameter]]):
+        """Reduction buckets: groups of parameters whose gradients are complete together (one layer each)."""
+        self.buckets = [[self.by_param[id(p)] for p in grp if id(p) in self.by_param] for grp in module_groups]
+        return self.buckets
+
+
+def grad_slot(p: torch.Tensor) -> Optional[torch.Tensor]:
+    fp = getattr(p, "_fyb_flat", None)
+    return fp.grad_view(p) if fp is not None else None
+
+
+class ZeroOptimizer:
+    """Sharded FP32 Adam (apex AdamW expression) over the owner's segment of a :class:`FlatParams`."""
+
+    def __init__(self, flat: FlatParams, optim_cfg, comm: str = "nccl", group=None, stage: int = 1):
+        self.flat, self.cfg, self.comm, self.group, self.stage = flat, optim_cfg, comm, group, stage
+        seg = flat.param_segment()
+        self.master = seg.float().clone()
+        self.exp_avg = torch.zeros_like(self.master)
+        self.exp_avg_sq = torch.zeros_like(self.master)
+        self.num_updates = 0
+        dev = flat.device
+        # device-resident hyper-parameters: [lr, bias_correction1, bias_correction2] (written by the host each step)
+        self.hyper = torch.zeros(4, dtype=torch.float32, device=dev)
+        self._hyper_host = torch.zeros(4, dtype=torch.float32, pin_memory=dev.type == "cuda")
+        self.p2p = None
+        self.last_grad_norm = None
+
+    # ---------------------------------------------------------------------------------------------------------
+    def reduce_grads(self):
+        """Average the gradient buffer over ranks into each owner's segment (BF16)."""
+        fp = self.flat
+        if fp.world == 1:
+            return
+        if self.comm == "fused" and self.p2p is not None:
+            self.p2p.reduce_to_owner(fp.grad_flat, fp.seg)
+            return
+        out = fp.grad_segment()
+        if dist.get_backend(self.group) == "nccl":
+            dist.reduce_scatter_tensor(out, fp.grad_flat, op=dist.ReduceOp.AVG, group=self.group)
+        else:
+            tmp = torch.empty_like(out)
+            dist.reduce_scatter_tensor(tmp, fp.grad_flat, op=dist.ReduceOp.SUM, group=self.group)
+            out.copy_(tmp / fp.world)
+
+    def all_gather_params(self):
+        fp = self.flat
+        if fp.world == 1:
+            return
+        if self.comm == "fused" and self.p2p is not None:
+            self.p2p.all_gather(fp.flat, fp.seg)
+            return
+        dist.all_gather_into_tensor(fp.flat, fp.param_segment(), group=self.group)
+
+    def prepare(self, lr: float):
+        """Host part before an update: learning rate and bias corrections into the device hyper-parameter vector."""
+        step = self.num_updates + 1
+        b1, b2 = self.cfg.betas
+        bc1 = float(torch.tensor(1.0 - b1 ** step, dtype=torch.float32))
+        bc2 = float(torch.tensor(1.0 - b2 ** step, dtype=torch.float32))
+        h = self._hyper_host
+        h[0], h[1], h[2], h[3] = lr, bc1, bc2, float(step)
+        self.hyper.copy_(h, non_blocking=True)
+        self._lr = lr
+
+    def finish(self):
+        self.num_updates += 1
+
+    def device_step(self, sample_size: torch.Tensor) -> torch.Tensor:
+        """Clip + Adam + parameter exchange, device work only (capturable). sample_size: device scalar summed
+        over ranks. Returns the grad norm (device scalar)."""
+        from .. import ops
+        fp = self.flat
+        g16 = fp.grad_segment()
+        factor = fp.world / torch.where(sample_size > 0, sample_size, torch.ones_like(sample_size)).float()
+        native = ops.native_on(g16)
+        if native:
+            sq = ops._C().sq_norm(g16)
+        else:
+            sq = g16.float().pow(2).sum().reshape(1)
+        if fp.world > 1:
+            if self.comm == "fused" and self.p2p is not None:
+                sq = self.p2p.all_reduce_vector(sq)
+            else:
+                dist.all_reduce(sq, group=self.group)
+        grad_norm = (factor * sq.sqrt()).reshape(())
+        clip = self.cfg.clip_norm
+        if clip > 0:
+            factor = factor * (clip / (grad_norm + 1e-6)).clamp(max=1.0)
+        b1, b2 = self.cfg.betas
+        seg = fp.param_segment()
+        if native:
+            ops._C().adam_step(self.master, g16, self.exp_avg, self.exp_avg_sq, seg, self.hyper,
+                               factor.reshape(1).float().contiguous(), float(b1), float(b2), float(self.cfg.eps),
+                               float(self.cfg.weight_decay), bool(self.cfg.adamw_mode))
+        else:
+            self._torch_adam(g16, seg, factor, self._lr)
+        self.all_gather_params()
+        self.last_grad_norm = grad_norm
+        return grad_norm
+
+    def step(self, sample_size: torch.Tensor, lr: float) -> torch.Tensor:
+        self.prepare(lr)
+        n = self.device_step(sample_size)
+        self.finish()
+        return n
+
+    def _torch_adam(self, g16, seg, factor, lr):
+        from ..ops import reference as ref
+        b1, b2 = self.cfg.betas
+        g32 = g16.float() * factor.float()
+        ref.adam_step_(self.master, g32, self.exp_avg, self.exp_avg_sq, lr=lr, beta1=b1, beta2=b2,
+                       eps=self.cfg.eps, step=self.num_updates + 1, weight_decay=self.cfg.weight_decay,
+                       adamw=self.cfg.adamw_mode, p16=seg)
+
+    # ---------------------------------------------------------------------------------------------------------
+    def state_dict(self):
+        return {"num_updates": self.num_updates, "master": self.master, "exp_avg": self.exp_avg,
+                "exp_avg_sq": self.exp_avg_sq, "seg": self.flat.seg, "rank": self.flat.rank,
+                "world": self.flat.world}
+
+    def load_state_dict(self, sd):
+        if sd["seg"] != self.flat.seg or sd["world"] != self.flat.world:
+            raise ValueError("optimizer shard layout does not match this run (seg/world differ)")
+        self.num_updates = int(sd["num_updates"])
+        self.master.copy_(sd["master"])
+        self.exp_avg.copy_(sd["exp_avg"])
+        self.exp_avg_sq.copy_(sd["exp_avg_sq"])
+
+    def consolidated_state(self):
+        """Per-parameter FP32 master / exp_avg / exp_avg_sq gathered on every rank (for a consolidated checkpoint)."""
+        fp = self.flat
+        shards = {}
+        for name, t in (("master", self.master), ("exp_avg", self.exp_avg), ("exp_avg_sq", self.exp_avg_sq)):
+            if fp.world > 1:
+                full = torch.empty(fp.world * fp.seg, dtype=t.dtype, device=t.device)
+                dist.all_gather_into_tensor(full, t, group=self.group)
+            else:
+                full = t
+            shards[name] = full
+        out = {}
+        for e in fp.entries:
+            out[e.name] = {k: v[e.offset:e.offset + e.numel].view(e.shape).cpu().clone() for k, v in shards.items()}
+        return out

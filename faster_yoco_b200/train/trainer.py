@@ -1,0 +1,158 @@
+"""The training step: forward, loss, backward, gradient reduction, clip, sharded Adam, parameter exchange.
+
+Reference: the patched fairseq ``Trainer.train_step`` (yoco/tasks/trainer_nosync.py:219-305) with ZeRO-1 fast path
+(yoco/tasks/zero1_fast.py) and the CUDA-graphed decoder layers (yoco/models/decoder/layer_graphs.py). Differences by
+design:
+
+* no host syncs at all inside an update: the gradient normaliser ``world / sample_size``, the clip coefficient, the
+  learning rate and Adam's bias corrections are device tensors; the non-finite / cross-rank-inconsistent grad-norm
+  abort is raised from pinned host memory at the latest one update later (``PendingChecks``);
+* ``graph_step=True`` captures the WHOLE update (forward, backward, gradient reduction, Adam, all-gather) as one CUDA
+  graph after warm-up; each update is then an input copy, a hyper-parameter copy and one graph launch.
+"""
+from __future__ import annotations
+
+import contextlib
+import math
+from typing import Dict, Optional
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..parallel import dist as D
+from ..parallel.zero import FlatParams, ZeroOptimizer
+from ..utils.faults import PendingChecks, grad_norm_consistent
+from .metrics import DeviceMeters
+from .schedule import PolynomialDecaySchedule
+
+
+class Trainer:
+    def __init__(self, model: torch.nn.Module, optim_cfg, *, device, comm: str = "nccl", zero_stage: int = 1,
+                 pad_idx: int = 1, graph_step: bool = False, group=None, check_consistency: bool = True):
+        self.model = model
+        self.device = torch.device(device)
+        self.cfg = optim_cfg
+        self.pad_idx = pad_idx
+        self.rank, self.world = D.rank(), D.world()
+        self.group = group
+        self.flat = FlatParams(model.named_parameters(), self.world, self.rank, self.device,
+                               dtype=next(model.parameters()).dtype)
+        self.flat.direct_grads = self.device.type == "cuda" and ops.get_backend() == "native"
+        self.zero = ZeroOptimizer(self.flat, optim_cfg, comm=comm, group=group, stage=zero_stage)
+        if comm == "fused" and self.world > 1 and self.device.type == "cuda":
+            from ..parallel.p2p import PeerComm
+            self.zero.p2p = PeerComm(group)
+        self.sched = PolynomialDecaySchedule(optim_cfg.lr, optim_cfg.warmup_updates, optim_cfg.total_num_update,
+                                             optim_cfg.end_learning_rate, optim_cfg.power)
+        self.pending = PendingChecks(self.device.type == "cuda")
+        self.meters = DeviceMeters(self.device)
+        self.check_consistency = check_consistency
+        self.graph_step = graph_step and self.device.type == "cuda"
+        self._graph = None
+        self._static: Dict[str, torch.Tensor] = {}
+        self._graph_out = None
+        self.vocab = None
+
+    # ------------------------------------------------------------------------------------------------------------
+    def num_updates(self) -> int:
+        return self.zero.num_updates
+
+    def _to_device(self, batch):
+        """Pinned host -> device copies without blocking (yoco/tasks/trainer_nosync.py:67-88)."""
+        out = {}
+        for k in ("src_tokens", "target"):
+            t = batch[k]
+            if t.device.type == "cpu" and self.device.type == "cuda":
+                if not t.is_pinned():
+                    t = t.pin_memory()
+                t = t.to(self.device, non_blocking=True)
+            out[k] = t
+        return out
+
+    def _forward_backward(self, src, tgt, ntok: torch.Tensor):
+        logits, _ = self.model(src)
+        V = logits.shape[-1]
+        loss = ops.cross_entropy(logits.view(-1, V), tgt.reshape(-1), self.pad_idx)
+        loss.backward()
+        return loss.detach()
+
+    def _reduce_stats(self, loss_sum, sample_size):
+        stats = torch.stack([loss_sum.float().reshape(()), sample_size.float().reshape(())])
+        if self.world > 1:
+            if self.zero.p2p is not None:
+                stats = self.zero.p2p.all_reduce_vector(stats)
+            else:
+                dist.all_reduce(stats, group=self.group)
+        return stats[0], stats[1]
+
+    def _device_update(self, src, tgt, ntok):
+        """All device work of one update (capturable): returns (loss_sum, sample_size, grad_norm, consistent)."""
+        self.flat.begin_update()
+        loss = self._forward_backward(src, tgt, ntok)
+        self.flat.collect_grads()          # p.grad -> slot for gradients not written there by a native op
+        loss_all, ss_all = self._reduce_stats(loss, ntok)
+        self.zero.reduce_grads()
+        gnorm = self.zero.device_step(ss_all)
+        consistent = (grad_norm_consistent(gnorm, self.rank, self.world, self.group)
+                      if self.check_consistency else torch.isfinite(gnorm))
+        return loss_all, ss_all, gnorm, consistent
+
+    def train_step(self, batch) -> torch.Tensor:
+        """One update; returns the (device) summed loss over ranks without waiting for it."""
+        self.pending.check(block=False)
+        self.model.train()
+        dev = self._to_device(batch)
+        ntok = torch.as_tensor(float(batch["ntokens"]), dtype=torch.float32)
+        lr = self.sched.lr_for(self.num_updates())
+        if self.graph_step:
+            out = self._graph_update(dev, ntok, lr)
+        else:
+            ntok_d = ntok.to(self.device, non_blocking=True) if self.device.type == "cuda" else ntok
+            self.zero.prepare(lr)
+            out = self._device_update(dev["src_tokens"], dev["target"], ntok_d)
+        loss_all, ss_all, gnorm, consistent = out
+        self.pending.check(block=True)
+        self.pending.arm(torch.isfinite(gnorm), consistent)
+        self.zero.finish()
+        self.meters.update(loss_all, ss_all, batch["ntokens"] * self.world, batch.get("nsentences", 1) * self.world,
+                           gnorm, self.cfg.clip_norm)
+        return loss_all
+
+    # ------------------------------------------------------------------------------------------------------------
+    def _graph_update(self, dev, ntok, lr):
+        st = self._static
+        if self._graph is None:
+            st["src"] = torch.empty_like(dev["src_tokens"])
+            st["tgt"] = torch.empty_like(dev["target"])
+            st["ntok"] = torch.zeros((), dtype=torch.float32, device=self.device)
+        st["src"].copy_(dev["src_tokens"], non_blocking=True)
+        st["tgt"].copy_(dev["target"], non_blocking=True)
+        st["ntok"].copy_(ntok, non_blocking=True)
+        self.zero.prepare(lr)
+        if self._graph is None:
+            # one eager update on a side stream (allocator warm-up, lazy init), then capture the next one
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                out = self._device_update(st["src"], st["tgt"], st["ntok"])
+            torch.cuda.current_stream().wait_stream(s)
+            self._graph = "warm"
+            return out
+        if self._graph == "warm":
+            g = torch.cuda.CUDAGraph()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g):
+                self._graph_out = self._device_update(st["src"], st["tgt"], st["ntok"])
+            self._graph = g
+        self._graph.replay()
+        return tuple(t.clone() for t in self._graph_out)
+
+    def release_graph(self):
+        """Drop the captured update (must happen before the process group is destroyed)."""
+        self._graph = None
+        self._graph_out = None
+
+    # ------------------------------------------------------------------------------------------------------------
+    def log_stats(self):
+        return self.meters.flush()
