@@ -1,0 +1,862 @@
+// Tiled attention on tcgen05 for sm_100a: causal / sliding-window softmax attention with GQA (the cross-decoder
+// and the sliding-window self-decoder: flash_attn_func in yoco/models/decoder/cross_attention.py:42 and
+// sliding_window_attention.py:65) and the parallel form of gated retention (gate_recurrent.py:266-276).
+//
+// One kernel family, two score transforms:
+//   kSoftmax   : P = softmax(scale * Q K^T) with an online max; O accumulated in registers
+//   kRetention : P = (scale * Q K^T) * exp(G_q - G_k) (G = fp32 cumsum of the per-step log decays), causal;
+//                no normalisation, so O accumulates directly in TMEM across key tiles
+//
+// Forward CTA (6 warps) = one (batch, head, 128-query tile):
+//   warp 0     TMA producer: Q once, K/V tiles (128 keys x 128 dims, 128B swizzle) in a 2-stage ring
+//   warp 1     UMMA issuer: S = Q K^T into one of two TMEM S buffers, then O_blk = P V (P from shared memory)
+//   warps 2..5 one thread per query row: read S (tcgen05.ld), mask, exponentiate, write P (bf16, swizzled K-major)
+//
+// Backward CTA = one (batch, kv head, 128-key tile), looping over the query heads of the GQA group and the query
+// tiles that see this key tile:  S^T = K Q^T, dP^T = V dO^T (TMEM); P^T, dS^T (bf16, shared memory);
+// dV += P^T dO, dK += dS^T Q (TMEM accumulators), dQ_tile = dS K (TMEM -> fp32 atomics into a dQ accumulator).
+// The UMMA descriptors read the same swizzled dS^T tile as K-major (for dK) and as MN-major (for dQ).
+//
+// Retention gate gradient, from dG_i = sum_j dP_ij P_ij - sum_k dP_ki P_ki:  dG_i = dO_i . O_i - V_i . dV_i
+// (the two sums collapse into row dot products), computed by the small post kernel.
+#include <ATen/ATen.h>
+
+#include "common/host.h"
+#include "common/ptx.cuh"
+
+namespace fyb {
+namespace {
+
+constexpr int kD = 128;      // head dim
+constexpr int kT = 128;      // tile rows (queries / keys)
+constexpr int kTileBytes = kT * kD * 2;   // 32 KB: two 16 KB swizzle-atom columns (dims 0-63, 64-127)
+constexpr int kAttnThreads = 192;
+enum Mode : int { kSoftmax = 0, kRetention = 1 };
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct AttnParams {
+  int B, Lq, Lk, Hq, Hk;
+  int q_offset;          // absolute position of query 0 minus position of key 0 (causal alignment)
+  int window;            // 0 = unlimited
+  int causal;
+  float scale;
+  __nv_bfloat16* O;      // [B, Lq, Hq, D] contiguous
+  float* lse;            // [B, Hq, Lq] (softmax)
+  const float* gcum;     // [B, H, L] (retention)
+  int* status;
+};
+
+// row r, 16-byte chunk c (0..15 over 128 bf16 values) of a [128 x 128] bf16 tile stored as two SW128 K-major atoms
+__device__ __forceinline__ uint32_t sw_off(int r, int c) {
+  return static_cast<uint32_t>((c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+// S/O tile descriptors for a 128-wide K dimension split in two 64-wide swizzle atoms (K-major)
+__device__ __forceinline__ uint64_t kmaj_desc(uint32_t base, int k16) {
+  return sw128_desc(base + (k16 >> 2) * 16384 + (k16 & 3) * 32, 16, 1024);
+}
+// MN-major operand whose 128 MN values sit in two 64-wide atoms 16 KB apart; K advances 16 rows per step
+__device__ __forceinline__ uint64_t mnmaj_desc(uint32_t base, int k16) {
+  return sw128_desc(base + k16 * 2048, 16384, 1024);
+}
+
+struct Range {
+  int j0, j1;
+};
+
+__device__ __forceinline__ Range kv_range(const AttnParams& p, int q0) {
+  const int qa_lo = q0 + p.q_offset;
+  const int qa_hi = min(q0 + kT, p.Lq) - 1 + p.q_offset;
+  int kend = p.Lk;
+  if (p.causal) kend = min(kend, qa_hi + 1);
+  int kbeg = 0;
+  if (p.window > 0) kbeg = max(0, qa_lo - p.window + 1);
+  Range r;
+  r.j0 = kbeg / kT;
+  r.j1 = kend <= 0 ? r.j0 : (kend + kT - 1) / kT;
+  if (r.j1 < r.j0) r.j1 = r.j0;
+  return r;
+}
+
+template <typename P>
+__device__ __forceinline__ bool key_valid(const P& p, int qa, int k) {
+  if (k >= p.Lk) return false;
+  if (p.causal && k > qa) return false;
+  if (p.window > 0 && k <= qa - p.window) return false;
+  return true;
+}
+
+// ======================================================================================================== forward
+
+template <int MODE>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kTileBytes;             // 2 stages
+  uint8_t* sV = sK + 2 * kTileBytes;         // 2 stages
+  uint8_t* sP = sV + 2 * kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kTileBytes);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* s_empty = bars + 11; // [2]
+  uint64_t* p_full = bars + 13;
+  uint64_t* p_empty = bars + 14;
+  uint64_t* o_full = bars + 15;  // [2]
+  uint64_t* o_empty = bars + 17; // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = (p.Lq + kT - 1) / kT;
+  const int qt = nq - 1 - (blockIdx.x % nq);     // heavy (late) query tiles first
+  const int bh = blockIdx.x / nq;
+  const int h = bh % p.Hq, b = bh / p.Hq;
+  const int hk = h / (p.Hq / p.Hk);
+  const int q0 = qt * kT;
+  const Range rg = kv_range(p, q0);
+  const int n = rg.j1 - rg.j0;
+  constexpr uint32_t IDESC_S = idesc_bf16(128, 128, false, false);
+  constexpr uint32_t IDESC_O = idesc_bf16(128, 128, false, true);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 19; ++i) mbar_init(&bars[i], 1);
+    mbar_init(&s_empty[0], 4);
+    mbar_init(&s_empty[1], 4);
+    mbar_init(p_full, 4);
+    mbar_init(&o_empty[0], 4);
+    mbar_init(&o_empty[1], 4);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;   // S[0] @ col 0, S[1] @ 128, O[0] @ 256, O[1] @ 384
+
+  if (warp == 0) {
+    if (lane == 0 && n > 0) {
+      const int rowq = b * p.Lq + q0;
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      tma_load_3d(sQ, &tmQ, q_full, 0, h, rowq);
+      tma_load_3d(sQ + 16384, &tmQ, q_full, 64, h, rowq);
+      for (int it = 0; it < n; ++it) {
+        const int st = it & 1;
+        const uint32_t ph = (it >> 1) & 1;
+        const int rowk = b * p.Lk + (rg.j0 + it) * kT;
+        if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, p.status, 20)) break;
+        mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+        tma_load_3d(sK + st * kTileBytes, &tmK, &k_full[st], 0, hk, rowk);
+        tma_load_3d(sK + st * kTileBytes + 16384, &tmK, &k_full[st], 64, hk, rowk);
+        if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, p.status, 21)) break;
+        mbar_arrive_expect_tx(&v_full[st], kTileBytes);
+        tma_load_3d(sV + st * kTileBytes, &tmV, &v_full[st], 0, hk, rowk);
+        tma_load_3d(sV + st * kTileBytes + 16384, &tmV, &v_full[st], 64, hk, rowk);
+      }
+      // drain the ring before exit
+      for (int it = n; it < n + 2; ++it) {
+        const int st = it & 1;
+        const uint32_t ph = (it >> 1) & 1;
+        mbar_wait(&k_empty[st], ph ^ 1u, nullptr, p.status, 22);
+        mbar_wait(&v_empty[st], ph ^ 1u, nullptr, p.status, 23);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n > 0) {
+      const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, 24);
+      auto issue_s = [&](int it) -> bool {
+        const int st = it & 1;
+        const uint32_t ph = (it >> 1) & 1;
+        if (!mbar_wait(&k_full[st], ph, abort_flag, p.status, 25)) return false;
+        if (!mbar_wait(&s_empty[st], ph ^ 1u, abort_flag, p.status, 26)) return false;
+        tc_fence_after();
+        const uint32_t aK = smem_u32(sK + st * kTileBytes);
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k)
+          umma_bf16(tmem + st * 128, kmaj_desc(aQ, k), kmaj_desc(aK, k), IDESC_S, k > 0 ? 1u : 0u);
+        umma_commit(&s_full[st]);
+        umma_commit(&k_empty[st]);
+        return true;
+      };
+      auto issue_pv = [&](int it) -> bool {
+        const int st = it & 1;
+        const uint32_t ph = (it >> 1) & 1;
+        if (!mbar_wait(p_full, it & 1, abort_flag, p.status, 27)) return false;
+        if (!mbar_wait(&v_full[st], ph, abort_flag, p.status, 28)) return false;
+        uint32_t dst = tmem + 256;
+        if (MODE == kSoftmax) {
+          if (!mbar_wait(&o_empty[st], ph ^ 1u, abort_flag, p.status, 29)) return false;
+          dst += st * 128;
+        }
+        tc_fence_after();
+        const uint32_t aV = smem_u32(sV + st * kTileBytes);
+#pragma unroll
+        for (int k = 0; k < kT / 16; ++k) {
+          const uint32_t acc = (MODE == kRetention) ? ((it > 0 || k > 0) ? 1u : 0u) : (k > 0 ? 1u : 0u);
+          umma_bf16(dst, kmaj_desc(aP, k), mnmaj_desc(aV, k), IDESC_O, acc);
+        }
+        umma_commit(p_empty);
+        umma_commit(&v_empty[st]);
+        if (MODE == kSoftmax) umma_commit(&o_full[st]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int it = 0; ok && it < n; ++it) {
+        if (it + 1 < n) ok = issue_s(it + 1);
+        if (ok) ok = issue_pv(it);
+      }
+      if (MODE == kRetention && ok) umma_commit(&o_full[0]);
+    }
+  } else {
+    // -------------------------------------------------------------------------------- score / softmax warps
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;                 // query row within the tile
+    const int qrow = q0 + r;
+    const int qa = qrow + p.q_offset;               // absolute query position
+    const uint32_t trow = static_cast<uint32_t>(quad * 32) << 16;
+    const float sl2 = p.scale * kLog2e;
+    float m_run = -INFINITY, l_run = 0.f, m_o = -INFINITY;
+    float o_acc[kD];
+    if (MODE == kSoftmax) {
+#pragma unroll
+      for (int i = 0; i < kD; ++i) o_acc[i] = 0.f;
+    }
+    float gq = 0.f;
+    const float* gbase = nullptr;
+    if (MODE == kRetention) {
+      gbase = p.gcum + (static_cast<int64_t>(b) * p.Hq + h) * p.Lq;
+      gq = qrow < p.Lq ? gbase[qrow] : 0.f;
+    }
+    bool ok = true;
+    // softmax: O block `it` was formed with P scaled by the running max of tile it (m_tile); o_acc is scaled to m_o
+    auto consume_o = [&](int it, float m_tile) {
+      const int st = it & 1;
+      const uint32_t ph = (it >> 1) & 1;
+      if (!mbar_wait(&o_full[st], ph, abort_flag, p.status, 30)) {
+        ok = false;
+        return;
+      }
+      tc_fence_after();
+      const float a = (m_o == -INFINITY) ? 0.f : exp2f(m_o - m_tile);
+#pragma unroll
+      for (int c = 0; c < kD; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + 256 + st * 128 + trow + c, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o_acc[c + i] = o_acc[c + i] * a + __uint_as_float(v[i]);
+      }
+      m_o = m_tile;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[st]);
+    };
+    float m_last = -INFINITY;   // running max used for the previous tile's P
+    for (int it = 0; ok && it < n; ++it) {
+      const int st = it & 1;
+      const uint32_t ph = (it >> 1) & 1;
+      const int k0 = (rg.j0 + it) * kT;
+      if (!mbar_wait(&s_full[st], ph, abort_flag, p.status, 31)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool full_tile = (k0 + kT <= p.Lk) && (!p.causal || k0 + kT - 1 <= q0 + p.q_offset) &&
+                             (p.window <= 0 || k0 > min(q0 + kT, p.Lq) - 1 + p.q_offset - p.window);
+      float m_new = m_run;
+      if (MODE == kSoftmax) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < kT; c += 32) {
+          uint32_t v[32];
+          tmem_ld32(tmem + st * 128 + trow + c, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const bool valid = full_tile || key_valid(p, qa, k0 + c + i);
+            if (valid) mx = fmaxf(mx, __uint_as_float(v[i]));
+          }
+        }
+        m_new = fmaxf(m_run, mx * sl2);
+      }
+      // P(it) may only be written once PV(it-1) has read P(it-1)
+      if (!mbar_wait(p_empty, (it & 1) ^ 1u, abort_flag, p.status, 32)) {
+        ok = false;
+        break;
+      }
+      float lsum = 0.f;
+      const float mref = (m_new == -INFINITY) ? 0.f : m_new;
+#pragma unroll
+      for (int c = 0; c < kT; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + st * 128 + trow + c, v);
+        tmem_ld_wait();
+        float pv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int kk = k0 + c + i;
+          const bool valid = full_tile || key_valid(p, qa, kk);
+          float x;
+          if (MODE == kSoftmax) {
+            x = valid ? exp2f(__uint_as_float(v[i]) * sl2 - mref) : 0.f;
+            lsum += x;
+          } else {
+            x = valid ? __uint_as_float(v[i]) * p.scale * __expf(gq - __ldg(gbase + kk)) : 0.f;
+          }
+          pv[i] = x;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int chunk = (c >> 3) + j;   // 16-byte chunk index 0..15 of the 256-byte row
+          const uint4 w = make_uint4(pack_bf16(pv[8 * j], pv[8 * j + 1]), pack_bf16(pv[8 * j + 2], pv[8 * j + 3]),
+                                     pack_bf16(pv[8 * j + 4], pv[8 * j + 5]),
+                                     pack_bf16(pv[8 * j + 6], pv[8 * j + 7]));
+          *reinterpret_cast<uint4*>(sP + sw_off(r, chunk)) = w;
+        }
+      }
+      if (MODE == kSoftmax) {
+        l_run = (m_new == -INFINITY) ? 0.f : l_run * exp2f(m_run - m_new) + lsum;
+        m_run = m_new;
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&s_empty[st]);
+        mbar_arrive(p_full);
+      }
+      if (MODE == kSoftmax) {
+        if (it >= 1) consume_o(it - 1, m_last);
+        m_last = m_run;
+      }
+    }
+    if (MODE == kSoftmax) {
+      if (ok && n > 0) consume_o(n - 1, m_last);
+      if (qrow < p.Lq) {
+        const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+        __nv_bfloat16* orow = p.O + ((static_cast<int64_t>(b) * p.Lq + qrow) * p.Hq + h) * kD;
+#pragma unroll
+        for (int c = 0; c < kD; c += 8)
+          *reinterpret_cast<uint4*>(orow + c) =
+              make_uint4(pack_bf16(o_acc[c] * inv, o_acc[c + 1] * inv), pack_bf16(o_acc[c + 2] * inv, o_acc[c + 3] * inv),
+                         pack_bf16(o_acc[c + 4] * inv, o_acc[c + 5] * inv), pack_bf16(o_acc[c + 6] * inv, o_acc[c + 7] * inv));
+        p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.Lq + qrow] =
+            l_run > 0.f ? (m_o + log2f(l_run)) * 0.6931471805599453f : -INFINITY;
+      }
+    } else {
+      const bool have = ok && n > 0 && mbar_wait(&o_full[0], 0, abort_flag, p.status, 33);
+      if (have) tc_fence_after();
+      __nv_bfloat16* orow = p.O + ((static_cast<int64_t>(b) * p.Lq + min(qrow, p.Lq - 1)) * p.Hq + h) * kD;
+#pragma unroll
+      for (int c = 0; c < kD; c += 32) {
+        uint32_t v[32];
+        if (have) {
+          tmem_ld32(tmem + 256 + trow + c, v);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0u;
+        }
+        if (qrow < p.Lq) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(orow + c + 8 * j) =
+                make_uint4(pack_bf16(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1])),
+                           pack_bf16(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3])),
+                           pack_bf16(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5])),
+                           pack_bf16(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7])));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ======================================================================================================= backward
+
+struct AttnBwdParams {
+  int B, Lq, Lk, Hq, Hk;
+  int q_offset, window, causal;
+  float scale;
+  const float* lse;      // softmax: [B, Hq, Lq]
+  const float* delta;    // softmax: [B, Hq, Lq] rowsum(dO * O)
+  const float* gcum;     // retention: [B, H, L]
+  float* dq_acc;         // [B, Lq, Hq, D] fp32
+  __nv_bfloat16* dK;     // [B, Lk, Hk, D]
+  __nv_bfloat16* dV;     // [B, Lk, Hk, D]
+  int* status;
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                    AttnBwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + kTileBytes;
+  uint8_t* sQ = sV + kTileBytes;
+  uint8_t* sdO = sQ + kTileBytes;
+  uint8_t* sPT = sdO + kTileBytes;
+  uint8_t* sdST = sPT + kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sdST + kTileBytes);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;
+  uint64_t* qdo_empty = bars + 2;
+  uint64_t* st_full = bars + 3;
+  uint64_t* pt_full = bars + 4;
+  uint64_t* dst_full = bars + 5;
+  uint64_t* pds_empty = bars + 6;
+  uint64_t* dq_full = bars + 7;
+  uint64_t* dq_empty = bars + 8;
+  uint64_t* fin = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nk = (p.Lk + kT - 1) / kT;
+  const int nq = (p.Lq + kT - 1) / kT;
+  const int kt = blockIdx.x % nk;
+  const int bh = blockIdx.x / nk;
+  const int hk = bh % p.Hk, b = bh / p.Hk;
+  const int G = p.Hq / p.Hk;
+  const int k0 = kt * kT;
+  const int k_hi = min(k0 + kT, p.Lk) - 1;
+  int i_lo = 0, i_hi = nq;
+  if (p.causal) i_lo = max(0, k0 - p.q_offset) / kT;
+  if (p.window > 0) i_hi = min(nq, max(0, k_hi + p.window - 1 - p.q_offset) / kT + 1);
+  const int per_h = max(0, i_hi - i_lo);
+  const int n_it = G * per_h;
+  constexpr uint32_t ID_KK = idesc_bf16(128, 128, false, false);
+  constexpr uint32_t ID_KM = idesc_bf16(128, 128, false, true);
+  constexpr uint32_t ID_MM = idesc_bf16(128, 128, true, true);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 10; ++i) mbar_init(&bars[i], 1);
+    mbar_init(pt_full, 4);
+    mbar_init(dst_full, 4);
+    mbar_init(dq_empty, 4);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;   // S^T/dQ @ 0, dP^T @ 128, dV @ 256, dK @ 384
+
+  if (warp == 0) {
+    if (lane == 0 && n_it > 0) {
+      const int rowk = b * p.Lk + k0;
+      mbar_arrive_expect_tx(kv_full, 2 * kTileBytes);
+      tma_load_3d(sK, &tmK, kv_full, 0, hk, rowk);
+      tma_load_3d(sK + 16384, &tmK, kv_full, 64, hk, rowk);
+      tma_load_3d(sV, &tmV, kv_full, 0, hk, rowk);
+      tma_load_3d(sV + 16384, &tmV, kv_full, 64, hk, rowk);
+      int it = 0;
+      for (; it < n_it; ++it) {
+        const int h = hk * G + it / per_h;
+        const int rowq = b * p.Lq + (i_lo + it % per_h) * kT;
+        if (!mbar_wait(qdo_empty, (it & 1) ^ 1u, abort_flag, p.status, 40)) break;
+        mbar_arrive_expect_tx(qdo_full, 2 * kTileBytes);
+        tma_load_3d(sQ, &tmQ, qdo_full, 0, h, rowq);
+        tma_load_3d(sQ + 16384, &tmQ, qdo_full, 64, h, rowq);
+        tma_load_3d(sdO, &tmdO, qdo_full, 0, h, rowq);
+        tma_load_3d(sdO + 16384, &tmdO, qdo_full, 64, h, rowq);
+      }
+      mbar_wait(qdo_empty, (it & 1) ^ 1u, nullptr, p.status, 41);   // drain the last load
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_it > 0) {
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), adO = smem_u32(sdO);
+      const uint32_t aPT = smem_u32(sPT), adST = smem_u32(sdST);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, 42);
+      for (int it = 0; ok && it < n_it; ++it) {
+        const uint32_t ph = it & 1;
+        if (!(ok = mbar_wait(qdo_full, ph, abort_flag, p.status, 43))) break;
+        if (it > 0 && !(ok = mbar_wait(dq_empty, ph ^ 1u, abort_flag, p.status, 44))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) umma_bf16(tmem + 0, kmaj_desc(aK, k), kmaj_desc(aQ, k), ID_KK, k > 0);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) umma_bf16(tmem + 128, kmaj_desc(aV, k), kmaj_desc(adO, k), ID_KK, k > 0);
+        umma_commit(st_full);
+        if (!(ok = mbar_wait(pt_full, ph, abort_flag, p.status, 45))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_bf16(tmem + 256, kmaj_desc(aPT, k), mnmaj_desc(adO, k), ID_KM, (it > 0 || k > 0) ? 1u : 0u);
+        if (!(ok = mbar_wait(dst_full, ph, abort_flag, p.status, 46))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_bf16(tmem + 384, kmaj_desc(adST, k), mnmaj_desc(aQ, k), ID_KM, (it > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) umma_bf16(tmem + 0, mnmaj_desc(adST, k), mnmaj_desc(aK, k), ID_MM, k > 0);
+        umma_commit(dq_full);
+        umma_commit(qdo_empty);
+        umma_commit(pds_empty);
+      }
+      if (ok) umma_commit(fin);
+    }
+  } else {
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;          // key row within the tile (S^T, dP^T, dK, dV) / query row (dQ)
+    const int kpos = k0 + r;
+    const uint32_t trow = static_cast<uint32_t>(quad * 32) << 16;
+    const float sl2 = p.scale * kLog2e;
+    float gk = 0.f;
+    if (MODE == kRetention) gk = kpos < p.Lk ? p.gcum[(static_cast<int64_t>(b) * p.Hk + hk) * p.Lk + kpos] : 0.f;
+    bool ok = true;
+    for (int it = 0; ok && it < n_it; ++it) {
+      const uint32_t ph = it & 1;
+      const int h = hk * G + it / per_h;
+      const int q0 = (i_lo + it % per_h) * kT;
+      const int64_t hq_base = (static_cast<int64_t>(b) * p.Hq + h) * p.Lq;
+      const bool full_tile = (q0 + kT <= p.Lq) && (k0 + kT <= p.Lk) &&
+                             (!p.causal || q0 + p.q_offset >= k0 + kT - 1) &&
+                             (p.window <= 0 || q0 + kT - 1 + p.q_offset < k0 + p.window);
+      if (!(ok = mbar_wait(st_full, ph, abort_flag, p.status, 47))) break;
+      tc_fence_after();
+      if (!(ok = mbar_wait(pds_empty, ph ^ 1u, abort_flag, p.status, 48))) break;
+      // ---- P^T
+#pragma unroll 1
+      for (int c = 0; c < kT; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + 0 + trow + c, v);
+        tmem_ld_wait();
+        float pv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int q = q0 + c + i;
+          const bool valid = full_tile || (q < p.Lq && key_valid(p, q + p.q_offset, kpos));
+          float x = 0.f;
+          if (valid) {
+            if (MODE == kSoftmax) x = exp2f(__uint_as_float(v[i]) * sl2 - __ldg(p.lse + hq_base + q) * kLog2e);
+            else x = __uint_as_float(v[i]) * p.scale * __expf(__ldg(p.gcum + hq_base + q) - gk);
+          }
+          pv[i] = x;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(sPT + sw_off(r, (c >> 3) + j)) =
+              make_uint4(pack_bf16(pv[8 * j], pv[8 * j + 1]), pack_bf16(pv[8 * j + 2], pv[8 * j + 3]),
+                         pack_bf16(pv[8 * j + 4], pv[8 * j + 5]), pack_bf16(pv[8 * j + 6], pv[8 * j + 7]));
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pt_full);
+      // ---- dS^T (scale folded in)
+#pragma unroll 1
+      for (int c = 0; c < kT; c += 32) {
+        uint32_t dp[32];
+        tmem_ld32(tmem + 128 + trow + c, dp);
+        uint32_t sv[32];
+        if (MODE == kSoftmax) tmem_ld32(tmem + 0 + trow + c, sv);
+        tmem_ld_wait();
+        float dsv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int q = q0 + c + i;
+          const bool valid = full_tile || (q < p.Lq && key_valid(p, q + p.q_offset, kpos));
+          float x = 0.f;
+          if (valid) {
+            if (MODE == kSoftmax) {
+              const float pr = exp2f(__uint_as_float(sv[i]) * sl2 - __ldg(p.lse + hq_base + q) * kLog2e);
+              x = pr * (__uint_as_float(dp[i]) - __ldg(p.delta + hq_base + q)) * p.scale;
+            } else {
+              x = __uint_as_float(dp[i]) * p.scale * __expf(__ldg(p.gcum + hq_base + q) - gk);
+            }
+          }
+          dsv[i] = x;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(sdST + sw_off(r, (c >> 3) + j)) =
+              make_uint4(pack_bf16(dsv[8 * j], dsv[8 * j + 1]), pack_bf16(dsv[8 * j + 2], dsv[8 * j + 3]),
+                         pack_bf16(dsv[8 * j + 4], dsv[8 * j + 5]), pack_bf16(dsv[8 * j + 6], dsv[8 * j + 7]));
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dst_full);
+      // ---- dQ tile (TMEM lane = query row) -> fp32 atomics
+      if (!(ok = mbar_wait(dq_full, ph, abort_flag, p.status, 49))) break;
+      tc_fence_after();
+      const int qrow = q0 + r;
+      float* dqr = p.dq_acc + ((static_cast<int64_t>(b) * p.Lq + min(qrow, p.Lq - 1)) * p.Hq + h) * kD;
+#pragma unroll 1
+      for (int c = 0; c < kD; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + 0 + trow + c, v);
+        tmem_ld_wait();
+        if (qrow < p.Lq) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            atomicAdd(reinterpret_cast<float4*>(dqr + c + j),
+                      make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                                  __uint_as_float(v[j + 3])));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_empty);
+    }
+    // ---- dK, dV
+    const bool have = ok && n_it > 0 && mbar_wait(fin, 0, abort_flag, p.status, 50);
+    if (have) tc_fence_after();
+    const int64_t orow = ((static_cast<int64_t>(b) * p.Lk + min(kpos, p.Lk - 1)) * p.Hk + hk) * kD;
+#pragma unroll 1
+    for (int which = 0; which < 2; ++which) {
+      __nv_bfloat16* dst = (which == 0 ? p.dK : p.dV) + orow;
+      const uint32_t col = which == 0 ? 384u : 256u;
+#pragma unroll 1
+      for (int c = 0; c < kD; c += 32) {
+        uint32_t v[32];
+        if (have) {
+          tmem_ld32(tmem + col + trow + c, v);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0u;
+        }
+        if (kpos < p.Lk) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(dst + c + 8 * j) =
+                make_uint4(pack_bf16(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1])),
+                           pack_bf16(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3])),
+                           pack_bf16(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5])),
+                           pack_bf16(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7])));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// rowdot[b, h, t] = sum_d X[b, t, h, d] * Y[b, t, h, d] (fp32); one warp per (b, t, h)
+__global__ void rowdot_kernel(const __nv_bfloat16* __restrict__ X, const __nv_bfloat16* __restrict__ Y,
+                              float* __restrict__ out, int B, int L, int H, float* __restrict__ sub_from) {
+  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= static_cast<int64_t>(B) * L * H) return;
+  const int h = static_cast<int>(wid % H);
+  const int64_t bt = wid / H;
+  const int t = static_cast<int>(bt % L);
+  const int b = static_cast<int>(bt / L);
+  const int64_t off = wid * kD + lane * 4;
+  const uint2 xu = *reinterpret_cast<const uint2*>(X + off);
+  const uint2 yu = *reinterpret_cast<const uint2*>(Y + off);
+  const float2 x0 = unpack_bf16(xu.x), x1 = unpack_bf16(xu.y), y0 = unpack_bf16(yu.x), y1 = unpack_bf16(yu.y);
+  float s = x0.x * y0.x + x0.y * y0.y + x1.x * y1.x + x1.y * y1.y;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) {
+    const int64_t idx = (static_cast<int64_t>(b) * H + h) * L + t;
+    out[idx] = sub_from != nullptr ? sub_from[idx] - s : s;
+  }
+}
+
+__global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, int64_t n) {
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (i + 4 <= n) {
+    const float4 v = *reinterpret_cast<const float4*>(x + i);
+    *reinterpret_cast<uint2*>(y + i) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+  } else {
+    for (int64_t j = i; j < n; ++j) y[j] = __float2bfloat16_rn(x[j]);
+  }
+}
+
+constexpr int kFwdSmem = 6 * kTileBytes + 256 + 1024;
+constexpr int kBwdSmem = 6 * kTileBytes + 256 + 1024;
+
+void check_qkv(const at::Tensor& t, const char* name) {
+  FYB_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 4 && t.size(3) == kD && t.stride(3) == 1,
+            std::string(name) + ": bf16 [B, L, H, 128] with contiguous last dim expected");
+  FYB_CHECK(t.stride(0) == t.size(1) * t.stride(1) || t.size(0) == 1,
+            std::string(name) + ": batch stride must equal L x token stride");
+  FYB_CHECK(t.stride(1) % 8 == 0 && t.stride(2) % 8 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+            std::string(name) + ": strides must be multiples of 8 elements, base 16-byte aligned");
+}
+
+CUtensorMap tmap_heads(const at::Tensor& t) {
+  return make_tmap_3d(t.data_ptr(), kD, t.size(2), t.size(0) * t.size(1), t.stride(2), t.stride(1), kT);
+}
+
+template <typename K>
+void set_smem(K kern, int bytes) {
+  FYB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+}
+
+}  // namespace
+
+// -------------------------------------------------------------------------------------------------------- host API
+
+std::vector<at::Tensor> attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, bool causal,
+                                      int64_t window, double scale) {
+  check_qkv(q, "q");
+  check_qkv(k, "k");
+  check_qkv(v, "v");
+  const int B = (int)q.size(0), Lq = (int)q.size(1), Hq = (int)q.size(2), Lk = (int)k.size(1), Hk = (int)k.size(2);
+  FYB_CHECK(k.size(0) == B && v.size(0) == B && v.size(1) == Lk && v.size(2) == Hk && Hq % Hk == 0,
+            "attention_fwd: shape mismatch");
+  c10::cuda::CUDAGuard guard(q.device());
+  auto o = at::empty({B, Lq, Hq, kD}, q.options());
+  auto lse = at::empty({B, Hq, Lq}, q.options().dtype(at::kFloat));
+  if (B == 0 || Lq == 0) return {o, lse};
+  AttnParams p{B, Lq, Lk, Hq, Hk, Lk - Lq, (int)window, causal ? 1 : 0, (float)scale,
+               reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), lse.data_ptr<float>(), nullptr, status_ptr()};
+  const CUtensorMap tq = tmap_heads(q), tk = tmap_heads(k), tv = tmap_heads(v);
+  static bool init = false;
+  if (!init) {
+    set_smem(attn_fwd_kernel<kSoftmax>, kFwdSmem);
+    init = true;
+  }
+  const int grid = B * Hq * ((Lq + kT - 1) / kT);
+  attn_fwd_kernel<kSoftmax><<<grid, kAttnThreads, kFwdSmem, cur_stream()>>>(tq, tk, tv, p);
+  check_launch("attn_fwd");
+  return {o, lse};
+}
+
+std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                      const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, bool causal,
+                                      int64_t window, double scale) {
+  check_qkv(q, "q");
+  check_qkv(k, "k");
+  check_qkv(v, "v");
+  FYB_CHECK(dout.is_contiguous() && o.is_contiguous() && dout.sizes() == q.sizes(), "attention_bwd: dout/o");
+  const int B = (int)q.size(0), Lq = (int)q.size(1), Hq = (int)q.size(2), Lk = (int)k.size(1), Hk = (int)k.size(2);
+  c10::cuda::CUDAGuard guard(q.device());
+  auto delta = at::empty({B, Hq, Lq}, q.options().dtype(at::kFloat));
+  auto dq_acc = at::zeros({B, Lq, Hq, kD}, q.options().dtype(at::kFloat));
+  auto dk = at::empty({B, Lk, Hk, kD}, q.options());
+  auto dv = at::empty({B, Lk, Hk, kD}, q.options());
+  auto dq = at::empty({B, Lq, Hq, kD}, q.options());
+  if (B == 0 || Lq == 0) return {dq.zero_(), dk.zero_(), dv.zero_()};
+  const int64_t rows = (int64_t)B * Lq * Hq;
+  rowdot_kernel<<<(rows * 32 + 255) / 256, 256, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()),
+      delta.data_ptr<float>(), B, Lq, Hq, nullptr);
+  check_launch("attn_bwd_delta");
+  AttnBwdParams p{B, Lq, Lk, Hq, Hk, Lk - Lq, (int)window, causal ? 1 : 0, (float)scale, lse.data_ptr<float>(),
+                  delta.data_ptr<float>(), nullptr, dq_acc.data_ptr<float>(),
+                  reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()),
+                  status_ptr()};
+  const CUtensorMap tq = tmap_heads(q), tk = tmap_heads(k), tv = tmap_heads(v), tdo = tmap_heads(dout);
+  static bool init = false;
+  if (!init) {
+    set_smem(attn_bwd_kernel<kSoftmax>, kBwdSmem);
+    init = true;
+  }
+  const int grid = B * Hk * ((Lk + kT - 1) / kT);
+  attn_bwd_kernel<kSoftmax><<<grid, kAttnThreads, kBwdSmem, cur_stream()>>>(tq, tk, tv, tdo, p);
+  check_launch("attn_bwd");
+  const int64_t n = dq.numel();
+  f32_to_bf16_kernel<<<(n / 4 + 255) / 256 + 1, 256, 0, cur_stream()>>>(
+      dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), n);
+  check_launch("attn_bwd_dq");
+  return {dq, dk, dv};
+}
+
+at::Tensor retention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& gcum) {
+  check_qkv(q, "q");
+  check_qkv(k, "k");
+  check_qkv(v, "v");
+  const int B = (int)q.size(0), L = (int)q.size(1), H = (int)q.size(2);
+  FYB_CHECK(k.sizes() == q.sizes() && v.sizes() == q.sizes(), "retention_fwd: q/k/v shapes differ");
+  FYB_CHECK(gcum.scalar_type() == at::kFloat && gcum.is_contiguous() && gcum.dim() == 3 && gcum.size(0) == B &&
+                gcum.size(1) == H && gcum.size(2) == L,
+            "retention_fwd: gcum must be contiguous fp32 [B, H, L]");
+  c10::cuda::CUDAGuard guard(q.device());
+  auto o = at::empty({B, L, H, kD}, q.options());
+  if (B == 0 || L == 0) return o;
+  AttnParams p{B, L, L, H, H, 0, 0, 1, (float)(1.0 / std::sqrt((double)kD)),
+               reinterpret_cast<__nv_bfloat16*>(o.data_ptr()), nullptr, gcum.data_ptr<float>(), status_ptr()};
+  const CUtensorMap tq = tmap_heads(q), tk = tmap_heads(k), tv = tmap_heads(v);
+  static bool init = false;
+  if (!init) {
+    set_smem(attn_fwd_kernel<kRetention>, kFwdSmem);
+    init = true;
+  }
+  const int grid = B * H * ((L + kT - 1) / kT);
+  attn_fwd_kernel<kRetention><<<grid, kAttnThreads, kFwdSmem, cur_stream()>>>(tq, tk, tv, p);
+  check_launch("retention_fwd");
+  return o;
+}
+
+std::vector<at::Tensor> retention_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                      const at::Tensor& v, const at::Tensor& gcum, const at::Tensor& o) {
+  check_qkv(q, "q");
+  check_qkv(k, "k");
+  check_qkv(v, "v");
+  FYB_CHECK(dout.is_contiguous() && o.is_contiguous() && dout.sizes() == q.sizes(), "retention_bwd: dout/o");
+  const int B = (int)q.size(0), L = (int)q.size(1), H = (int)q.size(2);
+  c10::cuda::CUDAGuard guard(q.device());
+  auto dgo = at::empty({B, H, L}, q.options().dtype(at::kFloat));
+  auto dg = at::empty({B, H, L}, q.options().dtype(at::kFloat));
+  auto dq_acc = at::zeros({B, L, H, kD}, q.options().dtype(at::kFloat));
+  auto dk = at::empty({B, L, H, kD}, q.options());
+  auto dv = at::empty({B, L, H, kD}, q.options());
+  auto dq = at::empty({B, L, H, kD}, q.options());
+  if (B == 0 || L == 0) return {dq.zero_(), dk.zero_(), dv.zero_(), dg.zero_()};
+  const int64_t rows = (int64_t)B * L * H;
+  rowdot_kernel<<<(rows * 32 + 255) / 256, 256, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()),
+      dgo.data_ptr<float>(), B, L, H, nullptr);
+  check_launch("retention_bwd_dot");
+  AttnBwdParams p{B, L, L, H, H, 0, 0, 1, (float)(1.0 / std::sqrt((double)kD)), nullptr, nullptr,
+                  gcum.data_ptr<float>(), dq_acc.data_ptr<float>(),
+                  reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()),
+                  status_ptr()};
+  const CUtensorMap tq = tmap_heads(q), tk = tmap_heads(k), tv = tmap_heads(v), tdo = tmap_heads(dout);
+  static bool init = false;
+  if (!init) {
+    set_smem(attn_bwd_kernel<kRetention>, kBwdSmem);
+    init = true;
+  }
+  const int grid = B * H * ((L + kT - 1) / kT);
+  attn_bwd_kernel<kRetention><<<grid, kAttnThreads, kBwdSmem, cur_stream()>>>(tq, tk, tv, tdo, p);
+  check_launch("retention_bwd");
+  // dG = dO.O - V.dV ; v may be strided -> use a contiguous copy only if needed
+  at::Tensor vc = v.is_contiguous() ? v : v.contiguous();
+  rowdot_kernel<<<(rows * 32 + 255) / 256, 256, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dv.data_ptr()),
+      dg.data_ptr<float>(), B, L, H, dgo.data_ptr<float>());
+  check_launch("retention_bwd_dg");
+  const int64_t n = dq.numel();
+  f32_to_bf16_kernel<<<(n / 4 + 255) / 256 + 1, 256, 0, cur_stream()>>>(
+      dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), n);
+  check_launch("retention_bwd_dq");
+  return {dq, dk, dv, dg};
+}
+
+}  // namespace fyb

@@ -29,6 +29,14 @@ void adam_step(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor
                const at::Tensor& hyper, const at::Tensor& factor, double b1, double b2, double eps, double wd,
                bool adamw);
 at::Tensor sq_norm(const at::Tensor& x);
+std::vector<at::Tensor> attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, bool causal,
+                                      int64_t window, double scale);
+std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                      const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, bool causal,
+                                      int64_t window, double scale);
+at::Tensor retention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& gcum);
+std::vector<at::Tensor> retention_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                      const at::Tensor& v, const at::Tensor& gcum, const at::Tensor& o);
 
 // one status word per device, allocated once (zero = ok)
 int* status_ptr() {
@@ -74,5 +82,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ignore"), py::arg("out") = py::none());
   m.def("adam_step", &fyb::adam_step);
   m.def("sq_norm", &fyb::sq_norm);
+  m.def("attention_fwd", &fyb::attention_fwd);
+  m.def("attention_bwd", &fyb::attention_bwd);
+  m.def("retention_fwd", &fyb::retention_fwd);
+  m.def("retention_bwd", &fyb::retention_bwd);
   m.def("status", &fyb::status_tensor, "device status word of the kernels with bounded waits");
 }

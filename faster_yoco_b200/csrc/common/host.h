@@ -27,7 +27,20 @@ namespace fyb {
                                " at " + __FILE__ + ":" + std::to_string(__LINE__));                  \
   } while (0)
 
+// Driver-API calls need the primary context current on the calling thread. Threads that only ever called
+// cudaGetDevice (autograd's device threads, for instance) may have none, so bind it once per thread.
+inline void ensure_context() {
+  thread_local bool bound = false;
+  if (!bound) {
+    int d;
+    FYB_CUDA(cudaGetDevice(&d));
+    FYB_CUDA(cudaSetDevice(d));
+    bound = true;
+  }
+}
+
 inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  ensure_context();
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (fn == nullptr) {
     void* p = nullptr;

@@ -200,8 +200,8 @@ __global__ void subln_swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dout, 
   const bool valid = hrow < static_cast<int64_t>(T) * H;
   const int64_t t = valid ? hrow / H : 0;
   const int h = valid ? static_cast<int>(hrow % H) : 0;
-  const int64_t ooff = t * (static_cast<int64_t>(H) * D) + h * D + sub * 8;
-  const int64_t goff = t * ldg + h * D + sub * 8;
+  const int64_t ooff = t * (static_cast<int64_t>(H) * D) + h * D + sub * 8;   // o, dout, d_o, dg: contiguous
+  const int64_t goff = t * ldg + h * D + sub * 8;                              // g: strided view
   float f[8], gv[8], dv[8], dn[8];
   float dot = 0.f;
   float r = 0.f;
@@ -219,7 +219,7 @@ __global__ void subln_swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dout, 
       dn[i] = bf16_round(gv[i] * s * dv[i]);
       dot += dn[i] * f[i] * r;
     }
-    store8(dg + goff, dgo);
+    store8(dg + ooff, dgo);
   }
 #pragma unroll
   for (int s = TPR / 2; s > 0; s >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, s);

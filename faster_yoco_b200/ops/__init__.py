@@ -183,12 +183,16 @@ class _NativeRope(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         cos, sin = ctx.saved_tensors
+        if dy.stride(-1) != 1 or any(st % 8 for st in dy.stride()[:-1]):
+            dy = dy.contiguous()
         return _C().rope_fwd(dy, cos, sin, True), None, None
 
 
 def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     """x: [B, L, H, D] (any strides with a contiguous last dim); returns a contiguous [B, L, H, D]."""
     if native_on(x):
+        if x.stride(-1) != 1 or any(st % 8 for st in x.stride()[:-1]):
+            x = x.contiguous()
         return _NativeRope.apply(x, cos, sin)
     return ref.apply_rope(x, cos, sin)
 
@@ -233,13 +237,13 @@ class _NativeRetention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, gcum):
         o = _C().retention_fwd(q, k, v, gcum)
-        ctx.save_for_backward(q, k, v, gcum)
+        ctx.save_for_backward(q, k, v, gcum, o)
         return o
 
     @staticmethod
     def backward(ctx, do):
-        q, k, v, gcum = ctx.saved_tensors
-        dq, dk, dv, dg = _C().retention_bwd(do.contiguous(), q, k, v, gcum)
+        q, k, v, gcum, o = ctx.saved_tensors
+        dq, dk, dv, dg = _C().retention_bwd(do.contiguous(), q, k, v, gcum, o)
         return dq, dk, dv, dg
 
 
@@ -250,7 +254,7 @@ def retention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, gt: torch.Tenso
     q, k, v: [B, L, H, D] (token-major, any strides with a contiguous last dim); gt: [B, L, H] per-step log decay
     (logsigmoid / normalizer, any float dtype). Returns o: [B, L, H, D] contiguous."""
     B, L, H, D = q.shape
-    if native_on(q) and _native.has("retention_fwd"):
+    if native_on(q) and D == 128:
         gcum = gt.float().transpose(1, 2).cumsum(-1).contiguous()      # [B, H, L] fp32
         return _NativeRetention.apply(q, k, v, gcum)
     qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
@@ -300,7 +304,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
               window: Optional[int] = None) -> torch.Tensor:
     """q: [B, Lq, Hq, D], k/v: [B, Lk, Hk, D] -> [B, Lq, Hq, D]; scale 1/sqrt(D); window as flash-attn (w-1, 0)."""
     scale = q.shape[-1] ** -0.5
-    if native_on(q) and _native.has("attention_fwd"):
+    if native_on(q) and q.shape[-1] == 128:
         return _NativeAttention.apply(q, k, v, causal, window, scale)
     if q.is_cuda and _flash():
         ws = (window - 1, 0) if window is not None else (-1, -1)

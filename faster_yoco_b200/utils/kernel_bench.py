@@ -1,0 +1,139 @@
+"""Per-kernel microbenchmarks: the sm_100a kernels against the library baselines (cuBLAS, flash-attn) on the
+YOCO-3B shapes, timed with CUDA events after warm-up, inputs rotated through a pool larger than L2.
+
+    python -m faster_yoco_b200.utils.kernel_bench [--only gemm|attn|ret]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+def _time(fn, iters=20, warmup=5):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def _pool(make, bytes_each):
+    n = max(2, int(math.ceil(2 * L2_BYTES / max(bytes_each, 1))))
+    n = min(n, 16)
+    return [make() for _ in range(n)]
+
+
+def gemm_shapes():
+    T, d, f, V = 2048, 3072, 8192, 100288
+    # (name, M, N, K, a_mn, b_mn): forward (x W^T), dgrad (dy W), wgrad (dy^T x)
+    out = []
+    for name, n_out, n_in in [("qkvg", 4 * d + 24, d), ("out_proj", d, d), ("fc1_gate", 2 * f, d), ("fc2", d, f),
+                              ("kv_proj", 2048, d), ("output_proj", V, d)]:
+        out.append((name + ".fwd", T, n_out, n_in, False, False))
+        out.append((name + ".dgrad", T, n_in, n_out, False, True))
+        out.append((name + ".wgrad", n_out, n_in, T, True, True))
+    return out
+
+
+def bench_gemm(results):
+    from faster_yoco_b200 import ops
+    dev = torch.device("cuda")
+    for name, M, N, K, a_mn, b_mn in gemm_shapes():
+        a_shape = (K, M) if a_mn else (M, K)
+        b_shape = (K, N) if b_mn else (N, K)
+        bytes_each = 2 * (M * K + N * K)
+        pool = _pool(lambda: (torch.randn(a_shape, device=dev, dtype=torch.bfloat16),
+                              torch.randn(b_shape, device=dev, dtype=torch.bfloat16)), bytes_each)
+        c = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        it = [0]
+
+        def ours():
+            a, b = pool[it[0] % len(pool)]
+            it[0] += 1
+            ops._C().gemm(a, b, c, a_mn, b_mn, None)
+
+        def cublas():
+            a, b = pool[it[0] % len(pool)]
+            it[0] += 1
+            A = a.T if a_mn else a
+            B = b if b_mn else b.T
+            torch.matmul(A, B, out=c)
+
+        t_ours, t_cub = _time(ours), _time(cublas)
+        fl = 2.0 * M * N * K
+        results.append({"kernel": "gemm", "shape": name, "M": M, "N": N, "K": K, "ours_ms": t_ours,
+                        "cublas_ms": t_cub, "ours_tflops": fl / t_ours / 1e9, "cublas_tflops": fl / t_cub / 1e9})
+
+
+def bench_attention(results, L=2048, Hq=24, Hk=8, B=1):
+    from faster_yoco_b200 import ops
+    dev = torch.device("cuda")
+    ops.set_backend("native")
+    q = torch.randn(B, L, Hq, 128, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(B, L, Hk, 128, device=dev, dtype=torch.bfloat16)
+    v = torch.randn(B, L, Hk, 128, device=dev, dtype=torch.bfloat16)
+    do = torch.randn_like(q)
+    C = ops._C()
+    sc = 128 ** -0.5
+    o, lse = C.attention_fwd(q, k, v, True, 0, sc)
+    t_f = _time(lambda: C.attention_fwd(q, k, v, True, 0, sc))
+    t_b = _time(lambda: C.attention_bwd(do, q, k, v, o, lse, True, 0, sc))
+    fl = 4.0 * B * Hq * L * L * 128 / 2
+    r = {"kernel": "attention_causal_gqa", "L": L, "Hq": Hq, "Hk": Hk, "fwd_ms": t_f, "bwd_ms": t_b,
+         "fwd_tflops": fl / t_f / 1e9, "bwd_tflops": 2.5 * fl / t_b / 1e9}
+    try:
+        from flash_attn import flash_attn_func
+        qq, kk, vv = q.clone().requires_grad_(), k.clone().requires_grad_(), v.clone().requires_grad_()
+        r["flash_attn_fwd_ms"] = _time(lambda: flash_attn_func(q, k, v, causal=True))
+        oo = flash_attn_func(qq, kk, vv, causal=True)
+        r["flash_attn_fwdbwd_ms"] = _time(lambda: torch.autograd.grad(flash_attn_func(qq, kk, vv, causal=True),
+                                                                      (qq, kk, vv), do))
+    except Exception as e:  # pragma: no cover
+        r["flash_attn"] = repr(e)[:100]
+    results.append(r)
+
+
+def bench_retention(results, L=2048, H=24, B=1):
+    from faster_yoco_b200 import ops
+    dev = torch.device("cuda")
+    q = torch.randn(B, L, H, 128, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(B, L, H, 128, device=dev, dtype=torch.bfloat16)
+    v = torch.randn(B, L, H, 128, device=dev, dtype=torch.bfloat16)
+    g = (torch.nn.functional.logsigmoid(torch.randn(B, H, L, device=dev)) / 16).cumsum(-1).contiguous()
+    do = torch.randn_like(q)
+    C = ops._C()
+    o = C.retention_fwd(q, k, v, g)
+    t_f = _time(lambda: C.retention_fwd(q, k, v, g))
+    t_b = _time(lambda: C.retention_bwd(do, q, k, v, g, o))
+    fl = 4.0 * B * H * L * L * 128 / 2
+    results.append({"kernel": "retention_parallel", "L": L, "H": H, "fwd_ms": t_f, "bwd_ms": t_b,
+                    "fwd_tflops": fl / t_f / 1e9, "bwd_tflops": 2.5 * fl / t_b / 1e9})
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--only", default=None)
+    a = p.parse_args()
+    res = []
+    if a.only in (None, "gemm"):
+        bench_gemm(res)
+    if a.only in (None, "attn"):
+        bench_attention(res)
+    if a.only in (None, "ret"):
+        bench_retention(res)
+    for r in res:
+        print(json.dumps(r))
+
+
+if __name__ == "__main__":
+    main()
