@@ -37,6 +37,17 @@ std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& 
 at::Tensor retention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& gcum);
 std::vector<at::Tensor> retention_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                       const at::Tensor& v, const at::Tensor& gcum, const at::Tensor& o);
+std::vector<at::Tensor> ipc_alloc(int64_t nbytes);
+int64_t ipc_open(const at::Tensor& handle_bytes);
+void ipc_close(int64_t ptr);
+void flag_barrier(const std::vector<int64_t>& peer_flags, const at::Tensor& my_flags, int64_t rank, int64_t slot,
+                  int64_t epoch);
+void reduce_owner(const std::vector<int64_t>& peer_grads, at::Tensor& out, int64_t base, int64_t n, at::Tensor& part,
+                  at::Tensor& sq);
+void gather_segments(const std::vector<int64_t>& peer_params, at::Tensor& dst, const at::Tensor& segs, int64_t rank,
+                     int64_t ctas);
+void mailbox_put(const std::vector<int64_t>& peer_boxes, const at::Tensor& vals, int64_t rank, int64_t slot_base);
+void mailbox_sum(const at::Tensor& box, at::Tensor& out, int64_t world, int64_t slot_base);
 
 // one status word per device, allocated once (zero = ok)
 int* status_ptr() {
@@ -86,5 +97,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_bwd", &fyb::attention_bwd);
   m.def("retention_fwd", &fyb::retention_fwd);
   m.def("retention_bwd", &fyb::retention_bwd);
+  m.def("ipc_alloc", &fyb::ipc_alloc, "cudaMalloc'd byte buffer + its CUDA IPC handle");
+  m.def("ipc_open", &fyb::ipc_open);
+  m.def("ipc_close", &fyb::ipc_close);
+  m.def("flag_barrier", &fyb::flag_barrier);
+  m.def("reduce_owner", &fyb::reduce_owner);
+  m.def("gather_segments", &fyb::gather_segments);
+  m.def("mailbox_put", &fyb::mailbox_put);
+  m.def("mailbox_sum", &fyb::mailbox_sum);
   m.def("status", &fyb::status_tensor, "device status word of the kernels with bounded waits");
 }

@@ -1,0 +1,272 @@
+// NVLink peer-memory collectives for ZeRO data parallelism (one process per GPU, buffers shared with CUDA IPC).
+//
+// Reference: the copy-engine reduce-to-owner (yoco/models/decoder/ce_reduce.py: IPC peer mappings,
+// cudaMemcpyAsync pushes into per-owner staging slots, a 1-element NCCL all-reduce as barrier, then the Triton
+// _sum_slots FP32 rank-order sum x 1/world -> bf16) and the in-place BF16 parameter all-gather
+// (yoco/tasks/zero1_fast.py:224-226). Here the SMs do the transfers themselves from inside the kernels that consume
+// them, with no staging copy:
+//
+//  * flag_barrier     : epoch-tagged all-to-all flags (st.release.sys to every peer, bounded ld.acquire.sys spin)
+//  * reduce_owner     : the owner reads every rank's bf16 gradient slice over NVLink in rank order, sums in FP32,
+//                       scales by 1/world, writes bf16 in place and emits per-CTA partial sums of squares (the
+//                       grad-norm partial) -- the reduce-scatter fused with the norm
+//  * gather_segments  : pulls a list of (offset, length, owner) ranges of the flat parameter buffer from their
+//                       owners (the all-gather, per layer so it can run ahead of the forward pass)
+//  * allreduce_small  : a few fp32 values summed in rank order through peer slots (loss, sample size, norm)
+//
+// Every spin is bounded (FYB_WAIT_NS); a timeout records a status word and the kernel returns.
+#include <ATen/ATen.h>
+
+#include <cstring>
+#include <vector>
+
+#include "common/host.h"
+#include "common/ptx.cuh"
+
+namespace fyb {
+namespace {
+
+constexpr int kMaxWorld = 8;
+
+struct PeerPtrs {
+  const void* p[kMaxWorld];
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* addr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// flags layout on every rank: [slots][kMaxWorld] uint32; rank r writes epoch into flags_q[slot][r] on every peer q
+__global__ void flag_barrier_kernel(PeerPtrs peer_flags, uint32_t* my_flags, int rank, int world, int slot,
+                                    uint32_t epoch, int* status) {
+  if (threadIdx.x < world) {
+    __threadfence_system();
+    uint32_t* f = reinterpret_cast<uint32_t*>(const_cast<void*>(peer_flags.p[threadIdx.x])) + slot * kMaxWorld + rank;
+    st_release_sys(f, epoch);
+  }
+  __syncthreads();
+  if (threadIdx.x < world) {
+    const uint32_t* f = my_flags + slot * kMaxWorld + threadIdx.x;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t it = 0;
+    while (static_cast<int32_t>(ld_acquire_sys(f) - epoch) < 0) {
+      if ((++it & 255u) == 0u && globaltimer_ns() - t0 > FYB_WAIT_NS) {
+        record_status(status, kPeerTimeout, 200 + slot);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  __threadfence_system();
+}
+
+// owner-side reduction of its segment [base, base + n): out = bf16(sum_r g_r / world) in rank order; per-CTA
+// partial sums of squares of the bf16 result in part[blockIdx.x]
+__global__ void reduce_owner_kernel(PeerPtrs grads, __nv_bfloat16* out, int64_t base, int64_t n, int world,
+                                    float inv_world, float* part) {
+  float ss = 0.f;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 8;
+  for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < n; i += stride) {
+    if (i + 8 <= n) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      uint4 u[kMaxWorld];
+#pragma unroll
+      for (int r = 0; r < kMaxWorld; ++r)
+        if (r < world) u[r] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(grads.p[r]) + base + i);
+#pragma unroll
+      for (int r = 0; r < kMaxWorld; ++r) {
+        if (r < world) {
+          const uint32_t w[4] = {u[r].x, u[r].y, u[r].z, u[r].w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = unpack_bf16(w[k]);
+            acc[2 * k] += f.x;
+            acc[2 * k + 1] += f.y;
+          }
+        }
+      }
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float a = bf16_round(acc[2 * k] * inv_world), b = bf16_round(acc[2 * k + 1] * inv_world);
+        ss += a * a + b * b;
+        o[k] = pack_bf16(a, b);
+      }
+      *reinterpret_cast<uint4*>(out + base + i) = make_uint4(o[0], o[1], o[2], o[3]);
+    } else {
+      for (int64_t j = i; j < n; ++j) {
+        float acc = 0.f;
+        for (int r = 0; r < world; ++r) acc += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(grads.p[r])[base + j]);
+        const float a = bf16_round(acc * inv_world);
+        ss += a * a;
+        out[base + j] = __float2bfloat16_rn(a);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+    part[blockIdx.x] = t;
+  }
+}
+
+__global__ void sum_partials_kernel(const float* __restrict__ part, int P, float* __restrict__ out) {
+  __shared__ float red[1024];
+  float s = 0.f;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) s += part[i];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out[0] = red[0];
+}
+
+// segments: [nseg][3] int64 = (element offset, element count, owner rank); each CTA walks segments in 16-byte
+// vectors (offsets and counts are multiples of 8 elements by construction of the flat layout)
+__global__ void gather_segments_kernel(PeerPtrs src, __nv_bfloat16* dst, const int64_t* __restrict__ segs, int nseg,
+                                       int rank) {
+  for (int s = 0; s < nseg; ++s) {
+    const int64_t off = segs[3 * s], cnt = segs[3 * s + 1];
+    const int owner = static_cast<int>(segs[3 * s + 2]);
+    if (owner == rank) continue;
+    const uint4* sp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(src.p[owner]) + off);
+    uint4* dp = reinterpret_cast<uint4*>(dst + off);
+    const int64_t nv = cnt / 8;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nv;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+      dp[i] = sp[i];
+    const int64_t tail0 = nv * 8;
+    if (blockIdx.x == 0)
+      for (int64_t j = tail0 + threadIdx.x; j < cnt; j += blockDim.x)
+        dst[off + j] = reinterpret_cast<const __nv_bfloat16*>(src.p[owner])[off + j];
+  }
+}
+
+// each rank writes its k values into slot [rank] of every peer's mailbox, then (after a flag barrier) sums the
+// world slots of its own mailbox in rank order
+__global__ void mailbox_put_kernel(PeerPtrs boxes, const float* __restrict__ vals, int k, int rank, int world,
+                                   int slot_base) {
+  for (int q = 0; q < world; ++q) {
+    float* box = reinterpret_cast<float*>(const_cast<void*>(boxes.p[q])) + slot_base + rank * 32;
+    for (int i = threadIdx.x; i < k; i += blockDim.x) box[i] = vals[i];
+  }
+}
+
+__global__ void mailbox_sum_kernel(const float* __restrict__ box, float* __restrict__ out, int k, int world,
+                                   int slot_base) {
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    float s = 0.f;
+    for (int r = 0; r < world; ++r) s += box[slot_base + r * 32 + i];
+    out[i] = s;
+  }
+}
+
+PeerPtrs to_ptrs(const std::vector<int64_t>& v) {
+  FYB_CHECK(static_cast<int>(v.size()) <= kMaxWorld, "at most 8 ranks");
+  PeerPtrs p{};
+  for (size_t i = 0; i < v.size(); ++i) p.p[i] = reinterpret_cast<const void*>(v[i]);
+  return p;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------------------------------- IPC buffers
+
+// cudaMalloc'd buffer (its own allocation, so its IPC handle maps exactly this range) + the handle bytes
+std::vector<at::Tensor> ipc_alloc(int64_t nbytes) {
+  ensure_context();
+  void* p = nullptr;
+  FYB_CUDA(cudaMalloc(&p, static_cast<size_t>(nbytes)));
+  FYB_CUDA(cudaMemset(p, 0, static_cast<size_t>(nbytes)));
+  cudaIpcMemHandle_t h;
+  FYB_CUDA(cudaIpcGetMemHandle(&h, p));
+  int dev;
+  FYB_CUDA(cudaGetDevice(&dev));
+  auto t = at::from_blob(
+      p, {nbytes}, [](void* q) { cudaFree(q); }, at::TensorOptions().dtype(at::kByte).device(at::kCUDA, dev));
+  auto hb = at::empty({static_cast<int64_t>(sizeof(h))}, at::TensorOptions().dtype(at::kByte));
+  std::memcpy(hb.data_ptr(), &h, sizeof(h));
+  return {t, hb};
+}
+
+int64_t ipc_open(const at::Tensor& handle_bytes) {
+  ensure_context();
+  FYB_CHECK(handle_bytes.numel() == static_cast<int64_t>(sizeof(cudaIpcMemHandle_t)), "ipc_open: bad handle");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle_bytes.data_ptr(), sizeof(h));
+  void* p = nullptr;
+  FYB_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t ptr) { FYB_CUDA(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr))); }
+
+// ------------------------------------------------------------------------------------------------------- kernels
+
+void flag_barrier(const std::vector<int64_t>& peer_flags, const at::Tensor& my_flags, int64_t rank, int64_t slot,
+                  int64_t epoch) {
+  const int world = static_cast<int>(peer_flags.size());
+  flag_barrier_kernel<<<1, 32, 0, cur_stream()>>>(to_ptrs(peer_flags), reinterpret_cast<uint32_t*>(my_flags.data_ptr()),
+                                                  static_cast<int>(rank), world, static_cast<int>(slot),
+                                                  static_cast<uint32_t>(epoch), status_ptr());
+  check_launch("flag_barrier");
+}
+
+int reduce_ctas() { return std::min(num_sms() * 2, 1024); }
+
+// reduce [base, base+n) of the flat gradient buffers into out (this rank's buffer) and sq[0] = sum of squares
+void reduce_owner(const std::vector<int64_t>& peer_grads, at::Tensor& out, int64_t base, int64_t n, at::Tensor& part,
+                  at::Tensor& sq) {
+  const int world = static_cast<int>(peer_grads.size());
+  FYB_CHECK(base % 8 == 0, "reduce_owner: segment base must be a multiple of 8 elements");
+  const int P = static_cast<int>(part.numel());
+  FYB_CHECK(P >= 1 && P <= 1024, "reduce_owner: 1..1024 partials");
+  reduce_owner_kernel<<<P, 256, 0, cur_stream()>>>(to_ptrs(peer_grads),
+                                                   reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), base, n, world,
+                                                   1.0f / static_cast<float>(world), part.data_ptr<float>());
+  check_launch("reduce_owner");
+  sum_partials_kernel<<<1, 1024, 0, cur_stream()>>>(part.data_ptr<float>(), P, sq.data_ptr<float>());
+  check_launch("reduce_owner_sum");
+}
+
+void gather_segments(const std::vector<int64_t>& peer_params, at::Tensor& dst, const at::Tensor& segs, int64_t rank,
+                     int64_t ctas) {
+  FYB_CHECK(segs.is_cuda() && segs.scalar_type() == at::kLong && segs.dim() == 2 && segs.size(1) == 3,
+            "gather_segments: segs must be a device int64 [n, 3]");
+  if (segs.size(0) == 0) return;
+  gather_segments_kernel<<<static_cast<int>(ctas), 512, 0, cur_stream()>>>(
+      to_ptrs(peer_params), reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()), segs.data_ptr<int64_t>(),
+      static_cast<int>(segs.size(0)), static_cast<int>(rank));
+  check_launch("gather_segments");
+}
+
+void mailbox_put(const std::vector<int64_t>& peer_boxes, const at::Tensor& vals, int64_t rank, int64_t slot_base) {
+  const int world = static_cast<int>(peer_boxes.size());
+  FYB_CHECK(vals.numel() <= 32 && vals.scalar_type() == at::kFloat, "mailbox_put: at most 32 fp32 values");
+  mailbox_put_kernel<<<1, 32, 0, cur_stream()>>>(to_ptrs(peer_boxes), vals.data_ptr<float>(),
+                                                 static_cast<int>(vals.numel()), static_cast<int>(rank), world,
+                                                 static_cast<int>(slot_base));
+  check_launch("mailbox_put");
+}
+
+void mailbox_sum(const at::Tensor& box, at::Tensor& out, int64_t world, int64_t slot_base) {
+  mailbox_sum_kernel<<<1, 32, 0, cur_stream()>>>(box.data_ptr<float>(), out.data_ptr<float>(),
+                                                 static_cast<int>(out.numel()), static_cast<int>(world),
+                                                 static_cast<int>(slot_base));
+  check_launch("mailbox_sum");
+}
+
+}  // namespace fyb

@@ -1,0 +1,123 @@
+"""NVLink peer-memory communication for ZeRO: CUDA-IPC shared buffers and the fused collectives of ``csrc/comm.cu``.
+
+Each rank ``cudaMalloc``s its flat parameter buffer, flat gradient buffer, a flag array and a small mailbox, exports
+IPC handles, and opens every peer's handles once (the reference does the same for its copy-engine path,
+yoco/models/decoder/ce_reduce.py:77-98). After that, the collectives of an update are plain kernel launches that
+read and write peer memory directly over NVLink / NVSwitch:
+
+* ``reduce_to_owner``: flag barrier (all ranks finished the backward), then the owner's kernel sums its segment of
+  every rank's gradient buffer in FP32 rank order, divides by world, writes BF16 in place and returns the segment's
+  sum of squares (the grad-norm partial) -- one pass instead of NCCL reduce + scale kernel + norm kernel;
+* ``all_gather``: flag barrier (all owners finished Adam), then every rank pulls the other segments;
+* ``all_reduce_vector``: up to 32 fp32 values summed in rank order through the mailboxes (loss / sample size /
+  grad norm) -- no NCCL launch on the update path.
+
+The order in which ranks call these is identical by construction, so one flag slot with a monotonically increasing
+epoch serves every barrier. All waits are bounded on the device (a timeout sets the status word read by
+:class:`faster_yoco_b200.utils.faults.DeviceStatus`).
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+
+
+class PeerComm:
+    def __init__(self, group=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("peer-memory collectives support at most 8 ranks (one NVSwitch domain)")
+        self.C = ops._C()
+        self.dev = torch.device("cuda", torch.cuda.current_device())
+        self._keep: List[torch.Tensor] = []
+        self._opened: List[int] = []
+        self.flags, self.peer_flags = self.share_bytes(16 * 8 * 4)
+        self.box, self.peer_box = self.share_bytes(2 * 8 * 32 * 4)
+        self.box_f = self.box.view(torch.float32)
+        self.epoch = 0
+        self.calls = 0
+        self.peers: Dict[str, List[int]] = {}
+        P = min(2 * torch.cuda.get_device_properties(self.dev).multi_processor_count, 1024)
+        self.part = torch.zeros(P, dtype=torch.float32, device=self.dev)
+        self.sq = torch.zeros(1, dtype=torch.float32, device=self.dev)
+        self._gather_segs: Dict[Tuple, torch.Tensor] = {}
+
+    # ------------------------------------------------------------------------------------------------- buffers
+    def share_bytes(self, nbytes: int) -> Tuple[torch.Tensor, List[int]]:
+        t, h = self.C.ipc_alloc(int(nbytes))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, h.tolist(), group=self.group)
+        ptrs = []
+        for r in range(self.world):
+            if r == self.rank:
+                ptrs.append(t.data_ptr())
+            else:
+                p = self.C.ipc_open(torch.tensor(handles[r], dtype=torch.uint8))
+                self._opened.append(p)
+                ptrs.append(p)
+        self._keep.append(t)
+        return t, ptrs
+
+    def alloc(self, name: str, numel: int, dtype: torch.dtype) -> torch.Tensor:
+        """A shared buffer of `numel` elements; peers' addresses of the same buffer are kept under `name`."""
+        esz = torch.empty((), dtype=dtype).element_size()
+        t, ptrs = self.share_bytes(numel * esz)
+        self.peers[name] = ptrs
+        return t.view(dtype)[:numel]
+
+    # ------------------------------------------------------------------------------------------------- collectives
+    def barrier(self):
+        self.epoch += 1
+        self.C.flag_barrier(self.peer_flags, self.flags, self.rank, 0, self.epoch)
+
+    def reduce_to_owner(self, grad_flat: torch.Tensor, seg: int, used: Optional[int] = None) -> torch.Tensor:
+        """Average the gradient buffers of all ranks over this rank's segment, in place. Returns the segment's
+        sum of squares after the BF16 rounding (device tensor [1])."""
+        n = seg if used is None else used
+        self.barrier()
+        self.C.reduce_owner(self.peers["grad"], grad_flat, self.rank * seg, n, self.part, self.sq)
+        return self.sq
+
+    def all_gather(self, flat: torch.Tensor, seg: int, used: Optional[List[int]] = None):
+        self.barrier()
+        key = (seg, tuple(used) if used else None)
+        segs = self._gather_segs.get(key)
+        if segs is None:
+            rows = [[r * seg, (used[r] if used else seg), r] for r in range(self.world) if r != self.rank]
+            segs = torch.tensor(rows, dtype=torch.int64, device=self.dev).view(-1, 3)
+            self._gather_segs[key] = segs
+        sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
+        self.C.gather_segments(self.peers["param"], flat, segs, self.rank, sms * 2)
+
+    def gather_ranges(self, flat: torch.Tensor, segs: torch.Tensor, ctas: int = 64):
+        """Pull explicit (offset, count, owner) ranges of the shared parameter buffer (per-layer prefetch)."""
+        self.C.gather_segments(self.peers["param"], flat, segs, self.rank, ctas)
+
+    def all_reduce_vector(self, v: torch.Tensor) -> torch.Tensor:
+        """Sum of a small fp32 vector over ranks, rank order (returns a new tensor)."""
+        v = v.reshape(-1).float().contiguous()
+        if v.numel() > 32:
+            raise ValueError("all_reduce_vector: at most 32 values")
+        base = (self.calls % 2) * 8 * 32
+        self.calls += 1
+        self.C.mailbox_put(self.peer_box, v, self.rank, base)
+        self.barrier()
+        out = torch.empty_like(v)
+        self.C.mailbox_sum(self.box_f, out, self.world, base)
+        return out
+
+    def close(self):
+        torch.cuda.synchronize()
+        for p in self._opened:
+            try:
+                self.C.ipc_close(p)
+            except Exception:
+                pass
+        self._opened.clear()
+        self._keep.clear()

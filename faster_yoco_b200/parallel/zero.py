@@ -58,7 +58,9 @@ class Entry:
 class FlatParams:
     """The flat BF16 parameter buffer + flat gradient buffer; model parameters become views of it."""
 
-    def __init__(self, named_params, world: int, rank: int, device, dtype=torch.bfloat16):
+    def __init__(self, named_params, world: int, rank: int, device, dtype=torch.bfloat16, allocator=None):
+        """allocator(name, numel, dtype) -> tensor: where the flat buffers live (peer-shared memory for the fused
+        NVLink collectives); default torch.zeros on `device`."""
         named = [(n, p) for n, p in named_params if p.requires_grad]
         self.world, self.rank, self.device, self.dtype = world, rank, torch.device(device), dtype
         owners = greedy_partition([p.numel() for _, p in named], world)
@@ -69,8 +71,12 @@ class FlatParams:
             fill[r] = _round_up(fill[r] + p.numel(), ALIGN)
         self.seg = max(_round_up(max(fill), 1024), 1024)
         self.used = fill                                     # used (aligned) length of each owner's segment
-        self.flat = torch.zeros(world * self.seg, dtype=dtype, device=self.device)
-        self.grad_flat = torch.zeros(world * self.seg, dtype=dtype, device=self.device)
+        if allocator is None:
+            self.flat = torch.zeros(world * self.seg, dtype=dtype, device=self.device)
+            self.grad_flat = torch.zeros(world * self.seg, dtype=dtype, device=self.device)
+        else:
+            self.flat = allocator("param", world * self.seg, dtype)
+            self.grad_flat = allocator("grad", world * self.seg, dtype)
         self.entries: List[Entry] = []
         self.by_param: Dict[int, Entry] = {}
         with torch.no_grad():
@@ -166,13 +172,13 @@ class ZeroOptimizer:
 
     # ---------------------------------------------------------------------------------------------------------
     def reduce_grads(self):
-        """Average the gradient buffer over ranks into each owner's segment (BF16)."""
+        """Average the gradient buffer over ranks into each owner's segment (BF16). Returns the owned segment's sum
+        of squares when the reduction produced it (fused path), else None."""
         fp = self.flat
         if fp.world == 1:
-            return
+            return None
         if self.comm == "fused" and self.p2p is not None:
-            self.p2p.reduce_to_owner(fp.grad_flat, fp.seg)
-            return
+            return self.p2p.reduce_to_owner(fp.grad_flat, fp.seg, fp.used[fp.rank])
         out = fp.grad_segment()
         if dist.get_backend(self.group) == "nccl":
             dist.reduce_scatter_tensor(out, fp.grad_flat, op=dist.ReduceOp.AVG, group=self.group)
@@ -180,13 +186,14 @@ class ZeroOptimizer:
             tmp = torch.empty_like(out)
             dist.reduce_scatter_tensor(tmp, fp.grad_flat, op=dist.ReduceOp.SUM, group=self.group)
             out.copy_(tmp / fp.world)
+        return None
 
     def all_gather_params(self):
         fp = self.flat
         if fp.world == 1:
             return
         if self.comm == "fused" and self.p2p is not None:
-            self.p2p.all_gather(fp.flat, fp.seg)
+            self.p2p.all_gather(fp.flat, fp.seg, fp.used)
             return
         dist.all_gather_into_tensor(fp.flat, fp.param_segment(), group=self.group)
 
@@ -204,15 +211,17 @@ class ZeroOptimizer:
     def finish(self):
         self.num_updates += 1
 
-    def device_step(self, sample_size: torch.Tensor) -> torch.Tensor:
+    def device_step(self, sample_size: torch.Tensor, sq: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Clip + Adam + parameter exchange, device work only (capturable). sample_size: device scalar summed
-        over ranks. Returns the grad norm (device scalar)."""
+        over ranks; sq: this owner's sum of squares if the reduction already produced it. Returns the grad norm."""
         from .. import ops
         fp = self.flat
         g16 = fp.grad_segment()
         factor = fp.world / torch.where(sample_size > 0, sample_size, torch.ones_like(sample_size)).float()
         native = ops.native_on(g16)
-        if native:
+        if sq is not None:
+            sq = sq.clone()
+        elif native:
             sq = ops._C().sq_norm(g16)
         else:
             sq = g16.float().pow(2).sum().reshape(1)

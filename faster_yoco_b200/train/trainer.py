@@ -36,13 +36,15 @@ class Trainer:
         self.pad_idx = pad_idx
         self.rank, self.world = D.rank(), D.world()
         self.group = group
-        self.flat = FlatParams(model.named_parameters(), self.world, self.rank, self.device,
-                               dtype=next(model.parameters()).dtype)
-        self.flat.direct_grads = self.device.type == "cuda" and ops.get_backend() == "native"
-        self.zero = ZeroOptimizer(self.flat, optim_cfg, comm=comm, group=group, stage=zero_stage)
+        p2p = None
         if comm == "fused" and self.world > 1 and self.device.type == "cuda":
             from ..parallel.p2p import PeerComm
-            self.zero.p2p = PeerComm(group)
+            p2p = PeerComm(group)
+        self.flat = FlatParams(model.named_parameters(), self.world, self.rank, self.device,
+                               dtype=next(model.parameters()).dtype, allocator=p2p.alloc if p2p else None)
+        self.flat.direct_grads = self.device.type == "cuda" and ops.get_backend() == "native"
+        self.zero = ZeroOptimizer(self.flat, optim_cfg, comm=comm, group=group, stage=zero_stage)
+        self.zero.p2p = p2p
         self.sched = PolynomialDecaySchedule(optim_cfg.lr, optim_cfg.warmup_updates, optim_cfg.total_num_update,
                                              optim_cfg.end_learning_rate, optim_cfg.power)
         self.pending = PendingChecks(self.device.type == "cuda")
@@ -92,10 +94,13 @@ class Trainer:
         loss = self._forward_backward(src, tgt, ntok)
         self.flat.collect_grads()          # p.grad -> slot for gradients not written there by a native op
         loss_all, ss_all = self._reduce_stats(loss, ntok)
-        self.zero.reduce_grads()
-        gnorm = self.zero.device_step(ss_all)
-        consistent = (grad_norm_consistent(gnorm, self.rank, self.world, self.group)
-                      if self.check_consistency else torch.isfinite(gnorm))
+        sq = self.zero.reduce_grads()
+        gnorm = self.zero.device_step(ss_all, sq)
+        if self.check_consistency:
+            reduce = self.zero.p2p.all_reduce_vector if self.zero.p2p is not None else None
+            consistent = grad_norm_consistent(gnorm, self.rank, self.world, self.group, reduce=reduce)
+        else:
+            consistent = torch.isfinite(gnorm)
         return loss_all, ss_all, gnorm, consistent
 
     def train_step(self, batch) -> torch.Tensor:

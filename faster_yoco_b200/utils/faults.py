@@ -43,13 +43,17 @@ class PendingChecks:
             raise FloatingPointError("gradients are Nan/Inf")
 
 
-def grad_norm_consistent(grad_norm: torch.Tensor, rank: int, world: int, group=None) -> torch.Tensor:
-    """Trainer._check_grad_norms as a device bool: every rank's norm equal to rank 0's within 1e-6 relative."""
+def grad_norm_consistent(grad_norm: torch.Tensor, rank: int, world: int, group=None, reduce=None) -> torch.Tensor:
+    """Trainer._check_grad_norms as a device bool: every rank's norm equal to rank 0's within 1e-6 relative.
+    `reduce` (optional) sums a small fp32 vector over ranks (the peer-memory mailbox); default NCCL/gloo."""
     if world == 1:
         return torch.isfinite(grad_norm).reshape(())
     buf = torch.zeros(world, dtype=torch.float32, device=grad_norm.device)
     buf[rank] = grad_norm.float()
-    dist.all_reduce(buf, group=group)
+    if reduce is not None:
+        buf = reduce(buf)
+    else:
+        dist.all_reduce(buf, group=group)
     return torch.isfinite(buf).all() & ((buf - buf[0]).abs().max() / (buf[0] + 1e-6) < 1e-6)
 
 
