@@ -10,8 +10,11 @@
 #include <ATen/ATen.h>
 #include <c10/util/Optional.h>
 
+#include <mutex>
+
 #include "common/host.h"
 #include "common/ptx.cuh"
+#include "noalloc.h"
 
 namespace fyb {
 namespace {
@@ -358,3 +361,85 @@ std::vector<at::Tensor> subln_swiglu_bwd(const at::Tensor& dout, const at::Tenso
 }
 
 }  // namespace fyb
+
+// ------------------------------------------------------------------------------------------------------------------
+// Allocation-free RMSNorm backward (declared and documented in noalloc.h; no counterpart in the reference).
+
+namespace {
+constexpr int kNoAllocMaxCtas = 64;
+constexpr int kNoAllocMaxN = 8192;
+}  // namespace
+
+// the partial sums of the weight gradient: one row of N floats per block, at most 64 blocks (2 MiB per device)
+static __device__ __align__(256) float g_fyb_rms_bwd_scratch[kNoAllocMaxCtas * kNoAllocMaxN];
+
+namespace {
+std::mutex g_noalloc_mu;
+float* g_noalloc_scratch[64] = {nullptr};
+
+// device address of the scratch array for the current device (looked up once per device, then cached)
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 5;
+  if (dev < 0 || dev >= 64) return 5;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_scratch[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_fyb_rms_bwd_scratch) != cudaSuccess || p == nullptr) return 4;
+    g_noalloc_scratch[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_scratch[dev];
+  return 0;
+}
+}  // namespace
+
+extern "C" int fyb_rms_norm_bwd_noalloc(const void* dy, const void* x, const void* w, const float* rstd, void* dx,
+                                        void* dw, int64_t M, int64_t N, cudaStream_t stream) {
+  using namespace fyb;
+  if (N <= 0 || N > kNoAllocMaxN) return 1;
+  if (N % 8 != 0) return 2;
+  if (M < 0) return 2;
+  if ((w == nullptr) != (dw == nullptr)) return 2;
+  for (const void* p : {dy, x, static_cast<const void*>(dx)})
+    if (p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 != 0) return 3;
+  if (w != nullptr && reinterpret_cast<uintptr_t>(w) % 16 != 0) return 3;
+  if (rstd == nullptr && M > 0) return 3;
+  float* part = nullptr;
+  if (w != nullptr) {
+    const int rc = noalloc_scratch(&part);
+    if (rc != 0) return rc;
+  }
+  if (M == 0) {
+    if (dw != nullptr && cudaMemsetAsync(dw, 0, static_cast<size_t>(N) * 2, stream) != cudaSuccess) return 6;
+    return 0;
+  }
+  const int P = static_cast<int>(std::min<int64_t>(M, kNoAllocMaxCtas));
+  const int rows_per = static_cast<int>((M + P - 1) / P);
+  const int grid = static_cast<int>((M + rows_per - 1) / rows_per);
+  const size_t shm = w != nullptr ? static_cast<size_t>(N) * sizeof(float) : 0;
+  rms_bwd_kernel<<<grid, kNormThreads, shm, stream>>>(
+      static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x),
+      static_cast<const __nv_bfloat16*>(w), rstd, static_cast<__nv_bfloat16*>(dx), part, static_cast<int>(M),
+      static_cast<int>(N), rows_per);
+  if (cudaGetLastError() != cudaSuccess) return 6;
+  if (w != nullptr) {
+    col_sum_kernel<<<static_cast<int>((N + 255) / 256), 256, 0, stream>>>(part, static_cast<__nv_bfloat16*>(dw), grid,
+                                                                         static_cast<int>(N));
+    if (cudaGetLastError() != cudaSuccess) return 6;
+  }
+  return 0;
+}
+
+extern "C" const char* fyb_noalloc_strerror(int code) {
+  switch (code) {
+    case 0: return "ok";
+    case 1: return "N is beyond the static scratch limit: at most 8192 columns";
+    case 2: return "invalid size: N must be a positive multiple of 8, M >= 0, and w / dw both given or both NULL";
+    case 3: return "a pointer is NULL or not 16-byte aligned";
+    case 4: return "cudaGetSymbolAddress of the static scratch array failed";
+    case 5: return "no valid current CUDA device";
+    case 6: return "kernel launch failed";
+    default: return "unknown error code";
+  }
+}
+
