@@ -3,19 +3,26 @@
 // sliding_window_attention.py:65) and the parallel form of gated retention (gate_recurrent.py:266-276).
 //
 // One kernel family, two score transforms:
-//   kSoftmax   : P = softmax(scale * Q K^T) with an online max; O accumulated in registers
-//   kRetention : P = (scale * Q K^T) * exp(G_q - G_k) (G = fp32 cumsum of the per-step log decays), causal;
-//                no normalisation, so O accumulates directly in TMEM across key tiles
+//   kSoftmax   : P = softmax(scale * Q K^T), online max with lazy rescaling: P is formed against a reference max
+//                m_ref and O (in TMEM) and the row sum are rescaled only when the row max exceeds m_ref by more
+//                than 2^8, so the common tile needs no O round trip
+//   kRetention : P = (scale * Q K^T) * exp(G_q - G_k) (G = fp32 cumsum of the per-step log decays), causal. For a
+//                key tile entirely before the query tile the decay factors into exp(G_q - G_e) * exp(G_e - G_k)
+//                (G_e = last key of the tile; both factors <= 1): one exp per row plus a per-key column factor
+//                staged in shared memory. Diagonal tiles use the exact per-element exp.
 //
-// Forward CTA (6 warps) = one (batch, head, 128-query tile):
-//   warp 0     TMA producer: Q once, K/V tiles (128 keys x 128 dims, 128B swizzle) in a 2-stage ring
-//   warp 1     UMMA issuer: S = Q K^T into one of two TMEM S buffers, then O_blk = P V (P from shared memory)
-//   warps 2..5 one thread per query row: read S (tcgen05.ld), mask, exponentiate, write P (bf16, swizzled K-major)
+// Forward CTA (10 warps) = one (batch, head, 128-query tile):
+//   warp 0     producer: Q once, K/V tiles (128 keys x 128 dims, 128B swizzle) in a 2-stage TMA ring, and the
+//              retention gate tiles (G_k, column factors) into shared memory
+//   warp 1     UMMA issuer: S = Q K^T into one of two TMEM S buffers; O += P V into one TMEM O accumulator
+//   warps 2..9 two threads per query row (TMEM lane quadrant = warp % 4, column half = (warp - 2) / 4): read S
+//              (tcgen05.ld), mask, exponentiate, write P (bf16, swizzled K-major) for the PV MMA
 //
 // Backward CTA = one (batch, kv head, 128-key tile), looping over the query heads of the GQA group and the query
 // tiles that see this key tile:  S^T = K Q^T, dP^T = V dO^T (TMEM); P^T, dS^T (bf16, shared memory);
 // dV += P^T dO, dK += dS^T Q (TMEM accumulators), dQ_tile = dS K (TMEM -> fp32 atomics into a dQ accumulator).
-// The UMMA descriptors read the same swizzled dS^T tile as K-major (for dK) and as MN-major (for dQ).
+// The UMMA descriptors read the same swizzled dS^T tile as K-major (for dK) and as MN-major (for dQ). The per-query
+// values (lse and delta, or the gates) of each query tile are staged in shared memory by the producer warp.
 //
 // Retention gate gradient, from dG_i = sum_j dP_ij P_ij - sum_k dP_ki P_ki:  dG_i = dO_i . O_i - V_i . dV_i
 // (the two sums collapse into row dot products), computed by the small post kernel.
@@ -30,10 +37,12 @@ namespace {
 constexpr int kD = 128;      // head dim
 constexpr int kT = 128;      // tile rows (queries / keys)
 constexpr int kTileBytes = kT * kD * 2;   // 32 KB: two 16 KB swizzle-atom columns (dims 0-63, 64-127)
-constexpr int kAttnThreads = 192;
+constexpr int kAttnThreads = 320;         // producer, MMA issuer, 8 score warps
+constexpr int kCompute = 8;               // score warps (mbarrier arrival count)
 enum Mode : int { kSoftmax = 0, kRetention = 1 };
 
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.0f;      // lazy rescale threshold (factor 256)
 
 struct AttnParams {
   int B, Lq, Lk, Hq, Hk;
@@ -52,7 +61,7 @@ __device__ __forceinline__ uint32_t sw_off(int r, int c) {
   return static_cast<uint32_t>((c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4));
 }
 
-// S/O tile descriptors for a 128-wide K dimension split in two 64-wide swizzle atoms (K-major)
+// descriptors for a 128-wide K dimension split in two 64-wide swizzle atoms (K-major)
 __device__ __forceinline__ uint64_t kmaj_desc(uint32_t base, int k16) {
   return sw128_desc(base + (k16 >> 2) * 16384 + (k16 & 3) * 32, 16, 1024);
 }
@@ -87,6 +96,15 @@ __device__ __forceinline__ bool key_valid(const P& p, int qa, int k) {
   return true;
 }
 
+__device__ __forceinline__ void store_row8(uint8_t* tile, int r, int chunk0, const float* v) {
+  // 32 consecutive values of row r starting at 16-byte chunk chunk0 -> 4 swizzled 16-byte stores
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4*>(tile + sw_off(r, chunk0 + j)) =
+        make_uint4(pack_bf16(v[8 * j], v[8 * j + 1]), pack_bf16(v[8 * j + 2], v[8 * j + 3]),
+                   pack_bf16(v[8 * j + 4], v[8 * j + 5]), pack_bf16(v[8 * j + 6], v[8 * j + 7]));
+}
+
 // ======================================================================================================== forward
 
 template <int MODE>
@@ -99,19 +117,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sK = sQ + kTileBytes;             // 2 stages
   uint8_t* sV = sK + 2 * kTileBytes;         // 2 stages
   uint8_t* sP = sV + 2 * kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kTileBytes);
+  float* sG = reinterpret_cast<float*>(sP + kTileBytes);   // [2][128] key gates (retention)
+  float* sCF = sG + 2 * kT;                                 // [2][128] column factors exp(G_e - G_k)
+  float* sL = sCF + 2 * kT;                                 // [2][128] row-sum halves (softmax)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sL + 2 * kT);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* s_empty = bars + 11; // [2]
-  uint64_t* p_full = bars + 13;
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* k_empty = bars + 3;   // [2]
+  uint64_t* v_full = bars + 5;    // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2]
+  uint64_t* s_empty = bars + 11;  // [2]  (kCompute arrivals)
+  uint64_t* p_full = bars + 13;   //      (kCompute arrivals)
   uint64_t* p_empty = bars + 14;
-  uint64_t* o_full = bars + 15;  // [2]
-  uint64_t* o_empty = bars + 17; // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  uint64_t* o_full = bars + 15;
+  uint64_t* g_full = bars + 16;   // [2]
+  uint64_t* g_empty = bars + 18;  // [2]  (kCompute arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -123,16 +145,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int q0 = qt * kT;
   const Range rg = kv_range(p, q0);
   const int n = rg.j1 - rg.j0;
+  const float* gbase = MODE == kRetention ? p.gcum + (static_cast<int64_t>(b) * p.Hq + h) * p.Lq : nullptr;
   constexpr uint32_t IDESC_S = idesc_bf16(128, 128, false, false);
   constexpr uint32_t IDESC_O = idesc_bf16(128, 128, false, true);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 19; ++i) mbar_init(&bars[i], 1);
-    mbar_init(&s_empty[0], 4);
-    mbar_init(&s_empty[1], 4);
-    mbar_init(p_full, 4);
-    mbar_init(&o_empty[0], 4);
-    mbar_init(&o_empty[1], 4);
+    for (int i = 0; i < 20; ++i) mbar_init(&bars[i], 1);
+    mbar_init(&s_empty[0], kCompute);
+    mbar_init(&s_empty[1], kCompute);
+    mbar_init(p_full, kCompute);
+    mbar_init(&g_empty[0], kCompute);
+    mbar_init(&g_empty[1], kCompute);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -143,44 +166,73 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;   // S[0] @ col 0, S[1] @ 128, O[0] @ 256, O[1] @ 384
+  const uint32_t tmem = *tmem_slot;   // S[0] @ col 0, S[1] @ 128, O @ 256
 
   if (warp == 0) {
-    if (lane == 0 && n > 0) {
-      const int rowq = b * p.Lq + q0;
-      mbar_arrive_expect_tx(q_full, kTileBytes);
-      tma_load_3d(sQ, &tmQ, q_full, 0, h, rowq);
-      tma_load_3d(sQ + 16384, &tmQ, q_full, 64, h, rowq);
+    // ---------------------------------------------------------------------------------------------- producer
+    if (n > 0) {
+      if (lane == 0) {
+        const int rowq = b * p.Lq + q0;
+        mbar_arrive_expect_tx(q_full, kTileBytes);
+        tma_load_3d(sQ, &tmQ, q_full, 0, h, rowq);
+        tma_load_3d(sQ + 16384, &tmQ, q_full, 64, h, rowq);
+      }
       for (int it = 0; it < n; ++it) {
         const int st = it & 1;
         const uint32_t ph = (it >> 1) & 1;
-        const int rowk = b * p.Lk + (rg.j0 + it) * kT;
-        if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, p.status, 20)) break;
-        mbar_arrive_expect_tx(&k_full[st], kTileBytes);
-        tma_load_3d(sK + st * kTileBytes, &tmK, &k_full[st], 0, hk, rowk);
-        tma_load_3d(sK + st * kTileBytes + 16384, &tmK, &k_full[st], 64, hk, rowk);
-        if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, p.status, 21)) break;
-        mbar_arrive_expect_tx(&v_full[st], kTileBytes);
-        tma_load_3d(sV + st * kTileBytes, &tmV, &v_full[st], 0, hk, rowk);
-        tma_load_3d(sV + st * kTileBytes + 16384, &tmV, &v_full[st], 64, hk, rowk);
+        const int k0 = (rg.j0 + it) * kT;
+        int ok = 1;
+        if (lane == 0) {
+          const int rowk = b * p.Lk + k0;
+          ok = mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, p.status, 20);
+          if (ok) {
+            mbar_arrive_expect_tx(&k_full[st], kTileBytes);
+            tma_load_3d(sK + st * kTileBytes, &tmK, &k_full[st], 0, hk, rowk);
+            tma_load_3d(sK + st * kTileBytes + 16384, &tmK, &k_full[st], 64, hk, rowk);
+            ok = mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, p.status, 21);
+          }
+          if (ok) {
+            mbar_arrive_expect_tx(&v_full[st], kTileBytes);
+            tma_load_3d(sV + st * kTileBytes, &tmV, &v_full[st], 0, hk, rowk);
+            tma_load_3d(sV + st * kTileBytes + 16384, &tmV, &v_full[st], 64, hk, rowk);
+          }
+          if (ok && MODE == kRetention) ok = mbar_wait(&g_empty[st], ph ^ 1u, abort_flag, p.status, 22);
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+        if (MODE == kRetention) {
+          const float ge = gbase[min(k0 + kT, p.Lk) - 1];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int c = lane * 4 + j;
+            const int kk = k0 + c;
+            const float g = kk < p.Lk ? gbase[kk] : 0.f;
+            sG[st * kT + c] = g;
+            sCF[st * kT + c] = kk < p.Lk ? __expf(ge - g) : 0.f;
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&g_full[st]);
+        }
       }
-      // drain the ring before exit
-      for (int it = n; it < n + 2; ++it) {
-        const int st = it & 1;
-        const uint32_t ph = (it >> 1) & 1;
-        mbar_wait(&k_empty[st], ph ^ 1u, nullptr, p.status, 22);
-        mbar_wait(&v_empty[st], ph ^ 1u, nullptr, p.status, 23);
+      if (lane == 0) {   // drain the ring before exit
+        for (int it = n; it < n + 2; ++it) {
+          const int st = it & 1;
+          const uint32_t ph = (it >> 1) & 1;
+          mbar_wait(&k_empty[st], ph ^ 1u, nullptr, p.status, 23);
+          mbar_wait(&v_empty[st], ph ^ 1u, nullptr, p.status, 24);
+        }
       }
     }
   } else if (warp == 1) {
+    // ---------------------------------------------------------------------------------------------- UMMA issuer
     if (lane == 0 && n > 0) {
       const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
-      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, 24);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, 25);
       auto issue_s = [&](int it) -> bool {
         const int st = it & 1;
         const uint32_t ph = (it >> 1) & 1;
-        if (!mbar_wait(&k_full[st], ph, abort_flag, p.status, 25)) return false;
-        if (!mbar_wait(&s_empty[st], ph ^ 1u, abort_flag, p.status, 26)) return false;
+        if (!mbar_wait(&k_full[st], ph, abort_flag, p.status, 26)) return false;
+        if (!mbar_wait(&s_empty[st], ph ^ 1u, abort_flag, p.status, 27)) return false;
         tc_fence_after();
         const uint32_t aK = smem_u32(sK + st * kTileBytes);
 #pragma unroll
@@ -193,23 +245,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       auto issue_pv = [&](int it) -> bool {
         const int st = it & 1;
         const uint32_t ph = (it >> 1) & 1;
-        if (!mbar_wait(p_full, it & 1, abort_flag, p.status, 27)) return false;
-        if (!mbar_wait(&v_full[st], ph, abort_flag, p.status, 28)) return false;
-        uint32_t dst = tmem + 256;
-        if (MODE == kSoftmax) {
-          if (!mbar_wait(&o_empty[st], ph ^ 1u, abort_flag, p.status, 29)) return false;
-          dst += st * 128;
-        }
+        if (!mbar_wait(p_full, it & 1, abort_flag, p.status, 28)) return false;
+        if (!mbar_wait(&v_full[st], ph, abort_flag, p.status, 29)) return false;
         tc_fence_after();
         const uint32_t aV = smem_u32(sV + st * kTileBytes);
 #pragma unroll
-        for (int k = 0; k < kT / 16; ++k) {
-          const uint32_t acc = (MODE == kRetention) ? ((it > 0 || k > 0) ? 1u : 0u) : (k > 0 ? 1u : 0u);
-          umma_bf16(dst, kmaj_desc(aP, k), mnmaj_desc(aV, k), IDESC_O, acc);
-        }
+        for (int k = 0; k < kT / 16; ++k)
+          umma_bf16(tmem + 256, kmaj_desc(aP, k), mnmaj_desc(aV, k), IDESC_O, (it > 0 || k > 0) ? 1u : 0u);
         umma_commit(p_empty);
         umma_commit(&v_empty[st]);
-        if (MODE == kSoftmax) umma_commit(&o_full[st]);
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -217,66 +261,34 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (it + 1 < n) ok = issue_s(it + 1);
         if (ok) ok = issue_pv(it);
       }
-      if (MODE == kRetention && ok) umma_commit(&o_full[0]);
+      if (ok) umma_commit(o_full);
     }
   } else {
-    // -------------------------------------------------------------------------------- score / softmax warps
+    // -------------------------------------------------------------------------------------------- score warps
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;                 // query row within the tile
     const int qrow = q0 + r;
+    const bool rowvalid = qrow < p.Lq;
     const int qa = qrow + p.q_offset;               // absolute query position
     const uint32_t trow = static_cast<uint32_t>(quad * 32) << 16;
+    const int c0 = half * 64;                       // this thread's columns of S / P / O
     const float sl2 = p.scale * kLog2e;
-    float m_run = -INFINITY, l_run = 0.f, m_o = -INFINITY;
-    float o_acc[kD];
-    if (MODE == kSoftmax) {
-#pragma unroll
-      for (int i = 0; i < kD; ++i) o_acc[i] = 0.f;
-    }
-    float gq = 0.f;
-    const float* gbase = nullptr;
-    if (MODE == kRetention) {
-      gbase = p.gcum + (static_cast<int64_t>(b) * p.Hq + h) * p.Lq;
-      gq = qrow < p.Lq ? gbase[qrow] : 0.f;
-    }
+    float m_ref = -INFINITY, l_part = 0.f;
+    const float gq = (MODE == kRetention && rowvalid) ? gbase[qrow] : 0.f;
     bool ok = true;
-    // softmax: O block `it` was formed with P scaled by the running max of tile it (m_tile); o_acc is scaled to m_o
-    auto consume_o = [&](int it, float m_tile) {
-      const int st = it & 1;
-      const uint32_t ph = (it >> 1) & 1;
-      if (!mbar_wait(&o_full[st], ph, abort_flag, p.status, 30)) {
-        ok = false;
-        return;
-      }
-      tc_fence_after();
-      const float a = (m_o == -INFINITY) ? 0.f : exp2f(m_o - m_tile);
-#pragma unroll
-      for (int c = 0; c < kD; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(tmem + 256 + st * 128 + trow + c, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o_acc[c + i] = o_acc[c + i] * a + __uint_as_float(v[i]);
-      }
-      m_o = m_tile;
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_empty[st]);
-    };
-    float m_last = -INFINITY;   // running max used for the previous tile's P
     for (int it = 0; ok && it < n; ++it) {
       const int st = it & 1;
       const uint32_t ph = (it >> 1) & 1;
       const int k0 = (rg.j0 + it) * kT;
-      if (!mbar_wait(&s_full[st], ph, abort_flag, p.status, 31)) {
-        ok = false;
-        break;
-      }
+      const bool full_tile = rowvalid ? ((k0 + kT <= p.Lk) && (!p.causal || k0 + kT - 1 <= q0 + p.q_offset) &&
+                                         (p.window <= 0 || k0 > min(q0 + kT, p.Lq) - 1 + p.q_offset - p.window))
+                                      : false;
+      if (MODE == kRetention && !(ok = mbar_wait(&g_full[st], ph, abort_flag, p.status, 30))) break;
+      if (!(ok = mbar_wait(&s_full[st], ph, abort_flag, p.status, 31))) break;
       tc_fence_after();
-      const bool full_tile = (k0 + kT <= p.Lk) && (!p.causal || k0 + kT - 1 <= q0 + p.q_offset) &&
-                             (p.window <= 0 || k0 > min(q0 + kT, p.Lq) - 1 + p.q_offset - p.window);
-      float m_new = m_run;
       if (MODE == kSoftmax) {
+        // full-row max (both threads of the row compute the same value, so their decisions agree)
         float mx = -INFINITY;
 #pragma unroll
         for (int c = 0; c < kT; c += 32) {
@@ -284,22 +296,38 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tmem_ld32(tmem + st * 128 + trow + c, v);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const bool valid = full_tile || key_valid(p, qa, k0 + c + i);
-            if (valid) mx = fmaxf(mx, __uint_as_float(v[i]));
-          }
+          for (int i = 0; i < 32; ++i)
+            if (full_tile || (rowvalid && key_valid(p, qa, k0 + c + i))) mx = fmaxf(mx, __uint_as_float(v[i]));
         }
-        m_new = fmaxf(m_run, mx * sl2);
-      }
-      // P(it) may only be written once PV(it-1) has read P(it-1)
-      if (!mbar_wait(p_empty, (it & 1) ^ 1u, abort_flag, p.status, 32)) {
-        ok = false;
-        break;
-      }
-      float lsum = 0.f;
-      const float mref = (m_new == -INFINITY) ? 0.f : m_new;
+        const float m_cand = fmaxf(m_ref, mx * sl2);
+        // O may be touched only after PV(it-1) has completed
+        if (!(ok = mbar_wait(p_empty, (it & 1) ^ 1u, abort_flag, p.status, 32))) break;
+        const bool need = m_cand > m_ref + kRescaleLog2;
+        const bool scale_o = need && m_ref != -INFINITY;
+        if (__any_sync(0xffffffffu, scale_o)) {
+          const float f = scale_o ? fast_exp2(m_ref - m_cand) : 1.0f;
+          tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < kT; c += 32) {
+          for (int c = 0; c < 64; c += 32) {
+            uint32_t v[32];
+            tmem_ld32(tmem + 256 + trow + c0 + c, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * f);
+            tmem_st32(tmem + 256 + trow + c0 + c, v);
+          }
+          tmem_st_wait();
+          if (scale_o) l_part *= f;
+        }
+        if (need) m_ref = m_cand;
+      } else {
+        if (!(ok = mbar_wait(p_empty, (it & 1) ^ 1u, abort_flag, p.status, 32))) break;
+      }
+      const bool diag = k0 + kT - 1 >= q0 + p.q_offset;   // retention: tile reaches the query tile
+      const float rf = (MODE == kRetention && !diag) ? __expf(gq - sG[st * kT + kT - 1]) * p.scale : 0.f;
+      const float mref = m_ref == -INFINITY ? 0.f : m_ref;
+#pragma unroll
+      for (int c = c0; c < c0 + 64; c += 32) {
         uint32_t v[32];
         tmem_ld32(tmem + st * 128 + trow + c, v);
         tmem_ld_wait();
@@ -307,28 +335,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int kk = k0 + c + i;
-          const bool valid = full_tile || key_valid(p, qa, kk);
-          float x;
+          const bool valid = full_tile || (rowvalid && key_valid(p, qa, kk));
+          float x = 0.f;
           if (MODE == kSoftmax) {
-            x = valid ? exp2f(__uint_as_float(v[i]) * sl2 - mref) : 0.f;
-            lsum += x;
-          } else {
-            x = valid ? __uint_as_float(v[i]) * p.scale * __expf(gq - __ldg(gbase + kk)) : 0.f;
+            x = valid ? fast_exp2(__uint_as_float(v[i]) * sl2 - mref) : 0.f;
+            l_part += x;
+          } else if (valid) {
+            const float decay = diag ? __expf(gq - sG[st * kT + c + i]) * p.scale : rf * sCF[st * kT + c + i];
+            x = __uint_as_float(v[i]) * decay;
           }
           pv[i] = x;
         }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int chunk = (c >> 3) + j;   // 16-byte chunk index 0..15 of the 256-byte row
-          const uint4 w = make_uint4(pack_bf16(pv[8 * j], pv[8 * j + 1]), pack_bf16(pv[8 * j + 2], pv[8 * j + 3]),
-                                     pack_bf16(pv[8 * j + 4], pv[8 * j + 5]),
-                                     pack_bf16(pv[8 * j + 6], pv[8 * j + 7]));
-          *reinterpret_cast<uint4*>(sP + sw_off(r, chunk)) = w;
-        }
-      }
-      if (MODE == kSoftmax) {
-        l_run = (m_new == -INFINITY) ? 0.f : l_run * exp2f(m_run - m_new) + lsum;
-        m_run = m_new;
+        store_row8(sP, r, c >> 3, pv);
       }
       tc_fence_before();
       fence_proxy_async_smem();
@@ -336,48 +354,41 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (lane == 0) {
         mbar_arrive(&s_empty[st]);
         mbar_arrive(p_full);
-      }
-      if (MODE == kSoftmax) {
-        if (it >= 1) consume_o(it - 1, m_last);
-        m_last = m_run;
+        if (MODE == kRetention) mbar_arrive(&g_empty[st]);
       }
     }
+    // ---------------------------------------------------------------------------------------------- epilogue
+    const bool have = ok && n > 0 && mbar_wait(o_full, 0, abort_flag, p.status, 33);
+    if (have) tc_fence_after();
+    float inv = 1.f;
     if (MODE == kSoftmax) {
-      if (ok && n > 0) consume_o(n - 1, m_last);
-      if (qrow < p.Lq) {
-        const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
-        __nv_bfloat16* orow = p.O + ((static_cast<int64_t>(b) * p.Lq + qrow) * p.Hq + h) * kD;
-#pragma unroll
-        for (int c = 0; c < kD; c += 8)
-          *reinterpret_cast<uint4*>(orow + c) =
-              make_uint4(pack_bf16(o_acc[c] * inv, o_acc[c + 1] * inv), pack_bf16(o_acc[c + 2] * inv, o_acc[c + 3] * inv),
-                         pack_bf16(o_acc[c + 4] * inv, o_acc[c + 5] * inv), pack_bf16(o_acc[c + 6] * inv, o_acc[c + 7] * inv));
+      sL[half * kT + r] = l_part;
+      named_barrier(1, kCompute * 32);
+      const float l_tot = sL[r] + sL[kT + r];
+      inv = l_tot > 0.f ? 1.0f / l_tot : 0.f;
+      if (half == 0 && rowvalid)
         p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.Lq + qrow] =
-            l_run > 0.f ? (m_o + log2f(l_run)) * 0.6931471805599453f : -INFINITY;
+            l_tot > 0.f ? (m_ref + __log2f(l_tot)) * 0.6931471805599453f : -INFINITY;
+    }
+    __nv_bfloat16* orow = p.O + ((static_cast<int64_t>(b) * p.Lq + (rowvalid ? qrow : 0)) * p.Hq + h) * kD;
+#pragma unroll
+    for (int c = c0; c < c0 + 64; c += 32) {
+      uint32_t v[32];
+      if (have) {
+        tmem_ld32(tmem + 256 + trow + c, v);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0u;
       }
-    } else {
-      const bool have = ok && n > 0 && mbar_wait(&o_full[0], 0, abort_flag, p.status, 33);
-      if (have) tc_fence_after();
-      __nv_bfloat16* orow = p.O + ((static_cast<int64_t>(b) * p.Lq + min(qrow, p.Lq - 1)) * p.Hq + h) * kD;
+      if (rowvalid) {
 #pragma unroll
-      for (int c = 0; c < kD; c += 32) {
-        uint32_t v[32];
-        if (have) {
-          tmem_ld32(tmem + 256 + trow + c, v);
-          tmem_ld_wait();
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0u;
-        }
-        if (qrow < p.Lq) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            *reinterpret_cast<uint4*>(orow + c + 8 * j) =
-                make_uint4(pack_bf16(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1])),
-                           pack_bf16(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3])),
-                           pack_bf16(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5])),
-                           pack_bf16(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7])));
-        }
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(orow + c + 8 * j) =
+              make_uint4(pack_bf16(__uint_as_float(v[8 * j]) * inv, __uint_as_float(v[8 * j + 1]) * inv),
+                         pack_bf16(__uint_as_float(v[8 * j + 2]) * inv, __uint_as_float(v[8 * j + 3]) * inv),
+                         pack_bf16(__uint_as_float(v[8 * j + 4]) * inv, __uint_as_float(v[8 * j + 5]) * inv),
+                         pack_bf16(__uint_as_float(v[8 * j + 6]) * inv, __uint_as_float(v[8 * j + 7]) * inv));
       }
     }
   }
@@ -418,24 +429,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sdO = sQ + kTileBytes;
   uint8_t* sPT = sdO + kTileBytes;
   uint8_t* sdST = sPT + kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sdST + kTileBytes);
+  float* sQA = reinterpret_cast<float*>(sdST + kTileBytes);   // softmax: lse * log2(e); retention: G_q
+  float* sQB = sQA + kT;                                      // softmax: delta; retention: exp(G_q - G_e)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sQB + kT);
   uint64_t* kv_full = bars + 0;
   uint64_t* qdo_full = bars + 1;
   uint64_t* qdo_empty = bars + 2;
   uint64_t* st_full = bars + 3;
-  uint64_t* pt_full = bars + 4;
-  uint64_t* dst_full = bars + 5;
+  uint64_t* pt_full = bars + 4;    // kCompute
+  uint64_t* dst_full = bars + 5;   // kCompute
   uint64_t* pds_empty = bars + 6;
   uint64_t* dq_full = bars + 7;
-  uint64_t* dq_empty = bars + 8;
+  uint64_t* dq_empty = bars + 8;   // kCompute
   uint64_t* fin = bars + 9;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* qv_full = bars + 10;
+  uint64_t* qv_empty = bars + 11;  // kCompute
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = (p.Lk + kT - 1) / kT;
   const int nq = (p.Lq + kT - 1) / kT;
-  const int kt = blockIdx.x % nk;
+  const int kt = nk - 1 - (blockIdx.x % nk);
   const int bh = blockIdx.x / nk;
   const int hk = bh % p.Hk, b = bh / p.Hk;
   const int G = p.Hq / p.Hk;
@@ -451,10 +466,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   constexpr uint32_t ID_MM = idesc_bf16(128, 128, true, true);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 10; ++i) mbar_init(&bars[i], 1);
-    mbar_init(pt_full, 4);
-    mbar_init(dst_full, 4);
-    mbar_init(dq_empty, 4);
+    for (int i = 0; i < 12; ++i) mbar_init(&bars[i], 1);
+    mbar_init(pt_full, kCompute);
+    mbar_init(dst_full, kCompute);
+    mbar_init(dq_empty, kCompute);
+    mbar_init(qv_empty, kCompute);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -466,49 +482,77 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;   // S^T/dQ @ 0, dP^T @ 128, dV @ 256, dK @ 384
+  const float g_end = (MODE == kRetention) ? p.gcum[(static_cast<int64_t>(b) * p.Hk + hk) * p.Lk + k_hi] : 0.f;
 
   if (warp == 0) {
-    if (lane == 0 && n_it > 0) {
-      const int rowk = b * p.Lk + k0;
-      mbar_arrive_expect_tx(kv_full, 2 * kTileBytes);
-      tma_load_3d(sK, &tmK, kv_full, 0, hk, rowk);
-      tma_load_3d(sK + 16384, &tmK, kv_full, 64, hk, rowk);
-      tma_load_3d(sV, &tmV, kv_full, 0, hk, rowk);
-      tma_load_3d(sV + 16384, &tmV, kv_full, 64, hk, rowk);
+    if (n_it > 0) {
+      if (lane == 0) {
+        const int rowk = b * p.Lk + k0;
+        mbar_arrive_expect_tx(kv_full, 2 * kTileBytes);
+        tma_load_3d(sK, &tmK, kv_full, 0, hk, rowk);
+        tma_load_3d(sK + 16384, &tmK, kv_full, 64, hk, rowk);
+        tma_load_3d(sV, &tmV, kv_full, 0, hk, rowk);
+        tma_load_3d(sV + 16384, &tmV, kv_full, 64, hk, rowk);
+      }
       int it = 0;
       for (; it < n_it; ++it) {
         const int h = hk * G + it / per_h;
-        const int rowq = b * p.Lq + (i_lo + it % per_h) * kT;
-        if (!mbar_wait(qdo_empty, (it & 1) ^ 1u, abort_flag, p.status, 40)) break;
-        mbar_arrive_expect_tx(qdo_full, 2 * kTileBytes);
-        tma_load_3d(sQ, &tmQ, qdo_full, 0, h, rowq);
-        tma_load_3d(sQ + 16384, &tmQ, qdo_full, 64, h, rowq);
-        tma_load_3d(sdO, &tmdO, qdo_full, 0, h, rowq);
-        tma_load_3d(sdO + 16384, &tmdO, qdo_full, 64, h, rowq);
+        const int q0 = (i_lo + it % per_h) * kT;
+        const int64_t hq_base = (static_cast<int64_t>(b) * p.Hq + h) * p.Lq;
+        int ok = 1;
+        if (lane == 0) {
+          ok = mbar_wait(qdo_empty, (it & 1) ^ 1u, abort_flag, p.status, 40);
+          if (ok) {
+            const int rowq = b * p.Lq + q0;
+            mbar_arrive_expect_tx(qdo_full, 2 * kTileBytes);
+            tma_load_3d(sQ, &tmQ, qdo_full, 0, h, rowq);
+            tma_load_3d(sQ + 16384, &tmQ, qdo_full, 64, h, rowq);
+            tma_load_3d(sdO, &tmdO, qdo_full, 0, h, rowq);
+            tma_load_3d(sdO + 16384, &tmdO, qdo_full, 64, h, rowq);
+            ok = mbar_wait(qv_empty, (it & 1) ^ 1u, abort_flag, p.status, 41);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = lane * 4 + j;
+          const int q = q0 + c;
+          if (MODE == kSoftmax) {
+            sQA[c] = q < p.Lq ? p.lse[hq_base + q] * kLog2e : INFINITY;
+            sQB[c] = q < p.Lq ? p.delta[hq_base + q] : 0.f;
+          } else {
+            const float g = q < p.Lq ? p.gcum[hq_base + q] : 0.f;
+            sQA[c] = g;
+            sQB[c] = q < p.Lq ? __expf(fminf(g - g_end, 0.f)) : 0.f;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(qv_full);
       }
-      mbar_wait(qdo_empty, (it & 1) ^ 1u, nullptr, p.status, 41);   // drain the last load
+      if (lane == 0) mbar_wait(qdo_empty, (it & 1) ^ 1u, nullptr, p.status, 42);   // drain the last load
     }
   } else if (warp == 1) {
     if (lane == 0 && n_it > 0) {
       const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), adO = smem_u32(sdO);
       const uint32_t aPT = smem_u32(sPT), adST = smem_u32(sdST);
-      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, 42);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, 43);
       for (int it = 0; ok && it < n_it; ++it) {
         const uint32_t ph = it & 1;
-        if (!(ok = mbar_wait(qdo_full, ph, abort_flag, p.status, 43))) break;
-        if (it > 0 && !(ok = mbar_wait(dq_empty, ph ^ 1u, abort_flag, p.status, 44))) break;
+        if (!(ok = mbar_wait(qdo_full, ph, abort_flag, p.status, 44))) break;
+        if (it > 0 && !(ok = mbar_wait(dq_empty, ph ^ 1u, abort_flag, p.status, 45))) break;
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k) umma_bf16(tmem + 0, kmaj_desc(aK, k), kmaj_desc(aQ, k), ID_KK, k > 0);
 #pragma unroll
         for (int k = 0; k < 8; ++k) umma_bf16(tmem + 128, kmaj_desc(aV, k), kmaj_desc(adO, k), ID_KK, k > 0);
         umma_commit(st_full);
-        if (!(ok = mbar_wait(pt_full, ph, abort_flag, p.status, 45))) break;
+        if (!(ok = mbar_wait(pt_full, ph, abort_flag, p.status, 46))) break;
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           umma_bf16(tmem + 256, kmaj_desc(aPT, k), mnmaj_desc(adO, k), ID_KM, (it > 0 || k > 0) ? 1u : 0u);
-        if (!(ok = mbar_wait(dst_full, ph, abort_flag, p.status, 46))) break;
+        if (!(ok = mbar_wait(dst_full, ph, abort_flag, p.status, 47))) break;
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k)
@@ -523,94 +567,85 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else {
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;          // key row within the tile (S^T, dP^T, dK, dV) / query row (dQ)
+    const int half = (warp - 2) >> 2;
+    const int r = quad * 32 + lane;          // key row (S^T, dP^T, dK, dV) / query row (dQ) within the tile
     const int kpos = k0 + r;
     const uint32_t trow = static_cast<uint32_t>(quad * 32) << 16;
+    const int c0 = half * 64;                // this thread's query columns of S^T / dP^T and d columns of dQ/dK/dV
     const float sl2 = p.scale * kLog2e;
-    float gk = 0.f;
-    if (MODE == kRetention) gk = kpos < p.Lk ? p.gcum[(static_cast<int64_t>(b) * p.Hk + hk) * p.Lk + kpos] : 0.f;
+    const float gk = (MODE == kRetention && kpos < p.Lk)
+                         ? p.gcum[(static_cast<int64_t>(b) * p.Hk + hk) * p.Lk + kpos] : 0.f;
+    const float rfk = (MODE == kRetention && kpos < p.Lk) ? __expf(g_end - gk) * p.scale : 0.f;
     bool ok = true;
     for (int it = 0; ok && it < n_it; ++it) {
       const uint32_t ph = it & 1;
       const int h = hk * G + it / per_h;
       const int q0 = (i_lo + it % per_h) * kT;
-      const int64_t hq_base = (static_cast<int64_t>(b) * p.Hq + h) * p.Lq;
-      const bool full_tile = (q0 + kT <= p.Lq) && (k0 + kT <= p.Lk) &&
-                             (!p.causal || q0 + p.q_offset >= k0 + kT - 1) &&
+      const bool full_tile = (q0 + kT <= p.Lq) && (kpos < p.Lk) && (!p.causal || q0 + p.q_offset >= k0 + kT - 1) &&
                              (p.window <= 0 || q0 + kT - 1 + p.q_offset < k0 + p.window);
-      if (!(ok = mbar_wait(st_full, ph, abort_flag, p.status, 47))) break;
+      const bool offdiag = q0 + p.q_offset > k_hi;
+      if (!(ok = mbar_wait(qv_full, ph, abort_flag, p.status, 48))) break;
+      if (!(ok = mbar_wait(st_full, ph, abort_flag, p.status, 49))) break;
       tc_fence_after();
-      if (!(ok = mbar_wait(pds_empty, ph ^ 1u, abort_flag, p.status, 48))) break;
-      // ---- P^T
-#pragma unroll 1
-      for (int c = 0; c < kT; c += 32) {
+      if (!(ok = mbar_wait(pds_empty, ph ^ 1u, abort_flag, p.status, 50))) break;
+      float pk[64];
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) {
         uint32_t v[32];
-        tmem_ld32(tmem + 0 + trow + c, v);
+        tmem_ld32(tmem + 0 + trow + c0 + c, v);
         tmem_ld_wait();
-        float pv[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const int q = q0 + c + i;
+          const int cc = c0 + c + i;
+          const int q = q0 + cc;
           const bool valid = full_tile || (q < p.Lq && key_valid(p, q + p.q_offset, kpos));
           float x = 0.f;
           if (valid) {
-            if (MODE == kSoftmax) x = exp2f(__uint_as_float(v[i]) * sl2 - __ldg(p.lse + hq_base + q) * kLog2e);
-            else x = __uint_as_float(v[i]) * p.scale * __expf(__ldg(p.gcum + hq_base + q) - gk);
+            if (MODE == kSoftmax) x = fast_exp2(__uint_as_float(v[i]) * sl2 - sQA[cc]);
+            else x = __uint_as_float(v[i]) * (offdiag ? rfk * sQB[cc] : __expf(sQA[cc] - gk) * p.scale);
           }
-          pv[i] = x;
+          pk[c + i] = x;
         }
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          *reinterpret_cast<uint4*>(sPT + sw_off(r, (c >> 3) + j)) =
-              make_uint4(pack_bf16(pv[8 * j], pv[8 * j + 1]), pack_bf16(pv[8 * j + 2], pv[8 * j + 3]),
-                         pack_bf16(pv[8 * j + 4], pv[8 * j + 5]), pack_bf16(pv[8 * j + 6], pv[8 * j + 7]));
+        store_row8(sPT, r, (c0 + c) >> 3, pk + c);
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(pt_full);
-      // ---- dS^T (scale folded in)
-#pragma unroll 1
-      for (int c = 0; c < kT; c += 32) {
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) {
         uint32_t dp[32];
-        tmem_ld32(tmem + 128 + trow + c, dp);
-        uint32_t sv[32];
-        if (MODE == kSoftmax) tmem_ld32(tmem + 0 + trow + c, sv);
+        tmem_ld32(tmem + 128 + trow + c0 + c, dp);
         tmem_ld_wait();
-        float dsv[32];
+        float ds[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const int q = q0 + c + i;
-          const bool valid = full_tile || (q < p.Lq && key_valid(p, q + p.q_offset, kpos));
-          float x = 0.f;
-          if (valid) {
-            if (MODE == kSoftmax) {
-              const float pr = exp2f(__uint_as_float(sv[i]) * sl2 - __ldg(p.lse + hq_base + q) * kLog2e);
-              x = pr * (__uint_as_float(dp[i]) - __ldg(p.delta + hq_base + q)) * p.scale;
-            } else {
-              x = __uint_as_float(dp[i]) * p.scale * __expf(__ldg(p.gcum + hq_base + q) - gk);
-            }
+          const int cc = c0 + c + i;
+          if (MODE == kSoftmax) {
+            ds[i] = pk[c + i] * (__uint_as_float(dp[i]) - sQB[cc]) * p.scale;
+          } else {
+            const int q = q0 + cc;
+            const bool valid = full_tile || (q < p.Lq && key_valid(p, q + p.q_offset, kpos));
+            ds[i] = valid ? __uint_as_float(dp[i]) * (offdiag ? rfk * sQB[cc] : __expf(sQA[cc] - gk) * p.scale) : 0.f;
           }
-          dsv[i] = x;
         }
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          *reinterpret_cast<uint4*>(sdST + sw_off(r, (c >> 3) + j)) =
-              make_uint4(pack_bf16(dsv[8 * j], dsv[8 * j + 1]), pack_bf16(dsv[8 * j + 2], dsv[8 * j + 3]),
-                         pack_bf16(dsv[8 * j + 4], dsv[8 * j + 5]), pack_bf16(dsv[8 * j + 6], dsv[8 * j + 7]));
+        store_row8(sdST, r, (c0 + c) >> 3, ds);
       }
       tc_fence_before();
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(dst_full);
-      // ---- dQ tile (TMEM lane = query row) -> fp32 atomics
-      if (!(ok = mbar_wait(dq_full, ph, abort_flag, p.status, 49))) break;
+      if (lane == 0) {
+        mbar_arrive(dst_full);
+        mbar_arrive(qv_empty);
+      }
+      // dQ tile (TMEM lane = query row) -> fp32 atomics
+      if (!(ok = mbar_wait(dq_full, ph, abort_flag, p.status, 51))) break;
       tc_fence_after();
       const int qrow = q0 + r;
-      float* dqr = p.dq_acc + ((static_cast<int64_t>(b) * p.Lq + min(qrow, p.Lq - 1)) * p.Hq + h) * kD;
-#pragma unroll 1
-      for (int c = 0; c < kD; c += 32) {
+      float* dqr = p.dq_acc + ((static_cast<int64_t>(b) * p.Lq + min(qrow, p.Lq - 1)) * p.Hq + h) * kD + c0;
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) {
         uint32_t v[32];
-        tmem_ld32(tmem + 0 + trow + c, v);
+        tmem_ld32(tmem + 0 + trow + c0 + c, v);
         tmem_ld_wait();
         if (qrow < p.Lq) {
 #pragma unroll
@@ -625,18 +660,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (lane == 0) mbar_arrive(dq_empty);
     }
     // ---- dK, dV
-    const bool have = ok && n_it > 0 && mbar_wait(fin, 0, abort_flag, p.status, 50);
+    const bool have = ok && n_it > 0 && mbar_wait(fin, 0, abort_flag, p.status, 52);
     if (have) tc_fence_after();
-    const int64_t orow = ((static_cast<int64_t>(b) * p.Lk + min(kpos, p.Lk - 1)) * p.Hk + hk) * kD;
+    const int64_t orow = ((static_cast<int64_t>(b) * p.Lk + min(kpos, p.Lk - 1)) * p.Hk + hk) * kD + c0;
 #pragma unroll 1
     for (int which = 0; which < 2; ++which) {
       __nv_bfloat16* dst = (which == 0 ? p.dK : p.dV) + orow;
       const uint32_t col = which == 0 ? 384u : 256u;
-#pragma unroll 1
-      for (int c = 0; c < kD; c += 32) {
+#pragma unroll
+      for (int c = 0; c < 64; c += 32) {
         uint32_t v[32];
         if (have) {
-          tmem_ld32(tmem + col + trow + c, v);
+          tmem_ld32(tmem + col + trow + c0 + c, v);
           tmem_ld_wait();
         } else {
 #pragma unroll
@@ -696,8 +731,8 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* _
   }
 }
 
-constexpr int kFwdSmem = 6 * kTileBytes + 256 + 1024;
-constexpr int kBwdSmem = 6 * kTileBytes + 256 + 1024;
+constexpr int kFwdSmem = 6 * kTileBytes + 6 * kT * 4 + 256 + 1024;
+constexpr int kBwdSmem = 6 * kTileBytes + 2 * kT * 4 + 256 + 1024;
 
 void check_qkv(const at::Tensor& t, const char* name) {
   FYB_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 4 && t.size(3) == kD && t.stride(3) == 1,
