@@ -96,6 +96,22 @@ __device__ __forceinline__ bool key_valid(const P& p, int qa, int k) {
   return true;
 }
 
+// bit i set when key kbase + i is visible from absolute query position qa (causal / window / key-count bounds)
+template <typename P>
+__device__ __forceinline__ uint32_t key_mask32(const P& p, int qa, int kbase, bool rowvalid) {
+  if (!rowvalid) return 0u;
+  int hi = p.Lk - kbase;                                    // exclusive upper bound (relative)
+  if (p.causal) hi = min(hi, qa + 1 - kbase);
+  int lo = 0;
+  if (p.window > 0) lo = max(0, qa - p.window + 1 - kbase);
+  hi = min(max(hi, 0), 32);
+  lo = min(lo, 32);
+  if (hi <= lo) return 0u;
+  const uint32_t up = hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u);
+  const uint32_t dn = lo >= 32 ? 0xffffffffu : ((1u << lo) - 1u);
+  return up & ~dn;
+}
+
 __device__ __forceinline__ void store_row8(uint8_t* tile, int r, int chunk0, const float* v) {
   // 32 consecutive values of row r starting at 16-byte chunk chunk0 -> 4 swizzled 16-byte stores
 #pragma unroll
@@ -291,13 +307,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         // full-row max (both threads of the row compute the same value, so their decisions agree)
         float mx = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < kT; c += 32) {
-          uint32_t v[32];
+        for (int c = 0; c < kT; c += 64) {
+          uint32_t v[32], w[32];
           tmem_ld32(tmem + st * 128 + trow + c, v);
+          tmem_ld32(tmem + st * 128 + trow + c + 32, w);
           tmem_ld_wait();
+          const uint32_t mv = full_tile ? 0xffffffffu : key_mask32(p, qa, k0 + c, rowvalid);
+          const uint32_t mw = full_tile ? 0xffffffffu : key_mask32(p, qa, k0 + c + 32, rowvalid);
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (full_tile || (rowvalid && key_valid(p, qa, k0 + c + i))) mx = fmaxf(mx, __uint_as_float(v[i]));
+          for (int i = 0; i < 32; ++i) {
+            mx = fmaxf(mx, ((mv >> i) & 1u) ? __uint_as_float(v[i]) : -INFINITY);
+            mx = fmaxf(mx, ((mw >> i) & 1u) ? __uint_as_float(w[i]) : -INFINITY);
+          }
         }
         const float m_cand = fmaxf(m_ref, mx * sl2);
         // O may be touched only after PV(it-1) has completed
@@ -326,27 +347,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const bool diag = k0 + kT - 1 >= q0 + p.q_offset;   // retention: tile reaches the query tile
       const float rf = (MODE == kRetention && !diag) ? __expf(gq - sG[st * kT + kT - 1]) * p.scale : 0.f;
       const float mref = m_ref == -INFINITY ? 0.f : m_ref;
-#pragma unroll
-      for (int c = c0; c < c0 + 64; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(tmem + st * 128 + trow + c, v);
+      {
+        uint32_t va[2][32];
+        tmem_ld32(tmem + st * 128 + trow + c0, va[0]);
+        tmem_ld32(tmem + st * 128 + trow + c0 + 32, va[1]);
         tmem_ld_wait();
-        float pv[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int kk = k0 + c + i;
-          const bool valid = full_tile || (rowvalid && key_valid(p, qa, kk));
-          float x = 0.f;
-          if (MODE == kSoftmax) {
-            x = valid ? fast_exp2(__uint_as_float(v[i]) * sl2 - mref) : 0.f;
-            l_part += x;
-          } else if (valid) {
-            const float decay = diag ? __expf(gq - sG[st * kT + c + i]) * p.scale : rf * sCF[st * kT + c + i];
-            x = __uint_as_float(v[i]) * decay;
+        for (int hh = 0; hh < 2; ++hh) {
+          const int c = c0 + 32 * hh;
+          const uint32_t m = full_tile ? 0xffffffffu : key_mask32(p, qa, k0 + c, rowvalid);
+          float pv[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const bool valid = (m >> i) & 1u;
+            float x;
+            if (MODE == kSoftmax) {
+              x = fast_exp2(__uint_as_float(va[hh][i]) * sl2 - mref);
+              x = valid ? x : 0.f;
+              l_part += x;
+            } else {
+              const float decay = diag ? __expf(gq - sG[st * kT + c + i]) * p.scale : rf * sCF[st * kT + c + i];
+              x = valid ? __uint_as_float(va[hh][i]) * decay : 0.f;
+            }
+            pv[i] = x;
           }
-          pv[i] = x;
+          store_row8(sP, r, c >> 3, pv);
         }
-        store_row8(sP, r, c >> 3, pv);
       }
       tc_fence_before();
       fence_proxy_async_smem();
@@ -588,47 +614,63 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (!(ok = mbar_wait(st_full, ph, abort_flag, p.status, 49))) break;
       tc_fence_after();
       if (!(ok = mbar_wait(pds_empty, ph ^ 1u, abort_flag, p.status, 50))) break;
+      // visibility of this key from the 32-query chunks: query q sees key kpos iff kpos <= qa (causal) and
+      // kpos > qa - window, i.e. qa in [kpos, kpos + window - 1]; qa = q + q_offset, q < Lq
+      uint32_t qm[2];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int qb = q0 + c0 + 32 * hh;          // first query of the chunk
+        if (full_tile) {
+          qm[hh] = 0xffffffffu;
+        } else if (kpos >= p.Lk) {
+          qm[hh] = 0u;
+        } else {
+          int lo = 0, hi = min(32, p.Lq - qb);
+          if (p.causal) lo = max(lo, kpos - p.q_offset - qb);
+          if (p.window > 0) hi = min(hi, kpos + p.window - p.q_offset - qb);
+          lo = max(lo, 0);
+          hi = min(hi, 32);
+          qm[hh] = hi <= lo ? 0u : ((hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u)) & ~(lo >= 32 ? 0xffffffffu : ((1u << lo) - 1u)));
+        }
+      }
       float pk[64];
 #pragma unroll
-      for (int c = 0; c < 64; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(tmem + 0 + trow + c0 + c, v);
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t va[32];
+        tmem_ld32(tmem + 0 + trow + c0 + 32 * hh, va);
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const int cc = c0 + c + i;
-          const int q = q0 + cc;
-          const bool valid = full_tile || (q < p.Lq && key_valid(p, q + p.q_offset, kpos));
-          float x = 0.f;
-          if (valid) {
-            if (MODE == kSoftmax) x = fast_exp2(__uint_as_float(v[i]) * sl2 - sQA[cc]);
-            else x = __uint_as_float(v[i]) * (offdiag ? rfk * sQB[cc] : __expf(sQA[cc] - gk) * p.scale);
-          }
-          pk[c + i] = x;
+          const int cc = c0 + 32 * hh + i;
+          float x;
+          if (MODE == kSoftmax) x = fast_exp2(__uint_as_float(va[i]) * sl2 - sQA[cc]);
+          else x = __uint_as_float(va[i]) * (offdiag ? rfk * sQB[cc] : __expf(sQA[cc] - gk) * p.scale);
+          pk[32 * hh + i] = ((qm[hh] >> i) & 1u) ? x : 0.f;
         }
-        store_row8(sPT, r, (c0 + c) >> 3, pk + c);
+        store_row8(sPT, r, (c0 + 32 * hh) >> 3, pk + 32 * hh);
       }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(pt_full);
 #pragma unroll
-      for (int c = 0; c < 64; c += 32) {
-        uint32_t dp[32];
-        tmem_ld32(tmem + 128 + trow + c0 + c, dp);
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t da[32];
+        tmem_ld32(tmem + 128 + trow + c0 + 32 * hh, da);
         tmem_ld_wait();
         float ds[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const int cc = c0 + c + i;
+          const int cc = c0 + 32 * hh + i;
+          float x;
           if (MODE == kSoftmax) {
-            ds[i] = pk[c + i] * (__uint_as_float(dp[i]) - sQB[cc]) * p.scale;
+            x = pk[32 * hh + i] * (__uint_as_float(da[i]) - sQB[cc]) * p.scale;
           } else {
-            const int q = q0 + cc;
-            const bool valid = full_tile || (q < p.Lq && key_valid(p, q + p.q_offset, kpos));
-            ds[i] = valid ? __uint_as_float(dp[i]) * (offdiag ? rfk * sQB[cc] : __expf(sQA[cc] - gk) * p.scale) : 0.f;
+            x = __uint_as_float(da[i]) * (offdiag ? rfk * sQB[cc] : __expf(sQA[cc] - gk) * p.scale);
+            x = ((qm[hh] >> i) & 1u) ? x : 0.f;
           }
+          ds[i] = x;
         }
-        store_row8(sdST, r, (c0 + c) >> 3, ds);
+        store_row8(sdST, r, (c0 + 32 * hh) >> 3, ds);
       }
       tc_fence_before();
       fence_proxy_async_smem();
