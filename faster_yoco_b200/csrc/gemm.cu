@@ -49,7 +49,8 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* Cv,
-                        const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, int* status) {
+                        const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, int splits,
+                        float* ws, int* status) {
   using S = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -66,6 +67,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_k = (K + BK - 1) / BK;
+  // split-K: work unit u = (tile u / splits, K slice u % splits); slices write fp32 partials to ws[slice, M, N]
+  const int num_units = num_tiles * splits;
+  const int k_chunk = (num_k + splits - 1) / splits;
   constexpr uint32_t TMEM_COLS = 2 * BN;
   constexpr uint32_t IDESC = idesc_bf16(BM, BN, A_MN, B_MN);
 
@@ -98,10 +102,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
-        for (int kb = 0; kb < num_k; ++kb) {
+        tile_coords(u / splits, num_m, num_n, mb, nb);
+        const int kb0 = (u % splits) * k_chunk, kb1 = min(num_k, kb0 + k_chunk);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, status, 1)) {
             ok = false;
             break;
@@ -144,11 +149,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_ph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         if (!mbar_wait(&tempty[acc], acc_ph ^ 1u, abort_flag, status, 2)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < num_k; ++kb) {
+        const int kb0 = (u % splits) * k_chunk, kb1 = min(num_k, kb0 + k_chunk);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[s], ph, abort_flag, status, 3)) {
             ok = false;
             break;
@@ -160,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = A_MN ? sw128_desc(a0 + k * 2048, 8192, 1024) : sw128_desc(a0 + k * 32, 16, 1024);
             const uint64_t bd = B_MN ? sw128_desc(b0 + k * 2048, 8192, 1024) : sw128_desc(b0 + k * 32, 16, 1024);
-            umma_bf16(d, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+            umma_bf16(d, ad, bd, IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit(&empty[s]);   // frees the smem stage once these MMAs have read it
           if (++s == STAGES) {
@@ -179,9 +185,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;   // TMEM lane quadrant this warp may access
     int acc = 0;
     uint32_t acc_ph = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
       int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      tile_coords(u / splits, num_m, num_n, mb, nb);
+      float* wsl = splits > 1 ? ws + static_cast<int64_t>(u % splits) * M * N : nullptr;
       if (!mbar_wait(&tfull[acc], acc_ph, abort_flag, status, 4)) break;
       tc_fence_after();
       const int row = mb * BM + q * 32 + lane;
@@ -192,7 +199,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(tb + c * 32, r);
         tmem_ld_wait();
         const int col = nb * BN + c * 32;
-        if (row < M && col < N) {
+        if (row < M && col < N && wsl != nullptr) {
+          float* W = wsl + static_cast<int64_t>(row) * N + col;
+          if (col + 32 <= N && (N % 4) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(W + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                              __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col + j < N) W[j] = __uint_as_float(r[j]);
+          }
+        } else if (row < M && col < N) {
           if (EPI == kEpiF32) {
             float* C = reinterpret_cast<float*>(Cv) + static_cast<int64_t>(row) * ldc + col;
             if (col + 32 <= N && (ldc % 4) == 0) {
@@ -269,9 +288,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// C = sum over slices of ws[slice] (+ R), fp32 sum in slice order
+template <int EPI>
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, void* Cv, const __nv_bfloat16* R,
+                                     int M, int N, int64_t ldc, int64_t ldr) {
+  const int64_t i4 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  const int64_t total = static_cast<int64_t>(M) * N;
+  if (i4 >= total) return;
+  for (int64_t i = i4; i < i4 + 4 && i < total; ++i) {
+    float acc = 0.f;
+    for (int sp = 0; sp < splits; ++sp) acc += ws[sp * total + i];
+    const int64_t row = i / N, col = i % N;
+    if (EPI == kEpiF32) {
+      reinterpret_cast<float*>(Cv)[row * ldc + col] = acc;
+    } else if (EPI == kEpiBf16Res) {
+      reinterpret_cast<__nv_bfloat16*>(Cv)[row * ldc + col] =
+          __float2bfloat16_rn(bf16_round(acc) + __bfloat162float(R[row * ldr + col]));
+    } else {
+      reinterpret_cast<__nv_bfloat16*>(Cv)[row * ldc + col] = __float2bfloat16_rn(acc);
+    }
+  }
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const __nv_bfloat16* R, int M, int N, int K,
-            int64_t ldc, int64_t ldr, cudaStream_t stream) {
+            int64_t ldc, int64_t ldr, int splits, float* ws, cudaStream_t stream) {
   using S = GemmSmem<BN, STAGES>;
   auto kern = gemm_tcgen05_kernel<BN, STAGES, A_MN, B_MN, EPI>;
   static bool attr_set = false;
@@ -279,31 +320,58 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const __nv_bf
     FYB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
     attr_set = true;
   }
-  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * splits;
   const int grid = std::min(tiles, num_sms());
-  kern<<<grid, kThreads, S::TOTAL, stream>>>(ta, tb, C, R, M, N, K, ldc, ldr, status_ptr());
+  kern<<<grid, kThreads, S::TOTAL, stream>>>(ta, tb, C, R, M, N, K, ldc, ldr, splits, ws, status_ptr());
   check_launch("gemm_tcgen05");
+  if (splits > 1) {
+    const int64_t total = static_cast<int64_t>(M) * N;
+    const int blocks = static_cast<int>((total / 4 + 255) / 256 + 1);
+    splitk_reduce_kernel<EPI><<<blocks, 256, 0, stream>>>(ws, splits, C, R, M, N, ldc, ldr);
+    check_launch("gemm_splitk_reduce");
+  }
 }
 
 template <int BN, int STAGES, int EPI>
 void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, void* C,
-                    const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, cudaStream_t st) {
-  if (!a_mn && !b_mn) launch<BN, STAGES, false, false, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
-  else if (!a_mn && b_mn) launch<BN, STAGES, false, true, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
-  else if (a_mn && b_mn) launch<BN, STAGES, true, true, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
-  else launch<BN, STAGES, true, false, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
+                    const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, int sp, float* ws,
+                    cudaStream_t st) {
+  if (!a_mn && !b_mn) launch<BN, STAGES, false, false, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, sp, ws, st);
+  else if (!a_mn && b_mn) launch<BN, STAGES, false, true, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, sp, ws, st);
+  else if (a_mn && b_mn) launch<BN, STAGES, true, true, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, sp, ws, st);
+  else launch<BN, STAGES, true, false, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, sp, ws, st);
 }
 
-// Pick the tile width whose last wave wastes the least of the machine (ties: the wider tile).
-int pick_bn(int M, int N) {
+struct Plan {
+  int bn, splits;
+};
+
+// Tile width and split-K factor: minimise (waves x per-unit work) + the fp32 split reduction, in tile-k-block
+// units. A unit of a BN-wide tile over kc k-blocks costs ~ BN * kc; the last partial wave costs a full wave.
+Plan pick_plan(int M, int N, int K) {
   const int sms = num_sms();
   const int tm = (M + BM - 1) / BM;
-  auto cost = [&](int bn) {
+  const int nk = (K + BK - 1) / BK;
+  Plan best{256, 1};
+  double best_cost = 1e30;
+  for (int bn : {256, 128}) {
     const long tiles = static_cast<long>(tm) * ((N + bn - 1) / bn);
-    const long waves = (tiles + sms - 1) / sms;
-    return waves * bn;   // time ~ waves x per-tile work (per-tile work ~ bn)
-  };
-  return cost(128) < cost(256) ? 128 : 256;
+    for (int sp : {1, 2, 3, 4, 6, 8}) {
+      if (sp > 1 && nk / sp < 8) break;                  // keep at least 8 k-blocks per slice
+      const long units = tiles * sp;
+      const long waves = (units + sms - 1) / sms;
+      const int kc = (nk + sp - 1) / sp;
+      double cost = static_cast<double>(waves) * bn * kc * (bn == 128 ? 1.15 : 1.0);   // narrow tiles: more traffic
+      // fp32 partials written and re-read once: ~ M*N*(sp+1)*4 bytes at HBM speed, in the same units
+      // (one BN=256 k-block of one SM ~ 512 tensor cycles ~ 2 units per cycle)
+      if (sp > 1) cost += static_cast<double>(M) * N * (sp + 1) * 6.0e-4;
+      if (cost < best_cost * 0.97) {
+        best_cost = cost;
+        best = Plan{bn, sp};
+      }
+    }
+  }
+  return best;
 }
 
 }  // namespace
@@ -342,7 +410,15 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bo
     else C.zero_();
     return;
   }
-  const int bn = pick_bn(static_cast<int>(M), static_cast<int>(N));
+  const Plan plan = pick_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
+  const int bn = plan.bn;
+  at::Tensor ws;
+  float* wsp = nullptr;
+  if (plan.splits > 1) {
+    ws = at::empty({plan.splits, M, N}, A.options().dtype(at::kFloat));
+    wsp = ws.data_ptr<float>();
+  }
+  const int sp = plan.splits;
   const CUtensorMap ta = a_mn ? make_tmap_2d(A.data_ptr(), K, M, A.stride(0), 64)
                               : make_tmap_2d(A.data_ptr(), M, K, A.stride(0), BM);
   const CUtensorMap tb = b_mn ? make_tmap_2d(B.data_ptr(), K, N, B.stride(0), 64)
@@ -352,13 +428,15 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bo
   const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
   const int64_t ldc = C.stride(0);
   if (bn == 256) {
-    if (epi == kEpiBf16) dispatch_major<256, 4, kEpiBf16>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
-    else if (epi == kEpiBf16Res) dispatch_major<256, 4, kEpiBf16Res>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
-    else dispatch_major<256, 4, kEpiF32>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
+    if (epi == kEpiBf16) dispatch_major<256, 4, kEpiBf16>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, sp, wsp, st);
+    else if (epi == kEpiBf16Res)
+      dispatch_major<256, 4, kEpiBf16Res>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, sp, wsp, st);
+    else dispatch_major<256, 4, kEpiF32>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, sp, wsp, st);
   } else {
-    if (epi == kEpiBf16) dispatch_major<128, 6, kEpiBf16>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
-    else if (epi == kEpiBf16Res) dispatch_major<128, 6, kEpiBf16Res>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
-    else dispatch_major<128, 6, kEpiF32>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
+    if (epi == kEpiBf16) dispatch_major<128, 6, kEpiBf16>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, sp, wsp, st);
+    else if (epi == kEpiBf16Res)
+      dispatch_major<128, 6, kEpiBf16Res>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, sp, wsp, st);
+    else dispatch_major<128, 6, kEpiF32>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, sp, wsp, st);
   }
 }
 

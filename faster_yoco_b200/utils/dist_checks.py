@@ -1,0 +1,108 @@
+"""Rank functions used by the multi-process tests (importable by spawned children)."""
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.distributed as dist
+
+
+def _tiny_trainer(device, comm="nccl", seed=0, graph=False, arch="yoco_tiny", dtype=torch.float32):
+    from ..config import OptimConfig, build_args
+    from ..models.yoco import YOCO
+    from ..train.trainer import Trainer
+    torch.manual_seed(seed)
+    args = build_args(arch, max_seq_len=256, init_std=0.02)
+    model = YOCO(args).to(device=device, dtype=dtype)
+    cfg = OptimConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, warmup_updates=0, total_num_update=20)
+    return model, Trainer(model, cfg, device=device, comm=comm, graph_step=graph)
+
+
+def _batches(rank, world, n, seed=1, batch=2, seq=256, vocab=1024):
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for _ in range(n):
+        ids = torch.randint(0, vocab, (world, batch, seq + 1), generator=g)
+        out.append(ids)
+    return out
+
+
+def zero_matches_single(rank, world, outdir, steps):
+    """World-size-N ZeRO training on N shards of each global batch; rank 0 saves the final flat params."""
+    model, tr = _tiny_trainer(torch.device("cpu"))
+    for ids in _batches(rank, world, steps):
+        mine = ids[rank]
+        b = {"src_tokens": mine[:, :-1].contiguous(), "target": mine[:, 1:].contiguous(),
+             "ntokens": mine.shape[0] * mine.shape[1], "nsentences": mine.shape[0]}
+        tr.train_step(b)
+    sd = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    if rank == 0:
+        torch.save({"sd": sd, "num_updates": tr.num_updates()}, os.path.join(outdir, f"ws{world}.pt"))
+
+
+def single_reference(outdir, world, steps):
+    """Single process, batch = all shards concatenated (the same global batch)."""
+    model, tr = _tiny_trainer(torch.device("cpu"))
+    for ids in _batches(0, world, steps):
+        allb = ids.reshape(-1, ids.shape[-1])
+        b = {"src_tokens": allb[:, :-1].contiguous(), "target": allb[:, 1:].contiguous(),
+             "ntokens": allb.shape[0] * allb.shape[1], "nsentences": allb.shape[0]}
+        tr.train_step(b)
+    return {k: v.detach().clone() for k, v in model.state_dict().items()}
+
+
+def checkpoint_resume(rank, world, outdir, steps, split):
+    """Train `steps`, or train `split`, checkpoint, rebuild everything, load, train the rest."""
+    from ..train.checkpoint import load_checkpoint, save_checkpoint
+    batches = _batches(rank, world, steps)
+
+    def run(tr, bs):
+        for ids in bs:
+            mine = ids[rank]
+            tr.train_step({"src_tokens": mine[:, :-1].contiguous(), "target": mine[:, 1:].contiguous(),
+                           "ntokens": mine.shape[0] * mine.shape[1], "nsentences": mine.shape[0]})
+
+    model, tr = _tiny_trainer(torch.device("cpu"))
+    run(tr, batches[:split])
+    path = os.path.join(outdir, "ckpt.pt")
+    save_checkpoint(path, model, tr)
+    dist.barrier()
+    model2, tr2 = _tiny_trainer(torch.device("cpu"), seed=123)      # different init: must be overwritten
+    load_checkpoint(path, model2, tr2)
+    run(tr2, batches[split:])
+    model3, tr3 = _tiny_trainer(torch.device("cpu"))
+    run(tr3, batches)
+    if rank == 0:
+        torch.save({"resumed": model2.state_dict(), "straight": model3.state_dict(),
+                    "n2": tr2.num_updates(), "n3": tr3.num_updates()}, os.path.join(outdir, "resume.pt"))
+
+
+def rank_fails_before_collective(rank, world, outdir):
+    """Host-injected failure: rank 1 raises before the collective; rank 0 must see a timeout/error, not hang."""
+    if rank == 1:
+        raise RuntimeError("injected failure on rank 1")
+    t = torch.ones(1)
+    dist.all_reduce(t)
+
+
+def fused_vs_nccl_gpu(rank, world, outdir, steps):
+    """GPU: the same training with the NVLink peer-memory collectives and with NCCL; rank 0 saves both."""
+    from .. import ops
+    ops.set_backend("native")
+    dev = torch.device("cuda", rank)
+    res = {}
+    for comm in ("nccl", "fused"):
+        model, tr = _tiny_trainer(dev, comm=comm, arch="yoco_small", dtype=torch.bfloat16)
+        losses = []
+        for ids in _batches(rank, world, steps, seq=256, vocab=8192):
+            mine = ids[rank]
+            b = {"src_tokens": mine[:, :-1].contiguous(), "target": mine[:, 1:].contiguous(),
+                 "ntokens": mine.shape[0] * mine.shape[1], "nsentences": mine.shape[0]}
+            losses.append(float(tr.train_step(b).item()))
+        torch.cuda.synchronize()
+        status = int(ops._C().status()[0].item())
+        res[comm] = {"losses": losses, "params": tr.flat.flat.float().cpu(), "status": status}
+        if tr.zero.p2p is not None:
+            tr.zero.p2p.close()
+    if rank == 0:
+        torch.save(res, os.path.join(outdir, "fused_vs_nccl.pt"))

@@ -1,0 +1,45 @@
+"""ZeRO data parallelism on CPU ranks (gloo, world_size 2): equivalence with single-process training,
+checkpoint/resume (world-size independent optimizer state) and host-injected failure detection."""
+import os
+import time
+
+import pytest
+import torch
+
+from faster_yoco_b200.parallel.zero import greedy_partition
+from faster_yoco_b200.utils import dist_checks
+from faster_yoco_b200.utils.launch import run_ranks
+
+
+def test_greedy_partition_is_oss_rule():
+    # next parameter to the rank with the smallest running total, ties to the lowest rank
+    assert greedy_partition([10, 10, 5, 5, 1], 2) == [0, 1, 0, 1, 0]
+    assert greedy_partition([100, 1, 1, 1], 3) == [0, 1, 2, 1]
+
+
+def test_zero_ws2_matches_single_process(tmp_path):
+    steps = 3
+    run_ranks(dist_checks.zero_matches_single, 2, str(tmp_path), steps)
+    got = torch.load(os.path.join(tmp_path, "ws2.pt"))
+    assert got["num_updates"] == steps
+    ref = dist_checks.single_reference(str(tmp_path), 2, steps)
+    for k, v in ref.items():
+        assert torch.allclose(got["sd"][k].float(), v.float(), atol=2e-5, rtol=1e-4), k
+
+
+def test_checkpoint_resume_matches_uninterrupted(tmp_path):
+    run_ranks(dist_checks.checkpoint_resume, 2, str(tmp_path), 4, 2)
+    r = torch.load(os.path.join(tmp_path, "resume.pt"))
+    assert r["n2"] == r["n3"] == 4
+    for k, v in r["straight"].items():
+        assert torch.allclose(r["resumed"][k].float(), v.float(), atol=1e-6, rtol=1e-5), k
+    ck = torch.load(os.path.join(tmp_path, "ckpt.pt"))
+    assert any(k.startswith("decoder.model.self_decoder.layers.0.mixer.q_proj") for k in ck["model"])
+    assert "self_decoder.layers.0.mixer.q_proj.weight" in ck["last_optimizer_state"]["exp_avg"]
+
+
+def test_injected_rank_failure_does_not_hang(tmp_path):
+    t0 = time.time()
+    with pytest.raises(RuntimeError):
+        run_ranks(dist_checks.rank_fails_before_collective, 2, str(tmp_path), timeout_s=20)
+    assert time.time() - t0 < 150

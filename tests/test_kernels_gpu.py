@@ -200,3 +200,19 @@ def test_adam_matches_reference_and_sq_norm():
     s = C().sq_norm(x)
     r = x.double().pow(2).sum()
     assert abs(s.item() - r.item()) / r.item() < 1e-4
+
+
+@pytest.mark.parametrize("M,N,K", [(2048, 3072, 16384), (2048, 3072, 100288)])
+def test_gemm_split_k_with_residual(M, N, K):
+    """Long-K / small-output shapes take the split-K path (fp32 slice partials + ordered reduction)."""
+    torch.manual_seed(7)
+    a = torch.randn(M, K, device=dev(), dtype=torch.bfloat16)
+    b = torch.randn(N, K, device=dev(), dtype=torch.bfloat16) * 0.05
+    r = torch.randn(M, N, device=dev(), dtype=torch.bfloat16)
+    ref = a.float() @ b.float().T
+    out = torch.empty(M, N, device=dev(), dtype=torch.bfloat16)
+    C().gemm(a, b.T.contiguous(), out, False, True, r)     # dgrad layout: B MN-major
+    assert rel(out, ref.to(torch.bfloat16).float() + r.float()) < 1e-2
+    out2 = torch.empty(M, N, device=dev(), dtype=torch.bfloat16)
+    C().gemm(a, b, out2, False, False, None)
+    assert rel(out2, ref) < 1e-2

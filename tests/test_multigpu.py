@@ -1,0 +1,21 @@
+"""2-GPU data parallelism: the NVLink peer-memory collectives (fused reduce-to-owner, all-gather, mailbox
+all-reduce) against the NCCL path on the same training run."""
+import os
+
+import pytest
+import torch
+
+from faster_yoco_b200.utils import dist_checks
+from faster_yoco_b200.utils.launch import run_ranks
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def test_fused_p2p_matches_nccl(tmp_path):
+    run_ranks(dist_checks.fused_vs_nccl_gpu, 2, str(tmp_path), 4, backend="nccl", timeout_s=300)
+    r = torch.load(os.path.join(tmp_path, "fused_vs_nccl.pt"))
+    assert r["fused"]["status"] == 0 and r["nccl"]["status"] == 0
+    for a, b in zip(r["fused"]["losses"], r["nccl"]["losses"]):
+        assert abs(a - b) / abs(b) < 2e-3, (r["fused"]["losses"], r["nccl"]["losses"])
+    pf, pn = r["fused"]["params"], r["nccl"]["params"]
+    assert ((pf - pn).abs().max() / pn.abs().max()).item() < 2e-2
