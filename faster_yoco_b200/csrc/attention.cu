@@ -437,8 +437,11 @@ struct AttnBwdParams {
   const float* delta;    // softmax: [B, Hq, Lq] rowsum(dO * O)
   const float* gcum;     // retention: [B, H, L]
   float* dq_acc;         // [B, Lq, Hq, D] fp32
-  __nv_bfloat16* dK;     // [B, Lk, Hk, D]
-  __nv_bfloat16* dV;     // [B, Lk, Hk, D]
+  __nv_bfloat16* dK;     // [B, Lk, Hk, D] view: token stride dk_ld, head stride D
+  __nv_bfloat16* dV;     // [B, Lk, Hk, D] view: token stride dv_ld
+  int64_t dk_ld, dv_ld;
+  const __nv_bfloat16* rope_cos;   // non-null: dK leaves through the conjugate rotation (keys were rotated)
+  const __nv_bfloat16* rope_sin;   // [Lk, D/2] tables
   int* status;
 };
 
@@ -704,10 +707,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // ---- dK, dV
     const bool have = ok && n_it > 0 && mbar_wait(fin, 0, abort_flag, p.status, 52);
     if (have) tc_fence_after();
-    const int64_t orow = ((static_cast<int64_t>(b) * p.Lk + min(kpos, p.Lk - 1)) * p.Hk + hk) * kD + c0;
+    const int64_t tok = static_cast<int64_t>(b) * p.Lk + min(kpos, p.Lk - 1);
 #pragma unroll 1
     for (int which = 0; which < 2; ++which) {
-      __nv_bfloat16* dst = (which == 0 ? p.dK : p.dV) + orow;
+      __nv_bfloat16* dst = which == 0 ? p.dK + tok * p.dk_ld + hk * kD + c0 : p.dV + tok * p.dv_ld + hk * kD + c0;
       const uint32_t col = which == 0 ? 384u : 256u;
 #pragma unroll
       for (int c = 0; c < 64; c += 32) {
@@ -718,6 +721,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         } else {
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = 0u;
+        }
+        if (which == 0 && p.rope_cos != nullptr && kpos < p.Lk) {
+          // conjugate rotation of interleaved pairs (2i, 2i+1) at position kpos
+          const __nv_bfloat16* cp = p.rope_cos + static_cast<int64_t>(kpos) * (kD / 2) + (c0 + c) / 2;
+          const __nv_bfloat16* sp = p.rope_sin + static_cast<int64_t>(kpos) * (kD / 2) + (c0 + c) / 2;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float cs = __bfloat162float(cp[i]), sn = __bfloat162float(sp[i]);
+            const float x0 = __uint_as_float(v[2 * i]), x1 = __uint_as_float(v[2 * i + 1]);
+            v[2 * i] = __float_as_uint(x0 * cs + x1 * sn);
+            v[2 * i + 1] = __float_as_uint(x1 * cs - x0 * sn);
+          }
         }
         if (kpos < p.Lk) {
 #pragma unroll
@@ -742,7 +757,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
 // rowdot[b, h, t] = sum_d X[b, t, h, d] * Y[b, t, h, d] (fp32); one warp per (b, t, h)
 __global__ void rowdot_kernel(const __nv_bfloat16* __restrict__ X, const __nv_bfloat16* __restrict__ Y,
-                              float* __restrict__ out, int B, int L, int H, float* __restrict__ sub_from) {
+                              float* __restrict__ out, int B, int L, int H, float* __restrict__ sub_from,
+                              int64_t ldx = -1, int64_t ldy = -1) {
   const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (wid >= static_cast<int64_t>(B) * L * H) return;
@@ -750,9 +766,11 @@ __global__ void rowdot_kernel(const __nv_bfloat16* __restrict__ X, const __nv_bf
   const int64_t bt = wid / H;
   const int t = static_cast<int>(bt % L);
   const int b = static_cast<int>(bt / L);
-  const int64_t off = wid * kD + lane * 4;
-  const uint2 xu = *reinterpret_cast<const uint2*>(X + off);
-  const uint2 yu = *reinterpret_cast<const uint2*>(Y + off);
+  const int64_t tok = static_cast<int64_t>(b) * L + t;
+  const int64_t xo = (ldx < 0 ? wid * kD : tok * ldx + h * kD) + lane * 4;
+  const int64_t yo = (ldy < 0 ? wid * kD : tok * ldy + h * kD) + lane * 4;
+  const uint2 xu = *reinterpret_cast<const uint2*>(X + xo);
+  const uint2 yu = *reinterpret_cast<const uint2*>(Y + yo);
   const float2 x0 = unpack_bf16(xu.x), x1 = unpack_bf16(xu.y), y0 = unpack_bf16(yu.x), y1 = unpack_bf16(yu.y);
   float s = x0.x * y0.x + x0.y * y0.y + x1.x * y1.x + x1.y * y1.y;
 #pragma unroll
@@ -761,6 +779,30 @@ __global__ void rowdot_kernel(const __nv_bfloat16* __restrict__ X, const __nv_bf
     const int64_t idx = (static_cast<int64_t>(b) * H + h) * L + t;
     out[idx] = sub_from != nullptr ? sub_from[idx] - s : s;
   }
+}
+
+// dq[b, t, h, :] (token stride ld) = bf16(conj_rope(acc[b, t, h, :])) ; acc contiguous [B, L, H, D] fp32
+__global__ void dq_out_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ out, int64_t ld, int B,
+                              int L, int H, const __nv_bfloat16* __restrict__ cos_t,
+                              const __nv_bfloat16* __restrict__ sin_t) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;   // one thread per 4 values
+  const int64_t total = static_cast<int64_t>(B) * L * H * (kD / 4);
+  if (i >= total) return;
+  const int c = static_cast<int>(i % (kD / 4)) * 4;
+  const int64_t bth = i / (kD / 4);
+  const int h = static_cast<int>(bth % H);
+  const int64_t bt = bth / H;
+  const int t = static_cast<int>(bt % L);
+  float4 v = *reinterpret_cast<const float4*>(acc + bth * kD + c);
+  if (cos_t != nullptr) {
+    const float c0 = __bfloat162float(cos_t[static_cast<int64_t>(t) * (kD / 2) + c / 2]);
+    const float s0 = __bfloat162float(sin_t[static_cast<int64_t>(t) * (kD / 2) + c / 2]);
+    const float c1 = __bfloat162float(cos_t[static_cast<int64_t>(t) * (kD / 2) + c / 2 + 1]);
+    const float s1 = __bfloat162float(sin_t[static_cast<int64_t>(t) * (kD / 2) + c / 2 + 1]);
+    const float x0 = v.x, x1 = v.y, x2 = v.z, x3 = v.w;
+    v = make_float4(x0 * c0 + x1 * s0, x1 * c0 - x0 * s0, x2 * c1 + x3 * s1, x3 * c1 - x2 * s1);
+  }
+  *reinterpret_cast<uint2*>(out + bt * ld + h * kD + c) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
 }
 
 __global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, int64_t n) {
@@ -824,9 +866,25 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& q, const at::Tensor& k, 
   return {o, lse};
 }
 
+at::Tensor out_view(const c10::optional<at::Tensor>& opt, int B, int L, int H, const at::TensorOptions& o,
+                    const char* name) {
+  if (opt.has_value() && opt->defined()) {
+    const at::Tensor& t = *opt;
+    FYB_CHECK(t.dim() == 4 && t.size(0) == B && t.size(1) == L && t.size(2) == H && t.size(3) == kD &&
+                  t.stride(3) == 1 && t.stride(2) == kD && (t.stride(0) == L * t.stride(1) || B == 1) &&
+                  t.stride(1) % 8 == 0 && t.scalar_type() == at::kBFloat16,
+              std::string(name) + ": output view must be bf16 [B, L, H, 128] with head stride 128");
+    return t;
+  }
+  return at::empty({B, L, H, kD}, o);
+}
+
 std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                       const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, bool causal,
-                                      int64_t window, double scale) {
+                                      int64_t window, double scale, const c10::optional<at::Tensor>& dq_out,
+                                      const c10::optional<at::Tensor>& dk_out, const c10::optional<at::Tensor>& dv_out,
+                                      const c10::optional<at::Tensor>& rope_cos,
+                                      const c10::optional<at::Tensor>& rope_sin, bool rope_q, bool rope_k) {
   check_qkv(q, "q");
   check_qkv(k, "k");
   check_qkv(v, "v");
@@ -835,9 +893,18 @@ std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& 
   c10::cuda::CUDAGuard guard(q.device());
   auto delta = at::empty({B, Hq, Lq}, q.options().dtype(at::kFloat));
   auto dq_acc = at::zeros({B, Lq, Hq, kD}, q.options().dtype(at::kFloat));
-  auto dk = at::empty({B, Lk, Hk, kD}, q.options());
-  auto dv = at::empty({B, Lk, Hk, kD}, q.options());
-  auto dq = at::empty({B, Lq, Hq, kD}, q.options());
+  auto dk = out_view(dk_out, B, Lk, Hk, q.options(), "attention_bwd dk");
+  auto dv = out_view(dv_out, B, Lk, Hk, q.options(), "attention_bwd dv");
+  auto dq = out_view(dq_out, B, Lq, Hq, q.options(), "attention_bwd dq");
+  const __nv_bfloat16* rc = nullptr;
+  const __nv_bfloat16* rs = nullptr;
+  if (rope_cos.has_value() && rope_cos->defined()) {
+    FYB_CHECK(rope_sin.has_value() && rope_cos->is_contiguous() && rope_sin->is_contiguous() &&
+                  rope_cos->size(0) >= std::max(Lq, Lk) && rope_cos->size(1) == kD / 2,
+              "attention_bwd: rope tables [L, 64] expected");
+    rc = reinterpret_cast<const __nv_bfloat16*>(rope_cos->data_ptr());
+    rs = reinterpret_cast<const __nv_bfloat16*>(rope_sin->data_ptr());
+  }
   if (B == 0 || Lq == 0) return {dq.zero_(), dk.zero_(), dv.zero_()};
   const int64_t rows = (int64_t)B * Lq * Hq;
   rowdot_kernel<<<(rows * 32 + 255) / 256, 256, 0, cur_stream()>>>(
@@ -847,7 +914,7 @@ std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& 
   AttnBwdParams p{B, Lq, Lk, Hq, Hk, Lk - Lq, (int)window, causal ? 1 : 0, (float)scale, lse.data_ptr<float>(),
                   delta.data_ptr<float>(), nullptr, dq_acc.data_ptr<float>(),
                   reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()),
-                  status_ptr()};
+                  dk.stride(1), dv.stride(1), rope_k ? rc : nullptr, rope_k ? rs : nullptr, status_ptr()};
   const CUtensorMap tq = tmap_heads(q), tk = tmap_heads(k), tv = tmap_heads(v), tdo = tmap_heads(dout);
   static bool init = false;
   if (!init) {
@@ -857,9 +924,10 @@ std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& 
   const int grid = B * Hk * ((Lk + kT - 1) / kT);
   attn_bwd_kernel<kSoftmax><<<grid, kAttnThreads, kBwdSmem, cur_stream()>>>(tq, tk, tv, tdo, p);
   check_launch("attn_bwd");
-  const int64_t n = dq.numel();
-  f32_to_bf16_kernel<<<(n / 4 + 255) / 256 + 1, 256, 0, cur_stream()>>>(
-      dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), n);
+  const int64_t nq4 = static_cast<int64_t>(B) * Lq * Hq * (kD / 4);
+  dq_out_kernel<<<static_cast<int>((nq4 + 255) / 256), 256, 0, cur_stream()>>>(
+      dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), dq.stride(1), B, Lq, Hq,
+      rope_q ? rc : nullptr, rope_q ? rs : nullptr);
   check_launch("attn_bwd_dq");
   return {dq, dk, dv};
 }
@@ -891,7 +959,11 @@ at::Tensor retention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Ten
 }
 
 std::vector<at::Tensor> retention_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
-                                      const at::Tensor& v, const at::Tensor& gcum, const at::Tensor& o) {
+                                      const at::Tensor& v, const at::Tensor& gcum, const at::Tensor& o,
+                                      const c10::optional<at::Tensor>& dq_out, const c10::optional<at::Tensor>& dk_out,
+                                      const c10::optional<at::Tensor>& dv_out,
+                                      const c10::optional<at::Tensor>& rope_cos,
+                                      const c10::optional<at::Tensor>& rope_sin) {
   check_qkv(q, "q");
   check_qkv(k, "k");
   check_qkv(v, "v");
@@ -901,9 +973,18 @@ std::vector<at::Tensor> retention_bwd(const at::Tensor& dout, const at::Tensor& 
   auto dgo = at::empty({B, H, L}, q.options().dtype(at::kFloat));
   auto dg = at::empty({B, H, L}, q.options().dtype(at::kFloat));
   auto dq_acc = at::zeros({B, L, H, kD}, q.options().dtype(at::kFloat));
-  auto dk = at::empty({B, L, H, kD}, q.options());
-  auto dv = at::empty({B, L, H, kD}, q.options());
-  auto dq = at::empty({B, L, H, kD}, q.options());
+  auto dk = out_view(dk_out, B, L, H, q.options(), "retention_bwd dk");
+  auto dv = out_view(dv_out, B, L, H, q.options(), "retention_bwd dv");
+  auto dq = out_view(dq_out, B, L, H, q.options(), "retention_bwd dq");
+  const __nv_bfloat16* rc = nullptr;
+  const __nv_bfloat16* rs = nullptr;
+  if (rope_cos.has_value() && rope_cos->defined()) {
+    FYB_CHECK(rope_sin.has_value() && rope_cos->is_contiguous() && rope_sin->is_contiguous() &&
+                  rope_cos->size(0) >= L && rope_cos->size(1) == kD / 2,
+              "retention_bwd: rope tables [L, 64] expected");
+    rc = reinterpret_cast<const __nv_bfloat16*>(rope_cos->data_ptr());
+    rs = reinterpret_cast<const __nv_bfloat16*>(rope_sin->data_ptr());
+  }
   if (B == 0 || L == 0) return {dq.zero_(), dk.zero_(), dv.zero_(), dg.zero_()};
   const int64_t rows = (int64_t)B * L * H;
   rowdot_kernel<<<(rows * 32 + 255) / 256, 256, 0, cur_stream()>>>(
@@ -913,7 +994,7 @@ std::vector<at::Tensor> retention_bwd(const at::Tensor& dout, const at::Tensor& 
   AttnBwdParams p{B, L, L, H, H, 0, 0, 1, (float)(1.0 / std::sqrt((double)kD)), nullptr, nullptr,
                   gcum.data_ptr<float>(), dq_acc.data_ptr<float>(),
                   reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()),
-                  status_ptr()};
+                  dk.stride(1), dv.stride(1), rc, rs, status_ptr()};
   const CUtensorMap tq = tmap_heads(q), tk = tmap_heads(k), tv = tmap_heads(v), tdo = tmap_heads(dout);
   static bool init = false;
   if (!init) {
@@ -923,15 +1004,14 @@ std::vector<at::Tensor> retention_bwd(const at::Tensor& dout, const at::Tensor& 
   const int grid = B * H * ((L + kT - 1) / kT);
   attn_bwd_kernel<kRetention><<<grid, kAttnThreads, kBwdSmem, cur_stream()>>>(tq, tk, tv, tdo, p);
   check_launch("retention_bwd");
-  // dG = dO.O - V.dV ; v may be strided -> use a contiguous copy only if needed
-  at::Tensor vc = v.is_contiguous() ? v : v.contiguous();
+  // dG = dO.O - V.dV (both operands may be token-strided views)
   rowdot_kernel<<<(rows * 32 + 255) / 256, 256, 0, cur_stream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dv.data_ptr()),
-      dg.data_ptr<float>(), B, L, H, dgo.data_ptr<float>());
+      reinterpret_cast<const __nv_bfloat16*>(v.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dv.data_ptr()),
+      dg.data_ptr<float>(), B, L, H, dgo.data_ptr<float>(), v.stride(1), dv.stride(1));
   check_launch("retention_bwd_dg");
-  const int64_t n = dq.numel();
-  f32_to_bf16_kernel<<<(n / 4 + 255) / 256 + 1, 256, 0, cur_stream()>>>(
-      dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), n);
+  const int64_t nq4 = static_cast<int64_t>(B) * L * H * (kD / 4);
+  dq_out_kernel<<<static_cast<int>((nq4 + 255) / 256), 256, 0, cur_stream()>>>(
+      dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), dq.stride(1), B, L, H, rc, rs);
   check_launch("retention_bwd_dq");
   return {dq, dk, dv, dg};
 }

@@ -12,12 +12,15 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bo
           const c10::optional<at::Tensor>& R);
 std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps);
 std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const c10::optional<at::Tensor>& w,
-                                     const at::Tensor& rstd);
+                                     const at::Tensor& rstd, const c10::optional<at::Tensor>& dres);
 std::vector<at::Tensor> subln_swiglu_fwd(const at::Tensor& o, const at::Tensor& g, double eps, int64_t D);
 std::vector<at::Tensor> subln_swiglu_bwd(const at::Tensor& dout, const at::Tensor& o, const at::Tensor& g,
-                                         const at::Tensor& rstd, int64_t D);
+                                         const at::Tensor& rstd, int64_t D, const c10::optional<at::Tensor>& dg_out);
 at::Tensor swiglu_fwd(const at::Tensor& x, const at::Tensor& y);
-std::vector<at::Tensor> swiglu_bwd(const at::Tensor& x, const at::Tensor& y, const at::Tensor& g);
+std::vector<at::Tensor> swiglu_bwd(const at::Tensor& x, const at::Tensor& y, const at::Tensor& g,
+                                   const c10::optional<at::Tensor>& dx_out, const c10::optional<at::Tensor>& dy_out);
+at::Tensor gate_cumsum_fwd(const at::Tensor& y, int64_t B, int64_t L, double normalizer);
+void gate_cumsum_bwd(const at::Tensor& dg, const at::Tensor& y, at::Tensor& dy, double normalizer);
 at::Tensor rope_fwd(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t, bool conj);
 at::Tensor embedding_fwd(const at::Tensor& tok, const at::Tensor& w, double scale);
 at::Tensor embedding_bwd(const at::Tensor& tok, const at::Tensor& dy, int64_t V, double scale,
@@ -33,10 +36,17 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& q, const at::Tensor& k, 
                                       int64_t window, double scale);
 std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                       const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, bool causal,
-                                      int64_t window, double scale);
+                                      int64_t window, double scale, const c10::optional<at::Tensor>& dq_out,
+                                      const c10::optional<at::Tensor>& dk_out, const c10::optional<at::Tensor>& dv_out,
+                                      const c10::optional<at::Tensor>& rope_cos,
+                                      const c10::optional<at::Tensor>& rope_sin, bool rope_q, bool rope_k);
 at::Tensor retention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& gcum);
 std::vector<at::Tensor> retention_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
-                                      const at::Tensor& v, const at::Tensor& gcum, const at::Tensor& o);
+                                      const at::Tensor& v, const at::Tensor& gcum, const at::Tensor& o,
+                                      const c10::optional<at::Tensor>& dq_out, const c10::optional<at::Tensor>& dk_out,
+                                      const c10::optional<at::Tensor>& dv_out,
+                                      const c10::optional<at::Tensor>& rope_cos,
+                                      const c10::optional<at::Tensor>& rope_sin);
 std::vector<at::Tensor> ipc_alloc(int64_t nbytes);
 int64_t ipc_open(const at::Tensor& handle_bytes);
 void ipc_close(int64_t ptr);
@@ -79,11 +89,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &fyb::gemm, "C = A @ B^T on tcgen05 (operands K-major or MN-major)", py::arg("A"), py::arg("B"),
         py::arg("C"), py::arg("a_mn_major"), py::arg("b_mn_major"), py::arg("residual") = py::none());
   m.def("rms_norm_fwd", &fyb::rms_norm_fwd);
-  m.def("rms_norm_bwd", &fyb::rms_norm_bwd);
+  m.def("rms_norm_bwd", &fyb::rms_norm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
+        py::arg("dres") = py::none());
   m.def("subln_swiglu_fwd", &fyb::subln_swiglu_fwd);
-  m.def("subln_swiglu_bwd", &fyb::subln_swiglu_bwd);
+  m.def("subln_swiglu_bwd", &fyb::subln_swiglu_bwd, py::arg("dout"), py::arg("o"), py::arg("g"), py::arg("rstd"),
+        py::arg("D"), py::arg("dg_out") = py::none());
   m.def("swiglu_fwd", &fyb::swiglu_fwd);
-  m.def("swiglu_bwd", &fyb::swiglu_bwd);
+  m.def("swiglu_bwd", &fyb::swiglu_bwd, py::arg("x"), py::arg("y"), py::arg("g"), py::arg("dx_out") = py::none(),
+        py::arg("dy_out") = py::none());
+  m.def("gate_cumsum_fwd", &fyb::gate_cumsum_fwd);
+  m.def("gate_cumsum_bwd", &fyb::gate_cumsum_bwd);
   m.def("rope_fwd", &fyb::rope_fwd);
   m.def("embedding_fwd", &fyb::embedding_fwd);
   m.def("embedding_bwd", &fyb::embedding_bwd, py::arg("tok"), py::arg("dy"), py::arg("V"), py::arg("scale"),
@@ -94,9 +109,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adam_step", &fyb::adam_step);
   m.def("sq_norm", &fyb::sq_norm);
   m.def("attention_fwd", &fyb::attention_fwd);
-  m.def("attention_bwd", &fyb::attention_bwd);
+  m.def("attention_bwd", &fyb::attention_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),
+        py::arg("o"), py::arg("lse"), py::arg("causal"), py::arg("window"), py::arg("scale"),
+        py::arg("dq_out") = py::none(), py::arg("dk_out") = py::none(), py::arg("dv_out") = py::none(),
+        py::arg("rope_cos") = py::none(), py::arg("rope_sin") = py::none(), py::arg("rope_q") = false,
+        py::arg("rope_k") = false);
   m.def("retention_fwd", &fyb::retention_fwd);
-  m.def("retention_bwd", &fyb::retention_bwd);
+  m.def("retention_bwd", &fyb::retention_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),
+        py::arg("gcum"), py::arg("o"), py::arg("dq_out") = py::none(), py::arg("dk_out") = py::none(),
+        py::arg("dv_out") = py::none(), py::arg("rope_cos") = py::none(), py::arg("rope_sin") = py::none());
   m.def("ipc_alloc", &fyb::ipc_alloc, "cudaMalloc'd byte buffer + its CUDA IPC handle");
   m.def("ipc_open", &fyb::ipc_open);
   m.def("ipc_close", &fyb::ipc_close);

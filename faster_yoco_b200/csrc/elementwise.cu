@@ -53,7 +53,7 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t l
 
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ y,
                                   int64_t ldy, const __nv_bfloat16* __restrict__ g, __nv_bfloat16* __restrict__ dx,
-                                  __nv_bfloat16* __restrict__ dy, int64_t M, int N) {
+                                  __nv_bfloat16* __restrict__ dy, int64_t M, int N, int64_t lddx, int64_t lddy) {
   const int per_row = N / 8;
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= M * per_row) return;
@@ -69,8 +69,8 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t l
     da[k] = s * (1.0f + a[k] * (1.0f - s)) * gg[k] * b[k];
     db[k] = a[k] * s * gg[k];
   }
-  store8(dx + r * N + c, da);
-  store8(dy + r * N + c, db);
+  store8(dx + r * lddx + c, da);
+  store8(dy + r * lddy + c, db);
 }
 
 // ------------------------------------------------------------------------------------------------------------------
@@ -347,10 +347,97 @@ __global__ void sq_final_kernel(const float* __restrict__ part, int P, float* __
   if (threadIdx.x == 0) out[0] = red[0];
 }
 
+// ------------------------------------------------------------------------------------------------------------------
+// retention gates: gcum[b, h, t] = sum_{s<=t} logsigmoid(y[b*L+s, h]) / normalizer (fp32), one warp per (b, h);
+// backward: dy[b*L+t, h] = sigmoid(-y) / normalizer * sum_{s>=t} dgcum[b, h, s]
+
+__device__ __forceinline__ float logsigmoidf_(float x) { return fminf(x, 0.f) - log1pf(__expf(-fabsf(x))); }
+
+__global__ void gate_cumsum_fwd_kernel(const __nv_bfloat16* __restrict__ y, int64_t ldy, float* __restrict__ gcum,
+                                       int B, int L, int H, float inv_norm) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= B * H) return;
+  const int b = w / H, h = w % H;
+  float carry = 0.f;
+  float* out = gcum + static_cast<int64_t>(w) * L;
+  for (int t0 = 0; t0 < L; t0 += 32) {
+    const int t = t0 + lane;
+    // F.logsigmoid on bf16 rounds its output to bf16; the division by the normaliser (a power of two) is exact
+    float v = t < L ? bf16_round(logsigmoidf_(__bfloat162float(y[(static_cast<int64_t>(b) * L + t) * ldy + h]))) *
+                          inv_norm
+                    : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += u;
+    }
+    v += carry;
+    if (t < L) out[t] = v;
+    carry = __shfl_sync(0xffffffffu, v, 31);
+  }
+}
+
+__global__ void gate_cumsum_bwd_kernel(const float* __restrict__ dg, const __nv_bfloat16* __restrict__ y, int64_t ldy,
+                                       __nv_bfloat16* __restrict__ dy, int64_t lddy, int B, int L, int H,
+                                       float inv_norm) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= B * H) return;
+  const int b = w / H, h = w % H;
+  const float* src = dg + static_cast<int64_t>(w) * L;
+  float carry = 0.f;
+  for (int t1 = L; t1 > 0; t1 -= 32) {
+    const int t = t1 - 1 - lane;                 // lane 0 takes the latest position of the chunk
+    float v = t >= 0 ? src[t] : 0.f;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += u;
+    }
+    v += carry;
+    if (t >= 0) {
+      const int64_t row = static_cast<int64_t>(b) * L + t;
+      const float x = __bfloat162float(y[row * ldy + h]);
+      dy[row * lddy + h] = __float2bfloat16_rn(v * inv_norm / (1.0f + __expf(x)));
+    }
+    carry = __shfl_sync(0xffffffffu, v, 31);
+  }
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------------------------------------------------------
 // host entry points
+
+at::Tensor gate_cumsum_fwd(const at::Tensor& y, int64_t B, int64_t L, double normalizer) {
+  FYB_CHECK(y.is_cuda() && y.scalar_type() == at::kBFloat16 && y.dim() == 2 && y.stride(1) == 1 && y.size(0) == B * L,
+            "gate_cumsum_fwd: bf16 [B*L, H] view expected");
+  c10::cuda::CUDAGuard guard(y.device());
+  const int H = static_cast<int>(y.size(1));
+  auto g = at::empty({B, H, L}, y.options().dtype(at::kFloat));
+  const int warps = static_cast<int>(B) * H;
+  if (warps > 0)
+    gate_cumsum_fwd_kernel<<<(warps * 32 + 255) / 256, 256, 0, cur_stream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0), g.data_ptr<float>(), (int)B, (int)L, H,
+        static_cast<float>(1.0 / normalizer));
+  check_launch("gate_cumsum_fwd");
+  return g;
+}
+
+void gate_cumsum_bwd(const at::Tensor& dg, const at::Tensor& y, at::Tensor& dy, double normalizer) {
+  const int64_t B = dg.size(0), H = dg.size(1), L = dg.size(2);
+  FYB_CHECK(dg.is_contiguous() && dg.scalar_type() == at::kFloat, "gate_cumsum_bwd: dg fp32 [B, H, L]");
+  FYB_CHECK(dy.stride(1) == 1 && dy.size(0) == B * L && dy.size(1) == H, "gate_cumsum_bwd: dy view [B*L, H]");
+  c10::cuda::CUDAGuard guard(y.device());
+  const int warps = static_cast<int>(B * H);
+  if (warps > 0)
+    gate_cumsum_bwd_kernel<<<(warps * 32 + 255) / 256, 256, 0, cur_stream()>>>(
+        dg.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
+        reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()), dy.stride(0), (int)B, (int)L, (int)H,
+        static_cast<float>(1.0 / normalizer));
+  check_launch("gate_cumsum_bwd");
+}
 
 at::Tensor swiglu_fwd(const at::Tensor& x, const at::Tensor& y) {
   FYB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16 && x.dim() == 2 &&
@@ -370,19 +457,28 @@ at::Tensor swiglu_fwd(const at::Tensor& x, const at::Tensor& y) {
   return out;
 }
 
-std::vector<at::Tensor> swiglu_bwd(const at::Tensor& x, const at::Tensor& y, const at::Tensor& g) {
+std::vector<at::Tensor> swiglu_bwd(const at::Tensor& x, const at::Tensor& y, const at::Tensor& g,
+                                   const c10::optional<at::Tensor>& dx_out, const c10::optional<at::Tensor>& dy_out) {
   const int64_t M = x.size(0), N = x.size(1);
   FYB_CHECK(g.is_contiguous() && g.size(0) == M && g.size(1) == N, "swiglu_bwd: grad");
   c10::cuda::CUDAGuard guard(x.device());
-  auto dx = at::empty({M, N}, x.options());
-  auto dy = at::empty({M, N}, x.options());
+  auto pick = [&](const c10::optional<at::Tensor>& o) {
+    if (o.has_value() && o->defined()) {
+      FYB_CHECK(o->size(0) == M && o->size(1) == N && o->stride(1) == 1 && o->stride(0) % 8 == 0,
+                "swiglu_bwd: output view");
+      return *o;
+    }
+    return at::empty({M, N}, x.options());
+  };
+  auto dx = pick(dx_out);
+  auto dy = pick(dy_out);
   const int64_t n = M * (N / 8);
   if (n > 0)
     swiglu_bwd_kernel<<<(n + 255) / 256, 256, 0, cur_stream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
         reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
         reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()),
-        reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()), M, (int)N);
+        reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()), M, (int)N, dx.stride(0), dy.stride(0));
   check_launch("swiglu_bwd");
   return {dx, dy};
 }

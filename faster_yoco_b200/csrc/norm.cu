@@ -91,7 +91,7 @@ __global__ void rms_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_b
 __global__ void rms_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                                const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
                                __nv_bfloat16* __restrict__ dx, float* __restrict__ part, int M, int N,
-                               int rows_per_cta) {
+                               int rows_per_cta, const __nv_bfloat16* __restrict__ dres = nullptr) {
   __shared__ float red[32];
   extern __shared__ float dw_acc[];   // N floats (only when w != nullptr)
   if (w != nullptr)
@@ -135,6 +135,13 @@ __global__ void rms_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) o[i] = r * (g[i] - f[i] * r * dot);
+      }
+      if (dres != nullptr) {
+        // gradient reaching x through the residual branch: bf16(dx_norm) + dres, as autograd's bf16 sum
+        float rr[8];
+        load8(dres + off + c, rr);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = bf16_round(o[i]) + rr[i];
       }
       store8(dx + off + c, o);
     }
@@ -195,7 +202,7 @@ template <int D>
 __global__ void subln_swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ o,
                                         const __nv_bfloat16* __restrict__ g, int64_t ldg,
                                         const float* __restrict__ rstd, __nv_bfloat16* __restrict__ d_o,
-                                        __nv_bfloat16* __restrict__ dg, int T, int H) {
+                                        __nv_bfloat16* __restrict__ dg, int T, int H, int64_t lddg) {
   constexpr int TPR = D / 8;
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t hrow = gid / TPR;
@@ -222,7 +229,7 @@ __global__ void subln_swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dout, 
       dn[i] = bf16_round(gv[i] * s * dv[i]);
       dot += dn[i] * f[i] * r;
     }
-    store8(dg + ooff, dgo);
+    store8(dg + t * lddg + h * D + sub * 8, dgo);
   }
 #pragma unroll
   for (int s = TPR / 2; s > 0; s >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, s);
@@ -260,7 +267,8 @@ std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const c10::optional<at
 // Gradient of RMSNorm. The weight gradient's per-CTA partials live in `part` (P x N fp32); pass an empty tensor to
 // have it allocated here.
 std::vector<at::Tensor> rms_norm_bwd_impl(const at::Tensor& dy, const at::Tensor& x, const c10::optional<at::Tensor>& w,
-                                          const at::Tensor& rstd, float* part, int P) {
+                                          const at::Tensor& rstd, float* part, int P,
+                                          const __nv_bfloat16* dres = nullptr) {
   const int64_t M = x.size(0), N = x.size(1);
   const bool has_w = w.has_value() && w->defined();
   auto dx = at::empty_like(x);
@@ -278,7 +286,8 @@ std::vector<at::Tensor> rms_norm_bwd_impl(const at::Tensor& dy, const at::Tensor
   kern<<<grid, kNormThreads, shm, cur_stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
       has_w ? reinterpret_cast<const __nv_bfloat16*>(w->data_ptr()) : nullptr, rstd.data_ptr<float>(),
-      reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), part, static_cast<int>(M), static_cast<int>(N), rows_per);
+      reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), part, static_cast<int>(M), static_cast<int>(N), rows_per,
+      dres);
   check_launch("rms_bwd");
   if (has_w) {
     col_sum_kernel<<<(N + 255) / 256, 256, 0, cur_stream()>>>(part, reinterpret_cast<__nv_bfloat16*>(dw.data_ptr()),
@@ -291,7 +300,7 @@ std::vector<at::Tensor> rms_norm_bwd_impl(const at::Tensor& dy, const at::Tensor
 int rms_bwd_ctas(int64_t M) { return static_cast<int>(std::min<int64_t>(M, 2 * num_sms())); }
 
 std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const c10::optional<at::Tensor>& w,
-                                     const at::Tensor& rstd) {
+                                     const at::Tensor& rstd, const c10::optional<at::Tensor>& dres) {
   FYB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.is_contiguous() &&
                 dy.is_contiguous() && dy.sizes() == x.sizes() && dy.scalar_type() == at::kBFloat16,
             "rms_norm_bwd: contiguous bf16 [M, N] expected");
@@ -301,7 +310,13 @@ std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, 
   const bool has_w = w.has_value() && w->defined();
   at::Tensor part;
   if (has_w) part = at::empty({P, x.size(1)}, x.options().dtype(at::kFloat));
-  return rms_norm_bwd_impl(dy, x, w, rstd, has_w ? part.data_ptr<float>() : nullptr, P);
+  const __nv_bfloat16* dr = nullptr;
+  if (dres.has_value() && dres->defined()) {
+    FYB_CHECK(dres->is_contiguous() && dres->sizes() == x.sizes() && dres->scalar_type() == at::kBFloat16,
+              "rms_norm_bwd: dres must be contiguous bf16 like x");
+    dr = reinterpret_cast<const __nv_bfloat16*>(dres->data_ptr());
+  }
+  return rms_norm_bwd_impl(dy, x, w, rstd, has_w ? part.data_ptr<float>() : nullptr, P, dr);
 }
 
 std::vector<at::Tensor> subln_swiglu_fwd(const at::Tensor& o, const at::Tensor& g, double eps, int64_t D) {
@@ -333,13 +348,19 @@ std::vector<at::Tensor> subln_swiglu_fwd(const at::Tensor& o, const at::Tensor& 
 }
 
 std::vector<at::Tensor> subln_swiglu_bwd(const at::Tensor& dout, const at::Tensor& o, const at::Tensor& g,
-                                         const at::Tensor& rstd, int64_t D) {
+                                         const at::Tensor& rstd, int64_t D, const c10::optional<at::Tensor>& dg_out) {
   FYB_CHECK(dout.is_contiguous() && dout.sizes() == o.sizes(), "subln_swiglu_bwd: dout");
   const int64_t T = o.size(0), HD = o.size(1);
   const int H = static_cast<int>(HD / D);
   c10::cuda::CUDAGuard guard(o.device());
   auto d_o = at::empty_like(o);
-  auto dg = at::empty({T, HD}, o.options());
+  at::Tensor dg;
+  if (dg_out.has_value() && dg_out->defined()) {
+    dg = *dg_out;
+    FYB_CHECK(dg.sizes() == o.sizes() && dg.stride(1) == 1 && dg.stride(0) % 8 == 0, "subln_swiglu_bwd: dg_out");
+  } else {
+    dg = at::empty({T, HD}, o.options());
+  }
   const int64_t threads = T * H * (D / 8);
   const int blocks = static_cast<int>((threads + 255) / 256);
   if (T > 0) {
@@ -348,13 +369,13 @@ std::vector<at::Tensor> subln_swiglu_bwd(const at::Tensor& dout, const at::Tenso
           reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
           reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()),
           g.stride(0), rstd.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(d_o.data_ptr()),
-          reinterpret_cast<__nv_bfloat16*>(dg.data_ptr()), (int)T, H);
+          reinterpret_cast<__nv_bfloat16*>(dg.data_ptr()), (int)T, H, dg.stride(0));
     else
       subln_swiglu_bwd_kernel<64><<<blocks, 256, 0, cur_stream()>>>(
           reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
           reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()),
           g.stride(0), rstd.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(d_o.data_ptr()),
-          reinterpret_cast<__nv_bfloat16*>(dg.data_ptr()), (int)T, H);
+          reinterpret_cast<__nv_bfloat16*>(dg.data_ptr()), (int)T, H, dg.stride(0));
   }
   check_launch("subln_swiglu_bwd");
   return {d_o, dg};

@@ -41,8 +41,29 @@ class DecoderLayer(nn.Module):
         self.ffn = FeedForwardNetwork(args.dim, args.hidden_dim)
         self.final_layer_norm = RMSNorm(args.dim, eps=args.norm_eps)
 
+    def _fused(self, x, key, value, rel_pos):
+        """The whole layer as one autograd Function (native training path, see models/fused.py)."""
+        from . import fused as Fz
+        m, f = self.mixer, self.ffn
+        cos, sin = rel_pos
+        common = (self.final_layer_norm.weight, f.fc1_gate.weight, f.fc2.weight)
+        if self.is_cross_layer:
+            cfg = (m.num_heads, m.head_dim, self.args.norm_eps, f.ffn_dim)
+            return Fz.CrossLayerFn.apply(x, key, value, self.mixer_layer_norm.weight, m.q_proj.weight,
+                                         m.out_proj.weight, *common, cos, sin, cfg)
+        if self.args.sliding_window is not None:
+            cfg = (m.num_heads, m.head_dim, self.args.norm_eps, m.window_size, f.ffn_dim)
+            return Fz.SelfWindowLayerFn.apply(x, self.mixer_layer_norm.weight, m.qkv_proj.weight, m.out_proj.weight,
+                                              *common, cos, sin, cfg)
+        cfg = (m.num_heads, m.head_dim, self.args.norm_eps, m.subln_eps, m.gate_logit_normalizer, f.ffn_dim)
+        return Fz.SelfRetentionLayerFn.apply(x, self.mixer_layer_norm.weight, m.qkvg_proj.weight, m.out_proj.weight,
+                                             *common, cos, sin, cfg)
+
     def forward(self, x, start_pos=0, key=None, value=None, rel_pos=None, incremental_state=None,
                 is_prefilling=False):
+        from .fused import fused_path_ok
+        if incremental_state is None and self.training and fused_path_ok(x, self.mixer.head_dim):
+            return self._fused(x, key, value, rel_pos)
         residual = x
         h = self.mixer_layer_norm(x)
         if self.is_cross_layer:
@@ -129,18 +150,25 @@ class CrossDecoder(nn.Module):
         self.rope = _RopeCache(self.head_dim, args.rope_theta, max(args.max_seq_len, 1))
         self.checkpoint_activations = args.checkpoint_activations
 
-    def shared_kv(self, x, start_pos=0):
+    def shared_kv(self, x, start_pos=0, fused: bool = False):
         B, L, _ = x.shape
         kvd = self.head_dim * self.num_heads
-        y = self.kv_proj(self.kv_layer_norm(x))
         rel_pos = self.rope.get(start_pos, L, x.dtype, x.device)
+        if fused:
+            from .fused import SharedKVFn
+            key, value = SharedKVFn.apply(x, self.kv_layer_norm.weight, self.kv_proj.weight, *rel_pos,
+                                          (self.num_heads, self.head_dim, self.args.norm_eps))
+            return key, value, rel_pos
+        y = self.kv_proj(self.kv_layer_norm(x))
         key = ops.rope(y[..., :kvd].view(B, L, self.num_heads, self.head_dim), *rel_pos)
         value = y[..., kvd:].view(B, L, self.num_heads, self.head_dim)
         return key, value, rel_pos
 
     def forward(self, x, incremental_state=None, start_pos=0, skip_cross_decoder=False):
         bsz, seqlen, dim = x.shape
-        key, value, rel_pos = self.shared_kv(x, start_pos)
+        from .fused import fused_path_ok
+        fused = incremental_state is None and self.training and fused_path_ok(x, self.head_dim)
+        key, value, rel_pos = self.shared_kv(x, start_pos, fused=fused)
         if incremental_state is not None:
             st = incremental_state
             if "prev_key" not in st:
