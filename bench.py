@@ -37,8 +37,9 @@ def parse():
     p.add_argument("--seq-len", type=int, default=2048)
     p.add_argument("--batch", type=int, default=1, help="sequences per GPU")
     p.add_argument("--kernels", default="native", choices=["native", "torch"])
-    p.add_argument("--comm", default="nccl", choices=["nccl", "fused"])
-    p.add_argument("--graph", type=int, default=0, help="capture the whole update as one CUDA graph")
+    p.add_argument("--comm", default="fused", choices=["nccl", "fused"],
+                   help="fused: NVLink peer-memory collectives overlapped with compute; nccl: the baseline path")
+    p.add_argument("--graph", type=int, default=1, help="capture the whole update as one CUDA graph")
     p.add_argument("--sliding-window", type=int, default=None)
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-e2e", action="store_true")
@@ -195,13 +196,11 @@ def main():
                "d2h_bytes_per_step": 4}
 
     launches = None
-    if args.count_launches and not args.graph:
+    if args.count_launches:
         try:
             launches = count_our_launches(lambda: step(0)) * args.steps
         except Exception:
             launches = None
-    elif args.count_launches:
-        launches = None
 
     if rank == 0:
         out = {

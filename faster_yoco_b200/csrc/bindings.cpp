@@ -50,14 +50,18 @@ std::vector<at::Tensor> retention_bwd(const at::Tensor& dout, const at::Tensor& 
 std::vector<at::Tensor> ipc_alloc(int64_t nbytes);
 int64_t ipc_open(const at::Tensor& handle_bytes);
 void ipc_close(int64_t ptr);
-void flag_barrier(const std::vector<int64_t>& peer_flags, const at::Tensor& my_flags, int64_t rank, int64_t slot,
-                  int64_t epoch);
+void flag_barrier(const std::vector<int64_t>& peer_flags, const at::Tensor& my_flags, const at::Tensor& counters,
+                  int64_t rank, int64_t slot);
 void reduce_owner(const std::vector<int64_t>& peer_grads, at::Tensor& out, int64_t base, int64_t n, at::Tensor& part,
                   at::Tensor& sq);
 void gather_segments(const std::vector<int64_t>& peer_params, at::Tensor& dst, const at::Tensor& segs, int64_t rank,
                      int64_t ctas);
-void mailbox_put(const std::vector<int64_t>& peer_boxes, const at::Tensor& vals, int64_t rank, int64_t slot_base);
-void mailbox_sum(const at::Tensor& box, at::Tensor& out, int64_t world, int64_t slot_base);
+void reduce_ranges(const std::vector<int64_t>& peer_grads, at::Tensor& out, const at::Tensor& ranges, at::Tensor& part,
+                   int64_t ctas);
+void sum_partials(const at::Tensor& part, at::Tensor& out);
+void mailbox_put(const std::vector<int64_t>& peer_boxes, const at::Tensor& vals, int64_t rank,
+                 const at::Tensor& counter);
+void mailbox_sum(const at::Tensor& box, at::Tensor& out, int64_t world, at::Tensor& counter);
 
 // one status word per device, allocated once (zero = ok)
 int* status_ptr() {
@@ -124,6 +128,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flag_barrier", &fyb::flag_barrier);
   m.def("reduce_owner", &fyb::reduce_owner);
   m.def("gather_segments", &fyb::gather_segments);
+  m.def("reduce_ranges", &fyb::reduce_ranges);
+  m.def("sum_partials", &fyb::sum_partials);
   m.def("mailbox_put", &fyb::mailbox_put);
   m.def("mailbox_sum", &fyb::mailbox_sum);
   m.def("status", &fyb::status_tensor, "device status word of the kernels with bounded waits");

@@ -42,9 +42,18 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
   return v;
 }
 
-// flags layout on every rank: [slots][kMaxWorld] uint32; rank r writes epoch into flags_q[slot][r] on every peer q
-__global__ void flag_barrier_kernel(PeerPtrs peer_flags, uint32_t* my_flags, int rank, int world, int slot,
-                                    uint32_t epoch, int* status) {
+// flags layout on every rank: [slots][kMaxWorld] uint32; rank r writes epoch into flags_q[slot][r] on every peer q.
+// The epoch of a slot is a per-rank device counter incremented by the barrier itself, so a captured CUDA graph
+// replays with fresh epochs (every rank runs the same barrier sequence, so the counters agree).
+__global__ void flag_barrier_kernel(PeerPtrs peer_flags, uint32_t* my_flags, uint32_t* counters, int rank, int world,
+                                    int slot, int* status) {
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0) {
+    s_epoch = counters[slot] + 1u;
+    counters[slot] = s_epoch;
+  }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
   if (threadIdx.x < world) {
     __threadfence_system();
     uint32_t* f = reinterpret_cast<uint32_t*>(const_cast<void*>(peer_flags.p[threadIdx.x])) + slot * kMaxWorld + rank;
@@ -121,6 +130,67 @@ __global__ void reduce_owner_kernel(PeerPtrs grads, __nv_bfloat16* out, int64_t 
   }
 }
 
+// owner-side reduction over a list of ranges [n][2] = (element offset, count) of the flat gradient buffers (ranges
+// that this rank owns); same arithmetic as reduce_owner_kernel; per-CTA partial sums of squares in part[blockIdx.x]
+__global__ void reduce_ranges_kernel(PeerPtrs grads, __nv_bfloat16* out, const int64_t* __restrict__ ranges,
+                                     int nranges, int world, float inv_world, float* part) {
+  float ss = 0.f;
+  for (int rg = 0; rg < nranges; ++rg) {
+    const int64_t base = ranges[2 * rg], n = ranges[2 * rg + 1];
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 8;
+    for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < n; i += stride) {
+      if (i + 8 <= n) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        uint4 u[kMaxWorld];
+#pragma unroll
+        for (int r = 0; r < kMaxWorld; ++r)
+          if (r < world)
+            u[r] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(grads.p[r]) + base + i);
+#pragma unroll
+        for (int r = 0; r < kMaxWorld; ++r) {
+          if (r < world) {
+            const uint32_t w[4] = {u[r].x, u[r].y, u[r].z, u[r].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = unpack_bf16(w[k]);
+              acc[2 * k] += f.x;
+              acc[2 * k + 1] += f.y;
+            }
+          }
+        }
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float a = bf16_round(acc[2 * k] * inv_world), b = bf16_round(acc[2 * k + 1] * inv_world);
+          ss += a * a + b * b;
+          o[k] = pack_bf16(a, b);
+        }
+        *reinterpret_cast<uint4*>(out + base + i) = make_uint4(o[0], o[1], o[2], o[3]);
+      } else {
+        for (int64_t j = i; j < n; ++j) {
+          float acc = 0.f;
+#pragma unroll
+          for (int r = 0; r < kMaxWorld; ++r)
+            if (r < world) acc += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(grads.p[r])[base + j]);
+          const float a = bf16_round(acc * inv_world);
+          ss += a * a;
+          out[base + j] = __float2bfloat16_rn(a);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+    part[blockIdx.x] = t;
+  }
+}
+
 __global__ void sum_partials_kernel(const float* __restrict__ part, int P, float* __restrict__ out) {
   __shared__ float red[1024];
   float s = 0.f;
@@ -145,9 +215,18 @@ __global__ void gather_segments_kernel(PeerPtrs src, __nv_bfloat16* dst, const i
     const uint4* sp = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(src.p[owner]) + off);
     uint4* dp = reinterpret_cast<uint4*>(dst + off);
     const int64_t nv = cnt / 8;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nv;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-      dp[i] = sp[i];
+    const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    // 4 independent 16-byte NVLink loads in flight per thread (remote latency is ~microseconds)
+    int64_t i = tid;
+    for (; i + 3 * nthr < nv; i += 4 * nthr) {
+      const uint4 a = sp[i], b = sp[i + nthr], c = sp[i + 2 * nthr], d = sp[i + 3 * nthr];
+      dp[i] = a;
+      dp[i + nthr] = b;
+      dp[i + 2 * nthr] = c;
+      dp[i + 3 * nthr] = d;
+    }
+    for (; i < nv; i += nthr) dp[i] = sp[i];
     const int64_t tail0 = nv * 8;
     if (blockIdx.x == 0)
       for (int64_t j = tail0 + threadIdx.x; j < cnt; j += blockDim.x)
@@ -158,7 +237,8 @@ __global__ void gather_segments_kernel(PeerPtrs src, __nv_bfloat16* dst, const i
 // each rank writes its k values into slot [rank] of every peer's mailbox, then (after a flag barrier) sums the
 // world slots of its own mailbox in rank order
 __global__ void mailbox_put_kernel(PeerPtrs boxes, const float* __restrict__ vals, int k, int rank, int world,
-                                   int slot_base) {
+                                   const uint32_t* __restrict__ counter) {
+  const int slot_base = static_cast<int>(counter[0] & 1u) * kMaxWorld * 32;
   for (int q = 0; q < world; ++q) {
     float* box = reinterpret_cast<float*>(const_cast<void*>(boxes.p[q])) + slot_base + rank * 32;
     for (int i = threadIdx.x; i < k; i += blockDim.x) box[i] = vals[i];
@@ -166,12 +246,15 @@ __global__ void mailbox_put_kernel(PeerPtrs boxes, const float* __restrict__ val
 }
 
 __global__ void mailbox_sum_kernel(const float* __restrict__ box, float* __restrict__ out, int k, int world,
-                                   int slot_base) {
+                                   uint32_t* __restrict__ counter) {
+  const int slot_base = static_cast<int>(counter[0] & 1u) * kMaxWorld * 32;
   for (int i = threadIdx.x; i < k; i += blockDim.x) {
     float s = 0.f;
     for (int r = 0; r < world; ++r) s += box[slot_base + r * 32 + i];
     out[i] = s;
   }
+  __syncthreads();
+  if (threadIdx.x == 0) counter[0] += 1u;
 }
 
 PeerPtrs to_ptrs(const std::vector<int64_t>& v) {
@@ -216,12 +299,13 @@ void ipc_close(int64_t ptr) { FYB_CUDA(cudaIpcCloseMemHandle(reinterpret_cast<vo
 
 // ------------------------------------------------------------------------------------------------------- kernels
 
-void flag_barrier(const std::vector<int64_t>& peer_flags, const at::Tensor& my_flags, int64_t rank, int64_t slot,
-                  int64_t epoch) {
+void flag_barrier(const std::vector<int64_t>& peer_flags, const at::Tensor& my_flags, const at::Tensor& counters,
+                  int64_t rank, int64_t slot) {
   const int world = static_cast<int>(peer_flags.size());
+  FYB_CHECK(counters.is_cuda() && counters.numel() > slot, "flag_barrier: counters");
   flag_barrier_kernel<<<1, 32, 0, cur_stream()>>>(to_ptrs(peer_flags), reinterpret_cast<uint32_t*>(my_flags.data_ptr()),
-                                                  static_cast<int>(rank), world, static_cast<int>(slot),
-                                                  static_cast<uint32_t>(epoch), status_ptr());
+                                                  reinterpret_cast<uint32_t*>(counters.data_ptr()),
+                                                  static_cast<int>(rank), world, static_cast<int>(slot), status_ptr());
   check_launch("flag_barrier");
 }
 
@@ -242,6 +326,29 @@ void reduce_owner(const std::vector<int64_t>& peer_grads, at::Tensor& out, int64
   check_launch("reduce_owner_sum");
 }
 
+// reduce the listed owned ranges; part (>= ctas floats) receives the per-CTA sums of squares
+void reduce_ranges(const std::vector<int64_t>& peer_grads, at::Tensor& out, const at::Tensor& ranges, at::Tensor& part,
+                   int64_t ctas) {
+  const int world = static_cast<int>(peer_grads.size());
+  FYB_CHECK(ranges.is_cuda() && ranges.scalar_type() == at::kLong && ranges.dim() == 2 && ranges.size(1) == 2,
+            "reduce_ranges: ranges must be a device int64 [n, 2]");
+  FYB_CHECK(part.numel() >= ctas && part.scalar_type() == at::kFloat, "reduce_ranges: partials buffer too small");
+  if (ranges.size(0) == 0) {
+    part.zero_();
+    return;
+  }
+  reduce_ranges_kernel<<<static_cast<int>(ctas), 256, 0, cur_stream()>>>(
+      to_ptrs(peer_grads), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ranges.data_ptr<int64_t>(),
+      static_cast<int>(ranges.size(0)), world, 1.0f / static_cast<float>(world), part.data_ptr<float>());
+  check_launch("reduce_ranges");
+}
+
+void sum_partials(const at::Tensor& part, at::Tensor& out) {
+  sum_partials_kernel<<<1, 1024, 0, cur_stream()>>>(part.data_ptr<float>(), static_cast<int>(part.numel()),
+                                                   out.data_ptr<float>());
+  check_launch("sum_partials");
+}
+
 void gather_segments(const std::vector<int64_t>& peer_params, at::Tensor& dst, const at::Tensor& segs, int64_t rank,
                      int64_t ctas) {
   FYB_CHECK(segs.is_cuda() && segs.scalar_type() == at::kLong && segs.dim() == 2 && segs.size(1) == 3,
@@ -253,19 +360,20 @@ void gather_segments(const std::vector<int64_t>& peer_params, at::Tensor& dst, c
   check_launch("gather_segments");
 }
 
-void mailbox_put(const std::vector<int64_t>& peer_boxes, const at::Tensor& vals, int64_t rank, int64_t slot_base) {
+void mailbox_put(const std::vector<int64_t>& peer_boxes, const at::Tensor& vals, int64_t rank,
+                 const at::Tensor& counter) {
   const int world = static_cast<int>(peer_boxes.size());
   FYB_CHECK(vals.numel() <= 32 && vals.scalar_type() == at::kFloat, "mailbox_put: at most 32 fp32 values");
   mailbox_put_kernel<<<1, 32, 0, cur_stream()>>>(to_ptrs(peer_boxes), vals.data_ptr<float>(),
                                                  static_cast<int>(vals.numel()), static_cast<int>(rank), world,
-                                                 static_cast<int>(slot_base));
+                                                 reinterpret_cast<const uint32_t*>(counter.data_ptr()));
   check_launch("mailbox_put");
 }
 
-void mailbox_sum(const at::Tensor& box, at::Tensor& out, int64_t world, int64_t slot_base) {
+void mailbox_sum(const at::Tensor& box, at::Tensor& out, int64_t world, at::Tensor& counter) {
   mailbox_sum_kernel<<<1, 32, 0, cur_stream()>>>(box.data_ptr<float>(), out.data_ptr<float>(),
                                                  static_cast<int>(out.numel()), static_cast<int>(world),
-                                                 static_cast<int>(slot_base));
+                                                 reinterpret_cast<uint32_t*>(counter.data_ptr()));
   check_launch("mailbox_sum");
 }
 

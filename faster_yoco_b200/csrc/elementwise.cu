@@ -353,55 +353,76 @@ __global__ void sq_final_kernel(const float* __restrict__ part, int P, float* __
 
 __device__ __forceinline__ float logsigmoidf_(float x) { return fminf(x, 0.f) - log1pf(__expf(-fabsf(x))); }
 
-__global__ void gate_cumsum_fwd_kernel(const __nv_bfloat16* __restrict__ y, int64_t ldy, float* __restrict__ gcum,
-                                       int B, int L, int H, float inv_norm) {
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (w >= B * H) return;
-  const int b = w / H, h = w % H;
-  float carry = 0.f;
-  float* out = gcum + static_cast<int64_t>(w) * L;
-  for (int t0 = 0; t0 < L; t0 += 32) {
-    const int t = t0 + lane;
-    // F.logsigmoid on bf16 rounds its output to bf16; the division by the normaliser (a power of two) is exact
-    float v = t < L ? bf16_round(logsigmoidf_(__bfloat162float(y[(static_cast<int64_t>(b) * L + t) * ldy + h]))) *
-                          inv_norm
-                    : 0.f;
+// One CTA (1024 threads) per (b, h); each thread owns a contiguous run of positions: local sums, a block-wide
+// exclusive scan of the run totals (warp shuffles + one shared-memory level), then the run is rewritten.
+constexpr int kScanThreads = 1024;
+
+__device__ __forceinline__ float block_exclusive_scan(float v, float* sh) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float u = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += u;
+  }
+  if (lane == 31) sh[w] = inc;
+  __syncthreads();
+  if (w == 0) {
+    float t = lane < (kScanThreads >> 5) ? sh[lane] : 0.f;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const float u = __shfl_up_sync(0xffffffffu, v, o);
-      if (lane >= o) v += u;
+      const float u = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += u;
     }
-    v += carry;
-    if (t < L) out[t] = v;
-    carry = __shfl_sync(0xffffffffu, v, 31);
+    sh[lane] = t;   // inclusive prefix of warp totals
+  }
+  __syncthreads();
+  const float before_warp = w > 0 ? sh[w - 1] : 0.f;
+  __syncthreads();
+  return before_warp + inc - v;
+}
+
+__global__ void __launch_bounds__(kScanThreads) gate_cumsum_fwd_kernel(const __nv_bfloat16* __restrict__ y,
+                                                                      int64_t ldy, float* __restrict__ gcum, int B,
+                                                                      int L, int H, float inv_norm) {
+  __shared__ float sh[32];
+  const int bh = blockIdx.x;
+  const int b = bh / H, h = bh % H;
+  const int per = (L + kScanThreads - 1) / kScanThreads;
+  const int t0 = threadIdx.x * per, t1 = min(L, t0 + per);
+  float local = 0.f;
+  for (int t = t0; t < t1; ++t)
+    // F.logsigmoid on bf16 rounds its output to bf16; the division by the normaliser (a power of two) is exact
+    local += bf16_round(logsigmoidf_(__bfloat162float(y[(static_cast<int64_t>(b) * L + t) * ldy + h]))) * inv_norm;
+  float run = block_exclusive_scan(local, sh);
+  float* out = gcum + static_cast<int64_t>(bh) * L;
+  for (int t = t0; t < t1; ++t) {
+    run += bf16_round(logsigmoidf_(__bfloat162float(y[(static_cast<int64_t>(b) * L + t) * ldy + h]))) * inv_norm;
+    out[t] = run;
   }
 }
 
-__global__ void gate_cumsum_bwd_kernel(const float* __restrict__ dg, const __nv_bfloat16* __restrict__ y, int64_t ldy,
-                                       __nv_bfloat16* __restrict__ dy, int64_t lddy, int B, int L, int H,
-                                       float inv_norm) {
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (w >= B * H) return;
-  const int b = w / H, h = w % H;
-  const float* src = dg + static_cast<int64_t>(w) * L;
-  float carry = 0.f;
-  for (int t1 = L; t1 > 0; t1 -= 32) {
-    const int t = t1 - 1 - lane;                 // lane 0 takes the latest position of the chunk
-    float v = t >= 0 ? src[t] : 0.f;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float u = __shfl_up_sync(0xffffffffu, v, o);
-      if (lane >= o) v += u;
-    }
-    v += carry;
-    if (t >= 0) {
-      const int64_t row = static_cast<int64_t>(b) * L + t;
-      const float x = __bfloat162float(y[row * ldy + h]);
-      dy[row * lddy + h] = __float2bfloat16_rn(v * inv_norm / (1.0f + __expf(x)));
-    }
-    carry = __shfl_sync(0xffffffffu, v, 31);
+// dy[b*L+t, h] = sigmoid(-y) / normalizer * sum_{s>=t} dg[b, h, s]  (reverse scan: thread i owns run i from the end)
+__global__ void __launch_bounds__(kScanThreads) gate_cumsum_bwd_kernel(const float* __restrict__ dg,
+                                                                      const __nv_bfloat16* __restrict__ y,
+                                                                      int64_t ldy, __nv_bfloat16* __restrict__ dy,
+                                                                      int64_t lddy, int B, int L, int H,
+                                                                      float inv_norm) {
+  __shared__ float sh[32];
+  const int bh = blockIdx.x;
+  const int b = bh / H, h = bh % H;
+  const float* src = dg + static_cast<int64_t>(bh) * L;
+  const int per = (L + kScanThreads - 1) / kScanThreads;
+  // run i covers positions [L - (i+1)*per, L - i*per)
+  const int t1 = L - threadIdx.x * per, t0 = max(0, t1 - per);
+  float local = 0.f;
+  for (int t = t0; t < t1; ++t) local += src[t];
+  float run = block_exclusive_scan(local, sh);   // sum over positions after this run
+  for (int t = t1 - 1; t >= t0; --t) {
+    run += src[t];
+    const int64_t row = static_cast<int64_t>(b) * L + t;
+    const float x = __bfloat162float(y[row * ldy + h]);
+    dy[row * lddy + h] = __float2bfloat16_rn(run * inv_norm / (1.0f + __expf(x)));
   }
 }
 
@@ -416,9 +437,9 @@ at::Tensor gate_cumsum_fwd(const at::Tensor& y, int64_t B, int64_t L, double nor
   c10::cuda::CUDAGuard guard(y.device());
   const int H = static_cast<int>(y.size(1));
   auto g = at::empty({B, H, L}, y.options().dtype(at::kFloat));
-  const int warps = static_cast<int>(B) * H;
-  if (warps > 0)
-    gate_cumsum_fwd_kernel<<<(warps * 32 + 255) / 256, 256, 0, cur_stream()>>>(
+  const int blocks = static_cast<int>(B) * H;
+  if (blocks > 0)
+    gate_cumsum_fwd_kernel<<<blocks, kScanThreads, 0, cur_stream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0), g.data_ptr<float>(), (int)B, (int)L, H,
         static_cast<float>(1.0 / normalizer));
   check_launch("gate_cumsum_fwd");
@@ -430,9 +451,9 @@ void gate_cumsum_bwd(const at::Tensor& dg, const at::Tensor& y, at::Tensor& dy, 
   FYB_CHECK(dg.is_contiguous() && dg.scalar_type() == at::kFloat, "gate_cumsum_bwd: dg fp32 [B, H, L]");
   FYB_CHECK(dy.stride(1) == 1 && dy.size(0) == B * L && dy.size(1) == H, "gate_cumsum_bwd: dy view [B*L, H]");
   c10::cuda::CUDAGuard guard(y.device());
-  const int warps = static_cast<int>(B * H);
-  if (warps > 0)
-    gate_cumsum_bwd_kernel<<<(warps * 32 + 255) / 256, 256, 0, cur_stream()>>>(
+  const int blocks = static_cast<int>(B * H);
+  if (blocks > 0)
+    gate_cumsum_bwd_kernel<<<blocks, kScanThreads, 0, cur_stream()>>>(
         dg.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
         reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()), dy.stride(0), (int)B, (int)L, (int)H,
         static_cast<float>(1.0 / normalizer));

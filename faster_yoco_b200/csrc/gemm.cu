@@ -295,6 +295,31 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, v
   const int64_t i4 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
   const int64_t total = static_cast<int64_t>(M) * N;
   if (i4 >= total) return;
+  if ((N % 4) == 0 && (ldc % 4) == 0 && (R == nullptr || (ldr % 4) == 0)) {
+    // 4 consecutive columns of one row
+    float4 acc = *reinterpret_cast<const float4*>(ws + i4);
+    for (int sp = 1; sp < splits; ++sp) {
+      const float4 v = *reinterpret_cast<const float4*>(ws + sp * total + i4);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    const int64_t row = i4 / N, col = i4 % N;
+    if (EPI == kEpiF32) {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(Cv) + row * ldc + col) = acc;
+    } else {
+      if (EPI == kEpiBf16Res) {
+        const uint2 ru = *reinterpret_cast<const uint2*>(R + row * ldr + col);
+        const float2 r0 = unpack_bf16(ru.x), r1 = unpack_bf16(ru.y);
+        acc = make_float4(bf16_round(acc.x) + r0.x, bf16_round(acc.y) + r0.y, bf16_round(acc.z) + r1.x,
+                          bf16_round(acc.w) + r1.y);
+      }
+      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(Cv) + row * ldc + col) =
+          make_uint2(pack_bf16(acc.x, acc.y), pack_bf16(acc.z, acc.w));
+    }
+    return;
+  }
   for (int64_t i = i4; i < i4 + 4 && i < total; ++i) {
     float acc = 0.f;
     for (int sp = 0; sp < splits; ++sp) acc += ws[sp * total + i];

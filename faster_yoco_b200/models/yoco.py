@@ -114,7 +114,7 @@ class SelfDecoder(nn.Module):
         self.rope = _RopeCache(self.head_dim, args.rope_theta, max(args.max_seq_len, 1))
         self.checkpoint_activations = args.checkpoint_activations
 
-    def forward(self, x, incremental_state=None, is_prefilling=False, start_pos=0):
+    def forward(self, x, incremental_state=None, is_prefilling=False, start_pos=0, comm_hooks=None, bucket0=1):
         pad = 0
         if is_prefilling and x.size(1) % self.block_size != 0 and self.args.sliding_window is None:
             pad = self.block_size - x.size(1) % self.block_size
@@ -124,6 +124,11 @@ class SelfDecoder(nn.Module):
             index_mask = torch.arange(x.size(1), device=x.device) >= (x.size(1) - pad)
         rel_pos = self.rope.get(start_pos, x.size(1), x.dtype, x.device)
         for idx, layer in enumerate(self.layers):
+            if comm_hooks is not None:
+                comm_hooks.before(bucket0 + idx)
+                if x.requires_grad:
+                    # fires once this layer's backward (all of its weight gradients) is complete
+                    x.register_hook(lambda g, b=bucket0 + idx: comm_hooks.ready(b))
             st = None
             if incremental_state is not None:
                 st = incremental_state.setdefault(idx, {})
@@ -164,9 +169,14 @@ class CrossDecoder(nn.Module):
         value = y[..., kvd:].view(B, L, self.num_heads, self.head_dim)
         return key, value, rel_pos
 
-    def forward(self, x, incremental_state=None, start_pos=0, skip_cross_decoder=False):
+    def forward(self, x, incremental_state=None, start_pos=0, skip_cross_decoder=False, comm_hooks=None,
+                bucket0=None):
         bsz, seqlen, dim = x.shape
         from .fused import fused_path_ok
+        if comm_hooks is not None:
+            comm_hooks.before(bucket0)             # shared K/V projection
+            if x.requires_grad:
+                x.register_hook(lambda g: (comm_hooks.ready(bucket0 + 1), comm_hooks.ready(bucket0)) and None)
         fused = incremental_state is None and self.training and fused_path_ok(x, self.head_dim)
         key, value, rel_pos = self.shared_kv(x, start_pos, fused=fused)
         if incremental_state is not None:
@@ -181,7 +191,11 @@ class CrossDecoder(nn.Module):
             value = st["prev_value"][:, :start_pos + seqlen]
         if skip_cross_decoder:
             return torch.zeros(bsz, 1, dim, device=x.device, dtype=x.dtype)
-        for layer in self.layers:
+        for i, layer in enumerate(self.layers):
+            if comm_hooks is not None:
+                comm_hooks.before(bucket0 + 1 + i)
+                if i > 0 and x.requires_grad:
+                    x.register_hook(lambda g, b=bucket0 + 1 + i: comm_hooks.ready(b))
             if self.checkpoint_activations and self.training and incremental_state is None:
                 x = torch.utils.checkpoint.checkpoint(layer, x, 0, key, value, rel_pos, None, False,
                                                       use_reentrant=False)
@@ -228,14 +242,48 @@ class YOCO(nn.Module):
                 m.weight.fill_(1.0)
 
     # ------------------------------------------------------------------------------------------------------------
+    def param_buckets(self):
+        """Parameter groups in forward order (the units of the overlapped gather / reduce): embedding, each
+        self-decoder layer, the shared K/V projection, each cross-decoder layer, final norm + output projection."""
+        seen = set()
+
+        def grp(params):
+            out = []
+            for p in params:
+                if p.requires_grad and id(p) not in seen:
+                    seen.add(id(p))
+                    out.append(p)
+            return out
+        groups = [grp([self.embed_tokens.weight])]
+        groups += [grp(l.parameters()) for l in self.self_decoder.layers]
+        groups.append(grp(list(self.cross_decoder.kv_proj.parameters()) +
+                          list(self.cross_decoder.kv_layer_norm.parameters())))
+        groups += [grp(l.parameters()) for l in self.cross_decoder.layers]
+        groups.append(grp(list(self.layer_norm.parameters()) + list(self.output_projection.parameters())))
+        rest = grp(self.parameters())
+        if rest:
+            groups[-1] += rest
+        return groups
+
     def forward(self, x, start_pos=0, incremental_state=None, is_prefilling=True, skip_cross_decoder=False,
-                return_hidden: bool = False):
-        """x: [B, L] token ids -> (logits [B, L, V], None) (yoco/models/decoder/yoco.py:285-315)."""
+                return_hidden: bool = False, comm_hooks=None):
+        """x: [B, L] token ids -> (logits [B, L, V], None) (yoco/models/decoder/yoco.py:285-315).
+
+        comm_hooks (training with overlapped ZeRO communication): before(b) is called ahead of bucket b's first
+        use in forward, ready(b) once its gradients are complete (see param_buckets for the bucket order)."""
+        n_self = len(self.self_decoder.layers)
+        if comm_hooks is not None:
+            comm_hooks.before(0)
         h = ops.embedding(x, self.embed_tokens.weight, self.embed_scale)
         h = self.self_decoder(h, incremental_state=incremental_state, is_prefilling=is_prefilling,
-                              start_pos=start_pos)
+                              start_pos=start_pos, comm_hooks=comm_hooks, bucket0=1)
         h = self.cross_decoder(h, start_pos=start_pos, incremental_state=incremental_state,
-                               skip_cross_decoder=skip_cross_decoder)
+                               skip_cross_decoder=skip_cross_decoder, comm_hooks=comm_hooks, bucket0=1 + n_self)
+        if comm_hooks is not None:
+            head = 2 + n_self + len(self.cross_decoder.layers)
+            comm_hooks.before(head)
+            if h.requires_grad:
+                h.register_hook(lambda g: comm_hooks.ready(head))
         h = self.layer_norm(h)
         if return_hidden:
             return h, None

@@ -27,6 +27,9 @@ from .. import ops
 
 
 class PeerComm:
+    NSLOTS = 64          # flag slots: 0 = generic barrier, 1..61 = reduction buckets, 63 = gather barrier
+    GATHER_SLOT = 63
+
     def __init__(self, group=None):
         self.group = group
         self.rank = dist.get_rank(group)
@@ -37,11 +40,12 @@ class PeerComm:
         self.dev = torch.device("cuda", torch.cuda.current_device())
         self._keep: List[torch.Tensor] = []
         self._opened: List[int] = []
-        self.flags, self.peer_flags = self.share_bytes(16 * 8 * 4)
+        self.flags, self.peer_flags = self.share_bytes(self.NSLOTS * 8 * 4)
         self.box, self.peer_box = self.share_bytes(2 * 8 * 32 * 4)
         self.box_f = self.box.view(torch.float32)
-        self.epoch = 0
-        self.calls = 0
+        # device-resident barrier epochs (one per flag slot) and mailbox call counter: graph replays stay correct
+        self.counters = torch.zeros(self.NSLOTS + 1, dtype=torch.int32, device=self.dev)
+        self.buckets = None
         self.peers: Dict[str, List[int]] = {}
         P = min(2 * torch.cuda.get_device_properties(self.dev).multi_processor_count, 1024)
         self.part = torch.zeros(P, dtype=torch.float32, device=self.dev)
@@ -72,9 +76,8 @@ class PeerComm:
         return t.view(dtype)[:numel]
 
     # ------------------------------------------------------------------------------------------------- collectives
-    def barrier(self):
-        self.epoch += 1
-        self.C.flag_barrier(self.peer_flags, self.flags, self.rank, 0, self.epoch)
+    def barrier(self, slot: int = 0):
+        self.C.flag_barrier(self.peer_flags, self.flags, self.counters, self.rank, slot)
 
     def reduce_to_owner(self, grad_flat: torch.Tensor, seg: int, used: Optional[int] = None) -> torch.Tensor:
         """Average the gradient buffers of all ranks over this rank's segment, in place. Returns the segment's
@@ -104,13 +107,85 @@ class PeerComm:
         v = v.reshape(-1).float().contiguous()
         if v.numel() > 32:
             raise ValueError("all_reduce_vector: at most 32 values")
-        base = (self.calls % 2) * 8 * 32
-        self.calls += 1
-        self.C.mailbox_put(self.peer_box, v, self.rank, base)
+        box_counter = self.counters[self.NSLOTS:]
+        self.C.mailbox_put(self.peer_box, v, self.rank, box_counter)
         self.barrier()
         out = torch.empty_like(v)
-        self.C.mailbox_sum(self.box_f, out, self.world, base)
+        self.C.mailbox_sum(self.box_f, out, self.world, box_counter)
         return out
+
+    # ------------------------------------------------------------------------------------ overlapped (bucketed)
+    def setup_buckets(self, flat, groups, reduce_ctas: int = 128, gather_ctas: int = 128):
+        """groups: parameter lists in FORWARD order (bucket b = groups[b]). Precomputes, per bucket, the ranges this
+        rank owns (reduced during backward) and the ranges it must pull from other owners (before forward)."""
+        if len(groups) > self.NSLOTS - 3:
+            raise ValueError("too many buckets")
+        self.flat = flat
+        owned, other = [], []
+        for grp in groups:
+            ents = [flat.by_param[id(p)] for p in grp if id(p) in flat.by_param]
+            own = [[e.offset, e.numel] for e in ents if e.owner == self.rank]
+            oth = [[e.offset, e.numel, e.owner] for e in ents if e.owner != self.rank]
+            owned.append(torch.tensor(own, dtype=torch.int64, device=self.dev).view(-1, 2))
+            other.append(torch.tensor(oth, dtype=torch.int64, device=self.dev).view(-1, 3))
+        self.buckets = (owned, other)
+        self.nb = len(groups)
+        self.red_ctas, self.gather_ctas = reduce_ctas, gather_ctas
+        self.bucket_part = torch.zeros(self.nb, reduce_ctas, dtype=torch.float32, device=self.dev)
+        self.stream = torch.cuda.Stream(device=self.dev, priority=-1)
+        self.ready_ev = [torch.cuda.Event() for _ in range(self.nb)]
+        self.gather_ev = [torch.cuda.Event() for _ in range(self.nb)]
+        self.start_ev = torch.cuda.Event()
+        self._reduced = [False] * self.nb
+
+    def _slot_barrier(self, slot: int):
+        self.C.flag_barrier(self.peer_flags, self.flags, self.counters, self.rank, slot)
+
+    def start_gather(self):
+        """After every owner's Adam step (previous update): pull all other owners' parameters, bucket by bucket,
+        on the communication stream. Forward waits per bucket (wait_gather)."""
+        cur = torch.cuda.current_stream(self.dev)
+        self.start_ev.record(cur)
+        owned, other = self.buckets
+        with torch.cuda.stream(self.stream):
+            self.stream.wait_event(self.start_ev)
+            self._slot_barrier(self.GATHER_SLOT)
+            for b in range(self.nb):
+                if other[b].numel():
+                    self.C.gather_segments(self.peers["param"], self.flat.flat, other[b], self.rank,
+                                           self.gather_ctas)
+                self.gather_ev[b].record(self.stream)
+        self._reduced = [False] * self.nb
+
+    def wait_gather(self, b: int):
+        torch.cuda.current_stream(self.dev).wait_event(self.gather_ev[b])
+
+    def bucket_ready(self, b: int):
+        """Bucket b's gradients are final on this rank (called from a gradient hook on the compute stream)."""
+        if self._reduced[b]:
+            return
+        self._reduced[b] = True
+        owned, _ = self.buckets
+        self.ready_ev[b].record(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(self.stream):
+            self.stream.wait_event(self.ready_ev[b])
+            self._slot_barrier(1 + b)
+            self.C.reduce_ranges(self.peers["grad"], self.flat.grad_flat, owned[b], self.bucket_part[b],
+                                 self.red_ctas)
+
+    def finish_reduce(self) -> torch.Tensor:
+        """Reduce the buckets no hook reported (in bucket order), join the streams, and return this owner's sum of
+        squares of the reduced gradients (fixed summation order)."""
+        for b in range(self.nb):
+            if not self._reduced[b]:
+                self.bucket_ready(b)
+        torch.cuda.current_stream(self.dev).wait_stream(self.stream)
+        self.C.sum_partials(self.bucket_part.view(-1), self.sq)
+        return self.sq
+
+    def finish_reduce_reset(self):
+        torch.cuda.current_stream(self.dev).wait_stream(self.stream)
+        self._reduced = [True] * self.nb
 
     def close(self):
         torch.cuda.synchronize()

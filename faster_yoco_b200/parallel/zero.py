@@ -178,6 +178,8 @@ class ZeroOptimizer:
         if fp.world == 1:
             return None
         if self.comm == "fused" and self.p2p is not None:
+            if self.p2p.buckets is not None:
+                return self.p2p.finish_reduce()
             return self.p2p.reduce_to_owner(fp.grad_flat, fp.seg, fp.used[fp.rank])
         out = fp.grad_segment()
         if dist.get_backend(self.group) == "nccl":
@@ -193,6 +195,8 @@ class ZeroOptimizer:
         if fp.world == 1:
             return
         if self.comm == "fused" and self.p2p is not None:
+            if self.p2p.buckets is not None:
+                return          # pulled bucket by bucket at the start of the next update (overlapped)
             self.p2p.all_gather(fp.flat, fp.seg, fp.used)
             return
         dist.all_gather_into_tensor(fp.flat, fp.param_segment(), group=self.group)

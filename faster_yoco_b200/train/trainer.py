@@ -27,9 +27,24 @@ from .metrics import DeviceMeters
 from .schedule import PolynomialDecaySchedule
 
 
+class _CommHooks:
+    """Per-bucket callbacks the model calls: before(b) ahead of bucket b's first forward use, ready(b) from the
+    gradient hook that fires once bucket b's backward is complete."""
+
+    def __init__(self, p2p):
+        self.p2p = p2p
+
+    def before(self, b: int):
+        self.p2p.wait_gather(b)
+
+    def ready(self, b: int):
+        self.p2p.bucket_ready(b)
+
+
 class Trainer:
     def __init__(self, model: torch.nn.Module, optim_cfg, *, device, comm: str = "nccl", zero_stage: int = 1,
-                 pad_idx: int = 1, graph_step: bool = False, group=None, check_consistency: bool = True):
+                 pad_idx: int = 1, graph_step: bool = False, group=None, check_consistency: bool = True,
+                 overlap: bool = True):
         self.model = model
         self.device = torch.device(device)
         self.cfg = optim_cfg
@@ -45,6 +60,9 @@ class Trainer:
         self.flat.direct_grads = self.device.type == "cuda" and ops.get_backend() == "native"
         self.zero = ZeroOptimizer(self.flat, optim_cfg, comm=comm, group=group, stage=zero_stage)
         self.zero.p2p = p2p
+        self.overlap = p2p is not None and overlap and hasattr(model, "param_buckets")
+        if self.overlap:
+            p2p.setup_buckets(self.flat, model.param_buckets())
         self.sched = PolynomialDecaySchedule(optim_cfg.lr, optim_cfg.warmup_updates, optim_cfg.total_num_update,
                                              optim_cfg.end_learning_rate, optim_cfg.power)
         self.pending = PendingChecks(self.device.type == "cuda")
@@ -73,7 +91,11 @@ class Trainer:
         return out
 
     def _forward_backward(self, src, tgt, ntok: torch.Tensor):
-        logits, _ = self.model(src)
+        if self.overlap:
+            self.zero.p2p.start_gather()
+            logits, _ = self.model(src, comm_hooks=_CommHooks(self.zero.p2p))
+        else:
+            logits, _ = self.model(src)
         V = logits.shape[-1]
         loss = ops.cross_entropy(logits.view(-1, V), tgt.reshape(-1), self.pad_idx)
         loss.backward()
@@ -152,6 +174,15 @@ class Trainer:
             self._graph = g
         self._graph.replay()
         return tuple(t.clone() for t in self._graph_out)
+
+    def sync_params(self):
+        """Make every rank's full parameter copy current (the overlapped path gathers lazily at the next update)."""
+        if getattr(self, "overlap", False):
+            p2p = self.zero.p2p
+            p2p.start_gather()
+            for b in range(p2p.nb):
+                p2p.wait_gather(b)
+            p2p.finish_reduce_reset()
 
     def release_graph(self):
         """Drop the captured update (must happen before the process group is destroyed)."""

@@ -7,7 +7,7 @@ import torch
 import torch.distributed as dist
 
 
-def _tiny_trainer(device, comm="nccl", seed=0, graph=False, arch="yoco_tiny", dtype=torch.float32):
+def _tiny_trainer(device, comm="nccl", seed=0, graph=False, arch="yoco_tiny", dtype=torch.float32, overlap=True):
     from ..config import OptimConfig, build_args
     from ..models.yoco import YOCO
     from ..train.trainer import Trainer
@@ -15,7 +15,7 @@ def _tiny_trainer(device, comm="nccl", seed=0, graph=False, arch="yoco_tiny", dt
     args = build_args(arch, max_seq_len=256, init_std=0.02)
     model = YOCO(args).to(device=device, dtype=dtype)
     cfg = OptimConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, warmup_updates=0, total_num_update=20)
-    return model, Trainer(model, cfg, device=device, comm=comm, graph_step=graph)
+    return model, Trainer(model, cfg, device=device, comm=comm, graph_step=graph, overlap=overlap)
 
 
 def _batches(rank, world, n, seed=1, batch=2, seq=256, vocab=1024):
@@ -91,17 +91,18 @@ def fused_vs_nccl_gpu(rank, world, outdir, steps):
     ops.set_backend("native")
     dev = torch.device("cuda", rank)
     res = {}
-    for comm in ("nccl", "fused"):
-        model, tr = _tiny_trainer(dev, comm=comm, arch="yoco_small", dtype=torch.bfloat16)
+    for name, comm, overlap in (("nccl", "nccl", False), ("fused", "fused", True), ("fused_serial", "fused", False)):
+        model, tr = _tiny_trainer(dev, comm=comm, arch="yoco_small", dtype=torch.bfloat16, overlap=overlap)
         losses = []
         for ids in _batches(rank, world, steps, seq=256, vocab=8192):
             mine = ids[rank]
             b = {"src_tokens": mine[:, :-1].contiguous(), "target": mine[:, 1:].contiguous(),
                  "ntokens": mine.shape[0] * mine.shape[1], "nsentences": mine.shape[0]}
             losses.append(float(tr.train_step(b).item()))
+        tr.sync_params()
         torch.cuda.synchronize()
         status = int(ops._C().status()[0].item())
-        res[comm] = {"losses": losses, "params": tr.flat.flat.float().cpu(), "status": status}
+        res[name] = {"losses": losses, "params": tr.flat.flat.float().cpu(), "status": status}
         if tr.zero.p2p is not None:
             tr.zero.p2p.close()
     if rank == 0:
