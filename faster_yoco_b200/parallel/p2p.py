@@ -124,8 +124,9 @@ class PeerComm:
         owned, other = [], []
         for grp in groups:
             ents = [flat.by_param[id(p)] for p in grp if id(p) in flat.by_param]
-            own = [[e.offset, e.numel] for e in ents if e.owner == self.rank]
-            oth = [[e.offset, e.numel, e.owner] for e in ents if e.owner != self.rank]
+            pieces = [pc for e in ents for pc in flat.owner_ranges(e)]
+            own = [[o, c] for o, c, r in pieces if r == self.rank]
+            oth = [[o, c, r] for o, c, r in pieces if r != self.rank]
             owned.append(torch.tensor(own, dtype=torch.int64, device=self.dev).view(-1, 2))
             other.append(torch.tensor(oth, dtype=torch.int64, device=self.dev).view(-1, 3))
         self.buckets = (owned, other)

@@ -58,19 +58,41 @@ class Entry:
 class FlatParams:
     """The flat BF16 parameter buffer + flat gradient buffer; model parameters become views of it."""
 
-    def __init__(self, named_params, world: int, rank: int, device, dtype=torch.bfloat16, allocator=None):
+    def __init__(self, named_params, world: int, rank: int, device, dtype=torch.bfloat16, allocator=None,
+                 partition: str = "even"):
         """allocator(name, numel, dtype) -> tensor: where the flat buffers live (peer-shared memory for the fused
-        NVLink collectives); default torch.zeros on `device`."""
+        NVLink collectives); default torch.zeros on `device`.
+
+        partition:
+          "greedy" -- fairscale OSS: whole parameters, each to the rank with the smallest running total; a rank's
+                      parameters sit in its own segment (the reference's layout, zero1_fast.py:52-75).
+          "even"   -- parameters laid out in model order and the flat buffer cut into `world` equal contiguous
+                      segments, so one large parameter (the 308M-element embedding) spreads over all owners and
+                      every rank sends and receives the same bytes. The optimizer math is elementwise, so the
+                      partition changes no result; checkpoints store per-parameter state either way."""
         named = [(n, p) for n, p in named_params if p.requires_grad]
         self.world, self.rank, self.device, self.dtype = world, rank, torch.device(device), dtype
-        owners = greedy_partition([p.numel() for _, p in named], world)
-        fill = [0] * world
+        self.partition = partition
         placed = []
-        for (name, p), r in zip(named, owners):
-            placed.append((name, p, r, fill[r]))
-            fill[r] = _round_up(fill[r] + p.numel(), ALIGN)
-        self.seg = max(_round_up(max(fill), 1024), 1024)
-        self.used = fill                                     # used (aligned) length of each owner's segment
+        if partition == "greedy":
+            owners = greedy_partition([p.numel() for _, p in named], world)
+            fill = [0] * world
+            for (name, p), r in zip(named, owners):
+                placed.append((name, p, r, fill[r]))
+                fill[r] = _round_up(fill[r] + p.numel(), ALIGN)
+            self.seg = max(_round_up(max(fill), 1024), 1024)
+            self.used = fill                                 # used (aligned) length of each owner's segment
+        elif partition == "even":
+            off = 0
+            for name, p in named:
+                placed.append((name, p, None, off))
+                off = _round_up(off + p.numel(), ALIGN)
+            self.seg = max(_round_up((off + world - 1) // world, 1024), 1024)
+            placed = [(n, p, min(o // self.seg, world - 1), o - min(o // self.seg, world - 1) * self.seg)
+                      for n, p, _, o in placed]
+            self.used = [max(0, min(self.seg, off - r * self.seg)) for r in range(world)]
+        else:
+            raise ValueError(f"unknown partition {partition!r}")
         if allocator is None:
             self.flat = torch.zeros(world * self.seg, dtype=dtype, device=self.device)
             self.grad_flat = torch.zeros(world * self.seg, dtype=dtype, device=self.device)
@@ -105,6 +127,16 @@ class FlatParams:
 
     def grad_segment(self, rank: Optional[int] = None) -> torch.Tensor:
         return self.grad_flat[self.owned(rank)]
+
+    def owner_ranges(self, e: "Entry"):
+        """[(global offset, count, owner)] pieces of one parameter, cut at segment boundaries."""
+        out, lo, hi = [], e.offset, e.offset + e.numel
+        while lo < hi:
+            r = lo // self.seg
+            cut = min(hi, (r + 1) * self.seg)
+            out.append((lo, cut - lo, r))
+            lo = cut
+        return out
 
     def grad_view(self, p) -> torch.Tensor:
         """A fresh view of p's gradient slot (fresh so autograd's AccumulateGrad adopts it without a copy)."""

@@ -111,16 +111,19 @@ def load_checkpoint(path: str, model, trainer) -> dict:
     own = fp.owned()
     with torch.no_grad():
         for e in fp.entries:
-            if e.owner != fp.rank:
-                continue
-            lo = e.offset - own.start
-            for key, dst in (("master", zero.master), ("exp_avg", zero.exp_avg), ("exp_avg_sq", zero.exp_avg_sq)):
-                t = _join_for_import(model, e.name, st.get(key, {}))
-                if t is None:
-                    if key == "master":
-                        dst[lo:lo + e.numel].copy_(e.param.detach().reshape(-1).float())
+            for off, cnt, owner in fp.owner_ranges(e):
+                if owner != fp.rank:
                     continue
-                dst[lo:lo + e.numel].copy_(t.reshape(-1).to(dst.device, torch.float32))
+                lo = off - own.start            # position in this rank's shard
+                pe = off - e.offset             # position inside the parameter
+                for key, dst in (("master", zero.master), ("exp_avg", zero.exp_avg),
+                                 ("exp_avg_sq", zero.exp_avg_sq)):
+                    t = _join_for_import(model, e.name, st.get(key, {}))
+                    if t is None:
+                        if key == "master":
+                            dst[lo:lo + cnt].copy_(e.param.detach().reshape(-1)[pe:pe + cnt].float())
+                        continue
+                    dst[lo:lo + cnt].copy_(t.reshape(-1)[pe:pe + cnt].to(dst.device, torch.float32))
     zero.num_updates = int(st.get("step", ck["optimizer_history"][-1]["num_updates"] if ck.get("optimizer_history")
                                       else 0))
     hist = ck.get("optimizer_history") or []

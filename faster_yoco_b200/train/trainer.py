@@ -44,7 +44,7 @@ class _CommHooks:
 class Trainer:
     def __init__(self, model: torch.nn.Module, optim_cfg, *, device, comm: str = "nccl", zero_stage: int = 1,
                  pad_idx: int = 1, graph_step: bool = False, group=None, check_consistency: bool = True,
-                 overlap: bool = True):
+                 overlap: bool = True, partition: str = "even"):
         self.model = model
         self.device = torch.device(device)
         self.cfg = optim_cfg
@@ -56,7 +56,8 @@ class Trainer:
             from ..parallel.p2p import PeerComm
             p2p = PeerComm(group)
         self.flat = FlatParams(model.named_parameters(), self.world, self.rank, self.device,
-                               dtype=next(model.parameters()).dtype, allocator=p2p.alloc if p2p else None)
+                               dtype=next(model.parameters()).dtype, allocator=p2p.alloc if p2p else None,
+                               partition=partition)
         self.flat.direct_grads = self.device.type == "cuda" and ops.get_backend() == "native"
         self.zero = ZeroOptimizer(self.flat, optim_cfg, comm=comm, group=group, stage=zero_stage)
         self.zero.p2p = p2p
