@@ -40,6 +40,9 @@ def parse():
     p.add_argument("--comm", default="fused", choices=["nccl", "fused"],
                    help="fused: NVLink peer-memory collectives overlapped with compute; nccl: the baseline path")
     p.add_argument("--graph", type=int, default=1, help="capture the whole update as one CUDA graph")
+    p.add_argument("--overlap", type=int, default=0,
+                   help="fused comm: bucketed push/reduce overlapped with forward/backward (SM-driven; co-running "
+                        "transfers slow the GEMMs on this hardware, so off by default)")
     p.add_argument("--sliding-window", type=int, default=None)
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-e2e", action="store_true")
@@ -148,7 +151,8 @@ def main():
         model = YOCO(margs)
     model = model.to(torch.bfloat16)
     optim = OptimConfig()
-    trainer = Trainer(model, optim, device=dev, comm=args.comm, graph_step=bool(args.graph))
+    trainer = Trainer(model, optim, device=dev, comm=args.comm, graph_step=bool(args.graph),
+                      overlap=bool(args.overlap))
     data = SyntheticLM(margs.vocab_size, args.seq_len, args.batch, seed=1, rank=rank, pin=True)
     batches = [next(data) for _ in range(4)]
 
@@ -195,6 +199,12 @@ def main():
                "h2d_bytes_per_step": int(b["src_tokens"].numel() * 8 + b["target"].numel() * 8),
                "d2h_bytes_per_step": 4}
 
+    if os.environ.get("FYB_TIMELINE") == "1" and not args.graph:
+        step(0)
+        tl = trainer.timeline()
+        if rank == 0:
+            print(json.dumps({"timeline_ms": [(n, round(t, 3)) for n, t in tl]}), flush=True)
+
     launches = None
     if args.count_launches:
         try:
@@ -212,6 +222,7 @@ def main():
                        "global_batch": args.batch * world, "seq_len": args.seq_len,
                        "tokens_per_update": tokens_per_update, "parallelism": f"dp{world}-zero1",
                        "kernels": args.kernels, "comm": args.comm, "cuda_graph": bool(args.graph),
+                       "comm_overlap": bool(args.overlap),
                        "l2": "working set (>=55 GB of params/grads/Adam state per update) >> 126 MB L2"},
             "clocks": clocks, "e2e": e2e, "gpu_launches": launches,
         }

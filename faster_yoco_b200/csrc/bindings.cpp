@@ -59,6 +59,16 @@ void gather_segments(const std::vector<int64_t>& peer_params, at::Tensor& dst, c
 void reduce_ranges(const std::vector<int64_t>& peer_grads, at::Tensor& out, const at::Tensor& ranges, at::Tensor& part,
                    int64_t ctas);
 void sum_partials(const at::Tensor& part, at::Tensor& out);
+void push_bucket(const at::Tensor& src, const std::vector<int64_t>& peer_dst, const std::vector<int64_t>& peer_arrive,
+                 const at::Tensor& ranges, int64_t bucket, int64_t rank, int64_t ctas);
+void wait_arrivals(const at::Tensor& arrive, at::Tensor& expected, int64_t bucket, int64_t increment);
+void push_grads(const at::Tensor& grad, const std::vector<int64_t>& peer_staging,
+                const std::vector<int64_t>& peer_arrive, const at::Tensor& pieces, int64_t bucket, int64_t rank,
+                int64_t seg, int64_t ctas);
+void reduce_staged(at::Tensor& grad, const at::Tensor& staging, const at::Tensor& ranges, int64_t world, int64_t rank,
+                   int64_t seg, at::Tensor& part, int64_t ctas);
+void push_range(const at::Tensor& src, const std::vector<int64_t>& peer_dst, int64_t off, int64_t n, int64_t rank,
+                int64_t ctas);
 void mailbox_put(const std::vector<int64_t>& peer_boxes, const at::Tensor& vals, int64_t rank,
                  const at::Tensor& counter);
 void mailbox_sum(const at::Tensor& box, at::Tensor& out, int64_t world, at::Tensor& counter);
@@ -130,6 +140,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gather_segments", &fyb::gather_segments);
   m.def("reduce_ranges", &fyb::reduce_ranges);
   m.def("sum_partials", &fyb::sum_partials);
+  m.def("push_range", &fyb::push_range);
+  m.def("push_bucket", &fyb::push_bucket);
+  m.def("wait_arrivals", &fyb::wait_arrivals);
+  m.def("push_grads", &fyb::push_grads);
+  m.def("reduce_staged", &fyb::reduce_staged);
   m.def("mailbox_put", &fyb::mailbox_put);
   m.def("mailbox_sum", &fyb::mailbox_sum);
   m.def("status", &fyb::status_tensor, "device status word of the kernels with bounded waits");

@@ -234,6 +234,161 @@ __global__ void gather_segments_kernel(PeerPtrs src, __nv_bfloat16* dst, const i
   }
 }
 
+// push form of the all-gather: this rank's range [off, off+n) of its flat buffer is stored into the same range of
+// every peer's buffer (remote stores are posted writes: no round trip per access, unlike remote loads)
+__global__ void push_range_kernel(const __nv_bfloat16* __restrict__ src, PeerPtrs dst, int64_t off, int64_t n,
+                                  int world, int rank) {
+  const uint4* sp = reinterpret_cast<const uint4*>(src + off);
+  const int64_t nv = n / 8;
+  const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nv; i += nthr) {
+    const uint4 v = sp[i];
+#pragma unroll
+    for (int q = 0; q < kMaxWorld; ++q)
+      if (q < world && q != rank)
+        reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(dst.p[q])) + off)[i] = v;
+  }
+  if (blockIdx.x == 0)
+    for (int64_t j = nv * 8 + threadIdx.x; j < n; j += blockDim.x)
+      for (int q = 0; q < world; ++q)
+        if (q != rank) reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(dst.p[q]))[off + j] = src[off + j];
+  __threadfence_system();   // the barrier that follows publishes these remote stores
+}
+
+// Push this rank's pieces of one bucket (ranges [n][2] = (offset, count)) into every peer's flat buffer, then each CTA
+// makes its stores visible system-wide and adds 1 to the bucket's arrival counter on every peer.
+__global__ void push_bucket_kernel(const __nv_bfloat16* __restrict__ src, PeerPtrs dst, PeerPtrs arrive,
+                                   const int64_t* __restrict__ ranges, int nranges, int bucket, int world, int rank) {
+  const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (int rg = 0; rg < nranges; ++rg) {
+    const int64_t off = ranges[2 * rg], n = ranges[2 * rg + 1];
+    const uint4* sp = reinterpret_cast<const uint4*>(src + off);
+    const int64_t nv = n / 8;
+    for (int64_t i = tid; i < nv; i += nthr) {
+      const uint4 v = sp[i];
+#pragma unroll
+      for (int q = 0; q < kMaxWorld; ++q)
+        if (q < world && q != rank)
+          reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(dst.p[q])) + off)[i] = v;
+    }
+    for (int64_t j = nv * 8 + tid; j < n; j += nthr)
+      for (int q = 0; q < world; ++q)
+        if (q != rank) reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(dst.p[q]))[off + j] = src[off + j];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < world && threadIdx.x != rank) {
+    uint32_t* c = reinterpret_cast<uint32_t*>(const_cast<void*>(arrive.p[threadIdx.x])) + bucket;
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(c), "r"(1u) : "memory");
+  }
+}
+
+// Gradient push for the owner-side reduction: for every piece (offset, count, owner q != rank) of this bucket, this
+// rank's gradient values are stored into owner q's staging buffer, slot `rank` (staging_q[rank * seg + offset -
+// q * seg]); then each CTA fences and adds 1 to the bucket's arrival counter on every peer.
+__global__ void push_grads_kernel(const __nv_bfloat16* __restrict__ grad, PeerPtrs staging, PeerPtrs arrive,
+                                  const int64_t* __restrict__ pieces, int npieces, int bucket, int world, int rank,
+                                  int64_t seg) {
+  const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (int pc = 0; pc < npieces; ++pc) {
+    const int64_t off = pieces[3 * pc], n = pieces[3 * pc + 1];
+    const int q = static_cast<int>(pieces[3 * pc + 2]);
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(staging.p[q])) +
+                         static_cast<int64_t>(rank) * seg + (off - static_cast<int64_t>(q) * seg);
+    const uint4* sp = reinterpret_cast<const uint4*>(grad + off);
+    const int64_t nv = n / 8;
+    for (int64_t i = tid; i < nv; i += nthr) reinterpret_cast<uint4*>(dst)[i] = sp[i];
+    for (int64_t j = nv * 8 + tid; j < n; j += nthr) dst[j] = grad[off + j];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < world && threadIdx.x != rank) {
+    uint32_t* c = reinterpret_cast<uint32_t*>(const_cast<void*>(arrive.p[threadIdx.x])) + bucket;
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(c), "r"(1u) : "memory");
+  }
+}
+
+// Owner-side sum from local memory: for each owned range, out = bf16(sum over ranks in rank order / world), where
+// rank `rank`'s own values come from its gradient buffer and the others' from the staging slots. Per-CTA partial
+// sums of squares of the result in part[blockIdx.x].
+__global__ void reduce_staged_kernel(__nv_bfloat16* __restrict__ grad, const __nv_bfloat16* __restrict__ staging,
+                                     const int64_t* __restrict__ ranges, int nranges, int world, int rank,
+                                     int64_t seg, float inv_world, float* __restrict__ part) {
+  float ss = 0.f;
+  const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (int rg = 0; rg < nranges; ++rg) {
+    const int64_t off = ranges[2 * rg], n = ranges[2 * rg + 1];
+    const int64_t loc = off - static_cast<int64_t>(rank) * seg;   // position inside the owner's segment
+    for (int64_t i = tid * 8; i < n; i += nthr * 8) {
+      if (i + 8 <= n) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+        for (int r = 0; r < kMaxWorld; ++r) {
+          if (r < world) {
+            const __nv_bfloat16* src = r == rank ? grad + off : staging + static_cast<int64_t>(r) * seg + loc;
+            const uint4 u = *reinterpret_cast<const uint4*>(src + i);
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = unpack_bf16(w[k]);
+              acc[2 * k] += f.x;
+              acc[2 * k + 1] += f.y;
+            }
+          }
+        }
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float a = bf16_round(acc[2 * k] * inv_world), b = bf16_round(acc[2 * k + 1] * inv_world);
+          ss += a * a + b * b;
+          o[k] = pack_bf16(a, b);
+        }
+        *reinterpret_cast<uint4*>(grad + off + i) = make_uint4(o[0], o[1], o[2], o[3]);
+      } else {
+        for (int64_t j = i; j < n; ++j) {
+          float acc = 0.f;
+          for (int r = 0; r < world; ++r)
+            acc += __bfloat162float(r == rank ? grad[off + j] : staging[static_cast<int64_t>(r) * seg + loc + j]);
+          const float a = bf16_round(acc * inv_world);
+          ss += a * a;
+          grad[off + j] = __float2bfloat16_rn(a);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+    part[blockIdx.x] = t;
+  }
+}
+
+// Compute-stream wait until bucket b's pushes of the current round have all arrived: expected[b] += increment, then
+// spin (bounded) until arrive[b] >= expected[b]. The expectation is device-resident, so graph replays stay correct.
+__global__ void wait_arrivals_kernel(const uint32_t* __restrict__ arrive, uint32_t* __restrict__ expected, int bucket,
+                                     uint32_t increment, int* status) {
+  if (threadIdx.x != 0) return;
+  const uint32_t want = expected[bucket] + increment;
+  expected[bucket] = want;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t it = 0;
+  while (static_cast<int32_t>(ld_acquire_sys(arrive + bucket) - want) < 0) {
+    if ((++it & 255u) == 0u && globaltimer_ns() - t0 > FYB_WAIT_NS) {
+      record_status(status, kPeerTimeout, 300 + bucket);
+      break;
+    }
+  }
+  __threadfence_system();
+}
+
 // each rank writes its k values into slot [rank] of every peer's mailbox, then (after a flag barrier) sums the
 // world slots of its own mailbox in rank order
 __global__ void mailbox_put_kernel(PeerPtrs boxes, const float* __restrict__ vals, int k, int rank, int world,
@@ -358,6 +513,64 @@ void gather_segments(const std::vector<int64_t>& peer_params, at::Tensor& dst, c
       to_ptrs(peer_params), reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()), segs.data_ptr<int64_t>(),
       static_cast<int>(segs.size(0)), static_cast<int>(rank));
   check_launch("gather_segments");
+}
+
+void push_range(const at::Tensor& src, const std::vector<int64_t>& peer_dst, int64_t off, int64_t n, int64_t rank,
+                int64_t ctas) {
+  const int world = static_cast<int>(peer_dst.size());
+  FYB_CHECK(off % 8 == 0, "push_range: offset must be a multiple of 8 elements");
+  if (n <= 0) return;
+  push_range_kernel<<<static_cast<int>(ctas), 512, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), to_ptrs(peer_dst), off, n, world,
+      static_cast<int>(rank));
+  check_launch("push_range");
+}
+
+void push_bucket(const at::Tensor& src, const std::vector<int64_t>& peer_dst, const std::vector<int64_t>& peer_arrive,
+                 const at::Tensor& ranges, int64_t bucket, int64_t rank, int64_t ctas) {
+  const int world = static_cast<int>(peer_dst.size());
+  FYB_CHECK(ranges.is_cuda() && ranges.scalar_type() == at::kLong && ranges.dim() == 2 && ranges.size(1) == 2,
+            "push_bucket: ranges must be a device int64 [n, 2]");
+  push_bucket_kernel<<<static_cast<int>(ctas), 512, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), to_ptrs(peer_dst), to_ptrs(peer_arrive),
+      ranges.data_ptr<int64_t>(), static_cast<int>(ranges.size(0)), static_cast<int>(bucket), world,
+      static_cast<int>(rank));
+  check_launch("push_bucket");
+}
+
+void push_grads(const at::Tensor& grad, const std::vector<int64_t>& peer_staging,
+                const std::vector<int64_t>& peer_arrive, const at::Tensor& pieces, int64_t bucket, int64_t rank,
+                int64_t seg, int64_t ctas) {
+  const int world = static_cast<int>(peer_staging.size());
+  FYB_CHECK(pieces.is_cuda() && pieces.scalar_type() == at::kLong && pieces.dim() == 2 && pieces.size(1) == 3,
+            "push_grads: pieces must be a device int64 [n, 3]");
+  push_grads_kernel<<<static_cast<int>(ctas), 512, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(grad.data_ptr()), to_ptrs(peer_staging), to_ptrs(peer_arrive),
+      pieces.data_ptr<int64_t>(), static_cast<int>(pieces.size(0)), static_cast<int>(bucket), world,
+      static_cast<int>(rank), seg);
+  check_launch("push_grads");
+}
+
+void reduce_staged(at::Tensor& grad, const at::Tensor& staging, const at::Tensor& ranges, int64_t world, int64_t rank,
+                   int64_t seg, at::Tensor& part, int64_t ctas) {
+  FYB_CHECK(part.numel() >= ctas, "reduce_staged: partials buffer too small");
+  if (ranges.size(0) == 0) {
+    part.zero_();
+    return;
+  }
+  reduce_staged_kernel<<<static_cast<int>(ctas), 256, 0, cur_stream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(grad.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(staging.data_ptr()),
+      ranges.data_ptr<int64_t>(), static_cast<int>(ranges.size(0)), static_cast<int>(world), static_cast<int>(rank),
+      seg, 1.0f / static_cast<float>(world), part.data_ptr<float>());
+  check_launch("reduce_staged");
+}
+
+void wait_arrivals(const at::Tensor& arrive, at::Tensor& expected, int64_t bucket, int64_t increment) {
+  wait_arrivals_kernel<<<1, 32, 0, cur_stream()>>>(reinterpret_cast<const uint32_t*>(arrive.data_ptr()),
+                                                   reinterpret_cast<uint32_t*>(expected.data_ptr()),
+                                                   static_cast<int>(bucket), static_cast<uint32_t>(increment),
+                                                   status_ptr());
+  check_launch("wait_arrivals");
 }
 
 void mailbox_put(const std::vector<int64_t>& peer_boxes, const at::Tensor& vals, int64_t rank,

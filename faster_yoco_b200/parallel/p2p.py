@@ -88,6 +88,15 @@ class PeerComm:
         return self.sq
 
     def all_gather(self, flat: torch.Tensor, seg: int, used: Optional[List[int]] = None):
+        """Push form (remote stores run at NVLink speed where remote loads do not): this rank stores its updated
+        segment into every peer's buffer, then one barrier publishes all pushes."""
+        n = used[self.rank] if used else seg
+        sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
+        self.C.push_range(flat, self.peers["param"], self.rank * seg, n, self.rank, sms)
+        self.barrier()
+
+    def all_gather_pull(self, flat: torch.Tensor, seg: int, used: Optional[List[int]] = None):
+        """Pull form of the all-gather (kept for measurement: remote loads are latency-bound, ~200 GB/s here)."""
         self.barrier()
         key = (seg, tuple(used) if used else None)
         segs = self._gather_segs.get(key)
@@ -115,11 +124,14 @@ class PeerComm:
         return out
 
     # ------------------------------------------------------------------------------------ overlapped (bucketed)
-    def setup_buckets(self, flat, groups, reduce_ctas: int = 128, gather_ctas: int = 128):
+    def setup_buckets(self, flat, groups, reduce_ctas: Optional[int] = None, gather_ctas: Optional[int] = None):
         """groups: parameter lists in FORWARD order (bucket b = groups[b]). Precomputes, per bucket, the ranges this
         rank owns (reduced during backward) and the ranges it must pull from other owners (before forward)."""
         if len(groups) > self.NSLOTS - 3:
             raise ValueError("too many buckets")
+        import os
+        reduce_ctas = int(os.environ.get("FYB_REDUCE_CTAS", reduce_ctas or 128))
+        gather_ctas = int(os.environ.get("FYB_PUSH_CTAS", gather_ctas or 128))
         self.flat = flat
         owned, other = [], []
         for grp in groups:
@@ -131,6 +143,15 @@ class PeerComm:
             other.append(torch.tensor(oth, dtype=torch.int64, device=self.dev).view(-1, 3))
         self.buckets = (owned, other)
         self.nb = len(groups)
+        # push-based parameter exchange: per-bucket arrival counters (peers add into ours) + local expectations
+        self.arrive, self.peer_arrive = self.share_bytes(self.NSLOTS * 4)
+        self.expected = torch.zeros(self.NSLOTS, dtype=torch.int32, device=self.dev)
+        self.push_ctas = gather_ctas
+        # push-based gradient reduction: peers store their pieces of this rank's segment into staging slot [peer]
+        self.staging = self.alloc("staging", self.world * flat.seg, flat.dtype)
+        self.garrive, self.peer_garrive = self.share_bytes(self.NSLOTS * 4)
+        self.gexpected = torch.zeros(self.NSLOTS, dtype=torch.int32, device=self.dev)
+        self.grad_push_ctas = reduce_ctas
         self.red_ctas, self.gather_ctas = reduce_ctas, gather_ctas
         self.bucket_part = torch.zeros(self.nb, reduce_ctas, dtype=torch.float32, device=self.dev)
         self.stream = torch.cuda.Stream(device=self.dev, priority=-1)
@@ -143,36 +164,38 @@ class PeerComm:
         self.C.flag_barrier(self.peer_flags, self.flags, self.counters, self.rank, slot)
 
     def start_gather(self):
-        """After every owner's Adam step (previous update): pull all other owners' parameters, bucket by bucket,
-        on the communication stream. Forward waits per bucket (wait_gather)."""
+        """Start of an update: this rank pushes the parameters it owns (updated by its previous Adam step), bucket
+        by bucket in forward order, into every peer's flat buffer on the communication stream; forward waits per
+        bucket for the peers' pushes (wait_gather). Safe: a peer's previous reads of bucket b ended with its
+        backward of b, which every owner's reduction of b (hence Adam) waited for."""
         cur = torch.cuda.current_stream(self.dev)
         self.start_ev.record(cur)
-        owned, other = self.buckets
+        owned, _ = self.buckets
         with torch.cuda.stream(self.stream):
             self.stream.wait_event(self.start_ev)
-            self._slot_barrier(self.GATHER_SLOT)
             for b in range(self.nb):
-                if other[b].numel():
-                    self.C.gather_segments(self.peers["param"], self.flat.flat, other[b], self.rank,
-                                           self.gather_ctas)
-                self.gather_ev[b].record(self.stream)
+                self.C.push_bucket(self.flat.flat, self.peers["param"], self.peer_arrive, owned[b], b, self.rank,
+                                   self.push_ctas)
         self._reduced = [False] * self.nb
 
     def wait_gather(self, b: int):
-        torch.cuda.current_stream(self.dev).wait_event(self.gather_ev[b])
+        self.C.wait_arrivals(self.arrive, self.expected, b, (self.world - 1) * self.push_ctas)
 
     def bucket_ready(self, b: int):
         """Bucket b's gradients are final on this rank (called from a gradient hook on the compute stream)."""
         if self._reduced[b]:
             return
         self._reduced[b] = True
-        owned, _ = self.buckets
+        owned, other = self.buckets
         self.ready_ev[b].record(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(self.stream):
             self.stream.wait_event(self.ready_ev[b])
-            self._slot_barrier(1 + b)
-            self.C.reduce_ranges(self.peers["grad"], self.flat.grad_flat, owned[b], self.bucket_part[b],
-                                 self.red_ctas)
+            # push my pieces of bucket b to their owners, wait for every peer's pieces of my part, sum locally
+            self.C.push_grads(self.flat.grad_flat, self.peers["staging"], self.peer_garrive, other[b], b, self.rank,
+                              self.flat.seg, self.grad_push_ctas)
+            self.C.wait_arrivals(self.garrive, self.gexpected, b, (self.world - 1) * self.grad_push_ctas)
+            self.C.reduce_staged(self.flat.grad_flat, self.staging, owned[b], self.world, self.rank, self.flat.seg,
+                                 self.bucket_part[b], self.red_ctas)
 
     def finish_reduce(self) -> torch.Tensor:
         """Reduce the buckets no hook reported (in bucket order), join the streams, and return this owner's sum of

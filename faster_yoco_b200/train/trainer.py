@@ -44,7 +44,7 @@ class _CommHooks:
 class Trainer:
     def __init__(self, model: torch.nn.Module, optim_cfg, *, device, comm: str = "nccl", zero_stage: int = 1,
                  pad_idx: int = 1, graph_step: bool = False, group=None, check_consistency: bool = True,
-                 overlap: bool = True, partition: str = "even"):
+                 overlap: bool = False, partition: str = "even"):
         self.model = model
         self.device = torch.device(device)
         self.cfg = optim_cfg
@@ -74,6 +74,9 @@ class Trainer:
         self._static: Dict[str, torch.Tensor] = {}
         self._graph_out = None
         self.vocab = None
+        import os as _os
+        self._timeline_on = _os.environ.get("FYB_TIMELINE", "0") == "1" and self.device.type == "cuda"
+        self._timeline = None
 
     # ------------------------------------------------------------------------------------------------------------
     def num_updates(self) -> int:
@@ -91,7 +94,25 @@ class Trainer:
             out[k] = t
         return out
 
+    def _mark(self, name):
+        """Device-event timeline of one update (FYB_TIMELINE=1, eager mode): phase boundaries on the compute stream."""
+        if self._timeline is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self._timeline.append((name, ev))
+
+    def timeline(self):
+        """[(phase, ms)] of the last update recorded with FYB_TIMELINE=1."""
+        if not self._timeline:
+            return []
+        torch.cuda.synchronize()
+        out = []
+        for (n0, e0), (n1, e1) in zip(self._timeline, self._timeline[1:]):
+            out.append((f"{n0}->{n1}", e0.elapsed_time(e1)))
+        return out
+
     def _forward_backward(self, src, tgt, ntok: torch.Tensor):
+        self._mark("start")
         if self.overlap:
             self.zero.p2p.start_gather()
             logits, _ = self.model(src, comm_hooks=_CommHooks(self.zero.p2p))
@@ -99,7 +120,9 @@ class Trainer:
             logits, _ = self.model(src)
         V = logits.shape[-1]
         loss = ops.cross_entropy(logits.view(-1, V), tgt.reshape(-1), self.pad_idx)
+        self._mark("forward")
         loss.backward()
+        self._mark("backward")
         return loss.detach()
 
     def _reduce_stats(self, loss_sum, sample_size):
@@ -113,12 +136,15 @@ class Trainer:
 
     def _device_update(self, src, tgt, ntok):
         """All device work of one update (capturable): returns (loss_sum, sample_size, grad_norm, consistent)."""
+        self._timeline = [] if (self._timeline_on and not self.graph_step) else None
         self.flat.begin_update()
         loss = self._forward_backward(src, tgt, ntok)
         self.flat.collect_grads()          # p.grad -> slot for gradients not written there by a native op
         loss_all, ss_all = self._reduce_stats(loss, ntok)
         sq = self.zero.reduce_grads()
+        self._mark("reduced")
         gnorm = self.zero.device_step(ss_all, sq)
+        self._mark("optimizer")
         if self.check_consistency:
             reduce = self.zero.p2p.all_reduce_vector if self.zero.p2p is not None else None
             consistent = grad_norm_consistent(gnorm, self.rank, self.world, self.group, reduce=reduce)
