@@ -1,0 +1,108 @@
+"""Training entry point (the reference's ``yoco/train.py`` -> fairseq ``cli_main``; call stack of one update in
+train/trainer.py).
+
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m faster_yoco_b200.cli.train DATA_DIR --arch yoco_3b \\
+        --task gpt --criterion cross_entropy --tokens-per-sample 2048 --batch-size 1 --tiktoken-model cl100k_base \\
+        --bf16 --zero-sharding os --max-update 1000
+
+Per update: ``update_freq`` micro-batches from the task's iterator, one ``Trainer.train_step``; a log line every
+``--log-interval`` updates (the only host read of device metrics); a checkpoint every ``--save-interval-updates``
+(model, consolidated optimizer state, LR schedule, every rank's data-iterator state). A run resumes from
+``<save-dir>/<restore-file>`` when it exists.
+"""
+from __future__ import annotations
+
+import os
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+from ..config import OptimConfig
+from ..parallel import dist as D
+from ..train.checkpoint import load_checkpoint, save_checkpoint
+from ..train.metrics import format_log
+from ..train.trainer import Trainer
+from .common import build_model, build_task, setup_runtime
+from .options import train_parser
+
+
+def _gather_iterator_states(itr):
+    st = itr.state_dict() if hasattr(itr, "state_dict") else None
+    if not D.is_dist():
+        return [st]
+    out = [None] * D.world()
+    dist.all_gather_object(out, st)
+    return out
+
+
+def main(argv=None) -> int:
+    args = train_parser().parse_args(argv)
+    device = setup_runtime(args)
+    rank, world = D.rank(), D.world()
+    if args.criterion != "cross_entropy":
+        raise SystemExit("training runs the cross_entropy criterion (the evaluation criterions are for validate)")
+    task = build_task(args)
+    ds = task.load_dataset("train")
+    model, family = build_model(args, task, device)
+    optim = OptimConfig(lr=args.lr[0], betas=args.adam_betas, eps=args.adam_eps, weight_decay=args.weight_decay,
+                        clip_norm=args.clip_norm, warmup_updates=args.warmup_updates,
+                        total_num_update=args.total_num_update, end_learning_rate=args.end_learning_rate,
+                        power=args.power)
+    comm = args.comm if (world > 1 and device.type == "cuda") else "nccl"
+    trainer = Trainer(model, optim, device=device, comm=comm, graph_step=bool(args.cuda_graph) and device.type == "cuda",
+                      overlap=bool(args.overlap), partition=args.partition, pad_idx=task.tokenizer.pad_id)
+    itr = task.get_batch_iterator(ds, max_sentences=args.batch_size, seed=args.seed, num_shards=world,
+                                  shard_id=rank)
+    restore = os.path.join(args.save_dir, args.restore_file)
+    if os.path.exists(restore) and not args.reset_optimizer:
+        ck = load_checkpoint(restore, model, trainer)
+        its = (ck.get("extra_state") or {}).get("train_iterator")
+        if its and not args.reset_dataloader and hasattr(itr, "load_state_dict") and len(its) == world:
+            itr.load_state_dict(its[rank])
+        if rank == 0:
+            print(f"| loaded checkpoint {restore} (num_updates {trainer.num_updates()})", flush=True)
+    if rank == 0:
+        n = sum(p.numel() for p in model.parameters())
+        print(f"| model {args.arch} ({family}), params {n:,}, world {world}, comm {comm}, device {device}", flush=True)
+
+    t_start = time.perf_counter()
+    while args.max_update <= 0 or trainer.num_updates() < args.max_update:
+        batches = [next(itr) for _ in range(args.update_freq)]
+        trainer.train_step(batches if args.update_freq > 1 else batches[0])
+        nu = trainer.num_updates()
+        if nu % args.log_interval == 0:
+            stats = trainer.log_stats()
+            stats["num_updates"] = nu
+            stats["lr"] = trainer.sched.lr_for(nu)
+            stats["train_wall"] = round(time.perf_counter() - t_start, 1)
+            if rank == 0:
+                print(format_log(stats), flush=True)
+        if not args.no_save and args.save_interval_updates > 0 and nu % args.save_interval_updates == 0:
+            states = _gather_iterator_states(itr)
+            save_checkpoint(os.path.join(args.save_dir, f"checkpoint_1_{nu}.pt"), model, trainer,
+                            extra_state={"train_iterator": states})
+            if rank == 0:
+                import shutil
+                shutil.copyfile(os.path.join(args.save_dir, f"checkpoint_1_{nu}.pt"),
+                                os.path.join(args.save_dir, "checkpoint_last.pt"))
+    trainer.pending.check(block=True)
+    if not args.no_save:
+        states = _gather_iterator_states(itr)
+        save_checkpoint(os.path.join(args.save_dir, "checkpoint_last.pt"), model, trainer,
+                        extra_state={"train_iterator": states})
+    if hasattr(itr, "close"):
+        itr.close()
+    trainer.release_graph()
+    D.barrier()
+    D.destroy()
+    return 0
+
+
+def cli_main():
+    sys.exit(main())
+
+
+if __name__ == "__main__":
+    cli_main()

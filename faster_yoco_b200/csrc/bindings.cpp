@@ -21,7 +21,7 @@ std::vector<at::Tensor> swiglu_bwd(const at::Tensor& x, const at::Tensor& y, con
                                    const c10::optional<at::Tensor>& dx_out, const c10::optional<at::Tensor>& dy_out);
 at::Tensor gate_cumsum_fwd(const at::Tensor& y, int64_t B, int64_t L, double normalizer);
 void gate_cumsum_bwd(const at::Tensor& dg, const at::Tensor& y, at::Tensor& dy, double normalizer);
-at::Tensor rope_fwd(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t, bool conj);
+at::Tensor rope_fwd(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t, bool conj, bool neox);
 at::Tensor embedding_fwd(const at::Tensor& tok, const at::Tensor& w, double scale);
 at::Tensor embedding_bwd(const at::Tensor& tok, const at::Tensor& dy, int64_t V, double scale,
                          const c10::optional<at::Tensor>& out);
@@ -113,7 +113,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("dy_out") = py::none());
   m.def("gate_cumsum_fwd", &fyb::gate_cumsum_fwd);
   m.def("gate_cumsum_bwd", &fyb::gate_cumsum_bwd);
-  m.def("rope_fwd", &fyb::rope_fwd);
+  m.def("rope_fwd", &fyb::rope_fwd, py::arg("x"), py::arg("cos"), py::arg("sin"), py::arg("conj") = false,
+        py::arg("neox") = false);
   m.def("embedding_fwd", &fyb::embedding_fwd);
   m.def("embedding_bwd", &fyb::embedding_bwd, py::arg("tok"), py::arg("dy"), py::arg("V"), py::arg("scale"),
         py::arg("out") = py::none());

@@ -104,6 +104,39 @@ __global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, int64_t sb, int
   store8(out + ((static_cast<int64_t>(b) * L + l) * H + h) * D + c8, o);
 }
 
+// NeoX / non-interleaved rotary: pairs (x[i], x[i + D/2]); each thread rotates 8 pairs.
+__global__ void rope_neox_kernel(const __nv_bfloat16* __restrict__ x, int64_t sb, int64_t sl, int64_t sh,
+                                 const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t,
+                                 __nv_bfloat16* __restrict__ out, int B, int L, int H, int D, float sign) {
+  const int half = D / 2;
+  const int per = half / 8;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t total = static_cast<int64_t>(B) * L * H * per;
+  if (i >= total) return;
+  const int c8 = static_cast<int>(i % per) * 8;
+  int64_t rest = i / per;
+  const int h = static_cast<int>(rest % H);
+  rest /= H;
+  const int l = static_cast<int>(rest % L);
+  const int b = static_cast<int>(rest / L);
+  float a[8], bb[8], oa[8], ob[8];
+  const __nv_bfloat16* src = x + b * sb + l * sl + h * sh;
+  load8(src + c8, a);
+  load8(src + half + c8, bb);
+  const __nv_bfloat16* cp = cos_t + static_cast<int64_t>(l) * half + c8;
+  const __nv_bfloat16* spp = sin_t + static_cast<int64_t>(l) * half + c8;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float cs = __bfloat162float(cp[k]);
+    const float sn = sign * __bfloat162float(spp[k]);
+    oa[k] = a[k] * cs - bb[k] * sn;
+    ob[k] = a[k] * sn + bb[k] * cs;
+  }
+  __nv_bfloat16* dst = out + ((static_cast<int64_t>(b) * L + l) * H + h) * D;
+  store8(dst + c8, oa);
+  store8(dst + half + c8, ob);
+}
+
 // ------------------------------------------------------------------------------------------------------------------
 // embedding: out[i] = bf16(w[tok[i]] * scale)
 
@@ -504,7 +537,7 @@ std::vector<at::Tensor> swiglu_bwd(const at::Tensor& x, const at::Tensor& y, con
   return {dx, dy};
 }
 
-at::Tensor rope_fwd(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t, bool conj) {
+at::Tensor rope_fwd(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t, bool conj, bool neox) {
   FYB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 4 && x.stride(3) == 1,
             "rope: bf16 [B, L, H, D] with contiguous last dim expected");
   const int B = (int)x.size(0), L = (int)x.size(1), H = (int)x.size(2), D = (int)x.size(3);
@@ -515,6 +548,18 @@ at::Tensor rope_fwd(const at::Tensor& x, const at::Tensor& cos_t, const at::Tens
             "rope: cos/sin must be contiguous bf16 [L, D/2]");
   c10::cuda::CUDAGuard guard(x.device());
   auto out = at::empty({B, L, H, D}, x.options());
+  if (neox) {
+    FYB_CHECK(D % 16 == 0, "rope (neox): head dim must be a multiple of 16");
+    const int64_t n = static_cast<int64_t>(B) * L * H * (D / 16);
+    if (n > 0)
+      rope_neox_kernel<<<(n + 255) / 256, 256, 0, cur_stream()>>>(
+          reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), x.stride(1), x.stride(2),
+          reinterpret_cast<const __nv_bfloat16*>(cos_t.data_ptr()),
+          reinterpret_cast<const __nv_bfloat16*>(sin_t.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+          B, L, H, D, conj ? -1.f : 1.f);
+    check_launch("rope_neox");
+    return out;
+  }
   const int64_t n = static_cast<int64_t>(B) * L * H * (D / 8);
   if (n > 0)
     rope_kernel<<<(n + 255) / 256, 256, 0, cur_stream()>>>(

@@ -101,7 +101,9 @@ class _NativeLinear(torch.autograd.Function):
 
 
 def linear(x: torch.Tensor, w: torch.Tensor, residual: Optional[torch.Tensor] = None) -> torch.Tensor:
-    if native_on(x):
+    """y = x @ w.T (+ residual). The tcgen05 GEMM needs 16-byte aligned rows (K and N multiples of 8 bf16);
+    other shapes (e.g. LLaMA's int(8 d / 3) FFN width) run on cuBLAS."""
+    if native_on(x) and x.shape[-1] % 8 == 0 and w.shape[0] % 8 == 0 and x.dtype == torch.bfloat16:
         return _NativeLinear.apply(x, w, residual)
     y = F.linear(x, w)
     return y + residual if residual is not None else y
@@ -176,25 +178,27 @@ def swiglu(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
 
 class _NativeRope(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, cos, sin):
+    def forward(ctx, x, cos, sin, neox):
         ctx.save_for_backward(cos, sin)
-        return _C().rope_fwd(x, cos, sin, False)
+        ctx.neox = neox
+        return _C().rope_fwd(x, cos, sin, False, neox)
 
     @staticmethod
     def backward(ctx, dy):
         cos, sin = ctx.saved_tensors
         if dy.stride(-1) != 1 or any(st % 8 for st in dy.stride()[:-1]):
             dy = dy.contiguous()
-        return _C().rope_fwd(dy, cos, sin, True), None, None
+        return _C().rope_fwd(dy, cos, sin, True, ctx.neox), None, None, None
 
 
-def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """x: [B, L, H, D] (any strides with a contiguous last dim); returns a contiguous [B, L, H, D]."""
-    if native_on(x):
+def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, interleaved: bool = True) -> torch.Tensor:
+    """x: [B, L, H, D] (any strides with a contiguous last dim); returns a contiguous [B, L, H, D].
+    ``interleaved=False`` rotates NeoX half pairs (the LLaMA baseline's mode)."""
+    if native_on(x) and (interleaved or x.size(-1) % 16 == 0):
         if x.stride(-1) != 1 or any(st % 8 for st in x.stride()[:-1]):
             x = x.contiguous()
-        return _NativeRope.apply(x, cos, sin)
-    return ref.apply_rope(x, cos, sin)
+        return _NativeRope.apply(x, cos, sin, not interleaved)
+    return ref.apply_rope(x, cos, sin, interleaved=interleaved)
 
 
 # ----------------------------------------------------------------------------------------------------------------------

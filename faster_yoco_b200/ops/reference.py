@@ -44,6 +44,12 @@ def gate_logsigmoid(gt: torch.Tensor, normalizer: float = 16.0) -> torch.Tensor:
     return F.logsigmoid(gt) / normalizer
 
 
+def llama_rope_angles(head_dim: int, max_len: int, theta: float, device=None) -> torch.Tensor:
+    """The LLaMA baseline's angles: t / theta ** (arange(0, D, 2) / D) (yoco/models/decoder/transformer.py:27-31)."""
+    freqs = 1.0 / (theta ** (torch.arange(0, head_dim, 2, device=device)[: head_dim // 2].float() / head_dim))
+    return torch.outer(torch.arange(max_len, device=device).float(), freqs)
+
+
 def rope_angles(head_dim: int, max_len: int, theta: float, device=None) -> torch.Tensor:
     """angle[t, i] = t / theta ** linspace(0, 1, head_dim // 2)[i] (note: linspace, not arange / d)."""
     angle = 1.0 / (theta ** torch.linspace(0, 1, head_dim // 2, dtype=torch.float, device=device))
@@ -59,9 +65,20 @@ def rope_tables(head_dim: int, start: int, length: int, theta: float, dtype, dev
     return torch.cos(a).to(dtype), torch.sin(a).to(dtype)
 
 
-def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, conjugate: bool = False) -> torch.Tensor:
-    """x: [B, L, H, D]; cos/sin: [L, D/2]. Interleaved pairs (x[2i], x[2i+1]); fp32 math, output in x.dtype."""
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, conjugate: bool = False,
+               interleaved: bool = True) -> torch.Tensor:
+    """x: [B, L, H, D]; cos/sin: [L, D/2]. Interleaved (GPT-J) pairs (x[2i], x[2i+1]) or, with
+    ``interleaved=False``, NeoX pairs (x[i], x[i + D/2]) (yoco/models/decoder/kernel/rotary.py:302-332);
+    fp32 math, output in x.dtype."""
     B, L, H, D = x.shape
+    if not interleaved:
+        xf = x.float()
+        c = cos.float()[None, :L, None, :]
+        s = sin.float()[None, :L, None, :]
+        if conjugate:
+            s = -s
+        x0, x1 = xf[..., :D // 2], xf[..., D // 2:]
+        return torch.cat([x0 * c - x1 * s, x0 * s + x1 * c], dim=-1).to(x.dtype)
     xf = x.float().view(B, L, H, D // 2, 2)
     c = cos.float()[None, :L, None, :]
     s = sin.float()[None, :L, None, :]
@@ -108,6 +125,32 @@ def chunk_gate_retention(q, k, v, g, chunk_size: int = 256, last_hidden_state=No
     attn = attn * (g[..., None] - g[..., None, :] + causal).exp().to(attn.dtype)
     inner = attn @ v
     return (cross + inner).view(bsz, num_head, tgt_len, head_dim)
+
+
+def hier_chunk_gate_retention(q, k, v, g, chunk_size: int = 256, hier_chunk_size: int = 16384):
+    """Two-level chunking for long sequences (yoco/models/decoder/kernel/gate_recurrent.py:230-251): the sequence
+    is cut into hierarchy chunks of ``hier_chunk_size``; each one is processed independently with the chunkwise form
+    (state 0 at its start), and the state carried across hierarchy chunks adds ``(q exp(G_local)) @ S_prev``. Equal
+    to chunk_gate_retention; the hierarchy chunks are independent units of work (e.g. one per rank or stream)."""
+    B, H, L, Dk = q.shape
+    Dv = v.shape[-1]
+    n = L // hier_chunk_size
+    if n * hier_chunk_size != L:
+        raise ValueError("sequence length must be a multiple of hier_chunk_size")
+    fold = lambda t, d: t.view(B, H, n, hier_chunk_size, d).transpose(1, 2).reshape(B * n, H, hier_chunk_size, d)
+    inner = chunk_gate_retention(fold(q, Dk), fold(k, Dk), fold(v, Dv),
+                                 g.view(B, H, n, hier_chunk_size).transpose(1, 2).reshape(B * n, H, hier_chunk_size),
+                                 chunk_size)
+    inner = inner.view(B, n, H, hier_chunk_size, Dv).transpose(1, 2).reshape(B, H, L, Dv)
+    # hierarchy-level states: exclusive scan over the per-chunk (sum of decayed k^T v, total decay)
+    qh = q.view(B, H, n, hier_chunk_size, Dk)
+    kh = k.view(B, H, n, hier_chunk_size, Dk) * (Dk ** -0.5)
+    vh = v.view(B, H, n, hier_chunk_size, Dv)
+    G = g.view(B, H, n, hier_chunk_size).float().cumsum(-1)
+    kv = kh.transpose(-1, -2) @ (vh * (G[..., -1:] - G).exp()[..., None].to(vh.dtype))
+    S = chunk_gate_recurrent_naive(kv, G[..., -1].exp().to(kv.dtype))
+    cross = (qh * G[..., None].exp().to(qh.dtype)) @ S
+    return inner + cross.view(B, H, L, Dv)
 
 
 def parallel_gate_retention(q, k, v, g):

@@ -154,7 +154,8 @@ class FlatParams:
         self._written.clear()
 
     def begin_microbatch(self, first: bool):
-        self.accumulate = not first
+        """Gradient accumulation needs no flag: a slot written by an earlier micro-batch of this update is
+        accumulated into (claim_grad), autograd accumulates p.grad for the others until collect_grads."""
 
     def collect_grads(self):
         """Move every p.grad into its slot and clear p.grad; slots that no gradient reached this update are zeroed."""
@@ -164,10 +165,10 @@ class FlatParams:
                 slot = self.grad_flat[e.offset:e.offset + e.numel]
                 written = id(e.param) in self._written
                 if g is None:
-                    if not written and not self.accumulate:
+                    if not written:
                         slot.zero_()
                 elif g.data_ptr() != slot.data_ptr():
-                    if written or self.accumulate:
+                    if written:
                         slot.view(e.shape).add_(g)
                     else:
                         slot.view(e.shape).copy_(g)

@@ -23,6 +23,7 @@ from .. import ops
 from ..parallel import dist as D
 from ..parallel.zero import FlatParams, ZeroOptimizer
 from ..utils.faults import PendingChecks, grad_norm_consistent
+from ..utils.tracing import phase
 from .metrics import DeviceMeters
 from .schedule import PolynomialDecaySchedule
 
@@ -44,7 +45,7 @@ class _CommHooks:
 class Trainer:
     def __init__(self, model: torch.nn.Module, optim_cfg, *, device, comm: str = "nccl", zero_stage: int = 1,
                  pad_idx: int = 1, graph_step: bool = False, group=None, check_consistency: bool = True,
-                 overlap: bool = False, partition: str = "even"):
+                 overlap: bool = False, partition: str = "even", criterion=None):
         self.model = model
         self.device = torch.device(device)
         self.cfg = optim_cfg
@@ -77,6 +78,7 @@ class Trainer:
         import os as _os
         self._timeline_on = _os.environ.get("FYB_TIMELINE", "0") == "1" and self.device.type == "cuda"
         self._timeline = None
+        self.criterion = criterion
 
     # ------------------------------------------------------------------------------------------------------------
     def num_updates(self) -> int:
@@ -111,17 +113,22 @@ class Trainer:
             out.append((f"{n0}->{n1}", e0.elapsed_time(e1)))
         return out
 
-    def _forward_backward(self, src, tgt, ntok: torch.Tensor):
+    def _forward_backward(self, src, tgt, first: bool = True, last: bool = True):
         self._mark("start")
-        if self.overlap:
-            self.zero.p2p.start_gather()
-            logits, _ = self.model(src, comm_hooks=_CommHooks(self.zero.p2p))
-        else:
-            logits, _ = self.model(src)
-        V = logits.shape[-1]
-        loss = ops.cross_entropy(logits.view(-1, V), tgt.reshape(-1), self.pad_idx)
+        with phase("forward"):
+            if self.overlap:
+                self.zero.p2p.start_gather()
+                logits, _ = self.model(src, comm_hooks=_CommHooks(self.zero.p2p))
+            else:
+                logits, _ = self.model(src)
+            V = logits.shape[-1]
+            if self.criterion is not None:
+                loss = self.criterion(logits, tgt)
+            else:
+                loss = ops.cross_entropy(logits.view(-1, V), tgt.reshape(-1), self.pad_idx)
         self._mark("forward")
-        loss.backward()
+        with phase("backward"):
+            loss.backward()
         self._mark("backward")
         return loss.detach()
 
@@ -134,16 +141,23 @@ class Trainer:
                 dist.all_reduce(stats, group=self.group)
         return stats[0], stats[1]
 
-    def _device_update(self, src, tgt, ntok):
-        """All device work of one update (capturable): returns (loss_sum, sample_size, grad_norm, consistent)."""
+    def _device_update(self, srcs, tgts, ntok):
+        """All device work of one update (capturable): returns (loss_sum, sample_size, grad_norm, consistent).
+        srcs / tgts: the update's micro-batches (``update_freq`` of them); gradients accumulate across them."""
         self._timeline = [] if (self._timeline_on and not self.graph_step) else None
         self.flat.begin_update()
-        loss = self._forward_backward(src, tgt, ntok)
-        self.flat.collect_grads()          # p.grad -> slot for gradients not written there by a native op
-        loss_all, ss_all = self._reduce_stats(loss, ntok)
-        sq = self.zero.reduce_grads()
+        loss = None
+        n = len(srcs)
+        for i, (src, tgt) in enumerate(zip(srcs, tgts)):
+            li = self._forward_backward(src, tgt, first=i == 0, last=i == n - 1)
+            loss = li if loss is None else loss + li
+        with phase("reduce-grads"):
+            self.flat.collect_grads()          # p.grad -> slot for gradients not written there by a native op
+            loss_all, ss_all = self._reduce_stats(loss, ntok)
+            sq = self.zero.reduce_grads()
         self._mark("reduced")
-        gnorm = self.zero.device_step(ss_all, sq)
+        with phase("optimizer"):
+            gnorm = self.zero.device_step(ss_all, sq)
         self._mark("optimizer")
         if self.check_consistency:
             reduce = self.zero.p2p.all_reduce_vector if self.zero.p2p is not None else None
@@ -153,35 +167,46 @@ class Trainer:
         return loss_all, ss_all, gnorm, consistent
 
     def train_step(self, batch) -> torch.Tensor:
-        """One update; returns the (device) summed loss over ranks without waiting for it."""
+        """One update over a batch, or over a list of micro-batches (``--update-freq``); returns the (device) summed
+        loss over ranks without waiting for it."""
         self.pending.check(block=False)
         self.model.train()
-        dev = self._to_device(batch)
-        ntok = torch.as_tensor(float(batch["ntokens"]), dtype=torch.float32)
+        batches = batch if isinstance(batch, (list, tuple)) else [batch]
+        if self.overlap and len(batches) > 1:
+            raise ValueError("overlapped communication hands gradients to their owners during backward; "
+                             "use update_freq 1 with it (or overlap=False)")
+        devs = [self._to_device(b) for b in batches]
+        ntokens = sum(int(b["ntokens"]) for b in batches)
+        nsent = sum(int(b.get("nsentences", b["src_tokens"].shape[0])) for b in batches)
+        ntok = torch.as_tensor(float(ntokens), dtype=torch.float32)
         lr = self.sched.lr_for(self.num_updates())
+        srcs, tgts = [d["src_tokens"] for d in devs], [d["target"] for d in devs]
         if self.graph_step:
-            out = self._graph_update(dev, ntok, lr)
+            out = self._graph_update(srcs, tgts, ntok, lr)
         else:
             ntok_d = ntok.to(self.device, non_blocking=True) if self.device.type == "cuda" else ntok
             self.zero.prepare(lr)
-            out = self._device_update(dev["src_tokens"], dev["target"], ntok_d)
+            out = self._device_update(srcs, tgts, ntok_d)
         loss_all, ss_all, gnorm, consistent = out
         self.pending.check(block=True)
         self.pending.arm(torch.isfinite(gnorm), consistent)
         self.zero.finish()
-        self.meters.update(loss_all, ss_all, batch["ntokens"] * self.world, batch.get("nsentences", 1) * self.world,
-                           gnorm, self.cfg.clip_norm)
+        self.meters.update(loss_all, ss_all, ntokens * self.world, nsent * self.world, gnorm, self.cfg.clip_norm)
         return loss_all
 
     # ------------------------------------------------------------------------------------------------------------
-    def _graph_update(self, dev, ntok, lr):
+    def _graph_update(self, srcs, tgts, ntok, lr):
         st = self._static
+        if self._graph is not None and ([tuple(s.shape) for s in srcs] != [tuple(s.shape) for s in st["src"]]):
+            self._graph, self._graph_out = None, None          # new batch geometry: capture again
         if self._graph is None:
-            st["src"] = torch.empty_like(dev["src_tokens"])
-            st["tgt"] = torch.empty_like(dev["target"])
+            st["src"] = [torch.empty_like(s) for s in srcs]
+            st["tgt"] = [torch.empty_like(t) for t in tgts]
             st["ntok"] = torch.zeros((), dtype=torch.float32, device=self.device)
-        st["src"].copy_(dev["src_tokens"], non_blocking=True)
-        st["tgt"].copy_(dev["target"], non_blocking=True)
+        for d, s in zip(st["src"], srcs):
+            d.copy_(s, non_blocking=True)
+        for d, t in zip(st["tgt"], tgts):
+            d.copy_(t, non_blocking=True)
         st["ntok"].copy_(ntok, non_blocking=True)
         self.zero.prepare(lr)
         if self._graph is None:

@@ -128,6 +128,20 @@ def test_rope_strided_and_conj():
     assert rel(back, x) < 2e-2
 
 
+@pytest.mark.parametrize("D", [128, 64])
+def test_rope_neox(D):
+    from faster_yoco_b200.ops import reference as ref
+    B, L, H = 2, 77, 4
+    big = torch.randn(B, L, 3 * H * D, device=dev(), dtype=torch.bfloat16)
+    x = big[..., H * D:2 * H * D].view(B, L, H, D)
+    ang = ref.llama_rope_angles(D, L, 1e4, dev())
+    cos, sin = torch.cos(ang).to(torch.bfloat16), torch.sin(ang).to(torch.bfloat16)
+    out = C().rope_fwd(x, cos, sin, False, True)
+    assert rel(out, ref.apply_rope(x, cos, sin, interleaved=False)) < 1e-2
+    back = C().rope_fwd(out, cos, sin, True, True)
+    assert rel(back, x) < 2e-2
+
+
 def test_subln_swiglu():
     from faster_yoco_b200.ops import reference as ref
     T, H, D = 257, 6, 128
