@@ -59,8 +59,29 @@ def add_common(p: argparse.ArgumentParser):
     return p
 
 
+def load_preset(name: str) -> dict:
+    """A named switch set (``faster_yoco_b200/presets/<name>.json``, or a path): {"args": {dest: value}}."""
+    import json
+    import os
+    path = name if os.path.exists(name) else os.path.join(os.path.dirname(os.path.dirname(__file__)), "presets",
+                                                           name + ".json")
+    with open(path) as f:
+        return json.load(f).get("args", {})
+
+
+def parse_with_preset(parser: argparse.ArgumentParser, argv=None):
+    """--preset NAME supplies defaults; flags given on the command line still win."""
+    pre = argparse.ArgumentParser(add_help=False)
+    pre.add_argument("--preset", default=None)
+    known, _ = pre.parse_known_args(argv)
+    if known.preset:
+        parser.set_defaults(**load_preset(known.preset))
+    return parser.parse_args(argv)
+
+
 def train_parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser("faster_yoco_b200 train")
+    p.add_argument("--preset", default=None, help="named switch set (presets/*.json)")
     p.add_argument("data", nargs="?", default=None)
     add_common(p)
     g = p.add_argument_group("optimization")
@@ -87,6 +108,9 @@ def train_parser() -> argparse.ArgumentParser:
     g.add_argument("--reset-optimizer", action="store_true")
     g.add_argument("--reset-dataloader", action="store_true")
     g.add_argument("--disable-validation", action="store_true")
+    g.add_argument("--save-model-only", action="store_true",
+                   help="paired-validation saves: bf16 model state dict model_<update>.pt on rank 0 (no optimizer "
+                        "state) at every save point, plus each rank's peak memory as a VALIDATION_MEM line")
     g = p.add_argument_group("B200 execution")
     g.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                    help="fused: NVLink peer-memory reduce/all-gather kernels; nccl: the NCCL baseline path")

@@ -25,7 +25,7 @@ from ..train.checkpoint import load_checkpoint, save_checkpoint
 from ..train.metrics import format_log
 from ..train.trainer import Trainer
 from .common import build_model, build_task, setup_runtime
-from .options import train_parser
+from .options import parse_with_preset, train_parser
 
 
 def _gather_iterator_states(itr):
@@ -37,8 +37,26 @@ def _gather_iterator_states(itr):
     return out
 
 
+def _save_model_only(args, model, nu: int, rank: int):
+    """bf16 model-only save on rank 0 (reference parameter names, ``decoder.model.`` prefix) and peak memory."""
+    import json
+    mem = {"rank": rank, "num_updates": nu, "time": time.time()}
+    if torch.cuda.is_available():
+        mem.update(max_allocated_gib=torch.cuda.max_memory_allocated() / 2 ** 30,
+                   max_reserved_gib=torch.cuda.max_memory_reserved() / 2 ** 30)
+    print("VALIDATION_MEM " + json.dumps(mem), flush=True)
+    path = os.path.join(args.save_dir, f"model_{nu:06d}.pt")
+    if rank == 0 and nu > 0 and not os.path.exists(path):
+        t0 = time.time()
+        os.makedirs(args.save_dir, exist_ok=True)
+        sd = {"decoder.model." + k: v.detach().to("cpu", copy=True) for k, v in model.state_dict().items()}
+        torch.save({"model": sd, "num_updates": nu}, path + ".tmp")
+        os.replace(path + ".tmp", path)
+        print(f"VALIDATION_CKPT {path} {time.time() - t0:.1f}s", flush=True)
+
+
 def main(argv=None) -> int:
-    args = train_parser().parse_args(argv)
+    args = parse_with_preset(train_parser(), argv)
     device = setup_runtime(args)
     rank, world = D.rank(), D.world()
     if args.criterion != "cross_entropy":
@@ -79,7 +97,9 @@ def main(argv=None) -> int:
             stats["train_wall"] = round(time.perf_counter() - t_start, 1)
             if rank == 0:
                 print(format_log(stats), flush=True)
-        if not args.no_save and args.save_interval_updates > 0 and nu % args.save_interval_updates == 0:
+        if args.save_model_only and args.save_interval_updates > 0 and nu % args.save_interval_updates == 0:
+            _save_model_only(args, model, nu, rank)
+        elif not args.no_save and args.save_interval_updates > 0 and nu % args.save_interval_updates == 0:
             states = _gather_iterator_states(itr)
             save_checkpoint(os.path.join(args.save_dir, f"checkpoint_1_{nu}.pt"), model, trainer,
                             extra_state={"train_iterator": states})
@@ -88,7 +108,9 @@ def main(argv=None) -> int:
                 shutil.copyfile(os.path.join(args.save_dir, f"checkpoint_1_{nu}.pt"),
                                 os.path.join(args.save_dir, "checkpoint_last.pt"))
     trainer.pending.check(block=True)
-    if not args.no_save:
+    if args.save_model_only:
+        _save_model_only(args, model, trainer.num_updates(), rank)
+    elif not args.no_save:
         states = _gather_iterator_states(itr)
         save_checkpoint(os.path.join(args.save_dir, "checkpoint_last.pt"), model, trainer,
                         extra_state={"train_iterator": states})

@@ -6,8 +6,9 @@ in ``<data_dir>/json/<name>.json``):
 1. the file list repeated 50 times and shuffled with ``Random(str(seed))``, cut into contiguous chunks, one per rank;
 2. each jsonl file read and tokenised document by document: a document splits on blank lines, then on lines; each
    line is encoded with its trailing newline(s), and the document's last piece gets EOS (``_doc_to_ids``);
-3. the pieces of a file packed into BOS-started samples of ``tokens_per_sample + 1`` ids: a piece that overflows is
-   truncated and starts a new sample; the remainder of the file is dropped;
+3. the pieces of a file packed into BOS-started samples of ``tokens_per_sample + 1`` ids: the piece that overflows
+   a sample fills it up to its end (the rest of that piece is dropped) and the next sample starts with BOS alone; the
+   partly filled sample at the end of a file is dropped;
 4. sources multiplexed by weight with ``Random(seed + n)`` for the n-th sample;
 5. blockwise shuffle (``batch_read_ahead`` samples per block, each block shuffled with ``Random(str(seed))``), fixed
    batches of ``batch_size``, collate: ``src_tokens = ids[:-1]``, ``target = ids[1:]`` (pad 1 up to

@@ -53,6 +53,40 @@ def main():
         y = torch.empty(2048, 3072, device=dev, dtype=torch.bfloat16)
         for _ in range(a.reps):
             C.gemm(dy, w, y, False, True, None)
+    elif a.what == "adam":
+        # a quarter of one rank's ZeRO segment at 8 GPUs (1.7 GB in total, well above L2)
+        n = 107_665_728
+        p32 = torch.randn(n, device=dev)
+        m = torch.zeros(n, device=dev)
+        v = torch.zeros(n, device=dev)
+        g16 = torch.randn(n, device=dev, dtype=torch.bfloat16)
+        p16 = torch.empty(n, device=dev, dtype=torch.bfloat16)
+        hyper = torch.tensor([1e-4, 0.1, 0.05, 0.0], device=dev)
+        factor = torch.tensor([1.0], device=dev)
+        for _ in range(a.reps):
+            C.adam_step(p32, g16, m, v, p16, hyper, factor, 0.9, 0.95, 1e-6, 0.05, True)
+    elif a.what in ("ce", "ce_bwd"):
+        x = (torch.randn(L, 100288, device=dev) * 2).to(torch.bfloat16)
+        t = torch.randint(0, 100288, (L,), device=dev)
+        loss, lse = C.ce_fwd(x, t, 1)
+        g = torch.ones(1, device=dev)
+        out = torch.empty_like(x)
+        for _ in range(a.reps):
+            if a.what == "ce":
+                C.ce_fwd(x, t, 1)
+            else:
+                C.ce_bwd(x, t, lse, g, 1, out)
+    elif a.what in ("rms", "rms_bwd"):
+        x = torch.randn(L, 3072, device=dev, dtype=torch.bfloat16)
+        w = torch.ones(3072, device=dev, dtype=torch.bfloat16)
+        y, rstd = C.rms_norm_fwd(x, w, 1e-5)
+        for _ in range(a.reps):
+            if a.what == "rms":
+                C.rms_norm_fwd(x, w, 1e-5)
+            else:
+                C.rms_norm_bwd(y, x, w, rstd)
+    else:
+        raise SystemExit(f"unknown --what {a.what}")
     torch.cuda.synchronize()
     st = int(C.status()[0].item())
     if st != 0:

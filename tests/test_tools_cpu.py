@@ -1,0 +1,124 @@
+"""Data builder, held-out pipeline, validation summary / verdict, performance views, presets (CPU)."""
+import gzip
+import json
+import os
+
+import pytest
+import torch
+
+from faster_yoco_b200.data.tokenizers import ByteTokenizer
+
+
+def _sources(tmp):
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+    fw = os.path.join(tmp, "fw.parquet")
+    pq.write_table(pa.table({"text": [f"web document {i} " * 20 if i % 7 else "" for i in range(60)]}), fw)
+    cp = os.path.join(tmp, "cp.json.gz")
+    with gzip.open(cp, "wt") as f:
+        for i in range(30):
+            f.write(json.dumps({"content": f"def f{i}():\n    return {i}\n" * 10}) + "\n")
+    return fw, cp
+
+
+def test_build_data_layout(tmp_path):
+    from faster_yoco_b200.data import build_data as B
+    fw, cp = _sources(str(tmp_path))
+    out = str(tmp_path / "out")
+    assert B.main(["--source", f"fineweb_edu:{fw}:text:0.8", "--source", f"codeparrot:{cp}:content:0.2",
+                   "--lines-per-shard", "20", out]) == 0
+    root = os.path.join(out, "Data")
+    train = json.load(open(os.path.join(root, "json", "train.json")))
+    assert train == [{"name": "fineweb_edu", "weight": 0.8}, {"name": "codeparrot", "weight": 0.2}]
+    shards = json.load(open(os.path.join(root, "json", "fineweb_edu.json")))
+    assert len(shards) == 3 and all(os.path.isabs(p) for p in shards)     # 51 non-empty docs / 20 per shard
+    m = json.load(open(os.path.join(out, "data_manifest.json")))
+    assert m["sources"]["fineweb_edu"]["docs"] == 51 and m["sources"]["fineweb_edu"]["skipped_empty"] == 9
+    with pytest.raises(ValueError):
+        B.build([B.Source("x", fw, "text", 1.0, sha256="0" * 64)], str(tmp_path / "out2"))
+    # the GPT task reads it
+    from faster_yoco_b200.data.lm_loader import LMLoader
+    L = LMLoader(train, root, ByteTokenizer(), tokens_per_sample=32, batch_size=2, prefetch=0, batch_read_ahead=4)
+    b = next(L)
+    assert b["src_tokens"].shape == (2, 32)
+
+
+def test_heldout_pipeline(tmp_path):
+    from faster_yoco_b200.data import build_data as B
+    from faster_yoco_b200.validation import heldout as H
+    fw, cp = _sources(str(tmp_path))
+    out = str(tmp_path / "out")
+    B.build([B.Source("fineweb_edu", fw, "text", 0.8), B.Source("codeparrot", cp, "content", 0.2)], out)
+    hd = str(tmp_path / "held")
+    r = H.extract(fw, cp, hd, 10, 5)
+    assert r["fineweb_edu"] == 10 and r["codeparrot"] == 5
+    # every held-out document also occurs in training here -> dedup drops them all
+    d = H.dedup(os.path.join(out, "Data"), hd)
+    assert d["fineweb_edu"] == {"kept": 0, "dropped": 10}
+    assert H.check(os.path.join(out, "Data"), hd)["exact_duplicates_in_training_shards"] == {}
+    # restore the originals and pack them
+    for n in H.SOURCES:
+        os.replace(os.path.join(hd, f"heldout_{n}.jsonl.orig"), os.path.join(hd, f"heldout_{n}.jsonl"))
+    res = H.build(hd, os.path.join(hd, "heldout.pt"), 2, 1, ByteTokenizer(), tokens_per_sample=64)
+    t = torch.load(os.path.join(hd, "heldout.pt"))
+    assert t["samples"]["fineweb_edu"].shape == (2, 65) and t["n_words"] == 264 and t["pad_id"] == 1
+    assert int(t["samples"]["codeparrot"][0, 0]) == 0
+
+
+def _fake_arm(d, offset, updates=4000, evals=(2000, 4000)):
+    os.makedirs(d, exist_ok=True)
+    with open(os.path.join(d, "train.log"), "w") as f:
+        for n in range(10, updates + 1, 10):
+            loss = 10.0 / (1 + n / 500) + offset
+            f.write(f"epoch 001: loss {loss:.4f} | ppl 1.0 | gnorm 0.5 | num_updates {n} | lr 1e-4 | "
+                    f"train_wall {n * 0.08:.1f}\n")
+        f.write('VALIDATION_MEM {"rank": 0, "num_updates": 4000, "max_allocated_gib": 61.5}\n')
+    ev = {f"model_{k:06d}.pt": {"num_updates": k, "fineweb_edu": {"loss_bits": 3.0 + offset - k / 1e4},
+                                "codeparrot": {"loss_bits": 2.0 + offset - k / 1e4},
+                                "mix_0.8_0.2_bits": 2.8 + offset - k / 1e4} for k in evals}
+    json.dump(ev, open(os.path.join(d, "eval.json"), "w"))
+
+
+def test_analyze_and_verdict(tmp_path):
+    from faster_yoco_b200.validation import analyze, verdict
+    V = str(tmp_path)
+    for arm, off in (("opt", 0.001), ("ref", 0.0), ("ref_s2", 0.01), ("opt_s2", 0.008)):
+        _fake_arm(os.path.join(V, arm), off)
+    assert analyze.main([V]) == 0
+    S = json.load(open(os.path.join(V, "summary.json")))["arms"]
+    assert S["opt"]["updates"] == 4000 and S["opt"]["peak_alloc_gib_max_rank"] == 61.5
+    assert abs(S["opt"]["s_per_update_excl_saves"] - 0.08) < 1e-3
+    assert verdict.main([V]) == 0
+    text = open(os.path.join(V, "verdict.md")).read()
+    v = json.loads(text[text.index("{"):])
+    assert v["mix"]["checkpoints"] == 2 and v["mix"]["final_within"] is True
+    _fake_arm(os.path.join(V, "opt"), 0.05)                    # far off: no longer within the seed yardstick
+    analyze.main([V])
+    verdict.main([V])
+    text = open(os.path.join(V, "verdict.md")).read()
+    assert json.loads(text[text.index("{"):])["mix"]["final_within"] is False
+
+
+def test_perf_views(tmp_path):
+    from faster_yoco_b200.utils import perf_views as P
+    json.dump([{"label": "a", "ms_per_update": 100.0}, {"label": "b", "ms_per_update": 50.0, "n_gpus": 8}],
+              open(tmp_path / "history.json", "w"))
+    json.dump({"phases": [["gemm", 30], ["adam", 10]]}, open(tmp_path / "time-budget.json", "w"))
+    json.dump({"arms": {"opt": {"updates": [1, 2, 3], "loss": [3, 2, 1]}}}, open(tmp_path / "validation.json", "w"))
+    out = P.render(str(tmp_path), str(tmp_path / "svg"))
+    assert len(out) == 3
+    for p in out:
+        s = open(p).read()
+        assert s.startswith("<svg") and s.rstrip().endswith("</svg>")
+    assert "75.0%" in open(out[1]).read()
+
+
+def test_presets_and_parse():
+    from faster_yoco_b200.cli.options import load_preset, parse_with_preset, train_parser
+    assert load_preset("b200_fused")["comm"] == "fused"
+    a = parse_with_preset(train_parser(), ["--preset", "torch_baseline", "DATA"])
+    assert a.kernels == "torch" and a.comm == "nccl" and a.cuda_graph is False and a.partition == "greedy"
+    a = parse_with_preset(train_parser(), ["--preset", "torch_baseline", "--comm", "fused", "DATA"])
+    assert a.comm == "fused"
+    a = parse_with_preset(train_parser(), ["DATA", "--adam-betas", "(0.9, 0.98)", "--lr", "3e-4"])
+    assert a.adam_betas == (0.9, 0.98) and a.lr == [3e-4]
