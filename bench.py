@@ -43,6 +43,8 @@ def parse():
     p.add_argument("--overlap", type=int, default=0,
                    help="fused comm: bucketed push/reduce overlapped with forward/backward (SM-driven; co-running "
                         "transfers slow the GEMMs on this hardware, so off by default)")
+    p.add_argument("--transport", default="sm", choices=["sm", "ce"],
+                   help="overlapped exchange: pushes by kernels (sm) or by the copy engines (ce)")
     p.add_argument("--sliding-window", type=int, default=None)
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-e2e", action="store_true")
@@ -152,7 +154,7 @@ def main():
     model = model.to(torch.bfloat16)
     optim = OptimConfig()
     trainer = Trainer(model, optim, device=dev, comm=args.comm, graph_step=bool(args.graph),
-                      overlap=bool(args.overlap))
+                      overlap=bool(args.overlap), transport=args.transport)
     data = SyntheticLM(margs.vocab_size, args.seq_len, args.batch, seed=1, rank=rank, pin=True)
     batches = [next(data) for _ in range(4)]
 
@@ -222,7 +224,7 @@ def main():
                        "global_batch": args.batch * world, "seq_len": args.seq_len,
                        "tokens_per_update": tokens_per_update, "parallelism": f"dp{world}-zero1",
                        "kernels": args.kernels, "comm": args.comm, "cuda_graph": bool(args.graph),
-                       "comm_overlap": bool(args.overlap),
+                       "comm_overlap": bool(args.overlap), "transport": args.transport if args.overlap else None,
                        "l2": "working set (>=55 GB of params/grads/Adam state per update) >> 126 MB L2"},
             "clocks": clocks, "e2e": e2e, "gpu_launches": launches,
         }

@@ -18,8 +18,9 @@
 //   warps 2..9 two threads per query row (TMEM lane quadrant = warp % 4, column half = (warp - 2) / 4): read S
 //              (tcgen05.ld), mask, exponentiate, write P (bf16, swizzled K-major) for the PV MMA
 //
-// Backward CTA = one (batch, kv head, 128-key tile), looping over the query heads of the GQA group and the query
-// tiles that see this key tile:  S^T = K Q^T, dP^T = V dO^T (TMEM); P^T, dS^T (bf16, shared memory);
+// Backward CTA = one (batch, kv head, 128-key tile) looping over the query tiles that see this key tile, for ONE
+// query head of the GQA group (fp32 dK / dV accumulators shared by the group's CTAs, finished by a post pass) or,
+// without GQA, for the head itself (dK / dV leave straight from TMEM):  S^T = K Q^T, dP^T = V dO^T (TMEM); P^T, dS^T (bf16, shared memory);
 // dV += P^T dO, dK += dS^T Q (TMEM accumulators), dQ_tile = dS K (TMEM -> fp32 atomics into a dQ accumulator).
 // The UMMA descriptors read the same swizzled dS^T tile as K-major (for dK) and as MN-major (for dQ). The per-query
 // values (lse and delta, or the gates) of each query tile are staged in shared memory by the producer warp.
@@ -154,8 +155,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = (p.Lq + kT - 1) / kT;
-  const int qt = nq - 1 - (blockIdx.x % nq);     // heavy (late) query tiles first
-  const int bh = blockIdx.x / nq;
+  // longest-first over the whole grid: every (batch, head) gets its last (heaviest causal) query tile before any
+  // CTA starts a lighter tile, so the block scheduler packs the tail with short tiles
+  const int units = p.B * p.Hq;
+  const int qt = nq - 1 - static_cast<int>(blockIdx.x / units);
+  const int bh = static_cast<int>(blockIdx.x % units);
   const int h = bh % p.Hq, b = bh / p.Hq;
   const int hk = h / (p.Hq / p.Hk);
   const int q0 = qt * kT;
@@ -437,6 +441,9 @@ struct AttnBwdParams {
   const float* delta;    // softmax: [B, Hq, Lq] rowsum(dO * O)
   const float* gcum;     // retention: [B, H, L]
   float* dq_acc;         // [B, Lq, Hq, D] fp32
+  float* dk_acc;         // split mode: [B, Lk, Hk, D] fp32 accumulators (one CTA per query head adds into them)
+  float* dv_acc;
+  int split;             // 1: one CTA per (key tile, query head); 0: a CTA loops over the GQA group's heads
   __nv_bfloat16* dK;     // [B, Lk, Hk, D] view: token stride dk_ld, head stride D
   __nv_bfloat16* dV;     // [B, Lk, Hk, D] view: token stride dv_ld
   int64_t dk_ld, dv_ld;
@@ -479,17 +486,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = (p.Lk + kT - 1) / kT;
   const int nq = (p.Lq + kT - 1) / kT;
-  const int kt = nk - 1 - (blockIdx.x % nk);
-  const int bh = blockIdx.x / nk;
-  const int hk = bh % p.Hk, b = bh / p.Hk;
   const int G = p.Hq / p.Hk;
+  const int S = p.split ? G : 1;                     // CTAs per (batch, kv head, key tile)
+  const int units = p.B * p.Hk * S;
+  // longest-first over the whole grid: under a causal mask the early key tiles see the most query tiles
+  const int kt = static_cast<int>(blockIdx.x / units);
+  const int unit = static_cast<int>(blockIdx.x % units);
+  const int bh = unit / S;
+  const int hk = bh % p.Hk, b = bh / p.Hk;
+  const int h_first = hk * G + (p.split ? unit % S : 0);
+  const int n_heads = p.split ? 1 : G;
   const int k0 = kt * kT;
   const int k_hi = min(k0 + kT, p.Lk) - 1;
   int i_lo = 0, i_hi = nq;
   if (p.causal) i_lo = max(0, k0 - p.q_offset) / kT;
   if (p.window > 0) i_hi = min(nq, max(0, k_hi + p.window - 1 - p.q_offset) / kT + 1);
   const int per_h = max(0, i_hi - i_lo);
-  const int n_it = G * per_h;
+  const int n_it = n_heads * per_h;
   constexpr uint32_t ID_KK = idesc_bf16(128, 128, false, false);
   constexpr uint32_t ID_KM = idesc_bf16(128, 128, false, true);
   constexpr uint32_t ID_MM = idesc_bf16(128, 128, true, true);
@@ -525,7 +538,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       int it = 0;
       for (; it < n_it; ++it) {
-        const int h = hk * G + it / per_h;
+        const int h = h_first + it / per_h;
         const int q0 = (i_lo + it % per_h) * kT;
         const int64_t hq_base = (static_cast<int64_t>(b) * p.Hq + h) * p.Lq;
         int ok = 1;
@@ -608,7 +621,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     bool ok = true;
     for (int it = 0; ok && it < n_it; ++it) {
       const uint32_t ph = it & 1;
-      const int h = hk * G + it / per_h;
+      const int h = h_first + it / per_h;
       const int q0 = (i_lo + it % per_h) * kT;
       const bool full_tile = (q0 + kT <= p.Lq) && (kpos < p.Lk) && (!p.causal || q0 + p.q_offset >= k0 + kT - 1) &&
                              (p.window <= 0 || q0 + kT - 1 + p.q_offset < k0 + p.window);
@@ -708,6 +721,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const bool have = ok && n_it > 0 && mbar_wait(fin, 0, abort_flag, p.status, 52);
     if (have) tc_fence_after();
     const int64_t tok = static_cast<int64_t>(b) * p.Lk + min(kpos, p.Lk - 1);
+    if (p.dk_acc != nullptr) {
+      // split mode: add this query head's share into the fp32 accumulators (rotation applied by the post pass).
+      // tcgen05.ld is warp-collective (.sync.aligned): it runs under the warp-uniform `have` only, and the
+      // lane-dependent key bound guards the atomics
+      if (have) {
+#pragma unroll 1
+        for (int which = 0; which < 2; ++which) {
+          float* acc = (which == 0 ? p.dk_acc : p.dv_acc) + (tok * p.Hk + hk) * kD + c0;
+          const uint32_t col = which == 0 ? 384u : 256u;
+#pragma unroll
+          for (int c = 0; c < 64; c += 32) {
+            uint32_t v[32];
+            tmem_ld32(tmem + col + trow + c0 + c, v);
+            tmem_ld_wait();
+            if (kpos < p.Lk) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                atomicAdd(reinterpret_cast<float4*>(acc + c + j),
+                          make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                                      __uint_as_float(v[j + 3])));
+            }
+          }
+        }
+      }
+    } else {
 #pragma unroll 1
     for (int which = 0; which < 2; ++which) {
       __nv_bfloat16* dst = which == 0 ? p.dK + tok * p.dk_ld + hk * kD + c0 : p.dV + tok * p.dv_ld + hk * kD + c0;
@@ -744,6 +782,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                            pack_bf16(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7])));
         }
       }
+    }
     }
   }
 
@@ -911,8 +950,19 @@ std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& 
       reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()),
       delta.data_ptr<float>(), B, Lq, Hq, nullptr);
   check_launch("attn_bwd_delta");
+  // GQA: one CTA per (key tile, query head) with fp32 dK / dV accumulators, so the grid is G times larger and the
+  // longest CTA walks one head's query tiles instead of the whole group's
+  const int G = Hq / Hk;
+  const bool split = G > 1;
+  at::Tensor dk_acc, dv_acc;
+  if (split) {
+    dk_acc = at::zeros({B, Lk, Hk, kD}, q.options().dtype(at::kFloat));
+    dv_acc = at::zeros({B, Lk, Hk, kD}, q.options().dtype(at::kFloat));
+  }
   AttnBwdParams p{B, Lq, Lk, Hq, Hk, Lk - Lq, (int)window, causal ? 1 : 0, (float)scale, lse.data_ptr<float>(),
                   delta.data_ptr<float>(), nullptr, dq_acc.data_ptr<float>(),
+                  split ? dk_acc.data_ptr<float>() : nullptr, split ? dv_acc.data_ptr<float>() : nullptr,
+                  split ? 1 : 0,
                   reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()),
                   dk.stride(1), dv.stride(1), rope_k ? rc : nullptr, rope_k ? rs : nullptr, status_ptr()};
   const CUtensorMap tq = tmap_heads(q), tk = tmap_heads(k), tv = tmap_heads(v), tdo = tmap_heads(dout);
@@ -921,9 +971,20 @@ std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& 
     set_smem(attn_bwd_kernel<kSoftmax>, kBwdSmem);
     init = true;
   }
-  const int grid = B * Hk * ((Lk + kT - 1) / kT);
+  const int grid = B * Hk * (split ? G : 1) * ((Lk + kT - 1) / kT);
   attn_bwd_kernel<kSoftmax><<<grid, kAttnThreads, kBwdSmem, cur_stream()>>>(tq, tk, tv, tdo, p);
   check_launch("attn_bwd");
+  if (split) {
+    const int64_t nk4 = static_cast<int64_t>(B) * Lk * Hk * (kD / 4);
+    dq_out_kernel<<<static_cast<int>((nk4 + 255) / 256), 256, 0, cur_stream()>>>(
+        dk_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()), dk.stride(1), B, Lk, Hk,
+        rope_k ? rc : nullptr, rope_k ? rs : nullptr);
+    check_launch("attn_bwd_dk");
+    dq_out_kernel<<<static_cast<int>((nk4 + 255) / 256), 256, 0, cur_stream()>>>(
+        dv_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()), dv.stride(1), B, Lk, Hk,
+        nullptr, nullptr);
+    check_launch("attn_bwd_dv");
+  }
   const int64_t nq4 = static_cast<int64_t>(B) * Lq * Hq * (kD / 4);
   dq_out_kernel<<<static_cast<int>((nq4 + 255) / 256), 256, 0, cur_stream()>>>(
       dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), dq.stride(1), B, Lq, Hq,
@@ -992,7 +1053,7 @@ std::vector<at::Tensor> retention_bwd(const at::Tensor& dout, const at::Tensor& 
       dgo.data_ptr<float>(), B, L, H, nullptr);
   check_launch("retention_bwd_dot");
   AttnBwdParams p{B, L, L, H, H, 0, 0, 1, (float)(1.0 / std::sqrt((double)kD)), nullptr, nullptr,
-                  gcum.data_ptr<float>(), dq_acc.data_ptr<float>(),
+                  gcum.data_ptr<float>(), dq_acc.data_ptr<float>(), nullptr, nullptr, 0,
                   reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()),
                   dk.stride(1), dv.stride(1), rc, rs, status_ptr()};
   const CUtensorMap tq = tmap_heads(q), tk = tmap_heads(k), tv = tmap_heads(v), tdo = tmap_heads(dout);

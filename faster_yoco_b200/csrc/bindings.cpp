@@ -62,6 +62,8 @@ void sum_partials(const at::Tensor& part, at::Tensor& out);
 void push_bucket(const at::Tensor& src, const std::vector<int64_t>& peer_dst, const std::vector<int64_t>& peer_arrive,
                  const at::Tensor& ranges, int64_t bucket, int64_t rank, int64_t ctas);
 void wait_arrivals(const at::Tensor& arrive, at::Tensor& expected, int64_t bucket, int64_t increment);
+void peer_copy(int64_t dst, int64_t src, int64_t nbytes);
+void signal_peer(int64_t counter_base, int64_t index);
 void push_grads(const at::Tensor& grad, const std::vector<int64_t>& peer_staging,
                 const std::vector<int64_t>& peer_arrive, const at::Tensor& pieces, int64_t bucket, int64_t rank,
                 int64_t seg, int64_t ctas);
@@ -144,6 +146,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("push_range", &fyb::push_range);
   m.def("push_bucket", &fyb::push_bucket);
   m.def("wait_arrivals", &fyb::wait_arrivals);
+  m.def("peer_copy", &fyb::peer_copy, "cudaMemcpyAsync of nbytes between (peer) device addresses on the current stream");
+  m.def("signal_peer", &fyb::signal_peer, "release-add 1 to counter_base[index] (a peer's counter) on the current stream");
   m.def("push_grads", &fyb::push_grads);
   m.def("reduce_staged", &fyb::reduce_staged);
   m.def("mailbox_put", &fyb::mailbox_put);

@@ -389,6 +389,17 @@ __global__ void wait_arrivals_kernel(const uint32_t* __restrict__ arrive, uint32
   __threadfence_system();
 }
 
+// Copy-engine transport: after the stream's peer copies (cudaMemcpyAsync, executed by the copy engines, so no SM
+// time is taken from the compute stream), one thread publishes their completion by adding 1 to a counter in the
+// destination GPU's memory. Stream order makes the copies complete before this kernel starts; the release add
+// orders them before the counter update for a reader that acquires the counter.
+__global__ void signal_peer_kernel(uint32_t* counter) {
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(counter), "r"(1u) : "memory");
+  }
+}
+
 // each rank writes its k values into slot [rank] of every peer's mailbox, then (after a flag barrier) sums the
 // world slots of its own mailbox in rank order
 __global__ void mailbox_put_kernel(PeerPtrs boxes, const float* __restrict__ vals, int k, int rank, int world,
@@ -563,6 +574,18 @@ void reduce_staged(at::Tensor& grad, const at::Tensor& staging, const at::Tensor
       ranges.data_ptr<int64_t>(), static_cast<int>(ranges.size(0)), static_cast<int>(world), static_cast<int>(rank),
       seg, 1.0f / static_cast<float>(world), part.data_ptr<float>());
   check_launch("reduce_staged");
+}
+
+void peer_copy(int64_t dst, int64_t src, int64_t nbytes) {
+  // one copy-engine transfer per call (the batched copy entry points are not used)
+  if (nbytes <= 0) return;
+  FYB_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src),
+                           static_cast<size_t>(nbytes), cudaMemcpyDeviceToDevice, cur_stream()));
+}
+
+void signal_peer(int64_t counter_base, int64_t index) {
+  signal_peer_kernel<<<1, 32, 0, cur_stream()>>>(reinterpret_cast<uint32_t*>(counter_base) + index);
+  check_launch("signal_peer");
 }
 
 void wait_arrivals(const at::Tensor& arrive, at::Tensor& expected, int64_t bucket, int64_t increment) {

@@ -152,6 +152,109 @@ __global__ void rms_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_
   }
 }
 
+// Register-resident RMSNorm backward for N <= 8192: one thread per 8 columns (blockDim = N/8 rounded up to a warp),
+// so each row's dy / x values are read once and kept in registers between the row-dot reduction and the dx store,
+// and the thread's 8 weight-gradient partials stay in registers over all rows of the CTA. The next row is loaded
+// before the current row's reduction so its global loads overlap the barrier.
+__global__ void rms_bwd_reg_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                   const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
+                                   __nv_bfloat16* __restrict__ dx, float* __restrict__ part, int M, int N,
+                                   int rows_per_cta, const __nv_bfloat16* __restrict__ dres) {
+  __shared__ float red[32];
+  const int c = threadIdx.x * 8;
+  const bool act = c < N;
+  const int row0 = blockIdx.x * rows_per_cta;
+  const int row1 = min(M, row0 + rows_per_cta);
+  float wf[8], dw[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    wf[i] = 1.f;
+    dw[i] = 0.f;
+  }
+  if (act && w != nullptr) load8(w + c, wf);
+  uint4 gu = make_uint4(0, 0, 0, 0), xu = make_uint4(0, 0, 0, 0);
+  if (act && row0 < row1) {
+    gu = *reinterpret_cast<const uint4*>(dy + static_cast<int64_t>(row0) * N + c);
+    xu = *reinterpret_cast<const uint4*>(x + static_cast<int64_t>(row0) * N + c);
+  }
+  for (int row = row0; row < row1; ++row) {
+    const int64_t off = static_cast<int64_t>(row) * N;
+    float g[8], f[8];
+    {
+      const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w}, xw[4] = {xu.x, xu.y, xu.z, xu.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = unpack_bf16(gw[i]), b = unpack_bf16(xw[i]);
+        g[2 * i] = a.x;
+        g[2 * i + 1] = a.y;
+        f[2 * i] = b.x;
+        f[2 * i + 1] = b.y;
+      }
+    }
+    if (act && row + 1 < row1) {             // prefetch the next row
+      gu = *reinterpret_cast<const uint4*>(dy + off + N + c);
+      xu = *reinterpret_cast<const uint4*>(x + off + N + c);
+    }
+    const float r = rstd[row];
+    float dot = 0.f;
+    if (act) {
+      if (w != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float n = f[i] * r;
+          dot += bf16_round(g[i] * wf[i]) * n;
+          dw[i] += g[i] * bf16_round(n);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dot += g[i] * f[i] * r;
+      }
+    }
+    dot = block_sum(dot, red) / static_cast<float>(N);
+    if (act) {
+      float o[8];
+      if (w != nullptr) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = r * (bf16_round(g[i] * wf[i]) - f[i] * r * dot);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = r * (g[i] - f[i] * r * dot);
+      }
+      if (dres != nullptr) {
+        float rr[8];
+        load8(dres + off + c, rr);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = bf16_round(o[i]) + rr[i];
+      }
+      store8(dx + off + c, o);
+    }
+  }
+  if (w != nullptr && act) {
+    float* pp = part + static_cast<int64_t>(blockIdx.x) * N + c;
+    *reinterpret_cast<float4*>(pp) = make_float4(dw[0], dw[1], dw[2], dw[3]);
+    *reinterpret_cast<float4*>(pp + 4) = make_float4(dw[4], dw[5], dw[6], dw[7]);
+  }
+}
+
+// dw[c] = bf16(sum_p part[p, c]): 32 columns x 8 row groups per CTA, each group sums rows p = g (mod 8) in order,
+// then the 8 group sums are added in group order (a fixed order, independent of timing)
+__global__ void col_sum8_kernel(const float* __restrict__ part, __nv_bfloat16* __restrict__ dw, int P, int N) {
+  __shared__ float acc[8][33];
+  const int col = blockIdx.x * 32 + (threadIdx.x & 31);
+  const int grp = threadIdx.x >> 5;
+  float s = 0.f;
+  if (col < N)
+    for (int p = grp; p < P; p += 8) s += part[static_cast<int64_t>(p) * N + col];
+  acc[grp][threadIdx.x & 31] = s;
+  __syncthreads();
+  if (grp == 0 && col < N) {
+    float t = 0.f;
+#pragma unroll
+    for (int g2 = 0; g2 < 8; ++g2) t += acc[g2][threadIdx.x];
+    dw[col] = __float2bfloat16_rn(t);
+  }
+}
+
 // dw[c] = bf16(sum_p part[p, c]) in a fixed order
 __global__ void col_sum_kernel(const float* __restrict__ part, __nv_bfloat16* __restrict__ dw, int P, int N) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
@@ -280,6 +383,21 @@ std::vector<at::Tensor> rms_norm_bwd_impl(const at::Tensor& dy, const at::Tensor
   }
   const int rows_per = static_cast<int>((M + P - 1) / P);
   const int grid = static_cast<int>((M + rows_per - 1) / rows_per);
+  if (N <= 8192) {
+    const int threads = static_cast<int>((N / 8 + 31) / 32 * 32);
+    rms_bwd_reg_kernel<<<grid, threads, 0, cur_stream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+        has_w ? reinterpret_cast<const __nv_bfloat16*>(w->data_ptr()) : nullptr, rstd.data_ptr<float>(),
+        reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), part, static_cast<int>(M), static_cast<int>(N), rows_per,
+        dres);
+    check_launch("rms_bwd_reg");
+    if (has_w) {
+      col_sum8_kernel<<<static_cast<int>((N + 31) / 32), 256, 0, cur_stream()>>>(
+          part, reinterpret_cast<__nv_bfloat16*>(dw.data_ptr()), grid, static_cast<int>(N));
+      check_launch("rms_bwd_colsum8");
+    }
+    return {dx, has_w ? dw : at::Tensor()};
+  }
   const size_t shm = has_w ? N * sizeof(float) : 0;
   auto kern = rms_bwd_kernel;
   if (shm > 48 * 1024) FYB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm));

@@ -141,7 +141,7 @@ class _NativeRMSNorm(torch.autograd.Function):
 
 
 def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float) -> torch.Tensor:
-    if native_on(x):
+    if native_on(x) and x.dtype == torch.bfloat16 and x.shape[-1] % 8 == 0:
         return _NativeRMSNorm.apply(x, weight, eps)
     return ref.rms_norm(x, weight, eps)
 
@@ -164,9 +164,16 @@ class _NativeSwiGLU(torch.autograd.Function):
         return dx, dy
 
 
+def _rows16(t: torch.Tensor) -> bool:
+    """bf16 rows of a multiple of 8 elements on 16-byte boundaries (the vector width of the elementwise kernels)."""
+    return (t.dtype == torch.bfloat16 and t.shape[-1] % 8 == 0 and t.stride(-1) == 1
+            and all(st % 8 == 0 for st in t.stride()[:-1]) and t.data_ptr() % 16 == 0)
+
+
 def swiglu(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
-    """x * y * sigmoid(x) (silu on the FIRST argument, as the reference's kernel/swiglu.py)."""
-    if native_on(x):
+    """x * y * sigmoid(x) (silu on the FIRST argument, as the reference's kernel/swiglu.py). Rows that are not
+    16-byte vectors (e.g. LLaMA's int(8 d / 3) width) take the PyTorch expression."""
+    if native_on(x) and _rows16(x) and _rows16(y):
         shp = x.shape
         return _NativeSwiGLU.apply(x.reshape(-1, shp[-1]), y.reshape(-1, shp[-1])).view(shp)
     return ref.swiglu(x, y)
@@ -310,7 +317,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
     scale = q.shape[-1] ** -0.5
     if native_on(q) and q.shape[-1] == 128:
         return _NativeAttention.apply(q, k, v, causal, window, scale)
-    if q.is_cuda and _flash():
+    if q.is_cuda and q.dtype in (torch.float16, torch.bfloat16) and _flash():
         ws = (window - 1, 0) if window is not None else (-1, -1)
         return _flash()(q, k, v, causal=causal, window_size=ws)
     return ref.attention(q, k, v, causal=causal, window=window, q_offset=k.shape[1] - q.shape[1])

@@ -124,11 +124,19 @@ class PeerComm:
         return out
 
     # ------------------------------------------------------------------------------------ overlapped (bucketed)
-    def setup_buckets(self, flat, groups, reduce_ctas: Optional[int] = None, gather_ctas: Optional[int] = None):
+    def setup_buckets(self, flat, groups, reduce_ctas: Optional[int] = None, gather_ctas: Optional[int] = None,
+                      transport: str = "sm"):
         """groups: parameter lists in FORWARD order (bucket b = groups[b]). Precomputes, per bucket, the ranges this
-        rank owns (reduced during backward) and the ranges it must pull from other owners (before forward)."""
+        rank owns (reduced during backward) and the ranges it must pull from other owners (before forward).
+
+        transport "sm": the pushes are kernels (remote stores from CTAs); "ce": the pushes are cudaMemcpyAsync
+        transfers on one stream per peer (the copy engines move the data, so no SM time is taken from the GEMMs of
+        the overlapped forward / backward), each followed by a one-thread kernel that publishes the arrival."""
         if len(groups) > self.NSLOTS - 3:
             raise ValueError("too many buckets")
+        if transport not in ("sm", "ce"):
+            raise ValueError(transport)
+        self.transport = transport
         import os
         reduce_ctas = int(os.environ.get("FYB_REDUCE_CTAS", reduce_ctas or 128))
         gather_ctas = int(os.environ.get("FYB_PUSH_CTAS", gather_ctas or 128))
@@ -159,15 +167,76 @@ class PeerComm:
         self.gather_ev = [torch.cuda.Event() for _ in range(self.nb)]
         self.start_ev = torch.cuda.Event()
         self._reduced = [False] * self.nb
+        if transport == "ce":
+            # host-side piece lists (byte offsets) and one copy stream per peer
+            esz = flat.flat.element_size()
+            self.ce_owned = [[(int(o) * esz, int(c) * esz) for o, c in t.tolist()] for t in owned]
+            self.ce_other = [[(int(o) * esz, int(c) * esz, int(q)) for o, c, q in t.tolist()] for t in other]
+            self.peer_streams = {q: torch.cuda.Stream(device=self.dev) for q in range(self.world) if q != self.rank}
+            self.ce_done = torch.cuda.Event()
 
     def _slot_barrier(self, slot: int):
         self.C.flag_barrier(self.peer_flags, self.flags, self.counters, self.rank, slot)
+
+    def _ce_start_gather(self):
+        cur = torch.cuda.current_stream(self.dev)
+        self.start_ev.record(cur)
+        src = self.flat.flat.data_ptr()
+        for q, st in self.peer_streams.items():
+            dst = self.peers["param"][q]
+            with torch.cuda.stream(st):
+                st.wait_event(self.start_ev)
+                for b in range(self.nb):
+                    for o, c in self.ce_owned[b]:
+                        self.C.peer_copy(dst + o, src + o, c)
+                    self.C.signal_peer(self.peer_arrive[q], b)
+        self._reduced = [False] * self.nb
+
+    def _ce_bucket_ready(self, b: int):
+        cur = torch.cuda.current_stream(self.dev)
+        self.ready_ev[b].record(cur)
+        grad = self.flat.grad_flat.data_ptr()
+        esz = self.flat.grad_flat.element_size()
+        seg_b = self.flat.seg * esz
+        for q, st in self.peer_streams.items():
+            dst = self.peers["staging"][q] + self.rank * seg_b - q * seg_b
+            with torch.cuda.stream(st):
+                st.wait_event(self.ready_ev[b])
+                for o, c, owner in self.ce_other[b]:
+                    if owner == q:
+                        self.C.peer_copy(dst + o, grad + o, c)
+                self.C.signal_peer(self.peer_garrive[q], b)
+
+    def _ce_finish_reduce(self) -> torch.Tensor:
+        cur = torch.cuda.current_stream(self.dev)
+        for st in self.peer_streams.values():
+            cur.wait_stream(st)                    # my pushes are done (staging of peers, gradient buffer reusable)
+        for b in range(self.nb):
+            self.C.wait_arrivals(self.garrive, self.gexpected, b, self.world - 1)
+        owned_all = self._owned_all()
+        part = self.bucket_part.view(-1)[: self.red_ctas_all]
+        self.C.reduce_staged(self.flat.grad_flat, self.staging, owned_all, self.world, self.rank, self.flat.seg,
+                             part, self.red_ctas_all)
+        self.C.sum_partials(part, self.sq)
+        return self.sq
+
+    def _owned_all(self) -> torch.Tensor:
+        if getattr(self, "_owned_all_t", None) is None:
+            owned, _ = self.buckets
+            rows = torch.cat([t for t in owned if t.numel()], 0) if any(t.numel() for t in owned) else \
+                torch.zeros(0, 2, dtype=torch.int64, device=self.dev)
+            self._owned_all_t = rows.contiguous()
+            sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
+            self.red_ctas_all = min(2 * sms, self.bucket_part.numel())
+        return self._owned_all_t
 
     def start_gather(self):
         """Start of an update: this rank pushes the parameters it owns (updated by its previous Adam step), bucket
         by bucket in forward order, into every peer's flat buffer on the communication stream; forward waits per
         bucket for the peers' pushes (wait_gather). Safe: a peer's previous reads of bucket b ended with its
         backward of b, which every owner's reduction of b (hence Adam) waited for."""
+        if self.transport == "ce":
+            return self._ce_start_gather()
         cur = torch.cuda.current_stream(self.dev)
         self.start_ev.record(cur)
         owned, _ = self.buckets
@@ -179,13 +248,16 @@ class PeerComm:
         self._reduced = [False] * self.nb
 
     def wait_gather(self, b: int):
-        self.C.wait_arrivals(self.arrive, self.expected, b, (self.world - 1) * self.push_ctas)
+        inc = (self.world - 1) * (1 if self.transport == "ce" else self.push_ctas)
+        self.C.wait_arrivals(self.arrive, self.expected, b, inc)
 
     def bucket_ready(self, b: int):
         """Bucket b's gradients are final on this rank (called from a gradient hook on the compute stream)."""
         if self._reduced[b]:
             return
         self._reduced[b] = True
+        if self.transport == "ce":
+            return self._ce_bucket_ready(b)
         owned, other = self.buckets
         self.ready_ev[b].record(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(self.stream):
@@ -203,12 +275,17 @@ class PeerComm:
         for b in range(self.nb):
             if not self._reduced[b]:
                 self.bucket_ready(b)
+        if self.transport == "ce":
+            return self._ce_finish_reduce()
         torch.cuda.current_stream(self.dev).wait_stream(self.stream)
         self.C.sum_partials(self.bucket_part.view(-1), self.sq)
         return self.sq
 
     def finish_reduce_reset(self):
-        torch.cuda.current_stream(self.dev).wait_stream(self.stream)
+        cur = torch.cuda.current_stream(self.dev)
+        cur.wait_stream(self.stream)
+        for st in getattr(self, "peer_streams", {}).values():
+            cur.wait_stream(st)
         self._reduced = [True] * self.nb
 
     def close(self):

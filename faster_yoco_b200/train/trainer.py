@@ -45,7 +45,7 @@ class _CommHooks:
 class Trainer:
     def __init__(self, model: torch.nn.Module, optim_cfg, *, device, comm: str = "nccl", zero_stage: int = 1,
                  pad_idx: int = 1, graph_step: bool = False, group=None, check_consistency: bool = True,
-                 overlap: bool = False, partition: str = "even", criterion=None):
+                 overlap: bool = False, partition: str = "even", criterion=None, transport: str = "sm"):
         self.model = model
         self.device = torch.device(device)
         self.cfg = optim_cfg
@@ -64,7 +64,7 @@ class Trainer:
         self.zero.p2p = p2p
         self.overlap = p2p is not None and overlap and hasattr(model, "param_buckets")
         if self.overlap:
-            p2p.setup_buckets(self.flat, model.param_buckets())
+            p2p.setup_buckets(self.flat, model.param_buckets(), transport=transport)
         self.sched = PolynomialDecaySchedule(optim_cfg.lr, optim_cfg.warmup_updates, optim_cfg.total_num_update,
                                              optim_cfg.end_learning_rate, optim_cfg.power)
         self.pending = PendingChecks(self.device.type == "cuda")

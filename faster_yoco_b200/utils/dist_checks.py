@@ -7,7 +7,8 @@ import torch
 import torch.distributed as dist
 
 
-def _tiny_trainer(device, comm="nccl", seed=0, graph=False, arch="yoco_tiny", dtype=torch.float32, overlap=True):
+def _tiny_trainer(device, comm="nccl", seed=0, graph=False, arch="yoco_tiny", dtype=torch.float32, overlap=True,
+                  transport="sm"):
     from ..config import OptimConfig, build_args
     from ..models.yoco import YOCO
     from ..train.trainer import Trainer
@@ -15,7 +16,8 @@ def _tiny_trainer(device, comm="nccl", seed=0, graph=False, arch="yoco_tiny", dt
     args = build_args(arch, max_seq_len=256, init_std=0.02)
     model = YOCO(args).to(device=device, dtype=dtype)
     cfg = OptimConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, warmup_updates=0, total_num_update=20)
-    return model, Trainer(model, cfg, device=device, comm=comm, graph_step=graph, overlap=overlap)
+    return model, Trainer(model, cfg, device=device, comm=comm, graph_step=graph, overlap=overlap,
+                          transport=transport)
 
 
 def _batches(rank, world, n, seed=1, batch=2, seq=256, vocab=1024):
@@ -91,8 +93,12 @@ def fused_vs_nccl_gpu(rank, world, outdir, steps):
     ops.set_backend("native")
     dev = torch.device("cuda", rank)
     res = {}
-    for name, comm, overlap in (("nccl", "nccl", False), ("fused", "fused", True), ("fused_serial", "fused", False)):
-        model, tr = _tiny_trainer(dev, comm=comm, arch="yoco_small", dtype=torch.bfloat16, overlap=overlap)
+    for name, comm, overlap, transport, graph in (
+            ("nccl", "nccl", False, "sm", False), ("fused", "fused", True, "sm", False),
+            ("fused_serial", "fused", False, "sm", False), ("fused_ce", "fused", True, "ce", False),
+            ("fused_ce_graph", "fused", True, "ce", True)):
+        model, tr = _tiny_trainer(dev, comm=comm, arch="yoco_small", dtype=torch.bfloat16, overlap=overlap,
+                                  transport=transport, graph=graph)
         losses = []
         for ids in _batches(rank, world, steps, seq=256, vocab=8192):
             mine = ids[rank]
@@ -100,6 +106,7 @@ def fused_vs_nccl_gpu(rank, world, outdir, steps):
                  "ntokens": mine.shape[0] * mine.shape[1], "nsentences": mine.shape[0]}
             losses.append(float(tr.train_step(b).item()))
         tr.sync_params()
+        tr.release_graph()
         torch.cuda.synchronize()
         status = int(ops._C().status()[0].item())
         res[name] = {"losses": losses, "params": tr.flat.flat.float().cpu(), "status": status}

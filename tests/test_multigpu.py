@@ -1,5 +1,6 @@
 """2-GPU data parallelism: the NVLink peer-memory collectives (fused reduce-to-owner, all-gather, mailbox
-all-reduce) against the NCCL path on the same training run."""
+all-reduce; serial, overlapped with kernel pushes, overlapped with copy-engine pushes, and the latter inside the
+whole-update CUDA graph) against the NCCL path on the same training run."""
 import os
 
 import pytest
@@ -14,12 +15,13 @@ pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 def test_fused_p2p_matches_nccl(tmp_path):
     run_ranks(dist_checks.fused_vs_nccl_gpu, 2, str(tmp_path), 4, backend="nccl", timeout_s=300)
     r = torch.load(os.path.join(tmp_path, "fused_vs_nccl.pt"))
-    for name in ("fused", "fused_serial"):
+    for name in ("fused", "fused_serial", "fused_ce", "fused_ce_graph"):
         assert r[name]["status"] == 0 and r["nccl"]["status"] == 0
         for a, b in zip(r[name]["losses"], r["nccl"]["losses"]):
             assert abs(a - b) / abs(b) < 2e-3, (name, r[name]["losses"], r["nccl"]["losses"])
         pf, pn = r[name]["params"], r["nccl"]["params"]
         assert ((pf - pn).abs().max() / pn.abs().max()).item() < 2e-2, name
     # the overlapped and the serial peer-memory paths do the same arithmetic in the same order
-    assert r["fused"]["losses"] == r["fused_serial"]["losses"]
-    assert torch.equal(r["fused"]["params"], r["fused_serial"]["params"])
+    for name in ("fused", "fused_ce", "fused_ce_graph"):
+        assert r[name]["losses"] == r["fused_serial"]["losses"], name
+        assert torch.equal(r[name]["params"], r["fused_serial"]["params"]), name
