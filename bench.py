@@ -40,10 +40,12 @@ def parse():
     p.add_argument("--comm", default="fused", choices=["nccl", "fused"],
                    help="fused: NVLink peer-memory collectives overlapped with compute; nccl: the baseline path")
     p.add_argument("--graph", type=int, default=1, help="capture the whole update as one CUDA graph")
-    p.add_argument("--overlap", type=int, default=0,
-                   help="fused comm: bucketed push/reduce overlapped with forward/backward (SM-driven; co-running "
-                        "transfers slow the GEMMs on this hardware, so off by default)")
-    p.add_argument("--transport", default="sm", choices=["sm", "ce"],
+    p.add_argument("--overlap", default="auto", choices=["auto", "0", "1"],
+                   help="fused comm: bucketed pushes overlapped with forward/backward. auto = on with the copy-engine "
+                        "transport at 2 GPUs (one peer: the copy engines reach 766 GB/s and take no SM time), off "
+                        "(serial P2P reduce + push all-gather after backward) at more GPUs, where the copy engines "
+                        "deliver only ~210 GB/s in aggregate to 7 peers")
+    p.add_argument("--transport", default="auto", choices=["auto", "sm", "ce"],
                    help="overlapped exchange: pushes by kernels (sm) or by the copy engines (ce)")
     p.add_argument("--sliding-window", type=int, default=None)
     p.add_argument("--e2e-steps", type=int, default=None)
@@ -145,6 +147,12 @@ def main():
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     dev = torch.device("cuda", dev_index)
     ops.set_backend(args.kernels)
+    if args.overlap == "auto":
+        args.overlap = 1 if (world == 2 and args.comm == "fused") else 0
+    else:
+        args.overlap = int(args.overlap)
+    if args.transport == "auto":
+        args.transport = "ce" if world == 2 else "sm"
     torch.manual_seed(1234)
 
     margs = build_args(args.arch, max_seq_len=args.seq_len, max_batch_size=args.batch, init_std=0.02,

@@ -115,7 +115,11 @@ def train_parser() -> argparse.ArgumentParser:
     g.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                    help="fused: NVLink peer-memory reduce/all-gather kernels; nccl: the NCCL baseline path")
     g.add_argument("--cuda-graph", type=_bool_int, default=True, help="capture each update as one CUDA graph")
-    g.add_argument("--overlap", type=_bool_int, default=False)
+    g.add_argument("--overlap", default="auto",
+                   help="overlap the ZeRO exchange with forward/backward: auto (copy-engine pushes at 2 GPUs, "
+                        "serial exchange otherwise), 1 or 0")
+    g.add_argument("--transport", default="auto", choices=["auto", "sm", "ce"],
+                   help="overlapped pushes by kernels (sm) or by the copy engines (ce)")
     g.add_argument("--partition", default="even", choices=["even", "greedy"],
                    help="ZeRO owner map: even contiguous split, or the fairscale OSS greedy per-parameter split")
     return p

@@ -28,6 +28,10 @@ from .common import build_model, build_task, setup_runtime
 from .options import parse_with_preset, train_parser
 
 
+def _flag(v) -> bool:
+    return str(v).lower() in ("1", "true", "yes", "on")
+
+
 def _gather_iterator_states(itr):
     st = itr.state_dict() if hasattr(itr, "state_dict") else None
     if not D.is_dist():
@@ -69,8 +73,10 @@ def main(argv=None) -> int:
                         total_num_update=args.total_num_update, end_learning_rate=args.end_learning_rate,
                         power=args.power)
     comm = args.comm if (world > 1 and device.type == "cuda") else "nccl"
+    overlap = (world == 2 and comm == "fused") if str(args.overlap) == "auto" else bool(_flag(args.overlap))
+    transport = ("ce" if world == 2 else "sm") if args.transport == "auto" else args.transport
     trainer = Trainer(model, optim, device=device, comm=comm, graph_step=bool(args.cuda_graph) and device.type == "cuda",
-                      overlap=bool(args.overlap), partition=args.partition, pad_idx=task.tokenizer.pad_id)
+                      overlap=overlap, transport=transport, partition=args.partition, pad_idx=task.tokenizer.pad_id)
     itr = task.get_batch_iterator(ds, max_sentences=args.batch_size, seed=args.seed, num_shards=world,
                                   shard_id=rank)
     restore = os.path.join(args.save_dir, args.restore_file)
