@@ -243,4 +243,10 @@ class Trainer:
 
     # ------------------------------------------------------------------------------------------------------------
     def log_stats(self):
-        return self.meters.flush()
+        """Flush the device meters (the one host read per log interval) and surface any device-side error word
+        (a bounded wait that ran out inside a kernel, a failed bounds check) as an exception."""
+        stats = self.meters.flush()
+        if self.device.type == "cuda" and ops.get_backend() == "native":
+            from ..utils.faults import DeviceStatus
+            DeviceStatus.native().raise_if_set()
+        return stats

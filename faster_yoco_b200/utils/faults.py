@@ -63,8 +63,20 @@ class DeviceStatus:
     CODES = {1: "peer flag wait timed out", 2: "mbarrier wait timed out", 3: "bounds check failed",
              4: "layout check failed"}
 
-    def __init__(self, device):
-        self.word = torch.zeros(4, dtype=torch.int32, device=device)
+    def __init__(self, device=None, word: torch.Tensor = None):
+        """word: the extension's status tensor (``_C.status()``, device memory the kernels write); a private zero
+        word when the extension is not in use (CPU)."""
+        if word is None:
+            word = torch.zeros(4, dtype=torch.int32, device=device)
+        self.word = word
+
+    @classmethod
+    def native(cls):
+        from .. import ops
+        return cls(word=ops._C().status())
+
+    def value(self) -> int:
+        return int(self.word[0].item())
 
     def raise_if_set(self):
         w = self.word.cpu().tolist()
