@@ -23,7 +23,7 @@ import torch
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-BASELINE_TOKS = 138983.0          # Faster-YOCO, 8 x H100, tokens/s over all GPUs
+BASELINE_TOKS = 138983.0          # published Faster-YOCO throughput, 8 x H100, tokens/s over all GPUs
 METRIC = "ms/update & tokens/sec, YOCO-3B 2048 tok/GPU, 1/2/4/8 B200, max over ranks"
 
 

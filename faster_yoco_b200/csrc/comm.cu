@@ -371,7 +371,7 @@ __global__ void reduce_staged_kernel(__nv_bfloat16* __restrict__ grad, const __n
   }
 }
 
-// Compute-stream wait until bucket b's pushes of the current round have all arrived: expected[b] += increment, then
+// Compute-stream wait until bucket b's pushes of the current update have all arrived: expected[b] += increment, then
 // spin (bounded) until arrive[b] >= expected[b]. The expectation is device-resident, so graph replays stay correct.
 __global__ void wait_arrivals_kernel(const uint32_t* __restrict__ arrive, uint32_t* __restrict__ expected, int bucket,
                                      uint32_t increment, int* status) {

@@ -163,26 +163,27 @@ __global__ void embed_fwd_kernel(const int64_t* __restrict__ tok, const __nv_bfl
 // Deterministic embedding gradient: block j handles the FIRST occurrence of token tok[j] and sums, in position
 // order, bf16(dy[i] * scale) over every position i with the same token (fp32 accumulation). Rows of tokens that do
 // not occur must be zero beforehand.
-__global__ void embed_bwd_kernel(const int64_t* __restrict__ tok, const __nv_bfloat16* __restrict__ dy,
-                                 __nv_bfloat16* __restrict__ dw, int M, int N, float scale, int64_t V) {
-  extern __shared__ int stok[];
-  for (int i = threadIdx.x; i < M; i += blockDim.x) stok[i] = static_cast<int>(tok[i]);
-  __syncthreads();
-  const int j = blockIdx.x;
-  const int t = stok[j];
+// Deterministic embedding gradient: positions sorted by token (stable, so equal tokens keep ascending position
+// order); the CTA at the first sorted position of each token sums that token's rows of dy in position order and
+// writes the row of dw once. Rows of dw that no position touches stay zero (memset before).
+__global__ void embed_bwd_kernel(const int64_t* __restrict__ sorted_tok, const int64_t* __restrict__ order,
+                                 const __nv_bfloat16* __restrict__ dy, __nv_bfloat16* __restrict__ dw, int64_t M,
+                                 int N, float scale, int64_t V) {
+  const int64_t j = blockIdx.x;
+  const int64_t t = sorted_tok[j];
   if (t < 0 || t >= V) return;
-  for (int i = 0; i < j; ++i)
-    if (stok[i] == t) return;   // not the first occurrence
+  if (j > 0 && sorted_tok[j - 1] == t) return;      // not the first position of this token
+  int64_t end = j + 1;
+  while (end < M && sorted_tok[end] == t) ++end;
   for (int c = threadIdx.x * 8; c < N; c += blockDim.x * 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int i = j; i < M; ++i) {
-      if (stok[i] != t) continue;
+    for (int64_t i = j; i < end; ++i) {
       float f[8];
-      load8(dy + static_cast<int64_t>(i) * N + c, f);
+      load8(dy + order[i] * N + c, f);
 #pragma unroll
       for (int k = 0; k < 8; ++k) acc[k] += bf16_round(f[k] * scale);
     }
-    store8(dw + static_cast<int64_t>(t) * N + c, acc);
+    store8(dw + t * N + c, acc);
   }
 }
 
@@ -592,7 +593,7 @@ at::Tensor embedding_bwd(const at::Tensor& tok, const at::Tensor& dy, int64_t V,
   FYB_CHECK(dy.is_contiguous() && dy.dim() == 2 && dy.size(1) % 8 == 0 && dy.size(0) == tok.size(0),
             "embedding_bwd: dy");
   const int64_t M = tok.size(0), N = dy.size(1);
-  FYB_CHECK(M <= 16384, "embedding_bwd: at most 16384 positions per call");
+  FYB_CHECK(M < (1ll << 31), "embedding_bwd: too many positions");
   c10::cuda::CUDAGuard guard(dy.device());
   at::Tensor dw;
   if (out_opt.has_value() && out_opt->defined()) {
@@ -603,10 +604,15 @@ at::Tensor embedding_bwd(const at::Tensor& tok, const at::Tensor& dy, int64_t V,
     dw = at::empty({V, N}, dy.options());
   }
   FYB_CUDA(cudaMemsetAsync(dw.data_ptr(), 0, dw.numel() * 2, cur_stream()));
-  if (M > 0)
-    embed_bwd_kernel<<<M, 128, M * sizeof(int), cur_stream()>>>(
-        tok.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
-        reinterpret_cast<__nv_bfloat16*>(dw.data_ptr()), (int)M, (int)N, (float)scale, V);
+  if (M > 0) {
+    // a stable sort of the (few thousand) token ids groups equal tokens, in position order
+    auto sorted = at::sort(tok, /*stable=*/true, /*dim=*/0, /*descending=*/false);
+    const at::Tensor& stok = std::get<0>(sorted);
+    const at::Tensor& order = std::get<1>(sorted);
+    embed_bwd_kernel<<<static_cast<unsigned>(M), 128, 0, cur_stream()>>>(
+        stok.data_ptr<int64_t>(), order.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
+        reinterpret_cast<__nv_bfloat16*>(dw.data_ptr()), M, (int)N, (float)scale, V);
+  }
   check_launch("embedding_bwd");
   return dw;
 }

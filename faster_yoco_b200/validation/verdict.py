@@ -24,7 +24,7 @@ def metric(arm: dict, k: int, m: str):
     return None if h is None else h[KEYS[m]]
 
 
-def judge(S: dict, checkpoints):
+def apply_criterion(S: dict, checkpoints):
     rows, verdict = [], {}
     for m in ("mix", "fineweb", "code", "train"):
         rows += [f"\n### {m} (bits)\n", "| update | opt | ref | ref_s2 | opt_s2 | Y | E1 | E2 | S | within |Y| |",
@@ -55,7 +55,7 @@ def main(argv=None):
     if missing:
         raise SystemExit(f"missing arms {missing}")
     cps = sorted({int(k) for a in S.values() for k in a["heldout"]})
-    text, verdict = judge(S, cps)
+    text, verdict = apply_criterion(S, cps)
     with open(os.path.join(V, "verdict.md"), "w") as f:
         f.write(text + "\n\n" + json.dumps(verdict, indent=1) + "\n")
     print(text)

@@ -159,8 +159,9 @@ def test_subln_swiglu():
     assert rel(do, of.grad) < 3e-2 and rel(dg, gf.grad) < 2e-2
 
 
-def test_embedding():
-    V, N, M = 1000, 256, 513
+@pytest.mark.parametrize("M", [513, 20000])
+def test_embedding(M):
+    V, N = 1000, 256
     w = torch.randn(V, N, device=dev(), dtype=torch.bfloat16)
     tok = torch.randint(0, V, (M,), device=dev())
     tok[:20] = 7                       # repeated tokens

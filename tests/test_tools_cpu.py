@@ -122,3 +122,20 @@ def test_presets_and_parse():
     assert a.comm == "fused"
     a = parse_with_preset(train_parser(), ["DATA", "--adam-betas", "(0.9, 0.98)", "--lr", "3e-4"])
     assert a.adam_betas == (0.9, 0.98) and a.lr == [3e-4]
+
+
+def test_parity_markov_data_and_criterion():
+    import math
+    from faster_yoco_b200.validation.parity import MarkovLM, criterion
+    d = MarkovLM(64, 16, 3, data_seed=5)
+    b = next(d)
+    assert b["src_tokens"].shape == (3, 16) and torch.equal(b["src_tokens"][:, 1:], b["target"][:, :-1])
+    assert int(b["src_tokens"].min()) >= 2 and 0 < d.entropy_nats() < math.log(4) + 1e-6
+    # every transition is one of the chain's successors
+    src, tgt = b["src_tokens"].reshape(-1), b["target"].reshape(-1)
+    assert all(int(t) in d.next[int(s)].tolist() for s, t in zip(src, tgt))
+    curves = {"torch_s1": [3.0] * 10, "torch_s2": [3.2] * 10, "native_s1": [3.05] * 10, "native_s2": [3.22] * 10}
+    r = criterion(curves, [0, 5, 10])
+    assert r["windows"][0]["within_Y"] and r["within_2sigma_all"]
+    curves["native_s1"] = [4.0] * 10
+    assert not criterion(curves, [0, 5, 10])["windows"][0]["within_Y"]
