@@ -8,9 +8,14 @@ read and write peer memory directly over NVLink / NVSwitch:
 * ``reduce_to_owner``: flag barrier (all ranks finished the backward), then the owner's kernel sums its segment of
   every rank's gradient buffer in FP32 rank order, divides by world, writes BF16 in place and returns the segment's
   sum of squares (the grad-norm partial) -- one pass instead of NCCL reduce + scale kernel + norm kernel;
-* ``all_gather``: flag barrier (all owners finished Adam), then every rank pulls the other segments;
+* ``all_gather``: every owner stores its updated segment into every peer's buffer (remote stores run at NVLink speed,
+  remote loads do not), then one flag barrier publishes the pushes;
 * ``all_reduce_vector``: up to 32 fp32 values summed in rank order through the mailboxes (loss / sample size /
-  grad norm) -- no NCCL launch on the update path.
+  grad norm) -- no NCCL launch on the update path;
+* bucketed overlap (``setup_buckets``): per layer bucket, gradient pieces are pushed to their owners during backward
+  and parameters are pushed ahead of the next forward, either by kernels (``transport="sm"``) or by the copy
+  engines (``transport="ce"``: one ``cudaMemcpyAsync`` per piece on one stream per peer, arrival published by a
+  one-thread release-add on the peer's counter); the owner sums the staged pieces from local memory.
 
 The order in which ranks call these is identical by construction, so one flag slot with a monotonically increasing
 epoch serves every barrier. All waits are bounded on the device (a timeout sets the status word read by
