@@ -154,6 +154,50 @@ class WeightNoRandomStateIterator(CheckpointableIterator):
         self.n = state["n"] if state else 0
 
 
+class WeightIterator(CheckpointableIterator):
+    """Source index drawn from ONE Random(seed) stream whose state is checkpointed (the carried-state variant of
+    WeightNoRandomStateIterator; yoco/tasks/data/utils.py:65-95)."""
+
+    def __init__(self, weights: List[float], seed):
+        self.weights, self.seed = list(weights), seed
+        self.setstate(None)
+
+    def __next__(self):
+        if self._rng is None:
+            self._rng = Random(self.seed)
+            if self._rng_state is not None:
+                self._rng.setstate(self._rng_state)
+        idx = self._rng.choices(range(len(self.weights)), self.weights)[0]
+        self._rng_state = self._rng.getstate()
+        return idx
+
+    def getstate(self):
+        return {"random_state": self._rng_state}
+
+    def setstate(self, state):
+        self._rng_state = state["random_state"] if state else None
+        self._rng = None
+
+
+class IndexIterator(CheckpointableIterator):
+    """0, 1, ..., num - 1, 0, 1, ... with the count of yielded items as its state (utils.py:124-144)."""
+
+    def __init__(self, num: int):
+        self.num = num
+        self.setstate(None)
+
+    def __next__(self):
+        item = self.n % self.num
+        self.n += 1
+        return item
+
+    def getstate(self):
+        return {"n": self.n}
+
+    def setstate(self, state):
+        self.n = state["n"] if state else 0
+
+
 class MultiplexIterator(CheckpointableIterator):
     def __init__(self, control: CheckpointableIterator, sources: List[CheckpointableIterator]):
         self.control, self.sources = control, sources

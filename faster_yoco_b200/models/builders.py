@@ -66,15 +66,22 @@ def yoco_args(cfg: ModelConfig, vocab_size: int) -> YOCOArgs:
 def build_yoco(cfg: ModelConfig, vocab_size: int, device=None, dtype=None):
     from .yoco import YOCO
     from ..train.checkpoint import load_model_weights
-    if cfg.model_parallel_size != 1:
-        raise ValueError("YOCO runs with model_parallel_size 1 (as every reference recipe); use data parallelism")
+    from ..parallel import tp as TP
     args = yoco_args(cfg, vocab_size)
     with torch.device(device or "cpu"):
         model = YOCO(args)
     if dtype is not None:
         model = model.to(dtype)
     if cfg.load_ckpt is not None:
-        load_model_weights(model, cfg.load_ckpt)
+        if TP.tp_size() > 1:                       # a full (TP = 1) checkpoint, sliced for this rank
+            from .yoco import shard_state_dict
+            from ..train.checkpoint import PREFIX
+            ck = torch.load(cfg.load_ckpt, map_location="cpu", mmap=True)
+            sd = ck.get("model", ck)
+            sd = {(k[len(PREFIX):] if k.startswith(PREFIX) else k): v for k, v in sd.items()}
+            model.load_state_dict(shard_state_dict(sd, TP.tp_size(), TP.tp_rank()))
+        else:
+            load_model_weights(model, cfg.load_ckpt)
     return model
 
 

@@ -256,4 +256,6 @@ class SharedKVFn(torch.autograd.Function):
 
 
 def fused_path_ok(x: torch.Tensor, head_dim: int) -> bool:
-    return ops.native_on(x) and torch.is_grad_enabled() and head_dim == 128 and x.dtype == torch.bfloat16
+    from ..parallel import tp as TP
+    return (ops.native_on(x) and torch.is_grad_enabled() and head_dim == 128 and x.dtype == torch.bfloat16
+            and TP.tp_size() == 1)

@@ -11,6 +11,13 @@ weights every forward under YOCO_FUSE_QKVG, yoco/models/decoder/gate_retention.p
 
 State dicts are written and read with the reference's per-projection names (``mixer.q_proj.weight`` ...) by the
 hooks in :mod:`faster_yoco_b200.models.yoco`.
+
+Tensor parallelism (``model_parallel_size`` > 1, after ``parallel.tp.init_model_parallel``) follows the reference's
+Megatron declarations (gate_retention.py:40-46, feedforward_network.py:24-26, cross_attention.py, decoder/yoco.py):
+every input projection is column-parallel (each rank holds its heads / its FFN columns of EVERY merged part),
+every output projection is row-parallel (partial products summed across the TP group before the residual add), the
+embedding is vocabulary-parallel and the output projection column-parallel with gathered logits. Master weights are
+initialised in full and sliced, so a TP run starts from the TP=1 weights.
 """
 from __future__ import annotations
 
@@ -20,7 +27,22 @@ import torch
 import torch.nn as nn
 
 from .. import ops
+from ..parallel import tp as TP
 from . import init as I
+
+
+def _tp() -> int:
+    return TP.tp_size()
+
+
+def _slice_rows(full: torch.Tensor) -> torch.Tensor:
+    n = full.shape[0] // _tp()
+    return full[TP.tp_rank() * n:(TP.tp_rank() + 1) * n]
+
+
+def _slice_cols(full: torch.Tensor) -> torch.Tensor:
+    n = full.shape[1] // _tp()
+    return full[:, TP.tp_rank() * n:(TP.tp_rank() + 1) * n]
 
 
 def _round8(n: int) -> int:
@@ -46,12 +68,17 @@ class RMSNorm(nn.Module):
 
 
 class MergedLinear(nn.Module):
-    """One weight [sum(parts) (+pad), in] whose row blocks are the logical projections ``names``."""
+    """One weight [sum(parts) (+pad), in] whose row blocks are the logical projections ``names``. Under tensor
+    parallelism every part is column-split: this rank keeps rows [rank * n / tp, (rank + 1) * n / tp) of each."""
 
     def __init__(self, in_features: int, parts, names, inits, pad_to8: bool = False):
         super().__init__()
         self.in_features = in_features
-        self.parts = list(parts)
+        self.full_parts = list(parts)
+        tp = _tp()
+        if any(n % tp for n in self.full_parts):
+            raise ValueError(f"merged projection parts {self.full_parts} not divisible by TP size {tp}")
+        self.parts = [n // tp for n in self.full_parts]
         self.names = list(names)
         rows = sum(self.parts)
         self.rows = _round8(rows) if pad_to8 else rows
@@ -63,8 +90,13 @@ class MergedLinear(nn.Module):
         with torch.no_grad():
             self.weight.zero_()
             off = 0
-            for n, f in zip(self.parts, self._inits):
-                (init_override or f)(self.weight[off:off + n])
+            for n_full, n, f in zip(self.full_parts, self.parts, self._inits):
+                if _tp() == 1:
+                    (init_override or f)(self.weight[off:off + n])
+                else:
+                    full = torch.empty(n_full, self.in_features, device=self.weight.device)
+                    (init_override or f)(full)
+                    self.weight[off:off + n].copy_(_slice_rows(full))
                 off += n
 
     def offsets(self):
@@ -79,18 +111,36 @@ class MergedLinear(nn.Module):
 
 
 class Linear(nn.Module):
-    def __init__(self, in_features: int, out_features: int, init=I.init_method):
+    """``parallel``: None (replicated), "column" (output features split across the TP group) or "row" (input
+    features split; the partial products are summed across the group before the residual is added)."""
+
+    def __init__(self, in_features: int, out_features: int, init=I.init_method, parallel: Optional[str] = None):
         super().__init__()
         self.in_features, self.out_features = in_features, out_features
-        self.weight = nn.Parameter(torch.empty(out_features, in_features))
+        self.parallel = parallel if _tp() > 1 else None
+        shape = [out_features, in_features]
+        if self.parallel == "column":
+            shape[0] //= _tp()
+        elif self.parallel == "row":
+            shape[1] //= _tp()
+        self.weight = nn.Parameter(torch.empty(*shape))
         self._init = init
         self.reset_parameters()
 
     def reset_parameters(self, init_override=None):
         with torch.no_grad():
-            (init_override or self._init)(self.weight)
+            fn = init_override or self._init
+            if self.parallel is None:
+                fn(self.weight)
+                return
+            full = torch.empty(self.out_features, self.in_features, device=self.weight.device)
+            fn(full)
+            self.weight.copy_(_slice_rows(full) if self.parallel == "column" else _slice_cols(full))
 
     def forward(self, x, residual=None):
+        if self.parallel == "row":
+            y = TP.reduce_from_tp(ops.linear(x, self.weight))
+            return y + residual if residual is not None else y
         return ops.linear(x, self.weight, residual)
 
 
@@ -101,11 +151,11 @@ class FeedForwardNetwork(nn.Module):
         super().__init__()
         self.embed_dim, self.ffn_dim = embed_dim, ffn_dim
         self.fc1_gate = MergedLinear(embed_dim, [ffn_dim, ffn_dim], ["fc1", "gate"], [I.init_method, I.init_method])
-        self.fc2 = Linear(ffn_dim, embed_dim, I.init_method)
+        self.fc2 = Linear(ffn_dim, embed_dim, I.init_method, parallel="row")
 
     def forward(self, x, residual=None):
-        h = self.fc1_gate(x)
-        f = self.ffn_dim
+        h = self.fc1_gate(TP.copy_to_tp(x))
+        f = self.fc1_gate.parts[0]
         a = ops.swiglu(h[..., :f], h[..., f:])
         return self.fc2(a, residual)
 
@@ -127,14 +177,15 @@ class GateRetention(nn.Module):
         self.qkvg_proj = MergedLinear(d, [d, d, d, d, args.n_self_heads], ["q_proj", "k_proj", "v_proj", "g_proj",
                                                                            "gt_proj"],
                                       [I.qkvg_init_method] * 5, pad_to8=True)
-        self.out_proj = Linear(d, d, I.out_init_method)
+        self.out_proj = Linear(d, d, I.out_init_method, parallel="row")
         self.subln_eps = args.norm_eps
         self.gate_logit_normalizer = args.gate_logit_normalizer
 
     def project(self, x):
         B, L, _ = x.shape
-        d, H, D = self.embed_dim, self.num_heads, self.head_dim
-        y = self.qkvg_proj(x)
+        H, D = self.num_heads, self.head_dim
+        d = H * D                                   # this rank's width (the full width without TP)
+        y = self.qkvg_proj(TP.copy_to_tp(x))
         q = y[..., 0 * d:1 * d].view(B, L, H, D)
         k = y[..., 1 * d:2 * d].view(B, L, H, D)
         v = y[..., 2 * d:3 * d].view(B, L, H, D)
@@ -196,12 +247,13 @@ class SlidingWindowAttention(nn.Module):
         self.head_dim = args.dim // args.n_self_heads
         d = args.dim
         self.qkv_proj = MergedLinear(d, [d, d, d], ["q_proj", "k_proj", "v_proj"], [I.init_method] * 3)
-        self.out_proj = Linear(d, d, I.init_method)
+        self.out_proj = Linear(d, d, I.init_method, parallel="row")
 
     def forward(self, x, rel_pos, start_pos=0, incremental_state=None, residual=None):
         B, L, _ = x.shape
-        d, H, D = self.embed_dim, self.num_heads, self.head_dim
-        y = self.qkv_proj(x)
+        H, D = self.num_heads, self.head_dim
+        d = H * D
+        y = self.qkv_proj(TP.copy_to_tp(x))
         q = ops.rope(y[..., :d].view(B, L, H, D), *rel_pos)
         k = ops.rope(y[..., d:2 * d].view(B, L, H, D), *rel_pos)
         v = y[..., 2 * d:].view(B, L, H, D)
@@ -235,12 +287,12 @@ class CrossAttention(nn.Module):
         self.num_heads = args.n_attn_heads // args.model_parallel_size
         self.num_kv_heads = args.n_attn_kv_heads // args.model_parallel_size
         self.head_dim = args.dim // args.n_attn_heads
-        self.q_proj = Linear(args.dim, args.dim, I.init_method)
-        self.out_proj = Linear(args.dim, args.dim, I.init_method)
+        self.q_proj = Linear(args.dim, args.dim, I.init_method, parallel="column")
+        self.out_proj = Linear(args.dim, args.dim, I.init_method, parallel="row")
 
     def forward(self, x, key, value, rel_pos, residual=None, q_offset: Optional[int] = None):
         B, L, _ = x.shape
-        q = ops.rope(self.q_proj(x).view(B, L, self.num_heads, self.head_dim), *rel_pos)
+        q = ops.rope(self.q_proj(TP.copy_to_tp(x)).view(B, L, self.num_heads, self.head_dim), *rel_pos)
         if key.shape[1] != L:
             off = key.shape[1] - L if q_offset is None else q_offset
             o = ops.ref.attention(q, key, value, causal=True, q_offset=off)

@@ -19,6 +19,7 @@ import torch.nn.functional as F
 
 from .. import ops
 from ..config import YOCOArgs
+from ..parallel import tp as TP
 from . import init as I
 from .layers import (CrossAttention, FeedForwardNetwork, GateRetention, Linear, MergedLinear, RMSNorm,
                      SlidingWindowAttention)
@@ -146,7 +147,7 @@ class CrossDecoder(nn.Module):
     def __init__(self, args: YOCOArgs):
         super().__init__()
         self.args = args
-        self.num_heads = args.n_attn_kv_heads
+        self.num_heads = args.n_attn_kv_heads // args.model_parallel_size    # this rank's KV heads
         self.head_dim = args.dim // args.n_attn_heads
         kvd = self.head_dim * args.n_attn_kv_heads
         self.kv_proj = MergedLinear(args.dim, [kvd, kvd], ["k_proj", "v_proj"], [I.init_method, I.init_method])
@@ -164,7 +165,7 @@ class CrossDecoder(nn.Module):
             key, value = SharedKVFn.apply(x, self.kv_layer_norm.weight, self.kv_proj.weight, *rel_pos,
                                           (self.num_heads, self.head_dim, self.args.norm_eps))
             return key, value, rel_pos
-        y = self.kv_proj(self.kv_layer_norm(x))
+        y = self.kv_proj(TP.copy_to_tp(self.kv_layer_norm(x)))
         key = ops.rope(y[..., :kvd].view(B, L, self.num_heads, self.head_dim), *rel_pos)
         value = y[..., kvd:].view(B, L, self.num_heads, self.head_dim)
         return key, value, rel_pos
@@ -218,9 +219,16 @@ class YOCO(nn.Module):
     def __init__(self, args: YOCOArgs):
         super().__init__()
         self.args = args
+        if args.model_parallel_size != TP.tp_size():
+            raise ValueError(f"model_parallel_size {args.model_parallel_size} but the tensor-parallel group has "
+                             f"{TP.tp_size()} ranks (call parallel.tp.init_model_parallel first)")
         self.embed_scale = math.sqrt(args.dim)
-        self.embed_tokens = nn.Embedding(args.vocab_size, args.dim)
-        self.output_projection = Linear(args.dim, args.vocab_size, I.init_method)
+        if TP.tp_size() > 1:
+            self.embed_tokens = TP.VocabParallelEmbedding(args.vocab_size, args.dim)
+            self.output_projection = TP.ColumnParallelLinear(args.dim, args.vocab_size, gather_output=True)
+        else:
+            self.embed_tokens = nn.Embedding(args.vocab_size, args.dim)
+            self.output_projection = Linear(args.dim, args.vocab_size, I.init_method)
         if args.share_input_output_embed:
             self.output_projection.weight = self.embed_tokens.weight
         self.self_decoder = SelfDecoder(args)
@@ -234,7 +242,11 @@ class YOCO(nn.Module):
     def reset_parameters(self):
         std = self.args.init_std
         override = I.normal_init(std) if std is not None else None
-        I.vocab_init_method(self.embed_tokens.weight) if override is None else override(self.embed_tokens.weight)
+        if isinstance(self.embed_tokens, TP.VocabParallelEmbedding):
+            self.embed_tokens.reset_parameters(override or I.vocab_init_method)
+            self.output_projection.reset_parameters(override or I.init_method)
+        else:
+            I.vocab_init_method(self.embed_tokens.weight) if override is None else override(self.embed_tokens.weight)
         for m in self.modules():
             if isinstance(m, (MergedLinear, Linear)):
                 m.reset_parameters(override)
@@ -274,7 +286,10 @@ class YOCO(nn.Module):
         n_self = len(self.self_decoder.layers)
         if comm_hooks is not None:
             comm_hooks.before(0)
-        h = ops.embedding(x, self.embed_tokens.weight, self.embed_scale)
+        if isinstance(self.embed_tokens, TP.VocabParallelEmbedding):
+            h = self.embed_tokens(x, self.embed_scale)
+        else:
+            h = ops.embedding(x, self.embed_tokens.weight, self.embed_scale)
         h = self.self_decoder(h, incremental_state=incremental_state, is_prefilling=is_prefilling,
                               start_pos=start_pos, comm_hooks=comm_hooks, bucket0=1)
         h = self.cross_decoder(h, start_pos=start_pos, incremental_state=incremental_state,
@@ -328,6 +343,28 @@ class YOCO(nn.Module):
                 if w.shape[0] < mod.rows:
                     w = torch.cat([w, w.new_zeros(mod.rows - w.shape[0], w.shape[1])], 0)
                 state_dict[internal_key] = w
+
+
+# reference parameter name suffix -> how a full (TP = 1) tensor is cut for one tensor-parallel rank
+_TP_COLUMN = ("mixer.q_proj.weight", "mixer.k_proj.weight", "mixer.v_proj.weight", "mixer.g_proj.weight",
+              "mixer.gt_proj.weight", "ffn.fc1.weight", "ffn.gate.weight", "cross_decoder.k_proj.weight",
+              "cross_decoder.v_proj.weight", "embed_tokens.weight", "output_projection.weight")
+_TP_ROW = ("mixer.out_proj.weight", "ffn.fc2.weight")
+
+
+def shard_state_dict(full: Dict[str, torch.Tensor], size: int, rank: int) -> Dict[str, torch.Tensor]:
+    """This TP rank's slice of a full reference-named state dict (the reference's TP-sliced load,
+    yoco/models/decoder/transformer.py:239-251, applied to YOCO's column / row-parallel declarations)."""
+    out = {}
+    for k, v in full.items():
+        if size > 1 and k.endswith(_TP_COLUMN):
+            n = v.shape[0] // size
+            v = v[rank * n:(rank + 1) * n]
+        elif size > 1 and k.endswith(_TP_ROW):
+            n = v.shape[1] // size
+            v = v[:, rank * n:(rank + 1) * n]
+        out[k] = v
+    return out
 
 
 def build_model(args: YOCOArgs, device=None, dtype=None) -> YOCO:

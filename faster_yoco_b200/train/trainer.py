@@ -46,6 +46,11 @@ class Trainer:
     def __init__(self, model: torch.nn.Module, optim_cfg, *, device, comm: str = "nccl", zero_stage: int = 1,
                  pad_idx: int = 1, graph_step: bool = False, group=None, check_consistency: bool = True,
                  overlap: bool = False, partition: str = "even", criterion=None, transport: str = "sm"):
+        from ..parallel import tp as TP
+        if TP.tp_size() > 1:
+            raise NotImplementedError(
+                "the ZeRO trainer runs pure data parallelism (tensor-parallel YOCO / LLaMA models serve evaluation "
+                "and custom loops; every reference recipe trains with model_parallel_size 1)")
         self.model = model
         self.device = torch.device(device)
         self.cfg = optim_cfg

@@ -78,3 +78,19 @@ def test_weight_iterator_is_stateless_per_position():
     seq = [next(w) for _ in range(10)]
     w.setstate({"n": 4})
     assert [next(w) for _ in range(6)] == seq[4:]
+
+
+def test_weight_and_index_iterators_resume():
+    w = it.WeightIterator([0.2, 0.8], 7)
+    seq = [next(w) for _ in range(12)]
+    w2 = it.WeightIterator([0.2, 0.8], 7)
+    for _ in range(5):
+        next(w2)
+    st = w2.getstate()
+    w3 = it.WeightIterator([0.2, 0.8], 7)
+    w3.setstate(st)
+    assert [next(w3) for _ in range(7)] == seq[5:]
+    ix = it.IndexIterator(3)
+    assert [next(ix) for _ in range(5)] == [0, 1, 2, 0, 1]
+    ix.setstate({"n": 4})
+    assert next(ix) == 1
