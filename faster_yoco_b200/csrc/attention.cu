@@ -916,6 +916,7 @@ void set_smem(K kern, int bytes) {
 
 std::vector<at::Tensor> attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, bool causal,
                                       int64_t window, double scale) {
+  FYB_RANGE("fyb::attention_fwd");
   check_qkv(q, "q");
   check_qkv(k, "k");
   check_qkv(v, "v");
@@ -959,6 +960,7 @@ std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& 
                                       const c10::optional<at::Tensor>& dk_out, const c10::optional<at::Tensor>& dv_out,
                                       const c10::optional<at::Tensor>& rope_cos,
                                       const c10::optional<at::Tensor>& rope_sin, bool rope_q, bool rope_k) {
+  FYB_RANGE("fyb::attention_bwd");
   check_qkv(q, "q");
   check_qkv(k, "k");
   check_qkv(v, "v");
@@ -1029,6 +1031,7 @@ std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& 
 }
 
 at::Tensor retention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& gcum) {
+  FYB_RANGE("fyb::retention_fwd");
   check_qkv(q, "q");
   check_qkv(k, "k");
   check_qkv(v, "v");
@@ -1060,6 +1063,7 @@ std::vector<at::Tensor> retention_bwd(const at::Tensor& dout, const at::Tensor& 
                                       const c10::optional<at::Tensor>& dv_out,
                                       const c10::optional<at::Tensor>& rope_cos,
                                       const c10::optional<at::Tensor>& rope_sin) {
+  FYB_RANGE("fyb::retention_bwd");
   check_qkv(q, "q");
   check_qkv(k, "k");
   check_qkv(v, "v");

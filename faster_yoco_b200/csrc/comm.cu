@@ -467,6 +467,7 @@ void ipc_close(int64_t ptr) { FYB_CUDA(cudaIpcCloseMemHandle(reinterpret_cast<vo
 
 void flag_barrier(const std::vector<int64_t>& peer_flags, const at::Tensor& my_flags, const at::Tensor& counters,
                   int64_t rank, int64_t slot) {
+  FYB_RANGE("fyb::flag_barrier");
   const int world = static_cast<int>(peer_flags.size());
   FYB_CHECK(counters.is_cuda() && counters.numel() > slot, "flag_barrier: counters");
   flag_barrier_kernel<<<1, 32, 0, cur_stream()>>>(to_ptrs(peer_flags), reinterpret_cast<uint32_t*>(my_flags.data_ptr()),
@@ -480,6 +481,7 @@ int reduce_ctas() { return std::min(num_sms() * 2, 1024); }
 // reduce [base, base+n) of the flat gradient buffers into out (this rank's buffer) and sq[0] = sum of squares
 void reduce_owner(const std::vector<int64_t>& peer_grads, at::Tensor& out, int64_t base, int64_t n, at::Tensor& part,
                   at::Tensor& sq) {
+  FYB_RANGE("fyb::reduce_owner");
   const int world = static_cast<int>(peer_grads.size());
   FYB_CHECK(base % 8 == 0, "reduce_owner: segment base must be a multiple of 8 elements");
   const int P = static_cast<int>(part.numel());
@@ -495,6 +497,7 @@ void reduce_owner(const std::vector<int64_t>& peer_grads, at::Tensor& out, int64
 // reduce the listed owned ranges; part (>= ctas floats) receives the per-CTA sums of squares
 void reduce_ranges(const std::vector<int64_t>& peer_grads, at::Tensor& out, const at::Tensor& ranges, at::Tensor& part,
                    int64_t ctas) {
+  FYB_RANGE("fyb::reduce_ranges");
   const int world = static_cast<int>(peer_grads.size());
   FYB_CHECK(ranges.is_cuda() && ranges.scalar_type() == at::kLong && ranges.dim() == 2 && ranges.size(1) == 2,
             "reduce_ranges: ranges must be a device int64 [n, 2]");
@@ -517,6 +520,7 @@ void sum_partials(const at::Tensor& part, at::Tensor& out) {
 
 void gather_segments(const std::vector<int64_t>& peer_params, at::Tensor& dst, const at::Tensor& segs, int64_t rank,
                      int64_t ctas) {
+  FYB_RANGE("fyb::gather_segments");
   FYB_CHECK(segs.is_cuda() && segs.scalar_type() == at::kLong && segs.dim() == 2 && segs.size(1) == 3,
             "gather_segments: segs must be a device int64 [n, 3]");
   if (segs.size(0) == 0) return;
@@ -528,6 +532,7 @@ void gather_segments(const std::vector<int64_t>& peer_params, at::Tensor& dst, c
 
 void push_range(const at::Tensor& src, const std::vector<int64_t>& peer_dst, int64_t off, int64_t n, int64_t rank,
                 int64_t ctas) {
+  FYB_RANGE("fyb::push_range");
   const int world = static_cast<int>(peer_dst.size());
   FYB_CHECK(off % 8 == 0, "push_range: offset must be a multiple of 8 elements");
   if (n <= 0) return;
@@ -539,6 +544,7 @@ void push_range(const at::Tensor& src, const std::vector<int64_t>& peer_dst, int
 
 void push_bucket(const at::Tensor& src, const std::vector<int64_t>& peer_dst, const std::vector<int64_t>& peer_arrive,
                  const at::Tensor& ranges, int64_t bucket, int64_t rank, int64_t ctas) {
+  FYB_RANGE("fyb::push_bucket");
   const int world = static_cast<int>(peer_dst.size());
   FYB_CHECK(ranges.is_cuda() && ranges.scalar_type() == at::kLong && ranges.dim() == 2 && ranges.size(1) == 2,
             "push_bucket: ranges must be a device int64 [n, 2]");
@@ -552,6 +558,7 @@ void push_bucket(const at::Tensor& src, const std::vector<int64_t>& peer_dst, co
 void push_grads(const at::Tensor& grad, const std::vector<int64_t>& peer_staging,
                 const std::vector<int64_t>& peer_arrive, const at::Tensor& pieces, int64_t bucket, int64_t rank,
                 int64_t seg, int64_t ctas) {
+  FYB_RANGE("fyb::push_grads");
   const int world = static_cast<int>(peer_staging.size());
   FYB_CHECK(pieces.is_cuda() && pieces.scalar_type() == at::kLong && pieces.dim() == 2 && pieces.size(1) == 3,
             "push_grads: pieces must be a device int64 [n, 3]");
@@ -564,6 +571,7 @@ void push_grads(const at::Tensor& grad, const std::vector<int64_t>& peer_staging
 
 void reduce_staged(at::Tensor& grad, const at::Tensor& staging, const at::Tensor& ranges, int64_t world, int64_t rank,
                    int64_t seg, at::Tensor& part, int64_t ctas) {
+  FYB_RANGE("fyb::reduce_staged");
   FYB_CHECK(part.numel() >= ctas, "reduce_staged: partials buffer too small");
   if (ranges.size(0) == 0) {
     part.zero_();
@@ -577,6 +585,7 @@ void reduce_staged(at::Tensor& grad, const at::Tensor& staging, const at::Tensor
 }
 
 void peer_copy(int64_t dst, int64_t src, int64_t nbytes) {
+  FYB_RANGE("fyb::peer_copy");
   // one copy-engine transfer per call (the batched copy entry points are not used)
   if (nbytes <= 0) return;
   FYB_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src),
@@ -589,6 +598,7 @@ void signal_peer(int64_t counter_base, int64_t index) {
 }
 
 void wait_arrivals(const at::Tensor& arrive, at::Tensor& expected, int64_t bucket, int64_t increment) {
+  FYB_RANGE("fyb::wait_arrivals");
   wait_arrivals_kernel<<<1, 32, 0, cur_stream()>>>(reinterpret_cast<const uint32_t*>(arrive.data_ptr()),
                                                    reinterpret_cast<uint32_t*>(expected.data_ptr()),
                                                    static_cast<int>(bucket), static_cast<uint32_t>(increment),
@@ -598,6 +608,7 @@ void wait_arrivals(const at::Tensor& arrive, at::Tensor& expected, int64_t bucke
 
 void mailbox_put(const std::vector<int64_t>& peer_boxes, const at::Tensor& vals, int64_t rank,
                  const at::Tensor& counter) {
+  FYB_RANGE("fyb::mailbox_put");
   const int world = static_cast<int>(peer_boxes.size());
   FYB_CHECK(vals.numel() <= 32 && vals.scalar_type() == at::kFloat, "mailbox_put: at most 32 fp32 values");
   mailbox_put_kernel<<<1, 32, 0, cur_stream()>>>(to_ptrs(peer_boxes), vals.data_ptr<float>(),
@@ -607,6 +618,7 @@ void mailbox_put(const std::vector<int64_t>& peer_boxes, const at::Tensor& vals,
 }
 
 void mailbox_sum(const at::Tensor& box, at::Tensor& out, int64_t world, at::Tensor& counter) {
+  FYB_RANGE("fyb::mailbox_sum");
   mailbox_sum_kernel<<<1, 32, 0, cur_stream()>>>(box.data_ptr<float>(), out.data_ptr<float>(),
                                                  static_cast<int>(out.numel()), static_cast<int>(world),
                                                  reinterpret_cast<uint32_t*>(counter.data_ptr()));

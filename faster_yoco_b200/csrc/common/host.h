@@ -7,6 +7,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <cstdint>
 #include <stdexcept>
@@ -102,6 +103,16 @@ inline int num_sms() {
 int* status_ptr();
 
 inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// Scoped NVTX range around a native op's host call (header-only NVTX 3: visible to an attached profiler such as
+// Nsight Systems, a few nanoseconds otherwise; host-side only, so legal during CUDA graph capture).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
+#define FYB_RANGE(name) ::fyb::NvtxRange fyb_nvtx_range_(name)
 
 inline void check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();

@@ -466,6 +466,7 @@ __global__ void __launch_bounds__(kScanThreads) gate_cumsum_bwd_kernel(const flo
 // host entry points
 
 at::Tensor gate_cumsum_fwd(const at::Tensor& y, int64_t B, int64_t L, double normalizer) {
+  FYB_RANGE("fyb::gate_cumsum_fwd");
   FYB_CHECK(y.is_cuda() && y.scalar_type() == at::kBFloat16 && y.dim() == 2 && y.stride(1) == 1 && y.size(0) == B * L,
             "gate_cumsum_fwd: bf16 [B*L, H] view expected");
   c10::cuda::CUDAGuard guard(y.device());
@@ -481,6 +482,7 @@ at::Tensor gate_cumsum_fwd(const at::Tensor& y, int64_t B, int64_t L, double nor
 }
 
 void gate_cumsum_bwd(const at::Tensor& dg, const at::Tensor& y, at::Tensor& dy, double normalizer) {
+  FYB_RANGE("fyb::gate_cumsum_bwd");
   const int64_t B = dg.size(0), H = dg.size(1), L = dg.size(2);
   FYB_CHECK(dg.is_contiguous() && dg.scalar_type() == at::kFloat, "gate_cumsum_bwd: dg fp32 [B, H, L]");
   FYB_CHECK(dy.stride(1) == 1 && dy.size(0) == B * L && dy.size(1) == H, "gate_cumsum_bwd: dy view [B*L, H]");
@@ -495,6 +497,7 @@ void gate_cumsum_bwd(const at::Tensor& dg, const at::Tensor& y, at::Tensor& dy, 
 }
 
 at::Tensor swiglu_fwd(const at::Tensor& x, const at::Tensor& y) {
+  FYB_RANGE("fyb::swiglu_fwd");
   FYB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16 && x.dim() == 2 &&
                 x.sizes() == y.sizes() && x.stride(1) == 1 && y.stride(1) == 1,
             "swiglu_fwd: bf16 [M, N] views with contiguous rows expected");
@@ -514,6 +517,7 @@ at::Tensor swiglu_fwd(const at::Tensor& x, const at::Tensor& y) {
 
 std::vector<at::Tensor> swiglu_bwd(const at::Tensor& x, const at::Tensor& y, const at::Tensor& g,
                                    const c10::optional<at::Tensor>& dx_out, const c10::optional<at::Tensor>& dy_out) {
+  FYB_RANGE("fyb::swiglu_bwd");
   const int64_t M = x.size(0), N = x.size(1);
   FYB_CHECK(g.is_contiguous() && g.size(0) == M && g.size(1) == N, "swiglu_bwd: grad");
   c10::cuda::CUDAGuard guard(x.device());
@@ -539,6 +543,7 @@ std::vector<at::Tensor> swiglu_bwd(const at::Tensor& x, const at::Tensor& y, con
 }
 
 at::Tensor rope_fwd(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t, bool conj, bool neox) {
+  FYB_RANGE("fyb::rope_fwd");
   FYB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 4 && x.stride(3) == 1,
             "rope: bf16 [B, L, H, D] with contiguous last dim expected");
   const int B = (int)x.size(0), L = (int)x.size(1), H = (int)x.size(2), D = (int)x.size(3);
@@ -572,6 +577,7 @@ at::Tensor rope_fwd(const at::Tensor& x, const at::Tensor& cos_t, const at::Tens
 }
 
 at::Tensor embedding_fwd(const at::Tensor& tok, const at::Tensor& w, double scale) {
+  FYB_RANGE("fyb::embedding_fwd");
   FYB_CHECK(tok.is_cuda() && tok.scalar_type() == at::kLong && tok.dim() == 1 && tok.is_contiguous(),
             "embedding_fwd: int64 token vector expected");
   FYB_CHECK(w.scalar_type() == at::kBFloat16 && w.dim() == 2 && w.is_contiguous() && w.size(1) % 8 == 0,
@@ -590,6 +596,7 @@ at::Tensor embedding_fwd(const at::Tensor& tok, const at::Tensor& w, double scal
 
 at::Tensor embedding_bwd(const at::Tensor& tok, const at::Tensor& dy, int64_t V, double scale,
                          const c10::optional<at::Tensor>& out_opt) {
+  FYB_RANGE("fyb::embedding_bwd");
   FYB_CHECK(dy.is_contiguous() && dy.dim() == 2 && dy.size(1) % 8 == 0 && dy.size(0) == tok.size(0),
             "embedding_bwd: dy");
   const int64_t M = tok.size(0), N = dy.size(1);
@@ -618,6 +625,7 @@ at::Tensor embedding_bwd(const at::Tensor& tok, const at::Tensor& dy, int64_t V,
 }
 
 std::vector<at::Tensor> ce_fwd(const at::Tensor& logits, const at::Tensor& target, int64_t ignore) {
+  FYB_RANGE("fyb::ce_fwd");
   FYB_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 && logits.stride(1) == 1,
             "ce_fwd: bf16 [M, V] logits with contiguous rows expected");
   FYB_CHECK(target.scalar_type() == at::kLong && target.is_contiguous() && target.numel() == logits.size(0),
@@ -636,6 +644,7 @@ std::vector<at::Tensor> ce_fwd(const at::Tensor& logits, const at::Tensor& targe
 
 at::Tensor ce_bwd(const at::Tensor& logits, const at::Tensor& target, const at::Tensor& lse, const at::Tensor& grad,
                   int64_t ignore, const c10::optional<at::Tensor>& out_opt) {
+  FYB_RANGE("fyb::ce_bwd");
   c10::cuda::CUDAGuard guard(logits.device());
   const int64_t M = logits.size(0), V = logits.size(1);
   at::Tensor dx = (out_opt.has_value() && out_opt->defined()) ? *out_opt : at::empty_like(logits);
@@ -653,6 +662,7 @@ at::Tensor ce_bwd(const at::Tensor& logits, const at::Tensor& target, const at::
 void adam_step(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor& v, at::Tensor& p16,
                const at::Tensor& hyper, const at::Tensor& factor, double b1, double b2, double eps, double wd,
                bool adamw) {
+  FYB_RANGE("fyb::adam_step");
   const int64_t n = p32.numel();
   FYB_CHECK(p32.is_contiguous() && m.is_contiguous() && v.is_contiguous() && g16.is_contiguous() &&
                 p16.is_contiguous() && g16.numel() == n && m.numel() == n && v.numel() == n && p16.numel() == n,
@@ -683,6 +693,7 @@ void sq_norm_into(const at::Tensor& x, float* part, int P, float* out) {
 }
 
 at::Tensor sq_norm(const at::Tensor& x) {
+  FYB_RANGE("fyb::sq_norm");
   FYB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() &&
                 reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
             "sq_norm: contiguous 16-byte aligned bf16 expected");

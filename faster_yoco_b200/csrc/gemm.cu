@@ -404,6 +404,7 @@ Plan pick_plan(int M, int N, int K) {
 // C = A @ B^T in the operand conventions above. C: bf16 or fp32 [M, N] (any row stride); R: optional bf16 residual.
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
           const c10::optional<at::Tensor>& R) {
+  FYB_RANGE("fyb::gemm");
   FYB_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm: CUDA tensors expected");
   FYB_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
   FYB_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm: 2-D tensors expected");

@@ -347,6 +347,7 @@ __global__ void subln_swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dout, 
 }  // namespace
 
 std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps) {
+  FYB_RANGE("fyb::rms_norm_fwd");
   FYB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.is_contiguous(),
             "rms_norm_fwd: contiguous bf16 [M, N] expected");
   const int64_t M = x.size(0), N = x.size(1);
@@ -419,6 +420,7 @@ int rms_bwd_ctas(int64_t M) { return static_cast<int>(std::min<int64_t>(M, 2 * n
 
 std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const c10::optional<at::Tensor>& w,
                                      const at::Tensor& rstd, const c10::optional<at::Tensor>& dres) {
+  FYB_RANGE("fyb::rms_norm_bwd");
   FYB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.is_contiguous() &&
                 dy.is_contiguous() && dy.sizes() == x.sizes() && dy.scalar_type() == at::kBFloat16,
             "rms_norm_bwd: contiguous bf16 [M, N] expected");
@@ -438,6 +440,7 @@ std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, 
 }
 
 std::vector<at::Tensor> subln_swiglu_fwd(const at::Tensor& o, const at::Tensor& g, double eps, int64_t D) {
+  FYB_RANGE("fyb::subln_swiglu_fwd");
   FYB_CHECK(o.is_cuda() && o.scalar_type() == at::kBFloat16 && o.dim() == 2 && o.is_contiguous(),
             "subln_swiglu_fwd: o must be contiguous bf16 [T, H*D]");
   FYB_CHECK(g.scalar_type() == at::kBFloat16 && g.dim() == 2 && g.stride(1) == 1 && g.sizes() == o.sizes() &&
@@ -467,6 +470,7 @@ std::vector<at::Tensor> subln_swiglu_fwd(const at::Tensor& o, const at::Tensor& 
 
 std::vector<at::Tensor> subln_swiglu_bwd(const at::Tensor& dout, const at::Tensor& o, const at::Tensor& g,
                                          const at::Tensor& rstd, int64_t D, const c10::optional<at::Tensor>& dg_out) {
+  FYB_RANGE("fyb::subln_swiglu_bwd");
   FYB_CHECK(dout.is_contiguous() && dout.sizes() == o.sizes(), "subln_swiglu_bwd: dout");
   const int64_t T = o.size(0), HD = o.size(1);
   const int H = static_cast<int>(HD / D);
