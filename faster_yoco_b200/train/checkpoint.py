@@ -27,6 +27,16 @@ import torch.distributed as dist
 PREFIX = "decoder.model."
 
 
+def _core(model):
+    """(module whose state dict goes under ``decoder.model.``, prefix of its parameter names inside `model`):
+    the LLaMA task wrapper holds the Transformer as ``.model`` (reference: LanguageModel.decoder = LLaMA,
+    LLaMA.model = Transformer, so its keys are ``decoder.model.layers...``)."""
+    from ..models.transformer import LLaMA
+    if isinstance(model, LLaMA):
+        return model.model, "model."
+    return model, ""
+
+
 def _split_for_export(model, name: str, t: torch.Tensor) -> Dict[str, torch.Tensor]:
     """Internal parameter name -> {reference name: slice} (identity for unmerged parameters)."""
     from ..models.layers import MergedLinear
@@ -65,12 +75,13 @@ def save_checkpoint(path: str, model, trainer, *, extra_state: Optional[dict] = 
     opt = trainer.zero.consolidated_state()            # {internal name: {master, exp_avg, exp_avg_sq}}
     if rank != 0:
         return None
+    core, strip = _core(model)
     state = {"master": {}, "exp_avg": {}, "exp_avg_sq": {}, "step": trainer.zero.num_updates}
     for name, st in opt.items():
         for key in ("master", "exp_avg", "exp_avg_sq"):
             for ref_name, t in _split_for_export(model, name, st[key]).items():
-                state[key][ref_name] = t.clone()
-    msd = {PREFIX + k: v.detach().cpu() for k, v in model.state_dict().items()}
+                state[key][ref_name[len(strip):] if strip and ref_name.startswith(strip) else ref_name] = t.clone()
+    msd = {PREFIX + k: v.detach().cpu() for k, v in core.state_dict().items()}
     ckpt = {
         "args": None,
         "cfg": cfg or {},
@@ -97,14 +108,16 @@ def load_model_weights(model, path_or_ckpt, strict: bool = True):
     ck = torch.load(path_or_ckpt, map_location="cpu", mmap=True) if isinstance(path_or_ckpt, str) else path_or_ckpt
     sd = ck.get("model", ck) if isinstance(ck, dict) else ck
     sd = {(k[len(PREFIX):] if k.startswith(PREFIX) else k): v for k, v in sd.items()}
+    core, _ = _core(model)
     with torch.no_grad():
-        missing, unexpected = model.load_state_dict(sd, strict=strict)
+        missing, unexpected = core.load_state_dict(sd, strict=strict)
     return ck
 
 
 def load_checkpoint(path: str, model, trainer) -> dict:
     """Restore model weights, this rank's optimizer shard, the update count and the LR schedule."""
     ck = load_model_weights(model, path)
+    _, strip = _core(model)
     st = ck.get("last_optimizer_state") or {}
     zero = trainer.zero
     fp = trainer.flat
@@ -118,7 +131,10 @@ def load_checkpoint(path: str, model, trainer) -> dict:
                 pe = off - e.offset             # position inside the parameter
                 for key, dst in (("master", zero.master), ("exp_avg", zero.exp_avg),
                                  ("exp_avg_sq", zero.exp_avg_sq)):
-                    t = _join_for_import(model, e.name, st.get(key, {}))
+                    entries = st.get(key, {})
+                    if strip:
+                        entries = {strip + k: v for k, v in entries.items()}
+                    t = _join_for_import(model, e.name, entries)
                     if t is None:
                         if key == "master":
                             dst[lo:lo + cnt].copy_(e.param.detach().reshape(-1)[pe:pe + cnt].float())

@@ -306,3 +306,30 @@ def test_cli_validate_harness(tmp_path, capsys):
                    "--tiktoken-model", "byte", "--tokens-per-sample", "128", "--cpu", "--kernels", "torch"]) == 0
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert 0.0 <= res["accuracy"] <= 100.0 and "accuracy_norm" in res
+
+
+def test_cli_llama_train_and_harness(tmp_path, capsys):
+    from faster_yoco_b200.cli import train as T
+    from faster_yoco_b200.cli import validate as V
+    data = str(tmp_path / "data")
+    _corpus(data)
+    small = ["--arch", "llama_from_scratch", "--dim", "64", "--n-layers", "2", "--n-heads", "4", "--n-kv-heads", "2",
+             "--tiktoken-model", "byte", "--cpu", "--kernels", "torch"]
+    assert T.main([data, "--task", "gpt", "--tokens-per-sample", "32", "--batch-size", "2", "--pad-to-max-len",
+                   "--batch-read-ahead", "4", "--log-interval", "2", "--warmup-updates", "1", "--max-update", "2",
+                   "--save-dir", str(tmp_path / "ck"), *small]) == 0
+    ck = torch.load(str(tmp_path / "ck" / "checkpoint_last.pt"), weights_only=False)
+    assert "decoder.model.layers.0.attention.wq.weight" in ck["model"]       # the reference's key layout
+    assert "layers.0.attention.wq.weight" in ck["last_optimizer_state"]["master"]
+    # resume reads the same layout back
+    assert T.main([data, "--task", "gpt", "--tokens-per-sample", "32", "--batch-size", "2", "--pad-to-max-len",
+                   "--batch-read-ahead", "4", "--log-interval", "2", "--warmup-updates", "1", "--max-update", "3",
+                   "--save-dir", str(tmp_path / "ck"), *small]) == 0
+    assert torch.load(str(tmp_path / "ck" / "checkpoint_last.pt"),
+                      weights_only=False)["optimizer_history"][-1]["num_updates"] == 3
+    _write_boolq(str(tmp_path / "h"))
+    capsys.readouterr()
+    assert V.main(["--task", "harness_eval", "--criterion", "harness_eval", "--eval-data", "harness_boolq",
+                   "--data-dir", str(tmp_path / "h"), "--batch-size", "2", "--tokens-per-sample", "128", *small]) == 0
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert "accuracy" in res
