@@ -105,7 +105,7 @@ def main():
         res["p2p_reduce_owner_ms"] = _time(
             lambda: comm.reduce_to_owner(g, seg), a.iters)
         for k in list(res):
-            if k.endswith("_ms"):
+            if k.endswith("_ms") or "_ms_c" in k:
                 res[k.replace("_ms", "_gbs")] = recv_gb / (res[k] / 1e3)
                 res[k.replace("_ms", "_frac")] = res[k.replace("_ms", "_gbs")] / LINK_GBS
         if rank == 0:
