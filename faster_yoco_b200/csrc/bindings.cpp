@@ -31,6 +31,9 @@ at::Tensor ce_bwd(const at::Tensor& logits, const at::Tensor& target, const at::
 void adam_step(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor& v, at::Tensor& p16,
                const at::Tensor& hyper, const at::Tensor& factor, double b1, double b2, double eps, double wd,
                bool adamw);
+void adam_push(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor& v, at::Tensor& p16,
+               const at::Tensor& hyper, const at::Tensor& factor, double b1, double b2, double eps, double wd,
+               bool adamw, const std::vector<int64_t>& peer_params, int64_t peer_off, int64_t rank);
 at::Tensor sq_norm(const at::Tensor& x);
 std::vector<at::Tensor> attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, bool causal,
                                       int64_t window, double scale);
@@ -124,6 +127,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_bwd", &fyb::ce_bwd, py::arg("logits"), py::arg("target"), py::arg("lse"), py::arg("grad"),
         py::arg("ignore"), py::arg("out") = py::none());
   m.def("adam_step", &fyb::adam_step);
+  m.def("adam_push", &fyb::adam_push, "Adam on this owner's segment fused with its all-gather push to every peer");
   m.def("sq_norm", &fyb::sq_norm);
   m.def("attention_fwd", &fyb::attention_fwd);
   m.def("attention_bwd", &fyb::attention_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),

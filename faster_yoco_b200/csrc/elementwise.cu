@@ -335,6 +335,77 @@ __global__ void adam_kernel(float* __restrict__ p32, const __nv_bfloat16* __rest
   }
 }
 
+// Adam fused with the ZeRO parameter all-gather: the owner updates its segment (the expression of adam_kernel,
+// 8 elements per thread) and stores each 16-byte group of new bf16 parameters into its own flat buffer AND into every
+// peer's flat buffer at the same offset (remote stores over NVLink into CUDA-IPC mapped memory), so the exchange
+// streams out while the HBM-bound update runs instead of after it. A flag barrier after the kernel publishes the
+// stores; the system fence at the end orders them before it.
+struct PushTargets {
+  void* p[8];
+};
+
+__global__ void adam_push_kernel(float* __restrict__ p32, const __nv_bfloat16* __restrict__ g16,
+                                 float* __restrict__ m, float* __restrict__ v, __nv_bfloat16* __restrict__ p16,
+                                 const float* __restrict__ hyper, const float* __restrict__ factor, int64_t n,
+                                 float b1, float b2, float eps, float wd, bool adamw, PushTargets peers,
+                                 int64_t peer_off, int world, int rank) {
+  const float lr = hyper[0], bc1 = hyper[1], bc2 = hyper[2];
+  const float f = factor[0];
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 8;
+  for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < n; i += stride) {
+    if (i + 8 <= n) {
+      float P[8], Mv[8], Vv[8], G[8];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float4 a = *reinterpret_cast<const float4*>(p32 + i + 4 * h);
+        const float4 b = *reinterpret_cast<const float4*>(m + i + 4 * h);
+        const float4 c = *reinterpret_cast<const float4*>(v + i + 4 * h);
+        P[4 * h] = a.x, P[4 * h + 1] = a.y, P[4 * h + 2] = a.z, P[4 * h + 3] = a.w;
+        Mv[4 * h] = b.x, Mv[4 * h + 1] = b.y, Mv[4 * h + 2] = b.z, Mv[4 * h + 3] = b.w;
+        Vv[4 * h] = c.x, Vv[4 * h + 1] = c.y, Vv[4 * h + 2] = c.z, Vv[4 * h + 3] = c.w;
+      }
+      {
+        const uint4 gu = *reinterpret_cast<const uint4*>(g16 + i);
+        const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 t = unpack_bf16(gw[k]);
+          G[2 * k] = t.x;
+          G[2 * k + 1] = t.y;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) adam_elem(P[k], Mv[k], Vv[k], G[k] * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        *reinterpret_cast<float4*>(p32 + i + 4 * h) = make_float4(P[4 * h], P[4 * h + 1], P[4 * h + 2], P[4 * h + 3]);
+        *reinterpret_cast<float4*>(m + i + 4 * h) = make_float4(Mv[4 * h], Mv[4 * h + 1], Mv[4 * h + 2], Mv[4 * h + 3]);
+        *reinterpret_cast<float4*>(v + i + 4 * h) = make_float4(Vv[4 * h], Vv[4 * h + 1], Vv[4 * h + 2], Vv[4 * h + 3]);
+      }
+      const uint4 out = make_uint4(pack_bf16(P[0], P[1]), pack_bf16(P[2], P[3]), pack_bf16(P[4], P[5]),
+                                   pack_bf16(P[6], P[7]));
+      *reinterpret_cast<uint4*>(p16 + i) = out;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (q < world && q != rank)
+          *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers.p[q]) + peer_off + i) = out;
+    } else {
+      for (int64_t j = i; j < n; ++j) {
+        float P = p32[j], Mv = m[j], Vv = v[j];
+        adam_elem(P, Mv, Vv, __bfloat162float(g16[j]) * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
+        p32[j] = P;
+        m[j] = Mv;
+        v[j] = Vv;
+        const __nv_bfloat16 o = __float2bfloat16_rn(P);
+        p16[j] = o;
+        for (int q = 0; q < world; ++q)
+          if (q != rank) reinterpret_cast<__nv_bfloat16*>(peers.p[q])[peer_off + j] = o;
+      }
+    }
+  }
+  __threadfence_system();
+}
+
 // ------------------------------------------------------------------------------------------------------------------
 // sum of squares of a bf16 vector: per-CTA fp32 partials, then one CTA sums them in a fixed order
 
@@ -680,6 +751,39 @@ void adam_step(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor
       v.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(p16.data_ptr()), hyper.data_ptr<float>(),
       factor.data_ptr<float>(), n, (float)b1, (float)b2, (float)eps, (float)wd, adamw);
   check_launch("adam");
+}
+
+void adam_push(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor& v, at::Tensor& p16,
+               const at::Tensor& hyper, const at::Tensor& factor, double b1, double b2, double eps, double wd,
+               bool adamw, const std::vector<int64_t>& peer_params, int64_t peer_off, int64_t rank) {
+  FYB_RANGE("fyb::adam_push");
+  const int64_t n = p32.numel();
+  const int world = static_cast<int>(peer_params.size());
+  FYB_CHECK(world >= 1 && world <= 8 && rank >= 0 && rank < world, "adam_push: 1..8 ranks");
+  FYB_CHECK(p32.is_contiguous() && m.is_contiguous() && v.is_contiguous() && g16.is_contiguous() &&
+                p16.is_contiguous() && g16.numel() == n && m.numel() == n && v.numel() == n && p16.numel() == n,
+            "adam_push: contiguous tensors of equal size expected");
+  FYB_CHECK(p32.scalar_type() == at::kFloat && g16.scalar_type() == at::kBFloat16 &&
+                p16.scalar_type() == at::kBFloat16,
+            "adam_push: fp32 master / bf16 grad / bf16 param");
+  FYB_CHECK(reinterpret_cast<uintptr_t>(g16.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(p16.data_ptr()) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(p32.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(m.data_ptr()) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(v.data_ptr()) % 16 == 0 && peer_off % 8 == 0,
+            "adam_push: 16-byte aligned buffers and a segment offset that is a multiple of 8 elements");
+  PushTargets t{};
+  for (int q = 0; q < world; ++q) {
+    FYB_CHECK(peer_params[q] % 16 == 0, "adam_push: peer buffers must be 16-byte aligned");
+    t.p[q] = reinterpret_cast<void*>(peer_params[q]);
+  }
+  c10::cuda::CUDAGuard guard(p32.device());
+  if (n == 0) return;
+  const int blocks = static_cast<int>(std::min<int64_t>((n / 8 + 255) / 256 + 1, num_sms() * 8));
+  adam_push_kernel<<<blocks, 256, 0, cur_stream()>>>(
+      p32.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(g16.data_ptr()), m.data_ptr<float>(),
+      v.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(p16.data_ptr()), hyper.data_ptr<float>(),
+      factor.data_ptr<float>(), n, (float)b1, (float)b2, (float)eps, (float)wd, adamw, t, peer_off,
+      world, static_cast<int>(rank));
+  check_launch("adam_push");
 }
 
 int sq_norm_ctas(int64_t n) { return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n + 4095) / 4096, 1024))); }

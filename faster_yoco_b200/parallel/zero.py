@@ -201,6 +201,10 @@ class ZeroOptimizer:
         self.hyper = torch.zeros(4, dtype=torch.float32, device=dev)
         self._hyper_host = torch.zeros(4, dtype=torch.float32, pin_memory=dev.type == "cuda")
         self.p2p = None
+        # serial peer-memory exchange: Adam and the all-gather push as one kernel (FYB_FUSE_ADAM_PUSH=0 runs them
+        # as two passes, Adam then push_range, for comparison)
+        import os
+        self.fuse_adam_push = os.environ.get("FYB_FUSE_ADAM_PUSH", "1") != "0"
         self.last_grad_norm = None
 
     # ---------------------------------------------------------------------------------------------------------
@@ -273,13 +277,23 @@ class ZeroOptimizer:
             factor = factor * (clip / (grad_norm + 1e-6)).clamp(max=1.0)
         b1, b2 = self.cfg.betas
         seg = fp.param_segment()
-        if native:
+        fused_push = (native and fp.world > 1 and self.comm == "fused" and self.p2p is not None
+                      and self.p2p.buckets is None and self.fuse_adam_push)
+        if fused_push:
+            # one pass: Adam on this owner's segment + the all-gather push of its new bf16 values to every peer
+            ops._C().adam_push(self.master, g16, self.exp_avg, self.exp_avg_sq, seg, self.hyper,
+                               factor.reshape(1).float().contiguous(), float(b1), float(b2), float(self.cfg.eps),
+                               float(self.cfg.weight_decay), bool(self.cfg.adamw_mode), self.p2p.peers["param"],
+                               fp.owned().start, fp.rank)
+            self.p2p.barrier()
+        elif native:
             ops._C().adam_step(self.master, g16, self.exp_avg, self.exp_avg_sq, seg, self.hyper,
                                factor.reshape(1).float().contiguous(), float(b1), float(b2), float(self.cfg.eps),
                                float(self.cfg.weight_decay), bool(self.cfg.adamw_mode))
         else:
             self._torch_adam(g16, seg, factor, self._lr)
-        self.all_gather_params()
+        if not fused_push:
+            self.all_gather_params()
         self.last_grad_norm = grad_norm
         return grad_norm
 

@@ -96,9 +96,11 @@ def fused_vs_nccl_gpu(rank, world, outdir, steps):
     for name, comm, overlap, transport, graph in (
             ("nccl", "nccl", False, "sm", False), ("fused", "fused", True, "sm", False),
             ("fused_serial", "fused", False, "sm", False), ("fused_ce", "fused", True, "ce", False),
-            ("fused_ce_graph", "fused", True, "ce", True)):
+            ("fused_ce_graph", "fused", True, "ce", True), ("fused_serial_two_pass", "fused", False, "sm", False)):
         model, tr = _tiny_trainer(dev, comm=comm, arch="yoco_small", dtype=torch.bfloat16, overlap=overlap,
                                   transport=transport, graph=graph)
+        # the serial variants differ only in Adam + all-gather: one fused kernel, or Adam then the push kernel
+        tr.zero.fuse_adam_push = name != "fused_serial_two_pass"
         losses = []
         for ids in _batches(rank, world, steps, seq=256, vocab=8192):
             mine = ids[rank]
