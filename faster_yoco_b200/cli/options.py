@@ -108,6 +108,10 @@ def train_parser() -> argparse.ArgumentParser:
     g.add_argument("--reset-optimizer", action="store_true")
     g.add_argument("--reset-dataloader", action="store_true")
     g.add_argument("--disable-validation", action="store_true")
+    g.add_argument("--validate-interval-updates", type=int, default=0,
+                   help="evaluate the valid subset every N updates (0: only after the last update)")
+    g.add_argument("--valid-subset", default="valid")
+    g.add_argument("--max-valid-steps", type=int, default=100)
     g.add_argument("--save-model-only", action="store_true",
                    help="paired-validation saves: bf16 model state dict model_<update>.pt on rank 0 (no optimizer "
                         "state) at every save point, plus each rank's peak memory as a VALIDATION_MEM line")

@@ -15,6 +15,7 @@ from __future__ import annotations
 import os
 import sys
 import time
+from typing import Optional
 
 import torch
 import torch.distributed as dist
@@ -57,6 +58,42 @@ def _save_model_only(args, model, nu: int, rank: int):
         torch.save({"model": sd, "num_updates": nu}, path + ".tmp")
         os.replace(path + ".tmp", path)
         print(f"VALIDATION_CKPT {path} {time.time() - t0:.1f}s", flush=True)
+
+
+def validate_lm(model, task, args, device, rank: int, world: int) -> Optional[dict]:
+    """Mean next-token loss (bits) over up to --max-valid-steps batches of the valid subset, summed over ranks
+    (fairseq's validation pass of the training loop; no gradients, the module path of the model)."""
+    import math
+    from .. import ops
+    try:
+        ds = task.load_dataset(args.valid_subset)
+    except (FileNotFoundError, KeyError):
+        return None
+    if not getattr(ds, "data", None):
+        return None                       # an empty source list (the reference corpus layout has one)
+    itr = task.get_batch_iterator(ds, max_sentences=args.batch_size, seed=args.seed, num_shards=world,
+                                  shard_id=rank, prefetch=0)
+    was_training = model.training
+    model.eval()
+    tot = torch.zeros(2, dtype=torch.float64, device=device)
+    with torch.no_grad():
+        for _ in range(args.max_valid_steps):
+            try:
+                b = next(itr)
+            except StopIteration:
+                break
+            src, tgt = b["src_tokens"].to(device), b["target"].to(device)
+            logits, _ = model(src)
+            loss = ops.cross_entropy(logits.reshape(-1, logits.shape[-1]), tgt.reshape(-1), task.tokenizer.pad_id)
+            tot += torch.stack([loss.double().reshape(()),
+                                torch.tensor(float(b["ntokens"]), dtype=torch.float64, device=device)])
+    if hasattr(itr, "close"):
+        itr.close()
+    if D.is_dist():
+        dist.all_reduce(tot)
+    model.train(was_training)
+    bits = float(tot[0] / tot[1].clamp_min(1)) / math.log(2)
+    return {"loss": round(bits, 3), "ppl": round(2 ** bits, 2), "ntokens": int(tot[1])}
 
 
 def main(argv=None) -> int:
@@ -103,6 +140,12 @@ def main(argv=None) -> int:
             stats["train_wall"] = round(time.perf_counter() - t_start, 1)
             if rank == 0:
                 print(format_log(stats), flush=True)
+        if (not args.disable_validation and args.validate_interval_updates > 0
+                and nu % args.validate_interval_updates == 0):
+            v = validate_lm(model, task, args, device, rank, world)
+            if v is not None and rank == 0:
+                print(f"valid on '{args.valid_subset}' subset | loss {v['loss']} | ppl {v['ppl']} | "
+                      f"num_updates {nu}", flush=True)
         if args.save_model_only and args.save_interval_updates > 0 and nu % args.save_interval_updates == 0:
             _save_model_only(args, model, nu, rank)
         elif not args.no_save and args.save_interval_updates > 0 and nu % args.save_interval_updates == 0:
@@ -114,6 +157,11 @@ def main(argv=None) -> int:
                 shutil.copyfile(os.path.join(args.save_dir, f"checkpoint_1_{nu}.pt"),
                                 os.path.join(args.save_dir, "checkpoint_last.pt"))
     trainer.pending.check(block=True)
+    if not args.disable_validation and args.validate_interval_updates <= 0:
+        v = validate_lm(model, task, args, device, rank, world)
+        if v is not None and rank == 0:
+            print(f"valid on '{args.valid_subset}' subset | loss {v['loss']} | ppl {v['ppl']} | "
+                  f"num_updates {trainer.num_updates()}", flush=True)
     if args.save_model_only:
         _save_model_only(args, model, trainer.num_updates(), rank)
     elif not args.no_save:

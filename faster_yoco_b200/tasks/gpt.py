@@ -14,6 +14,8 @@ from .base import Task, TaskConfig
 @register_task("gpt")
 class GPTPretrainingTask(Task):
     def load_dataset(self, split: str, epoch: int = 1, combine: bool = False, **kwargs):
+        if self.cfg.data is None:
+            raise FileNotFoundError("no data directory given")
         with open(os.path.join(self.cfg.data, "json", f"{split}.json")) as f:
             data = json.load(f)
         self.datasets[split] = SimpleNamespace(data=data, data_dir=self.cfg.data, shuffle=split == "train")

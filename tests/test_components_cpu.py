@@ -279,6 +279,19 @@ def _corpus(root):
     json.dump([{"name": "web", "weight": 1.0}], open(os.path.join(root, "json", "train.json"), "w"))
 
 
+def test_cli_train_validation_pass(tmp_path, capsys):
+    from faster_yoco_b200.cli import train as T
+    data = str(tmp_path / "data")
+    _corpus(data)
+    json.dump([{"name": "web", "weight": 1.0}], open(os.path.join(data, "json", "valid.json"), "w"))
+    assert T.main([data, "--arch", "yoco_tiny", "--n-layers", "2", "--task", "gpt", "--tiktoken-model", "byte",
+                   "--tokens-per-sample", "64", "--batch-size", "2", "--pad-to-max-len", "--batch-read-ahead", "4",
+                   "--log-interval", "2", "--validate-interval-updates", "2", "--max-valid-steps", "3",
+                   "--max-update", "4", "--no-save", "--cpu", "--kernels", "torch"]) == 0
+    lines = [l for l in capsys.readouterr().out.splitlines() if l.startswith("valid on 'valid' subset")]
+    assert len(lines) == 2 and "num_updates 4" in lines[-1]
+
+
 def test_cli_train_save_resume(tmp_path, capsys):
     from faster_yoco_b200.cli import train as T
     data = str(tmp_path / "data")
