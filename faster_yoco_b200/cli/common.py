@@ -23,6 +23,11 @@ def setup_runtime(args):
     if args.model_parallel_size > 1:
         from ..parallel import tp
         tp.init_model_parallel(args.model_parallel_size)
+    if getattr(args, "context_parallel_size", 1) > 1:
+        if args.model_parallel_size > 1:
+            raise SystemExit("context and tensor parallelism together are not supported")
+        from ..parallel import context
+        context.init_context_parallel(args.context_parallel_size)
     return device
 
 

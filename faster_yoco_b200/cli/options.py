@@ -30,6 +30,8 @@ def add_common(p: argparse.ArgumentParser):
     g.add_argument("--load-ckpt", default=None)
     g.add_argument("--batch-size", type=int, default=1)
     g.add_argument("--model-parallel-size", type=int, default=1)
+    g.add_argument("--context-parallel-size", type=int, default=1,
+                   help="split every sequence into this many contiguous blocks, one per rank (YOCO)")
     g.add_argument("--seed", type=int, default=1)
     g.add_argument("--bf16", action="store_true")
     g.add_argument("--fp16", action="store_true")

@@ -29,6 +29,22 @@ from .common import build_model, build_task, setup_runtime
 from .options import parse_with_preset, train_parser
 
 
+def _cp_slice(batch, cp: int):
+    """This rank's contiguous block of every sequence under context parallelism; the token count (the gradient
+    normaliser, summed over all ranks) is split so that the blocks of a sequence add up to its count."""
+    if cp <= 1:
+        return batch
+    from ..parallel import context as CP
+    r = CP.cp_rank()
+    L = batch["src_tokens"].shape[1] // cp
+    out = dict(batch)
+    out["src_tokens"] = batch["src_tokens"][:, r * L:(r + 1) * L].contiguous()
+    out["target"] = batch["target"][:, r * L:(r + 1) * L].contiguous()
+    n = int(batch["ntokens"])
+    out["ntokens"] = n // cp + (n % cp if r == cp - 1 else 0)
+    return out
+
+
 def _flag(v) -> bool:
     return str(v).lower() in ("1", "true", "yes", "on")
 
@@ -109,13 +125,21 @@ def main(argv=None) -> int:
                         clip_norm=args.clip_norm, warmup_updates=args.warmup_updates,
                         total_num_update=args.total_num_update, end_learning_rate=args.end_learning_rate,
                         power=args.power)
-    comm = args.comm if (world > 1 and device.type == "cuda") else "nccl"
+    comm = args.comm if (world > 1 and device.type == "cuda" and args.context_parallel_size == 1) else "nccl"
     overlap = (world == 2 and comm == "fused") if str(args.overlap) == "auto" else bool(_flag(args.overlap))
     transport = ("ce" if world == 2 else "sm") if args.transport == "auto" else args.transport
-    trainer = Trainer(model, optim, device=device, comm=comm, graph_step=bool(args.cuda_graph) and device.type == "cuda",
+    graph = bool(args.cuda_graph) and device.type == "cuda" and args.context_parallel_size == 1
+    trainer = Trainer(model, optim, device=device, comm=comm, graph_step=graph,
                       overlap=overlap, transport=transport, partition=args.partition, pad_idx=task.tokenizer.pad_id)
-    itr = task.get_batch_iterator(ds, max_sentences=args.batch_size, seed=args.seed, num_shards=world,
-                                  shard_id=rank)
+    cp = args.context_parallel_size
+    if cp > 1:
+        if family != "yoco":
+            raise SystemExit("context parallelism is implemented for YOCO")
+        if args.tokens_per_sample % cp:
+            raise SystemExit("--tokens-per-sample must be divisible by --context-parallel-size")
+    # data shards are per data-parallel replica; the ranks of one context-parallel group read the same batches
+    itr = task.get_batch_iterator(ds, max_sentences=args.batch_size, seed=args.seed, num_shards=world // cp,
+                                  shard_id=rank // cp)
     restore = os.path.join(args.save_dir, args.restore_file)
     if os.path.exists(restore) and not args.reset_optimizer:
         ck = load_checkpoint(restore, model, trainer)
@@ -130,7 +154,7 @@ def main(argv=None) -> int:
 
     t_start = time.perf_counter()
     while args.max_update <= 0 or trainer.num_updates() < args.max_update:
-        batches = [next(itr) for _ in range(args.update_freq)]
+        batches = [_cp_slice(next(itr), cp) for _ in range(args.update_freq)]
         trainer.train_step(batches if args.update_freq > 1 else batches[0])
         nu = trainer.num_updates()
         if nu % args.log_interval == 0:

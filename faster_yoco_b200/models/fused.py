@@ -256,6 +256,7 @@ class SharedKVFn(torch.autograd.Function):
 
 
 def fused_path_ok(x: torch.Tensor, head_dim: int) -> bool:
+    from ..parallel import context as CP
     from ..parallel import tp as TP
     return (ops.native_on(x) and torch.is_grad_enabled() and head_dim == 128 and x.dtype == torch.bfloat16
-            and TP.tp_size() == 1)
+            and TP.tp_size() == 1 and CP.cp_size() == 1)

@@ -27,6 +27,7 @@ import torch
 import torch.nn as nn
 
 from .. import ops
+from ..parallel import context as CP
 from ..parallel import tp as TP
 from . import init as I
 
@@ -207,6 +208,10 @@ class GateRetention(nn.Module):
             o = self._prefill(q, k, v, gt, incremental_state)
         else:
             o = ops.retention(q, k, v, gt, chunk_size=self.args.chunk_size)      # [B, L, H, D]
+            if CP.cp_size() > 1:       # state carried in from the earlier sequence blocks of the group
+                carry = CP.retention_carry(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                           gt.transpose(1, 2))
+                o = o + carry.transpose(1, 2).to(o.dtype)
         o = ops.subln_swiglu(o.reshape(B * L, H * D), g.reshape(B * L, H * D), self.subln_eps, D)
         o = o.view(B, L, H * D)
         return self.out_proj(o, residual)
@@ -272,6 +277,9 @@ class SlidingWindowAttention(nn.Module):
             st["prev_value"][:B, :keep] = value[:, -keep:]
             st["filled"] = keep
             o = ops.ref.attention(q, key, value, causal=True, window=w, q_offset=key.shape[1] - L)
+        elif CP.cp_size() > 1:
+            kk, vv = CP.gather_seq(k, 1), CP.gather_seq(v, 1)
+            o = ops.ref.attention(q, kk, vv, causal=True, window=self.window_size, q_offset=CP.cp_rank() * L)
         else:
             o = ops.attention(q, k, v, causal=True, window=self.window_size)
         return self.out_proj(o.reshape(B, L, H * D), residual)
@@ -293,6 +301,8 @@ class CrossAttention(nn.Module):
     def forward(self, x, key, value, rel_pos, residual=None, q_offset: Optional[int] = None):
         B, L, _ = x.shape
         q = ops.rope(self.q_proj(TP.copy_to_tp(x)).view(B, L, self.num_heads, self.head_dim), *rel_pos)
+        if q_offset is None and CP.cp_size() > 1 and key.shape[1] == CP.cp_size() * L:
+            q_offset = CP.cp_rank() * L              # this rank's block inside the gathered sequence
         if key.shape[1] != L:
             off = key.shape[1] - L if q_offset is None else q_offset
             o = ops.ref.attention(q, key, value, causal=True, q_offset=off)

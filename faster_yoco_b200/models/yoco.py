@@ -19,6 +19,7 @@ import torch.nn.functional as F
 
 from .. import ops
 from ..config import YOCOArgs
+from ..parallel import context as CP
 from ..parallel import tp as TP
 from . import init as I
 from .layers import (CrossAttention, FeedForwardNetwork, GateRetention, Linear, MergedLinear, RMSNorm,
@@ -117,12 +118,15 @@ class SelfDecoder(nn.Module):
 
     def forward(self, x, incremental_state=None, is_prefilling=False, start_pos=0, comm_hooks=None, bucket0=1):
         pad = 0
-        if is_prefilling and x.size(1) % self.block_size != 0 and self.args.sliding_window is None:
+        cp = CP.cp_size() > 1 and incremental_state is None
+        if is_prefilling and x.size(1) % self.block_size != 0 and self.args.sliding_window is None and not cp:
             pad = self.block_size - x.size(1) % self.block_size
             x = F.pad(x, (0, 0, 0, pad), value=0)
         index_mask = None
         if incremental_state is not None and is_prefilling:
             index_mask = torch.arange(x.size(1), device=x.device) >= (x.size(1) - pad)
+        if cp:
+            start_pos = start_pos + CP.cp_rank() * x.size(1)      # absolute positions of this rank's block
         rel_pos = self.rope.get(start_pos, x.size(1), x.dtype, x.device)
         for idx, layer in enumerate(self.layers):
             if comm_hooks is not None:
@@ -179,7 +183,12 @@ class CrossDecoder(nn.Module):
             if x.requires_grad:
                 x.register_hook(lambda g: (comm_hooks.ready(bucket0 + 1), comm_hooks.ready(bucket0)) and None)
         fused = incremental_state is None and self.training and fused_path_ok(x, self.head_dim)
+        cp = CP.cp_size() > 1 and incremental_state is None
+        if cp:
+            start_pos = start_pos + CP.cp_rank() * seqlen
         key, value, rel_pos = self.shared_kv(x, start_pos, fused=fused)
+        if cp:                                   # the one shared K / V over the whole sequence, for every layer
+            key, value = CP.gather_seq(key, 1), CP.gather_seq(value, 1)
         if incremental_state is not None:
             st = incremental_state
             if "prev_key" not in st:

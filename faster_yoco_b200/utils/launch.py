@@ -31,7 +31,8 @@ def _entry(rank, world, port, backend, fn, args, errq, timeout_s):
         dist.init_process_group(backend, rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=timeout_s), **kw)
         fn(rank, world, *args)
-        dist.barrier()
+        if dist.is_initialized():          # fn may have torn the group down itself (the CLI entry points do)
+            dist.barrier()
     except Exception:
         errq.put((rank, traceback.format_exc()))
         raise
