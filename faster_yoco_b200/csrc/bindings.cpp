@@ -59,8 +59,6 @@ void reduce_owner(const std::vector<int64_t>& peer_grads, at::Tensor& out, int64
                   at::Tensor& sq);
 void gather_segments(const std::vector<int64_t>& peer_params, at::Tensor& dst, const at::Tensor& segs, int64_t rank,
                      int64_t ctas);
-void reduce_ranges(const std::vector<int64_t>& peer_grads, at::Tensor& out, const at::Tensor& ranges, at::Tensor& part,
-                   int64_t ctas);
 void sum_partials(const at::Tensor& part, at::Tensor& out);
 void push_bucket(const at::Tensor& src, const std::vector<int64_t>& peer_dst, const std::vector<int64_t>& peer_arrive,
                  const at::Tensor& ranges, int64_t bucket, int64_t rank, int64_t ctas);
@@ -145,7 +143,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flag_barrier", &fyb::flag_barrier);
   m.def("reduce_owner", &fyb::reduce_owner);
   m.def("gather_segments", &fyb::gather_segments);
-  m.def("reduce_ranges", &fyb::reduce_ranges);
   m.def("sum_partials", &fyb::sum_partials);
   m.def("push_range", &fyb::push_range);
   m.def("push_bucket", &fyb::push_bucket);

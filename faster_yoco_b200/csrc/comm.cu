@@ -130,67 +130,6 @@ __global__ void reduce_owner_kernel(PeerPtrs grads, __nv_bfloat16* out, int64_t 
   }
 }
 
-// owner-side reduction over a list of ranges [n][2] = (element offset, count) of the flat gradient buffers (ranges
-// that this rank owns); same arithmetic as reduce_owner_kernel; per-CTA partial sums of squares in part[blockIdx.x]
-__global__ void reduce_ranges_kernel(PeerPtrs grads, __nv_bfloat16* out, const int64_t* __restrict__ ranges,
-                                     int nranges, int world, float inv_world, float* part) {
-  float ss = 0.f;
-  for (int rg = 0; rg < nranges; ++rg) {
-    const int64_t base = ranges[2 * rg], n = ranges[2 * rg + 1];
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 8;
-    for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < n; i += stride) {
-      if (i + 8 <= n) {
-        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        uint4 u[kMaxWorld];
-#pragma unroll
-        for (int r = 0; r < kMaxWorld; ++r)
-          if (r < world)
-            u[r] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(grads.p[r]) + base + i);
-#pragma unroll
-        for (int r = 0; r < kMaxWorld; ++r) {
-          if (r < world) {
-            const uint32_t w[4] = {u[r].x, u[r].y, u[r].z, u[r].w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 f = unpack_bf16(w[k]);
-              acc[2 * k] += f.x;
-              acc[2 * k + 1] += f.y;
-            }
-          }
-        }
-        uint32_t o[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float a = bf16_round(acc[2 * k] * inv_world), b = bf16_round(acc[2 * k + 1] * inv_world);
-          ss += a * a + b * b;
-          o[k] = pack_bf16(a, b);
-        }
-        *reinterpret_cast<uint4*>(out + base + i) = make_uint4(o[0], o[1], o[2], o[3]);
-      } else {
-        for (int64_t j = i; j < n; ++j) {
-          float acc = 0.f;
-#pragma unroll
-          for (int r = 0; r < kMaxWorld; ++r)
-            if (r < world) acc += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(grads.p[r])[base + j]);
-          const float a = bf16_round(acc * inv_world);
-          ss += a * a;
-          out[base + j] = __float2bfloat16_rn(a);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  __shared__ float red[32];
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.f;
-    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
-    part[blockIdx.x] = t;
-  }
-}
-
 __global__ void sum_partials_kernel(const float* __restrict__ part, int P, float* __restrict__ out) {
   __shared__ float red[1024];
   float s = 0.f;
@@ -495,23 +434,6 @@ void reduce_owner(const std::vector<int64_t>& peer_grads, at::Tensor& out, int64
 }
 
 // reduce the listed owned ranges; part (>= ctas floats) receives the per-CTA sums of squares
-void reduce_ranges(const std::vector<int64_t>& peer_grads, at::Tensor& out, const at::Tensor& ranges, at::Tensor& part,
-                   int64_t ctas) {
-  FYB_RANGE("fyb::reduce_ranges");
-  const int world = static_cast<int>(peer_grads.size());
-  FYB_CHECK(ranges.is_cuda() && ranges.scalar_type() == at::kLong && ranges.dim() == 2 && ranges.size(1) == 2,
-            "reduce_ranges: ranges must be a device int64 [n, 2]");
-  FYB_CHECK(part.numel() >= ctas && part.scalar_type() == at::kFloat, "reduce_ranges: partials buffer too small");
-  if (ranges.size(0) == 0) {
-    part.zero_();
-    return;
-  }
-  reduce_ranges_kernel<<<static_cast<int>(ctas), 256, 0, cur_stream()>>>(
-      to_ptrs(peer_grads), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), ranges.data_ptr<int64_t>(),
-      static_cast<int>(ranges.size(0)), world, 1.0f / static_cast<float>(world), part.data_ptr<float>());
-  check_launch("reduce_ranges");
-}
-
 void sum_partials(const at::Tensor& part, at::Tensor& out) {
   sum_partials_kernel<<<1, 1024, 0, cur_stream()>>>(part.data_ptr<float>(), static_cast<int>(part.numel()),
                                                    out.data_ptr<float>());

@@ -100,22 +100,6 @@ class PeerComm:
         self.C.push_range(flat, self.peers["param"], self.rank * seg, n, self.rank, sms)
         self.barrier()
 
-    def all_gather_pull(self, flat: torch.Tensor, seg: int, used: Optional[List[int]] = None):
-        """Pull form of the all-gather (kept for measurement: remote loads are latency-bound, ~200 GB/s here)."""
-        self.barrier()
-        key = (seg, tuple(used) if used else None)
-        segs = self._gather_segs.get(key)
-        if segs is None:
-            rows = [[r * seg, (used[r] if used else seg), r] for r in range(self.world) if r != self.rank]
-            segs = torch.tensor(rows, dtype=torch.int64, device=self.dev).view(-1, 3)
-            self._gather_segs[key] = segs
-        sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
-        self.C.gather_segments(self.peers["param"], flat, segs, self.rank, sms * 2)
-
-    def gather_ranges(self, flat: torch.Tensor, segs: torch.Tensor, ctas: int = 64):
-        """Pull explicit (offset, count, owner) ranges of the shared parameter buffer (per-layer prefetch)."""
-        self.C.gather_segments(self.peers["param"], flat, segs, self.rank, ctas)
-
     def all_reduce_vector(self, v: torch.Tensor) -> torch.Tensor:
         """Sum of a small fp32 vector over ranks, rank order (returns a new tensor)."""
         v = v.reshape(-1).float().contiguous()
