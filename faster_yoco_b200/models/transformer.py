@@ -76,10 +76,17 @@ class Attention(nn.Module):
         else:
             st = incremental_state
             if self.window is None:
-                if "cache_k" not in st:
-                    shape = (max(self.args.max_batch_size, B), self.cache_len, self.n_kv_heads, self.head_dim)
-                    st["cache_k"] = torch.zeros(shape, dtype=k.dtype, device=k.device)
-                    st["cache_v"] = torch.zeros(shape, dtype=v.dtype, device=v.device)
+                need = start_pos + L
+                have = st["cache_k"].shape[1] if "cache_k" in st else 0
+                if need > have:             # max_seq_len positions, grown for longer prompts + generation
+                    size = max(self.cache_len, (need + 1023) // 1024 * 1024)
+                    shape = (max(self.args.max_batch_size, B), size, self.n_kv_heads, self.head_dim)
+                    nk = torch.zeros(shape, dtype=k.dtype, device=k.device)
+                    nv = torch.zeros(shape, dtype=v.dtype, device=v.device)
+                    if have:
+                        nk[:, :have] = st["cache_k"]
+                        nv[:, :have] = st["cache_v"]
+                    st["cache_k"], st["cache_v"] = nk, nv
                 st["cache_k"][:B, start_pos:start_pos + L] = k
                 st["cache_v"][:B, start_pos:start_pos + L] = v
                 key = st["cache_k"][:B, :start_pos + L]

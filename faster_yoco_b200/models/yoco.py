@@ -191,10 +191,19 @@ class CrossDecoder(nn.Module):
             key, value = CP.gather_seq(key, 1), CP.gather_seq(value, 1)
         if incremental_state is not None:
             st = incremental_state
-            if "prev_key" not in st:
-                shape = (bsz, self.args.max_seq_len, self.num_heads, self.head_dim)
-                st["prev_key"] = torch.empty(shape, device=x.device, dtype=x.dtype)
-                st["prev_value"] = torch.empty(shape, device=x.device, dtype=x.dtype)
+            need = start_pos + seqlen
+            have = st["prev_key"].shape[1] if "prev_key" in st else 0
+            if need > have:
+                # the shared KV cache holds max_seq_len positions; a longer prompt + generation grows it (the
+                # filled prefix is kept)
+                size = max(self.args.max_seq_len, (need + 1023) // 1024 * 1024)
+                shape = (bsz, size, self.num_heads, self.head_dim)
+                nk = torch.empty(shape, device=x.device, dtype=x.dtype)
+                nv = torch.empty(shape, device=x.device, dtype=x.dtype)
+                if have:
+                    nk[:, :have] = st["prev_key"]
+                    nv[:, :have] = st["prev_value"]
+                st["prev_key"], st["prev_value"] = nk, nv
             st["prev_key"][:, start_pos:start_pos + seqlen] = key
             st["prev_value"][:, start_pos:start_pos + seqlen] = value
             key = st["prev_key"][:, :start_pos + seqlen]

@@ -346,3 +346,16 @@ def test_cli_llama_train_and_harness(tmp_path, capsys):
                    "--data-dir", str(tmp_path / "h"), "--batch-size", "2", "--tokens-per-sample", "128", *small]) == 0
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert "accuracy" in res
+
+
+def test_cli_validate_needle(tmp_path, capsys):
+    from faster_yoco_b200.cli import validate as V
+    essays = tmp_path / "essays"
+    essays.mkdir()
+    (essays / "a.txt").write_text("\n".join(f"line {j} of an essay" for j in range(60)))
+    assert V.main(["--task", "pseudo", "--criterion", "needle_haystack", "--batch-size", "1", "--arch", "yoco_tiny",
+                   "--n-layers", "2", "--tiktoken-model", "byte", "--tokens-per-sample", "256", "--interval", "256",
+                   "--needle-file-path", str(essays), "--cpu", "--kernels", "torch"]) == 0
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    ret = res["retrieval"][0]
+    assert list(ret) == ["256"] or list(ret) == [256]
