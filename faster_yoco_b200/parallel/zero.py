@@ -1,10 +1,12 @@
 """ZeRO-1 / ZeRO-2 data parallelism over one flat, owner-partitioned parameter buffer.
 
-Partition: fairscale OSS's greedy rule -- parameters in model order, each to the rank with the smallest running
-element total (yoco/tasks/zero1_fast.py:52-75 replicates it for the reference's fast path). Every rank holds the same
-layout: ``flat[r*seg:(r+1)*seg]`` is owner r's segment, each parameter a view at a 128-byte aligned offset. Gradients
-live in a second buffer with the same layout, so "reduce to owner" is a reduce-scatter of equal segments, and the
-parameter exchange after the step is an all-gather of equal segments (in place).
+Partition (``FlatParams(partition=...)``): "even" (default) cuts the model-ordered flat buffer into equal contiguous
+segments, so every owner sends and receives the same bytes; "greedy" is fairscale OSS's rule -- whole parameters in
+model order, each to the rank with the smallest running element total (yoco/tasks/zero1_fast.py:52-75 replicates it
+for the reference's fast path). Every rank holds the same layout: ``flat[r*seg:(r+1)*seg]`` is owner r's segment,
+each parameter a view at a 128-byte aligned offset. Gradients live in a second buffer with the same layout, so
+"reduce to owner" is a reduce-scatter of equal segments, and the parameter exchange after the step is an all-gather
+of equal segments (in place).
 
 Per update (reference call stack yoco/tasks/trainer_nosync.py:219-305 and zero1_fast.py:139-235):
 
@@ -14,11 +16,13 @@ Per update (reference call stack yoco/tasks/trainer_nosync.py:219-305 and zero1_
    all-reduce); ``factor *= min(1, clip / (norm + 1e-6))``;
 3. the owner runs Adam on its FP32 master shard with ``g32 = float(g16) * factor`` and writes the BF16 parameter into
    its segment;
-4. every rank receives every segment (all-gather).
+4. every rank receives every segment (all-gather: NCCL, or -- ``fused`` -- the same kernel as step 3 also stores each
+   new BF16 value into every peer's buffer over NVLink, or per-layer pushes overlapped with the next forward).
 """
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence
 
@@ -203,7 +207,6 @@ class ZeroOptimizer:
         self.p2p = None
         # serial peer-memory exchange: Adam and the all-gather push as one kernel (FYB_FUSE_ADAM_PUSH=0 runs them
         # as two passes, Adam then push_range, for comparison)
-        import os
         self.fuse_adam_push = os.environ.get("FYB_FUSE_ADAM_PUSH", "1") != "0"
         self.last_grad_norm = None
 
@@ -233,7 +236,7 @@ class ZeroOptimizer:
             return
         if self.comm == "fused" and self.p2p is not None:
             if self.p2p.buckets is not None:
-                return          # pulled bucket by bucket at the start of the next update (overlapped)
+                return          # pushed bucket by bucket ahead of the next update's forward (overlapped)
             self.p2p.all_gather(fp.flat, fp.seg, fp.used)
             return
         dist.all_gather_into_tensor(fp.flat, fp.param_segment(), group=self.group)
