@@ -214,6 +214,30 @@ class MultiplexIterator(CheckpointableIterator):
             s.setstate(state["sources"][i] if state else None)
 
 
+class ChainIterator(CheckpointableIterator):
+    """The items of each source in turn (evaluation passes over several sources)."""
+
+    def __init__(self, sources: List[CheckpointableIterator]):
+        self.sources = sources
+        self.setstate(None)
+
+    def __next__(self):
+        while self.i < len(self.sources):
+            try:
+                return next(self.sources[self.i])
+            except StopIteration:
+                self.i += 1
+        raise StopIteration
+
+    def getstate(self):
+        return {"i": self.i, "src": self.sources[self.i].getstate() if self.i < len(self.sources) else None}
+
+    def setstate(self, state):
+        self.i = state["i"] if state else 0
+        for j, src in enumerate(self.sources):
+            src.setstate(state["src"] if (state and j == self.i) else None)
+
+
 class RepeatIterator(CheckpointableIterator):
     """Restart the source when it is exhausted (the loader 'never ends'); state counts passes."""
 

@@ -80,7 +80,11 @@ def read_jsonl_samples(path: str, tokenizer, tokens_per_sample: int) -> List[Lis
 class LMLoader:
     def __init__(self, data: List[Dict], data_dir: str, tokenizer, *, tokens_per_sample: int, batch_size: int,
                  seed: int = 1, num_shards: int = 1, shard_id: int = 0, batch_read_ahead: int = 1000,
-                 pad_to_max_len: bool = True, epochs: int = 50, prefetch: int = 10, absolute_path: bool = False):
+                 pad_to_max_len: bool = True, epochs: int = 50, prefetch: int = 10, absolute_path: bool = False,
+                 endless: bool = True):
+        """endless=False (evaluation): one pass over the files in their listed order (no repetition, no shuffle),
+        then StopIteration."""
+        self.endless = endless
         self.data, self.data_dir, self.tok = data, data_dir, tokenizer
         self.tps, self.bsz, self.seed = tokens_per_sample, batch_size, str(seed)
         self.num_shards, self.shard_id = num_shards, shard_id
@@ -100,6 +104,8 @@ class LMLoader:
 
     def _lines(self, d: Dict):
         files = self._source_files(d)
+        if not self.endless:
+            return it.SelectManyIterator(it.chunked_source(list(files), self.num_shards, self.shard_id), self._read)
 
         def make(epoch: int):
             items = files * self.epochs
@@ -116,6 +122,8 @@ class LMLoader:
         sources = [self._lines(d) for d in self.data]
         if len(sources) == 1:
             lines = sources[0]
+        elif not self.endless:
+            lines = it.ChainIterator(sources)          # evaluation: every source once, in order
         else:
             weights = [float(d["weight"]) if "weight" in d else int(d["count"]) for d in self.data]
             lines = it.MultiplexIterator(it.WeightNoRandomStateIterator(weights, int(self.seed)), sources)

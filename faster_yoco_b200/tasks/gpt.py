@@ -29,4 +29,4 @@ class GPTPretrainingTask(Task):
                         shard_id=shard_id,
                         batch_read_ahead=self.cfg.batch_read_ahead if dataset.shuffle else 0,
                         pad_to_max_len=self.cfg.pad_to_max_len, prefetch=prefetch,
-                        absolute_path=self.cfg.absolute_path)
+                        absolute_path=self.cfg.absolute_path, endless=dataset.shuffle)

@@ -359,3 +359,15 @@ def test_cli_validate_needle(tmp_path, capsys):
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     ret = res["retrieval"][0]
     assert list(ret) == ["256"] or list(ret) == [256]
+
+
+def test_cli_validate_lm_perplexity(tmp_path, capsys):
+    from faster_yoco_b200.cli import validate as V
+    data = str(tmp_path / "data")
+    _corpus(data)
+    json.dump([{"name": "web", "weight": 1.0}], open(os.path.join(data, "json", "valid.json"), "w"))
+    assert V.main([data, "--task", "gpt", "--criterion", "cross_entropy", "--valid-subset", "valid", "--arch",
+                   "yoco_tiny", "--n-layers", "2", "--tiktoken-model", "byte", "--tokens-per-sample", "64",
+                   "--batch-size", "2", "--pad-to-max-len", "--cpu", "--kernels", "torch"]) == 0
+    res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert 0 < res["loss"] < 20 and res["ntokens"] > 0          # one finite pass over the valid split

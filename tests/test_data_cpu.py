@@ -94,3 +94,15 @@ def test_weight_and_index_iterators_resume():
     assert [next(ix) for _ in range(5)] == [0, 1, 2, 0, 1]
     ix.setstate({"n": 4})
     assert next(ix) == 1
+
+
+def test_loader_single_pass_for_evaluation(tmp_path):
+    _make_corpus(str(tmp_path), n_files=2, docs=10)
+    data = [{"name": "a", "weight": 0.5}, {"name": "b", "weight": 0.5}]
+    L = LMLoader(data, str(tmp_path), ByteTokenizer(), tokens_per_sample=64, batch_size=2, batch_read_ahead=0,
+                 prefetch=0, endless=False)
+    n = sum(1 for _ in L)
+    L2 = LMLoader(data, str(tmp_path), ByteTokenizer(), tokens_per_sample=64, batch_size=2, batch_read_ahead=0,
+                  prefetch=2, endless=False)
+    assert n > 0 and sum(1 for _ in L2) == n          # finite, and the same count with prefetching
+    L2.close()
