@@ -10,6 +10,7 @@
 #include <nvtx3/nvToolsExt.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -114,8 +115,23 @@ struct NvtxRange {
 };
 #define FYB_RANGE(name) ::fyb::NvtxRange fyb_nvtx_range_(name)
 
+// FYB_DEBUG_SYNC=1: synchronise the stream after every native launch (outside graph capture), so that an
+// asynchronous kernel error is reported by the op that caused it instead of a later, unrelated call.
+inline bool debug_sync() {
+  static const bool on = [] {
+    const char* e = std::getenv("FYB_DEBUG_SYNC");
+    return e != nullptr && e[0] == '1';
+  }();
+  return on;
+}
+
 inline void check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess && debug_sync()) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(cur_stream(), &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone)
+      e = cudaStreamSynchronize(cur_stream());
+  }
   if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
 }
 

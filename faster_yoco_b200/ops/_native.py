@@ -7,7 +7,6 @@ PyTorch expressions and the extension is never touched.
 from __future__ import annotations
 
 import importlib
-import os
 
 _C = None
 _ERR = None
@@ -53,6 +52,3 @@ def has(name: str) -> bool:
     m = load()
     return m is not None and hasattr(m, name)
 
-
-def debug_enabled() -> bool:
-    return os.environ.get("FYB_DEBUG_SYNC", "0") == "1"
