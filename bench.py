@@ -68,6 +68,28 @@ def reference_arm(args):
     return 0
 
 
+def nvml_handle(nv, props, index: int):
+    """NVML handle of the CUDA device with properties ``props``. NVML numbers every GPU of the machine and ignores
+    CUDA_VISIBLE_DEVICES, so the device is found by its UUID (then its PCI address); the CUDA index is used only
+    when neither is available and no device is hidden."""
+    uuid = getattr(props, "uuid", None)
+    if uuid is not None:
+        text = str(uuid)
+        try:
+            return nv.nvmlDeviceGetHandleByUUID(text if text.startswith("GPU-") else "GPU-" + text)
+        except Exception:
+            pass
+    if getattr(props, "pci_bus_id", None) is not None:
+        bus = "%08x:%02x:%02x.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
+        try:
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            pass
+    if os.environ.get("CUDA_VISIBLE_DEVICES") is None:
+        return nv.nvmlDeviceGetHandleByIndex(index)
+    raise RuntimeError("cannot map CUDA device %d to an NVML device" % index)
+
+
 class ClockSampler:
     """Samples SM clock / max clock / throttle reasons through NVML while the timed region runs."""
 
@@ -85,7 +107,7 @@ class ClockSampler:
             import pynvml
             pynvml.nvmlInit()
             self.nv = pynvml
-            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.h = nvml_handle(pynvml, torch.cuda.get_device_properties(index), index)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
             self.ok = True
         except Exception:
@@ -114,6 +136,19 @@ class ClockSampler:
             self.t.join()
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def merge_clocks(per_rank):
+    """One clock record for the job from every rank's samples: the median SM clock over ranks, each rank's median,
+    and the union of the throttle reasons any rank saw."""
+    meds = [c["sm_mhz"] for c in per_rank if c.get("sm_mhz") is not None]
+    reasons = sorted(set(r for c in per_rank for r in c.get("reasons", [])))
+    maxes = [c["sm_max_mhz"] for c in per_rank if c.get("sm_max_mhz") is not None]
+    out = {"sm_mhz": statistics.median(meds) if meds else None, "sm_max_mhz": max(maxes) if maxes else None,
+           "reasons": reasons, "samples": sum(c.get("samples", 0) for c in per_rank)}
+    if len(per_rank) > 1:
+        out["per_rank_sm_mhz"] = [c.get("sm_mhz") for c in per_rank]
+    return out
 
 
 def count_our_launches(step_fn) -> int:
@@ -185,7 +220,7 @@ def main():
     end.record()
     torch.cuda.synchronize()
     D.barrier()
-    clocks = sampler.stop()
+    clocks = merge_clocks(D.all_gather_object(sampler.stop()))
     ms = start.elapsed_time(end) / args.steps
     ms = D.all_reduce_max(ms, dev)
     tokens_per_update = args.batch * args.seq_len * world

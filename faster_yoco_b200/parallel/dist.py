@@ -68,6 +68,15 @@ def all_reduce_max(x: float, device=None) -> float:
     return float(t.item())
 
 
+def all_gather_object(obj) -> list:
+    """Every rank's ``obj`` (picklable), in rank order; ``[obj]`` without a process group."""
+    if not is_dist():
+        return [obj]
+    out = [None] * dist.get_world_size()
+    dist.all_gather_object(out, obj)
+    return out
+
+
 def destroy():
     if is_dist():
         dist.destroy_process_group()

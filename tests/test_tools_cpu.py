@@ -139,3 +139,67 @@ def test_parity_markov_data_and_criterion():
     assert r["windows"][0]["within_Y"] and r["within_2sigma_all"]
     curves["native_s1"] = [4.0] * 10
     assert not criterion(curves, [0, 5, 10])["windows"][0]["within_Y"]
+
+
+def _bench():
+    import importlib.util
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("fyb_bench", os.path.join(root, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+class _FakeNVML:
+    """Two NVML devices; the one the CUDA process sees is NVML device 1."""
+
+    def __init__(self, uuid_ok=True, pci_ok=True):
+        self.uuid_ok, self.pci_ok = uuid_ok, pci_ok
+
+    def nvmlDeviceGetHandleByUUID(self, u):
+        if not self.uuid_ok or u != "GPU-1234abcd-0000-0000-0000-000000000001":
+            raise RuntimeError("not found")
+        return "dev1"
+
+    def nvmlDeviceGetHandleByPciBusId(self, bus):
+        if not self.pci_ok or bus != "00000000:1b:00.0":
+            raise RuntimeError("not found")
+        return "dev1"
+
+    def nvmlDeviceGetHandleByIndex(self, i):
+        return "dev%d" % i
+
+
+class _Props:
+    uuid = "1234abcd-0000-0000-0000-000000000001"
+    pci_domain_id, pci_bus_id, pci_device_id = 0, 0x1B, 0
+
+
+def test_bench_clock_sampler_maps_visible_device(monkeypatch):
+    """The clock sampler must read the GPU that the process runs on, not NVML's device with the same index."""
+    bench = _bench()
+    monkeypatch.setenv("CUDA_VISIBLE_DEVICES", "1")
+    assert bench.nvml_handle(_FakeNVML(), _Props(), 0) == "dev1"
+    assert bench.nvml_handle(_FakeNVML(uuid_ok=False), _Props(), 0) == "dev1"
+    with pytest.raises(RuntimeError):
+        bench.nvml_handle(_FakeNVML(uuid_ok=False, pci_ok=False), _Props(), 0)
+    monkeypatch.delenv("CUDA_VISIBLE_DEVICES")
+    assert bench.nvml_handle(_FakeNVML(uuid_ok=False, pci_ok=False), _Props(), 0) == "dev0"
+
+
+def test_bench_reference_arm_line(capsys, monkeypatch):
+    bench = _bench()
+    monkeypatch.setenv("RANK", "0")
+    assert bench.reference_arm(None) == 0
+    line = json.loads(capsys.readouterr().out.strip())
+    assert line["impl"] == "reference" and line["unavailable"]
+
+
+def test_bench_merge_clocks():
+    bench = _bench()
+    one = {"sm_mhz": 1900, "sm_max_mhz": 1965, "reasons": ["sw_power_cap"], "samples": 10}
+    assert bench.merge_clocks([one])["sm_mhz"] == 1900 and "per_rank_sm_mhz" not in bench.merge_clocks([one])
+    two = {"sm_mhz": 1500, "sm_max_mhz": 1965, "reasons": ["hw_slowdown"], "samples": 9}
+    m = bench.merge_clocks([one, two, one])
+    assert m["sm_mhz"] == 1900 and m["per_rank_sm_mhz"] == [1900, 1500, 1900]
+    assert m["reasons"] == ["hw_slowdown", "sw_power_cap"] and m["samples"] == 29
