@@ -45,8 +45,10 @@ def parse():
                         "transport at 2 GPUs (one peer: the copy engines reach 766 GB/s and take no SM time), off "
                         "(serial P2P reduce + push all-gather after backward) at more GPUs, where the copy engines "
                         "deliver only ~210 GB/s in aggregate to 7 peers")
-    p.add_argument("--transport", default="auto", choices=["auto", "sm", "ce"],
-                   help="overlapped exchange: pushes by kernels (sm) or by the copy engines (ce)")
+    p.add_argument("--transport", default="auto", choices=["auto", "sm", "ce", "gemm"],
+                   help="overlapped exchange: pushes by kernels (sm) or by the copy engines (ce); gemm: serial "
+                        "schedule whose weight-gradient GEMMs store every element at its ZeRO owner over NVLink "
+                        "(GEMM fused with the reduce-scatter)")
     p.add_argument("--sliding-window", type=int, default=None)
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-e2e", action="store_true")
@@ -183,9 +185,11 @@ def main():
     dev = torch.device("cuda", dev_index)
     ops.set_backend(args.kernels)
     if args.overlap == "auto":
-        args.overlap = 1 if (world == 2 and args.comm == "fused") else 0
+        args.overlap = 1 if (world == 2 and args.comm == "fused" and args.transport != "gemm") else 0
     else:
         args.overlap = int(args.overlap)
+    if args.transport == "gemm" and args.overlap:
+        raise SystemExit("--transport gemm runs the serial exchange schedule (--overlap 0)")
     if args.transport == "auto":
         args.transport = "ce" if world == 2 else "sm"
     torch.manual_seed(1234)
@@ -267,7 +271,8 @@ def main():
                        "global_batch": args.batch * world, "seq_len": args.seq_len,
                        "tokens_per_update": tokens_per_update, "parallelism": f"dp{world}-zero1",
                        "kernels": args.kernels, "comm": args.comm, "cuda_graph": bool(args.graph),
-                       "comm_overlap": bool(args.overlap), "transport": args.transport if args.overlap else None,
+                       "comm_overlap": bool(args.overlap),
+                       "transport": args.transport if (args.overlap or args.transport == "gemm") else None,
                        "l2": "working set (>=55 GB of params/grads/Adam state per update) >> 126 MB L2"},
             "clocks": clocks, "e2e": e2e, "gpu_launches": launches,
         }

@@ -124,8 +124,10 @@ def train_parser() -> argparse.ArgumentParser:
     g.add_argument("--overlap", default="auto",
                    help="overlap the ZeRO exchange with forward/backward: auto (copy-engine pushes at 2 GPUs, "
                         "serial exchange otherwise), 1 or 0")
-    g.add_argument("--transport", default="auto", choices=["auto", "sm", "ce"],
-                   help="overlapped pushes by kernels (sm) or by the copy engines (ce)")
+    g.add_argument("--transport", default="auto", choices=["auto", "sm", "ce", "gemm"],
+                   help="overlapped pushes by kernels (sm) or by the copy engines (ce); gemm: serial schedule whose "
+                        "weight-gradient GEMMs store each element at its ZeRO owner (GEMM fused with the "
+                        "reduce-scatter)")
     g.add_argument("--partition", default="even", choices=["even", "greedy"],
                    help="ZeRO owner map: even contiguous split, or the fairscale OSS greedy per-parameter split")
     return p

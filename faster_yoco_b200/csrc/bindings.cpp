@@ -10,6 +10,8 @@ namespace fyb {
 
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
           const c10::optional<at::Tensor>& R);
+void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, const at::Tensor& grad_flat,
+                  const at::Tensor& bases, int64_t seg, int64_t rank);
 std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps);
 std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const c10::optional<at::Tensor>& w,
                                      const at::Tensor& rstd, const c10::optional<at::Tensor>& dres);
@@ -105,6 +107,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "faster_yoco_b200 sm_100a kernels";
   m.def("gemm", &fyb::gemm, "C = A @ B^T on tcgen05 (operands K-major or MN-major)", py::arg("A"), py::arg("B"),
         py::arg("C"), py::arg("a_mn_major"), py::arg("b_mn_major"), py::arg("residual") = py::none());
+  m.def("gemm_scatter", &fyb::gemm_scatter,
+        "weight gradient dW = A^T B stored straight into each element's ZeRO owner (own slot or peer staging)",
+        py::arg("A"), py::arg("B"), py::arg("C"), py::arg("accumulate"), py::arg("grad_flat"), py::arg("bases"),
+        py::arg("seg"), py::arg("rank"));
   m.def("rms_norm_fwd", &fyb::rms_norm_fwd);
   m.def("rms_norm_bwd", &fyb::rms_norm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
         py::arg("dres") = py::none());

@@ -24,7 +24,28 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
 
-enum Epi : int { kEpiBf16 = 0, kEpiBf16Res = 1, kEpiF32 = 2 };
+enum Epi : int { kEpiBf16 = 0, kEpiBf16Res = 1, kEpiF32 = 2, kEpiScatter = 3, kEpiScatterRes = 4 };
+
+// Owner-scatter epilogue (GEMM fused with the ZeRO reduce-scatter): the output C is a weight's slot in the flat
+// gradient buffer, element (row, col) has flat index x = x0 + row * ldc + col, and x belongs to owner o = x / seg.
+// Instead of storing locally, the epilogue stores the value where the owner sums it: this rank's own slot when
+// o == rank, else owner o's staging buffer, slot `rank` (bases[o] + rank * seg + (x - o * seg)), over NVLink.
+// Every 8-element vector lies inside one segment (seg, x0, ldc multiples of 8), so one owner lookup per vector.
+struct OwnerScatter {
+  const unsigned long long* bases;   // [world] staging buffer of every rank (peer pointers)
+  __nv_bfloat16* own;                // this rank's flat gradient buffer
+  int64_t x0, seg;
+  int rank;
+};
+
+__device__ __forceinline__ __nv_bfloat16* owner_dst(const OwnerScatter& s, int64_t x) {
+  const int64_t o = x / s.seg;
+  if (o == s.rank) return s.own + x;
+  return reinterpret_cast<__nv_bfloat16*>(s.bases[o]) + (static_cast<int64_t>(s.rank) * s.seg + (x - o * s.seg));
+}
+
+__host__ __device__ constexpr bool epi_scatter(int e) { return e == kEpiScatter || e == kEpiScatterRes; }
+__host__ __device__ constexpr bool epi_res(int e) { return e == kEpiBf16Res || e == kEpiScatterRes; }
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -50,7 +71,7 @@ template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* Cv,
                         const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, int splits,
-                        float* ws, int* status) {
+                        float* ws, int* status, const OwnerScatter sc) {
   using S = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -227,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(Cv) + static_cast<int64_t>(row) * ldc + col;
             uint32_t p[16];
-            if (EPI == kEpiBf16Res) {
+            if (epi_res(EPI)) {
               const __nv_bfloat16* Rr = R + static_cast<int64_t>(row) * ldr + col;
               if (col + 32 <= N && (ldr % 8) == 0) {
 #pragma unroll
@@ -255,7 +276,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j) p[j] = pack_bf16(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
             }
-            if (col + 32 <= N && (ldc % 8) == 0) {
+            if (epi_scatter(EPI)) {
+              const int64_t x = sc.x0 + static_cast<int64_t>(row) * ldc + col;
+              if (col + 32 <= N) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  *reinterpret_cast<uint4*>(owner_dst(sc, x + 8 * j)) =
+                      make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  if (col + j < N) {
+                    const uint16_t h = (j & 1) ? static_cast<uint16_t>(p[j >> 1] >> 16)
+                                               : static_cast<uint16_t>(p[j >> 1] & 0xffffu);
+                    *owner_dst(sc, x + j) = __ushort_as_bfloat16(h);
+                  }
+                }
+              }
+            } else if (col + 32 <= N && (ldc % 8) == 0) {
 #pragma unroll
               for (int j = 0; j < 4; ++j)
                 *reinterpret_cast<uint4*>(C + 8 * j) = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
@@ -291,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // C = sum over slices of ws[slice] (+ R), fp32 sum in slice order
 template <int EPI>
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, void* Cv, const __nv_bfloat16* R,
-                                     int M, int N, int64_t ldc, int64_t ldr) {
+                                     int M, int N, int64_t ldc, int64_t ldr, const OwnerScatter sc) {
   const int64_t i4 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
   const int64_t total = static_cast<int64_t>(M) * N;
   if (i4 >= total) return;
@@ -309,14 +347,15 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, v
     if (EPI == kEpiF32) {
       *reinterpret_cast<float4*>(reinterpret_cast<float*>(Cv) + row * ldc + col) = acc;
     } else {
-      if (EPI == kEpiBf16Res) {
+      if (epi_res(EPI)) {
         const uint2 ru = *reinterpret_cast<const uint2*>(R + row * ldr + col);
         const float2 r0 = unpack_bf16(ru.x), r1 = unpack_bf16(ru.y);
         acc = make_float4(bf16_round(acc.x) + r0.x, bf16_round(acc.y) + r0.y, bf16_round(acc.z) + r1.x,
                           bf16_round(acc.w) + r1.y);
       }
-      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(Cv) + row * ldc + col) =
-          make_uint2(pack_bf16(acc.x, acc.y), pack_bf16(acc.z, acc.w));
+      __nv_bfloat16* dst = epi_scatter(EPI) ? owner_dst(sc, sc.x0 + row * ldc + col)
+                                            : reinterpret_cast<__nv_bfloat16*>(Cv) + row * ldc + col;
+      *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16(acc.x, acc.y), pack_bf16(acc.z, acc.w));
     }
     return;
   }
@@ -326,18 +365,19 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, v
     const int64_t row = i / N, col = i % N;
     if (EPI == kEpiF32) {
       reinterpret_cast<float*>(Cv)[row * ldc + col] = acc;
-    } else if (EPI == kEpiBf16Res) {
-      reinterpret_cast<__nv_bfloat16*>(Cv)[row * ldc + col] =
-          __float2bfloat16_rn(bf16_round(acc) + __bfloat162float(R[row * ldr + col]));
     } else {
-      reinterpret_cast<__nv_bfloat16*>(Cv)[row * ldc + col] = __float2bfloat16_rn(acc);
+      const float v = epi_res(EPI) ? bf16_round(acc) + __bfloat162float(R[row * ldr + col]) : acc;
+      __nv_bfloat16* dst = epi_scatter(EPI) ? owner_dst(sc, sc.x0 + row * ldc + col)
+                                            : reinterpret_cast<__nv_bfloat16*>(Cv) + row * ldc + col;
+      *dst = __float2bfloat16_rn(v);
     }
   }
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const __nv_bfloat16* R, int M, int N, int K,
-            int64_t ldc, int64_t ldr, int splits, float* ws, cudaStream_t stream) {
+            int64_t ldc, int64_t ldr, int splits, float* ws, cudaStream_t stream,
+            const OwnerScatter& sc = OwnerScatter{}) {
   using S = GemmSmem<BN, STAGES>;
   auto kern = gemm_tcgen05_kernel<BN, STAGES, A_MN, B_MN, EPI>;
   static bool attr_set = false;
@@ -347,12 +387,12 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const __nv_bf
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * splits;
   const int grid = std::min(tiles, num_sms());
-  kern<<<grid, kThreads, S::TOTAL, stream>>>(ta, tb, C, R, M, N, K, ldc, ldr, splits, ws, status_ptr());
+  kern<<<grid, kThreads, S::TOTAL, stream>>>(ta, tb, C, R, M, N, K, ldc, ldr, splits, ws, status_ptr(), sc);
   check_launch("gemm_tcgen05");
   if (splits > 1) {
     const int64_t total = static_cast<int64_t>(M) * N;
     const int blocks = static_cast<int>((total / 4 + 255) / 256 + 1);
-    splitk_reduce_kernel<EPI><<<blocks, 256, 0, stream>>>(ws, splits, C, R, M, N, ldc, ldr);
+    splitk_reduce_kernel<EPI><<<blocks, 256, 0, stream>>>(ws, splits, C, R, M, N, ldc, ldr, sc);
     check_launch("gemm_splitk_reduce");
   }
 }
@@ -463,6 +503,64 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bo
     else if (epi == kEpiBf16Res)
       dispatch_major<128, 6, kEpiBf16Res>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, sp, wsp, st);
     else dispatch_major<128, 6, kEpiF32>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, sp, wsp, st);
+  }
+}
+
+// Weight gradient fused with the ZeRO reduce-scatter: dW = A^T B (A = dy [T, M], B = x [T, N], both MN-major) with
+// every element stored where its owner sums it (OwnerScatter above). C is dW's slot inside grad_flat (only its
+// position is used: C's own memory receives the rows this rank owns); with `accumulate`, C's current contents (the
+// earlier micro-batches of the update, held locally) are added first, as the residual. bases: int64 [world] device
+// tensor of every rank's staging buffer address (this rank's entry is not read).
+void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, const at::Tensor& grad_flat,
+                  const at::Tensor& bases, int64_t seg, int64_t rank) {
+  FYB_RANGE("fyb::gemm_scatter");
+  FYB_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda() && bases.is_cuda(), "gemm_scatter: CUDA tensors expected");
+  FYB_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 &&
+                C.scalar_type() == at::kBFloat16 && grad_flat.scalar_type() == at::kBFloat16,
+            "gemm_scatter: bf16 tensors expected");
+  FYB_CHECK(bases.scalar_type() == at::kLong && bases.dim() == 1 && rank >= 0 && rank < bases.size(0),
+            "gemm_scatter: bases must be int64 [world]");
+  FYB_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1 && C.is_contiguous(),
+            "gemm_scatter: 2-D operands with contiguous rows and a contiguous output expected");
+  const int64_t K = A.size(0), M = A.size(1), N = B.size(1);
+  FYB_CHECK(B.size(0) == K && C.size(0) == M && C.size(1) == N, "gemm_scatter: shape mismatch");
+  FYB_CHECK(K > 0 && M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm_scatter: bad dimensions");
+  const auto base = reinterpret_cast<uintptr_t>(grad_flat.data_ptr());
+  const auto cptr = reinterpret_cast<uintptr_t>(C.data_ptr());
+  FYB_CHECK(cptr >= base && cptr + C.numel() * 2 <= base + grad_flat.numel() * 2,
+            "gemm_scatter: C must be a slot of grad_flat");
+  const int64_t x0 = static_cast<int64_t>((cptr - base) / 2);
+  FYB_CHECK(seg > 0 && seg % 8 == 0 && x0 % 8 == 0 && N % 8 == 0,
+            "gemm_scatter: segment size, slot offset and row length must be multiples of 8 elements");
+  FYB_CHECK((x0 + C.numel() + seg - 1) / seg <= bases.size(0), "gemm_scatter: slot beyond the last owner");
+  if (M == 0 || N == 0) return;
+  c10::cuda::CUDAGuard guard(A.device());
+  cudaStream_t st = cur_stream();
+  OwnerScatter sc;
+  sc.bases = reinterpret_cast<const unsigned long long*>(bases.data_ptr<int64_t>());
+  sc.own = reinterpret_cast<__nv_bfloat16*>(grad_flat.data_ptr());
+  sc.x0 = x0;
+  sc.seg = seg;
+  sc.rank = static_cast<int>(rank);
+  const Plan plan = pick_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
+  at::Tensor ws;
+  float* wsp = nullptr;
+  if (plan.splits > 1) {
+    ws = at::empty({plan.splits, M, N}, A.options().dtype(at::kFloat));
+    wsp = ws.data_ptr<float>();
+  }
+  const CUtensorMap ta = make_tmap_2d(A.data_ptr(), K, M, A.stride(0), 64);
+  const CUtensorMap tb = make_tmap_2d(B.data_ptr(), K, N, B.stride(0), 64);
+  void* Cp = C.data_ptr();
+  const __nv_bfloat16* Rp = accumulate ? reinterpret_cast<const __nv_bfloat16*>(Cp) : nullptr;
+  const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
+  const int64_t ld = N;
+  if (plan.bn == 256) {
+    if (accumulate) launch<256, 4, true, true, kEpiScatterRes>(ta, tb, Cp, Rp, m, n, k, ld, ld, plan.splits, wsp, st, sc);
+    else launch<256, 4, true, true, kEpiScatter>(ta, tb, Cp, Rp, m, n, k, ld, ld, plan.splits, wsp, st, sc);
+  } else {
+    if (accumulate) launch<128, 6, true, true, kEpiScatterRes>(ta, tb, Cp, Rp, m, n, k, ld, ld, plan.splits, wsp, st, sc);
+    else launch<128, 6, true, true, kEpiScatter>(ta, tb, Cp, Rp, m, n, k, ld, ld, plan.splits, wsp, st, sc);
   }
 }
 

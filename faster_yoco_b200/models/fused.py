@@ -27,10 +27,8 @@ def _C():
 
 
 def _wgrad(w: torch.Tensor, dy: torch.Tensor, x: torch.Tensor):
-    """dW = dy^T x into w's gradient slot (returns None) or as a new tensor."""
-    slot, acc = ops._grad_slot(w)
-    if slot is not None:
-        ops.gemm(dy, x, a_mn_major=True, b_mn_major=True, out=slot, residual=slot if acc else None)
+    """dW = dy^T x into w's gradient slot or at its ZeRO owners (returns None), or as a new tensor."""
+    if ops.wgrad_into(w, dy, x):
         return None
     return ops.gemm(dy, x, a_mn_major=True, b_mn_major=True)
 

@@ -51,6 +51,25 @@ def _grad_slot(p):
     return fp.claim_grad(p)
 
 
+def wgrad_into(w: torch.Tensor, dy: torch.Tensor, x: torch.Tensor) -> bool:
+    """dW = dy^T x (dy [T, N], x [T, K]) written into w's flat gradient slot; False when w has no slot.
+
+    With the GEMM-fused reduce-scatter on (``FlatParams.scatter``), the GEMM's epilogue stores every element at
+    its ZeRO owner instead (this rank's slot for the rows it owns, the owner's staging buffer over NVLink for the
+    others), so no separate gradient exchange pass reads the slot again."""
+    fp = getattr(w, "_fyb_flat", None)
+    if fp is None or not fp.direct_grads:
+        return False
+    slot, acc = fp.claim_grad(w)
+    if fp.scatter is not None and slot.numel() % 8 == 0 and w.shape[-1] % 8 == 0:
+        bases = fp.scatter_target(w)
+        if bases is not None:
+            _C().gemm_scatter(dy, x, slot, acc, fp.grad_flat, bases, fp.seg, fp.rank)
+            return True
+    gemm(dy, x, a_mn_major=True, b_mn_major=True, out=slot, residual=slot if acc else None)
+    return True
+
+
 # ----------------------------------------------------------------------------------------------------------------------
 # GEMM: y = x @ w.T (+ residual)
 
@@ -91,11 +110,8 @@ class _NativeLinear(torch.autograd.Function):
         if ctx.needs_input_grad[0]:
             dx = gemm(dy2, w, b_mn_major=True).view(ctx.shp)
         if ctx.needs_input_grad[1]:
-            slot, acc = _grad_slot(w)
-            if slot is not None:
-                # the weight gradient lands in the flat gradient buffer; autograd sees no gradient for w
-                gemm(dy2, x2, a_mn_major=True, b_mn_major=True, out=slot, residual=slot if acc else None)
-            else:
+            # the weight gradient lands in the flat gradient buffer (or at its owners); autograd sees none for w
+            if not wgrad_into(w, dy2, x2):
                 dw = gemm(dy2, x2, a_mn_major=True, b_mn_major=True)
         return dx, dw, (dy if ctx.has_res else None)
 

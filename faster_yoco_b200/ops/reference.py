@@ -272,3 +272,29 @@ def polynomial_decay_lr(step: int, lr: float, warmup: int, total: int, end_lr: f
         return end_lr
     pct = 1 - (step - warmup) / float(total - warmup)
     return (lr - end_lr) * pct ** power + end_lr
+
+
+def owner_scatter(dw: torch.Tensor, x0: int, seg: int, rank: int, own: torch.Tensor, staging) -> None:
+    """Where the GEMM-fused ZeRO reduce-scatter stores a weight gradient computed on ``rank``: element i of
+    ``dw.reshape(-1)`` has flat index x = x0 + i and owner o = x // seg; it goes to ``own[x]`` when o == rank, else
+    to ``staging[o][rank * seg + x - o * seg]`` (owner o's slot for this rank)."""
+    flat = dw.reshape(-1)
+    x = torch.arange(x0, x0 + flat.numel(), device=flat.device)
+    o = torch.div(x, seg, rounding_mode="floor")
+    mine = o == rank
+    own[x[mine]] = flat[mine].to(own.dtype)
+    for q in torch.unique(o[~mine]).tolist():
+        m = o == q
+        staging[q][rank * seg + x[m] - q * seg] = flat[m].to(staging[q].dtype)
+
+
+def staged_owner_sum(own: torch.Tensor, staging: torch.Tensor, rank: int, world: int, seg: int, lo: int,
+                     n: int) -> torch.Tensor:
+    """The owner's reduction of [lo, lo + n) of its segment: fp32 sum over ranks in rank order (its own values from
+    its gradient buffer, the others' from staging slot r), divided by world, rounded to bf16."""
+    loc = lo - rank * seg
+    acc = torch.zeros(n, dtype=torch.float32, device=own.device)
+    for r in range(world):
+        src = own[lo:lo + n] if r == rank else staging[r * seg + loc: r * seg + loc + n]
+        acc += src.float()
+    return (acc * (1.0 / world)).to(torch.bfloat16)

@@ -112,6 +112,61 @@ class PeerComm:
         self.C.mailbox_sum(self.box_f, out, self.world, box_counter)
         return out
 
+    # ------------------------------------------------------------------------- GEMM-fused reduce-scatter (serial)
+    def setup_scatter(self, flat, push_ctas: Optional[int] = None):
+        """Weight-gradient GEMMs store straight at the owners: every rank gets a staging buffer of world x seg
+        elements (slot r = rank r's contribution to this rank's segment), and ``flat.scatter`` is set to the device
+        list of every rank's staging address, which ``ops.wgrad_into`` passes to the scatter epilogue."""
+        if "staging" not in self.peers:
+            self.staging = self.alloc("staging", self.world * flat.seg, flat.dtype)
+        self.flat = flat
+        self.scatter_bases = torch.tensor(self.peers["staging"], dtype=torch.int64, device=self.dev)
+        flat.scatter = self.scatter_bases
+        sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
+        self.scatter_push_ctas = push_ctas or sms
+        self.scatter_red_ctas = min(2 * sms, self.part.numel())
+        self._sarrive, self._peer_sarrive = self.share_bytes(self.NSLOTS * 4)
+        self._scatter_tables: Dict[frozenset, Tuple[torch.Tensor, torch.Tensor]] = {}
+
+    def _scatter_tables_for(self, flat) -> Tuple[torch.Tensor, torch.Tensor]:
+        """(pieces of gradients NOT stored at their owners by a GEMM that other ranks own: [n, 3] offset, count,
+        owner; every piece this rank owns: [m, 2] offset, count). Built on the first (eager) update and reused, so
+        a captured update launches with fixed tables."""
+        key = flat.scattered()
+        t = self._scatter_tables.get(key)
+        if t is None:
+            if self.dev.type == "cuda" and torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("GEMM-fused reduce-scatter: the set of scattered weights changed under capture")
+            push, own = [], []
+            for e in flat.entries:
+                for o, c, r in flat.owner_ranges(e):
+                    if r == self.rank:
+                        own.append([o, c])
+                    elif id(e.param) not in key:
+                        push.append([o, c, r])
+            t = (torch.tensor(push, dtype=torch.int64, device=self.dev).view(-1, 3),
+                 torch.tensor(own, dtype=torch.int64, device=self.dev).view(-1, 2))
+            self._scatter_tables[key] = t
+        return t
+
+    def reduce_scattered(self, flat) -> torch.Tensor:
+        """End of backward with the GEMM-fused reduce-scatter: push the gradients no GEMM delivered (norm weights,
+        the embedding, anything autograd produced) to their owners' staging slots, one barrier (every rank's GEMM
+        epilogue stores and pushes are done), then the owner sums its segment from local memory in rank order
+        (its own slot + the staging slots; same arithmetic as ``reduce_to_owner``). Returns the segment's sum of
+        squares after the BF16 rounding."""
+        push, own = self._scatter_tables_for(flat)
+        if push.numel():
+            # the arrival counts of this push are not waited on: the barrier below publishes it
+            self.C.push_grads(flat.grad_flat, self.peers["staging"], self._peer_sarrive, push, 0, self.rank,
+                              flat.seg, self.scatter_push_ctas)
+        self.barrier()
+        part = self.part[: self.scatter_red_ctas]
+        self.C.reduce_staged(flat.grad_flat, self.staging, own, self.world, self.rank, flat.seg, part,
+                             self.scatter_red_ctas)
+        self.C.sum_partials(part, self.sq)
+        return self.sq
+
     # ------------------------------------------------------------------------------------ overlapped (bucketed)
     def setup_buckets(self, flat, groups, reduce_ctas: Optional[int] = None, gather_ctas: Optional[int] = None,
                       transport: str = "sm"):

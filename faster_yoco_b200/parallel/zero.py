@@ -120,6 +120,11 @@ class FlatParams:
         self.direct_grads = False          # native ops write weight gradients straight into their slots
         self.accumulate = False            # later micro-batches of an update add into the slots
         self._written = set()
+        # GEMM-fused reduce-scatter (set by PeerComm.setup_scatter): weight-gradient GEMMs of an update's last
+        # micro-batch store each element at its owner (own slot or the owner's staging slot for this rank)
+        self.scatter = None                # device int64 [world]: every rank's staging buffer address
+        self.scatter_now = True            # the current micro-batch is the update's last one
+        self._scattered = set()
 
     # ---------------------------------------------------------------------------------------------------------
     def owned(self, rank: Optional[int] = None) -> slice:
@@ -153,13 +158,28 @@ class FlatParams:
         self._written.add(id(p))
         return self.grad_view(p), acc
 
+    def scatter_target(self, p):
+        """Staging addresses when p's weight gradient is to be stored at its owners by the GEMM (GEMM-fused
+        reduce-scatter on, last micro-batch of the update), else None. Marks p as delivered to its owners."""
+        if self.scatter is None or not self.scatter_now:
+            return None
+        self._scattered.add(id(p))
+        return self.scatter
+
+    def scattered(self) -> frozenset:
+        return frozenset(self._scattered)
+
     def begin_update(self):
         self.accumulate = False
         self._written.clear()
+        self._scattered.clear()
 
-    def begin_microbatch(self, first: bool):
+    def begin_microbatch(self, first: bool, last: bool = True):
         """Gradient accumulation needs no flag: a slot written by an earlier micro-batch of this update is
-        accumulated into (claim_grad), autograd accumulates p.grad for the others until collect_grads."""
+        accumulated into (claim_grad), autograd accumulates p.grad for the others until collect_grads. With the
+        GEMM-fused reduce-scatter, only the last micro-batch's weight-gradient GEMMs store at the owners (adding
+        the earlier micro-batches' sums held in the local slots)."""
+        self.scatter_now = last
 
     def collect_grads(self):
         """Move every p.grad into its slot and clear p.grad; slots that no gradient reached this update are zeroed."""
@@ -168,6 +188,8 @@ class FlatParams:
                 g = e.param.grad
                 slot = self.grad_flat[e.offset:e.offset + e.numel]
                 written = id(e.param) in self._written
+                if g is not None and id(e.param) in self._scattered:
+                    raise RuntimeError(f"{e.name}: gradient from autograd for a weight already stored at its owners")
                 if g is None:
                     if not written:
                         slot.zero_()
@@ -220,6 +242,8 @@ class ZeroOptimizer:
         if self.comm == "fused" and self.p2p is not None:
             if self.p2p.buckets is not None:
                 return self.p2p.finish_reduce()
+            if fp.scatter is not None:
+                return self.p2p.reduce_scattered(fp)
             return self.p2p.reduce_to_owner(fp.grad_flat, fp.seg, fp.used[fp.rank])
         out = fp.grad_segment()
         if dist.get_backend(self.group) == "nccl":

@@ -67,9 +67,15 @@ class Trainer:
         self.flat.direct_grads = self.device.type == "cuda" and ops.get_backend() == "native"
         self.zero = ZeroOptimizer(self.flat, optim_cfg, comm=comm, group=group, stage=zero_stage)
         self.zero.p2p = p2p
-        self.overlap = p2p is not None and overlap and hasattr(model, "param_buckets")
+        if transport not in ("sm", "ce", "gemm"):
+            raise ValueError(f"unknown transport {transport!r}")
+        self.overlap = p2p is not None and overlap and hasattr(model, "param_buckets") and transport != "gemm"
         if self.overlap:
             p2p.setup_buckets(self.flat, model.param_buckets(), transport=transport)
+        elif p2p is not None and transport == "gemm":
+            if not self.flat.direct_grads:
+                raise ValueError("transport 'gemm' needs the native kernels (weight gradients written by the GEMM)")
+            p2p.setup_scatter(self.flat)
         self.sched = PolynomialDecaySchedule(optim_cfg.lr, optim_cfg.warmup_updates, optim_cfg.total_num_update,
                                              optim_cfg.end_learning_rate, optim_cfg.power)
         self.pending = PendingChecks(self.device.type == "cuda")
@@ -154,6 +160,7 @@ class Trainer:
         loss = None
         n = len(srcs)
         for i, (src, tgt) in enumerate(zip(srcs, tgts)):
+            self.flat.begin_microbatch(i == 0, i == n - 1)
             li = self._forward_backward(src, tgt, first=i == 0, last=i == n - 1)
             loss = li if loss is None else loss + li
         with phase("reduce-grads"):

@@ -116,3 +116,33 @@ def fused_vs_nccl_gpu(rank, world, outdir, steps):
             tr.zero.p2p.close()
     if rank == 0:
         torch.save(res, os.path.join(outdir, "fused_vs_nccl.pt"))
+
+
+def gemm_scatter_vs_serial_gpu(rank, world, outdir, steps):
+    """GPU: serial P2P exchange against the GEMM-fused reduce-scatter (weight-gradient GEMMs store at the owners),
+    eager and graphed, and with two micro-batches per update; rank 0 saves every variant's losses and parameters."""
+    from .. import ops
+    ops.set_backend("native")
+    dev = torch.device("cuda", rank)
+    res = {}
+    for name, transport, graph, uf in (("serial", "sm", False, 1), ("gemm", "gemm", False, 1),
+                                       ("gemm_graph", "gemm", True, 1), ("serial_uf2", "sm", False, 2),
+                                       ("gemm_uf2", "gemm", False, 2)):
+        model, tr = _tiny_trainer(dev, comm="fused", arch="yoco_small", dtype=torch.bfloat16, overlap=False,
+                                  transport=transport, graph=graph)
+        losses = []
+        for ids in _batches(rank, world, steps, seq=256, vocab=8192, batch=2 * uf):
+            mine = ids[rank]
+            micro = []
+            for m in mine.chunk(uf, 0):
+                micro.append({"src_tokens": m[:, :-1].contiguous(), "target": m[:, 1:].contiguous(),
+                              "ntokens": m.shape[0] * (m.shape[1] - 1), "nsentences": m.shape[0]})
+            losses.append(float(tr.train_step(micro if uf > 1 else micro[0]).item()))
+        tr.sync_params()
+        tr.release_graph()
+        torch.cuda.synchronize()
+        status = int(ops._C().status()[0].item())
+        res[name] = {"losses": losses, "params": tr.flat.flat.float().cpu(), "status": status}
+        tr.zero.p2p.close()
+    if rank == 0:
+        torch.save(res, os.path.join(outdir, "gemm_scatter.pt"))
