@@ -49,6 +49,10 @@ def parse():
                    help="overlapped exchange: pushes by kernels (sm) or by the copy engines (ce); gemm: serial "
                         "schedule whose weight-gradient GEMMs store every element at its ZeRO owner over NVLink "
                         "(GEMM fused with the reduce-scatter)")
+    p.add_argument("--partition", default="even", choices=["even", "greedy", "cyclic"],
+                   help="ZeRO owner map: even contiguous segments, the OSS greedy per-parameter rule, or block-cyclic "
+                        "chunks (every weight spread over all owners)")
+    p.add_argument("--zero-chunk", type=int, default=None, help="chunk size (elements) of --partition cyclic")
     p.add_argument("--sliding-window", type=int, default=None)
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-e2e", action="store_true")
@@ -201,7 +205,8 @@ def main():
     model = model.to(torch.bfloat16)
     optim = OptimConfig()
     trainer = Trainer(model, optim, device=dev, comm=args.comm, graph_step=bool(args.graph),
-                      overlap=bool(args.overlap), transport=args.transport)
+                      overlap=bool(args.overlap), transport=args.transport, partition=args.partition,
+                      chunk=args.zero_chunk)
     data = SyntheticLM(margs.vocab_size, args.seq_len, args.batch, seed=1, rank=rank, pin=True)
     batches = [next(data) for _ in range(4)]
 
@@ -271,7 +276,7 @@ def main():
                        "global_batch": args.batch * world, "seq_len": args.seq_len,
                        "tokens_per_update": tokens_per_update, "parallelism": f"dp{world}-zero1",
                        "kernels": args.kernels, "comm": args.comm, "cuda_graph": bool(args.graph),
-                       "comm_overlap": bool(args.overlap),
+                       "comm_overlap": bool(args.overlap), "zero_partition": args.partition,
                        "transport": args.transport if (args.overlap or args.transport == "gemm") else None,
                        "l2": "working set (>=55 GB of params/grads/Adam state per update) >> 126 MB L2"},
             "clocks": clocks, "e2e": e2e, "gpu_launches": launches,

@@ -128,8 +128,10 @@ def train_parser() -> argparse.ArgumentParser:
                    help="overlapped pushes by kernels (sm) or by the copy engines (ce); gemm: serial schedule whose "
                         "weight-gradient GEMMs store each element at its ZeRO owner (GEMM fused with the "
                         "reduce-scatter)")
-    g.add_argument("--partition", default="even", choices=["even", "greedy"],
-                   help="ZeRO owner map: even contiguous split, or the fairscale OSS greedy per-parameter split")
+    g.add_argument("--partition", default="even", choices=["even", "greedy", "cyclic"],
+                   help="ZeRO owner map: even contiguous split, the fairscale OSS greedy per-parameter split, or "
+                        "block-cyclic chunks (every weight spread over all owners)")
+    g.add_argument("--zero-chunk", type=int, default=None, help="chunk size (elements) of --partition cyclic")
     return p
 
 

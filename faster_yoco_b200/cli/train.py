@@ -133,7 +133,8 @@ def main(argv=None) -> int:
     transport = ("ce" if world == 2 else "sm") if args.transport == "auto" else args.transport
     graph = bool(args.cuda_graph) and device.type == "cuda" and args.context_parallel_size == 1
     trainer = Trainer(model, optim, device=device, comm=comm, graph_step=graph,
-                      overlap=overlap, transport=transport, partition=args.partition, pad_idx=task.tokenizer.pad_id)
+                      overlap=overlap, transport=transport, partition=args.partition, pad_idx=task.tokenizer.pad_id,
+                      chunk=args.zero_chunk)
     cp = args.context_parallel_size
     if cp > 1:
         if family != "yoco":

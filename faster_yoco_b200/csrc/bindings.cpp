@@ -11,7 +11,7 @@ namespace fyb {
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
           const c10::optional<at::Tensor>& R);
 void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, const at::Tensor& grad_flat,
-                  const at::Tensor& bases, int64_t seg, int64_t rank);
+                  const at::Tensor& bases, int64_t seg, int64_t rank, int64_t chunk);
 std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps);
 std::vector<at::Tensor> rms_norm_bwd(const at::Tensor& dy, const at::Tensor& x, const c10::optional<at::Tensor>& w,
                                      const at::Tensor& rstd, const c10::optional<at::Tensor>& dres);
@@ -32,10 +32,10 @@ at::Tensor ce_bwd(const at::Tensor& logits, const at::Tensor& target, const at::
                   int64_t ignore, const c10::optional<at::Tensor>& out);
 void adam_step(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor& v, at::Tensor& p16,
                const at::Tensor& hyper, const at::Tensor& factor, double b1, double b2, double eps, double wd,
-               bool adamw);
+               bool adamw, int64_t chunk, int64_t world, int64_t rank);
 void adam_push(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor& v, at::Tensor& p16,
                const at::Tensor& hyper, const at::Tensor& factor, double b1, double b2, double eps, double wd,
-               bool adamw, const std::vector<int64_t>& peer_params, int64_t peer_off, int64_t rank);
+               bool adamw, const std::vector<int64_t>& peer_params, int64_t peer_off, int64_t rank, int64_t chunk);
 at::Tensor sq_norm(const at::Tensor& x);
 std::vector<at::Tensor> attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, bool causal,
                                       int64_t window, double scale);
@@ -58,7 +58,7 @@ void ipc_close(int64_t ptr);
 void flag_barrier(const std::vector<int64_t>& peer_flags, const at::Tensor& my_flags, const at::Tensor& counters,
                   int64_t rank, int64_t slot);
 void reduce_owner(const std::vector<int64_t>& peer_grads, at::Tensor& out, int64_t base, int64_t n, at::Tensor& part,
-                  at::Tensor& sq);
+                  at::Tensor& sq, int64_t chunk, int64_t rank);
 void gather_segments(const std::vector<int64_t>& peer_params, at::Tensor& dst, const at::Tensor& segs, int64_t rank,
                      int64_t ctas);
 void sum_partials(const at::Tensor& part, at::Tensor& out);
@@ -69,11 +69,13 @@ void peer_copy(int64_t dst, int64_t src, int64_t nbytes);
 void signal_peer(int64_t counter_base, int64_t index);
 void push_grads(const at::Tensor& grad, const std::vector<int64_t>& peer_staging,
                 const std::vector<int64_t>& peer_arrive, const at::Tensor& pieces, int64_t bucket, int64_t rank,
-                int64_t seg, int64_t ctas);
+                int64_t seg, int64_t ctas, int64_t chunk);
 void reduce_staged(at::Tensor& grad, const at::Tensor& staging, const at::Tensor& ranges, int64_t world, int64_t rank,
-                   int64_t seg, at::Tensor& part, int64_t ctas);
+                   int64_t seg, at::Tensor& part, int64_t ctas, int64_t chunk);
+void reduce_compact(at::Tensor& grad, const at::Tensor& staging, int64_t n, int64_t world, int64_t rank, int64_t seg,
+                    int64_t chunk, at::Tensor& part, int64_t ctas);
 void push_range(const at::Tensor& src, const std::vector<int64_t>& peer_dst, int64_t off, int64_t n, int64_t rank,
-                int64_t ctas);
+                int64_t ctas, int64_t chunk);
 void mailbox_put(const std::vector<int64_t>& peer_boxes, const at::Tensor& vals, int64_t rank,
                  const at::Tensor& counter);
 void mailbox_sum(const at::Tensor& box, at::Tensor& out, int64_t world, at::Tensor& counter);
@@ -110,7 +112,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_scatter", &fyb::gemm_scatter,
         "weight gradient dW = A^T B stored straight into each element's ZeRO owner (own slot or peer staging)",
         py::arg("A"), py::arg("B"), py::arg("C"), py::arg("accumulate"), py::arg("grad_flat"), py::arg("bases"),
-        py::arg("seg"), py::arg("rank"));
+        py::arg("seg"), py::arg("rank"), py::arg("chunk") = 0);
   m.def("rms_norm_fwd", &fyb::rms_norm_fwd);
   m.def("rms_norm_bwd", &fyb::rms_norm_bwd, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
         py::arg("dres") = py::none());
@@ -130,8 +132,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_fwd", &fyb::ce_fwd);
   m.def("ce_bwd", &fyb::ce_bwd, py::arg("logits"), py::arg("target"), py::arg("lse"), py::arg("grad"),
         py::arg("ignore"), py::arg("out") = py::none());
-  m.def("adam_step", &fyb::adam_step);
-  m.def("adam_push", &fyb::adam_push, "Adam on this owner's segment fused with its all-gather push to every peer");
+  m.def("adam_step", &fyb::adam_step, "Adam (apex expression) on this owner's state + the bf16 parameter copy",
+        py::arg("p32"), py::arg("g16"), py::arg("m"), py::arg("v"), py::arg("p16"), py::arg("hyper"),
+        py::arg("factor"), py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"), py::arg("adamw"),
+        py::arg("chunk") = 0, py::arg("world") = 1, py::arg("rank") = 0);
+  m.def("adam_push", &fyb::adam_push, "Adam on this owner's segment fused with its all-gather push to every peer",
+        py::arg("p32"), py::arg("g16"), py::arg("m"), py::arg("v"), py::arg("p16"), py::arg("hyper"),
+        py::arg("factor"), py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"), py::arg("adamw"),
+        py::arg("peer_params"), py::arg("peer_off"), py::arg("rank"), py::arg("chunk") = 0);
   m.def("sq_norm", &fyb::sq_norm);
   m.def("attention_fwd", &fyb::attention_fwd);
   m.def("attention_bwd", &fyb::attention_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),
@@ -147,16 +155,24 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", &fyb::ipc_open);
   m.def("ipc_close", &fyb::ipc_close);
   m.def("flag_barrier", &fyb::flag_barrier);
-  m.def("reduce_owner", &fyb::reduce_owner);
+  m.def("reduce_owner", &fyb::reduce_owner, py::arg("peer_grads"), py::arg("out"), py::arg("base"), py::arg("n"),
+        py::arg("part"), py::arg("sq"), py::arg("chunk") = 0, py::arg("rank") = 0);
   m.def("gather_segments", &fyb::gather_segments);
   m.def("sum_partials", &fyb::sum_partials);
-  m.def("push_range", &fyb::push_range);
+  m.def("push_range", &fyb::push_range, py::arg("src"), py::arg("peer_dst"), py::arg("off"), py::arg("n"),
+        py::arg("rank"), py::arg("ctas"), py::arg("chunk") = 0);
   m.def("push_bucket", &fyb::push_bucket);
   m.def("wait_arrivals", &fyb::wait_arrivals);
   m.def("peer_copy", &fyb::peer_copy, "cudaMemcpyAsync of nbytes between (peer) device addresses on the current stream");
   m.def("signal_peer", &fyb::signal_peer, "release-add 1 to counter_base[index] (a peer's counter) on the current stream");
-  m.def("push_grads", &fyb::push_grads);
-  m.def("reduce_staged", &fyb::reduce_staged);
+  m.def("push_grads", &fyb::push_grads, py::arg("grad"), py::arg("peer_staging"), py::arg("peer_arrive"),
+        py::arg("pieces"), py::arg("bucket"), py::arg("rank"), py::arg("seg"), py::arg("ctas"), py::arg("chunk") = 0);
+  m.def("reduce_staged", &fyb::reduce_staged, py::arg("grad"), py::arg("staging"), py::arg("ranges"), py::arg("world"),
+        py::arg("rank"), py::arg("seg"), py::arg("part"), py::arg("ctas"), py::arg("chunk") = 0);
+  m.def("reduce_compact", &fyb::reduce_compact,
+        "owner's segment summed from its gradient buffer and the staging slots (GEMM-fused reduce-scatter)",
+        py::arg("grad"), py::arg("staging"), py::arg("n"), py::arg("world"), py::arg("rank"), py::arg("seg"),
+        py::arg("chunk"), py::arg("part"), py::arg("ctas"));
   m.def("mailbox_put", &fyb::mailbox_put);
   m.def("mailbox_sum", &fyb::mailbox_sum);
   m.def("status", &fyb::status_tensor, "device status word of the kernels with bounded waits");

@@ -22,6 +22,7 @@
 
 #include "common/host.h"
 #include "common/ptx.cuh"
+#include "common/zero_map.cuh"
 
 namespace fyb {
 namespace {
@@ -75,19 +76,21 @@ __global__ void flag_barrier_kernel(PeerPtrs peer_flags, uint32_t* my_flags, uin
   __threadfence_system();
 }
 
-// owner-side reduction of its segment [base, base + n): out = bf16(sum_r g_r / world) in rank order; per-CTA
-// partial sums of squares of the bf16 result in part[blockIdx.x]
+// owner-side reduction of its n owned elements: out = bf16(sum_r g_r / world) in rank order; per-CTA partial sums of
+// squares of the bf16 result in part[blockIdx.x]. Local element i is flat element base + zero_flat(z, i) (the segment
+// [base, base + n) in the contiguous layout).
 __global__ void reduce_owner_kernel(PeerPtrs grads, __nv_bfloat16* out, int64_t base, int64_t n, int world,
-                                    float inv_world, float* part) {
+                                    float inv_world, float* part, const ZeroMap z) {
   float ss = 0.f;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 8;
   for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < n; i += stride) {
     if (i + 8 <= n) {
+      const int64_t x = base + zero_flat(z, i);
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       uint4 u[kMaxWorld];
 #pragma unroll
       for (int r = 0; r < kMaxWorld; ++r)
-        if (r < world) u[r] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(grads.p[r]) + base + i);
+        if (r < world) u[r] = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(grads.p[r]) + x);
 #pragma unroll
       for (int r = 0; r < kMaxWorld; ++r) {
         if (r < world) {
@@ -107,14 +110,15 @@ __global__ void reduce_owner_kernel(PeerPtrs grads, __nv_bfloat16* out, int64_t 
         ss += a * a + b * b;
         o[k] = pack_bf16(a, b);
       }
-      *reinterpret_cast<uint4*>(out + base + i) = make_uint4(o[0], o[1], o[2], o[3]);
+      *reinterpret_cast<uint4*>(out + x) = make_uint4(o[0], o[1], o[2], o[3]);
     } else {
       for (int64_t j = i; j < n; ++j) {
+        const int64_t xj = base + zero_flat(z, j);
         float acc = 0.f;
-        for (int r = 0; r < world; ++r) acc += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(grads.p[r])[base + j]);
+        for (int r = 0; r < world; ++r) acc += __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(grads.p[r])[xj]);
         const float a = bf16_round(acc * inv_world);
         ss += a * a;
-        out[base + j] = __float2bfloat16_rn(a);
+        out[xj] = __float2bfloat16_rn(a);
       }
     }
   }
@@ -175,22 +179,26 @@ __global__ void gather_segments_kernel(PeerPtrs src, __nv_bfloat16* dst, const i
 
 // push form of the all-gather: this rank's range [off, off+n) of its flat buffer is stored into the same range of
 // every peer's buffer (remote stores are posted writes: no round trip per access, unlike remote loads)
+// (n owned elements; local element c is flat element off + zero_flat(z, c))
 __global__ void push_range_kernel(const __nv_bfloat16* __restrict__ src, PeerPtrs dst, int64_t off, int64_t n,
-                                  int world, int rank) {
-  const uint4* sp = reinterpret_cast<const uint4*>(src + off);
+                                  int world, int rank, int64_t chunk) {
+  const ZeroMap z{chunk, world, rank};
   const int64_t nv = n / 8;
   const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nv; i += nthr) {
-    const uint4 v = sp[i];
+    const int64_t x = off + zero_flat(z, i * 8);
+    const uint4 v = *reinterpret_cast<const uint4*>(src + x);
 #pragma unroll
     for (int q = 0; q < kMaxWorld; ++q)
       if (q < world && q != rank)
-        reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(dst.p[q])) + off)[i] = v;
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(dst.p[q])) + x) = v;
   }
   if (blockIdx.x == 0)
-    for (int64_t j = nv * 8 + threadIdx.x; j < n; j += blockDim.x)
+    for (int64_t j = nv * 8 + threadIdx.x; j < n; j += blockDim.x) {
+      const int64_t x = off + zero_flat(z, j);
       for (int q = 0; q < world; ++q)
-        if (q != rank) reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(dst.p[q]))[off + j] = src[off + j];
+        if (q != rank) reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(dst.p[q]))[x] = src[x];
+    }
   __threadfence_system();   // the barrier that follows publishes these remote stores
 }
 
@@ -228,14 +236,15 @@ __global__ void push_bucket_kernel(const __nv_bfloat16* __restrict__ src, PeerPt
 // q * seg]); then each CTA fences and adds 1 to the bucket's arrival counter on every peer.
 __global__ void push_grads_kernel(const __nv_bfloat16* __restrict__ grad, PeerPtrs staging, PeerPtrs arrive,
                                   const int64_t* __restrict__ pieces, int npieces, int bucket, int world, int rank,
-                                  int64_t seg) {
+                                  int64_t seg, int64_t chunk) {
   const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   for (int pc = 0; pc < npieces; ++pc) {
     const int64_t off = pieces[3 * pc], n = pieces[3 * pc + 1];
     const int q = static_cast<int>(pieces[3 * pc + 2]);
+    // a piece lies inside one chunk (one owner segment in the contiguous layout): its local positions are contiguous
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(staging.p[q])) +
-                         static_cast<int64_t>(rank) * seg + (off - static_cast<int64_t>(q) * seg);
+                         static_cast<int64_t>(rank) * seg + zero_local(chunk, world, seg, off);
     const uint4* sp = reinterpret_cast<const uint4*>(grad + off);
     const int64_t nv = n / 8;
     for (int64_t i = tid; i < nv; i += nthr) reinterpret_cast<uint4*>(dst)[i] = sp[i];
@@ -254,13 +263,13 @@ __global__ void push_grads_kernel(const __nv_bfloat16* __restrict__ grad, PeerPt
 // sums of squares of the result in part[blockIdx.x].
 __global__ void reduce_staged_kernel(__nv_bfloat16* __restrict__ grad, const __nv_bfloat16* __restrict__ staging,
                                      const int64_t* __restrict__ ranges, int nranges, int world, int rank,
-                                     int64_t seg, float inv_world, float* __restrict__ part) {
+                                     int64_t seg, float inv_world, float* __restrict__ part, int64_t chunk) {
   float ss = 0.f;
   const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   for (int rg = 0; rg < nranges; ++rg) {
     const int64_t off = ranges[2 * rg], n = ranges[2 * rg + 1];
-    const int64_t loc = off - static_cast<int64_t>(rank) * seg;   // position inside the owner's segment
+    const int64_t loc = zero_local(chunk, world, seg, off);        // position inside the owner's segment
     for (int64_t i = tid * 8; i < n; i += nthr * 8) {
       if (i + 8 <= n) {
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -295,6 +304,65 @@ __global__ void reduce_staged_kernel(__nv_bfloat16* __restrict__ grad, const __n
           ss += a * a;
           grad[off + j] = __float2bfloat16_rn(a);
         }
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+    part[blockIdx.x] = t;
+  }
+}
+
+// Owner-side sum of a whole owned segment from local memory (GEMM-fused reduce-scatter): local element c in [0, n)
+// is flat element base + zero_flat(z, c); this rank's own value is read from its gradient buffer there, rank r's from
+// staging slot r (staging[r * seg + c]); out = bf16(sum in rank order / world) is written back to the gradient
+// buffer. Same arithmetic as reduce_owner_kernel. Per-CTA partial sums of squares in part[blockIdx.x].
+__global__ void reduce_compact_kernel(__nv_bfloat16* __restrict__ grad, const __nv_bfloat16* __restrict__ staging,
+                                      int64_t base, int64_t n, int64_t seg, float inv_world, float* __restrict__ part,
+                                      const ZeroMap z) {
+  float ss = 0.f;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 8;
+  for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < n; i += stride) {
+    if (i + 8 <= n) {
+      const int64_t x = base + zero_flat(z, i);
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+      for (int r = 0; r < kMaxWorld; ++r) {
+        if (r < z.world) {
+          const __nv_bfloat16* src = r == z.rank ? grad + x : staging + static_cast<int64_t>(r) * seg + i;
+          const uint4 u = *reinterpret_cast<const uint4*>(src);
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float2 f = unpack_bf16(w[k]);
+            acc[2 * k] += f.x;
+            acc[2 * k + 1] += f.y;
+          }
+        }
+      }
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float a = bf16_round(acc[2 * k] * inv_world), b = bf16_round(acc[2 * k + 1] * inv_world);
+        ss += a * a + b * b;
+        o[k] = pack_bf16(a, b);
+      }
+      *reinterpret_cast<uint4*>(grad + x) = make_uint4(o[0], o[1], o[2], o[3]);
+    } else {
+      for (int64_t j = i; j < n; ++j) {
+        const int64_t xj = base + zero_flat(z, j);
+        float acc = 0.f;
+        for (int r = 0; r < z.world; ++r)
+          acc += __bfloat162float(r == z.rank ? grad[xj] : staging[static_cast<int64_t>(r) * seg + j]);
+        const float a = bf16_round(acc * inv_world);
+        ss += a * a;
+        grad[xj] = __float2bfloat16_rn(a);
       }
     }
   }
@@ -418,16 +486,20 @@ void flag_barrier(const std::vector<int64_t>& peer_flags, const at::Tensor& my_f
 int reduce_ctas() { return std::min(num_sms() * 2, 1024); }
 
 // reduce [base, base+n) of the flat gradient buffers into out (this rank's buffer) and sq[0] = sum of squares
+// (chunk > 0: block-cyclic layout, base must be 0 and local element c is flat element zero_flat(c))
 void reduce_owner(const std::vector<int64_t>& peer_grads, at::Tensor& out, int64_t base, int64_t n, at::Tensor& part,
-                  at::Tensor& sq) {
+                  at::Tensor& sq, int64_t chunk, int64_t rank) {
   FYB_RANGE("fyb::reduce_owner");
   const int world = static_cast<int>(peer_grads.size());
   FYB_CHECK(base % 8 == 0, "reduce_owner: segment base must be a multiple of 8 elements");
+  FYB_CHECK(chunk == 0 || (chunk % 8 == 0 && base == 0 && rank >= 0 && rank < world),
+            "reduce_owner: block-cyclic layout needs chunk % 8 == 0, base 0 and this rank");
   const int P = static_cast<int>(part.numel());
   FYB_CHECK(P >= 1 && P <= 1024, "reduce_owner: 1..1024 partials");
   reduce_owner_kernel<<<P, 256, 0, cur_stream()>>>(to_ptrs(peer_grads),
                                                    reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), base, n, world,
-                                                   1.0f / static_cast<float>(world), part.data_ptr<float>());
+                                                   1.0f / static_cast<float>(world), part.data_ptr<float>(),
+                                                   ZeroMap{chunk, world, static_cast<int>(rank)});
   check_launch("reduce_owner");
   sum_partials_kernel<<<1, 1024, 0, cur_stream()>>>(part.data_ptr<float>(), P, sq.data_ptr<float>());
   check_launch("reduce_owner_sum");
@@ -453,14 +525,15 @@ void gather_segments(const std::vector<int64_t>& peer_params, at::Tensor& dst, c
 }
 
 void push_range(const at::Tensor& src, const std::vector<int64_t>& peer_dst, int64_t off, int64_t n, int64_t rank,
-                int64_t ctas) {
+                int64_t ctas, int64_t chunk) {
   FYB_RANGE("fyb::push_range");
   const int world = static_cast<int>(peer_dst.size());
   FYB_CHECK(off % 8 == 0, "push_range: offset must be a multiple of 8 elements");
+  FYB_CHECK(chunk == 0 || (chunk % 8 == 0 && off == 0), "push_range: block-cyclic layout needs chunk % 8 == 0, off 0");
   if (n <= 0) return;
   push_range_kernel<<<static_cast<int>(ctas), 512, 0, cur_stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), to_ptrs(peer_dst), off, n, world,
-      static_cast<int>(rank));
+      static_cast<int>(rank), chunk);
   check_launch("push_range");
 }
 
@@ -479,7 +552,7 @@ void push_bucket(const at::Tensor& src, const std::vector<int64_t>& peer_dst, co
 
 void push_grads(const at::Tensor& grad, const std::vector<int64_t>& peer_staging,
                 const std::vector<int64_t>& peer_arrive, const at::Tensor& pieces, int64_t bucket, int64_t rank,
-                int64_t seg, int64_t ctas) {
+                int64_t seg, int64_t ctas, int64_t chunk) {
   FYB_RANGE("fyb::push_grads");
   const int world = static_cast<int>(peer_staging.size());
   FYB_CHECK(pieces.is_cuda() && pieces.scalar_type() == at::kLong && pieces.dim() == 2 && pieces.size(1) == 3,
@@ -487,12 +560,12 @@ void push_grads(const at::Tensor& grad, const std::vector<int64_t>& peer_staging
   push_grads_kernel<<<static_cast<int>(ctas), 512, 0, cur_stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(grad.data_ptr()), to_ptrs(peer_staging), to_ptrs(peer_arrive),
       pieces.data_ptr<int64_t>(), static_cast<int>(pieces.size(0)), static_cast<int>(bucket), world,
-      static_cast<int>(rank), seg);
+      static_cast<int>(rank), seg, chunk);
   check_launch("push_grads");
 }
 
 void reduce_staged(at::Tensor& grad, const at::Tensor& staging, const at::Tensor& ranges, int64_t world, int64_t rank,
-                   int64_t seg, at::Tensor& part, int64_t ctas) {
+                   int64_t seg, at::Tensor& part, int64_t ctas, int64_t chunk) {
   FYB_RANGE("fyb::reduce_staged");
   FYB_CHECK(part.numel() >= ctas, "reduce_staged: partials buffer too small");
   if (ranges.size(0) == 0) {
@@ -502,8 +575,30 @@ void reduce_staged(at::Tensor& grad, const at::Tensor& staging, const at::Tensor
   reduce_staged_kernel<<<static_cast<int>(ctas), 256, 0, cur_stream()>>>(
       reinterpret_cast<__nv_bfloat16*>(grad.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(staging.data_ptr()),
       ranges.data_ptr<int64_t>(), static_cast<int>(ranges.size(0)), static_cast<int>(world), static_cast<int>(rank),
-      seg, 1.0f / static_cast<float>(world), part.data_ptr<float>());
+      seg, 1.0f / static_cast<float>(world), part.data_ptr<float>(), chunk);
   check_launch("reduce_staged");
+}
+
+// The owner's n local elements summed from its gradient buffer (own values) and the staging slots (peers'), written
+// back in place; part (>= ctas floats) receives the per-CTA sums of squares.
+void reduce_compact(at::Tensor& grad, const at::Tensor& staging, int64_t n, int64_t world, int64_t rank, int64_t seg,
+                    int64_t chunk, at::Tensor& part, int64_t ctas) {
+  FYB_RANGE("fyb::reduce_compact");
+  FYB_CHECK(world >= 1 && world <= kMaxWorld && rank >= 0 && rank < world, "reduce_compact: 1..8 ranks");
+  FYB_CHECK(seg % 8 == 0 && chunk % 8 == 0 && n <= seg, "reduce_compact: seg / chunk multiples of 8, n <= seg");
+  FYB_CHECK(grad.numel() == world * seg && staging.numel() == world * seg,
+            "reduce_compact: gradient and staging buffers of world x seg elements");
+  FYB_CHECK(part.numel() >= ctas && ctas >= 1, "reduce_compact: partials buffer too small");
+  if (n == 0) {
+    part.zero_();
+    return;
+  }
+  const int64_t base = chunk == 0 ? rank * seg : 0;
+  reduce_compact_kernel<<<static_cast<int>(ctas), 256, 0, cur_stream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(grad.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(staging.data_ptr()),
+      base, n, seg, 1.0f / static_cast<float>(world), part.data_ptr<float>(),
+      ZeroMap{chunk, static_cast<int>(world), static_cast<int>(rank)});
+  check_launch("reduce_compact");
 }
 
 void peer_copy(int64_t dst, int64_t src, int64_t nbytes) {

@@ -11,6 +11,7 @@
 
 #include "common/host.h"
 #include "common/ptx.cuh"
+#include "common/zero_map.cuh"
 
 namespace fyb {
 namespace {
@@ -303,16 +304,17 @@ __device__ __forceinline__ void adam_elem(float& p, float& m, float& v, float g,
 __global__ void adam_kernel(float* __restrict__ p32, const __nv_bfloat16* __restrict__ g16, float* __restrict__ m,
                             float* __restrict__ v, __nv_bfloat16* __restrict__ p16, const float* __restrict__ hyper,
                             const float* __restrict__ factor, int64_t n, float b1, float b2, float eps, float wd,
-                            bool adamw) {
+                            bool adamw, const ZeroMap z) {
   const float lr = hyper[0], bc1 = hyper[1], bc2 = hyper[2];
   const float f = factor[0];
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 4;
   for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < n; i += stride) {
     if (i + 4 <= n) {
+      const int64_t x = zero_flat(z, i);   // the bf16 gradient / parameter of local element i (4 in one chunk)
       float4 P = *reinterpret_cast<float4*>(p32 + i);
       float4 Mv = *reinterpret_cast<float4*>(m + i);
       float4 Vv = *reinterpret_cast<float4*>(v + i);
-      const uint2 gu = *reinterpret_cast<const uint2*>(g16 + i);
+      const uint2 gu = *reinterpret_cast<const uint2*>(g16 + x);
       const float2 g01 = unpack_bf16(gu.x), g23 = unpack_bf16(gu.y);
       adam_elem(P.x, Mv.x, Vv.x, g01.x * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
       adam_elem(P.y, Mv.y, Vv.y, g01.y * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
@@ -321,15 +323,16 @@ __global__ void adam_kernel(float* __restrict__ p32, const __nv_bfloat16* __rest
       *reinterpret_cast<float4*>(p32 + i) = P;
       *reinterpret_cast<float4*>(m + i) = Mv;
       *reinterpret_cast<float4*>(v + i) = Vv;
-      *reinterpret_cast<uint2*>(p16 + i) = make_uint2(pack_bf16(P.x, P.y), pack_bf16(P.z, P.w));
+      *reinterpret_cast<uint2*>(p16 + x) = make_uint2(pack_bf16(P.x, P.y), pack_bf16(P.z, P.w));
     } else {
       for (int64_t j = i; j < n; ++j) {
+        const int64_t x = zero_flat(z, j);
         float P = p32[j], Mv = m[j], Vv = v[j];
-        adam_elem(P, Mv, Vv, __bfloat162float(g16[j]) * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
+        adam_elem(P, Mv, Vv, __bfloat162float(g16[x]) * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
         p32[j] = P;
         m[j] = Mv;
         v[j] = Vv;
-        p16[j] = __float2bfloat16_rn(P);
+        p16[x] = __float2bfloat16_rn(P);
       }
     }
   }
@@ -348,12 +351,14 @@ __global__ void adam_push_kernel(float* __restrict__ p32, const __nv_bfloat16* _
                                  float* __restrict__ m, float* __restrict__ v, __nv_bfloat16* __restrict__ p16,
                                  const float* __restrict__ hyper, const float* __restrict__ factor, int64_t n,
                                  float b1, float b2, float eps, float wd, bool adamw, PushTargets peers,
-                                 int64_t peer_off, int world, int rank) {
+                                 int64_t peer_off, int world, int rank, int64_t chunk) {
   const float lr = hyper[0], bc1 = hyper[1], bc2 = hyper[2];
   const float f = factor[0];
+  const ZeroMap z{chunk, world, rank};
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x * 8;
   for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < n; i += stride) {
     if (i + 8 <= n) {
+      const int64_t x = zero_flat(z, i);   // 8 local elements lie in one chunk
       float P[8], Mv[8], Vv[8], G[8];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -365,7 +370,7 @@ __global__ void adam_push_kernel(float* __restrict__ p32, const __nv_bfloat16* _
         Vv[4 * h] = c.x, Vv[4 * h + 1] = c.y, Vv[4 * h + 2] = c.z, Vv[4 * h + 3] = c.w;
       }
       {
-        const uint4 gu = *reinterpret_cast<const uint4*>(g16 + i);
+        const uint4 gu = *reinterpret_cast<const uint4*>(g16 + x);
         const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -384,22 +389,23 @@ __global__ void adam_push_kernel(float* __restrict__ p32, const __nv_bfloat16* _
       }
       const uint4 out = make_uint4(pack_bf16(P[0], P[1]), pack_bf16(P[2], P[3]), pack_bf16(P[4], P[5]),
                                    pack_bf16(P[6], P[7]));
-      *reinterpret_cast<uint4*>(p16 + i) = out;
+      *reinterpret_cast<uint4*>(p16 + x) = out;
 #pragma unroll
       for (int q = 0; q < 8; ++q)
         if (q < world && q != rank)
-          *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers.p[q]) + peer_off + i) = out;
+          *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peers.p[q]) + peer_off + x) = out;
     } else {
       for (int64_t j = i; j < n; ++j) {
+        const int64_t xj = zero_flat(z, j);
         float P = p32[j], Mv = m[j], Vv = v[j];
-        adam_elem(P, Mv, Vv, __bfloat162float(g16[j]) * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
+        adam_elem(P, Mv, Vv, __bfloat162float(g16[xj]) * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
         p32[j] = P;
         m[j] = Mv;
         v[j] = Vv;
         const __nv_bfloat16 o = __float2bfloat16_rn(P);
-        p16[j] = o;
+        p16[xj] = o;
         for (int q = 0; q < world; ++q)
-          if (q != rank) reinterpret_cast<__nv_bfloat16*>(peers.p[q])[peer_off + j] = o;
+          if (q != rank) reinterpret_cast<__nv_bfloat16*>(peers.p[q])[peer_off + xj] = o;
       }
     }
   }
@@ -730,14 +736,29 @@ at::Tensor ce_bwd(const at::Tensor& logits, const at::Tensor& target, const at::
   return dx;
 }
 
+// chunk > 0 (block-cyclic ZeRO layout): g16 / p16 are the whole flat buffers and local element c of this owner is
+// flat element ((c / chunk) * world + rank) * chunk + c % chunk; chunk == 0: g16 / p16 are this owner's segment.
+void check_zero_map(const char* what, int64_t n, const at::Tensor& g16, const at::Tensor& p16, int64_t chunk,
+                    int64_t world, int64_t rank) {
+  if (chunk == 0) {
+    FYB_CHECK(g16.numel() == n && p16.numel() == n, std::string(what) + ": segment views of the state's size expected");
+    return;
+  }
+  FYB_CHECK(chunk % 8 == 0 && n % chunk == 0 && world >= 1 && rank >= 0 && rank < world,
+            std::string(what) + ": chunk must be a multiple of 8 dividing the owned size");
+  FYB_CHECK(g16.numel() == n * world && p16.numel() == n * world,
+            std::string(what) + ": block-cyclic layout needs the whole flat buffers (world x owned size)");
+}
+
 void adam_step(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor& v, at::Tensor& p16,
                const at::Tensor& hyper, const at::Tensor& factor, double b1, double b2, double eps, double wd,
-               bool adamw) {
+               bool adamw, int64_t chunk, int64_t world, int64_t rank) {
   FYB_RANGE("fyb::adam_step");
   const int64_t n = p32.numel();
   FYB_CHECK(p32.is_contiguous() && m.is_contiguous() && v.is_contiguous() && g16.is_contiguous() &&
-                p16.is_contiguous() && g16.numel() == n && m.numel() == n && v.numel() == n && p16.numel() == n,
+                p16.is_contiguous() && m.numel() == n && v.numel() == n,
             "adam_step: contiguous tensors of equal size expected");
+  check_zero_map("adam_step", n, g16, p16, chunk, world, rank);
   FYB_CHECK(p32.scalar_type() == at::kFloat && g16.scalar_type() == at::kBFloat16 &&
                 p16.scalar_type() == at::kBFloat16,
             "adam_step: fp32 master / bf16 grad / bf16 param");
@@ -749,20 +770,23 @@ void adam_step(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor
   adam_kernel<<<blocks, 256, 0, cur_stream()>>>(
       p32.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(g16.data_ptr()), m.data_ptr<float>(),
       v.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(p16.data_ptr()), hyper.data_ptr<float>(),
-      factor.data_ptr<float>(), n, (float)b1, (float)b2, (float)eps, (float)wd, adamw);
+      factor.data_ptr<float>(), n, (float)b1, (float)b2, (float)eps, (float)wd, adamw,
+      ZeroMap{chunk, static_cast<int>(world), static_cast<int>(rank)});
   check_launch("adam");
 }
 
 void adam_push(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor& v, at::Tensor& p16,
                const at::Tensor& hyper, const at::Tensor& factor, double b1, double b2, double eps, double wd,
-               bool adamw, const std::vector<int64_t>& peer_params, int64_t peer_off, int64_t rank) {
+               bool adamw, const std::vector<int64_t>& peer_params, int64_t peer_off, int64_t rank, int64_t chunk) {
   FYB_RANGE("fyb::adam_push");
   const int64_t n = p32.numel();
   const int world = static_cast<int>(peer_params.size());
   FYB_CHECK(world >= 1 && world <= 8 && rank >= 0 && rank < world, "adam_push: 1..8 ranks");
   FYB_CHECK(p32.is_contiguous() && m.is_contiguous() && v.is_contiguous() && g16.is_contiguous() &&
-                p16.is_contiguous() && g16.numel() == n && m.numel() == n && v.numel() == n && p16.numel() == n,
+                p16.is_contiguous() && m.numel() == n && v.numel() == n,
             "adam_push: contiguous tensors of equal size expected");
+  check_zero_map("adam_push", n, g16, p16, chunk, world, rank);
+  FYB_CHECK(chunk == 0 || peer_off == 0, "adam_push: the block-cyclic layout addresses peers from their buffer start");
   FYB_CHECK(p32.scalar_type() == at::kFloat && g16.scalar_type() == at::kBFloat16 &&
                 p16.scalar_type() == at::kBFloat16,
             "adam_push: fp32 master / bf16 grad / bf16 param");
@@ -782,7 +806,7 @@ void adam_push(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor
       p32.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(g16.data_ptr()), m.data_ptr<float>(),
       v.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(p16.data_ptr()), hyper.data_ptr<float>(),
       factor.data_ptr<float>(), n, (float)b1, (float)b2, (float)eps, (float)wd, adamw, t, peer_off,
-      world, static_cast<int>(rank));
+      world, static_cast<int>(rank), chunk);
   check_launch("adam_push");
 }
 

@@ -16,6 +16,7 @@
 
 #include "common/host.h"
 #include "common/ptx.cuh"
+#include "common/zero_map.cuh"
 
 namespace fyb {
 namespace {
@@ -27,21 +28,23 @@ constexpr int kThreads = 192;
 enum Epi : int { kEpiBf16 = 0, kEpiBf16Res = 1, kEpiF32 = 2, kEpiScatter = 3, kEpiScatterRes = 4 };
 
 // Owner-scatter epilogue (GEMM fused with the ZeRO reduce-scatter): the output C is a weight's slot in the flat
-// gradient buffer, element (row, col) has flat index x = x0 + row * ldc + col, and x belongs to owner o = x / seg.
-// Instead of storing locally, the epilogue stores the value where the owner sums it: this rank's own slot when
-// o == rank, else owner o's staging buffer, slot `rank` (bases[o] + rank * seg + (x - o * seg)), over NVLink.
-// Every 8-element vector lies inside one segment (seg, x0, ldc multiples of 8), so one owner lookup per vector.
+// gradient buffer, element (row, col) has flat index x = x0 + row * ldc + col, and x belongs to owner o (its segment
+// x / seg, or its chunk's owner in the block-cyclic layout, zero_map.cuh). Instead of storing locally, the epilogue
+// stores the value where the owner sums it: this rank's own slot when o == rank, else owner o's staging buffer, slot
+// `rank`, at the element's local index (bases[o] + rank * seg + local(x)), over NVLink. Every 8-element vector lies
+// inside one segment / chunk (seg, chunk, x0, ldc multiples of 8), so one owner lookup per vector.
 struct OwnerScatter {
   const unsigned long long* bases;   // [world] staging buffer of every rank (peer pointers)
   __nv_bfloat16* own;                // this rank's flat gradient buffer
-  int64_t x0, seg;
-  int rank;
+  int64_t x0, seg, chunk;
+  int rank, world;
 };
 
 __device__ __forceinline__ __nv_bfloat16* owner_dst(const OwnerScatter& s, int64_t x) {
-  const int64_t o = x / s.seg;
+  const int o = zero_owner(s.chunk, s.world, s.seg, x);
   if (o == s.rank) return s.own + x;
-  return reinterpret_cast<__nv_bfloat16*>(s.bases[o]) + (static_cast<int64_t>(s.rank) * s.seg + (x - o * s.seg));
+  return reinterpret_cast<__nv_bfloat16*>(s.bases[o]) +
+         (static_cast<int64_t>(s.rank) * s.seg + zero_local(s.chunk, s.world, s.seg, x));
 }
 
 __host__ __device__ constexpr bool epi_scatter(int e) { return e == kEpiScatter || e == kEpiScatterRes; }
@@ -512,7 +515,7 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bo
 // earlier micro-batches of the update, held locally) are added first, as the residual. bases: int64 [world] device
 // tensor of every rank's staging buffer address (this rank's entry is not read).
 void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, const at::Tensor& grad_flat,
-                  const at::Tensor& bases, int64_t seg, int64_t rank) {
+                  const at::Tensor& bases, int64_t seg, int64_t rank, int64_t chunk) {
   FYB_RANGE("fyb::gemm_scatter");
   FYB_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda() && bases.is_cuda(), "gemm_scatter: CUDA tensors expected");
   FYB_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 &&
@@ -530,9 +533,10 @@ void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
   FYB_CHECK(cptr >= base && cptr + C.numel() * 2 <= base + grad_flat.numel() * 2,
             "gemm_scatter: C must be a slot of grad_flat");
   const int64_t x0 = static_cast<int64_t>((cptr - base) / 2);
-  FYB_CHECK(seg > 0 && seg % 8 == 0 && x0 % 8 == 0 && N % 8 == 0,
-            "gemm_scatter: segment size, slot offset and row length must be multiples of 8 elements");
-  FYB_CHECK((x0 + C.numel() + seg - 1) / seg <= bases.size(0), "gemm_scatter: slot beyond the last owner");
+  FYB_CHECK(seg > 0 && seg % 8 == 0 && chunk % 8 == 0 && x0 % 8 == 0 && N % 8 == 0,
+            "gemm_scatter: segment size, chunk, slot offset and row length must be multiples of 8 elements");
+  FYB_CHECK(x0 + C.numel() <= bases.size(0) * seg, "gemm_scatter: slot beyond the last owner");
+  FYB_CHECK(chunk == 0 || seg % chunk == 0, "gemm_scatter: the segment must hold whole chunks");
   if (M == 0 || N == 0) return;
   c10::cuda::CUDAGuard guard(A.device());
   cudaStream_t st = cur_stream();
@@ -541,7 +545,9 @@ void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
   sc.own = reinterpret_cast<__nv_bfloat16*>(grad_flat.data_ptr());
   sc.x0 = x0;
   sc.seg = seg;
+  sc.chunk = chunk;
   sc.rank = static_cast<int>(rank);
+  sc.world = static_cast<int>(bases.size(0));
   const Plan plan = pick_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
   at::Tensor ws;
   float* wsp = nullptr;

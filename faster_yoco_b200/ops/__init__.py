@@ -64,7 +64,7 @@ def wgrad_into(w: torch.Tensor, dy: torch.Tensor, x: torch.Tensor) -> bool:
     if fp.scatter is not None and slot.numel() % 8 == 0 and w.shape[-1] % 8 == 0:
         bases = fp.scatter_target(w)
         if bases is not None:
-            _C().gemm_scatter(dy, x, slot, acc, fp.grad_flat, bases, fp.seg, fp.rank)
+            _C().gemm_scatter(dy, x, slot, acc, fp.grad_flat, bases, fp.seg, fp.rank, fp.chunk)
             return True
     gemm(dy, x, a_mn_major=True, b_mn_major=True, out=slot, residual=slot if acc else None)
     return True

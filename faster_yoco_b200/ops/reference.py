@@ -274,18 +274,27 @@ def polynomial_decay_lr(step: int, lr: float, warmup: int, total: int, end_lr: f
     return (lr - end_lr) * pct ** power + end_lr
 
 
-def owner_scatter(dw: torch.Tensor, x0: int, seg: int, rank: int, own: torch.Tensor, staging) -> None:
+def zero_owner_local(x: torch.Tensor, seg: int, chunk: int = 0, world: int = 1):
+    """(owner, local index) of flat elements x under the ZeRO owner map: contiguous segments of ``seg`` elements
+    (chunk 0), or chunks of ``chunk`` elements dealt to ``world`` ranks in turn."""
+    if chunk:
+        return (x // chunk) % world, (x // (chunk * world)) * chunk + x % chunk
+    o = torch.div(x, seg, rounding_mode="floor")
+    return o, x - o * seg
+
+
+def owner_scatter(dw: torch.Tensor, x0: int, seg: int, rank: int, own: torch.Tensor, staging, chunk: int = 0) -> None:
     """Where the GEMM-fused ZeRO reduce-scatter stores a weight gradient computed on ``rank``: element i of
-    ``dw.reshape(-1)`` has flat index x = x0 + i and owner o = x // seg; it goes to ``own[x]`` when o == rank, else
-    to ``staging[o][rank * seg + x - o * seg]`` (owner o's slot for this rank)."""
+    ``dw.reshape(-1)`` has flat index x = x0 + i, owner o and local index l (``zero_owner_local``); it goes to
+    ``own[x]`` when o == rank, else to ``staging[o][rank * seg + l]`` (owner o's slot for this rank)."""
     flat = dw.reshape(-1)
     x = torch.arange(x0, x0 + flat.numel(), device=flat.device)
-    o = torch.div(x, seg, rounding_mode="floor")
+    o, loc = zero_owner_local(x, seg, chunk, len(staging))
     mine = o == rank
     own[x[mine]] = flat[mine].to(own.dtype)
     for q in torch.unique(o[~mine]).tolist():
         m = o == q
-        staging[q][rank * seg + x[m] - q * seg] = flat[m].to(staging[q].dtype)
+        staging[q][rank * seg + loc[m]] = flat[m].to(staging[q].dtype)
 
 
 def staged_owner_sum(own: torch.Tensor, staging: torch.Tensor, rank: int, world: int, seg: int, lo: int,

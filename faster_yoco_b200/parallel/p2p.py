@@ -84,20 +84,22 @@ class PeerComm:
     def barrier(self, slot: int = 0):
         self.C.flag_barrier(self.peer_flags, self.flags, self.counters, self.rank, slot)
 
-    def reduce_to_owner(self, grad_flat: torch.Tensor, seg: int, used: Optional[int] = None) -> torch.Tensor:
-        """Average the gradient buffers of all ranks over this rank's segment, in place. Returns the segment's
-        sum of squares after the BF16 rounding (device tensor [1])."""
+    def reduce_to_owner(self, grad_flat: torch.Tensor, seg: int, used: Optional[int] = None,
+                        chunk: int = 0) -> torch.Tensor:
+        """Average the gradient buffers of all ranks over this rank's owned elements (its segment, or its chunks in
+        the block-cyclic layout), in place. Returns their sum of squares after the BF16 rounding (device [1])."""
         n = seg if used is None else used
         self.barrier()
-        self.C.reduce_owner(self.peers["grad"], grad_flat, self.rank * seg, n, self.part, self.sq)
+        base = 0 if chunk else self.rank * seg
+        self.C.reduce_owner(self.peers["grad"], grad_flat, base, n, self.part, self.sq, chunk, self.rank)
         return self.sq
 
-    def all_gather(self, flat: torch.Tensor, seg: int, used: Optional[List[int]] = None):
+    def all_gather(self, flat: torch.Tensor, seg: int, used: Optional[List[int]] = None, chunk: int = 0):
         """Push form (remote stores run at NVLink speed where remote loads do not): this rank stores its updated
-        segment into every peer's buffer, then one barrier publishes all pushes."""
+        elements into every peer's buffer, then one barrier publishes all pushes."""
         n = used[self.rank] if used else seg
         sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
-        self.C.push_range(flat, self.peers["param"], self.rank * seg, n, self.rank, sms)
+        self.C.push_range(flat, self.peers["param"], 0 if chunk else self.rank * seg, n, self.rank, sms, chunk)
         self.barrier()
 
     def all_reduce_vector(self, v: torch.Tensor) -> torch.Tensor:
@@ -119,6 +121,9 @@ class PeerComm:
         list of every rank's staging address, which ``ops.wgrad_into`` passes to the scatter epilogue."""
         if "staging" not in self.peers:
             self.staging = self.alloc("staging", self.world * flat.seg, flat.dtype)
+        # slots no rank writes (padding) must read as zero in the owner's sum
+        self.staging.zero_()
+        torch.cuda.synchronize(self.dev)
         self.flat = flat
         self.scatter_bases = torch.tensor(self.peers["staging"], dtype=torch.int64, device=self.dev)
         flat.scatter = self.scatter_bases
@@ -126,44 +131,39 @@ class PeerComm:
         self.scatter_push_ctas = push_ctas or sms
         self.scatter_red_ctas = min(2 * sms, self.part.numel())
         self._sarrive, self._peer_sarrive = self.share_bytes(self.NSLOTS * 4)
-        self._scatter_tables: Dict[frozenset, Tuple[torch.Tensor, torch.Tensor]] = {}
+        self._scatter_tables: Dict[frozenset, torch.Tensor] = {}
+        dist.barrier(group=self.group)      # every rank's staging is zeroed before any peer can store into it
 
-    def _scatter_tables_for(self, flat) -> Tuple[torch.Tensor, torch.Tensor]:
-        """(pieces of gradients NOT stored at their owners by a GEMM that other ranks own: [n, 3] offset, count,
-        owner; every piece this rank owns: [m, 2] offset, count). Built on the first (eager) update and reused, so
-        a captured update launches with fixed tables."""
+    def _scatter_tables_for(self, flat) -> torch.Tensor:
+        """Pieces of the gradients NOT stored at their owners by a GEMM that other ranks own ([n, 3]: flat offset,
+        count, owner). Built on the first (eager) update and reused, so a captured update launches with a fixed
+        table."""
         key = flat.scattered()
         t = self._scatter_tables.get(key)
         if t is None:
             if self.dev.type == "cuda" and torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("GEMM-fused reduce-scatter: the set of scattered weights changed under capture")
-            push, own = [], []
-            for e in flat.entries:
-                for o, c, r in flat.owner_ranges(e):
-                    if r == self.rank:
-                        own.append([o, c])
-                    elif id(e.param) not in key:
-                        push.append([o, c, r])
-            t = (torch.tensor(push, dtype=torch.int64, device=self.dev).view(-1, 3),
-                 torch.tensor(own, dtype=torch.int64, device=self.dev).view(-1, 2))
+            push = [[o, c, r] for e in flat.entries if id(e.param) not in key
+                    for o, c, r in flat.owner_ranges(e) if r != self.rank]
+            t = torch.tensor(push, dtype=torch.int64, device=self.dev).view(-1, 3)
             self._scatter_tables[key] = t
         return t
 
     def reduce_scattered(self, flat) -> torch.Tensor:
         """End of backward with the GEMM-fused reduce-scatter: push the gradients no GEMM delivered (norm weights,
         the embedding, anything autograd produced) to their owners' staging slots, one barrier (every rank's GEMM
-        epilogue stores and pushes are done), then the owner sums its segment from local memory in rank order
-        (its own slot + the staging slots; same arithmetic as ``reduce_to_owner``). Returns the segment's sum of
+        epilogue stores and pushes are done), then the owner sums its owned elements from local memory in rank
+        order (its own values + the staging slots; same arithmetic as ``reduce_to_owner``). Returns their sum of
         squares after the BF16 rounding."""
-        push, own = self._scatter_tables_for(flat)
+        push = self._scatter_tables_for(flat)
         if push.numel():
             # the arrival counts of this push are not waited on: the barrier below publishes it
             self.C.push_grads(flat.grad_flat, self.peers["staging"], self._peer_sarrive, push, 0, self.rank,
-                              flat.seg, self.scatter_push_ctas)
+                              flat.seg, self.scatter_push_ctas, flat.chunk)
         self.barrier()
         part = self.part[: self.scatter_red_ctas]
-        self.C.reduce_staged(flat.grad_flat, self.staging, own, self.world, self.rank, flat.seg, part,
-                             self.scatter_red_ctas)
+        self.C.reduce_compact(flat.grad_flat, self.staging, flat.used[self.rank], self.world, self.rank, flat.seg,
+                              flat.chunk, part, self.scatter_red_ctas)
         self.C.sum_partials(part, self.sq)
         return self.sq
 
@@ -180,6 +180,9 @@ class PeerComm:
             raise ValueError("too many buckets")
         if transport not in ("sm", "ce"):
             raise ValueError(transport)
+        if flat.chunk:
+            raise ValueError("the bucketed overlap transports run on contiguous owner segments (partition even / "
+                             "greedy), not on the block-cyclic layout")
         self.transport = transport
         import os
         reduce_ctas = int(os.environ.get("FYB_REDUCE_CTAS", reduce_ctas or 128))

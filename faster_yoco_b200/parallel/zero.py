@@ -32,6 +32,7 @@ import torch.distributed as dist
 from . import dist as D
 
 ALIGN = 64          # elements (128 bytes of bf16): every parameter view starts 128-byte aligned
+CYCLIC_CHUNK = 1 << 18   # elements per chunk of the block-cyclic owner map (512 KB of bf16)
 
 
 def greedy_partition(sizes: Sequence[int], world: int) -> List[int]:
@@ -63,7 +64,7 @@ class FlatParams:
     """The flat BF16 parameter buffer + flat gradient buffer; model parameters become views of it."""
 
     def __init__(self, named_params, world: int, rank: int, device, dtype=torch.bfloat16, allocator=None,
-                 partition: str = "even"):
+                 partition: str = "even", chunk: Optional[int] = None):
         """allocator(name, numel, dtype) -> tensor: where the flat buffers live (peer-shared memory for the fused
         NVLink collectives); default torch.zeros on `device`.
 
@@ -73,10 +74,16 @@ class FlatParams:
           "even"   -- parameters laid out in model order and the flat buffer cut into `world` equal contiguous
                       segments, so one large parameter (the 308M-element embedding) spreads over all owners and
                       every rank sends and receives the same bytes. The optimizer math is elementwise, so the
-                      partition changes no result; checkpoints store per-parameter state either way."""
+                      partition changes no result; checkpoints store per-parameter state either way.
+          "cyclic" -- parameters laid out in model order, the flat buffer cut into chunks of ``chunk`` elements
+                      (default 256 Ki) dealt to the ranks in turn: rank r owns chunks r, r + world, ... . Every
+                      large weight is spread over all owners, so an exchange that runs layer by layer during the
+                      backward pass (the GEMM-fused reduce-scatter) keeps every rank's NVLink port busy instead of
+                      one owner's. An owner's optimizer state is its owned chunks in order (local index c)."""
         named = [(n, p) for n, p in named_params if p.requires_grad]
         self.world, self.rank, self.device, self.dtype = world, rank, torch.device(device), dtype
         self.partition = partition
+        self.chunk = 0                     # 0: contiguous owner segments
         placed = []
         if partition == "greedy":
             owners = greedy_partition([p.numel() for _, p in named], world)
@@ -95,6 +102,17 @@ class FlatParams:
             placed = [(n, p, min(o // self.seg, world - 1), o - min(o // self.seg, world - 1) * self.seg)
                       for n, p, _, o in placed]
             self.used = [max(0, min(self.seg, off - r * self.seg)) for r in range(world)]
+        elif partition == "cyclic":
+            c = _round_up(int(chunk or CYCLIC_CHUNK), ALIGN)
+            off = 0
+            for name, p in named:
+                placed.append((name, p, None, off))
+                off = _round_up(off + p.numel(), ALIGN)
+            span = c * world
+            self.chunk = c
+            self.seg = max(_round_up(off, span), span) // world
+            placed = [(n, p, self.owner_of(o), o - self.owner_of(o) * self.seg) for n, p, _, o in placed]
+            self.used = [self.seg] * world
         else:
             raise ValueError(f"unknown partition {partition!r}")
         if allocator is None:
@@ -127,23 +145,58 @@ class FlatParams:
         self._scattered = set()
 
     # ---------------------------------------------------------------------------------------------------------
+    def owner_of(self, x: int) -> int:
+        """Owner rank of flat element x."""
+        return (x // self.chunk) % self.world if self.chunk else x // self.seg
+
+    def local_of(self, x: int) -> int:
+        """Index of flat element x in its owner's optimizer state."""
+        if self.chunk:
+            return (x // (self.chunk * self.world)) * self.chunk + x % self.chunk
+        return x - (x // self.seg) * self.seg
+
     def owned(self, rank: Optional[int] = None) -> slice:
+        """This owner's contiguous segment (contiguous layouts only)."""
+        if self.chunk:
+            raise RuntimeError("the block-cyclic layout has no contiguous owned segment (use owned_view)")
         r = self.rank if rank is None else rank
         return slice(r * self.seg, r * self.seg + self.seg)
 
+    def owned_view(self, buf: torch.Tensor, rank: Optional[int] = None) -> torch.Tensor:
+        """The owned elements of a flat buffer in local order: a contiguous [seg] slice, or in the block-cyclic
+        layout a strided [seg / chunk, chunk] view whose row-major order is the local order."""
+        r = self.rank if rank is None else rank
+        if self.chunk:
+            return buf.view(-1, self.world, self.chunk)[:, r, :]
+        return buf[r * self.seg:(r + 1) * self.seg]
+
     def param_segment(self, rank: Optional[int] = None) -> torch.Tensor:
-        return self.flat[self.owned(rank)]
+        return self.owned_view(self.flat, rank)
 
     def grad_segment(self, rank: Optional[int] = None) -> torch.Tensor:
-        return self.grad_flat[self.owned(rank)]
+        return self.owned_view(self.grad_flat, rank)
+
+    def to_owner_major(self, buf: torch.Tensor) -> torch.Tensor:
+        """A flat buffer rearranged as [world, seg] (row r = rank r's owned elements in local order): itself in the
+        contiguous layouts, a permuted copy in the block-cyclic one."""
+        if self.chunk:
+            return buf.view(-1, self.world, self.chunk).transpose(0, 1).reshape(self.world, self.seg)
+        return buf.view(self.world, self.seg)
+
+    def from_owner_major(self, buf: torch.Tensor, owner_major: torch.Tensor):
+        """Inverse of to_owner_major: write [world, seg] data back into the flat buffer."""
+        if self.chunk:
+            buf.view(-1, self.world, self.chunk).copy_(owner_major.view(self.world, -1, self.chunk).transpose(0, 1))
+        elif owner_major.data_ptr() != buf.data_ptr():
+            buf.copy_(owner_major.view(-1))
 
     def owner_ranges(self, e: "Entry"):
-        """[(global offset, count, owner)] pieces of one parameter, cut at segment boundaries."""
+        """[(global offset, count, owner)] pieces of one parameter, cut at owner boundaries (segment or chunk)."""
+        step = self.chunk or self.seg
         out, lo, hi = [], e.offset, e.offset + e.numel
         while lo < hi:
-            r = lo // self.seg
-            cut = min(hi, (r + 1) * self.seg)
-            out.append((lo, cut - lo, r))
+            cut = min(hi, (lo // step + 1) * step)
+            out.append((lo, cut - lo, self.owner_of(lo)))
             lo = cut
         return out
 
@@ -218,7 +271,7 @@ class ZeroOptimizer:
     def __init__(self, flat: FlatParams, optim_cfg, comm: str = "nccl", group=None, stage: int = 1):
         self.flat, self.cfg, self.comm, self.group, self.stage = flat, optim_cfg, comm, group, stage
         seg = flat.param_segment()
-        self.master = seg.float().clone()
+        self.master = seg.reshape(-1).float().clone()       # local order (a gather in the block-cyclic layout)
         self.exp_avg = torch.zeros_like(self.master)
         self.exp_avg_sq = torch.zeros_like(self.master)
         self.num_updates = 0
@@ -244,14 +297,18 @@ class ZeroOptimizer:
                 return self.p2p.finish_reduce()
             if fp.scatter is not None:
                 return self.p2p.reduce_scattered(fp)
-            return self.p2p.reduce_to_owner(fp.grad_flat, fp.seg, fp.used[fp.rank])
-        out = fp.grad_segment()
+            return self.p2p.reduce_to_owner(fp.grad_flat, fp.seg, fp.used[fp.rank], chunk=fp.chunk)
+        # library path: reduce-scatter over the owner-major arrangement (the buffer itself when contiguous)
+        src = fp.to_owner_major(fp.grad_flat).reshape(-1)
+        out = fp.grad_segment() if not fp.chunk else torch.empty(fp.seg, dtype=fp.dtype, device=fp.device)
         if dist.get_backend(self.group) == "nccl":
-            dist.reduce_scatter_tensor(out, fp.grad_flat, op=dist.ReduceOp.AVG, group=self.group)
+            dist.reduce_scatter_tensor(out, src, op=dist.ReduceOp.AVG, group=self.group)
         else:
             tmp = torch.empty_like(out)
-            dist.reduce_scatter_tensor(tmp, fp.grad_flat, op=dist.ReduceOp.SUM, group=self.group)
+            dist.reduce_scatter_tensor(tmp, src, op=dist.ReduceOp.SUM, group=self.group)
             out.copy_(tmp / fp.world)
+        if fp.chunk:
+            fp.grad_segment().copy_(out.view(-1, fp.chunk))
         return None
 
     def all_gather_params(self):
@@ -261,9 +318,14 @@ class ZeroOptimizer:
         if self.comm == "fused" and self.p2p is not None:
             if self.p2p.buckets is not None:
                 return          # pushed bucket by bucket ahead of the next update's forward (overlapped)
-            self.p2p.all_gather(fp.flat, fp.seg, fp.used)
+            self.p2p.all_gather(fp.flat, fp.seg, fp.used, chunk=fp.chunk)
             return
-        dist.all_gather_into_tensor(fp.flat, fp.param_segment(), group=self.group)
+        if not fp.chunk:
+            dist.all_gather_into_tensor(fp.flat, fp.param_segment(), group=self.group)
+            return
+        full = torch.empty(fp.world * fp.seg, dtype=fp.dtype, device=fp.device)
+        dist.all_gather_into_tensor(full, fp.param_segment().reshape(-1), group=self.group)
+        fp.from_owner_major(fp.flat, full.view(fp.world, fp.seg))
 
     def prepare(self, lr: float):
         """Host part before an update: learning rate and bias corrections into the device hyper-parameter vector."""
@@ -290,7 +352,7 @@ class ZeroOptimizer:
         if sq is not None:
             sq = sq.clone()
         elif native:
-            sq = ops._C().sq_norm(g16)
+            sq = ops._C().sq_norm(g16.reshape(-1))
         else:
             sq = g16.float().pow(2).sum().reshape(1)
         if fp.world > 1:
@@ -306,17 +368,21 @@ class ZeroOptimizer:
         seg = fp.param_segment()
         fused_push = (native and fp.world > 1 and self.comm == "fused" and self.p2p is not None
                       and self.p2p.buckets is None and self.fuse_adam_push)
+        # the kernels address this owner's bf16 gradients / parameters through the owner map: its segment views
+        # (contiguous layouts) or the whole flat buffers + the chunk size (block-cyclic)
+        g_arg, p_arg = (fp.grad_flat, fp.flat) if fp.chunk else (g16, seg)
         if fused_push:
             # one pass: Adam on this owner's segment + the all-gather push of its new bf16 values to every peer
-            ops._C().adam_push(self.master, g16, self.exp_avg, self.exp_avg_sq, seg, self.hyper,
+            ops._C().adam_push(self.master, g_arg, self.exp_avg, self.exp_avg_sq, p_arg, self.hyper,
                                factor.reshape(1).float().contiguous(), float(b1), float(b2), float(self.cfg.eps),
                                float(self.cfg.weight_decay), bool(self.cfg.adamw_mode), self.p2p.peers["param"],
-                               fp.owned().start, fp.rank)
+                               0 if fp.chunk else fp.owned().start, fp.rank, fp.chunk)
             self.p2p.barrier()
         elif native:
-            ops._C().adam_step(self.master, g16, self.exp_avg, self.exp_avg_sq, seg, self.hyper,
+            ops._C().adam_step(self.master, g_arg, self.exp_avg, self.exp_avg_sq, p_arg, self.hyper,
                                factor.reshape(1).float().contiguous(), float(b1), float(b2), float(self.cfg.eps),
-                               float(self.cfg.weight_decay), bool(self.cfg.adamw_mode))
+                               float(self.cfg.weight_decay), bool(self.cfg.adamw_mode), fp.chunk, fp.world,
+                               fp.rank)
         else:
             self._torch_adam(g16, seg, factor, self._lr)
         if not fused_push:
@@ -333,20 +399,21 @@ class ZeroOptimizer:
     def _torch_adam(self, g16, seg, factor, lr):
         from ..ops import reference as ref
         b1, b2 = self.cfg.betas
-        g32 = g16.float() * factor.float()
+        g32 = g16.reshape(-1).float() * factor.float()
         ref.adam_step_(self.master, g32, self.exp_avg, self.exp_avg_sq, lr=lr, beta1=b1, beta2=b2,
                        eps=self.cfg.eps, step=self.num_updates + 1, weight_decay=self.cfg.weight_decay,
-                       adamw=self.cfg.adamw_mode, p16=seg)
+                       adamw=self.cfg.adamw_mode)
+        seg.copy_(self.master.view(seg.shape).to(seg.dtype))
 
     # ---------------------------------------------------------------------------------------------------------
     def state_dict(self):
         return {"num_updates": self.num_updates, "master": self.master, "exp_avg": self.exp_avg,
                 "exp_avg_sq": self.exp_avg_sq, "seg": self.flat.seg, "rank": self.flat.rank,
-                "world": self.flat.world}
+                "world": self.flat.world, "chunk": self.flat.chunk}
 
     def load_state_dict(self, sd):
-        if sd["seg"] != self.flat.seg or sd["world"] != self.flat.world:
-            raise ValueError("optimizer shard layout does not match this run (seg/world differ)")
+        if sd["seg"] != self.flat.seg or sd["world"] != self.flat.world or sd.get("chunk", 0) != self.flat.chunk:
+            raise ValueError("optimizer shard layout does not match this run (seg/world/chunk differ)")
         self.num_updates = int(sd["num_updates"])
         self.master.copy_(sd["master"])
         self.exp_avg.copy_(sd["exp_avg"])
@@ -362,6 +429,10 @@ class ZeroOptimizer:
                 dist.all_gather_into_tensor(full, t, group=self.group)
             else:
                 full = t
+            if fp.chunk:                      # owner-major -> flat order
+                flat_order = torch.empty_like(full)
+                fp.from_owner_major(flat_order, full.view(fp.world, fp.seg))
+                full = flat_order
             shards[name] = full
         out = {}
         for e in fp.entries:

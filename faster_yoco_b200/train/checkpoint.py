@@ -121,13 +121,12 @@ def load_checkpoint(path: str, model, trainer) -> dict:
     st = ck.get("last_optimizer_state") or {}
     zero = trainer.zero
     fp = trainer.flat
-    own = fp.owned()
     with torch.no_grad():
         for e in fp.entries:
             for off, cnt, owner in fp.owner_ranges(e):
                 if owner != fp.rank:
                     continue
-                lo = off - own.start            # position in this rank's shard
+                lo = fp.local_of(off)           # position in this rank's shard (a piece is contiguous there)
                 pe = off - e.offset             # position inside the parameter
                 for key, dst in (("master", zero.master), ("exp_avg", zero.exp_avg),
                                  ("exp_avg_sq", zero.exp_avg_sq)):

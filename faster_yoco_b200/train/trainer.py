@@ -45,7 +45,8 @@ class _CommHooks:
 class Trainer:
     def __init__(self, model: torch.nn.Module, optim_cfg, *, device, comm: str = "nccl", zero_stage: int = 1,
                  pad_idx: int = 1, graph_step: bool = False, group=None, check_consistency: bool = True,
-                 overlap: bool = False, partition: str = "even", criterion=None, transport: str = "sm"):
+                 overlap: bool = False, partition: str = "even", criterion=None, transport: str = "sm",
+                 chunk: Optional[int] = None):
         from ..parallel import tp as TP
         if TP.tp_size() > 1:
             raise NotImplementedError(
@@ -63,7 +64,7 @@ class Trainer:
             p2p = PeerComm(group)
         self.flat = FlatParams(model.named_parameters(), self.world, self.rank, self.device,
                                dtype=next(model.parameters()).dtype, allocator=p2p.alloc if p2p else None,
-                               partition=partition)
+                               partition=partition, chunk=chunk)
         self.flat.direct_grads = self.device.type == "cuda" and ops.get_backend() == "native"
         self.zero = ZeroOptimizer(self.flat, optim_cfg, comm=comm, group=group, stage=zero_stage)
         self.zero.p2p = p2p

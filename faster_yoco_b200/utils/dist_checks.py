@@ -8,7 +8,7 @@ import torch.distributed as dist
 
 
 def _tiny_trainer(device, comm="nccl", seed=0, graph=False, arch="yoco_tiny", dtype=torch.float32, overlap=True,
-                  transport="sm"):
+                  transport="sm", partition="even", chunk=None):
     from ..config import OptimConfig, build_args
     from ..models.yoco import YOCO
     from ..train.trainer import Trainer
@@ -17,7 +17,7 @@ def _tiny_trainer(device, comm="nccl", seed=0, graph=False, arch="yoco_tiny", dt
     model = YOCO(args).to(device=device, dtype=dtype)
     cfg = OptimConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, warmup_updates=0, total_num_update=20)
     return model, Trainer(model, cfg, device=device, comm=comm, graph_step=graph, overlap=overlap,
-                          transport=transport)
+                          transport=transport, partition=partition, chunk=chunk)
 
 
 def _batches(rank, world, n, seed=1, batch=2, seq=256, vocab=1024):
@@ -29,9 +29,9 @@ def _batches(rank, world, n, seed=1, batch=2, seq=256, vocab=1024):
     return out
 
 
-def zero_matches_single(rank, world, outdir, steps):
+def zero_matches_single(rank, world, outdir, steps, partition="even", chunk=None):
     """World-size-N ZeRO training on N shards of each global batch; rank 0 saves the final flat params."""
-    model, tr = _tiny_trainer(torch.device("cpu"))
+    model, tr = _tiny_trainer(torch.device("cpu"), partition=partition, chunk=chunk)
     for ids in _batches(rank, world, steps):
         mine = ids[rank]
         b = {"src_tokens": mine[:, :-1].contiguous(), "target": mine[:, 1:].contiguous(),
@@ -39,7 +39,7 @@ def zero_matches_single(rank, world, outdir, steps):
         tr.train_step(b)
     sd = {k: v.detach().clone() for k, v in model.state_dict().items()}
     if rank == 0:
-        torch.save({"sd": sd, "num_updates": tr.num_updates()}, os.path.join(outdir, f"ws{world}.pt"))
+        torch.save({"sd": sd, "num_updates": tr.num_updates()}, os.path.join(outdir, f"ws{world}_{partition}.pt"))
 
 
 def single_reference(outdir, world, steps):
@@ -53,8 +53,9 @@ def single_reference(outdir, world, steps):
     return {k: v.detach().clone() for k, v in model.state_dict().items()}
 
 
-def checkpoint_resume(rank, world, outdir, steps, split):
-    """Train `steps`, or train `split`, checkpoint, rebuild everything, load, train the rest."""
+def checkpoint_resume(rank, world, outdir, steps, split, partition="even", chunk=None, resume_partition=None):
+    """Train `steps`, or train `split`, checkpoint, rebuild everything (optionally with another owner map: the
+    checkpoint holds per-parameter optimizer state), load, train the rest."""
     from ..train.checkpoint import load_checkpoint, save_checkpoint
     batches = _batches(rank, world, steps)
 
@@ -64,15 +65,17 @@ def checkpoint_resume(rank, world, outdir, steps, split):
             tr.train_step({"src_tokens": mine[:, :-1].contiguous(), "target": mine[:, 1:].contiguous(),
                            "ntokens": mine.shape[0] * mine.shape[1], "nsentences": mine.shape[0]})
 
-    model, tr = _tiny_trainer(torch.device("cpu"))
+    model, tr = _tiny_trainer(torch.device("cpu"), partition=partition, chunk=chunk)
     run(tr, batches[:split])
     path = os.path.join(outdir, "ckpt.pt")
     save_checkpoint(path, model, tr)
     dist.barrier()
-    model2, tr2 = _tiny_trainer(torch.device("cpu"), seed=123)      # different init: must be overwritten
+    rp = resume_partition or partition
+    model2, tr2 = _tiny_trainer(torch.device("cpu"), seed=123, partition=rp,  # different init: must be overwritten
+                                chunk=chunk)
     load_checkpoint(path, model2, tr2)
     run(tr2, batches[split:])
-    model3, tr3 = _tiny_trainer(torch.device("cpu"))
+    model3, tr3 = _tiny_trainer(torch.device("cpu"), partition=partition, chunk=chunk)
     run(tr3, batches)
     if rank == 0:
         torch.save({"resumed": model2.state_dict(), "straight": model3.state_dict(),
@@ -125,11 +128,13 @@ def gemm_scatter_vs_serial_gpu(rank, world, outdir, steps):
     ops.set_backend("native")
     dev = torch.device("cuda", rank)
     res = {}
-    for name, transport, graph, uf in (("serial", "sm", False, 1), ("gemm", "gemm", False, 1),
-                                       ("gemm_graph", "gemm", True, 1), ("serial_uf2", "sm", False, 2),
-                                       ("gemm_uf2", "gemm", False, 2)):
+    for name, transport, graph, uf, part in (
+            ("serial", "sm", False, 1, "even"), ("gemm", "gemm", False, 1, "even"),
+            ("gemm_graph", "gemm", True, 1, "even"), ("serial_uf2", "sm", False, 2, "even"),
+            ("gemm_uf2", "gemm", False, 2, "even"), ("serial_cyclic", "sm", False, 1, "cyclic"),
+            ("gemm_cyclic", "gemm", False, 1, "cyclic"), ("gemm_cyclic_graph", "gemm", True, 1, "cyclic")):
         model, tr = _tiny_trainer(dev, comm="fused", arch="yoco_small", dtype=torch.bfloat16, overlap=False,
-                                  transport=transport, graph=graph)
+                                  transport=transport, graph=graph, partition=part, chunk=1 << 14)
         losses = []
         for ids in _batches(rank, world, steps, seq=256, vocab=8192, batch=2 * uf):
             mine = ids[rank]

@@ -17,18 +17,21 @@ def test_greedy_partition_is_oss_rule():
     assert greedy_partition([100, 1, 1, 1], 3) == [0, 1, 2, 1]
 
 
-def test_zero_ws2_matches_single_process(tmp_path):
+@pytest.mark.parametrize("partition,chunk", [("even", None), ("cyclic", 1024)])
+def test_zero_ws2_matches_single_process(tmp_path, partition, chunk):
     steps = 3
-    run_ranks(dist_checks.zero_matches_single, 2, str(tmp_path), steps)
-    got = torch.load(os.path.join(tmp_path, "ws2.pt"))
+    run_ranks(dist_checks.zero_matches_single, 2, str(tmp_path), steps, partition, chunk)
+    got = torch.load(os.path.join(tmp_path, f"ws2_{partition}.pt"))
     assert got["num_updates"] == steps
     ref = dist_checks.single_reference(str(tmp_path), 2, steps)
     for k, v in ref.items():
         assert torch.allclose(got["sd"][k].float(), v.float(), atol=2e-5, rtol=1e-4), k
 
 
-def test_checkpoint_resume_matches_uninterrupted(tmp_path):
-    run_ranks(dist_checks.checkpoint_resume, 2, str(tmp_path), 4, 2)
+@pytest.mark.parametrize("partition,resume_partition", [("even", "even"), ("cyclic", "cyclic"),
+                                                        ("cyclic", "even")])
+def test_checkpoint_resume_matches_uninterrupted(tmp_path, partition, resume_partition):
+    run_ranks(dist_checks.checkpoint_resume, 2, str(tmp_path), 4, 2, partition, 1024, resume_partition)
     r = torch.load(os.path.join(tmp_path, "resume.pt"))
     assert r["n2"] == r["n3"] == 4
     for k, v in r["straight"].items():

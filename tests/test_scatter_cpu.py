@@ -1,5 +1,6 @@
 """GEMM-fused ZeRO reduce-scatter, host side (CPU): where each weight-gradient element is stored, that the owners'
 staged sums equal the plain average over ranks, and the push / own tables that complete the exchange."""
+import pytest
 import torch
 
 from faster_yoco_b200.ops import reference as ref
@@ -56,23 +57,25 @@ class _FakePeers:
         self.tables = PeerComm._scatter_tables_for.__get__(self)
 
 
-def test_scatter_tables_cover_every_piece_once():
+@pytest.mark.parametrize("partition", ["even", "cyclic"])
+def test_scatter_tables_cover_every_piece_once(partition):
     world = 3
     for rank in range(world):
-        fp = FlatParams(_model().named_parameters(), world, rank, "cpu")
+        fp = FlatParams(_model().named_parameters(), world, rank, "cpu", partition=partition, chunk=256)
         fp.scatter = torch.zeros(world, dtype=torch.int64)
         fp.begin_update()
         gemm_written = [e for e in fp.entries if e.name in ("qkv.weight", "fc.weight")]
         for e in gemm_written:
             assert fp.scatter_target(e.param) is fp.scatter
-        push, own = _FakePeers(rank).tables(fp)
-        pieces = [pc for e in fp.entries for pc in fp.owner_ranges(e)]
-        want_own = sorted((o, c) for o, c, r in pieces if r == rank)
+        push = _FakePeers(rank).tables(fp)
         scattered = {id(e.param) for e in gemm_written}
         want_push = sorted((o, c, r) for e in fp.entries if id(e.param) not in scattered
                            for o, c, r in fp.owner_ranges(e) if r != rank)
-        assert sorted(map(tuple, own.tolist())) == want_own
         assert sorted(map(tuple, push.tolist())) == want_push
+        # together with the GEMM-written weights, every piece another rank owns reaches it exactly once
+        sent = sorted(map(tuple, push.tolist())) + sorted(
+            (o, c, r) for e in gemm_written for o, c, r in fp.owner_ranges(e) if r != rank)
+        assert sorted(sent) == sorted((o, c, r) for e in fp.entries for o, c, r in fp.owner_ranges(e) if r != rank)
 
 
 def test_scatter_target_only_on_last_microbatch():
@@ -93,3 +96,63 @@ def test_scatter_target_only_on_last_microbatch():
         assert "owners" in str(e)
     else:
         raise AssertionError("collect_grads accepted an autograd gradient for a scattered weight")
+
+
+def test_cyclic_owner_map_is_consistent():
+    world, chunk = 3, 128
+    fp = FlatParams(_model().named_parameters(), world, 1, "cpu", partition="cyclic", chunk=chunk)
+    assert fp.chunk == chunk and fp.seg % chunk == 0 and fp.flat.numel() == world * fp.seg
+    n = fp.flat.numel()
+    x = torch.arange(n)
+    owner = torch.tensor([fp.owner_of(int(i)) for i in x])
+    local = torch.tensor([fp.local_of(int(i)) for i in x])
+    # every (owner, local) pair is hit exactly once and local indices cover [0, seg) per owner
+    for r in range(world):
+        assert sorted(local[owner == r].tolist()) == list(range(fp.seg))
+    # the owned view lists this rank's elements in local order
+    probe = x.to(torch.float64)
+    for r in range(world):
+        v = fp.owned_view(probe, r).reshape(-1)
+        assert torch.equal(local[v.long()], torch.arange(fp.seg)) and bool((owner[v.long()] == r).all())
+    # owner-major arrangement and back
+    om = fp.to_owner_major(probe)
+    assert om.shape == (world, fp.seg)
+    back = torch.empty_like(probe)
+    fp.from_owner_major(back, om)
+    assert torch.equal(back, probe)
+    # pieces never cross a chunk and carry their owner; every large weight has pieces at every owner
+    for e in fp.entries:
+        pcs = fp.owner_ranges(e)
+        assert sum(c for _, c, _ in pcs) == e.numel
+        for o, c, r in pcs:
+            assert o // chunk == (o + c - 1) // chunk and fp.owner_of(o) == r
+        if e.numel >= world * chunk * 2:
+            assert {r for _, _, r in pcs} == set(range(world))
+
+
+def test_owner_scatter_cyclic_staging_layout():
+    """The cyclic layout's scatter destination: owner (x // chunk) % world, slot position local(x)."""
+    world, chunk, rank = 4, 64, 2
+    fp = FlatParams(_model().named_parameters(), world, rank, "cpu", partition="cyclic", chunk=chunk)
+    seg = fp.seg
+    e = max(fp.entries, key=lambda t: t.numel)
+    dw = torch.randn(e.shape).to(torch.bfloat16)
+    own = torch.zeros(world * seg, dtype=torch.bfloat16)
+    staging = [torch.zeros(world * seg, dtype=torch.bfloat16) for _ in range(world)]
+    flat = dw.reshape(-1)
+    for i in range(flat.numel()):
+        x = e.offset + i
+        o = fp.owner_of(x)
+        if o == rank:
+            own[x] = flat[i]
+        else:
+            staging[o][rank * seg + fp.local_of(x)] = flat[i]
+    # the owner-side view: owner o reads slot `rank` in local order; the elements it owns of this weight match
+    for o in range(world):
+        if o == rank:
+            continue
+        for off, c, r in fp.owner_ranges(e):
+            if r != o:
+                continue
+            lo = fp.local_of(off)
+            assert torch.equal(staging[o][rank * seg + lo: rank * seg + lo + c], flat[off - e.offset: off - e.offset + c])
