@@ -46,9 +46,10 @@ def parse():
                         "(serial P2P reduce + push all-gather after backward) at more GPUs, where the copy engines "
                         "deliver only ~210 GB/s in aggregate to 7 peers")
     p.add_argument("--transport", default="auto", choices=["auto", "sm", "ce", "gemm"],
-                   help="overlapped exchange: pushes by kernels (sm) or by the copy engines (ce); gemm: serial "
-                        "schedule whose weight-gradient GEMMs store every element at its ZeRO owner over NVLink "
-                        "(GEMM fused with the reduce-scatter)")
+                   help="overlapped exchange: pushes by kernels (sm) or by the copy engines (ce); gemm: the "
+                        "weight-gradient GEMMs store every element at its ZeRO owner over NVLink (GEMM fused with the "
+                        "reduce-scatter), parameters pushed after the update (--overlap 0) or per layer ahead of "
+                        "the next forward (--overlap 1)")
     p.add_argument("--partition", default="even", choices=["even", "greedy", "cyclic"],
                    help="ZeRO owner map: even contiguous segments, the OSS greedy per-parameter rule, or block-cyclic "
                         "chunks (every weight spread over all owners)")
@@ -192,8 +193,6 @@ def main():
         args.overlap = 1 if (world == 2 and args.comm == "fused" and args.transport != "gemm") else 0
     else:
         args.overlap = int(args.overlap)
-    if args.transport == "gemm" and args.overlap:
-        raise SystemExit("--transport gemm runs the serial exchange schedule (--overlap 0)")
     if args.transport == "auto":
         args.transport = "ce" if world == 2 else "sm"
     torch.manual_seed(1234)

@@ -128,8 +128,6 @@ def main(argv=None) -> int:
     comm = args.comm if (world > 1 and device.type == "cuda" and args.context_parallel_size == 1) else "nccl"
     overlap = (world == 2 and comm == "fused" and args.transport != "gemm") if str(args.overlap) == "auto" \
         else bool(_flag(args.overlap))
-    if args.transport == "gemm" and overlap:
-        raise SystemExit("--transport gemm runs the serial exchange schedule (--overlap 0)")
     transport = ("ce" if world == 2 else "sm") if args.transport == "auto" else args.transport
     graph = bool(args.cuda_graph) and device.type == "cuda" and args.context_parallel_size == 1
     trainer = Trainer(model, optim, device=device, comm=comm, graph_step=graph,

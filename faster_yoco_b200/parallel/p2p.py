@@ -169,7 +169,7 @@ class PeerComm:
 
     # ------------------------------------------------------------------------------------ overlapped (bucketed)
     def setup_buckets(self, flat, groups, reduce_ctas: Optional[int] = None, gather_ctas: Optional[int] = None,
-                      transport: str = "sm"):
+                      transport: str = "sm", grads: str = "push"):
         """groups: parameter lists in FORWARD order (bucket b = groups[b]). Precomputes, per bucket, the ranges this
         rank owns (reduced during backward) and the ranges it must pull from other owners (before forward).
 
@@ -178,12 +178,12 @@ class PeerComm:
         the overlapped forward / backward), each followed by a one-thread kernel that publishes the arrival."""
         if len(groups) > self.NSLOTS - 3:
             raise ValueError("too many buckets")
-        if transport not in ("sm", "ce"):
-            raise ValueError(transport)
-        if flat.chunk:
-            raise ValueError("the bucketed overlap transports run on contiguous owner segments (partition even / "
-                             "greedy), not on the block-cyclic layout")
+        if transport not in ("sm", "ce") or grads not in ("push", "scatter"):
+            raise ValueError((transport, grads))
         self.transport = transport
+        # grads "scatter": the weight-gradient GEMMs store at the owners (setup_scatter), so no bucket pushes
+        # gradients; finish_reduce pushes the rest and sums (reduce_scattered)
+        self.grads_mode = grads
         import os
         reduce_ctas = int(os.environ.get("FYB_REDUCE_CTAS", reduce_ctas or 128))
         gather_ctas = int(os.environ.get("FYB_PUSH_CTAS", gather_ctas or 128))
@@ -203,7 +203,8 @@ class PeerComm:
         self.expected = torch.zeros(self.NSLOTS, dtype=torch.int32, device=self.dev)
         self.push_ctas = gather_ctas
         # push-based gradient reduction: peers store their pieces of this rank's segment into staging slot [peer]
-        self.staging = self.alloc("staging", self.world * flat.seg, flat.dtype)
+        if "staging" not in self.peers:
+            self.staging = self.alloc("staging", self.world * flat.seg, flat.dtype)
         self.garrive, self.peer_garrive = self.share_bytes(self.NSLOTS * 4)
         self.gexpected = torch.zeros(self.NSLOTS, dtype=torch.int32, device=self.dev)
         self.grad_push_ctas = reduce_ctas
@@ -246,12 +247,12 @@ class PeerComm:
         esz = self.flat.grad_flat.element_size()
         seg_b = self.flat.seg * esz
         for q, st in self.peer_streams.items():
-            dst = self.peers["staging"][q] + self.rank * seg_b - q * seg_b
+            slot = self.peers["staging"][q] + self.rank * seg_b     # owner q's staging slot for this rank
             with torch.cuda.stream(st):
                 st.wait_event(self.ready_ev[b])
                 for o, c, owner in self.ce_other[b]:
                     if owner == q:
-                        self.C.peer_copy(dst + o, grad + o, c)
+                        self.C.peer_copy(slot + self.flat.local_of(o // esz) * esz, grad + o, c)
                 self.C.signal_peer(self.peer_garrive[q], b)
 
     def _ce_finish_reduce(self) -> torch.Tensor:
@@ -263,7 +264,7 @@ class PeerComm:
         owned_all = self._owned_all()
         part = self.bucket_part.view(-1)[: self.red_ctas_all]
         self.C.reduce_staged(self.flat.grad_flat, self.staging, owned_all, self.world, self.rank, self.flat.seg,
-                             part, self.red_ctas_all)
+                             part, self.red_ctas_all, self.flat.chunk)
         self.C.sum_partials(part, self.sq)
         return self.sq
 
@@ -303,6 +304,8 @@ class PeerComm:
         if self._reduced[b]:
             return
         self._reduced[b] = True
+        if self.grads_mode == "scatter":
+            return
         if self.transport == "ce":
             return self._ce_bucket_ready(b)
         owned, other = self.buckets
@@ -311,10 +314,10 @@ class PeerComm:
             self.stream.wait_event(self.ready_ev[b])
             # push my pieces of bucket b to their owners, wait for every peer's pieces of my part, sum locally
             self.C.push_grads(self.flat.grad_flat, self.peers["staging"], self.peer_garrive, other[b], b, self.rank,
-                              self.flat.seg, self.grad_push_ctas)
+                              self.flat.seg, self.grad_push_ctas, self.flat.chunk)
             self.C.wait_arrivals(self.garrive, self.gexpected, b, (self.world - 1) * self.grad_push_ctas)
             self.C.reduce_staged(self.flat.grad_flat, self.staging, owned[b], self.world, self.rank, self.flat.seg,
-                                 self.bucket_part[b], self.red_ctas)
+                                 self.bucket_part[b], self.red_ctas, self.flat.chunk)
 
     def finish_reduce(self) -> torch.Tensor:
         """Reduce the buckets no hook reported (in bucket order), join the streams, and return this owner's sum of
@@ -322,6 +325,12 @@ class PeerComm:
         for b in range(self.nb):
             if not self._reduced[b]:
                 self.bucket_ready(b)
+        if self.grads_mode == "scatter":
+            cur = torch.cuda.current_stream(self.dev)
+            cur.wait_stream(self.stream)                 # this update's parameter pushes are done
+            for st in getattr(self, "peer_streams", {}).values():
+                cur.wait_stream(st)
+            return self.reduce_scattered(self.flat)
         if self.transport == "ce":
             return self._ce_finish_reduce()
         torch.cuda.current_stream(self.dev).wait_stream(self.stream)

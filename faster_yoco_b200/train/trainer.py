@@ -70,13 +70,17 @@ class Trainer:
         self.zero.p2p = p2p
         if transport not in ("sm", "ce", "gemm"):
             raise ValueError(f"unknown transport {transport!r}")
-        self.overlap = p2p is not None and overlap and hasattr(model, "param_buckets") and transport != "gemm"
-        if self.overlap:
-            p2p.setup_buckets(self.flat, model.param_buckets(), transport=transport)
-        elif p2p is not None and transport == "gemm":
+        self.overlap = p2p is not None and overlap and hasattr(model, "param_buckets")
+        if p2p is not None and transport == "gemm":
+            # gradients: the weight-gradient GEMMs store at the owners; parameters: pushed per layer bucket ahead of
+            # the next forward (overlap) or by the fused Adam + push after the update (serial)
             if not self.flat.direct_grads:
                 raise ValueError("transport 'gemm' needs the native kernels (weight gradients written by the GEMM)")
             p2p.setup_scatter(self.flat)
+            if self.overlap:
+                p2p.setup_buckets(self.flat, model.param_buckets(), transport="sm", grads="scatter")
+        elif self.overlap:
+            p2p.setup_buckets(self.flat, model.param_buckets(), transport=transport)
         self.sched = PolynomialDecaySchedule(optim_cfg.lr, optim_cfg.warmup_updates, optim_cfg.total_num_update,
                                              optim_cfg.end_learning_rate, optim_cfg.power)
         self.pending = PendingChecks(self.device.type == "cuda")

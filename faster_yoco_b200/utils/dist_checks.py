@@ -132,9 +132,12 @@ def gemm_scatter_vs_serial_gpu(rank, world, outdir, steps):
             ("serial", "sm", False, 1, "even"), ("gemm", "gemm", False, 1, "even"),
             ("gemm_graph", "gemm", True, 1, "even"), ("serial_uf2", "sm", False, 2, "even"),
             ("gemm_uf2", "gemm", False, 2, "even"), ("serial_cyclic", "sm", False, 1, "cyclic"),
-            ("gemm_cyclic", "gemm", False, 1, "cyclic"), ("gemm_cyclic_graph", "gemm", True, 1, "cyclic")):
-        model, tr = _tiny_trainer(dev, comm="fused", arch="yoco_small", dtype=torch.bfloat16, overlap=False,
-                                  transport=transport, graph=graph, partition=part, chunk=1 << 14)
+            ("gemm_cyclic", "gemm", False, 1, "cyclic"), ("gemm_cyclic_graph", "gemm", True, 1, "cyclic"),
+            ("gemm_overlap_cyclic", "gemm+overlap", True, 1, "cyclic"), ("sm_overlap_cyclic", "sm+overlap", False,
+                                                                          1, "cyclic")):
+        overlap = transport.endswith("+overlap")
+        model, tr = _tiny_trainer(dev, comm="fused", arch="yoco_small", dtype=torch.bfloat16, overlap=overlap,
+                                  transport=transport.split("+")[0], graph=graph, partition=part, chunk=1 << 14)
         losses = []
         for ids in _batches(rank, world, steps, seq=256, vocab=8192, batch=2 * uf):
             mine = ids[rank]
