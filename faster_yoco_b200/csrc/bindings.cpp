@@ -74,6 +74,11 @@ void reduce_staged(at::Tensor& grad, const at::Tensor& staging, const at::Tensor
                    int64_t seg, at::Tensor& part, int64_t ctas, int64_t chunk);
 void reduce_compact(at::Tensor& grad, const at::Tensor& staging, int64_t n, int64_t world, int64_t rank, int64_t seg,
                     int64_t chunk, at::Tensor& part, int64_t ctas);
+void zero_staged(at::Tensor& staging, const at::Tensor& ranges, int64_t world, int64_t rank, int64_t seg,
+                 int64_t ctas);
+void embedding_bwd_scatter(const at::Tensor& tok, const at::Tensor& dy, double scale, at::Tensor& slot,
+                           const at::Tensor& grad_flat, const at::Tensor& bases, int64_t seg, int64_t rank,
+                           int64_t chunk);
 void push_range(const at::Tensor& src, const std::vector<int64_t>& peer_dst, int64_t off, int64_t n, int64_t rank,
                 int64_t ctas, int64_t chunk);
 void mailbox_put(const std::vector<int64_t>& peer_boxes, const at::Tensor& vals, int64_t rank,
@@ -173,6 +178,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "owner's segment summed from its gradient buffer and the staging slots (GEMM-fused reduce-scatter)",
         py::arg("grad"), py::arg("staging"), py::arg("n"), py::arg("world"), py::arg("rank"), py::arg("seg"),
         py::arg("chunk"), py::arg("part"), py::arg("ctas"));
+  m.def("zero_staged", &fyb::zero_staged, "clear other ranks' staging slots over local ranges [n, 2]",
+        py::arg("staging"), py::arg("ranges"), py::arg("world"), py::arg("rank"), py::arg("seg"), py::arg("ctas"));
+  m.def("embedding_bwd_scatter", &fyb::embedding_bwd_scatter,
+        "embedding weight gradient, touched rows stored at their ZeRO owners", py::arg("tok"), py::arg("dy"),
+        py::arg("scale"), py::arg("slot"), py::arg("grad_flat"), py::arg("bases"), py::arg("seg"), py::arg("rank"),
+        py::arg("chunk") = 0);
   m.def("mailbox_put", &fyb::mailbox_put);
   m.def("mailbox_sum", &fyb::mailbox_sum);
   m.def("status", &fyb::status_tensor, "device status word of the kernels with bounded waits");

@@ -378,6 +378,25 @@ __global__ void reduce_compact_kernel(__nv_bfloat16* __restrict__ grad, const __
   }
 }
 
+// Clear the staging slots of every other rank over the listed local ranges ([n][2] = (local offset, count)) of this
+// owner's segment: the regions peers fill sparsely (the embedding rows of the tokens in their batch) must read zero
+// where nothing was stored.
+__global__ void zero_staged_kernel(__nv_bfloat16* __restrict__ staging, const int64_t* __restrict__ ranges,
+                                   int nranges, int world, int rank, int64_t seg) {
+  const int64_t nthr = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  for (int rg = 0; rg < nranges; ++rg) {
+    const int64_t lo = ranges[2 * rg], n = ranges[2 * rg + 1];
+    for (int r = 0; r < world; ++r) {
+      if (r == rank) continue;
+      __nv_bfloat16* p = staging + static_cast<int64_t>(r) * seg + lo;
+      const int64_t nv = n / 8;
+      for (int64_t i = tid; i < nv; i += nthr) reinterpret_cast<uint4*>(p)[i] = make_uint4(0, 0, 0, 0);
+      for (int64_t j = nv * 8 + tid; j < n; j += nthr) p[j] = __float2bfloat16_rn(0.f);
+    }
+  }
+}
+
 // Compute-stream wait until bucket b's pushes of the current update have all arrived: expected[b] += increment, then
 // spin (bounded) until arrive[b] >= expected[b]. The expectation is device-resident, so graph replays stay correct.
 __global__ void wait_arrivals_kernel(const uint32_t* __restrict__ arrive, uint32_t* __restrict__ expected, int bucket,
@@ -577,6 +596,19 @@ void reduce_staged(at::Tensor& grad, const at::Tensor& staging, const at::Tensor
       ranges.data_ptr<int64_t>(), static_cast<int>(ranges.size(0)), static_cast<int>(world), static_cast<int>(rank),
       seg, 1.0f / static_cast<float>(world), part.data_ptr<float>(), chunk);
   check_launch("reduce_staged");
+}
+
+void zero_staged(at::Tensor& staging, const at::Tensor& ranges, int64_t world, int64_t rank, int64_t seg,
+                 int64_t ctas) {
+  FYB_RANGE("fyb::zero_staged");
+  FYB_CHECK(ranges.is_cuda() && ranges.scalar_type() == at::kLong && ranges.dim() == 2 && ranges.size(1) == 2,
+            "zero_staged: ranges must be a device int64 [n, 2]");
+  FYB_CHECK(staging.numel() == world * seg && seg % 8 == 0, "zero_staged: staging of world x seg elements");
+  if (ranges.size(0) == 0) return;
+  zero_staged_kernel<<<static_cast<int>(ctas), 256, 0, cur_stream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(staging.data_ptr()), ranges.data_ptr<int64_t>(),
+      static_cast<int>(ranges.size(0)), static_cast<int>(world), static_cast<int>(rank), seg);
+  check_launch("zero_staged");
 }
 
 // The owner's n local elements summed from its gradient buffer (own values) and the staging slots (peers'), written

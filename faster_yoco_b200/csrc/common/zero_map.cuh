@@ -8,6 +8,8 @@
 // An owner's optimizer state is compact: its c-th owned element has "local" index c in [0, seg).
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include <cstdint>
 
 namespace fyb {
@@ -35,6 +37,25 @@ __host__ __device__ __forceinline__ int64_t zero_local(int64_t chunk, int world,
   if (chunk == 0) return x - (x / seg) * seg;
   const int64_t span = chunk * world;
   return (x / span) * chunk + x % chunk;
+}
+
+// Owner scatter (a gradient producer fused with the ZeRO reduce-scatter): a weight's gradient slot starts at flat
+// index x0 of the gradient buffer; instead of storing element x locally, the producer stores it where its owner o
+// sums it: this rank's own buffer when o == rank, else owner o's staging buffer, slot `rank`, at the element's local
+// index (bases[o] + rank * seg + local(x)), over NVLink. Every 8-element vector lies inside one segment / chunk
+// (seg, chunk, x0 and the row length multiples of 8), so one owner lookup per vector.
+struct OwnerScatter {
+  const unsigned long long* bases;   // [world] staging buffer of every rank (peer pointers)
+  __nv_bfloat16* own;                // this rank's flat gradient buffer
+  int64_t x0, seg, chunk;
+  int rank, world;
+};
+
+__device__ __forceinline__ __nv_bfloat16* owner_dst(const OwnerScatter& s, int64_t x) {
+  const int o = zero_owner(s.chunk, s.world, s.seg, x);
+  if (o == s.rank) return s.own + x;
+  return reinterpret_cast<__nv_bfloat16*>(s.bases[o]) +
+         (static_cast<int64_t>(s.rank) * s.seg + zero_local(s.chunk, s.world, s.seg, x));
 }
 
 }  // namespace fyb

@@ -188,6 +188,30 @@ __global__ void embed_bwd_kernel(const int64_t* __restrict__ sorted_tok, const i
   }
 }
 
+// Embedding backward fused with the ZeRO reduce-scatter: the same per-token sums as embed_bwd_kernel, each row of
+// the weight gradient stored at its owners (OwnerScatter: this rank's slot or the owner's staging slot) instead of
+// locally. Only the rows of tokens in the batch are stored: the owners keep the rest of their staging slots zero.
+__global__ void embed_bwd_scatter_kernel(const int64_t* __restrict__ sorted_tok, const int64_t* __restrict__ order,
+                                         const __nv_bfloat16* __restrict__ dy, int64_t M, int N, float scale,
+                                         int64_t V, const OwnerScatter sc) {
+  const int64_t j = blockIdx.x;
+  const int64_t t = sorted_tok[j];
+  if (t < 0 || t >= V) return;
+  if (j > 0 && sorted_tok[j - 1] == t) return;      // not the first position of this token
+  int64_t end = j + 1;
+  while (end < M && sorted_tok[end] == t) ++end;
+  for (int c = threadIdx.x * 8; c < N; c += blockDim.x * 8) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int64_t i = j; i < end; ++i) {
+      float f[8];
+      load8(dy + order[i] * N + c, f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] += bf16_round(f[k] * scale);
+    }
+    store8(owner_dst(sc, sc.x0 + t * N + c), acc);
+  }
+}
+
 // ------------------------------------------------------------------------------------------------------------------
 // cross-entropy over bf16 logits [M, V] (row stride ld), one CTA per row
 
@@ -699,6 +723,52 @@ at::Tensor embedding_bwd(const at::Tensor& tok, const at::Tensor& dy, int64_t V,
   }
   check_launch("embedding_bwd");
   return dw;
+}
+
+// Weight gradient of the embedding stored at its ZeRO owners (embed_bwd_scatter_kernel): slot is the weight's
+// [V, N] slot inside grad_flat; its local copy is zeroed (the rows this rank owns and no token touched stay zero),
+// the touched rows go to their owners. bases: int64 [world] device tensor of every rank's staging buffer.
+void embedding_bwd_scatter(const at::Tensor& tok, const at::Tensor& dy, double scale, at::Tensor& slot,
+                           const at::Tensor& grad_flat, const at::Tensor& bases, int64_t seg, int64_t rank,
+                           int64_t chunk) {
+  FYB_RANGE("fyb::embedding_bwd_scatter");
+  FYB_CHECK(dy.is_cuda() && dy.is_contiguous() && dy.dim() == 2 && dy.size(1) % 8 == 0 && dy.size(0) == tok.size(0),
+            "embedding_bwd_scatter: dy");
+  FYB_CHECK(slot.is_contiguous() && slot.dim() == 2 && slot.size(1) == dy.size(1) &&
+                slot.scalar_type() == at::kBFloat16 && grad_flat.scalar_type() == at::kBFloat16,
+            "embedding_bwd_scatter: slot must be a contiguous bf16 [V, N] slot of grad_flat");
+  FYB_CHECK(bases.is_cuda() && bases.scalar_type() == at::kLong && bases.dim() == 1 && rank >= 0 &&
+                rank < bases.size(0),
+            "embedding_bwd_scatter: bases must be int64 [world]");
+  const auto base = reinterpret_cast<uintptr_t>(grad_flat.data_ptr());
+  const auto sp = reinterpret_cast<uintptr_t>(slot.data_ptr());
+  FYB_CHECK(sp >= base && sp + slot.numel() * 2 <= base + grad_flat.numel() * 2,
+            "embedding_bwd_scatter: slot must lie inside grad_flat");
+  const int64_t x0 = static_cast<int64_t>((sp - base) / 2);
+  FYB_CHECK(seg > 0 && seg % 8 == 0 && chunk % 8 == 0 && x0 % 8 == 0 && (chunk == 0 || seg % chunk == 0) &&
+                x0 + slot.numel() <= bases.size(0) * seg,
+            "embedding_bwd_scatter: seg / chunk / slot offset must be multiples of 8 inside the owners' range");
+  const int64_t M = tok.size(0), N = dy.size(1), V = slot.size(0);
+  FYB_CHECK(M < (1ll << 31), "embedding_bwd_scatter: too many positions");
+  c10::cuda::CUDAGuard guard(dy.device());
+  FYB_CUDA(cudaMemsetAsync(slot.data_ptr(), 0, slot.numel() * 2, cur_stream()));
+  if (M > 0) {
+    OwnerScatter sc;
+    sc.bases = reinterpret_cast<const unsigned long long*>(bases.data_ptr<int64_t>());
+    sc.own = reinterpret_cast<__nv_bfloat16*>(grad_flat.data_ptr());
+    sc.x0 = x0;
+    sc.seg = seg;
+    sc.chunk = chunk;
+    sc.rank = static_cast<int>(rank);
+    sc.world = static_cast<int>(bases.size(0));
+    auto sorted = at::sort(tok, /*stable=*/true, /*dim=*/0, /*descending=*/false);
+    const at::Tensor& stok = std::get<0>(sorted);
+    const at::Tensor& order = std::get<1>(sorted);
+    embed_bwd_scatter_kernel<<<static_cast<unsigned>(M), 128, 0, cur_stream()>>>(
+        stok.data_ptr<int64_t>(), order.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
+        M, (int)N, (float)scale, V, sc);
+  }
+  check_launch("embedding_bwd_scatter");
 }
 
 std::vector<at::Tensor> ce_fwd(const at::Tensor& logits, const at::Tensor& target, int64_t ignore) {

@@ -25,27 +25,9 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
 
+// kEpiScatter / kEpiScatterRes: the owner-scatter epilogue (OwnerScatter, zero_map.cuh) -- the GEMM fused with the
+// ZeRO reduce-scatter: element (row, col) of C has flat index x0 + row * ldc + col in the gradient buffer.
 enum Epi : int { kEpiBf16 = 0, kEpiBf16Res = 1, kEpiF32 = 2, kEpiScatter = 3, kEpiScatterRes = 4 };
-
-// Owner-scatter epilogue (GEMM fused with the ZeRO reduce-scatter): the output C is a weight's slot in the flat
-// gradient buffer, element (row, col) has flat index x = x0 + row * ldc + col, and x belongs to owner o (its segment
-// x / seg, or its chunk's owner in the block-cyclic layout, zero_map.cuh). Instead of storing locally, the epilogue
-// stores the value where the owner sums it: this rank's own slot when o == rank, else owner o's staging buffer, slot
-// `rank`, at the element's local index (bases[o] + rank * seg + local(x)), over NVLink. Every 8-element vector lies
-// inside one segment / chunk (seg, chunk, x0, ldc multiples of 8), so one owner lookup per vector.
-struct OwnerScatter {
-  const unsigned long long* bases;   // [world] staging buffer of every rank (peer pointers)
-  __nv_bfloat16* own;                // this rank's flat gradient buffer
-  int64_t x0, seg, chunk;
-  int rank, world;
-};
-
-__device__ __forceinline__ __nv_bfloat16* owner_dst(const OwnerScatter& s, int64_t x) {
-  const int o = zero_owner(s.chunk, s.world, s.seg, x);
-  if (o == s.rank) return s.own + x;
-  return reinterpret_cast<__nv_bfloat16*>(s.bases[o]) +
-         (static_cast<int64_t>(s.rank) * s.seg + zero_local(s.chunk, s.world, s.seg, x));
-}
 
 __host__ __device__ constexpr bool epi_scatter(int e) { return e == kEpiScatter || e == kEpiScatterRes; }
 __host__ __device__ constexpr bool epi_res(int e) { return e == kEpiBf16Res || e == kEpiScatterRes; }

@@ -359,6 +359,13 @@ class _NativeEmbedding(torch.autograd.Function):
         slot, acc = _grad_slot(ctx.param)
         dy2 = dy.reshape(-1, ctx.vshape[1]).contiguous()
         if slot is not None and not acc:
+            fp = ctx.param._fyb_flat
+            bases = fp.sparse_target(ctx.param) if fp.scatter is not None and ctx.vshape[1] % 8 == 0 else None
+            if bases is not None:
+                # GEMM-fused reduce-scatter on: the rows of this batch's tokens go straight to their owners
+                _C().embedding_bwd_scatter(tokens.reshape(-1), dy2, float(ctx.scale), slot, fp.grad_flat, bases,
+                                           fp.seg, fp.rank, fp.chunk)
+                return None, None, None
             _C().embedding_bwd(tokens, dy2, int(ctx.vshape[0]), float(ctx.scale), slot)
             return None, None, None
         dw = _C().embedding_bwd(tokens, dy2, int(ctx.vshape[0]), float(ctx.scale), None)

@@ -131,7 +131,7 @@ class PeerComm:
         self.scatter_push_ctas = push_ctas or sms
         self.scatter_red_ctas = min(2 * sms, self.part.numel())
         self._sarrive, self._peer_sarrive = self.share_bytes(self.NSLOTS * 4)
-        self._scatter_tables: Dict[frozenset, torch.Tensor] = {}
+        self._scatter_tables: Dict[object, torch.Tensor] = {}
         dist.barrier(group=self.group)      # every rank's staging is zeroed before any peer can store into it
 
     def _scatter_tables_for(self, flat) -> torch.Tensor:
@@ -165,7 +165,26 @@ class PeerComm:
         self.C.reduce_compact(flat.grad_flat, self.staging, flat.used[self.rank], self.world, self.rank, flat.seg,
                               flat.chunk, part, self.scatter_red_ctas)
         self.C.sum_partials(part, self.sq)
+        # rows stored sparsely (the embedding): clear them for the next update; peers store again only after the
+        # barrier that ends this update's parameter exchange, which this rank reaches after the clear
+        zero = self._sparse_table_for(flat)
+        if zero.numel():
+            self.C.zero_staged(self.staging, zero, self.world, self.rank, flat.seg, self.scatter_push_ctas)
         return self.sq
+
+    def _sparse_table_for(self, flat) -> torch.Tensor:
+        """Local ranges [n, 2] (local offset, count) of this owner's pieces of the sparsely scattered weights."""
+        key = ("sparse", flat.sparse())
+        t = self._scatter_tables.get(key)
+        if t is None:
+            if self.dev.type == "cuda" and torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("GEMM-fused reduce-scatter: the set of sparsely scattered weights changed under "
+                                   "capture")
+            rows = [[flat.local_of(o), c] for e in flat.entries if id(e.param) in key[1]
+                    for o, c, r in flat.owner_ranges(e) if r == self.rank]
+            t = torch.tensor(rows, dtype=torch.int64, device=self.dev).view(-1, 2)
+            self._scatter_tables[key] = t
+        return t
 
     # ------------------------------------------------------------------------------------ overlapped (bucketed)
     def setup_buckets(self, flat, groups, reduce_ctas: Optional[int] = None, gather_ctas: Optional[int] = None,

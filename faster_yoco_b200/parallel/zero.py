@@ -143,6 +143,7 @@ class FlatParams:
         self.scatter = None                # device int64 [world]: every rank's staging buffer address
         self.scatter_now = True            # the current micro-batch is the update's last one
         self._scattered = set()
+        self._sparse = set()               # scattered by row (only the rows of tokens in the batch)
 
     # ---------------------------------------------------------------------------------------------------------
     def owner_of(self, x: int) -> int:
@@ -207,6 +208,9 @@ class FlatParams:
 
     def claim_grad(self, p):
         """Slot for p's weight gradient from a native backward: (view, accumulate-into-it)."""
+        if id(p) in self._scattered:
+            raise RuntimeError("a weight whose gradient was already stored at its owners got a second gradient "
+                               "producer (tied weights): the GEMM-fused reduce-scatter cannot accumulate it")
         acc = self.accumulate or id(p) in self._written
         self._written.add(id(p))
         return self.grad_view(p), acc
@@ -219,13 +223,25 @@ class FlatParams:
         self._scattered.add(id(p))
         return self.scatter
 
+    def sparse_target(self, p):
+        """Like scatter_target, for a producer that stores only some rows at the owners (the embedding): the owners
+        keep the rest of these staging regions zero (PeerComm.reduce_scattered)."""
+        bases = self.scatter_target(p)
+        if bases is not None:
+            self._sparse.add(id(p))
+        return bases
+
     def scattered(self) -> frozenset:
         return frozenset(self._scattered)
+
+    def sparse(self) -> frozenset:
+        return frozenset(self._sparse)
 
     def begin_update(self):
         self.accumulate = False
         self._written.clear()
         self._scattered.clear()
+        self._sparse.clear()
 
     def begin_microbatch(self, first: bool, last: bool = True):
         """Gradient accumulation needs no flag: a slot written by an earlier micro-batch of this update is

@@ -76,6 +76,9 @@ class Trainer:
             # the next forward (overlap) or by the fused Adam + push after the update (serial)
             if not self.flat.direct_grads:
                 raise ValueError("transport 'gemm' needs the native kernels (weight gradients written by the GEMM)")
+            if len(list(model.named_parameters(remove_duplicate=False))) != len(list(model.parameters())):
+                raise ValueError("transport 'gemm' stores each weight gradient at its owners once: tied weights "
+                                 "(share_input_output_embed) need transport 'sm' or 'ce'")
             p2p.setup_scatter(self.flat)
             if self.overlap:
                 p2p.setup_buckets(self.flat, model.param_buckets(), transport="sm", grads="scatter")

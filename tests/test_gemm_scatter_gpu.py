@@ -182,3 +182,59 @@ def test_gemm_scatter_training_matches_serial_exchange(tmp_path):
             assert abs(a - b) / abs(b) < 2e-4, (name, r[name]["losses"], r[base]["losses"])
         pf, ps = r[name]["params"], r[base]["params"]
         assert ((pf - ps).abs().max() / ps.abs().max()).item() < 1e-2, name
+
+
+@pytest.mark.parametrize("chunk", [0, 1024])
+def test_embedding_bwd_scatter_and_zero_staged(chunk):
+    """The embedding's weight gradient with the touched rows stored at their owners (four ranks emulated in local
+    memory) against the local embedding backward + the scatter oracle; then the owner clears the staging regions."""
+    ops.set_backend("native")
+    C = ops._C()
+    dev = torch.device("cuda", 0)
+    world, rank, V, N, M, x0 = 4, 3, 1000, 96, 700, 4096
+    numel = V * N
+    seg = int(math.ceil((x0 + numel) / (world * (chunk or 1024)))) * (chunk or 1024)
+    g = torch.Generator(device=dev).manual_seed(11 + chunk)
+    tok = torch.randint(0, V, (M,), generator=g, device=dev)
+    dy = torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16)
+    grad_flat = torch.randn(world * seg, generator=g, device=dev).to(torch.bfloat16)
+    staging = [torch.zeros(world * seg, dtype=torch.bfloat16, device=dev) for _ in range(world)]
+    bases = torch.tensor([t.data_ptr() for t in staging], dtype=torch.int64, device=dev)
+    want = C.embedding_bwd(tok, dy, V, 2.0, None)                  # dense [V, N], zero rows for unseen tokens
+    own_exp = grad_flat.clone()
+    own_exp[x0:x0 + numel] = 0
+    stag_exp = [t.clone() for t in staging]
+    # the oracle stores every row; the kernel only the touched ones, so the expected staging keeps zeros elsewhere
+    ref.owner_scatter(want, x0, seg, rank, own_exp, stag_exp, chunk)
+    slot = grad_flat[x0:x0 + numel].view(V, N)
+    C.embedding_bwd_scatter(tok, dy, 2.0, slot, grad_flat, bases, seg, rank, chunk)
+    torch.cuda.synchronize()
+    assert torch.equal(grad_flat, own_exp)
+    for q in range(world):
+        assert torch.equal(staging[q], stag_exp[q]), q
+    # an owner q clears, over its local ranges of this weight, every other rank's slot
+    q = 1
+    x = torch.arange(x0, x0 + numel, device=dev)
+    o, loc = ref.zero_owner_local(x, seg, chunk, world)
+    lq = loc[o == q]
+    ranges = []
+    lo = prev = None
+    for v in lq.tolist():                                           # contiguous runs of local indices
+        if lo is None:
+            lo = prev = v
+        elif v == prev + 1:
+            prev = v
+        else:
+            ranges.append([lo, prev - lo + 1])
+            lo = prev = v
+    ranges.append([lo, prev - lo + 1])
+    staging[q][q * seg:(q + 1) * seg] = 1.0                         # its own slot must stay untouched
+    C.zero_staged(staging[q], torch.tensor(ranges, dtype=torch.int64, device=dev), world, q, seg, 16)
+    torch.cuda.synchronize()
+    for r in range(world):
+        sl = staging[q][r * seg:(r + 1) * seg]
+        if r == q:
+            assert bool((sl == 1.0).all())
+        else:
+            assert not bool(sl[lq].any())
+    assert int(C.status()[0].item()) == 0
