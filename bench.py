@@ -58,6 +58,9 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--count-launches", type=int, default=1)
+    p.add_argument("--exposed-comm", type=int, default=0,
+                   help="after the measurements, time the same updates without any cross-rank exchange and report "
+                        "exposed_comm_ms = ms_per_step - that (serial schedule only; N > 1)")
     return p.parse_args()
 
 
@@ -265,6 +268,23 @@ def main():
         except Exception:
             launches = None
 
+    exposed = None
+    if args.exposed_comm and world > 1:
+        trainer.measure_without_exchange(True)
+        for i in range(max(args.warmup, 3)):
+            step(i)
+        D.barrier()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for i in range(args.steps):
+            step(i)
+        s1.record()
+        torch.cuda.synchronize()
+        D.barrier()
+        ms_local = D.all_reduce_max(s0.elapsed_time(s1) / args.steps, dev)
+        exposed = {"compute_only_ms_per_step": ms_local, "exposed_comm_ms": ms - ms_local}
+
     if rank == 0:
         out = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -280,6 +300,8 @@ def main():
                        "l2": "working set (>=55 GB of params/grads/Adam state per update) >> 126 MB L2"},
             "clocks": clocks, "e2e": e2e, "gpu_launches": launches,
         }
+        if exposed is not None:
+            out["exposed_comm"] = exposed
         print(json.dumps(out), flush=True)
     trainer.release_graph()
     D.barrier()

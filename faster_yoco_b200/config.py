@@ -164,7 +164,8 @@ class TrainConfig:
     update_freq: int = 1
     max_update: int = 0
     seed: int = 1
-    zero_sharding: str = "os"          # none | os (ZeRO-1) | grad (ZeRO-2 reduce-to-owner)
+    zero_sharding: str = "os"          # none | os: optimizer state sharded (ZeRO-1); gradients go to their owners only
+    #                                    (reduce-to-owner, the reference's "ZeRO-2 style" gradient path)
     comm: str = "fused"                # fused (P2P kernels over NVLink) | nccl (the in-repo baseline)
     kernels: str = "native"            # native (sm_100a kernels) | torch (cuBLAS/SDPA baseline)
     layer_graphs: bool = True

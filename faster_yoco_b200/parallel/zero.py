@@ -284,8 +284,8 @@ def grad_slot(p: torch.Tensor) -> Optional[torch.Tensor]:
 class ZeroOptimizer:
     """Sharded FP32 Adam (apex AdamW expression) over the owner's segment of a :class:`FlatParams`."""
 
-    def __init__(self, flat: FlatParams, optim_cfg, comm: str = "nccl", group=None, stage: int = 1):
-        self.flat, self.cfg, self.comm, self.group, self.stage = flat, optim_cfg, comm, group, stage
+    def __init__(self, flat: FlatParams, optim_cfg, comm: str = "nccl", group=None):
+        self.flat, self.cfg, self.comm, self.group = flat, optim_cfg, comm, group
         seg = flat.param_segment()
         self.master = seg.reshape(-1).float().clone()       # local order (a gather in the block-cyclic layout)
         self.exp_avg = torch.zeros_like(self.master)
@@ -300,13 +300,16 @@ class ZeroOptimizer:
         # as two passes, Adam then push_range, for comparison)
         self.fuse_adam_push = os.environ.get("FYB_FUSE_ADAM_PUSH", "1") != "0"
         self.last_grad_norm = None
+        # measurement only (Trainer.measure_without_exchange): no cross-rank exchange at all, each rank steps its
+        # owned parameters from its own gradients -- the compute-only time of an update, not a training mode
+        self.skip_exchange = False
 
     # ---------------------------------------------------------------------------------------------------------
     def reduce_grads(self):
         """Average the gradient buffer over ranks into each owner's segment (BF16). Returns the owned segment's sum
         of squares when the reduction produced it (fused path), else None."""
         fp = self.flat
-        if fp.world == 1:
+        if fp.world == 1 or self.skip_exchange:
             return None
         if self.comm == "fused" and self.p2p is not None:
             if self.p2p.buckets is not None:
@@ -329,7 +332,7 @@ class ZeroOptimizer:
 
     def all_gather_params(self):
         fp = self.flat
-        if fp.world == 1:
+        if fp.world == 1 or self.skip_exchange:
             return
         if self.comm == "fused" and self.p2p is not None:
             if self.p2p.buckets is not None:
@@ -371,7 +374,7 @@ class ZeroOptimizer:
             sq = ops._C().sq_norm(g16.reshape(-1))
         else:
             sq = g16.float().pow(2).sum().reshape(1)
-        if fp.world > 1:
+        if fp.world > 1 and not self.skip_exchange:
             if self.comm == "fused" and self.p2p is not None:
                 sq = self.p2p.all_reduce_vector(sq)
             else:
@@ -383,7 +386,7 @@ class ZeroOptimizer:
         b1, b2 = self.cfg.betas
         seg = fp.param_segment()
         fused_push = (native and fp.world > 1 and self.comm == "fused" and self.p2p is not None
-                      and self.p2p.buckets is None and self.fuse_adam_push)
+                      and self.p2p.buckets is None and self.fuse_adam_push and not self.skip_exchange)
         # the kernels address this owner's bf16 gradients / parameters through the owner map: its segment views
         # (contiguous layouts) or the whole flat buffers + the chunk size (block-cyclic)
         g_arg, p_arg = (fp.grad_flat, fp.flat) if fp.chunk else (g16, seg)

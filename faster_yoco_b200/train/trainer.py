@@ -43,7 +43,7 @@ class _CommHooks:
 
 
 class Trainer:
-    def __init__(self, model: torch.nn.Module, optim_cfg, *, device, comm: str = "nccl", zero_stage: int = 1,
+    def __init__(self, model: torch.nn.Module, optim_cfg, *, device, comm: str = "nccl",
                  pad_idx: int = 1, graph_step: bool = False, group=None, check_consistency: bool = True,
                  overlap: bool = False, partition: str = "even", criterion=None, transport: str = "sm",
                  chunk: Optional[int] = None):
@@ -66,7 +66,7 @@ class Trainer:
                                dtype=next(model.parameters()).dtype, allocator=p2p.alloc if p2p else None,
                                partition=partition, chunk=chunk)
         self.flat.direct_grads = self.device.type == "cuda" and ops.get_backend() == "native"
-        self.zero = ZeroOptimizer(self.flat, optim_cfg, comm=comm, group=group, stage=zero_stage)
+        self.zero = ZeroOptimizer(self.flat, optim_cfg, comm=comm, group=group)
         self.zero.p2p = p2p
         if transport not in ("sm", "ce", "gemm"):
             raise ValueError(f"unknown transport {transport!r}")
@@ -151,9 +151,27 @@ class Trainer:
         self._mark("backward")
         return loss.detach()
 
+    def measure_without_exchange(self, on: bool = True):
+        """Measurement only: run updates with no cross-rank exchange at all (no gradient reduction, parameter
+        all-gather, statistics or grad-norm all-reduce; weight gradients stay local), so that the step time of the
+        same work minus its communication can be timed and the exposed communication derived. Ranks' parameters
+        diverge: use it after the real measurements. Drops the captured graph (the update is captured again)."""
+        if self.overlap:
+            raise ValueError("measure_without_exchange runs the serial schedule (overlap off)")
+        self.release_graph()
+        self.zero.skip_exchange = on
+        if on:
+            self._scatter_saved = self.flat.scatter
+            self.flat.scatter = None
+            self._consistency_saved = self.check_consistency
+            self.check_consistency = False
+        else:
+            self.flat.scatter = getattr(self, "_scatter_saved", self.flat.scatter)
+            self.check_consistency = getattr(self, "_consistency_saved", self.check_consistency)
+
     def _reduce_stats(self, loss_sum, sample_size):
         stats = torch.stack([loss_sum.float().reshape(()), sample_size.float().reshape(())])
-        if self.world > 1:
+        if self.world > 1 and not self.zero.skip_exchange:
             if self.zero.p2p is not None:
                 stats = self.zero.p2p.all_reduce_vector(stats)
             else:

@@ -154,3 +154,30 @@ def gemm_scatter_vs_serial_gpu(rank, world, outdir, steps):
         tr.zero.p2p.close()
     if rank == 0:
         torch.save(res, os.path.join(outdir, "gemm_scatter.pt"))
+
+
+def exchange_free_steps(rank, world, outdir, steps):
+    """Updates without any cross-rank exchange (the measurement mode behind exposed-communication timing): they run
+    without collectives, so ranks diverge; normal updates work again afterwards."""
+    model, tr = _tiny_trainer(torch.device("cpu"))
+    bs = _batches(rank, world, 2 * steps + 1)
+
+    def one(ids):
+        mine = ids[rank]
+        return tr.train_step({"src_tokens": mine[:, :-1].contiguous(), "target": mine[:, 1:].contiguous(),
+                              "ntokens": mine.shape[0] * mine.shape[1], "nsentences": mine.shape[0]})
+
+    for ids in bs[:steps]:
+        one(ids)
+    same_before = tr.flat.flat.clone()
+    tr.measure_without_exchange(True)
+    for ids in bs[steps:2 * steps]:
+        one(ids)
+    tr.measure_without_exchange(False)
+    mine = tr.flat.flat.clone()
+    allp = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(allp, mine)
+    loss = float(one(bs[-1]))
+    if rank == 0:
+        torch.save({"diverged": not torch.equal(allp[0], allp[1]), "loss": loss,
+                    "changed": not torch.equal(same_before, mine)}, os.path.join(outdir, "noexchange.pt"))

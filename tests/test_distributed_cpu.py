@@ -46,3 +46,9 @@ def test_injected_rank_failure_does_not_hang(tmp_path):
     with pytest.raises(RuntimeError):
         run_ranks(dist_checks.rank_fails_before_collective, 2, str(tmp_path), timeout_s=20)
     assert time.time() - t0 < 150
+
+
+def test_exchange_free_measurement_mode(tmp_path):
+    run_ranks(dist_checks.exchange_free_steps, 2, str(tmp_path), 2)
+    r = torch.load(os.path.join(tmp_path, "noexchange.pt"))
+    assert r["diverged"] and r["changed"] and r["loss"] == r["loss"]
