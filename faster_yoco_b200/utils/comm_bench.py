@@ -5,7 +5,14 @@
 * copy-engine push all-gather (one cudaMemcpyAsync per peer on per-peer streams), and how much a GEMM chain slows
   down while the copy engines push (the question for overlapping the exchange with compute);
 * gradient reduce-scatter: NCCL reduce_scatter_tensor (AVG, bf16) vs the owner-side FP32 rank-order reduction over
-  NVLink (reduce_owner, with the grad-norm partial).
+  NVLink (reduce_owner, with the grad-norm partial);
+* ``--fused-gemm 1``: the GEMM fused with the reduce-scatter -- the q/k/v/g weight gradient dW = dy^T x
+  ([2048 x 12312]^T [2048 x 3072]) stored by the GEMM's epilogue at each element's owner (block-cyclic owner map)
+  and summed by the owner from local memory -- against GEMM + NCCL reduce-scatter and GEMM + P2P reduce-to-owner;
+  roofline = max(FLOPs / measured bf16 peak, bytes this rank sends over NVLink / 770 GB/s);
+* ``--fused-adam 1``: reduce-scatter + sharded Adam + parameter all-gather over per-rank segments of 1 MB .. 1 GB
+  (gradients N(0, 1e-3)): P2P reduce-to-owner + Adam fused with the push all-gather, against NCCL reduce-scatter +
+  Adam + NCCL all-gather; roofline = max(inbound NVLink bytes / 770 GB/s, Adam's HBM bytes / measured HBM bandwidth).
 
 Each point is timed with CUDA events on the launching stream after warm-up, max over ranks; bandwidth is the bytes
 this rank receives ((world-1)/world of the gathered / reduced buffer) per second, and `frac` is that over the
@@ -20,6 +27,8 @@ import torch
 import torch.distributed as dist
 
 LINK_GBS = 770.0
+BF16_TFLOPS = 1661.4      # measured cuBLAS bf16 burst throughput of this pool's B200s
+HBM_GBS = 6529.1          # measured copy bandwidth of this pool's B200s
 
 
 def _time(fn, iters):
@@ -44,6 +53,9 @@ def main():
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--ctas", default="64,148,296")
     ap.add_argument("--interference", type=int, default=1)
+    ap.add_argument("--fused-gemm", type=int, default=0)
+    ap.add_argument("--fused-adam", type=int, default=0)
+    ap.add_argument("--skip-sweep", type=int, default=0, help="only the --fused-* sections")
     a = ap.parse_args()
     from faster_yoco_b200.parallel import dist as D
     from faster_yoco_b200.parallel.p2p import PeerComm
@@ -57,6 +69,15 @@ def main():
     flat.normal_()
     grad.normal_()
     C = comm.C
+    if a.fused_gemm:
+        fused_gemm_bench(comm, a.iters)
+    if a.fused_adam:
+        fused_adam_bench(comm, [int(x) for x in a.sizes_mb.split(",")], a.iters)
+    if a.skip_sweep:
+        comm.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        return
     for mb in (int(x) for x in a.sizes_mb.split(",")):
         seg = mb * 1024 * 1024 // 2
         recv_gb = (world - 1) * seg * 2 / 1e9
@@ -148,6 +169,96 @@ def main():
     comm.close()
     dist.barrier()
     dist.destroy_process_group()
+
+
+def fused_gemm_bench(comm, iters, T=2048, M=12312, N=3072, chunk=1 << 18):
+    """GEMM -> reduce-scatter of the q/k/v/g weight gradient: fused (owner-scatter epilogue + local owner sum) vs
+    GEMM then NCCL reduce-scatter vs GEMM then the P2P reduce-to-owner."""
+    C = comm.C
+    rank, world = comm.rank, comm.world
+    numel = M * N
+    span = chunk * world
+    seg = -(-numel // span) * chunk                         # whole chunks per owner
+    grad = comm.alloc("fg_grad", world * seg, torch.bfloat16)
+    staging = comm.alloc("fg_staging", world * seg, torch.bfloat16)
+    bases = torch.tensor(comm.peers["fg_staging"], dtype=torch.int64, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(rank)
+    dy = torch.randn(T, M, generator=g, device="cuda").to(torch.bfloat16)
+    x = torch.randn(T, N, generator=g, device="cuda").to(torch.bfloat16)
+    slot = grad[:numel].view(M, N)
+    part = torch.zeros(296, device="cuda")
+    sq = torch.zeros(1, device="cuda")
+    out = torch.empty(seg, dtype=torch.bfloat16, device="cuda")
+    res = {"fused_gemm": "qkvg wgrad", "world": world, "T": T, "M": M, "N": N, "chunk": chunk}
+    res["gemm_only_ms"] = _time(lambda: C.gemm(dy, x, slot, True, True, None), iters)
+    res["gemm_scatter_only_ms"] = _time(
+        lambda: (C.gemm_scatter(dy, x, slot, False, grad, bases, seg, rank, chunk), comm.barrier()), iters)
+    res["fused_gemm_reduce_scatter_ms"] = _time(
+        lambda: (C.gemm_scatter(dy, x, slot, False, grad, bases, seg, rank, chunk), comm.barrier(),
+                 C.reduce_compact(grad, staging, seg, world, rank, seg, chunk, part, 296), C.sum_partials(part, sq)),
+        iters)
+    res["gemm_then_nccl_reduce_scatter_ms"] = _time(
+        lambda: (C.gemm(dy, x, slot, True, True, None),
+                 dist.reduce_scatter_tensor(out, grad, op=dist.ReduceOp.AVG)), iters)
+    res["gemm_then_p2p_reduce_owner_ms"] = _time(
+        lambda: (C.gemm(dy, x, slot, True, True, None), comm.barrier(),
+                 C.reduce_owner(comm.peers["fg_grad"], grad, rank * seg, seg, part, sq, 0, rank)), iters)
+    t_compute = 2.0 * T * M * N / (BF16_TFLOPS * 1e12) * 1e3
+    t_link = (world - 1) / world * numel * 2 / (LINK_GBS * 1e9) * 1e3
+    res["roofline_ms"] = max(t_compute, t_link)
+    res["roofline_compute_ms"], res["roofline_link_ms"] = t_compute, t_link
+    for k in [k for k in res if k.endswith("_ms") and not k.startswith("roofline")]:
+        res[k.replace("_ms", "_frac_of_roofline")] = res["roofline_ms"] / res[k]
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+def fused_adam_bench(comm, sizes_mb, iters):
+    """Reduce-scatter + Adam + all-gather over per-rank segments: ours (P2P FP32 rank-order reduce-to-owner with
+    the norm partial, then Adam fused with the push all-gather, one barrier) vs NCCL reduce-scatter + Adam + NCCL
+    all-gather."""
+    C = comm.C
+    rank, world = comm.rank, comm.world
+    seg_max = max(sizes_mb) * 1024 * 1024 // 2
+    grad = comm.alloc("fa_grad", world * seg_max, torch.bfloat16)
+    param = comm.alloc("fa_param", world * seg_max, torch.bfloat16)
+    grad.normal_(0.0, 1e-3)
+    param.normal_(0.0, 0.02)
+    hyper = torch.tensor([1.5e-4, 0.1, 0.05, 1.0], device="cuda")
+    factor = torch.ones(1, device="cuda")
+    part = torch.zeros(296, device="cuda")
+    sq = torch.zeros(1, device="cuda")
+    for mb in sizes_mb:
+        seg = mb * 1024 * 1024 // 2
+        g, p = grad[: world * seg], param[: world * seg]
+        p32 = p[rank * seg:(rank + 1) * seg].float()
+        m = torch.zeros_like(p32)
+        v = torch.zeros_like(p32)
+        out = torch.empty(seg, dtype=torch.bfloat16, device="cuda")
+
+        def ours():
+            comm.barrier()
+            C.reduce_owner(comm.peers["fa_grad"], g, rank * seg, seg, part, sq, 0, rank)
+            C.adam_push(p32, g[rank * seg:(rank + 1) * seg], m, v, p[rank * seg:(rank + 1) * seg], hyper, factor,
+                        0.9, 0.95, 1e-6, 0.05, True, comm.peers["fa_param"], rank * seg, rank, 0)
+            comm.barrier()
+
+        def nccl():
+            dist.reduce_scatter_tensor(out, g, op=dist.ReduceOp.AVG)
+            C.adam_step(p32, out, m, v, p[rank * seg:(rank + 1) * seg], hyper, factor, 0.9, 0.95, 1e-6, 0.05, True)
+            dist.all_gather_into_tensor(p, p[rank * seg:(rank + 1) * seg])
+
+        res = {"fused_adam": True, "size_mb_per_rank": mb, "world": world}
+        res["p2p_reduce_adam_push_ms"] = _time(ours, iters)
+        res["nccl_reduce_scatter_adam_allgather_ms"] = _time(nccl, iters)
+        t_link = 2 * (world - 1) * seg * 2 / (LINK_GBS * 1e9) * 1e3     # reduce in + all-gather in, per rank
+        t_hbm = seg * 28 / (HBM_GBS * 1e9) * 1e3                        # Adam: fp32 p/m/v r+w, bf16 g r, bf16 p w
+        res["roofline_ms"] = max(t_link, t_hbm)
+        res["roofline_link_ms"], res["roofline_hbm_ms"] = t_link, t_hbm
+        for k in ("p2p_reduce_adam_push_ms", "nccl_reduce_scatter_adam_allgather_ms"):
+            res[k.replace("_ms", "_frac_of_roofline")] = res["roofline_ms"] / res[k]
+        if rank == 0:
+            print(json.dumps(res), flush=True)
 
 
 if __name__ == "__main__":
