@@ -82,7 +82,22 @@ def nvml_handle(nv, props, index: int):
     """NVML handle of the CUDA device with properties ``props``. NVML numbers every GPU of the machine and ignores
     CUDA_VISIBLE_DEVICES, so the device is found by its UUID (then its PCI address); the CUDA index is used only
     when neither is available and no device is hidden."""
+    def norm(u):
+        u = (u.decode() if isinstance(u, bytes) else str(u)).lower()
+        return u[4:] if u.startswith("gpu-") else u
+
     uuid = getattr(props, "uuid", None)
+    pci = tuple(getattr(props, k, None) for k in ("pci_domain_id", "pci_bus_id", "pci_device_id"))
+    try:                                    # enumerate: independent of how either side formats the ids
+        for i in range(nv.nvmlDeviceGetCount()):
+            h = nv.nvmlDeviceGetHandleByIndex(i)
+            if uuid is not None and norm(nv.nvmlDeviceGetUUID(h)) == norm(uuid):
+                return h
+            info = nv.nvmlDeviceGetPciInfo(h)
+            if None not in pci and (info.domain, info.bus, info.device) == pci:
+                return h
+    except Exception:
+        pass
     if uuid is not None:
         text = str(uuid)
         try:

@@ -170,6 +170,25 @@ class _FakeNVML:
         return "dev%d" % i
 
 
+class _FakeNVMLEnum(_FakeNVML):
+    """Direct lookups fail; enumeration finds the device by its UUID (bytes, upper case) or PCI address."""
+
+    def __init__(self, by_uuid=True):
+        super().__init__(uuid_ok=False, pci_ok=False)
+        self.by_uuid = by_uuid
+
+    def nvmlDeviceGetCount(self):
+        return 2
+
+    def nvmlDeviceGetUUID(self, h):
+        return b"GPU-1234ABCD-0000-0000-0000-000000000001" if (h == "dev1" and self.by_uuid) else b"GPU-other"
+
+    def nvmlDeviceGetPciInfo(self, h):
+        class Info:
+            domain, bus, device = (0, 0x1B, 0) if h == "dev1" else (0, 0x2C, 0)
+        return Info()
+
+
 class _Props:
     uuid = "1234abcd-0000-0000-0000-000000000001"
     pci_domain_id, pci_bus_id, pci_device_id = 0, 0x1B, 0
@@ -183,6 +202,8 @@ def test_bench_clock_sampler_maps_visible_device(monkeypatch):
     assert bench.nvml_handle(_FakeNVML(uuid_ok=False), _Props(), 0) == "dev1"
     with pytest.raises(RuntimeError):
         bench.nvml_handle(_FakeNVML(uuid_ok=False, pci_ok=False), _Props(), 0)
+    assert bench.nvml_handle(_FakeNVMLEnum(True), _Props(), 0) == "dev1"
+    assert bench.nvml_handle(_FakeNVMLEnum(False), _Props(), 0) == "dev1"
     monkeypatch.delenv("CUDA_VISIBLE_DEVICES")
     assert bench.nvml_handle(_FakeNVML(uuid_ok=False, pci_ok=False), _Props(), 0) == "dev0"
 
