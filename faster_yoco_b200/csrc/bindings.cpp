@@ -97,6 +97,9 @@ int* status_ptr() {
   int* p = nullptr;
   FYB_CUDA(cudaMalloc(&p, 4 * sizeof(int)));
   FYB_CUDA(cudaMemset(p, 0, 4 * sizeof(int)));
+  bind_bounds_gemm(p);
+  bind_bounds_elementwise(p);
+  bind_bounds_comm(p);
   ptrs[dev] = p;
   return p;
 }

@@ -242,6 +242,7 @@ __global__ void push_grads_kernel(const __nv_bfloat16* __restrict__ grad, PeerPt
   for (int pc = 0; pc < npieces; ++pc) {
     const int64_t off = pieces[3 * pc], n = pieces[3 * pc + 1];
     const int q = static_cast<int>(pieces[3 * pc + 2]);
+    if (!FYB_IN_BOUNDS(q, world, 510) || !FYB_IN_BOUNDS(off + n - 1, static_cast<int64_t>(world) * seg, 511)) continue;
     // a piece lies inside one chunk (one owner segment in the contiguous layout): its local positions are contiguous
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(staging.p[q])) +
                          static_cast<int64_t>(rank) * seg + zero_local(chunk, world, seg, off);
@@ -269,6 +270,9 @@ __global__ void reduce_staged_kernel(__nv_bfloat16* __restrict__ grad, const __n
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   for (int rg = 0; rg < nranges; ++rg) {
     const int64_t off = ranges[2 * rg], n = ranges[2 * rg + 1];
+    if (!FYB_IN_BOUNDS(off, static_cast<int64_t>(world) * seg, 512) ||
+        !FYB_IN_BOUNDS(off + n - 1, static_cast<int64_t>(world) * seg, 512))
+      continue;
     const int64_t loc = zero_local(chunk, world, seg, off);        // position inside the owner's segment
     for (int64_t i = tid * 8; i < n; i += nthr * 8) {
       if (i + 8 <= n) {
@@ -387,6 +391,7 @@ __global__ void zero_staged_kernel(__nv_bfloat16* __restrict__ staging, const in
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   for (int rg = 0; rg < nranges; ++rg) {
     const int64_t lo = ranges[2 * rg], n = ranges[2 * rg + 1];
+    if (!FYB_IN_BOUNDS(lo, seg, 513) || !FYB_IN_BOUNDS(lo + n - 1, seg, 513)) continue;
     for (int r = 0; r < world; ++r) {
       if (r == rank) continue;
       __nv_bfloat16* p = staging + static_cast<int64_t>(r) * seg + lo;
@@ -673,5 +678,7 @@ void mailbox_sum(const at::Tensor& box, at::Tensor& out, int64_t world, at::Tens
                                                  reinterpret_cast<uint32_t*>(counter.data_ptr()));
   check_launch("mailbox_sum");
 }
+
+FYB_BOUNDS_BINDER(bind_bounds_comm)
 
 }  // namespace fyb

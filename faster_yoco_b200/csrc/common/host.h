@@ -103,6 +103,12 @@ inline int num_sms() {
 // Device status word shared by all kernels with bounded waits (one int per device, zero = ok).
 int* status_ptr();
 
+// Debug builds (FYB_BOUNDS_CHECK): hand the status word to the bounds checks of each translation unit that has them
+// (no-ops in release builds).
+void bind_bounds_gemm(int* status);
+void bind_bounds_elementwise(int* status);
+void bind_bounds_comm(int* status);
+
 inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
 // Scoped NVTX range around a native op's host call (header-only NVTX 3: visible to an attached profiler such as

@@ -12,6 +12,8 @@
 
 #include <cstdint>
 
+#include "bounds.cuh"
+
 namespace fyb {
 
 struct ZeroMap {
@@ -51,7 +53,9 @@ struct OwnerScatter {
   int rank, world;
 };
 
+// (nullptr when a debug build's bounds check fails: the caller skips the store)
 __device__ __forceinline__ __nv_bfloat16* owner_dst(const OwnerScatter& s, int64_t x) {
+  if (!FYB_IN_BOUNDS(x, static_cast<int64_t>(s.world) * s.seg, 520)) return nullptr;
   const int o = zero_owner(s.chunk, s.world, s.seg, x);
   if (o == s.rank) return s.own + x;
   return reinterpret_cast<__nv_bfloat16*>(s.bases[o]) +

@@ -11,6 +11,7 @@
 
 #include "common/host.h"
 #include "common/ptx.cuh"
+#include "common/bounds.cuh"
 #include "common/zero_map.cuh"
 
 namespace fyb {
@@ -172,7 +173,7 @@ __global__ void embed_bwd_kernel(const int64_t* __restrict__ sorted_tok, const i
                                  int N, float scale, int64_t V) {
   const int64_t j = blockIdx.x;
   const int64_t t = sorted_tok[j];
-  if (t < 0 || t >= V) return;
+  if (!FYB_IN_BOUNDS(t, V, 503) || t < 0 || t >= V) return;
   if (j > 0 && sorted_tok[j - 1] == t) return;      // not the first position of this token
   int64_t end = j + 1;
   while (end < M && sorted_tok[end] == t) ++end;
@@ -196,7 +197,7 @@ __global__ void embed_bwd_scatter_kernel(const int64_t* __restrict__ sorted_tok,
                                          int64_t V, const OwnerScatter sc) {
   const int64_t j = blockIdx.x;
   const int64_t t = sorted_tok[j];
-  if (t < 0 || t >= V) return;
+  if (!FYB_IN_BOUNDS(t, V, 504) || t < 0 || t >= V) return;
   if (j > 0 && sorted_tok[j - 1] == t) return;      // not the first position of this token
   int64_t end = j + 1;
   while (end < M && sorted_tok[end] == t) ++end;
@@ -208,7 +209,7 @@ __global__ void embed_bwd_scatter_kernel(const int64_t* __restrict__ sorted_tok,
 #pragma unroll
       for (int k = 0; k < 8; ++k) acc[k] += bf16_round(f[k] * scale);
     }
-    store8(owner_dst(sc, sc.x0 + t * N + c), acc);
+    if (__nv_bfloat16* d = owner_dst(sc, sc.x0 + t * N + c)) store8(d, acc);
   }
 }
 
@@ -272,7 +273,8 @@ __global__ void __launch_bounds__(kCeThreads) ce_fwd_kernel(const __nv_bfloat16*
     const float lse = M_ + logf(S_);
     const int64_t t = tgt[row];
     lse_out[row] = lse;
-    loss[row] = (t == ignore || t < 0 || t >= V) ? 0.f : lse - __bfloat162float(xr[t]);
+    const bool valid = t != ignore && FYB_IN_BOUNDS(t, V, 502) && t >= 0 && t < V;
+    loss[row] = valid ? lse - __bfloat162float(xr[t]) : 0.f;
   }
 }
 
@@ -902,5 +904,7 @@ at::Tensor sq_norm(const at::Tensor& x) {
   sq_norm_into(x, part.data_ptr<float>(), P, out.data_ptr<float>());
   return out;
 }
+
+FYB_BOUNDS_BINDER(bind_bounds_elementwise)
 
 }  // namespace fyb

@@ -266,15 +266,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (col + 32 <= N) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
-                  *reinterpret_cast<uint4*>(owner_dst(sc, x + 8 * j)) =
-                      make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+                  if (__nv_bfloat16* d = owner_dst(sc, x + 8 * j))
+                    *reinterpret_cast<uint4*>(d) = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
               } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                   if (col + j < N) {
                     const uint16_t h = (j & 1) ? static_cast<uint16_t>(p[j >> 1] >> 16)
                                                : static_cast<uint16_t>(p[j >> 1] & 0xffffu);
-                    *owner_dst(sc, x + j) = __ushort_as_bfloat16(h);
+                    if (__nv_bfloat16* d = owner_dst(sc, x + j)) *d = __ushort_as_bfloat16(h);
                   }
                 }
               }
@@ -340,7 +340,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, v
       }
       __nv_bfloat16* dst = epi_scatter(EPI) ? owner_dst(sc, sc.x0 + row * ldc + col)
                                             : reinterpret_cast<__nv_bfloat16*>(Cv) + row * ldc + col;
-      *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16(acc.x, acc.y), pack_bf16(acc.z, acc.w));
+      if (dst != nullptr) *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16(acc.x, acc.y), pack_bf16(acc.z, acc.w));
     }
     return;
   }
@@ -354,7 +354,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, v
       const float v = epi_res(EPI) ? bf16_round(acc) + __bfloat162float(R[row * ldr + col]) : acc;
       __nv_bfloat16* dst = epi_scatter(EPI) ? owner_dst(sc, sc.x0 + row * ldc + col)
                                             : reinterpret_cast<__nv_bfloat16*>(Cv) + row * ldc + col;
-      *dst = __float2bfloat16_rn(v);
+      if (dst != nullptr) *dst = __float2bfloat16_rn(v);
     }
   }
 }
@@ -551,5 +551,7 @@ void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
     else launch<128, 6, true, true, kEpiScatter>(ta, tb, Cp, Rp, m, n, k, ld, ld, plan.splits, wsp, st, sc);
   }
 }
+
+FYB_BOUNDS_BINDER(bind_bounds_gemm)
 
 }  // namespace fyb
