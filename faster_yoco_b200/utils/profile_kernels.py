@@ -1,6 +1,10 @@
 """Small, self-terminating launches of the hot kernels for `ncu` captures (a few MB on the device, a handful of
 launches each). Used as:  ncu --set full --clock-control none -k regex:<kernel> -s <n> -c <m> \\
-    python -m faster_yoco_b200.utils.profile_kernels --what attn|ret|gemm|attn_bwd|ret_bwd|norm|ce|adam
+    python -m faster_yoco_b200.utils.profile_kernels --what <case>
+
+cases: attn, attn_bwd, swa, swa_bwd (sliding window 1024), ret, ret_bwd, gemm, gemm_dgrad, gemm_scatter (weight
+gradient stored at 4 emulated owners, block-cyclic map), adam, ce, ce_bwd, rms, rms_bwd, subln, subln_bwd, swiglu,
+swiglu_bwd, rope, embed, embed_bwd, reduce_compact.
 """
 import argparse
 
@@ -18,7 +22,18 @@ def main():
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
     L = a.L
-    if a.what in ("attn", "attn_bwd"):
+    if a.what in ("swa", "swa_bwd"):
+        q = torch.randn(1, L, 24, 128, device=dev, dtype=torch.bfloat16)
+        k = torch.randn(1, L, 24, 128, device=dev, dtype=torch.bfloat16)
+        v = torch.randn(1, L, 24, 128, device=dev, dtype=torch.bfloat16)
+        o, lse = C.attention_fwd(q, k, v, True, 1024, 128 ** -0.5)
+        do = torch.randn_like(o)
+        for _ in range(a.reps):
+            if a.what == "swa":
+                C.attention_fwd(q, k, v, True, 1024, 128 ** -0.5)
+            else:
+                C.attention_bwd(do, q, k, v, o, lse, True, 1024, 128 ** -0.5)
+    elif a.what in ("attn", "attn_bwd"):
         q = torch.randn(1, L, 24, 128, device=dev, dtype=torch.bfloat16)
         k = torch.randn(1, L, 8, 128, device=dev, dtype=torch.bfloat16)
         v = torch.randn(1, L, 8, 128, device=dev, dtype=torch.bfloat16)
@@ -85,6 +100,58 @@ def main():
                 C.rms_norm_fwd(x, w, 1e-5)
             else:
                 C.rms_norm_bwd(y, x, w, rstd)
+    elif a.what in ("subln", "subln_bwd"):
+        o = torch.randn(L, 3072, device=dev, dtype=torch.bfloat16)
+        g = torch.randn(L, 3072, device=dev, dtype=torch.bfloat16)
+        out, rstd = C.subln_swiglu_fwd(o, g, 1e-6, 128)
+        dout = torch.randn_like(out)
+        for _ in range(a.reps):
+            if a.what == "subln":
+                C.subln_swiglu_fwd(o, g, 1e-6, 128)
+            else:
+                C.subln_swiglu_bwd(dout, o, g, rstd, 128)
+    elif a.what in ("swiglu", "swiglu_bwd"):
+        u = torch.randn(L, 16384, device=dev, dtype=torch.bfloat16)
+        x, y = u[:, :8192], u[:, 8192:]
+        da = torch.randn(L, 8192, device=dev, dtype=torch.bfloat16)
+        for _ in range(a.reps):
+            if a.what == "swiglu":
+                C.swiglu_fwd(x, y)
+            else:
+                C.swiglu_bwd(x, y, da)
+    elif a.what == "rope":
+        from faster_yoco_b200.ops import reference as ref
+        x = torch.randn(1, L, 24, 128, device=dev, dtype=torch.bfloat16)
+        cos, sin = ref.rope_tables(128, 0, L, 1e4, torch.bfloat16, dev)
+        for _ in range(a.reps):
+            C.rope_fwd(x, cos, sin, False)
+    elif a.what in ("embed", "embed_bwd"):
+        w = torch.randn(100288, 3072, device=dev, dtype=torch.bfloat16)
+        tok = torch.randint(0, 100288, (L,), device=dev)
+        dy = torch.randn(L, 3072, device=dev, dtype=torch.bfloat16)
+        dw = torch.empty_like(w)
+        for _ in range(a.reps):
+            if a.what == "embed":
+                C.embedding_fwd(tok, w, 3072 ** 0.5)
+            else:
+                C.embedding_bwd(tok, dy, 100288, 3072 ** 0.5, dw)
+    elif a.what in ("gemm_scatter", "reduce_compact"):
+        # four owners emulated in this GPU's memory (the kernels only see addresses); block-cyclic map
+        world, rank, chunk = 4, 1, 1 << 18
+        M, N, T = 12312, 3072, 2048
+        seg = -(-(M * N) // (world * chunk)) * chunk
+        grad = torch.zeros(world * seg, device=dev, dtype=torch.bfloat16)
+        staging = [torch.zeros(world * seg, device=dev, dtype=torch.bfloat16) for _ in range(world)]
+        bases = torch.tensor([t.data_ptr() for t in staging], dtype=torch.int64, device=dev)
+        dy = torch.randn(T, M, device=dev, dtype=torch.bfloat16)
+        x = torch.randn(T, N, device=dev, dtype=torch.bfloat16)
+        slot = grad[:M * N].view(M, N)
+        part = torch.zeros(296, device=dev)
+        for _ in range(a.reps):
+            if a.what == "gemm_scatter":
+                C.gemm_scatter(dy, x, slot, False, grad, bases, seg, rank, chunk)
+            else:
+                C.reduce_compact(grad, staging[rank], seg, world, rank, seg, chunk, part, 296)
     else:
         raise SystemExit(f"unknown --what {a.what}")
     torch.cuda.synchronize()
