@@ -22,7 +22,7 @@ import torch.distributed as dist
 
 from ..config import OptimConfig
 from ..parallel import dist as D
-from ..train.checkpoint import load_checkpoint, save_checkpoint
+from ..train.checkpoint import load_checkpoint, part_path, save_checkpoint
 from ..train.metrics import format_log
 from ..train.trainer import Trainer
 from .common import build_model, build_task, setup_runtime
@@ -59,14 +59,15 @@ def _gather_iterator_states(itr):
 
 
 def _save_model_only(args, model, nu: int, rank: int):
-    """bf16 model-only save on rank 0 (reference parameter names, ``decoder.model.`` prefix) and peak memory."""
+    """bf16 model-only save on data-parallel rank 0 (reference parameter names, ``decoder.model.`` prefix; one part
+    file per tensor-parallel rank) and peak memory. ``rank``: this rank's data-parallel rank."""
     import json
     mem = {"rank": rank, "num_updates": nu, "time": time.time()}
     if torch.cuda.is_available():
         mem.update(max_allocated_gib=torch.cuda.max_memory_allocated() / 2 ** 30,
                    max_reserved_gib=torch.cuda.max_memory_reserved() / 2 ** 30)
     print("VALIDATION_MEM " + json.dumps(mem), flush=True)
-    path = os.path.join(args.save_dir, f"model_{nu:06d}.pt")
+    path = part_path(os.path.join(args.save_dir, f"model_{nu:06d}.pt"))
     if rank == 0 and nu > 0 and not os.path.exists(path):
         t0 = time.time()
         os.makedirs(args.save_dir, exist_ok=True)
@@ -76,9 +77,12 @@ def _save_model_only(args, model, nu: int, rank: int):
         print(f"VALIDATION_CKPT {path} {time.time() - t0:.1f}s", flush=True)
 
 
-def validate_lm(model, task, args, device, rank: int, world: int) -> Optional[dict]:
+def validate_lm(model, task, args, device, rank: int, world: int, rep: int = 1, cp: int = 1,
+                tp: int = 1) -> Optional[dict]:
     """Mean next-token loss (bits) over up to --max-valid-steps batches of the valid subset, summed over ranks
-    (fairseq's validation pass of the training loop; no gradients, the module path of the model)."""
+    (fairseq's validation pass of the training loop; no gradients, the module path of the model). The `rep`
+    consecutive ranks of one model replica (a context- or tensor-parallel group) read the same batches; under context
+    parallelism each takes its block of every sequence."""
     import math
     from .. import ops
     try:
@@ -87,8 +91,8 @@ def validate_lm(model, task, args, device, rank: int, world: int) -> Optional[di
         return None
     if not getattr(ds, "data", None):
         return None                       # an empty source list (the reference corpus layout has one)
-    itr = task.get_batch_iterator(ds, max_sentences=args.batch_size, seed=args.seed, num_shards=world,
-                                  shard_id=rank, prefetch=0)
+    itr = task.get_batch_iterator(ds, max_sentences=args.batch_size, seed=args.seed, num_shards=world // rep,
+                                  shard_id=rank // rep, prefetch=0)
     was_training = model.training
     model.eval()
     tot = torch.zeros(2, dtype=torch.float64, device=device)
@@ -98,6 +102,7 @@ def validate_lm(model, task, args, device, rank: int, world: int) -> Optional[di
                 b = next(itr)
             except StopIteration:
                 break
+            b = _cp_slice(b, cp)
             src, tgt = b["src_tokens"].to(device), b["target"].to(device)
             logits, _ = model(src)
             loss = ops.cross_entropy(logits.reshape(-1, logits.shape[-1]), tgt.reshape(-1), task.tokenizer.pad_id)
@@ -107,6 +112,7 @@ def validate_lm(model, task, args, device, rank: int, world: int) -> Optional[di
         itr.close()
     if D.is_dist():
         dist.all_reduce(tot)
+        tot /= tp                       # the ranks of a tensor-parallel group computed the same loss
     model.train(was_training)
     bits = float(tot[0] / tot[1].clamp_min(1)) / math.log(2)
     return {"loss": round(bits, 3), "ppl": round(2 ** bits, 2), "ntokens": int(tot[1])}
@@ -125,25 +131,35 @@ def main(argv=None) -> int:
                         clip_norm=args.clip_norm, warmup_updates=args.warmup_updates,
                         total_num_update=args.total_num_update, end_learning_rate=args.end_learning_rate,
                         power=args.power)
-    comm = args.comm if (world > 1 and device.type == "cuda" and args.context_parallel_size == 1) else "nccl"
+    tp = args.model_parallel_size
+    cp = args.context_parallel_size
+    if tp > 1 and cp > 1:
+        raise SystemExit("tensor and context parallelism cannot be combined")
+    rep = cp if cp > 1 else tp                # consecutive ranks that hold one model replica
+    dp = world // rep
+    comm = args.comm if (dp > 1 and device.type == "cuda" and rep == 1) else "nccl"
     overlap = (world == 2 and comm == "fused" and args.transport != "gemm") if str(args.overlap) == "auto" \
         else bool(_flag(args.overlap))
+    if tp > 1:
+        overlap = False
     transport = ("ce" if world == 2 else "sm") if args.transport == "auto" else args.transport
-    graph = bool(args.cuda_graph) and device.type == "cuda" and args.context_parallel_size == 1
+    if tp > 1:
+        transport = "sm"
+    graph = bool(args.cuda_graph) and device.type == "cuda" and rep == 1
     trainer = Trainer(model, optim, device=device, comm=comm, graph_step=graph,
                       overlap=overlap, transport=transport, partition=args.partition, pad_idx=task.tokenizer.pad_id,
                       chunk=args.zero_chunk)
-    cp = args.context_parallel_size
     if cp > 1:
         if family != "yoco":
             raise SystemExit("context parallelism is implemented for YOCO")
         if args.tokens_per_sample % cp:
             raise SystemExit("--tokens-per-sample must be divisible by --context-parallel-size")
-    # data shards are per data-parallel replica; the ranks of one context-parallel group read the same batches
-    itr = task.get_batch_iterator(ds, max_sentences=args.batch_size, seed=args.seed, num_shards=world // cp,
-                                  shard_id=rank // cp)
+    # data shards are per data-parallel replica; the ranks of one context- / tensor-parallel group read the same
+    # batches
+    itr = task.get_batch_iterator(ds, max_sentences=args.batch_size, seed=args.seed, num_shards=dp,
+                                  shard_id=rank // rep)
     restore = os.path.join(args.save_dir, args.restore_file)
-    if os.path.exists(restore) and not args.reset_optimizer:
+    if os.path.exists(part_path(restore)) and not args.reset_optimizer:
         ck = load_checkpoint(restore, model, trainer)
         its = (ck.get("extra_state") or {}).get("train_iterator")
         if its and not args.reset_dataloader and hasattr(itr, "load_state_dict") and len(its) == world:
@@ -168,28 +184,28 @@ def main(argv=None) -> int:
                 print(format_log(stats), flush=True)
         if (not args.disable_validation and args.validate_interval_updates > 0
                 and nu % args.validate_interval_updates == 0):
-            v = validate_lm(model, task, args, device, rank, world)
+            v = validate_lm(model, task, args, device, rank, world, rep, cp, tp)
             if v is not None and rank == 0:
                 print(f"valid on '{args.valid_subset}' subset | loss {v['loss']} | ppl {v['ppl']} | "
                       f"num_updates {nu}", flush=True)
         if args.save_model_only and args.save_interval_updates > 0 and nu % args.save_interval_updates == 0:
-            _save_model_only(args, model, nu, rank)
+            _save_model_only(args, model, nu, trainer.rank)
         elif not args.no_save and args.save_interval_updates > 0 and nu % args.save_interval_updates == 0:
             states = _gather_iterator_states(itr)
             save_checkpoint(os.path.join(args.save_dir, f"checkpoint_1_{nu}.pt"), model, trainer,
                             extra_state={"train_iterator": states})
-            if rank == 0:
+            if trainer.rank == 0:            # data-parallel rank 0 of every tensor-parallel slice
                 import shutil
-                shutil.copyfile(os.path.join(args.save_dir, f"checkpoint_1_{nu}.pt"),
-                                os.path.join(args.save_dir, "checkpoint_last.pt"))
+                shutil.copyfile(part_path(os.path.join(args.save_dir, f"checkpoint_1_{nu}.pt")),
+                                part_path(os.path.join(args.save_dir, "checkpoint_last.pt")))
     trainer.pending.check(block=True)
     if not args.disable_validation and args.validate_interval_updates <= 0:
-        v = validate_lm(model, task, args, device, rank, world)
+        v = validate_lm(model, task, args, device, rank, world, rep, cp, tp)
         if v is not None and rank == 0:
             print(f"valid on '{args.valid_subset}' subset | loss {v['loss']} | ppl {v['ppl']} | "
                   f"num_updates {trainer.num_updates()}", flush=True)
     if args.save_model_only:
-        _save_model_only(args, model, trainer.num_updates(), rank)
+        _save_model_only(args, model, trainer.num_updates(), trainer.rank)
     elif not args.no_save:
         states = _gather_iterator_states(itr)
         save_checkpoint(os.path.join(args.save_dir, "checkpoint_last.pt"), model, trainer,

@@ -83,7 +83,7 @@ class MergedLinear(nn.Module):
         self.names = list(names)
         rows = sum(self.parts)
         self.rows = _round8(rows) if pad_to8 else rows
-        self.weight = nn.Parameter(torch.empty(self.rows, in_features))
+        self.weight = TP.mark_sharded(nn.Parameter(torch.empty(self.rows, in_features)))
         self._inits = list(inits)
         self.reset_parameters()
 
@@ -125,6 +125,8 @@ class Linear(nn.Module):
         elif self.parallel == "row":
             shape[1] //= _tp()
         self.weight = nn.Parameter(torch.empty(*shape))
+        if self.parallel is not None:
+            TP.mark_sharded(self.weight)
         self._init = init
         self.reset_parameters()
 

@@ -233,6 +233,21 @@ _MERGED = {
 }
 
 
+def _rng_snapshot():
+    """CPU generator + the current CUDA device's generator (only when CUDA is already initialised: no new context)."""
+    cuda = None
+    if torch.cuda.is_available() and torch.cuda.is_initialized():
+        cuda = (torch.cuda.current_device(), torch.cuda.get_rng_state())
+    return torch.get_rng_state(), cuda
+
+
+def _rng_restore(snap):
+    cpu, cuda = snap
+    torch.set_rng_state(cpu)
+    if cuda is not None:
+        torch.cuda.set_rng_state(cuda[1], cuda[0])
+
+
 class YOCO(nn.Module):
     def __init__(self, args: YOCOArgs):
         super().__init__()
@@ -241,6 +256,10 @@ class YOCO(nn.Module):
             raise ValueError(f"model_parallel_size {args.model_parallel_size} but the tensor-parallel group has "
                              f"{TP.tp_size()} ranks (call parallel.tp.init_model_parallel first)")
         self.embed_scale = math.sqrt(args.dim)
+        # the weights come from reset_parameters below, started from this RNG state: what the submodule
+        # constructors draw (which differs between the tensor-parallel and single-rank layer classes) does not
+        # shift them, so a seed gives the same logical weights at every TP degree
+        rng = _rng_snapshot()
         if TP.tp_size() > 1:
             self.embed_tokens = TP.VocabParallelEmbedding(args.vocab_size, args.dim)
             self.output_projection = TP.ColumnParallelLinear(args.dim, args.vocab_size, gather_output=True)
@@ -252,6 +271,7 @@ class YOCO(nn.Module):
         self.self_decoder = SelfDecoder(args)
         self.cross_decoder = CrossDecoder(args)
         self.layer_norm = RMSNorm(args.dim, eps=args.norm_eps)
+        _rng_restore(rng)
         self.reset_parameters()
         self._register_state_dict_hook(YOCO._export_hook)
         self._register_load_state_dict_pre_hook(YOCO._import_hook, with_module=True)

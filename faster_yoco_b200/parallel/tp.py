@@ -170,6 +170,18 @@ scatter_to_model_parallel_region = scatter_to_tp
 # layers
 
 
+def mark_sharded(p: torch.nn.Parameter) -> torch.nn.Parameter:
+    """Tag a parameter that holds only this rank's slice of the logical weight (the ZeRO trainer counts replicated
+    parameters once, sharded ones once per TP rank, in the global gradient norm)."""
+    if _TP_SIZE > 1:
+        p._fyb_tp_sharded = True
+    return p
+
+
+def is_sharded(p: torch.Tensor) -> bool:
+    return bool(getattr(p, "_fyb_tp_sharded", False))
+
+
 def _master_slice(shape, init: Optional[Callable], dim: int, dtype=None, device=None) -> torch.Tensor:
     full = torch.empty(shape, dtype=dtype or torch.float32, device=device)
     if init is not None:
@@ -188,7 +200,7 @@ class ColumnParallelLinear(nn.Module):
             raise ValueError("bias is not supported (no layer of the model family uses one)")
         self.in_features, self.out_features, self.gather_output = in_features, out_features, gather_output
         self.init_method = init_method
-        self.weight = nn.Parameter(_master_slice((out_features, in_features), init_method, 0))
+        self.weight = mark_sharded(nn.Parameter(_master_slice((out_features, in_features), init_method, 0)))
 
     @torch.no_grad()
     def reset_parameters(self, init_override=None):
@@ -211,7 +223,7 @@ class RowParallelLinear(nn.Module):
             raise ValueError("bias is not supported (no layer of the model family uses one)")
         self.in_features, self.out_features, self.input_is_parallel = in_features, out_features, input_is_parallel
         self.init_method = init_method
-        self.weight = nn.Parameter(_master_slice((out_features, in_features), init_method, 1))
+        self.weight = mark_sharded(nn.Parameter(_master_slice((out_features, in_features), init_method, 1)))
 
     @torch.no_grad()
     def reset_parameters(self, init_override=None):
@@ -236,7 +248,7 @@ class VocabParallelEmbedding(nn.Module):
         self.per = num_embeddings // _TP_SIZE
         self.start = _TP_RANK * self.per
         self.init_method = init_method
-        self.weight = nn.Parameter(_master_slice((num_embeddings, embedding_dim), init_method, 0))
+        self.weight = mark_sharded(nn.Parameter(_master_slice((num_embeddings, embedding_dim), init_method, 0)))
 
     @torch.no_grad()
     def reset_parameters(self, init_override=None):

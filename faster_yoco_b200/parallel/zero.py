@@ -303,7 +303,17 @@ class ZeroOptimizer:
         # measurement only (Trainer.measure_without_exchange): no cross-rank exchange at all, each rank steps its
         # owned parameters from its own gradients -- the compute-only time of an update, not a training mode
         self.skip_exchange = False
+        self.tp_group = None
 
+    def set_tensor_parallel(self, tp_group, tp_rank: int, is_sharded):
+        """Tensor x data parallelism: this optimizer shards over the data-parallel group; the global gradient norm
+        adds every TP rank's sharded parameters and counts the replicated ones (identical on all TP ranks: norm
+        weights) once, so clipping matches TP = 1."""
+        fp = self.flat
+        self.tp_group, self.tp_rank = tp_group, tp_rank
+        rep = [(o, c) for e in fp.entries if not is_sharded(e.param)
+               for o, c, r in fp.owner_ranges(e) if r == fp.rank]
+        self._rep_pieces = rep
     # ---------------------------------------------------------------------------------------------------------
     def reduce_grads(self):
         """Average the gradient buffer over ranks into each owner's segment (BF16). Returns the owned segment's sum
@@ -374,11 +384,17 @@ class ZeroOptimizer:
             sq = ops._C().sq_norm(g16.reshape(-1))
         else:
             sq = g16.float().pow(2).sum().reshape(1)
+        if self.tp_group is not None and self.tp_rank != 0 and self._rep_pieces:
+            # replicated parameters enter the norm once: from TP rank 0 (the reduced gradients are identical there)
+            rep = torch.stack([fp.grad_flat[o:o + c].float().pow(2).sum() for o, c in self._rep_pieces]).sum()
+            sq = sq - rep.reshape(1)
         if fp.world > 1 and not self.skip_exchange:
             if self.comm == "fused" and self.p2p is not None:
                 sq = self.p2p.all_reduce_vector(sq)
             else:
                 dist.all_reduce(sq, group=self.group)
+        if self.tp_group is not None:
+            dist.all_reduce(sq, group=self.tp_group)
         grad_norm = (factor * sq.sqrt()).reshape(())
         clip = self.cfg.clip_norm
         if clip > 0:

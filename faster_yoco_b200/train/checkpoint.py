@@ -68,10 +68,21 @@ def _join_for_import(model, name: str, entries: Dict[str, torch.Tensor]) -> Opti
     return entries.get(name)
 
 
+def part_path(path: str) -> str:
+    """Tensor parallelism: each TP rank's slice goes to its own file, fairseq's `<name>-model_part-<tp_rank>.pt`."""
+    from ..parallel import tp as TP
+    if TP.tp_size() <= 1:
+        return path
+    base, ext = os.path.splitext(path)
+    return f"{base}-model_part-{TP.tp_rank()}{ext or '.pt'}"
+
+
 def save_checkpoint(path: str, model, trainer, *, extra_state: Optional[dict] = None, cfg: Optional[dict] = None,
                     rank: Optional[int] = None):
-    """Collective (every rank must call): gathers the optimizer state, rank 0 writes `path`."""
+    """Collective (every rank must call): gathers the optimizer state, rank 0 of the data-parallel group writes
+    `path` (with tensor parallelism: one part file per TP rank, see part_path)."""
     rank = trainer.rank if rank is None else rank
+    path = part_path(path)
     opt = trainer.zero.consolidated_state()            # {internal name: {master, exp_avg, exp_avg_sq}}
     if rank != 0:
         return None
@@ -116,7 +127,7 @@ def load_model_weights(model, path_or_ckpt, strict: bool = True):
 
 def load_checkpoint(path: str, model, trainer) -> dict:
     """Restore model weights, this rank's optimizer shard, the update count and the LR schedule."""
-    ck = load_model_weights(model, path)
+    ck = load_model_weights(model, part_path(path))
     _, strip = _core(model)
     st = ck.get("last_optimizer_state") or {}
     zero = trainer.zero

@@ -48,15 +48,23 @@ class Trainer:
                  overlap: bool = False, partition: str = "even", criterion=None, transport: str = "sm",
                  chunk: Optional[int] = None):
         from ..parallel import tp as TP
-        if TP.tp_size() > 1:
-            raise NotImplementedError(
-                "the ZeRO trainer runs pure data parallelism (tensor-parallel YOCO / LLaMA models serve evaluation "
-                "and custom loops; every reference recipe trains with model_parallel_size 1)")
+        self.tp = TP.tp_size()
+        if self.tp > 1:
+            # tensor x data parallelism: ZeRO shards over the data-parallel group (ranks holding the same TP slice);
+            # the model's TP layers carry their own collectives; the module path runs without a captured graph
+            if group is None:
+                group = TP.dp_group()
+            if comm == "fused" or transport == "gemm" or overlap:
+                raise ValueError("tensor-parallel training runs the NCCL data-parallel exchange (--comm nccl)")
+            graph_step = False
         self.model = model
         self.device = torch.device(device)
         self.cfg = optim_cfg
         self.pad_idx = pad_idx
-        self.rank, self.world = D.rank(), D.world()
+        if group is not None:
+            self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        else:
+            self.rank, self.world = D.rank(), D.world()
         self.group = group
         p2p = None
         if comm == "fused" and self.world > 1 and self.device.type == "cuda":
@@ -67,6 +75,8 @@ class Trainer:
                                partition=partition, chunk=chunk)
         self.flat.direct_grads = self.device.type == "cuda" and ops.get_backend() == "native"
         self.zero = ZeroOptimizer(self.flat, optim_cfg, comm=comm, group=group)
+        if self.tp > 1:
+            self.zero.set_tensor_parallel(TP.tp_group(), TP.tp_rank(), TP.is_sharded)
         self.zero.p2p = p2p
         if transport not in ("sm", "ce", "gemm"):
             raise ValueError(f"unknown transport {transport!r}")

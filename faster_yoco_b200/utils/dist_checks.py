@@ -42,7 +42,7 @@ def zero_matches_single(rank, world, outdir, steps, partition="even", chunk=None
         torch.save({"sd": sd, "num_updates": tr.num_updates()}, os.path.join(outdir, f"ws{world}_{partition}.pt"))
 
 
-def single_reference(outdir, world, steps):
+def single_reference(outdir, world, steps, with_norm=False):
     """Single process, batch = all shards concatenated (the same global batch)."""
     model, tr = _tiny_trainer(torch.device("cpu"))
     for ids in _batches(0, world, steps):
@@ -50,7 +50,8 @@ def single_reference(outdir, world, steps):
         b = {"src_tokens": allb[:, :-1].contiguous(), "target": allb[:, 1:].contiguous(),
              "ntokens": allb.shape[0] * allb.shape[1], "nsentences": allb.shape[0]}
         tr.train_step(b)
-    return {k: v.detach().clone() for k, v in model.state_dict().items()}
+    sd = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    return (sd, float(tr.zero.last_grad_norm)) if with_norm else sd
 
 
 def checkpoint_resume(rank, world, outdir, steps, split, partition="even", chunk=None, resume_partition=None):
@@ -181,3 +182,31 @@ def exchange_free_steps(rank, world, outdir, steps):
     if rank == 0:
         torch.save({"diverged": not torch.equal(allp[0], allp[1]), "loss": loss,
                     "changed": not torch.equal(same_before, mine)}, os.path.join(outdir, "noexchange.pt"))
+
+
+def tp_dp_matches_single(rank, world, outdir, steps, full_sd):
+    """Tensor x data parallel training (TP 2 x DP world/2) of the tiny YOCO started from the slices of `full_sd`;
+    data-parallel rank 0 of every TP slice saves its final weights (reference names, this slice's shapes)."""
+    from ..config import OptimConfig, build_args
+    from ..models.yoco import YOCO, shard_state_dict
+    from ..parallel import tp as TP
+    from ..train.trainer import Trainer
+    tps = 2
+    TP.init_model_parallel(tps)
+    dp, dpr = world // tps, rank // tps
+    torch.manual_seed(0)
+    args = build_args("yoco_tiny", max_seq_len=256, init_std=0.02, model_parallel_size=tps)
+    model = YOCO(args).to(torch.float32)
+    model.load_state_dict(shard_state_dict(full_sd, tps, TP.tp_rank()), strict=True)
+    cfg = OptimConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, warmup_updates=0, total_num_update=20)
+    tr = Trainer(model, cfg, device=torch.device("cpu"), comm="nccl")
+    assert tr.world == dp and tr.rank == dpr
+    for ids in _batches(dpr, dp, steps):
+        mine = ids[dpr]
+        tr.train_step({"src_tokens": mine[:, :-1].contiguous(), "target": mine[:, 1:].contiguous(),
+                       "ntokens": mine.shape[0] * mine.shape[1], "nsentences": mine.shape[0]})
+    gn = float(tr.zero.last_grad_norm)
+    if dpr == 0:
+        torch.save({"sd": {k: v.detach().clone() for k, v in model.state_dict().items()}, "gnorm": gn},
+                   os.path.join(outdir, f"tp{TP.tp_rank()}.pt"))
+    TP.destroy_model_parallel()

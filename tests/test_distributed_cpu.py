@@ -52,3 +52,22 @@ def test_exchange_free_measurement_mode(tmp_path):
     run_ranks(dist_checks.exchange_free_steps, 2, str(tmp_path), 2)
     r = torch.load(os.path.join(tmp_path, "noexchange.pt"))
     assert r["diverged"] and r["changed"] and r["loss"] == r["loss"]
+
+
+def test_tensor_x_data_parallel_training_matches_single_process(tmp_path):
+    """TP 2 x DP 2 on 4 gloo ranks: every slice ends where the matching slice of single-process training (same
+    global batch, same initial weights) ends, and the clipped norm is the global one."""
+    from faster_yoco_b200.models.yoco import shard_state_dict
+    steps = 3
+    model, tr = dist_checks._tiny_trainer(torch.device("cpu"))
+    full0 = {k: v.detach().clone() for k, v in model.state_dict().items()}
+    run_ranks(dist_checks.tp_dp_matches_single, 4, str(tmp_path), steps, full0, timeout_s=240)
+    ref, ref_norm = dist_checks.single_reference(str(tmp_path), 2, steps, with_norm=True)
+    for r in range(2):
+        saved = torch.load(os.path.join(tmp_path, f"tp{r}.pt"))
+        assert abs(saved["gnorm"] - ref_norm) <= 1e-5 * ref_norm, (saved["gnorm"], ref_norm)
+        got = saved["sd"]
+        want = shard_state_dict(ref, 2, r)
+        assert set(got) == set(want)
+        for k, v in want.items():
+            assert torch.allclose(got[k].float(), v.float(), atol=2e-5, rtol=1e-4), k

@@ -61,3 +61,63 @@ def test_tp2_retention_yoco_matches_tp1():
 
 def test_tp2_sliding_window_yoco_matches_tp1():
     _run(16)
+
+
+def _cli_tp_worker(rank, world, data, save, out, max_update):
+    import contextlib
+    import io
+    from faster_yoco_b200.cli import train as T
+    from faster_yoco_b200.parallel import tp
+    buf = io.StringIO()
+    with contextlib.redirect_stdout(buf):
+        rc = T.main([data, "--arch", "yoco_tiny", "--n-layers", "2", "--task", "gpt", "--tiktoken-model", "byte",
+                     "--tokens-per-sample", "64", "--batch-size", "2", "--pad-to-max-len", "--batch-read-ahead", "4",
+                     "--log-interval", "2", "--warmup-updates", "1", "--max-update", str(max_update),
+                     "--save-dir", save, "--cpu", "--kernels", "torch", "--model-parallel-size", "2", "--seed", "3"])
+    assert rc == 0
+    if rank == 0:
+        open(out, "w").write(buf.getvalue())
+    tp.destroy_model_parallel()
+
+
+def test_cli_tensor_parallel_training_matches_single_rank(tmp_path):
+    """The train CLI with --model-parallel-size 2 on 2 ranks: the same losses / gradient norms as one rank, one
+    checkpoint part per TP rank holding that rank's slices of the single-rank weights, and resume from the parts."""
+    import contextlib
+    import io
+    import json
+    import os
+    from faster_yoco_b200.cli import train as T
+    from faster_yoco_b200.models.yoco import shard_state_dict
+    data = str(tmp_path / "data")
+    os.makedirs(os.path.join(data, "json"))
+    os.makedirs(os.path.join(data, "shard", "w"))
+    with open(os.path.join(data, "shard", "w", "00000.jsonl"), "w") as f:
+        for d in range(40):
+            f.write(json.dumps({"text": f"doc {d}: a few words to pack\n\nmore words"}) + "\n")
+    json.dump(["shard/w/00000.jsonl"], open(os.path.join(data, "json", "w.json"), "w"))
+    json.dump([{"name": "w", "weight": 1.0}], open(os.path.join(data, "json", "train.json"), "w"))
+    buf = io.StringIO()
+    with contextlib.redirect_stdout(buf):
+        assert T.main([data, "--arch", "yoco_tiny", "--n-layers", "2", "--task", "gpt", "--tiktoken-model", "byte",
+                       "--tokens-per-sample", "64", "--batch-size", "2", "--pad-to-max-len", "--batch-read-ahead",
+                       "4", "--log-interval", "2", "--warmup-updates", "1", "--max-update", "2",
+                       "--save-dir", str(tmp_path / "s1"), "--cpu", "--kernels", "torch", "--seed", "3"]) == 0
+    single = [l for l in buf.getvalue().splitlines() if l.startswith("epoch")][-1]
+    out = str(tmp_path / "tp.log")
+    run_ranks(_cli_tp_worker, 2, data, str(tmp_path / "s2"), out, 2)
+    tpline = [l for l in open(out).read().splitlines() if l.startswith("epoch")][-1]
+    loss = lambda l: float(l.split("loss ")[1].split(" ")[0])
+    gn = lambda l: float(l.split("gnorm ")[1].split(" ")[0])
+    assert abs(loss(single) - loss(tpline)) < 2e-3 and abs(gn(single) - gn(tpline)) < 2e-3 * max(1.0, gn(single))
+    s1 = torch.load(str(tmp_path / "s1" / "checkpoint_last.pt"), weights_only=False)["model"]
+    full = {k[len("decoder.model."):]: v.float() for k, v in s1.items()}
+    for r in range(2):
+        part = torch.load(str(tmp_path / "s2" / f"checkpoint_last-model_part-{r}.pt"), weights_only=False)["model"]
+        want = shard_state_dict(full, 2, r)
+        for k in ("embed_tokens.weight", "self_decoder.layers.0.mixer.q_proj.weight",
+                  "self_decoder.layers.0.mixer.out_proj.weight", "self_decoder.layers.0.mixer_layer_norm.weight"):
+            torch.testing.assert_close(part["decoder.model." + k].float(), want[k], atol=1e-5, rtol=1e-4)
+    # resume from the parts and take one more update
+    run_ranks(_cli_tp_worker, 2, data, str(tmp_path / "s2"), out, 3)
+    assert "loaded checkpoint" in open(out).read()
