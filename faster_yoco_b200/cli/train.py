@@ -135,6 +135,9 @@ def main(argv=None) -> int:
     cp = args.context_parallel_size
     if tp > 1 and cp > 1:
         raise SystemExit("tensor and context parallelism cannot be combined")
+    if tp > 1 and family != "yoco":
+        raise SystemExit("tensor-parallel training is implemented for YOCO (the LLaMA baseline's output layer returns "
+                         "only this rank's vocabulary slice, as in the reference, which evaluation handles)")
     rep = cp if cp > 1 else tp                # consecutive ranks that hold one model replica
     dp = world // rep
     comm = args.comm if (dp > 1 and device.type == "cuda" and rep == 1) else "nccl"
