@@ -44,6 +44,7 @@ def main(argv=None) -> int:
     args = validate_parser().parse_args(argv)
     device = setup_runtime(args)
     rank, world = D.rank(), D.world()
+    tp = max(1, int(getattr(args, "model_parallel_size", 1) or 1))
     task = build_task(args)
     model, family = build_model(args, task, device)
     model.eval()
@@ -55,8 +56,9 @@ def main(argv=None) -> int:
             logs = [log]
         else:
             ds = task.load_dataset(args.valid_subset)
-            itr = task.get_batch_iterator(ds, max_sentences=args.batch_size, seed=args.seed, num_shards=world,
-                                          shard_id=rank)
+            # the ranks of one tensor-parallel group evaluate the same batches (consecutive ranks form a group)
+            itr = task.get_batch_iterator(ds, max_sentences=args.batch_size, seed=args.seed, num_shards=world // tp,
+                                          shard_id=rank // tp)
             logs = []
             for i, sample in enumerate(itr):
                 if args.max_valid_steps is not None and i >= args.max_valid_steps:
@@ -69,7 +71,7 @@ def main(argv=None) -> int:
     if D.is_dist():
         gathered = [None] * world
         dist.all_gather_object(gathered, logs)
-        logs = [l for part in gathered for l in part]
+        logs = [l for g, part in enumerate(gathered) if g % tp == 0 for l in part]   # one copy per replica
     results = type(crit).reduce_metrics(logs)
     if rank == 0:
         print(json.dumps({"subset": args.valid_subset, "task": args.task, "criterion": args.criterion,

@@ -121,3 +121,34 @@ def test_cli_tensor_parallel_training_matches_single_rank(tmp_path):
     # resume from the parts and take one more update
     run_ranks(_cli_tp_worker, 2, data, str(tmp_path / "s2"), out, 3)
     assert "loaded checkpoint" in open(out).read()
+
+
+def _cli_validate_tp_worker(rank, world, data_dir, out, mp):
+    import contextlib
+    import io
+    from faster_yoco_b200.cli import validate as V
+    from faster_yoco_b200.parallel import tp
+    buf = io.StringIO()
+    with contextlib.redirect_stdout(buf):
+        assert V.main(["--task", "harness_eval", "--criterion", "harness_eval", "--eval-data", "harness_boolq",
+                       "--data-dir", data_dir, "--batch-size", "4", "--arch", "yoco_tiny", "--n-layers", "2",
+                       "--tiktoken-model", "byte", "--tokens-per-sample", "128", "--cpu", "--kernels", "torch",
+                       "--model-parallel-size", str(mp), "--seed", "5"]) == 0
+    if rank == 0:
+        open(out, "w").write(buf.getvalue())
+    tp.destroy_model_parallel()
+
+
+def test_cli_validate_tensor_parallel_matches_single_rank(tmp_path):
+    """Harness evaluation with --model-parallel-size 2 on 2 ranks (both ranks on the same batches) reproduces the
+    single-rank accuracy and loss."""
+    import json
+    import test_components_cpu as TC
+    TC._write_boolq(str(tmp_path))
+    one, two = str(tmp_path / "one.log"), str(tmp_path / "two.log")
+    run_ranks(_cli_validate_tp_worker, 1, str(tmp_path), one, 1)
+    run_ranks(_cli_validate_tp_worker, 2, str(tmp_path), two, 2)
+    a = json.loads(open(one).read().strip().splitlines()[-1])
+    b = json.loads(open(two).read().strip().splitlines()[-1])
+    assert a["accuracy"] == b["accuracy"] and a["accuracy_norm"] == b["accuracy_norm"]
+    assert abs(a["loss"] - b["loss"]) <= 2e-3, (a, b)            # per-option NLL: the same model outputs
