@@ -176,6 +176,29 @@ def merge_clocks(per_rank):
     return out
 
 
+def result_line(args, world: int, ms: float, clocks, e2e, launches, exposed=None) -> dict:
+    """The one JSON line of the benchmark contract (rank 0 prints it)."""
+    tokens_per_update = args.batch * args.seq_len * world
+    value = tokens_per_update / (ms / 1000.0)
+    out = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": value / BASELINE_TOKS, "dtype": "bf16",
+        "data": "synthetic uniform-random token ids, N(0,0.02) random-init weights",
+        "config": {"model": args.arch + ("-swa%d" % args.sliding_window if args.sliding_window else ""),
+                   "global_batch": args.batch * world, "seq_len": args.seq_len,
+                   "tokens_per_update": tokens_per_update, "parallelism": f"dp{world}-zero1",
+                   "kernels": args.kernels, "comm": args.comm, "cuda_graph": bool(args.graph),
+                   "comm_overlap": bool(args.overlap), "zero_partition": args.partition,
+                   "transport": args.transport if (args.overlap or args.transport == "gemm") else None,
+                   "l2": "working set (>=55 GB of params/grads/Adam state per update) >> 126 MB L2"},
+        "clocks": clocks, "e2e": e2e, "gpu_launches": launches,
+    }
+    if exposed is not None:
+        out["exposed_comm"] = exposed
+    return out
+
+
 def count_our_launches(step_fn) -> int:
     """Kernels from this repository's extension launched by one update (profiled separately, not timed)."""
     from torch.profiler import ProfilerActivity, profile
@@ -301,22 +324,7 @@ def main():
         exposed = {"compute_only_ms_per_step": ms_local, "exposed_comm_ms": ms - ms_local}
 
     if rank == 0:
-        out = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": value / BASELINE_TOKS, "dtype": "bf16",
-            "data": "synthetic uniform-random token ids, N(0,0.02) random-init weights",
-            "config": {"model": args.arch + ("-swa%d" % args.sliding_window if args.sliding_window else ""),
-                       "global_batch": args.batch * world, "seq_len": args.seq_len,
-                       "tokens_per_update": tokens_per_update, "parallelism": f"dp{world}-zero1",
-                       "kernels": args.kernels, "comm": args.comm, "cuda_graph": bool(args.graph),
-                       "comm_overlap": bool(args.overlap), "zero_partition": args.partition,
-                       "transport": args.transport if (args.overlap or args.transport == "gemm") else None,
-                       "l2": "working set (>=55 GB of params/grads/Adam state per update) >> 126 MB L2"},
-            "clocks": clocks, "e2e": e2e, "gpu_launches": launches,
-        }
-        if exposed is not None:
-            out["exposed_comm"] = exposed
+        out = result_line(args, world, ms, clocks, e2e, launches, exposed)
         print(json.dumps(out), flush=True)
     trainer.release_graph()
     D.barrier()

@@ -224,3 +224,34 @@ def test_bench_merge_clocks():
     m = bench.merge_clocks([one, two, one])
     assert m["sm_mhz"] == 1900 and m["per_rank_sm_mhz"] == [1900, 1500, 1900]
     assert m["reasons"] == ["hw_slowdown", "sw_power_cap"] and m["samples"] == 29
+
+
+def test_bench_result_line_contract(monkeypatch):
+    """Every key of the benchmark line the driver reads, with the right types (no GPU needed to assemble it)."""
+    import sys
+    bench = _bench()
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--steps", "7", "--warmup", "2"])
+    args = bench.parse()
+    args.overlap = 0
+    clocks = bench.merge_clocks([{"sm_mhz": 1900, "sm_max_mhz": 1965, "reasons": ["sw_power_cap"], "samples": 5}])
+    e2e = {"value": 28000.0, "unit": "tokens/s", "ms_per_step": 73.0, "h2d_bytes_per_step": 32768,
+           "d2h_bytes_per_step": 4}
+    out = bench.result_line(args, 8, 70.0, clocks, e2e, 8000)
+    line = json.loads(json.dumps(out))
+    for k, t in (("metric", str), ("value", float), ("unit", str), ("n_gpus", int), ("steps", int),
+                 ("warmup", int), ("ms_per_step", float), ("higher_is_better", bool), ("scaling", str),
+                 ("vs_baseline", float), ("dtype", str), ("data", str), ("config", dict), ("clocks", dict),
+                 ("e2e", dict), ("gpu_launches", int)):
+        assert isinstance(line[k], t), k
+    assert line["warmup"] >= 3 and line["steps"] == 7 and line["n_gpus"] == 8 and line["scaling"] == "weak"
+    assert abs(line["value"] - 8 * 2048 / 0.070) < 1e-6 * line["value"]
+    assert abs(line["vs_baseline"] - line["value"] / 138983.0) < 1e-9
+    for k in ("model", "global_batch", "seq_len", "parallelism", "l2"):
+        assert k in line["config"], k
+    assert line["config"]["model"] == "yoco_3b" and line["config"]["global_batch"] == 8
+    for k in ("sm_mhz", "sm_max_mhz", "reasons"):
+        assert k in line["clocks"], k
+    for k in ("value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step"):
+        assert k in line["e2e"], k
+    assert line["metric"] == json.load(open(os.path.join(os.path.dirname(os.path.dirname(
+        os.path.abspath(__file__))), "BASELINE.json")))["metric"]
