@@ -151,7 +151,7 @@ def main(argv=None) -> int:
     graph = bool(args.cuda_graph) and device.type == "cuda" and rep == 1
     trainer = Trainer(model, optim, device=device, comm=comm, graph_step=graph,
                       overlap=overlap, transport=transport, partition=args.partition, pad_idx=task.tokenizer.pad_id,
-                      chunk=args.zero_chunk)
+                      chunk=args.zero_chunk, zero_sharding=args.zero_sharding)
     if cp > 1:
         if family != "yoco":
             raise SystemExit("context parallelism is implemented for YOCO")

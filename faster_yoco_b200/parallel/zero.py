@@ -284,8 +284,14 @@ def grad_slot(p: torch.Tensor) -> Optional[torch.Tensor]:
 class ZeroOptimizer:
     """Sharded FP32 Adam (apex AdamW expression) over the owner's segment of a :class:`FlatParams`."""
 
-    def __init__(self, flat: FlatParams, optim_cfg, comm: str = "nccl", group=None):
+    def __init__(self, flat: FlatParams, optim_cfg, comm: str = "nccl", group=None, replicas: int = 1):
+        """replicas > 1: no sharding (``--zero-sharding none``, fairseq's plain data parallelism): ``flat`` is one
+        segment holding everything, the gradient buffer is averaged over the `replicas` ranks of `group` and every
+        rank runs the full Adam step."""
         self.flat, self.cfg, self.comm, self.group = flat, optim_cfg, comm, group
+        self.replicas = replicas
+        if replicas > 1 and flat.world != 1:
+            raise ValueError("unsharded data parallelism keeps one segment (FlatParams world 1)")
         seg = flat.param_segment()
         self.master = seg.reshape(-1).float().clone()       # local order (a gather in the block-cyclic layout)
         self.exp_avg = torch.zeros_like(self.master)
@@ -319,6 +325,14 @@ class ZeroOptimizer:
         """Average the gradient buffer over ranks into each owner's segment (BF16). Returns the owned segment's sum
         of squares when the reduction produced it (fused path), else None."""
         fp = self.flat
+        if self.replicas > 1 and not self.skip_exchange:
+            g = fp.grad_flat
+            if dist.get_backend(self.group) == "nccl":
+                dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.group)
+            else:
+                dist.all_reduce(g, group=self.group)
+                g.div_(self.replicas)
+            return None
         if fp.world == 1 or self.skip_exchange:
             return None
         if self.comm == "fused" and self.p2p is not None:
@@ -376,7 +390,8 @@ class ZeroOptimizer:
         from .. import ops
         fp = self.flat
         g16 = fp.grad_segment()
-        factor = fp.world / torch.where(sample_size > 0, sample_size, torch.ones_like(sample_size)).float()
+        factor = max(fp.world, self.replicas) / torch.where(sample_size > 0, sample_size,
+                                                            torch.ones_like(sample_size)).float()
         native = ops.native_on(g16)
         if sq is not None:
             sq = sq.clone()

@@ -46,7 +46,7 @@ class Trainer:
     def __init__(self, model: torch.nn.Module, optim_cfg, *, device, comm: str = "nccl",
                  pad_idx: int = 1, graph_step: bool = False, group=None, check_consistency: bool = True,
                  overlap: bool = False, partition: str = "even", criterion=None, transport: str = "sm",
-                 chunk: Optional[int] = None):
+                 chunk: Optional[int] = None, zero_sharding: str = "os"):
         from ..parallel import tp as TP
         self.tp = TP.tp_size()
         if self.tp > 1:
@@ -66,15 +66,22 @@ class Trainer:
         else:
             self.rank, self.world = D.rank(), D.world()
         self.group = group
+        if zero_sharding not in ("os", "none"):
+            raise ValueError(f"unknown zero_sharding {zero_sharding!r}")
+        replicas = 1
+        if zero_sharding == "none":
+            # fairseq's plain data parallelism: every rank keeps all optimizer state; gradients all-reduced
+            replicas, comm, overlap = self.world, "nccl", False
         p2p = None
         if comm == "fused" and self.world > 1 and self.device.type == "cuda":
             from ..parallel.p2p import PeerComm
             p2p = PeerComm(group)
-        self.flat = FlatParams(model.named_parameters(), self.world, self.rank, self.device,
+        fw, fr = (1, 0) if replicas > 1 else (self.world, self.rank)
+        self.flat = FlatParams(model.named_parameters(), fw, fr, self.device,
                                dtype=next(model.parameters()).dtype, allocator=p2p.alloc if p2p else None,
                                partition=partition, chunk=chunk)
         self.flat.direct_grads = self.device.type == "cuda" and ops.get_backend() == "native"
-        self.zero = ZeroOptimizer(self.flat, optim_cfg, comm=comm, group=group)
+        self.zero = ZeroOptimizer(self.flat, optim_cfg, comm=comm, group=group, replicas=replicas)
         if self.tp > 1:
             self.zero.set_tensor_parallel(TP.tp_group(), TP.tp_rank(), TP.is_sharded)
         self.zero.p2p = p2p

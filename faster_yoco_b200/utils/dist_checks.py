@@ -8,7 +8,7 @@ import torch.distributed as dist
 
 
 def _tiny_trainer(device, comm="nccl", seed=0, graph=False, arch="yoco_tiny", dtype=torch.float32, overlap=True,
-                  transport="sm", partition="even", chunk=None):
+                  transport="sm", partition="even", chunk=None, zero_sharding="os"):
     from ..config import OptimConfig, build_args
     from ..models.yoco import YOCO
     from ..train.trainer import Trainer
@@ -17,7 +17,7 @@ def _tiny_trainer(device, comm="nccl", seed=0, graph=False, arch="yoco_tiny", dt
     model = YOCO(args).to(device=device, dtype=dtype)
     cfg = OptimConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, warmup_updates=0, total_num_update=20)
     return model, Trainer(model, cfg, device=device, comm=comm, graph_step=graph, overlap=overlap,
-                          transport=transport, partition=partition, chunk=chunk)
+                          transport=transport, partition=partition, chunk=chunk, zero_sharding=zero_sharding)
 
 
 def _batches(rank, world, n, seed=1, batch=2, seq=256, vocab=1024):
@@ -29,9 +29,9 @@ def _batches(rank, world, n, seed=1, batch=2, seq=256, vocab=1024):
     return out
 
 
-def zero_matches_single(rank, world, outdir, steps, partition="even", chunk=None):
+def zero_matches_single(rank, world, outdir, steps, partition="even", chunk=None, zero_sharding="os"):
     """World-size-N ZeRO training on N shards of each global batch; rank 0 saves the final flat params."""
-    model, tr = _tiny_trainer(torch.device("cpu"), partition=partition, chunk=chunk)
+    model, tr = _tiny_trainer(torch.device("cpu"), partition=partition, chunk=chunk, zero_sharding=zero_sharding)
     for ids in _batches(rank, world, steps):
         mine = ids[rank]
         b = {"src_tokens": mine[:, :-1].contiguous(), "target": mine[:, 1:].contiguous(),
@@ -39,7 +39,8 @@ def zero_matches_single(rank, world, outdir, steps, partition="even", chunk=None
         tr.train_step(b)
     sd = {k: v.detach().clone() for k, v in model.state_dict().items()}
     if rank == 0:
-        torch.save({"sd": sd, "num_updates": tr.num_updates()}, os.path.join(outdir, f"ws{world}_{partition}.pt"))
+        torch.save({"sd": sd, "num_updates": tr.num_updates()},
+                   os.path.join(outdir, f"ws{world}_{partition}_{zero_sharding}.pt"))
 
 
 def single_reference(outdir, world, steps, with_norm=False):

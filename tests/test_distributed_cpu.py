@@ -17,11 +17,13 @@ def test_greedy_partition_is_oss_rule():
     assert greedy_partition([100, 1, 1, 1], 3) == [0, 1, 2, 1]
 
 
-@pytest.mark.parametrize("partition,chunk", [("even", None), ("cyclic", 1024)])
-def test_zero_ws2_matches_single_process(tmp_path, partition, chunk):
+@pytest.mark.parametrize("partition,chunk,sharding", [("even", None, "os"), ("cyclic", 1024, "os"),
+                                                      ("even", None, "none")])
+def test_zero_ws2_matches_single_process(tmp_path, partition, chunk, sharding):
+    """ZeRO-1 (contiguous and block-cyclic owner maps) and unsharded data parallelism (--zero-sharding none)."""
     steps = 3
-    run_ranks(dist_checks.zero_matches_single, 2, str(tmp_path), steps, partition, chunk)
-    got = torch.load(os.path.join(tmp_path, f"ws2_{partition}.pt"))
+    run_ranks(dist_checks.zero_matches_single, 2, str(tmp_path), steps, partition, chunk, sharding)
+    got = torch.load(os.path.join(tmp_path, f"ws2_{partition}_{sharding}.pt"))
     assert got["num_updates"] == steps
     ref = dist_checks.single_reference(str(tmp_path), 2, steps)
     for k, v in ref.items():
