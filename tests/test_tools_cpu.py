@@ -255,3 +255,29 @@ def test_bench_result_line_contract(monkeypatch):
         assert k in line["e2e"], k
     assert line["metric"] == json.load(open(os.path.join(os.path.dirname(os.path.dirname(
         os.path.abspath(__file__))), "BASELINE.json")))["metric"]
+
+
+def test_reference_recipe_command_lines_parse():
+    """The reference's training and evaluation command lines (scripts/train.sh, eval_task.sh, eval_needle.sh) are
+    accepted unchanged."""
+    from faster_yoco_b200.cli.options import train_parser, validate_parser
+    a = train_parser().parse_args([
+        "DATA", "--save-interval-updates", "5000", "--no-epoch-checkpoints", "--arch", "yoco_base", "--criterion",
+        "cross_entropy", "--task", "gpt", "--tokens-per-sample", "2048", "--tokenizer-pad-to-multiple", "8",
+        "--pad-to-max-len", "--optimizer", "adam", "--adam-betas", "(0.9, 0.95)", "--adam-eps", "1e-06",
+        "--clip-norm", "2.0", "--lr", "0.00015", "--lr-scheduler", "polynomial_decay", "--warmup-updates", "50",
+        "--weight-decay", "0.05", "--batch-size", "1", "--model-parallel-size", "1", "--update-freq", "1",
+        "--batch-read-ahead", "1000", "--total-num-update", "300000", "--log-format", "simple", "--log-interval", "10",
+        "--disable-validation", "--tiktoken-model", "cl100k_base", "--no-save", "--bf16", "--zero-sharding", "os"])
+    assert a.adam_betas == (0.9, 0.95) and a.clip_norm == 2.0 and a.total_num_update == 300000
+    v = validate_parser()
+    v.parse_args(["--data-dir", "hd/", "--criterion", "harness_eval", "--task", "harness_eval", "--batch-size", "4",
+                  "--eval-data", "harness_boolq", "--log-format", "simple", "--log-interval", "10", "--bf16",
+                  "--tokenizer-pad-to-multiple", "8", "--arch", "yoco_3b_new", "--tiktoken-model", "cl100k_base",
+                  "--load-ckpt", "c/checkpoint.pth", "--yoco-model", "c", "--tokens-per-sample", "4096"])
+    v.parse_args(["--arch", "llama_from_ckpt", "--llama-model", "l", "--load-ckpt", "l/consolidated.00.pth",
+                  "--tokens-per-sample", "4096", "--task", "harness_eval", "--criterion", "harness_eval"])
+    v.parse_args(["--task", "pseudo", "--criterion", "multi_needle", "--needle-num", "4", "--batch-size", "1",
+                  "--max-epoch", "1", "--no-save", "--tiktoken-model", "cl100k_base", "--bf16", "--arch", "yoco_3b_new",
+                  "--load-ckpt", "c/c.pth", "--yoco-model", "c", "--tokens-per-sample", "1048576", "--interval",
+                  "1048576"])
