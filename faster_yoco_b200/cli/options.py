@@ -109,6 +109,12 @@ def train_parser() -> argparse.ArgumentParser:
     g.add_argument("--restore-file", default="checkpoint_last.pt")
     g.add_argument("--reset-optimizer", action="store_true")
     g.add_argument("--reset-dataloader", action="store_true")
+    g.add_argument("--reset-lr-scheduler", action="store_true",
+                   help="resume without the checkpoint's learning-rate schedule state")
+    g.add_argument("--reset-meters", action="store_true",
+                   help="fairseq compatibility: meters are never restored from a checkpoint here")
+    g.add_argument("--keep-interval-updates", type=int, default=-1,
+                   help="keep only the last N checkpoint_1_<update>.pt files (-1: keep all)")
     g.add_argument("--disable-validation", action="store_true")
     g.add_argument("--validate-interval-updates", type=int, default=0,
                    help="evaluate the valid subset every N updates (0: only after the last update)")

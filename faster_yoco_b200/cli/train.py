@@ -22,7 +22,7 @@ import torch.distributed as dist
 
 from ..config import OptimConfig
 from ..parallel import dist as D
-from ..train.checkpoint import load_checkpoint, part_path, save_checkpoint
+from ..train.checkpoint import load_checkpoint, part_path, prune_interval_checkpoints, save_checkpoint
 from ..train.metrics import format_log
 from ..train.trainer import Trainer
 from .common import build_model, build_task, setup_runtime
@@ -163,7 +163,7 @@ def main(argv=None) -> int:
                                   shard_id=rank // rep)
     restore = os.path.join(args.save_dir, args.restore_file)
     if os.path.exists(part_path(restore)) and not args.reset_optimizer:
-        ck = load_checkpoint(restore, model, trainer)
+        ck = load_checkpoint(restore, model, trainer, reset_lr_scheduler=args.reset_lr_scheduler)
         its = (ck.get("extra_state") or {}).get("train_iterator")
         if its and not args.reset_dataloader and hasattr(itr, "load_state_dict") and len(its) == world:
             itr.load_state_dict(its[rank])
@@ -201,6 +201,9 @@ def main(argv=None) -> int:
                 import shutil
                 shutil.copyfile(part_path(os.path.join(args.save_dir, f"checkpoint_1_{nu}.pt")),
                                 part_path(os.path.join(args.save_dir, "checkpoint_last.pt")))
+            D.barrier()                      # every part written before any rank prunes
+            if rank == 0:
+                prune_interval_checkpoints(args.save_dir, args.keep_interval_updates)
     trainer.pending.check(block=True)
     if not args.disable_validation and args.validate_interval_updates <= 0:
         v = validate_lm(model, task, args, device, rank, world, rep, cp, tp)

@@ -125,8 +125,9 @@ def load_model_weights(model, path_or_ckpt, strict: bool = True):
     return ck
 
 
-def load_checkpoint(path: str, model, trainer) -> dict:
-    """Restore model weights, this rank's optimizer shard, the update count and the LR schedule."""
+def load_checkpoint(path: str, model, trainer, reset_lr_scheduler: bool = False) -> dict:
+    """Restore model weights, this rank's optimizer shard, the update count and (unless reset_lr_scheduler) the LR
+    schedule."""
     ck = load_model_weights(model, part_path(path))
     _, strip = _core(model)
     st = ck.get("last_optimizer_state") or {}
@@ -153,8 +154,28 @@ def load_checkpoint(path: str, model, trainer) -> dict:
     zero.num_updates = int(st.get("step", ck["optimizer_history"][-1]["num_updates"] if ck.get("optimizer_history")
                                       else 0))
     hist = ck.get("optimizer_history") or []
-    if hist and "lr_scheduler_state" in hist[-1]:
+    if hist and "lr_scheduler_state" in hist[-1] and not reset_lr_scheduler:
         trainer.sched.load_state_dict(hist[-1]["lr_scheduler_state"])
     if dist.is_initialized():
         dist.barrier()
     return ck
+
+
+def prune_interval_checkpoints(save_dir: str, keep: int) -> list:
+    """fairseq's --keep-interval-updates: delete all but the newest `keep` checkpoint_1_<update>.pt files (and their
+    tensor-parallel part files). Returns the removed paths."""
+    import re
+    if keep < 0 or not os.path.isdir(save_dir):
+        return []
+    pat = re.compile(r"^checkpoint_1_(\d+)(-model_part-\d+)?\.pt$")
+    found = {}
+    for f in os.listdir(save_dir):
+        m = pat.match(f)
+        if m:
+            found.setdefault(int(m.group(1)), []).append(os.path.join(save_dir, f))
+    removed = []
+    for nu in sorted(found)[:max(0, len(found) - keep)]:
+        for p in found[nu]:
+            os.remove(p)
+            removed.append(p)
+    return removed

@@ -371,3 +371,19 @@ def test_cli_validate_lm_perplexity(tmp_path, capsys):
                    "--batch-size", "2", "--pad-to-max-len", "--cpu", "--kernels", "torch"]) == 0
     res = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert 0 < res["loss"] < 20 and res["ntokens"] > 0          # one finite pass over the valid split
+
+
+def test_cli_keep_interval_updates(tmp_path, capsys):
+    """--save-interval-updates 1 --keep-interval-updates 2: only the newest two interval checkpoints remain."""
+    from faster_yoco_b200.cli import train as T
+    data = str(tmp_path / "data")
+    _corpus(data)
+    save = str(tmp_path / "ckpt")
+    assert T.main([data, "--arch", "yoco_tiny", "--n-layers", "2", "--task", "gpt", "--tiktoken-model", "byte",
+                   "--tokens-per-sample", "64", "--batch-size", "2", "--pad-to-max-len", "--batch-read-ahead", "8",
+                   "--log-interval", "2", "--warmup-updates", "2", "--save-dir", save, "--cpu", "--kernels", "torch",
+                   "--max-update", "4", "--save-interval-updates", "1", "--keep-interval-updates", "2",
+                   "--reset-meters"]) == 0
+    kept = sorted(f for f in os.listdir(save) if f.startswith("checkpoint_1_"))
+    assert kept == ["checkpoint_1_3.pt", "checkpoint_1_4.pt"], kept
+    assert os.path.exists(os.path.join(save, "checkpoint_last.pt"))
