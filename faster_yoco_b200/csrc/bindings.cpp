@@ -10,6 +10,8 @@ namespace fyb {
 
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
           const c10::optional<at::Tensor>& R);
+void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
+               const c10::optional<at::Tensor>& R);
 void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, const at::Tensor& grad_flat,
                   const at::Tensor& bases, int64_t seg, int64_t rank, int64_t chunk);
 std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps);
@@ -117,6 +119,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "faster_yoco_b200 sm_100a kernels";
   m.def("gemm", &fyb::gemm, "C = A @ B^T on tcgen05 (operands K-major or MN-major)", py::arg("A"), py::arg("B"),
         py::arg("C"), py::arg("a_mn_major"), py::arg("b_mn_major"), py::arg("residual") = py::none());
+  m.def("gemm_pair", &fyb::gemm_pair, "C = A @ B^T on CTA pairs (tcgen05.mma.cta_group::2, 256 x 256 tiles)",
+        py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn_major"), py::arg("b_mn_major"),
+        py::arg("residual") = py::none());
   m.def("gemm_scatter", &fyb::gemm_scatter,
         "weight gradient dW = A^T B stored straight into each element's ZeRO owner (own slot or peer staging)",
         py::arg("A"), py::arg("B"), py::arg("C"), py::arg("accumulate"), py::arg("grad_flat"), py::arg("bases"),

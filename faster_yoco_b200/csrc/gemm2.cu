@@ -1,0 +1,421 @@
+// Two-CTA tcgen05 GEMM for sm_100a: C[M,N] = sum_k A(m,k) * B(n,k) (+ R), tiles of 256 x 256 computed by a CTA pair.
+//
+// The one-CTA kernel (gemm.cu) fills 48 KB of shared memory per 64-wide K slab for each 128 x 256 output tile: the
+// whole 256-row B slab goes to every CTA. Here a cluster of two CTAs on one TPC issues tcgen05.mma.cta_group::2 with
+// M = 256: CTA r holds rows [128 r, 128 r + 128) of the A tile and rows [128 r, 128 r + 128) of the B tile (its half),
+// the tensor cores of the pair exchange the B halves, and each CTA's TMEM receives its 128 rows of the 256 x 256 fp32
+// accumulator. Per SM that is 32 KB of operand fill per K slab for the same 128 x 256 output (one third less), which
+// is what limited the one-CTA kernel (tensor pipe 63 % active, operand feed from L2).
+//
+// Roles (6 warps per CTA, both CTAs):
+//   warp 0      : TMA producer (one lane): loads this CTA's A rows and B half; the bytes of BOTH CTAs complete on
+//                 the leader CTA's (rank 0) full barrier, which only the leader's producer arms with the pair's total
+//   warp 1      : TMEM allocation for the pair (cta_group::2, both CTAs); on the leader, one lane issues the MMAs and
+//                 commits: stage release to both CTAs' empty barriers, accumulator ready to both CTAs' tfull barriers
+//                 (one commit per CTA, addressed through mapa)
+//   warps 2..5  : epilogue on each CTA's own TMEM rows; the peer's warps arrive on the leader's tempty barrier
+// Loads are plain cp.async.bulk.tensor of this GPU's memory in the .cta_group::2 form; nothing is multicast.
+// Every wait is bounded (2 s) and records a status word; both CTAs always reach the final cluster barrier.
+#include <ATen/ATen.h>
+#include <c10/util/Optional.h>
+
+#include "common/host.h"
+#include "common/ptx.cuh"
+
+namespace fyb {
+namespace {
+
+constexpr int kBM = 128;        // rows of A (and of the output) per CTA
+constexpr int kBN = 256;        // output columns per tile; each CTA loads kBN / 2 rows of B
+constexpr int kBK = 64;
+constexpr int kThreads2 = 192;
+constexpr int kStages2 = 6;
+
+enum Epi2 : int { kE2Bf16 = 0, kE2Bf16Res = 1, kE2F32 = 2 };
+
+struct Smem2 {
+  static constexpr int A_BYTES = kBM * kBK * 2;             // 16 KB
+  static constexpr int B_BYTES = (kBN / 2) * kBK * 2;       // 16 KB: this CTA's half of the B slab
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFF = kStages2 * STAGE_BYTES;
+  static constexpr int TOTAL = BAR_OFF + 256 + 1024;
+};
+static_assert(Smem2::TOTAL <= 227 * 1024, "two-CTA GEMM shared memory above the per-CTA limit");
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the same shared-memory location in CTA `rank` of this cluster
+__device__ __forceinline__ uint32_t mapa_u32(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// TMA 2-D load into this CTA's shared memory whose completion bytes go to the mbarrier at cluster address bar
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// arrive (once) on the mbarrier at cluster address bar when the pair's previously issued MMAs have completed
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// bounded wait with cluster-scope acquire (arrivals from the peer CTA)
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort, int* status,
+                                                  int site) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 63u) == 0u) {
+      if (abort != nullptr && *abort) return false;
+      if (globaltimer_ns() - t0 > FYB_WAIT_NS) {
+        record_status(status, kMbarTimeout, site);
+        if (abort != nullptr) *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ void store_row32(const uint32_t (&r)[32], void* Cv, const __nv_bfloat16* R, int row,
+                                            int col, int N, int64_t ldc, int64_t ldr) {
+  if (EPI == kE2F32) {
+    float* C = reinterpret_cast<float*>(Cv) + static_cast<int64_t>(row) * ldc + col;
+    if (col + 32 <= N && (ldc % 4) == 0) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(C + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                        __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col + j < N) C[j] = __uint_as_float(r[j]);
+    }
+    return;
+  }
+  __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(Cv) + static_cast<int64_t>(row) * ldc + col;
+  uint32_t p[16];
+  if (EPI == kE2Bf16Res) {
+    const __nv_bfloat16* Rr = R + static_cast<int64_t>(row) * ldr + col;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int e = 2 * j;
+      const float r0 = col + e < N ? __bfloat162float(Rr[e]) : 0.f;
+      const float r1 = col + e + 1 < N ? __bfloat162float(Rr[e + 1]) : 0.f;
+      p[j] = pack_bf16(bf16_round(__uint_as_float(r[e])) + r0, bf16_round(__uint_as_float(r[e + 1])) + r1);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) p[j] = pack_bf16(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+  }
+  if (col + 32 <= N && (ldc % 8) == 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<uint4*>(C + 8 * j) = make_uint4(p[4 * j], p[4 * j + 1], p[4 * j + 2], p[4 * j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (col + j < N) {
+        const uint16_t h = (j & 1) ? static_cast<uint16_t>(p[j >> 1] >> 16) : static_cast<uint16_t>(p[j >> 1] & 0xffffu);
+        C[j] = __ushort_as_bfloat16(h);
+      }
+    }
+  }
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* Cv,
+                     const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, int* status) {
+  using S = Smem2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+  uint64_t* empty = full + kStages2;
+  uint64_t* tfull = empty + kStages2;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_rank();            // 0: leader (issues the MMAs), 1: peer
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+  const int num_m = (M + 2 * kBM - 1) / (2 * kBM);
+  const int num_n = (N + kBN - 1) / kBN;
+  const int num_tiles = num_m * num_n;
+  const int num_k = (K + kBK - 1) / kBK;
+  constexpr uint32_t TMEM_COLS = 2 * kBN;
+  constexpr uint32_t IDESC = idesc_bf16(2 * kBM, kBN, A_MN, B_MN);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages2; ++s) {
+      mbar_init(&full[s], 1);       // the leader's producer arms it with the pair's bytes
+      mbar_init(&empty[s], 1);      // one commit from the leader's MMA thread
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);      // one commit from the leader's MMA thread
+      mbar_init(&tempty[b], 8);     // 4 epilogue warps of each CTA (only the leader's is used)
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();                    // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int u = cluster_id; u < num_tiles && ok; u += num_clusters) {
+        const int mb = u % num_m, nb = u / num_m;
+        const int m0 = mb * 2 * kBM + static_cast<int>(crank) * kBM;
+        const int n0 = nb * kBN + static_cast<int>(crank) * (kBN / 2);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, status, 21)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * S::STAGE_BYTES;
+          uint8_t* sb = sa + S::A_BYTES;
+          const uint32_t bar = mapa_u32(&full[s], 0);
+          if (crank == 0) mbar_arrive_expect_tx(&full[s], 2 * S::STAGE_BYTES);
+          if (!A_MN) {
+            tma_load_2d_pair(sa, &tmA, bar, kb * kBK, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBM / 64; ++j) tma_load_2d_pair(sa + j * 8192, &tmA, bar, m0 + 64 * j, kb * kBK);
+          }
+          if (!B_MN) {
+            tma_load_2d_pair(sb, &tmB, bar, kb * kBK, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < (kBN / 2) / 64; ++j) tma_load_2d_pair(sb + j * 8192, &tmB, bar, n0 + 64 * j, kb * kBK);
+          }
+          if (++s == kStages2) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // drain: every issued stage must have been consumed before the CTA may exit
+      for (int i = 0; i < kStages2; ++i) {
+        mbar_wait(&empty[s], ph ^ 1u, nullptr, status, 22);
+        if (++s == kStages2) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------------------------------- UMMA issuer (leader)
+    if (crank == 0 && lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t acc_ph = 0;
+      bool ok = true;
+      for (int u = cluster_id; u < num_tiles && ok; u += num_clusters) {
+        if (!mbar_wait_cluster(&tempty[acc], acc_ph ^ 1u, abort_flag, status, 23)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * kBN);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag, status, 24)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(smem + s * S::STAGE_BYTES);
+          const uint32_t b0 = a0 + S::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = A_MN ? sw128_desc(a0 + k * 2048, 8192, 1024) : sw128_desc(a0 + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sw128_desc(b0 + k * 2048, 8192, 1024) : sw128_desc(b0 + k * 32, 16, 1024);
+            umma_bf16_pair(d, ad, bd, IDESC, (kb != 0 || k != 0) ? 1u : 0u);
+          }
+          // the stage may be refilled in both CTAs once these MMAs have read it
+          umma_commit_pair(mapa_u32(&empty[s], 0));
+          umma_commit_pair(mapa_u32(&empty[s], 1));
+          if (++s == kStages2) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(mapa_u32(&tfull[acc], 0));   // accumulator rows ready in both CTAs' TMEM
+        umma_commit_pair(mapa_u32(&tfull[acc], 1));
+        acc ^= 1;
+        if (acc == 0) acc_ph ^= 1u;
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_ph = 0;
+    for (int u = cluster_id; u < num_tiles; u += num_clusters) {
+      const int mb = u % num_m, nb = u / num_m;
+      if (!mbar_wait(&tfull[acc], acc_ph, abort_flag, status, 25)) break;
+      tc_fence_after();
+      const int row = mb * 2 * kBM + static_cast<int>(crank) * kBM + q * 32 + lane;
+      const uint32_t tb = tmem_base + static_cast<uint32_t>(acc * kBN) + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tb + c * 32, r);        // warp-collective: every lane, whatever its row
+        tmem_ld_wait();
+        const int col = nb * kBN + c * 32;
+        if (row < M && col < N) store_row32<EPI>(r, Cv, R, row, col, N, ldc, ldr);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_u32(&tempty[acc], 0));
+      acc ^= 1;
+      if (acc == 0) acc_ph ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();                    // both CTAs done with TMEM and with each other's barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const __nv_bfloat16* R, int M, int N, int K,
+                 int64_t ldc, int64_t ldr, cudaStream_t stream) {
+  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    FYB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem2::TOTAL));
+    attr_set = true;
+  }
+  const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
+  const int clusters = std::max(1, std::min(tiles, num_sms() / 2));
+  kern<<<2 * clusters, kThreads2, Smem2::TOTAL, stream>>>(ta, tb, C, R, M, N, K, ldc, ldr, status_ptr());
+  check_launch("gemm_pair");
+}
+
+template <int EPI>
+void dispatch_pair(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, void* C,
+                   const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, cudaStream_t st) {
+  if (!a_mn && !b_mn) launch_pair<false, false, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
+  else if (!a_mn && b_mn) launch_pair<false, true, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
+  else if (a_mn && b_mn) launch_pair<true, true, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
+  else launch_pair<true, false, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
+}
+
+}  // namespace
+
+// C = A @ B^T on CTA pairs (operand conventions as gemm()); no split-K. C: bf16 or fp32 [M, N]; R: bf16 residual.
+void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
+               const c10::optional<at::Tensor>& R) {
+  FYB_RANGE("fyb::gemm_pair");
+  FYB_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm_pair: CUDA tensors expected");
+  FYB_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm_pair: bf16 operands expected");
+  FYB_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm_pair: 2-D tensors expected");
+  FYB_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm_pair: last dimension must be contiguous");
+  const int64_t M = a_mn ? A.size(1) : A.size(0);
+  const int64_t K = a_mn ? A.size(0) : A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0);
+  const int64_t Kb = b_mn ? B.size(0) : B.size(1);
+  FYB_CHECK(K == Kb && K > 0, "gemm_pair: inner dimensions differ or are empty");
+  FYB_CHECK(C.size(0) == M && C.size(1) == N, "gemm_pair: output shape mismatch");
+  FYB_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm_pair: dimension too large");
+  const bool f32 = C.scalar_type() == at::kFloat;
+  FYB_CHECK(f32 || C.scalar_type() == at::kBFloat16, "gemm_pair: output must be bf16 or fp32");
+  const __nv_bfloat16* Rp = nullptr;
+  int64_t ldr = 0;
+  if (R.has_value() && R->defined()) {
+    FYB_CHECK(!f32, "gemm_pair: residual needs a bf16 output");
+    FYB_CHECK(R->scalar_type() == at::kBFloat16 && R->dim() == 2 && R->size(0) == M && R->size(1) == N &&
+                  R->stride(1) == 1,
+              "gemm_pair: residual must be bf16 [M, N] with contiguous rows");
+    Rp = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr());
+    ldr = R->stride(0);
+  }
+  if (M == 0 || N == 0) return;
+  c10::cuda::CUDAGuard guard(A.device());
+  cudaStream_t st = cur_stream();
+  const CUtensorMap ta = a_mn ? make_tmap_2d(A.data_ptr(), K, M, A.stride(0), 64)
+                              : make_tmap_2d(A.data_ptr(), M, K, A.stride(0), kBM);
+  const CUtensorMap tb = b_mn ? make_tmap_2d(B.data_ptr(), K, N, B.stride(0), 64)
+                              : make_tmap_2d(B.data_ptr(), N, K, B.stride(0), kBN / 2);
+  void* Cp = C.data_ptr();
+  const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
+  const int64_t ldc = C.stride(0);
+  if (f32) dispatch_pair<kE2F32>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
+  else if (Rp != nullptr) dispatch_pair<kE2Bf16Res>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
+  else dispatch_pair<kE2Bf16>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
+}
+
+}  // namespace fyb

@@ -13,6 +13,7 @@ The backend is a process-wide setting (``set_backend``), not a per-call dispatch
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -41,6 +42,10 @@ def native_on(t: torch.Tensor) -> bool:
 
 def _C():
     return _native.lib()
+
+
+# FYB_GEMM_PAIR=1: route large GEMMs to the CTA-pair kernel (gemm2.cu; not yet measured, off by default)
+_GEMM_PAIR = os.environ.get("FYB_GEMM_PAIR", "0") == "1"
 
 
 def _grad_slot(p):
@@ -84,7 +89,12 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn_major: bool = False, b_mn_maj
     N = b.shape[1] if b_mn_major else b.shape[0]
     if out is None:
         out = torch.empty(M, N, dtype=out_dtype or a.dtype, device=a.device)
-    _C().gemm(a, b, out, a_mn_major, b_mn_major, residual)
+    if _GEMM_PAIR and ((M + 255) // 256) * ((N + 255) // 256) >= 64:
+        # opt-in: CTA-pair kernel (256 x 256 tiles) for shapes with at least about a wave of tiles; the skinny
+        # shapes that need split-K stay on the one-CTA kernel
+        _C().gemm_pair(a, b, out, a_mn_major, b_mn_major, residual)
+    else:
+        _C().gemm(a, b, out, a_mn_major, b_mn_major, residual)
     return out
 
 

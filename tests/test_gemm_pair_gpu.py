@@ -1,0 +1,53 @@
+"""The CTA-pair GEMM (tcgen05.mma.cta_group::2, 256 x 256 tiles over two CTAs, gemm2.cu) against the one-CTA GEMM
+and an fp32 PyTorch oracle: every operand layout (forward, input gradient, weight gradient), M / N / K tails, the
+residual epilogue and fp32 output, two calls in a row.
+
+Marked ``gpu_pending``: this kernel has not yet run on a GPU, so ``-m gpu`` does not select it; run it with
+``-m gpu_pending``."""
+import pytest
+import torch
+
+from faster_yoco_b200 import ops
+
+pytestmark = pytest.mark.gpu_pending
+
+
+def _operands(M, N, K, a_mn, b_mn, g):
+    dev = torch.device("cuda", 0)
+    a = torch.randn((K, M) if a_mn else (M, K), generator=g, device=dev).to(torch.bfloat16)
+    b = torch.randn((K, N) if b_mn else (N, K), generator=g, device=dev).to(torch.bfloat16)
+    return a, b
+
+
+@pytest.mark.parametrize("M,N,K,a_mn,b_mn", [
+    (2048, 12312, 3072, False, False),     # q/k/v/g projection forward
+    (2048, 3072, 16384, False, True),      # FFN input gradient
+    (12312, 3072, 2048, True, True),       # q/k/v/g weight gradient
+    (300, 520, 200, False, False),         # tails in M, N and K
+    (520, 300, 136, True, False),
+])
+@pytest.mark.parametrize("epi", ["bf16", "res", "f32"])
+def test_gemm_pair_matches_one_cta_and_fp32(M, N, K, a_mn, b_mn, epi):
+    C = ops._C()
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    a, b = _operands(M, N, K, a_mn, b_mn, g)
+    dev = a.device
+    dt = torch.float32 if epi == "f32" else torch.bfloat16
+    res = torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16) if epi == "res" else None
+    one = torch.empty(M, N, dtype=dt, device=dev)
+    C.gemm(a, b, one, a_mn, b_mn, res)
+    for _ in range(2):
+        pair = torch.full((M, N), float("nan"), dtype=dt, device=dev)
+        C.gemm_pair(a, b, pair, a_mn, b_mn, res)
+        torch.cuda.synchronize()
+        assert int(C.status()[0].item()) == 0
+        assert not bool(torch.isnan(pair.float()).any()), "unwritten output"
+        # same per-element K order in both kernels: equal up to the tensor cores' accumulation rounding
+        torch.testing.assert_close(pair.float(), one.float(), atol=2e-2, rtol=1e-2)
+    A32 = (a.float().t() if a_mn else a.float())
+    B32 = (b.float() if b_mn else b.float().t())
+    ref = A32 @ B32
+    if res is not None:
+        ref = ref + res.float()
+    err = ((pair.float() - ref).abs().max() / ref.abs().max()).item()
+    assert err < 2e-2, err
