@@ -15,7 +15,13 @@ read and write peer memory directly over NVLink / NVSwitch:
 * bucketed overlap (``setup_buckets``): per layer bucket, gradient pieces are pushed to their owners during backward
   and parameters are pushed ahead of the next forward, either by kernels (``transport="sm"``) or by the copy
   engines (``transport="ce"``: one ``cudaMemcpyAsync`` per piece on one stream per peer, arrival published by a
-  one-thread release-add on the peer's counter); the owner sums the staged pieces from local memory.
+  one-thread release-add on the peer's counter); the owner sums the staged pieces from local memory;
+* GEMM-fused reduce-scatter (``setup_scatter`` / ``reduce_scattered``): the weight-gradient GEMMs and the embedding
+  backward store their output at the owners' staging slots while backward runs; after it, one push of the remaining
+  gradients, one barrier and the owner's local rank-order sum.
+
+Every kernel addresses owned elements through the owner map of the flat buffers (contiguous segments, or the
+block-cyclic chunks of ``FlatParams(partition="cyclic")``, ``csrc/common/zero_map.cuh``).
 
 The order in which ranks call these is identical by construction, so one flag slot with a monotonically increasing
 epoch serves every barrier. All waits are bounded on the device (a timeout sets the status word read by
