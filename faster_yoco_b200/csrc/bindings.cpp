@@ -12,6 +12,8 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bo
           const c10::optional<at::Tensor>& R);
 void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
                const c10::optional<at::Tensor>& R);
+int64_t gemm_sq(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, at::Tensor& sq_part);
+int64_t gemm_sq_slots(int64_t M, int64_t N, int64_t K);
 void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, const at::Tensor& grad_flat,
                   const at::Tensor& bases, int64_t seg, int64_t rank, int64_t chunk);
 std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps);
@@ -122,6 +124,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pair", &fyb::gemm_pair, "C = A @ B^T on CTA pairs (tcgen05.mma.cta_group::2, 256 x 256 tiles)",
         py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn_major"), py::arg("b_mn_major"),
         py::arg("residual") = py::none());
+  m.def("gemm_sq", &fyb::gemm_sq,
+        "weight gradient dW = A^T B (bf16, optionally accumulated) with fp32 sum-of-squares partials of the stored "
+        "values; returns the number of partials", py::arg("A"), py::arg("B"), py::arg("C"), py::arg("accumulate"),
+        py::arg("sq_part"));
+  m.def("gemm_sq_slots", &fyb::gemm_sq_slots, "partials a gemm_sq call of this shape writes");
   m.def("gemm_scatter", &fyb::gemm_scatter,
         "weight gradient dW = A^T B stored straight into each element's ZeRO owner (own slot or peer staging)",
         py::arg("A"), py::arg("B"), py::arg("C"), py::arg("accumulate"), py::arg("grad_flat"), py::arg("bases"),

@@ -27,10 +27,18 @@ constexpr int kThreads = 192;
 
 // kEpiScatter / kEpiScatterRes: the owner-scatter epilogue (OwnerScatter, zero_map.cuh) -- the GEMM fused with the
 // ZeRO reduce-scatter: element (row, col) of C has flat index x0 + row * ldc + col in the gradient buffer.
-enum Epi : int { kEpiBf16 = 0, kEpiBf16Res = 1, kEpiF32 = 2, kEpiScatter = 3, kEpiScatterRes = 4 };
+// kEpiBf16Sq / kEpiBf16ResSq: the bf16 store plus the sum of squares of the stored (bf16-rounded) values, one fp32
+// partial per (tile, epilogue warp) in sq_part[unit * 4 + warp quadrant] -- the weight gradient's share of the
+// gradient norm without a second pass over it (deterministic: no atomics, fixed slots).
+enum Epi : int {
+  kEpiBf16 = 0, kEpiBf16Res = 1, kEpiF32 = 2, kEpiScatter = 3, kEpiScatterRes = 4, kEpiBf16Sq = 5, kEpiBf16ResSq = 6
+};
 
 __host__ __device__ constexpr bool epi_scatter(int e) { return e == kEpiScatter || e == kEpiScatterRes; }
-__host__ __device__ constexpr bool epi_res(int e) { return e == kEpiBf16Res || e == kEpiScatterRes; }
+__host__ __device__ constexpr bool epi_res(int e) {
+  return e == kEpiBf16Res || e == kEpiScatterRes || e == kEpiBf16ResSq;
+}
+__host__ __device__ constexpr bool epi_sq(int e) { return e == kEpiBf16Sq || e == kEpiBf16ResSq; }
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -56,7 +64,7 @@ template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* Cv,
                         const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, int splits,
-                        float* ws, int* status, const OwnerScatter sc) {
+                        float* ws, int* status, const OwnerScatter sc, float* sq_part) {
   using S = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -197,6 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* wsl = splits > 1 ? ws + static_cast<int64_t>(u % splits) * M * N : nullptr;
       if (!mbar_wait(&tfull[acc], acc_ph, abort_flag, status, 4)) break;
       tc_fence_after();
+      float ss = 0.f;                       // sum of squares of this thread's stored values (epi_sq)
       const int row = mb * BM + q * 32 + lane;
       const uint32_t tb = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll 1
@@ -261,6 +270,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 16; ++j) p[j] = pack_bf16(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
             }
+            if (epi_sq(EPI)) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float2 f = unpack_bf16(p[j]);
+                if (col + 2 * j < N) ss += f.x * f.x;
+                if (col + 2 * j + 1 < N) ss += f.y * f.y;
+              }
+            }
             if (epi_scatter(EPI)) {
               const int64_t x = sc.x0 + static_cast<int64_t>(row) * ldc + col;
               if (col + 32 <= N) {
@@ -298,6 +315,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (epi_sq(EPI) && wsl == nullptr) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) sq_part[static_cast<int64_t>(u) * 4 + q] = ss;
+      }
       acc ^= 1;
       if (acc == 0) acc_ph ^= 1u;
     }
@@ -359,10 +381,42 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, v
   }
 }
 
+// split-K reduction for the bf16 outputs with the sum of squares of the stored values: one partial per block in
+// sq_part[blockIdx.x] (every block writes its slot; no early exit before the block reduction)
+template <bool RES>
+__global__ void splitk_reduce_sq_kernel(const float* __restrict__ ws, int splits, void* Cv, const __nv_bfloat16* R,
+                                        int M, int N, int64_t ldc, int64_t ldr, float* __restrict__ sq_part) {
+  const int64_t i4 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  const int64_t total = static_cast<int64_t>(M) * N;
+  float ss = 0.f;
+  if (i4 < total) {
+    for (int64_t i = i4; i < i4 + 4 && i < total; ++i) {
+      float acc = 0.f;
+      for (int sp = 0; sp < splits; ++sp) acc += ws[sp * total + i];
+      const int64_t row = i / N, col = i % N;
+      const float v = RES ? bf16_round(acc) + __bfloat162float(R[row * ldr + col]) : acc;
+      const __nv_bfloat16 o = __float2bfloat16_rn(v);
+      reinterpret_cast<__nv_bfloat16*>(Cv)[row * ldc + col] = o;
+      const float f = __bfloat162float(o);
+      ss += f * f;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+    sq_part[blockIdx.x] = t;
+  }
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const __nv_bfloat16* R, int M, int N, int K,
             int64_t ldc, int64_t ldr, int splits, float* ws, cudaStream_t stream,
-            const OwnerScatter& sc = OwnerScatter{}) {
+            const OwnerScatter& sc = OwnerScatter{}, float* sq_part = nullptr) {
   using S = GemmSmem<BN, STAGES>;
   auto kern = gemm_tcgen05_kernel<BN, STAGES, A_MN, B_MN, EPI>;
   static bool attr_set = false;
@@ -372,14 +426,24 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const __nv_bf
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * splits;
   const int grid = std::min(tiles, num_sms());
-  kern<<<grid, kThreads, S::TOTAL, stream>>>(ta, tb, C, R, M, N, K, ldc, ldr, splits, ws, status_ptr(), sc);
+  kern<<<grid, kThreads, S::TOTAL, stream>>>(ta, tb, C, R, M, N, K, ldc, ldr, splits, ws, status_ptr(), sc, sq_part);
   check_launch("gemm_tcgen05");
   if (splits > 1) {
     const int64_t total = static_cast<int64_t>(M) * N;
     const int blocks = static_cast<int>((total / 4 + 255) / 256 + 1);
-    splitk_reduce_kernel<EPI><<<blocks, 256, 0, stream>>>(ws, splits, C, R, M, N, ldc, ldr, sc);
+    if constexpr (epi_sq(EPI)) {
+      splitk_reduce_sq_kernel<epi_res(EPI)><<<blocks, 256, 0, stream>>>(ws, splits, C, R, M, N, ldc, ldr, sq_part);
+    } else {
+      splitk_reduce_kernel<EPI><<<blocks, 256, 0, stream>>>(ws, splits, C, R, M, N, ldc, ldr, sc);
+    }
     check_launch("gemm_splitk_reduce");
   }
+}
+
+// partial-sum slots a gemm_sq call writes: one per (tile, epilogue warp), or one per split-K reduction block
+int64_t sq_slots(int M, int N, int bn, int splits) {
+  if (splits > 1) return (static_cast<int64_t>(M) * N / 4 + 255) / 256 + 1;
+  return static_cast<int64_t>((M + BM - 1) / BM) * ((N + bn - 1) / bn) * 4;
 }
 
 template <int BN, int STAGES, int EPI>
@@ -550,6 +614,60 @@ void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
     if (accumulate) launch<128, 6, true, true, kEpiScatterRes>(ta, tb, Cp, Rp, m, n, k, ld, ld, plan.splits, wsp, st, sc);
     else launch<128, 6, true, true, kEpiScatter>(ta, tb, Cp, Rp, m, n, k, ld, ld, plan.splits, wsp, st, sc);
   }
+}
+
+// Weight gradient (both operands MN-major: dW = A^T B) stored as bf16 into C (optionally + C's current contents,
+// the earlier micro-batches) with the sum of squares of the stored values as fp32 partials in sq_part: one per
+// (tile, epilogue warp), or one per split-K reduction block. Returns the number of partials written (the first
+// entries of sq_part; the caller sums them). sq_part must hold at least gemm_sq_slots(...) floats.
+int64_t gemm_sq_slots(int64_t M, int64_t N, int64_t K) {
+  const Plan plan = pick_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
+  return sq_slots(static_cast<int>(M), static_cast<int>(N), plan.bn, plan.splits);
+}
+
+int64_t gemm_sq(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, at::Tensor& sq_part) {
+  FYB_RANGE("fyb::gemm_sq");
+  FYB_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda() && sq_part.is_cuda(), "gemm_sq: CUDA tensors expected");
+  FYB_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16 && C.scalar_type() == at::kBFloat16,
+            "gemm_sq: bf16 tensors expected");
+  FYB_CHECK(sq_part.scalar_type() == at::kFloat && sq_part.is_contiguous(), "gemm_sq: fp32 partials expected");
+  FYB_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1,
+            "gemm_sq: 2-D operands with contiguous rows expected");
+  const int64_t K = A.size(0), M = A.size(1), N = B.size(1);
+  FYB_CHECK(B.size(0) == K && C.size(0) == M && C.size(1) == N && K > 0, "gemm_sq: shape mismatch");
+  FYB_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm_sq: dimension too large");
+  const Plan plan = pick_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
+  const int64_t slots = sq_slots(static_cast<int>(M), static_cast<int>(N), plan.bn, plan.splits);
+  FYB_CHECK(sq_part.numel() >= slots, "gemm_sq: partials buffer too small");
+  if (M == 0 || N == 0) return 0;
+  c10::cuda::CUDAGuard guard(A.device());
+  cudaStream_t st = cur_stream();
+  FYB_CUDA(cudaMemsetAsync(sq_part.data_ptr(), 0, slots * sizeof(float), st));
+  at::Tensor ws;
+  float* wsp = nullptr;
+  if (plan.splits > 1) {
+    ws = at::empty({plan.splits, M, N}, A.options().dtype(at::kFloat));
+    wsp = ws.data_ptr<float>();
+  }
+  const CUtensorMap ta = make_tmap_2d(A.data_ptr(), K, M, A.stride(0), 64);
+  const CUtensorMap tb = make_tmap_2d(B.data_ptr(), K, N, B.stride(0), 64);
+  void* Cp = C.data_ptr();
+  const __nv_bfloat16* Rp = accumulate ? reinterpret_cast<const __nv_bfloat16*>(Cp) : nullptr;
+  const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
+  const int64_t ldc = C.stride(0);
+  float* sp = sq_part.data_ptr<float>();
+  if (plan.bn == 256) {
+    if (accumulate) launch<256, 4, true, true, kEpiBf16ResSq>(ta, tb, Cp, Rp, m, n, k, ldc, ldc, plan.splits, wsp, st,
+                                                              OwnerScatter{}, sp);
+    else launch<256, 4, true, true, kEpiBf16Sq>(ta, tb, Cp, Rp, m, n, k, ldc, ldc, plan.splits, wsp, st,
+                                                OwnerScatter{}, sp);
+  } else {
+    if (accumulate) launch<128, 6, true, true, kEpiBf16ResSq>(ta, tb, Cp, Rp, m, n, k, ldc, ldc, plan.splits, wsp, st,
+                                                              OwnerScatter{}, sp);
+    else launch<128, 6, true, true, kEpiBf16Sq>(ta, tb, Cp, Rp, m, n, k, ldc, ldc, plan.splits, wsp, st,
+                                                OwnerScatter{}, sp);
+  }
+  return slots;
 }
 
 FYB_BOUNDS_BINDER(bind_bounds_gemm)

@@ -71,6 +71,12 @@ def wgrad_into(w: torch.Tensor, dy: torch.Tensor, x: torch.Tensor) -> bool:
         if bases is not None:
             _C().gemm_scatter(dy, x, slot, acc, fp.grad_flat, bases, fp.seg, fp.rank, fp.chunk)
             return True
+    if fp.sq_mode:
+        part = fp.sq_partials(w)
+        if part is not None:
+            # the GEMM also writes the sum of squares of the stored gradient (one-GPU gradient norm, no extra pass)
+            fp.sq_used += int(_C().gemm_sq(dy, x, slot, acc, part))
+            return True
     gemm(dy, x, a_mn_major=True, b_mn_major=True, out=slot, residual=slot if acc else None)
     return True
 

@@ -144,6 +144,12 @@ class FlatParams:
         self.scatter_now = True            # the current micro-batch is the update's last one
         self._scattered = set()
         self._sparse = set()               # scattered by row (only the rows of tokens in the batch)
+        # one-GPU gradient norm from the weight-gradient GEMMs (enable_grad_sq): the GEMMs of the update's last
+        # micro-batch write sum-of-squares partials of their bf16 output, so only the other gradients need a pass
+        self.sq_mode = False
+        self.sq_buf = None
+        self.sq_used = 0
+        self._sq_covered = set()
 
     # ---------------------------------------------------------------------------------------------------------
     def owner_of(self, x: int) -> int:
@@ -234,6 +240,28 @@ class FlatParams:
     def scattered(self) -> frozenset:
         return frozenset(self._scattered)
 
+    def enable_grad_sq(self, slots: int = 1 << 21):
+        self.sq_mode = True
+        self.sq_buf = torch.zeros(slots, dtype=torch.float32, device=self.device)
+
+    def sq_partials(self, p) -> Optional[torch.Tensor]:
+        """The free part of the partials buffer when p's weight-gradient GEMM should produce its sum of squares
+        (sum-of-squares mode, last micro-batch, no owner scatter), else None. Marks p as covered."""
+        if not self.sq_mode or not self.scatter_now or self.scatter is not None:
+            return None
+        self._sq_covered.add(id(p))
+        return self.sq_buf[self.sq_used:]
+
+    def grad_sq_total(self) -> torch.Tensor:
+        """Sum of squares of the whole (bf16) gradient buffer: the GEMM partials of this update plus one pass over
+        every gradient no GEMM covered (device tensor [1])."""
+        from .. import ops
+        parts = [self.sq_buf[:self.sq_used].sum().reshape(1)] if self.sq_used else []
+        for e in self.entries:
+            if id(e.param) not in self._sq_covered:
+                parts.append(ops._C().sq_norm(self.grad_flat[e.offset:e.offset + e.numel]))
+        return torch.stack(parts).sum().reshape(1)
+
     def sparse(self) -> frozenset:
         return frozenset(self._sparse)
 
@@ -242,6 +270,8 @@ class FlatParams:
         self._written.clear()
         self._scattered.clear()
         self._sparse.clear()
+        self._sq_covered.clear()
+        self.sq_used = 0
 
     def begin_microbatch(self, first: bool, last: bool = True):
         """Gradient accumulation needs no flag: a slot written by an earlier micro-batch of this update is
@@ -395,6 +425,8 @@ class ZeroOptimizer:
         native = ops.native_on(g16)
         if sq is not None:
             sq = sq.clone()
+        elif native and fp.sq_mode and fp.world == 1 and self.replicas == 1 and self.tp_group is None:
+            sq = fp.grad_sq_total()
         elif native:
             sq = ops._C().sq_norm(g16.reshape(-1))
         else:

@@ -82,6 +82,11 @@ class Trainer:
                                partition=partition, chunk=chunk)
         self.flat.direct_grads = self.device.type == "cuda" and ops.get_backend() == "native"
         self.zero = ZeroOptimizer(self.flat, optim_cfg, comm=comm, group=group, replicas=replicas)
+        import os as _os0
+        if (_os0.environ.get("FYB_GEMM_SQ", "0") == "1" and self.world == 1 and self.flat.direct_grads
+                and TP.tp_size() == 1):
+            # one GPU: the gradient norm from the weight-gradient GEMMs' epilogues (no second pass over 6.9 GB)
+            self.flat.enable_grad_sq()
         if self.tp > 1:
             self.zero.set_tensor_parallel(TP.tp_group(), TP.tp_rank(), TP.is_sharded)
         self.zero.p2p = p2p
