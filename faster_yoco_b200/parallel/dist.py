@@ -21,6 +21,16 @@ def env_local_rank() -> int:
     return int(os.environ.get("LOCAL_RANK", "0"))
 
 
+def single_node(group=None) -> bool:
+    """True when every rank of `group` (default: all) runs on this node: torch.distributed.run's LOCAL_WORLD_SIZE
+    covers the whole group. Peer-memory (CUDA IPC) collectives need it; without the variable one node is assumed."""
+    local = os.environ.get("LOCAL_WORLD_SIZE")
+    if local is None:
+        return True
+    size = dist.get_world_size(group) if dist.is_initialized() else env_world()
+    return int(local) >= size and int(local) >= env_world()
+
+
 def init(backend: Optional[str] = None, timeout_s: float = 600.0) -> int:
     """Initialise the default process group if WORLD_SIZE > 1; returns this rank's CUDA device index (or -1)."""
     dev = -1

@@ -72,6 +72,11 @@ class Trainer:
         if zero_sharding == "none":
             # fairseq's plain data parallelism: every rank keeps all optimizer state; gradients all-reduced
             replicas, comm, overlap = self.world, "nccl", False
+        if comm == "fused" and self.world > 1 and not D.single_node(group):
+            # CUDA IPC peer mappings exist only between the GPUs of one node: across nodes the NCCL path runs
+            comm, overlap = "nccl", False
+            if transport == "gemm":
+                transport = "sm"
         p2p = None
         if comm == "fused" and self.world > 1 and self.device.type == "cuda":
             from ..parallel.p2p import PeerComm

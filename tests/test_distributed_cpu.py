@@ -73,3 +73,14 @@ def test_tensor_x_data_parallel_training_matches_single_process(tmp_path):
         assert set(got) == set(want)
         for k, v in want.items():
             assert torch.allclose(got[k].float(), v.float(), atol=2e-5, rtol=1e-4), k
+
+
+def test_single_node_detection(monkeypatch):
+    from faster_yoco_b200.parallel import dist as D
+    monkeypatch.delenv("LOCAL_WORLD_SIZE", raising=False)
+    assert D.single_node()
+    monkeypatch.setenv("WORLD_SIZE", "16")
+    monkeypatch.setenv("LOCAL_WORLD_SIZE", "8")
+    assert not D.single_node()
+    monkeypatch.setenv("LOCAL_WORLD_SIZE", "16")
+    assert D.single_node()
