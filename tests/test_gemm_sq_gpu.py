@@ -59,3 +59,22 @@ def test_one_gpu_training_norm_from_gemm_partials(graph):
         assert abs(a - b) <= 1e-4 * abs(a), runs
     for a, b in zip(runs["pass"][0], runs["gemm"][0]):
         assert abs(a - b) <= 2e-4 * abs(a), runs
+
+
+def test_adam_eight_wide_matches_adam():
+    """FYB_ADAM8: the one-segment Adam through the 8-wide (Adam + push, no peers) kernel gives the same parameters."""
+    from faster_yoco_b200.utils import dist_checks
+    ops.set_backend("native")
+    dev = torch.device("cuda", 0)
+    out = {}
+    for wide in (False, True):
+        model, tr = dist_checks._tiny_trainer(dev, arch="yoco_small", dtype=torch.bfloat16, overlap=False)
+        tr.zero.adam8 = wide
+        for ids in dist_checks._batches(0, 1, 2, seq=256, vocab=8192):
+            b = {"src_tokens": ids[0, :, :-1].contiguous(), "target": ids[0, :, 1:].contiguous(),
+                 "ntokens": ids.shape[1] * (ids.shape[2] - 1), "nsentences": ids.shape[1]}
+            tr.train_step(b)
+        torch.cuda.synchronize()
+        out[wide] = (tr.zero.master.clone(), tr.flat.flat.clone())
+    # identical expression per element; only the attention dQ atomics' order differs between runs
+    assert torch.allclose(out[False][0], out[True][0], rtol=1e-3, atol=1e-5)
