@@ -281,3 +281,17 @@ def test_reference_recipe_command_lines_parse():
                   "--max-epoch", "1", "--no-save", "--tiktoken-model", "cl100k_base", "--bf16", "--arch", "yoco_3b_new",
                   "--load-ckpt", "c/c.pth", "--yoco-model", "c", "--tokens-per-sample", "1048576", "--interval",
                   "1048576"])
+
+
+def test_every_module_imports():
+    """Every module of the package (tools that only run on GPU boxes included) imports on a CPU machine."""
+    import importlib
+    import pkgutil
+    import faster_yoco_b200
+    failed = []
+    for m in pkgutil.walk_packages(faster_yoco_b200.__path__, "faster_yoco_b200."):
+        try:
+            importlib.import_module(m.name)
+        except Exception as e:          # pragma: no cover - the assertion below reports it
+            failed.append((m.name, repr(e)))
+    assert not failed, failed
