@@ -60,7 +60,7 @@ def parse():
     p.add_argument("--count-launches", type=int, default=1)
     p.add_argument("--exposed-comm", type=int, default=0,
                    help="after the measurements, time the same updates without any cross-rank exchange and report "
-                        "exposed_comm_ms = ms_per_step - that (serial schedule only; N > 1)")
+                        "exposed_comm_ms = ms_per_step - that (N > 1)")
     return p.parse_args()
 
 

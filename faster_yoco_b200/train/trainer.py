@@ -183,18 +183,16 @@ class Trainer:
         all-gather, statistics or grad-norm all-reduce; weight gradients stay local), so that the step time of the
         same work minus its communication can be timed and the exposed communication derived. Ranks' parameters
         diverge: use it after the real measurements. Drops the captured graph (the update is captured again)."""
-        if self.overlap:
-            raise ValueError("measure_without_exchange runs the serial schedule (overlap off)")
         self.release_graph()
         self.zero.skip_exchange = on
         if on:
-            self._scatter_saved = self.flat.scatter
+            self._saved_modes = (self.flat.scatter, self.check_consistency, self.overlap)
             self.flat.scatter = None
-            self._consistency_saved = self.check_consistency
             self.check_consistency = False
-        else:
-            self.flat.scatter = getattr(self, "_scatter_saved", self.flat.scatter)
-            self.check_consistency = getattr(self, "_consistency_saved", self.check_consistency)
+            self.overlap = False             # no per-bucket pushes or waits either
+        elif getattr(self, "_saved_modes", None) is not None:
+            self.flat.scatter, self.check_consistency, self.overlap = self._saved_modes
+            self._saved_modes = None
 
     def _reduce_stats(self, loss_sum, sample_size):
         stats = torch.stack([loss_sum.float().reshape(()), sample_size.float().reshape(())])
