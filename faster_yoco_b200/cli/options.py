@@ -44,7 +44,7 @@ def add_common(p: argparse.ArgumentParser):
               "n-kv-heads"):
         g.add_argument(f"--{k}", type=int, default=None)
     g.add_argument("--init-std", type=float, default=None, help="N(0, std) for every weight (benchmark init)")
-    g.add_argument("--log-format", default="simple")
+    g.add_argument("--log-format", default="simple", choices=["simple", "json", "tqdm", "none"])
     g.add_argument("--log-interval", type=int, default=10)
     g.add_argument("--kernels", default="native", choices=["native", "torch"])
     # data

@@ -183,8 +183,9 @@ def main(argv=None) -> int:
             stats["num_updates"] = nu
             stats["lr"] = trainer.sched.lr_for(nu)
             stats["train_wall"] = round(time.perf_counter() - t_start, 1)
-            if rank == 0:
-                print(format_log(stats), flush=True)
+            line = format_log(stats, fmt=args.log_format)
+            if rank == 0 and line:
+                print(line, flush=True)
         if (not args.disable_validation and args.validate_interval_updates > 0
                 and nu % args.validate_interval_updates == 0):
             v = validate_lm(model, task, args, device, rank, world, rep, cp, tp)

@@ -49,7 +49,14 @@ class DeviceMeters:
         }
 
 
-def format_log(stats: Dict[str, float], epoch: int = 1) -> str:
-    """fairseq ``--log-format simple`` style line."""
+def format_log(stats: Dict[str, float], epoch: int = 1, fmt: str = "simple") -> str:
+    """One training log line in fairseq's ``--log-format``: ``simple`` (``epoch 001: loss 3.1 | ...``, also used
+    for ``tqdm``), ``json`` (one JSON object per line) or ``none`` (empty: nothing to print)."""
+    if fmt == "none":
+        return ""
+    if fmt == "json":
+        import json
+        return json.dumps(dict({"epoch": epoch}, **{k: (round(v, 4) if isinstance(v, float) else v)
+                                                   for k, v in stats.items()}))
     body = " | ".join(f"{k} {v}" for k, v in stats.items())
     return f"epoch {epoch:03d}: {body}"

@@ -295,3 +295,11 @@ def test_every_module_imports():
         except Exception as e:          # pragma: no cover - the assertion below reports it
             failed.append((m.name, repr(e)))
     assert not failed, failed
+
+
+def test_log_formats():
+    from faster_yoco_b200.train.metrics import format_log
+    st = {"loss": 3.14159, "num_updates": 10}
+    assert format_log(st).startswith("epoch 001: loss 3.14159 | num_updates 10")
+    assert json.loads(format_log(st, fmt="json")) == {"epoch": 1, "loss": 3.1416, "num_updates": 10}
+    assert format_log(st, fmt="none") == "" and format_log(st, fmt="tqdm") == format_log(st)
