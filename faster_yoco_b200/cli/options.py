@@ -57,7 +57,9 @@ def add_common(p: argparse.ArgumentParser):
     g.add_argument("--needle-num", type=int, default=4)
     g.add_argument("--interval", type=int, default=1024)
     g.add_argument("--needle-file-path", default=None)
-    g.add_argument("--max-len-b", type=int, default=5)
+    g.add_argument("--max-len-b", type=int, default=5,
+                   help="accepted as in the reference's needle criterion config, which never reads it either: the "
+                        "needle criterions generate 20 tokens")
     return p
 
 
