@@ -31,7 +31,8 @@ def test_zero_ws2_matches_single_process(tmp_path, partition, chunk, sharding):
 
 
 @pytest.mark.parametrize("partition,resume_partition", [("even", "even"), ("cyclic", "cyclic"),
-                                                        ("cyclic", "even")])
+                                                        ("cyclic", "even"), ("greedy", "cyclic"),
+                                                        ("even", "greedy")])
 def test_checkpoint_resume_matches_uninterrupted(tmp_path, partition, resume_partition):
     run_ranks(dist_checks.checkpoint_resume, 2, str(tmp_path), 4, 2, partition, 1024, resume_partition)
     r = torch.load(os.path.join(tmp_path, "resume.pt"))
