@@ -1,7 +1,7 @@
 """Per-kernel microbenchmarks: the sm_100a kernels against the library baselines (cuBLAS, flash-attn) on the
 YOCO-3B shapes, timed with CUDA events after warm-up, inputs rotated through a pool larger than L2.
 
-    python -m faster_yoco_b200.utils.kernel_bench [--only gemm|attn|ret]
+    python -m faster_yoco_b200.utils.kernel_bench [--only gemm|attn|ret] [--pair 1]
 """
 from __future__ import annotations
 
@@ -45,7 +45,8 @@ def gemm_shapes():
     return out
 
 
-def bench_gemm(results):
+def bench_gemm(results, pair_too: bool = False):
+    """pair_too: also time the CTA-pair kernel (gemm2.cu) on every shape."""
     from faster_yoco_b200 import ops
     dev = torch.device("cuda")
     for name, M, N, K, a_mn, b_mn in gemm_shapes():
@@ -62,6 +63,11 @@ def bench_gemm(results):
             it[0] += 1
             ops._C().gemm(a, b, c, a_mn, b_mn, None)
 
+        def pair():
+            a, b = pool[it[0] % len(pool)]
+            it[0] += 1
+            ops._C().gemm_pair(a, b, c, a_mn, b_mn, None)
+
         def cublas():
             a, b = pool[it[0] % len(pool)]
             it[0] += 1
@@ -71,8 +77,12 @@ def bench_gemm(results):
 
         t_ours, t_cub = _time(ours), _time(cublas)
         fl = 2.0 * M * N * K
-        results.append({"kernel": "gemm", "shape": name, "M": M, "N": N, "K": K, "ours_ms": t_ours,
-                        "cublas_ms": t_cub, "ours_tflops": fl / t_ours / 1e9, "cublas_tflops": fl / t_cub / 1e9})
+        r = {"kernel": "gemm", "shape": name, "M": M, "N": N, "K": K, "ours_ms": t_ours, "cublas_ms": t_cub,
+             "ours_tflops": fl / t_ours / 1e9, "cublas_tflops": fl / t_cub / 1e9}
+        if pair_too:
+            t_pair = _time(pair)
+            r.update(pair_ms=t_pair, pair_tflops=fl / t_pair / 1e9)
+        results.append(r)
 
 
 def bench_attention(results, L=2048, Hq=24, Hk=8, B=1):
@@ -123,10 +133,11 @@ def bench_retention(results, L=2048, H=24, B=1):
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("--only", default=None)
+    p.add_argument("--pair", type=int, default=0, help="GEMMs: also time the CTA-pair kernel")
     a = p.parse_args()
     res = []
     if a.only in (None, "gemm"):
-        bench_gemm(res)
+        bench_gemm(res, pair_too=bool(a.pair))
     if a.only in (None, "attn"):
         bench_attention(res)
     if a.only in (None, "ret"):
