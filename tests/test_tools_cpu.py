@@ -303,3 +303,16 @@ def test_log_formats():
     assert format_log(st).startswith("epoch 001: loss 3.14159 | num_updates 10")
     assert json.loads(format_log(st, fmt="json")) == {"epoch": 1, "loss": 3.1416, "num_updates": 10}
     assert format_log(st, fmt="none") == "" and format_log(st, fmt="tqdm") == format_log(st)
+
+
+def test_every_preset_parses():
+    """Each switch set in presets/ applies to the train parser with values its choices accept."""
+    import glob
+    from faster_yoco_b200.cli.options import parse_with_preset, train_parser
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    names = sorted(os.path.splitext(os.path.basename(f))[0]
+                   for f in glob.glob(os.path.join(root, "faster_yoco_b200", "presets", "*.json")))
+    assert "b200_gemm_scatter" in names and len(names) >= 5
+    for n in names:
+        a = parse_with_preset(train_parser(), ["--preset", n, "DATA"])
+        assert a.comm in ("fused", "nccl") and a.partition in ("even", "greedy", "cyclic"), n
