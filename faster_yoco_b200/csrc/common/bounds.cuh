@@ -19,10 +19,12 @@ namespace fyb {
 // status_ptr() allocates the word
 static __device__ int* g_bounds_status = nullptr;
 
-__device__ __forceinline__ bool bounds_ok(int64_t i, int64_t n, int site) {
+__host__ __device__ __forceinline__ bool bounds_ok(int64_t i, int64_t n, int site) {
   if (i >= 0 && i < n) return true;
+#ifdef __CUDA_ARCH__
   int* s = g_bounds_status;
   if (s != nullptr && atomicCAS(s, 0, (kBounds << 16) | (site & 0xffff)) == 0) s[1] = static_cast<int>(i);
+#endif
   return false;
 }
 

@@ -54,7 +54,7 @@ struct OwnerScatter {
 };
 
 // (nullptr when a debug build's bounds check fails: the caller skips the store)
-__device__ __forceinline__ __nv_bfloat16* owner_dst(const OwnerScatter& s, int64_t x) {
+__host__ __device__ __forceinline__ __nv_bfloat16* owner_dst(const OwnerScatter& s, int64_t x) {
   if (!FYB_IN_BOUNDS(x, static_cast<int64_t>(s.world) * s.seg, 520)) return nullptr;
   const int o = zero_owner(s.chunk, s.world, s.seg, x);
   if (o == s.rank) return s.own + x;
