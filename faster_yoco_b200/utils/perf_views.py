@@ -99,6 +99,11 @@ def render(data_dir: str, out_dir: str) -> List[str]:
         tb = json.load(open(p))
         written.append(_write(out_dir, "time-budget.svg",
                               stacked([(n, float(v)) for n, v in tb["phases"]], tb.get("title", "time budget"))))
+    p = os.path.join(data_dir, "exchange.json")
+    if os.path.exists(p):
+        ex = json.load(open(p))
+        written.append(_write(out_dir, "exchange.svg",
+                              bars([(n, float(v)) for n, v in ex["bars"]], ex.get("title", "exchange"), "GB/s")))
     p = os.path.join(data_dir, "validation.json")
     if os.path.exists(p):
         v = json.load(open(p))
