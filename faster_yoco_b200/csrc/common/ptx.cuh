@@ -84,7 +84,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // ------------------------------------------------------------------------------------------------------------------
-// TMA tensor loads -- never multicast in this project (each CTA loads its own tiles)
+// TMA tensor loads: each CTA loads its own tiles from this GPU's memory
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -10,7 +10,7 @@
 //   warp 1      : TMEM allocator + UMMA issuer (one lane): 4 x tcgen05.mma (M=128, N=BN, K=16) per stage
 //   warps 2..5  : epilogue -- tcgen05.ld of the fp32 accumulator, bf16 convert (+ residual), global store
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of tile i overlaps the MMAs of i+1.
-// No TMA multicast anywhere (this kernel also runs on operands that other ranks wrote).
+// Each CTA loads its own tiles with plain TMA loads of this GPU's memory (this kernel also runs on operands that other ranks wrote).
 #include <ATen/ATen.h>
 #include <c10/util/Optional.h>
 

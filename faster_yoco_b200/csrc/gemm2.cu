@@ -14,7 +14,7 @@
 //                 commits: stage release to both CTAs' empty barriers, accumulator ready to both CTAs' tfull barriers
 //                 (one commit per CTA, addressed through mapa)
 //   warps 2..5  : epilogue on each CTA's own TMEM rows; the peer's warps arrive on the leader's tempty barrier
-// Loads are plain cp.async.bulk.tensor of this GPU's memory in the .cta_group::2 form; nothing is multicast.
+// Loads are plain cp.async.bulk.tensor of this GPU's memory in the .cta_group::2 form; each CTA loads its own tiles.
 // Every wait is bounded (2 s) and records a status word; both CTAs always reach the final cluster barrier.
 #include <ATen/ATen.h>
 #include <c10/util/Optional.h>

@@ -17,6 +17,7 @@
 //   * The first call on a device, with that device current, looks up the array's device address
 //     (cudaGetSymbolAddress) and caches it; make that first call before any stream capture.
 //   * It calls no cudaMalloc, cudaFree or other allocating routine.
+//   * A CUDA error that earlier work left pending is not consumed: the call returns code 7 without launching.
 #pragma once
 
 #include <cuda_runtime.h>

@@ -547,6 +547,8 @@ extern "C" int fyb_rms_norm_bwd_noalloc(const void* dy, const void* x, const voi
     if (p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 != 0) return 3;
   if (w != nullptr && reinterpret_cast<uintptr_t>(w) % 16 != 0) return 3;
   if (rstd == nullptr && M > 0) return 3;
+  // an error left pending by the caller's earlier work is reported as such (code 7), not taken for our launch's
+  if (cudaPeekAtLastError() != cudaSuccess) return 7;
   float* part = nullptr;
   if (w != nullptr) {
     const int rc = noalloc_scratch(&part);
@@ -582,6 +584,7 @@ extern "C" const char* fyb_noalloc_strerror(int code) {
     case 4: return "cudaGetSymbolAddress of the static scratch array failed";
     case 5: return "no valid current CUDA device";
     case 6: return "kernel launch failed";
+    case 7: return "a CUDA error from earlier work was already pending on entry (left pending, nothing launched)";
     default: return "unknown error code";
   }
 }

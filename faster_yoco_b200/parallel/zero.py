@@ -150,6 +150,7 @@ class FlatParams:
         self.sq_buf = None
         self.sq_used = 0
         self._sq_covered = set()
+        self._sq_region = {}               # id(p) -> (start, end) of p's partials in sq_buf this update
 
     # ---------------------------------------------------------------------------------------------------------
     def owner_of(self, x: int) -> int:
@@ -219,6 +220,14 @@ class FlatParams:
                                "producer (tied weights): the GEMM-fused reduce-scatter cannot accumulate it")
         acc = self.accumulate or id(p) in self._written
         self._written.add(id(p))
+        if id(p) in self._sq_covered:
+            # a second gradient producer of one weight (tied weights: the output projection's GEMM, then the
+            # embedding backward): the first GEMM's sum-of-squares partials no longer describe the slot, so they are
+            # cleared and the slot is counted by the pass over uncovered gradients instead
+            self._sq_covered.discard(id(p))
+            a, b = self._sq_region.pop(id(p), (0, 0))
+            if b > a:
+                self.sq_buf[a:b].zero_()
         return self.grad_view(p), acc
 
     def scatter_target(self, p):
@@ -252,6 +261,11 @@ class FlatParams:
         self._sq_covered.add(id(p))
         return self.sq_buf[self.sq_used:]
 
+    def sq_commit(self, p, count: int):
+        """Record that p's GEMM wrote `count` partials at the free part of sq_buf."""
+        self._sq_region[id(p)] = (self.sq_used, self.sq_used + count)
+        self.sq_used += count
+
     def grad_sq_total(self) -> torch.Tensor:
         """Sum of squares of the whole (bf16) gradient buffer: the GEMM partials of this update plus one pass over
         every gradient no GEMM covered (device tensor [1])."""
@@ -271,6 +285,7 @@ class FlatParams:
         self._scattered.clear()
         self._sparse.clear()
         self._sq_covered.clear()
+        self._sq_region.clear()
         self.sq_used = 0
 
     def begin_microbatch(self, first: bool, last: bool = True):

@@ -8,12 +8,12 @@ import torch.distributed as dist
 
 
 def _tiny_trainer(device, comm="nccl", seed=0, graph=False, arch="yoco_tiny", dtype=torch.float32, overlap=True,
-                  transport="sm", partition="even", chunk=None, zero_sharding="os"):
+                  transport="sm", partition="even", chunk=None, zero_sharding="os", **arch_overrides):
     from ..config import OptimConfig, build_args
     from ..models.yoco import YOCO
     from ..train.trainer import Trainer
     torch.manual_seed(seed)
-    args = build_args(arch, max_seq_len=256, init_std=0.02)
+    args = build_args(arch, max_seq_len=256, init_std=0.02, **arch_overrides)
     model = YOCO(args).to(device=device, dtype=dtype)
     cfg = OptimConfig(lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1, warmup_updates=0, total_num_update=20)
     return model, Trainer(model, cfg, device=device, comm=comm, graph_step=graph, overlap=overlap,

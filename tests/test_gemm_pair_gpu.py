@@ -1,15 +1,12 @@
 """The CTA-pair GEMM (tcgen05.mma.cta_group::2, 256 x 256 tiles over two CTAs, gemm2.cu) against the one-CTA GEMM
 and an fp32 PyTorch oracle: every operand layout (forward, input gradient, weight gradient), M / N / K tails, the
-residual epilogue and fp32 output, two calls in a row.
-
-Marked ``gpu_pending``: this kernel has not yet run on a GPU, so ``-m gpu`` does not select it; run it with
-``-m gpu_pending``."""
+residual epilogue and fp32 output, two calls in a row."""
 import pytest
 import torch
 
 from faster_yoco_b200 import ops
 
-pytestmark = pytest.mark.gpu_pending
+pytestmark = pytest.mark.gpu
 
 
 def _operands(M, N, K, a_mn, b_mn, g):
@@ -17,6 +14,15 @@ def _operands(M, N, K, a_mn, b_mn, g):
     a = torch.randn((K, M) if a_mn else (M, K), generator=g, device=dev).to(torch.bfloat16)
     b = torch.randn((K, N) if b_mn else (N, K), generator=g, device=dev).to(torch.bfloat16)
     return a, b
+
+
+def _close_in_ulps(x, y, ulps):
+    """|x - y| within `ulps` bf16 units in the last place of the larger magnitude (plus a small absolute floor)."""
+    mag = torch.maximum(x.abs(), y.abs()).clamp_min(1e-30)
+    ulp = torch.exp2(torch.floor(torch.log2(mag)) - 7)        # bf16: 8 significant bits
+    tol = ulps * ulp + 2e-2 if ulps else 1e-2 + 1e-3 * mag
+    bad = (x - y).abs() > tol
+    assert not bool(bad.any()), (int(bad.sum()), float((x - y).abs().max()))
 
 
 @pytest.mark.parametrize("M,N,K,a_mn,b_mn", [
@@ -42,8 +48,9 @@ def test_gemm_pair_matches_one_cta_and_fp32(M, N, K, a_mn, b_mn, epi):
         torch.cuda.synchronize()
         assert int(C.status()[0].item()) == 0
         assert not bool(torch.isnan(pair.float()).any()), "unwritten output"
-        # same per-element K order in both kernels: equal up to the tensor cores' accumulation rounding
-        torch.testing.assert_close(pair.float(), one.float(), atol=2e-2, rtol=1e-2)
+        # same per-element K order in both kernels: equal up to the tensor cores' accumulation rounding, which can
+        # move a bf16 output by one unit in the last place (two with the residual epilogue's second rounding)
+        _close_in_ulps(pair.float(), one.float(), 2 if dt == torch.bfloat16 else 0)
     A32 = (a.float().t() if a_mn else a.float())
     B32 = (b.float() if b_mn else b.float().t())
     ref = A32 @ B32

@@ -1,9 +1,6 @@
 """GEMM-fused ZeRO reduce-scatter on the GPU: the weight-gradient GEMM whose epilogue stores every element at its
 owner, against the plain GEMM + the host-side oracle of where each element goes (one GPU, four ranks' staging
-buffers emulated in local memory: the kernel only sees addresses), and 2-GPU training against the serial exchange.
-
-Marked ``gpu_pending``: this path has not yet run on a GPU, so ``-m gpu`` does not select it; run it with
-``-m gpu_pending``."""
+buffers emulated in local memory: the kernel only sees addresses), and 2-GPU training against the serial exchange."""
 import math
 import os
 
@@ -13,7 +10,7 @@ import torch
 from faster_yoco_b200 import ops
 from faster_yoco_b200.ops import reference as ref
 
-pytestmark = pytest.mark.gpu_pending
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("chunk", [0, 1024])

@@ -1,15 +1,12 @@
 """Weight-gradient GEMM with the sum of squares of its stored bf16 output (the one-GPU gradient norm without a
 second pass over the gradient buffer): against the plain GEMM and a PyTorch sum of squares, and one-GPU training
-with and without it.
-
-Marked ``gpu_pending``: this path has not yet run on a GPU, so ``-m gpu`` does not select it; run it with
-``-m gpu_pending``."""
+with and without it."""
 import pytest
 import torch
 
 from faster_yoco_b200 import ops
 
-pytestmark = pytest.mark.gpu_pending
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("M,N,T", [(3072, 3072, 2048), (24, 3072, 2048), (12312, 3072, 2048), (200, 96, 256)])
@@ -36,15 +33,17 @@ def test_gemm_sq_output_and_partials(M, N, T, acc):
         assert bool((part[n:] == 7.0).all())                 # nothing written past the reported slots
 
 
-@pytest.mark.parametrize("graph", [False, True])
-def test_one_gpu_training_norm_from_gemm_partials(graph):
+@pytest.mark.parametrize("graph,tied", [(False, False), (True, False), (False, True)])
+def test_one_gpu_training_norm_from_gemm_partials(graph, tied):
+    """tied: the output projection shares the embedding weight, so one slot has two gradient producers (the
+    output projection's GEMM, then the embedding backward); the GEMM's partials must then not be counted."""
     from faster_yoco_b200.utils import dist_checks
     ops.set_backend("native")
     dev = torch.device("cuda", 0)
     runs = {}
     for mode in ("pass", "gemm"):
         model, tr = dist_checks._tiny_trainer(dev, arch="yoco_small", dtype=torch.bfloat16, graph=graph,
-                                              overlap=False)
+                                              overlap=False, share_input_output_embed=tied)
         if mode == "gemm":
             tr.flat.enable_grad_sq()
         norms, losses = [], []

@@ -245,7 +245,10 @@ def test_bench_result_line_contract(monkeypatch):
         assert isinstance(line[k], t), k
     assert line["warmup"] >= 3 and line["steps"] == 7 and line["n_gpus"] == 8 and line["scaling"] == "weak"
     assert abs(line["value"] - 8 * 2048 / 0.070) < 1e-6 * line["value"]
-    assert abs(line["vs_baseline"] - line["value"] / 138983.0) < 1e-9
+    assert abs(line["vs_baseline"] - line["value"] / 138983.0) < 1e-9      # N = 8: whole job vs whole job
+    one = bench.result_line(args, 1, 70.0, clocks, e2e, 8000)             # N = 1: per GPU vs per GPU
+    assert abs(one["vs_baseline"] - one["value"] / (138983.0 / 8)) < 1e-9
+    assert one["config"]["comm"] == "none" and one["config"]["transport"] is None
     for k in ("model", "global_batch", "seq_len", "parallelism", "l2"):
         assert k in line["config"], k
     assert line["config"]["model"] == "yoco_3b" and line["config"]["global_batch"] == 8
