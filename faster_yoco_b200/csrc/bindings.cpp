@@ -25,7 +25,7 @@ std::vector<at::Tensor> subln_swiglu_bwd(const at::Tensor& dout, const at::Tenso
 at::Tensor swiglu_fwd(const at::Tensor& x, const at::Tensor& y);
 std::vector<at::Tensor> swiglu_bwd(const at::Tensor& x, const at::Tensor& y, const at::Tensor& g,
                                    const c10::optional<at::Tensor>& dx_out, const c10::optional<at::Tensor>& dy_out);
-at::Tensor gate_cumsum_fwd(const at::Tensor& y, int64_t B, int64_t L, double normalizer);
+at::Tensor gate_cumsum_fwd(const at::Tensor& y, int64_t B, int64_t L, double normalizer, bool chunk_local);
 void gate_cumsum_bwd(const at::Tensor& dg, const at::Tensor& y, at::Tensor& dy, double normalizer);
 at::Tensor rope_fwd(const at::Tensor& x, const at::Tensor& cos_t, const at::Tensor& sin_t, bool conj, bool neox);
 at::Tensor embedding_fwd(const at::Tensor& tok, const at::Tensor& w, double scale);
@@ -50,6 +50,23 @@ std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& 
                                       const c10::optional<at::Tensor>& rope_cos,
                                       const c10::optional<at::Tensor>& rope_sin, bool rope_q, bool rope_k);
 at::Tensor retention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& gcum);
+at::Tensor retention_chunk_cumsum(const at::Tensor& g);
+std::vector<at::Tensor> retention_chunk_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                            const at::Tensor& gloc, const c10::optional<at::Tensor>& state_in,
+                                            bool want_state);
+at::Tensor retention_chunk_state(const at::Tensor& k, const at::Tensor& v, const at::Tensor& gloc,
+                                 const c10::optional<at::Tensor>& state_in);
+std::vector<at::Tensor> retention_chunk_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                            const at::Tensor& v, const at::Tensor& gloc, const at::Tensor& states,
+                                            const c10::optional<at::Tensor>& dstate_out, bool want_dstate_in,
+                                            bool has_state_in, const c10::optional<at::Tensor>& dq_out,
+                                            const c10::optional<at::Tensor>& dk_out,
+                                            const c10::optional<at::Tensor>& dv_out,
+                                            const c10::optional<at::Tensor>& rope_cos,
+                                            const c10::optional<at::Tensor>& rope_sin,
+                                            const c10::optional<at::Tensor>& o);
+at::Tensor retention_decode(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
+                            at::Tensor& state);
 std::vector<at::Tensor> retention_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                       const at::Tensor& v, const at::Tensor& gcum, const at::Tensor& o,
                                       const c10::optional<at::Tensor>& dq_out, const c10::optional<at::Tensor>& dk_out,
@@ -142,7 +159,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_fwd", &fyb::swiglu_fwd);
   m.def("swiglu_bwd", &fyb::swiglu_bwd, py::arg("x"), py::arg("y"), py::arg("g"), py::arg("dx_out") = py::none(),
         py::arg("dy_out") = py::none());
-  m.def("gate_cumsum_fwd", &fyb::gate_cumsum_fwd);
+  m.def("gate_cumsum_fwd", &fyb::gate_cumsum_fwd, py::arg("y"), py::arg("B"), py::arg("L"), py::arg("normalizer"),
+        py::arg("chunk_local") = false);
   m.def("gate_cumsum_bwd", &fyb::gate_cumsum_bwd);
   m.def("rope_fwd", &fyb::rope_fwd, py::arg("x"), py::arg("cos"), py::arg("sin"), py::arg("conj") = false,
         py::arg("neox") = false);
@@ -168,6 +186,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rope_cos") = py::none(), py::arg("rope_sin") = py::none(), py::arg("rope_q") = false,
         py::arg("rope_k") = false);
   m.def("retention_fwd", &fyb::retention_fwd);
+  m.def("retention_chunk_cumsum", &fyb::retention_chunk_cumsum);
+  m.def("retention_chunk_fwd", &fyb::retention_chunk_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("gloc"),
+        py::arg("state_in") = py::none(), py::arg("want_state") = false);
+  m.def("retention_chunk_state", &fyb::retention_chunk_state, py::arg("k"), py::arg("v"), py::arg("gloc"),
+        py::arg("state_in") = py::none());
+  m.def("retention_chunk_bwd", &fyb::retention_chunk_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),
+        py::arg("gloc"), py::arg("states"), py::arg("dstate_out") = py::none(), py::arg("want_dstate_in") = false,
+        py::arg("has_state_in") = false, py::arg("dq") = py::none(), py::arg("dk") = py::none(),
+        py::arg("dv") = py::none(), py::arg("rope_cos") = py::none(), py::arg("rope_sin") = py::none(),
+        py::arg("o") = py::none());
+  m.def("retention_decode", &fyb::retention_decode);
   m.def("retention_bwd", &fyb::retention_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),
         py::arg("gcum"), py::arg("o"), py::arg("dq_out") = py::none(), py::arg("dk_out") = py::none(),
         py::arg("dv_out") = py::none(), py::arg("rope_cos") = py::none(), py::arg("rope_sin") = py::none());

@@ -539,6 +539,42 @@ __global__ void __launch_bounds__(kScanThreads) gate_cumsum_fwd_kernel(const __n
   }
 }
 
+// Chunk-local variant (chunkwise retention): the cumsum restarts at every multiple of 128 positions. One warp per
+// (b, h, chunk), four positions per lane, a warp scan of the lane totals.
+__global__ void __launch_bounds__(256) gate_cumsum_chunk_kernel(const __nv_bfloat16* __restrict__ y, int64_t ldy,
+                                                                float* __restrict__ gcum, int B, int L, int H,
+                                                                float inv_norm) {
+  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nc = (L + 127) / 128;
+  if (wid >= static_cast<int64_t>(B) * H * nc) return;
+  const int c = static_cast<int>(wid % nc);
+  const int bh = static_cast<int>(wid / nc);
+  const int b = bh / H, h = bh % H;
+  const int t0 = c * 128 + lane * 4;
+  float v[4];
+  float run = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = t0 + i;
+    const float x = t < L ? bf16_round(logsigmoidf_(__bfloat162float(y[(static_cast<int64_t>(b) * L + t) * ldy + h])))
+                                * inv_norm : 0.f;
+    run += x;
+    v[i] = run;
+  }
+  float inc = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float u = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += u;
+  }
+  const float excl = inc - run;
+  float* out = gcum + static_cast<int64_t>(bh) * L;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (t0 + i < L) out[t0 + i] = excl + v[i];
+}
+
 // dy[b*L+t, h] = sigmoid(-y) / normalizer * sum_{s>=t} dg[b, h, s]  (reverse scan: thread i owns run i from the end)
 __global__ void __launch_bounds__(kScanThreads) gate_cumsum_bwd_kernel(const float* __restrict__ dg,
                                                                       const __nv_bfloat16* __restrict__ y,
@@ -568,13 +604,22 @@ __global__ void __launch_bounds__(kScanThreads) gate_cumsum_bwd_kernel(const flo
 // ------------------------------------------------------------------------------------------------------------------
 // host entry points
 
-at::Tensor gate_cumsum_fwd(const at::Tensor& y, int64_t B, int64_t L, double normalizer) {
+at::Tensor gate_cumsum_fwd(const at::Tensor& y, int64_t B, int64_t L, double normalizer, bool chunk_local) {
   FYB_RANGE("fyb::gate_cumsum_fwd");
   FYB_CHECK(y.is_cuda() && y.scalar_type() == at::kBFloat16 && y.dim() == 2 && y.stride(1) == 1 && y.size(0) == B * L,
             "gate_cumsum_fwd: bf16 [B*L, H] view expected");
   c10::cuda::CUDAGuard guard(y.device());
   const int H = static_cast<int>(y.size(1));
   auto g = at::empty({B, H, L}, y.options().dtype(at::kFloat));
+  if (chunk_local) {
+    const int64_t warps = B * H * ((L + 127) / 128);
+    if (warps > 0)
+      gate_cumsum_chunk_kernel<<<static_cast<int>((warps * 32 + 255) / 256), 256, 0, cur_stream()>>>(
+          reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0), g.data_ptr<float>(), (int)B, (int)L, H,
+          static_cast<float>(1.0 / normalizer));
+    check_launch("gate_cumsum_chunk");
+    return g;
+  }
   const int blocks = static_cast<int>(B) * H;
   if (blocks > 0)
     gate_cumsum_fwd_kernel<<<blocks, kScanThreads, 0, cur_stream()>>>(

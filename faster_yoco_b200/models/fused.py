@@ -82,13 +82,18 @@ class SelfRetentionLayerFn(torch.autograd.Function):
         q = C.rope_fwd(y3[..., :d].view(B, L, H, D), cos, sin, False)
         k = C.rope_fwd(y3[..., d:2 * d].view(B, L, H, D), cos, sin, False)
         v = y3[..., 2 * d:3 * d].view(B, L, H, D)
-        gcum = C.gate_cumsum_fwd(y[:, 4 * d:4 * d + H], B, L, float(norm))
-        o = C.retention_fwd(q, k, v, gcum)
+        if ops.RETENTION_FORM == "parallel":
+            gcum = C.gate_cumsum_fwd(y[:, 4 * d:4 * d + H], B, L, float(norm))
+            o = C.retention_fwd(q, k, v, gcum)
+            states = gcum
+        else:                      # chunkwise: chunk-local gate cumsum, entering states kept for the backward
+            gcum = C.gate_cumsum_fwd(y[:, 4 * d:4 * d + H], B, L, float(norm), True)
+            o, states, _ = C.retention_chunk_fwd(q, k, v, gcum)
         o2, rs = C.subln_swiglu_fwd(o.view(T, d), y[:, 3 * d:4 * d], float(sub_eps), D)
         x1 = ops.gemm(o2, wout, residual=x2)
         xo, ffn_saved = _ffn_forward(x1, wn2, wfc1g, wfc2, eps, f)
         ctx.save_for_backward(x2, h1, r1, y, q, k, gcum, o, rs, o2, x1, *ffn_saved, wn1, wqkvg, wout, wn2, wfc1g,
-                              wfc2, cos, sin)
+                              wfc2, cos, sin, states)
         ctx.cfg = cfg
         ctx.shape = (B, L, d)
         return xo.view(B, L, d)
@@ -97,7 +102,7 @@ class SelfRetentionLayerFn(torch.autograd.Function):
     def backward(ctx, dxo):
         C = _C()
         (x2, h1, r1, y, q, k, gcum, o, rs, o2, x1, h2, r2, u, a, wn1, wqkvg, wout, wn2, wfc1g, wfc2, cos,
-         sin) = ctx.saved_tensors
+         sin, states) = ctx.saved_tensors
         H, D, eps, sub_eps, norm, f = ctx.cfg
         B, L, d = ctx.shape
         T = B * L
@@ -110,9 +115,12 @@ class SelfRetentionLayerFn(torch.autograd.Function):
         dy3 = dy.view(B, L, R)
         do, _ = C.subln_swiglu_bwd(do2, o.view(T, d), y[:, 3 * d:4 * d], rs, D, dy[:, 3 * d:4 * d])
         v = y.view(B, L, R)[..., 2 * d:3 * d].view(B, L, H, D)
-        _, _, _, dg = C.retention_bwd(do.view(B, L, H, D), q, k, v, gcum, o,
-                                      dy3[..., :d].view(B, L, H, D), dy3[..., d:2 * d].view(B, L, H, D),
-                                      dy3[..., 2 * d:3 * d].view(B, L, H, D), cos, sin)
+        dqv, dkv, dvv = (dy3[..., i * d:(i + 1) * d].view(B, L, H, D) for i in range(3))
+        if ops.RETENTION_FORM == "parallel":
+            _, _, _, dg = C.retention_bwd(do.view(B, L, H, D), q, k, v, gcum, o, dqv, dkv, dvv, cos, sin)
+        else:
+            dg = C.retention_chunk_bwd(do.view(B, L, H, D), q, k, v, gcum, states, dq=dqv, dk=dkv, dv=dvv,
+                                       rope_cos=cos, rope_sin=sin, o=o)[4]
         ydg = dy[:, 4 * d:4 * d + H]
         C.gate_cumsum_bwd(dg, y[:, 4 * d:4 * d + H], ydg, float(norm))
         if R > 4 * d + H:

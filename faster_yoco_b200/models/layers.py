@@ -218,17 +218,30 @@ class GateRetention(nn.Module):
         o = o.view(B, L, H * D)
         return self.out_proj(o, residual)
 
-    # inference paths (yoco/models/decoder/gate_retention.py:83-97); PyTorch expressions of the reference
+    # inference paths (yoco/models/decoder/gate_retention.py:83-97): on the GPU the chunkwise prefill and the decode
+    # step are native kernels (fp32 state); elsewhere the PyTorch expressions of the reference
     def _decode(self, q, k, v, gt, st):
+        if ops.native_on(q) and q.shape[-1] == 128:
+            last = st.get("last_hidden_state")
+            if last is None or last.dtype != torch.float32 or not last.is_contiguous():
+                B, _, H, D = q.shape
+                last = (last.float().contiguous() if last is not None
+                        else torch.zeros(B, H, D, D, dtype=torch.float32, device=q.device))
+            o = ops.retention_decode(q, k, v, gt, last)
+            st["last_hidden_state"] = last
+            return o
         qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
         o, st["last_hidden_state"] = ops.ref.recurrent_gate_retention(qh, kh, vh, gt.transpose(1, 2),
                                                                        st.get("last_hidden_state"))
         return o.transpose(1, 2)
 
     def _prefill(self, q, k, v, gt, st):
-        qh, kh, vh, gh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), gt.transpose(1, 2)
         index_mask = st.get("index_mask")
         last = st.get("last_hidden_state")
+        if ops.native_on(q) and q.shape[-1] == 128:
+            o, st["last_hidden_state"] = ops.retention_prefill(q, k, v, gt, last, index_mask)
+            return o
+        qh, kh, vh, gh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), gt.transpose(1, 2)
         st["last_hidden_state"] = ops.ref.retention_prefill_state(kh, vh, gh, index_mask, last)
         L = qh.shape[2]
         cs = self.args.chunk_size

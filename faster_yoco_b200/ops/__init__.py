@@ -277,6 +277,11 @@ def gate_logsigmoid(gt: torch.Tensor, normalizer: float) -> torch.Tensor:
     return F.logsigmoid(gt) / normalizer
 
 
+# FYB_RETENTION=parallel: the quadratic parallel-form kernel (attention.cu) instead of the chunkwise kernels
+# (retention.cu); kept as a second implementation for comparison
+RETENTION_FORM = os.environ.get("FYB_RETENTION", "chunk")
+
+
 class _NativeRetention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, gcum):
@@ -291,6 +296,54 @@ class _NativeRetention(torch.autograd.Function):
         return dq, dk, dv, dg
 
 
+class _NativeChunkRetention(torch.autograd.Function):
+    """Chunkwise retention (retention.cu) on the per-step log decays g [B, H, L] (fp32): the kernels see the
+    chunk-local cumsum; the gate gradient comes back w.r.t. the global cumsum G, so dL/dg = reverse cumsum of it."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g):
+        C = _C()
+        gloc = C.retention_chunk_cumsum(g)
+        o, states, _ = C.retention_chunk_fwd(q, k, v, gloc)
+        ctx.save_for_backward(q, k, v, gloc, states, o)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, gloc, states, o = ctx.saved_tensors
+        dq, dk, dv, _, dG = _C().retention_chunk_bwd(do.contiguous(), q, k, v, gloc, states, o=o)
+        dg = dG.flip(-1).cumsum(-1).flip(-1)
+        return dq, dk, dv, dg
+
+
+def retention_prefill(q, k, v, g, state=None, index_mask=None):
+    """Chunked prefill on the GPU: outputs of a block of L tokens and the state after it.
+
+    q, k, v: [B, L, H, 128] bf16; g: [B, L, H] per-step log decays; state: fp32 [B, H, 128, 128] entering the block
+    (or None). index_mask: optional bool [B, H, L] (True = padding), applied to the state only, as the reference's
+    prefill does (outputs use every position). Returns (o [B, L, H, 128], new fp32 state)."""
+    C = _C()
+    gh = g.float().transpose(1, 2).contiguous()
+    gloc = C.retention_chunk_cumsum(gh)
+    st = state.float().contiguous() if state is not None else None
+    if index_mask is None:
+        o, _, nxt = C.retention_chunk_fwd(q, k, v, gloc, state_in=st, want_state=True)
+        return o, nxt
+    o, _, _ = C.retention_chunk_fwd(q, k, v, gloc, state_in=st)
+    index_mask = torch.broadcast_to(index_mask.to(q.device), gh.shape)
+    keep = (~index_mask).transpose(1, 2).unsqueeze(-1)                 # [B, L, H, 1]
+    km = (k * keep.to(k.dtype)).contiguous()
+    gm = C.retention_chunk_cumsum(gh.masked_fill(index_mask, 0.0).contiguous())
+    return o, C.retention_chunk_state(km, v, gm, state_in=st)
+
+
+def retention_decode(q, k, v, g, state):
+    """One decode step: q, k, v [B, 1, H, 128] bf16, g [B, 1, H] log decays, state fp32 [B, H, 128, 128] (updated in
+    place). Returns o [B, 1, H, 128]."""
+    o = _C().retention_decode(q[:, 0], k[:, 0], v[:, 0], g[:, 0].float().contiguous(), state)
+    return o.unsqueeze(1)
+
+
 def retention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, gt: torch.Tensor,
               chunk_size: int = 256) -> torch.Tensor:
     """Gated retention over a full sequence (training path).
@@ -299,8 +352,10 @@ def retention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, gt: torch.Tenso
     (logsigmoid / normalizer, any float dtype). Returns o: [B, L, H, D] contiguous."""
     B, L, H, D = q.shape
     if native_on(q) and D == 128:
-        gcum = gt.float().transpose(1, 2).cumsum(-1).contiguous()      # [B, H, L] fp32
-        return _NativeRetention.apply(q, k, v, gcum)
+        if RETENTION_FORM == "parallel":
+            gcum = gt.float().transpose(1, 2).cumsum(-1).contiguous()      # [B, H, L] fp32
+            return _NativeRetention.apply(q, k, v, gcum)
+        return _NativeChunkRetention.apply(q, k, v, gt.float().transpose(1, 2).contiguous())
     qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
     gh = gt.transpose(1, 2)
     if L % chunk_size == 0:
@@ -430,5 +485,5 @@ def cross_entropy(logits: torch.Tensor, target: torch.Tensor, ignore_index: int)
 
 __all__ = [
     "set_backend", "get_backend", "gemm", "linear", "rms_norm", "swiglu", "rope", "subln_swiglu", "gate_logsigmoid",
-    "retention", "attention", "embedding", "cross_entropy", "ref",
+    "retention", "retention_prefill", "retention_decode", "attention", "embedding", "cross_entropy", "ref",
 ]

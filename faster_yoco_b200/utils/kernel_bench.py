@@ -128,6 +128,19 @@ def bench_retention(results, L=2048, H=24, B=1):
     fl = 4.0 * B * H * L * L * 128 / 2
     results.append({"kernel": "retention_parallel", "L": L, "H": H, "fwd_ms": t_f, "bwd_ms": t_b,
                     "fwd_tflops": fl / t_f / 1e9, "bwd_tflops": 2.5 * fl / t_b / 1e9})
+    # chunkwise kernels (chunk 128): forward = the state outer products, the scan and the per-chunk outputs
+    # (4 MMAs of 128^3 per chunk: K^T V, Q K^T, Q S, P V); backward = Q^T dO, the reverse scan and the per-chunk
+    # gradients (8 MMAs per chunk) plus the gate row dots
+    gl = C.retention_chunk_cumsum((torch.nn.functional.logsigmoid(torch.randn(B, H, L, device=dev)) / 16)
+                                  .contiguous())
+    o, states, _ = C.retention_chunk_fwd(q, k, v, gl)
+    t_cf = _time(lambda: C.retention_chunk_fwd(q, k, v, gl))
+    t_cb = _time(lambda: C.retention_chunk_bwd(do, q, k, v, gl, states, o=o))
+    nc = (L + 127) // 128
+    fl_f = 4 * 2.0 * 128 ** 3 * B * H * nc
+    results.append({"kernel": "retention_chunk", "L": L, "H": H, "fwd_ms": t_cf, "bwd_ms": t_cb,
+                    "fwd_tflops": fl_f / t_cf / 1e9, "bwd_tflops": 2 * fl_f / t_cb / 1e9,
+                    "speedup_vs_parallel": (t_f + t_b) / (t_cf + t_cb)})
 
 
 def main():

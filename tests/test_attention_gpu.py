@@ -45,9 +45,12 @@ def test_attention_fwd_bwd(B, L, Hq, Hk, window):
     assert int(ops._C().status()[0].item()) == 0
 
 
+@pytest.mark.parametrize("form", ["chunk", "parallel"])
 @pytest.mark.parametrize("B,L,H", [(1, 256, 2), (2, 384, 3), (1, 2048, 2), (1, 200, 1)])
-def test_retention_fwd_bwd(B, L, H):
+def test_retention_fwd_bwd(B, L, H, form, monkeypatch):
+    """Both native forms: the chunkwise kernels (default) and the quadratic parallel-form kernel."""
     ops.set_backend("native")
+    monkeypatch.setattr(ops, "RETENTION_FORM", form)
     D = 128
     q = strided_heads(B, L, H, D, seed=4).requires_grad_()
     k = strided_heads(B, L, H, D, seed=5).requires_grad_()

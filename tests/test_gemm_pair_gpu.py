@@ -16,9 +16,14 @@ def _operands(M, N, K, a_mn, b_mn, g):
     return a, b
 
 
-def _close_in_ulps(x, y, ulps):
-    """|x - y| within `ulps` bf16 units in the last place of the larger magnitude (plus a small absolute floor)."""
-    mag = torch.maximum(x.abs(), y.abs()).clamp_min(1e-30)
+def _close_in_ulps(x, y, ulps, acc_mag=None):
+    """|x - y| within `ulps` bf16 units in the last place of the larger magnitude (plus a small absolute floor).
+    acc_mag: magnitude of the product before a residual was added (the residual epilogue rounds the product to
+    bf16 first, so a one-unit flip there is measured in units of the product, not of the smaller sum)."""
+    mag = torch.maximum(x.abs(), y.abs())
+    if acc_mag is not None:
+        mag = torch.maximum(mag, acc_mag)
+    mag = mag.clamp_min(1e-30)
     ulp = torch.exp2(torch.floor(torch.log2(mag)) - 7)        # bf16: 8 significant bits
     tol = ulps * ulp + 2e-2 if ulps else 1e-2 + 1e-3 * mag
     bad = (x - y).abs() > tol
@@ -42,6 +47,9 @@ def test_gemm_pair_matches_one_cta_and_fp32(M, N, K, a_mn, b_mn, epi):
     res = torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16) if epi == "res" else None
     one = torch.empty(M, N, dtype=dt, device=dev)
     C.gemm(a, b, one, a_mn, b_mn, res)
+    A32 = (a.float().t() if a_mn else a.float())
+    B32 = (b.float() if b_mn else b.float().t())
+    prod = A32 @ B32
     for _ in range(2):
         pair = torch.full((M, N), float("nan"), dtype=dt, device=dev)
         C.gemm_pair(a, b, pair, a_mn, b_mn, res)
@@ -50,10 +58,8 @@ def test_gemm_pair_matches_one_cta_and_fp32(M, N, K, a_mn, b_mn, epi):
         assert not bool(torch.isnan(pair.float()).any()), "unwritten output"
         # same per-element K order in both kernels: equal up to the tensor cores' accumulation rounding, which can
         # move a bf16 output by one unit in the last place (two with the residual epilogue's second rounding)
-        _close_in_ulps(pair.float(), one.float(), 2 if dt == torch.bfloat16 else 0)
-    A32 = (a.float().t() if a_mn else a.float())
-    B32 = (b.float() if b_mn else b.float().t())
-    ref = A32 @ B32
+        _close_in_ulps(pair.float(), one.float(), 2 if dt == torch.bfloat16 else 0, prod.abs())
+    ref = prod
     if res is not None:
         ref = ref + res.float()
     err = ((pair.float() - ref).abs().max() / ref.abs().max()).item()
