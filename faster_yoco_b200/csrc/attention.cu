@@ -14,16 +14,19 @@
 // Forward CTA (10 warps) = one (batch, head, 128-query tile):
 //   warp 0     producer: Q once, K/V tiles (128 keys x 128 dims, 128B swizzle) in a 2-stage TMA ring, and the
 //              retention gate tiles (G_k, column factors) into shared memory
-//   warp 1     UMMA issuer: S = Q K^T into one of two TMEM S buffers; O += P V into one TMEM O accumulator
+//   warp 1     UMMA issuer: S = Q K^T into one of two TMEM S buffers; O += P V into one TMEM O accumulator, P
+//              read from TMEM (A operand)
 //   warps 2..9 two threads per query row (TMEM lane quadrant = warp % 4, column half = (warp - 2) / 4): read S
-//              (tcgen05.ld), mask, exponentiate, write P (bf16, swizzled K-major) for the PV MMA
+//              (tcgen05.ld), mask, exponentiate, write P as bf16 pairs into one of two TMEM P buffers (tcgen05.st),
+//              so the softmax of tile j + 1 overlaps the PV MMA of tile j
 //
 // Backward CTA = one (batch, kv head, 128-key tile) looping over the query tiles that see this key tile, for ONE
 // query head of the GQA group (fp32 dK / dV partial per head, summed in head order by a post pass) or,
 // without GQA, for the head itself (dK / dV leave straight from TMEM). Per query tile: S^T = K Q^T and
 // dP^T = V dO^T (TMEM); P^T goes back into the S^T columns as bf16 pairs and is the TMEM A operand of
 // dV += P^T dO; dS^T (bf16, shared memory) feeds dK += dS^T Q and dQ_tile = dS K (TMEM, in the dP^T columns ->
-// fp32 atomics into a dQ accumulator). The UMMA descriptors read the same swizzled dS^T tile as K-major (for dK)
+// bulk tensor reductions into an fp32 dQ accumulator, staged per warp in the dS^T tile the dQ MMA has finished
+// reading). The UMMA descriptors read the same swizzled dS^T tile as K-major (for dK)
 // and as MN-major (for dQ). Q / dO are double-buffered, so the next tile's TMA load and S^T overlap this tile's
 // dQ drain. The per-query values (lse and delta, or the gates) are staged in shared memory by the producer warp.
 //
@@ -135,8 +138,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + kTileBytes;             // 2 stages
   uint8_t* sV = sK + 2 * kTileBytes;         // 2 stages
-  uint8_t* sP = sV + 2 * kTileBytes;
-  float* sG = reinterpret_cast<float*>(sP + kTileBytes);   // [2][128] key gates (retention)
+  float* sG = reinterpret_cast<float*>(sV + 2 * kTileBytes);   // [2][128] key gates (retention)
   float* sCF = sG + 2 * kT;                                 // [2][128] column factors exp(G_e - G_k)
   float* sL = sCF + 2 * kT;                                 // [2][128] row-sum halves (softmax)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sL + 2 * kT);
@@ -188,7 +190,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;   // S[0] @ col 0, S[1] @ 128, O @ 256
+  // S[0] @ col 0, S[1] @ 128, O @ 256, P[0] @ 384, P[1] @ 448 (P: bf16 pairs, 64 columns per 128 keys)
+  const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
     // ---------------------------------------------------------------------------------------------- producer
@@ -248,7 +251,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp == 1) {
     // ---------------------------------------------------------------------------------------------- UMMA issuer
     if (lane == 0 && n > 0) {
-      const uint32_t aQ = smem_u32(sQ), aP = smem_u32(sP);
+      const uint32_t aQ = smem_u32(sQ);
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status, 25);
       auto issue_s = [&](int it) -> bool {
         const int st = it & 1;
@@ -271,9 +274,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (!mbar_wait(&v_full[st], ph, abort_flag, p.status, 29)) return false;
         tc_fence_after();
         const uint32_t aV = smem_u32(sV + st * kTileBytes);
+        // O += P V with P (bf16 pairs) in TMEM: K step k = keys 16k..16k+15 of column half k / 4
 #pragma unroll
         for (int k = 0; k < kT / 16; ++k)
-          umma_bf16(tmem + 256, kmaj_desc(aP, k), mnmaj_desc(aV, k), IDESC_O, (it > 0 || k > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + 256, tmem + 384 + st * 64 + (k >> 2) * 32 + (k & 3) * 8, mnmaj_desc(aV, k), IDESC_O,
+                       (it > 0 || k > 0) ? 1u : 0u);
         umma_commit(p_empty);
         umma_commit(&v_empty[st]);
         return true;
@@ -327,11 +332,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
         const float m_cand = fmaxf(m_ref, mx * sl2);
-        // O may be touched only after PV(it-1) has completed
-        if (!(ok = mbar_wait(p_empty, (it & 1) ^ 1u, abort_flag, p.status, 32))) break;
         const bool need = m_cand > m_ref + kRescaleLog2;
         const bool scale_o = need && m_ref != -INFINITY;
         if (__any_sync(0xffffffffu, scale_o)) {
+          // O may be touched only after PV(it-1) has completed. PV(it-2) is complete (S(it), whose commit this
+          // thread waited for, was issued after it) and PV(it) is not issued yet, so the parity of phase it - 1
+          // names exactly one phase
+          if (!(ok = mbar_wait(p_empty, (it & 1) ^ 1u, abort_flag, p.status, 32))) break;
           const float f = scale_o ? fast_exp2(m_ref - m_cand) : 1.0f;
           tc_fence_after();
 #pragma unroll
@@ -347,14 +354,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (scale_o) l_part *= f;
         }
         if (need) m_ref = m_cand;
-      } else {
-        if (!(ok = mbar_wait(p_empty, (it & 1) ^ 1u, abort_flag, p.status, 32))) break;
       }
       const bool diag = k0 + kT - 1 >= q0 + p.q_offset;   // retention: tile reaches the query tile
       const float rf = (MODE == kRetention && !diag) ? __expf(gq - sG[st * kT + kT - 1]) * p.scale : 0.f;
       const float mref = m_ref == -INFINITY ? 0.f : m_ref;
       {
         uint32_t va[2][32];
+        uint32_t pp[32];
         tmem_ld32(tmem + st * 128 + trow + c0, va[0]);
         tmem_ld32(tmem + st * 128 + trow + c0 + 32, va[1]);
         tmem_ld_wait();
@@ -377,11 +383,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
             pv[i] = x;
           }
-          store_row8(sP, r, c >> 3, pv);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pp[16 * hh + i] = pack_bf16(pv[2 * i], pv[2 * i + 1]);
         }
+        // P row r, keys c0..c0+63 -> 32 packed columns of P[st]. PV(it-2), the last reader of P[st], was issued
+        // before S(it) and so has completed
+        tmem_st32(tmem + 384 + st * 64 + trow + half * 32, pp);
+        tmem_st_wait();
       }
       tc_fence_before();
-      fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&s_empty[st]);
@@ -458,7 +468,7 @@ template <int MODE>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
-                    AttnBwdParams p) {
+                    const __grid_constant__ CUtensorMap tmdQ, AttnBwdParams p) {
   // Shared memory: K, V (once), Q / dO double-buffered (the next query tile loads while this one computes),
   // dS^T (bf16, read by the dK MMA as K-major and by the dQ MMA as MN-major). P^T never touches shared memory:
   // the score warps store it (bf16 pairs) into the TMEM columns of S^T they have just read, and the dV MMA takes
@@ -703,6 +713,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (!(ok = mbar_wait(dp_full, ph, abort_flag, p.status, 53))) break;
       if (!(ok = mbar_wait(ds_empty, ph ^ 1u, abort_flag, p.status, 50))) break;
       tc_fence_after();
+      // this warp's slice of dS^T (rows quad*32.., columns c0..) is the 4 KB block it staged dQ in last iteration:
+      // the bulk reduction must have read it
+      if (lane == 0) bulk_wait_read0();
+      __syncwarp();
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
         uint32_t da[32];
@@ -730,28 +744,43 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_arrive(dst_full);
         mbar_arrive(qv_empty);
       }
-      // dQ tile (TMEM lane = query row, columns 128..255) -> fp32 atomics
+      // dQ tile (TMEM lane = query row, columns 128..255) -> fp32 bulk tensor reductions: each warp stages its
+      // 32 rows x 32 columns (4 KB, 128-byte swizzle) in its own slice of the dS^T tile, which the dK / dQ MMAs of
+      // this iteration have finished reading (dq_full), and one lane reduces it into dq_acc
       if (!(ok = mbar_wait(dq_full, ph, abort_flag, p.status, 51))) break;
       tc_fence_after();
       const int qrow = q0 + r;
-      float* dqr = p.dq_acc + ((static_cast<int64_t>(b) * p.Lq + min(qrow, p.Lq - 1)) * p.Hq + h) * kD + c0;
+      uint8_t* stage = sdST + half * 16384 + quad * 4096;
 #pragma unroll
       for (int c = 0; c < 64; c += 32) {
         uint32_t v[32];
         tmem_ld32(tmem + 128 + trow + c0 + c, v);
         tmem_ld_wait();
-        if (qrow < p.Lq) {
+        if (c > 0) {                        // the first chunk's reduction must have read the staging block
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+        }
+        const bool live = qrow < p.Lq;      // rows past Lq belong to the next sequence: add zeros there
 #pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            atomicAdd(reinterpret_cast<float4*>(dqr + c + j),
-                      make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
-                                  __uint_as_float(v[j + 3])));
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<float4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+              live ? make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                 __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_3d(&tmdQ, stage, c0 + c, h, b * p.Lq + q0 + quad * 32);
+          bulk_commit_group();
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_empty);
     }
+    // the last dQ reductions complete before the CTA ends (their shared-memory source included)
+    if (lane == 0) bulk_wait0();
+    __syncwarp();
     // ---- dK, dV
     const bool have = ok && n_it > 0 && mbar_wait(fin, 0, abort_flag, p.status, 52);
     if (have) tc_fence_after();
@@ -888,7 +917,7 @@ __global__ void dq_out_kernel(const float* __restrict__ acc, __nv_bfloat16* __re
   *reinterpret_cast<uint2*>(out + bt * ld + h * kD + c) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
 }
 
-constexpr int kFwdSmem = 6 * kTileBytes + 6 * kT * 4 + 256 + 1024;
+constexpr int kFwdSmem = 5 * kTileBytes + 6 * kT * 4 + 256 + 1024;
 constexpr int kBwdSmem = 7 * kTileBytes + 2 * kT * 4 + 256 + 1024;
 static_assert(kBwdSmem <= 227 * 1024, "attention backward shared memory");
 
@@ -899,6 +928,11 @@ void check_qkv(const at::Tensor& t, const char* name) {
             std::string(name) + ": batch stride must equal L x token stride");
   FYB_CHECK(t.stride(1) % 8 == 0 && t.stride(2) % 8 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
             std::string(name) + ": strides must be multiples of 8 elements, base 16-byte aligned");
+}
+
+// dQ accumulator [B, L, H, 128] fp32 (contiguous) as {128, H, B * L} with 32 x 1 x 32 boxes
+CUtensorMap tmap_dq(const at::Tensor& acc) {
+  return make_tmap_3d_f32(acc.data_ptr(), kD, acc.size(2), acc.size(0) * acc.size(1), kD, acc.size(2) * kD, 32);
 }
 
 CUtensorMap tmap_heads(const at::Tensor& t) {
@@ -1003,13 +1037,14 @@ std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& 
                   reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()),
                   dk.stride(1), dv.stride(1), rope_k ? rc : nullptr, rope_k ? rs : nullptr, status_ptr()};
   const CUtensorMap tq = tmap_heads(q), tk = tmap_heads(k), tv = tmap_heads(v), tdo = tmap_heads(dout);
+  const CUtensorMap tdq = tmap_dq(dq_acc);
   static bool init = false;
   if (!init) {
     set_smem(attn_bwd_kernel<kSoftmax>, kBwdSmem);
     init = true;
   }
   const int grid = B * Hk * (split ? G : 1) * ((Lk + kT - 1) / kT);
-  attn_bwd_kernel<kSoftmax><<<grid, kAttnThreads, kBwdSmem, cur_stream()>>>(tq, tk, tv, tdo, p);
+  attn_bwd_kernel<kSoftmax><<<grid, kAttnThreads, kBwdSmem, cur_stream()>>>(tq, tk, tv, tdo, tdq, p);
   check_launch("attn_bwd");
   if (split) {
     const int64_t nk4 = static_cast<int64_t>(B) * Lk * Hk * (kD / 4);
@@ -1096,13 +1131,14 @@ std::vector<at::Tensor> retention_bwd(const at::Tensor& dout, const at::Tensor& 
                   reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()),
                   dk.stride(1), dv.stride(1), rc, rs, status_ptr()};
   const CUtensorMap tq = tmap_heads(q), tk = tmap_heads(k), tv = tmap_heads(v), tdo = tmap_heads(dout);
+  const CUtensorMap tdq = tmap_dq(dq_acc);
   static bool init = false;
   if (!init) {
     set_smem(attn_bwd_kernel<kRetention>, kBwdSmem);
     init = true;
   }
   const int grid = B * H * ((L + kT - 1) / kT);
-  attn_bwd_kernel<kRetention><<<grid, kAttnThreads, kBwdSmem, cur_stream()>>>(tq, tk, tv, tdo, p);
+  attn_bwd_kernel<kRetention><<<grid, kAttnThreads, kBwdSmem, cur_stream()>>>(tq, tk, tv, tdo, tdq, p);
   check_launch("retention_bwd");
   // dG = dO.O - V.dV (both operands may be token-strided views)
   rowdot_kernel<<<(rows * 32 + 255) / 256, 256, 0, cur_stream()>>>(

@@ -63,8 +63,7 @@ std::vector<at::Tensor> retention_chunk_bwd(const at::Tensor& dout, const at::Te
                                             const c10::optional<at::Tensor>& dk_out,
                                             const c10::optional<at::Tensor>& dv_out,
                                             const c10::optional<at::Tensor>& rope_cos,
-                                            const c10::optional<at::Tensor>& rope_sin,
-                                            const c10::optional<at::Tensor>& o);
+                                            const c10::optional<at::Tensor>& rope_sin, bool want_dgate);
 at::Tensor retention_decode(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
                             at::Tensor& state);
 std::vector<at::Tensor> retention_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
@@ -195,7 +194,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gloc"), py::arg("states"), py::arg("dstate_out") = py::none(), py::arg("want_dstate_in") = false,
         py::arg("has_state_in") = false, py::arg("dq") = py::none(), py::arg("dk") = py::none(),
         py::arg("dv") = py::none(), py::arg("rope_cos") = py::none(), py::arg("rope_sin") = py::none(),
-        py::arg("o") = py::none());
+        py::arg("want_dgate") = false);
   m.def("retention_decode", &fyb::retention_decode);
   m.def("retention_bwd", &fyb::retention_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),
         py::arg("gcum"), py::arg("o"), py::arg("dq_out") = py::none(), py::arg("dk_out") = py::none(),

@@ -90,6 +90,24 @@ inline CUtensorMap make_tmap_3d(const void* base, int64_t d0, int64_t d1, int64_
   return m;
 }
 
+// 3-D fp32 tensor map: dims {d0 (contiguous), d1, d2}, strides (elements) s1, s2, box {32, 1, box2}, 128-byte
+// swizzle (a box row is 32 floats = 128 bytes). Used by bulk tensor reductions of fp32 accumulators.
+inline CUtensorMap make_tmap_3d_f32(const void* base, int64_t d0, int64_t d1, int64_t d2, int64_t s1, int64_t s2,
+                                    int box2) {
+  FYB_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base address must be 16-byte aligned");
+  FYB_CHECK((s1 * 4) % 16 == 0 && (s2 * 4) % 16 == 0, "TMA strides must be multiples of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1), static_cast<cuuint64_t>(d2)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(s1 * 4), static_cast<cuuint64_t>(s2 * 4)};
+  cuuint32_t box[3] = {32u, 1u, static_cast<cuuint32_t>(box2)};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  FYB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (3d f32) code " + std::to_string(static_cast<int>(r)));
+  return m;
+}
+
 inline int num_sms() {
   static int n = 0;
   if (n == 0) {

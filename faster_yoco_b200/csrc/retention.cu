@@ -21,8 +21,10 @@
 //   S^T = K Q^T, dP^T = V dO^T; dV = diag(w) K~ D_{c+1} + P^T dO; dK = diag(w) V D_{c+1}^T + dS^T Q;
 //   dQ = diag(e^gamma) dO S_c^T + dS K~   (w = e^(Gamma - gamma) / sqrt(D), dS = dP o E o tril / sqrt(D))
 // with the row scalings applied to the TMEM accumulators between MMAs. The gate gradient needs no recurrence of its
-// own: for the global cumsum G, dL/dG_i = dO_i . O_i - v_i . dv_i (+ <dS_out, S_out> at the last position), one
-// row-dot pass over the outputs (ret_dgate_kernel).
+// own: for the global cumsum G, dL/dG_i = dO_i . O_i - v_i . dv_i (+ <dS_out, S_out> at the last position). The
+// chunk kernel evaluates it with the diagonal terms (which cancel) left out, from fp32 TMEM values:
+// sum_{j<i} P_ij dP_ij + dO_i . O_state_i - sum_{t>i} P_ti dP_ti - v_i . dV_state_i, so strongly decaying gates
+// (where the two dot products nearly cancel) keep their precision.
 //
 // Every wait is bounded (2 s) and records a status word instead of hanging; TMA loads read this GPU's memory only.
 #include <ATen/ATen.h>
@@ -70,6 +72,34 @@ __device__ __forceinline__ void tmem_scale64(uint32_t taddr, float f) {
     tmem_st32(taddr + c, v);
   }
   tmem_st_wait();
+}
+
+// TMEM row r, 64 fp32 columns from taddr (feature columns c0..c0+63): multiply by f in place and return the dot
+// product of the scaled values with row r, features c0..c0+63, of a bf16 tile in shared memory
+__device__ __forceinline__ float tmem_scale64_dot(uint32_t taddr, float f, const uint8_t* tile, int r, int c0) {
+  float dot = 0.f;
+#pragma unroll
+  for (int c = 0; c < 64; c += 32) {
+    uint32_t v[32];
+    tmem_ld32(taddr + c, v);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 u = *reinterpret_cast<const uint4*>(tile + swz(r, (c0 + c) / 8 + j));
+      const uint32_t e[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 x = unpack_bf16(e[i]);
+        const float a0 = __uint_as_float(v[8 * j + 2 * i]) * f, a1 = __uint_as_float(v[8 * j + 2 * i + 1]) * f;
+        v[8 * j + 2 * i] = __float_as_uint(a0);
+        v[8 * j + 2 * i + 1] = __float_as_uint(a1);
+        dot = fmaf(a0, x.x, fmaf(a1, x.y, dot));
+      }
+    }
+    tmem_st32(taddr + c, v);
+  }
+  tmem_st_wait();
+  return dot;
 }
 
 struct RetParams {
@@ -422,6 +452,7 @@ struct BwdArgs {
   const __nv_bfloat16* rope_sin;   // [L, D/2]
   int has_state0;              // chunk 0 has an entering state (S_0 != 0)
   int has_dlast;               // the last chunk has a leaving-state gradient (D_NC != 0)
+  float* dG;                   // optional [B, H, L]: gate gradient w.r.t. the global cumsum
 };
 
 __device__ __forceinline__ void store_grad_row(__nv_bfloat16* dst, uint32_t taddr, bool have, bool valid, int pos,
@@ -629,6 +660,15 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
     const float gr = sG[r];
     const float gend = sG[nvalid - 1];
     const float w = rowvalid ? __expf(fminf(gend - gr, 0.f)) * p.scale : 0.f;   // key row's state weight
+    // Gate gradient (w.r.t. the global cumsum), without the cancellation of dO.O - v.dv: the diagonal terms
+    // P_ii dP_ii cancel exactly, so dG_i = sum_{j<i} P_ij dP_ij + dO_i . O_state_i - sum_{t>i} P_ti dP_ti
+    // - v_i . dV_state_i, every term from fp32 TMEM values. Scratch: the D_{c+1} tile, dead once the state MMAs
+    // have completed (or never loaded).
+    float* qpart = reinterpret_cast<float*>(sDn);         // [4 quads][128 queries]: column sums of M
+    float* kpart = qpart + 4 * kC;                         // [2 halves][128 keys]: row sums of M + key state term
+    float* qst = kpart + 2 * kC;                           // [2 halves][128 queries]: query state term
+    float pk[64];                                          // this thread's fp32 P^T values (key r, 64 queries)
+    float kst = 0.f;
     bool ok = mbar_wait(s_full, 0, abort_flag, p.status, 100);
     if (ok) {
       tc_fence_after();
@@ -640,16 +680,13 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
 #pragma unroll
       for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float x[2];
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int q = c0 + 32 * hh + 2 * i + t;          // query position in the chunk
-            const bool vis = rowvalid && q >= r && q < nvalid;
-            x[t] = vis ? __uint_as_float(va[hh][2 * i + t]) * __expf(fminf(sG[q] - gr, 0.f)) * p.scale : 0.f;
-          }
-          pp[16 * hh + i] = pack_bf16(x[0], x[1]);
+        for (int i = 0; i < 32; ++i) {
+          const int q = c0 + 32 * hh + i;                    // query position in the chunk
+          const bool vis = rowvalid && q >= r && q < nvalid;
+          pk[32 * hh + i] = vis ? __uint_as_float(va[hh][i]) * __expf(fminf(sG[q] - gr, 0.f)) * p.scale : 0.f;
         }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pp[16 * hh + i] = pack_bf16(pk[32 * hh + 2 * i], pk[32 * hh + 2 * i + 1]);
       }
       tmem_st32(tmem + trow + c0, pp);           // P^T row r, queries c0..c0+63 -> 32 packed columns at c0
       tmem_st_wait();
@@ -658,7 +695,7 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
       ok = mbar_wait(st_full, 0, abort_flag, p.status, 101);
       if (ok) {
         tc_fence_after();
-        tmem_scale64(tmem + 256 + trow + c0, w);
+        kst = tmem_scale64_dot(tmem + 256 + trow + c0, w, sV, r, c0);      // v_r . dV_state_r (this half)
         tmem_scale64(tmem + 384 + trow + c0, w);
       }
     }
@@ -666,6 +703,7 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(pt_full);
     if (ok) ok = mbar_wait(dp_full, 0, abort_flag, p.status, 102);
+    float krow = 0.f;
     if (ok) {
       tc_fence_after();
 #pragma unroll
@@ -678,7 +716,11 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
         for (int i = 0; i < 32; ++i) {
           const int q = c0 + 32 * hh + i;
           const bool vis = rowvalid && q >= r && q < nvalid;
-          ds[i] = vis ? __uint_as_float(da[i]) * __expf(fminf(sG[q] - gr, 0.f)) * p.scale : 0.f;
+          const float dp = __uint_as_float(da[i]);
+          ds[i] = vis ? dp * __expf(fminf(sG[q] - gr, 0.f)) * p.scale : 0.f;
+          const float m = q > r ? pk[32 * hh + i] * dp : 0.f;      // strictly causal pairs only
+          pk[32 * hh + i] = m;
+          krow += m;
         }
         store_row32(sdST, r, (c0 + 32 * hh) >> 3, ds);
       }
@@ -687,15 +729,38 @@ __global__ void __launch_bounds__(kChunkThreads, 1)
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(dst_full);
+    // column sums of M over this warp's 32 key rows: butterfly over the lanes, lane l ends with queries
+    // c0 + 2l and c0 + 2l + 1
+#pragma unroll
+    for (int m = 16, n = 32; m >= 1; m >>= 1, n >>= 1) {
+      const bool upper = (lane & m) != 0;
+#pragma unroll
+      for (int i = 0; i < n; ++i) {
+        const float mine = upper ? pk[n + i] : pk[i];
+        const float other = upper ? pk[i] : pk[n + i];
+        pk[i] = mine + __shfl_xor_sync(0xffffffffu, other, m);
+      }
+    }
+    qpart[quad * kC + c0 + 2 * lane] = pk[0];
+    qpart[quad * kC + c0 + 2 * lane + 1] = pk[1];
+    kpart[half * kC + r] = krow + kst;
+    float qs = 0.f;
     if (has_state) {
       if (ok) ok = mbar_wait(dqs_full, 0, abort_flag, p.status, 103);
       if (ok) {
         tc_fence_after();
-        tmem_scale64(tmem + 128 + trow + c0, __expf(fminf(gr, 0.f)));     // dQ row r = query r
+        // dQ row r = query r: scale the state term by e^gamma_r; e^gamma_r q_r . (dO_r S_c^T) = dO_r . O_state_r
+        qs = tmem_scale64_dot(tmem + 128 + trow + c0, __expf(fminf(gr, 0.f)), sQ, r, c0);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dqs_done);
+    }
+    qst[half * kC + r] = qs;
+    named_barrier(2, kRowWarps * 32);
+    if (a.dG != nullptr && half == 0 && rowvalid) {
+      const float qside = qpart[r] + qpart[kC + r] + qpart[2 * kC + r] + qpart[3 * kC + r] + qst[r] + qst[kC + r];
+      a.dG[static_cast<int64_t>(bh) * p.L + pos0 + r] = qside - (kpart[r] + kpart[kC + r]);
     }
     const bool have = ok && mbar_wait(fin, 0, abort_flag, p.status, 104);
     if (have) tc_fence_after();
@@ -747,30 +812,6 @@ __global__ void __launch_bounds__(256) ret_decode_kernel(const __nv_bfloat16* __
   if (t >= kD) part[col] = acc;
   __syncthreads();
   if (t < kD) o[b * ldo + h * kD + col] = __float2bfloat16_rn(acc + part[col]);
-}
-
-// Gate gradient w.r.t. the global cumsum: dG[b, h, t] = dO . O - v . dv (one warp per (b, t, h); every operand a
-// [B, L, H, 128] view with its own token stride)
-__global__ void ret_dgate_kernel(const __nv_bfloat16* __restrict__ dO, const __nv_bfloat16* __restrict__ O,
-                                 const __nv_bfloat16* __restrict__ V, const __nv_bfloat16* __restrict__ dV,
-                                 float* __restrict__ out, int B, int L, int H, int64_t ld_do, int64_t ld_o,
-                                 int64_t ld_v, int64_t ld_dv) {
-  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (wid >= static_cast<int64_t>(B) * L * H) return;
-  const int h = static_cast<int>(wid % H);
-  const int64_t tok = wid / H;                      // b * L + t
-  const int t = static_cast<int>(tok % L), b = static_cast<int>(tok / L);
-  auto dot4 = [&](const __nv_bfloat16* X, int64_t ldx, const __nv_bfloat16* Y, int64_t ldy) {
-    const uint2 xu = *reinterpret_cast<const uint2*>(X + tok * ldx + h * kD + lane * 4);
-    const uint2 yu = *reinterpret_cast<const uint2*>(Y + tok * ldy + h * kD + lane * 4);
-    const float2 x0 = unpack_bf16(xu.x), x1 = unpack_bf16(xu.y), y0 = unpack_bf16(yu.x), y1 = unpack_bf16(yu.y);
-    return x0.x * y0.x + x0.y * y0.y + x1.x * y1.x + x1.y * y1.y;
-  };
-  float s = dot4(dO, ld_do, O, ld_o) - dot4(V, ld_v, dV, ld_dv);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) out[(static_cast<int64_t>(b) * H + h) * L + t] = s;
 }
 
 constexpr int kOuterSmem = 2 * kTile + kC * 4 + 64 + 1024;
@@ -921,9 +962,10 @@ at::Tensor retention_chunk_state(const at::Tensor& k, const at::Tensor& v, const
 // Backward. dout, q, k, v, gloc, states as in / from the forward; dstate_out: optional fp32 gradient of the leaving
 // state; want_dstate_in: also return dL/dS_in. dq / dk / dv: optional output views (bf16 [B, L, H, 128], head
 // stride 128). rope tables: dq and dk leave through the conjugate interleaved rotation.
-// o: optional forward output; when given, the gate gradient w.r.t. the global cumsum G is returned as well:
-// dL/dG_i = dO_i . O_i - v_i . dv_i (plus <dS_out, S_out> at the last position when dstate_out is given, which the
-// caller adds). Returns {dq, dk, dv, dstate_in or empty, dG [B, H, L] or empty}.
+// want_dgate: also return the gate gradient w.r.t. the global cumsum G, dL/dG_i = dO_i . O_i - v_i . dv_i, computed
+// inside the chunk kernel from fp32 values with the cancelling diagonal terms left out (plus <dS_out, S_out> at
+// the last position when dstate_out is given, which the caller adds). Returns {dq, dk, dv, dstate_in or empty,
+// dG [B, H, L] or empty}.
 std::vector<at::Tensor> retention_chunk_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                             const at::Tensor& v, const at::Tensor& gloc, const at::Tensor& states,
                                             const c10::optional<at::Tensor>& dstate_out, bool want_dstate_in,
@@ -931,8 +973,7 @@ std::vector<at::Tensor> retention_chunk_bwd(const at::Tensor& dout, const at::Te
                                             const c10::optional<at::Tensor>& dk_out,
                                             const c10::optional<at::Tensor>& dv_out,
                                             const c10::optional<at::Tensor>& rope_cos,
-                                            const c10::optional<at::Tensor>& rope_sin,
-                                            const c10::optional<at::Tensor>& o) {
+                                            const c10::optional<at::Tensor>& rope_sin, bool want_dgate) {
   FYB_RANGE("fyb::retention_chunk_bwd");
   const int64_t B = q.size(0), L = q.size(1), H = q.size(2);
   check_heads(q, "q", B, L, H);
@@ -958,15 +999,13 @@ std::vector<at::Tensor> retention_chunk_bwd(const at::Tensor& dout, const at::Te
     d_out = dstate_out->data_ptr<float>();
   }
   at::Tensor dg;
-  if (o.has_value() && o->defined()) {
-    check_heads(*o, "o", B, L, H);
-    dg = at::empty({B, H, L}, q.options().dtype(at::kFloat));
-  }
+  if (want_dgate) dg = at::empty({B, H, L}, q.options().dtype(at::kFloat));
   if (B == 0 || H == 0 || L == 0) {
     if (want_dstate_in) {
       if (d_out != nullptr) dstate_in.copy_(*dstate_out);
       else dstate_in.zero_();
     }
+    if (want_dgate) dg.zero_();
     return {dq, dk, dv, dstate_in, dg};
   }
   const RetParams p = make_params(B, L, H, gloc);
@@ -997,18 +1036,9 @@ std::vector<at::Tensor> retention_chunk_bwd(const at::Tensor& dout, const at::Te
   const CUtensorMap ts = tmap_states(states), tdn = tmap_states(dnext);
   BwdArgs a{reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()),
             reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()), dq.stride(1), dk.stride(1), dv.stride(1), rc, rs,
-            has_state_in ? 1 : 0, d_out != nullptr ? 1 : 0};
+            has_state_in ? 1 : 0, d_out != nullptr ? 1 : 0, want_dgate ? dg.data_ptr<float>() : nullptr};
   ret_bwd_kernel<<<B * H * p.NC, kChunkThreads, kBwdSmem, cur_stream()>>>(tq, tk, tv, tdo, ts, tdn, p, a);
   check_launch("retention_chunk_grad");
-  if (dg.defined()) {
-    const int64_t rows = B * L * H;
-    ret_dgate_kernel<<<static_cast<int>((rows * 32 + 255) / 256), 256, 0, cur_stream()>>>(
-        reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(o->data_ptr()),
-        reinterpret_cast<const __nv_bfloat16*>(v.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dv.data_ptr()),
-        dg.data_ptr<float>(), static_cast<int>(B), static_cast<int>(L), static_cast<int>(H), dout.stride(1),
-        o->stride(1), v.stride(1), dv.stride(1));
-    check_launch("retention_chunk_dgate");
-  }
   return {dq, dk, dv, dstate_in, dg};
 }
 

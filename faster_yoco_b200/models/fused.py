@@ -120,7 +120,7 @@ class SelfRetentionLayerFn(torch.autograd.Function):
             _, _, _, dg = C.retention_bwd(do.view(B, L, H, D), q, k, v, gcum, o, dqv, dkv, dvv, cos, sin)
         else:
             dg = C.retention_chunk_bwd(do.view(B, L, H, D), q, k, v, gcum, states, dq=dqv, dk=dkv, dv=dvv,
-                                       rope_cos=cos, rope_sin=sin, o=o)[4]
+                                       rope_cos=cos, rope_sin=sin, want_dgate=True)[4]
         ydg = dy[:, 4 * d:4 * d + H]
         C.gate_cumsum_bwd(dg, y[:, 4 * d:4 * d + H], ydg, float(norm))
         if R > 4 * d + H:

@@ -305,13 +305,13 @@ class _NativeChunkRetention(torch.autograd.Function):
         C = _C()
         gloc = C.retention_chunk_cumsum(g)
         o, states, _ = C.retention_chunk_fwd(q, k, v, gloc)
-        ctx.save_for_backward(q, k, v, gloc, states, o)
+        ctx.save_for_backward(q, k, v, gloc, states)
         return o
 
     @staticmethod
     def backward(ctx, do):
-        q, k, v, gloc, states, o = ctx.saved_tensors
-        dq, dk, dv, _, dG = _C().retention_chunk_bwd(do.contiguous(), q, k, v, gloc, states, o=o)
+        q, k, v, gloc, states = ctx.saved_tensors
+        dq, dk, dv, _, dG = _C().retention_chunk_bwd(do.contiguous(), q, k, v, gloc, states, want_dgate=True)
         dg = dG.flip(-1).cumsum(-1).flip(-1)
         return dq, dk, dv, dg
 

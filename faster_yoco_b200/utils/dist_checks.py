@@ -116,7 +116,9 @@ def fused_vs_nccl_gpu(rank, world, outdir, steps):
         tr.release_graph()
         torch.cuda.synchronize()
         status = int(ops._C().status()[0].item())
-        res[name] = {"losses": losses, "params": tr.flat.flat.float().cpu(), "status": status}
+        # parameters in model order (the padding of the flat buffer differs between owner maps)
+        params = torch.cat([p.detach().float().reshape(-1) for p in model.parameters()]).cpu()
+        res[name] = {"losses": losses, "params": params, "status": status}
         if tr.zero.p2p is not None:
             tr.zero.p2p.close()
     if rank == 0:

@@ -135,7 +135,7 @@ def bench_retention(results, L=2048, H=24, B=1):
                                   .contiguous())
     o, states, _ = C.retention_chunk_fwd(q, k, v, gl)
     t_cf = _time(lambda: C.retention_chunk_fwd(q, k, v, gl))
-    t_cb = _time(lambda: C.retention_chunk_bwd(do, q, k, v, gl, states, o=o))
+    t_cb = _time(lambda: C.retention_chunk_bwd(do, q, k, v, gl, states, want_dgate=True))
     nc = (L + 127) // 128
     fl_f = 4 * 2.0 * 128 ** 3 * B * H * nc
     results.append({"kernel": "retention_chunk", "L": L, "H": H, "fwd_ms": t_cf, "bwd_ms": t_cb,

@@ -2,7 +2,8 @@
 launches each). Used as:  ncu --set full --clock-control none -k regex:<kernel> -s <n> -c <m> \\
     python -m faster_yoco_b200.utils.profile_kernels --what <case>
 
-cases: attn, attn_bwd, swa, swa_bwd (sliding window 1024), ret, ret_bwd, gemm, gemm_dgrad, gemm_scatter (weight
+cases: attn, attn_bwd, swa, swa_bwd (sliding window 1024), ret, ret_bwd (parallel form), ret_chunk,
+ret_chunk_bwd (chunkwise kernels), gemm, gemm_dgrad, gemm_scatter (weight
 gradient stored at 4 emulated owners, block-cyclic map), adam, ce, ce_bwd, rms, rms_bwd, subln, subln_bwd, swiglu,
 swiglu_bwd, rope, embed, embed_bwd, reduce_compact.
 """
@@ -56,6 +57,19 @@ def main():
                 C.retention_fwd(q, k, v, g)
             else:
                 C.retention_bwd(do, q, k, v, g, o)
+    elif a.what in ("ret_chunk", "ret_chunk_bwd"):
+        q = torch.randn(1, L, 24, 128, device=dev, dtype=torch.bfloat16)
+        k = torch.randn(1, L, 24, 128, device=dev, dtype=torch.bfloat16)
+        v = torch.randn(1, L, 24, 128, device=dev, dtype=torch.bfloat16)
+        gl = C.retention_chunk_cumsum((torch.nn.functional.logsigmoid(torch.randn(1, 24, L, device=dev)) / 16)
+                                      .contiguous())
+        o, states, _ = C.retention_chunk_fwd(q, k, v, gl)
+        do = torch.randn_like(o)
+        for _ in range(a.reps):
+            if a.what == "ret_chunk":
+                C.retention_chunk_fwd(q, k, v, gl)
+            else:
+                C.retention_chunk_bwd(do, q, k, v, gl, states, want_dgate=True)
     elif a.what == "gemm":
         x = torch.randn(2048, 3072, device=dev, dtype=torch.bfloat16)
         w = torch.randn(12312, 3072, device=dev, dtype=torch.bfloat16)
