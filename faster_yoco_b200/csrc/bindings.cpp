@@ -11,9 +11,10 @@ namespace fyb {
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
           const c10::optional<at::Tensor>& R);
 void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
-               const c10::optional<at::Tensor>& R);
+               const c10::optional<at::Tensor>& R, int64_t bn, int64_t splits);
 int64_t gemm_sq(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, at::Tensor& sq_part);
 int64_t gemm_sq_slots(int64_t M, int64_t N, int64_t K);
+std::vector<int64_t> gemm_route(int64_t M, int64_t N, int64_t K);
 void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, const at::Tensor& grad_flat,
                   const at::Tensor& bases, int64_t seg, int64_t rank, int64_t chunk);
 std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps);
@@ -137,9 +138,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "faster_yoco_b200 sm_100a kernels";
   m.def("gemm", &fyb::gemm, "C = A @ B^T on tcgen05 (operands K-major or MN-major)", py::arg("A"), py::arg("B"),
         py::arg("C"), py::arg("a_mn_major"), py::arg("b_mn_major"), py::arg("residual") = py::none());
-  m.def("gemm_pair", &fyb::gemm_pair, "C = A @ B^T on CTA pairs (tcgen05.mma.cta_group::2, 256 x 256 tiles)",
+  m.def("gemm_pair", &fyb::gemm_pair, "C = A @ B^T on CTA pairs (tcgen05.mma.cta_group::2, 256 x bn tiles)",
         py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn_major"), py::arg("b_mn_major"),
-        py::arg("residual") = py::none());
+        py::arg("residual") = py::none(), py::arg("bn") = 256, py::arg("splits") = 1);
+  m.def("gemm_route", &fyb::gemm_route, "kernel choice {0 one-CTA / 1 CTA pair, splits} for an M x N x K GEMM");
   m.def("gemm_sq", &fyb::gemm_sq,
         "weight gradient dW = A^T B (bf16, optionally accumulated) with fp32 sum-of-squares partials of the stored "
         "values; returns the number of partials", py::arg("A"), py::arg("B"), py::arg("C"), py::arg("accumulate"),

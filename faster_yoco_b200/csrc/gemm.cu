@@ -490,6 +490,23 @@ Plan pick_plan(int M, int N, int K) {
 
 }  // namespace
 
+// Kernel choice for C[M, N] = A B^T with K-deep products: {kernel (0 = one-CTA, 1 = CTA pair), splits}.
+// Measured on the YOCO-3B shapes (one B200): the CTA-pair kernel (256 x 256 tiles) is faster than the one-CTA kernel
+// on every shape whose one-CTA plan needs no split-K; shapes with a K far longer than M and N (the output
+// projection's input gradient, K = 100,288) keep the one-CTA kernel's split-K plan. On the pair kernel, a K split in
+// two halves pays when the tiles fill the last round of clusters poorly (96 tiles on 74 clusters: 2 rounds of whole
+// tiles against 3 of half tiles).
+std::vector<int64_t> gemm_route(int64_t M, int64_t N, int64_t K) {
+  const Plan one = pick_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
+  if (one.splits > 1) return {0, one.splits};
+  const int64_t clusters = std::max(1, num_sms() / 2);
+  const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  const int64_t nk = (K + BK - 1) / BK;
+  const double r1 = static_cast<double>((tiles + clusters - 1) / clusters);
+  const double r2 = static_cast<double>((2 * tiles + clusters - 1) / clusters) / 2.0 * 1.10;
+  return {1, (nk >= 8 && r2 < r1) ? 2 : 1};
+}
+
 // C = A @ B^T in the operand conventions above. C: bf16 or fp32 [M, N] (any row stride); R: optional bf16 residual.
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
           const c10::optional<at::Tensor>& R) {

@@ -26,21 +26,32 @@ namespace fyb {
 namespace {
 
 constexpr int kBM = 128;        // rows of A (and of the output) per CTA
-constexpr int kBN = 256;        // output columns per tile; each CTA loads kBN / 2 rows of B
 constexpr int kBK = 64;
 constexpr int kThreads2 = 192;
-constexpr int kStages2 = 6;
 
 enum Epi2 : int { kE2Bf16 = 0, kE2Bf16Res = 1, kE2F32 = 2 };
 
+// BN: output columns per tile (256, or 128 for shapes whose 256-wide tiles leave a mostly empty last wave); each CTA
+// loads BN / 2 rows of B per K slab
+template <int BN, int STAGES>
 struct Smem2 {
   static constexpr int A_BYTES = kBM * kBK * 2;             // 16 KB
-  static constexpr int B_BYTES = (kBN / 2) * kBK * 2;       // 16 KB: this CTA's half of the B slab
+  static constexpr int B_BYTES = (BN / 2) * kBK * 2;        // this CTA's half of the B slab
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFF = kStages2 * STAGE_BYTES;
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;
+  static_assert(TOTAL <= 227 * 1024, "two-CTA GEMM shared memory above the per-CTA limit");
 };
-static_assert(Smem2::TOTAL <= 227 * 1024, "two-CTA GEMM shared memory above the per-CTA limit");
+template <int BN>
+struct PairCfg;
+template <>
+struct PairCfg<256> {
+  static constexpr int STAGES = 6;
+};
+template <>
+struct PairCfg<128> {
+  static constexpr int STAGES = 8;
+};
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -179,11 +190,13 @@ __device__ __forceinline__ void store_row32(const uint32_t (&r)[32], void* Cv, c
   }
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* Cv,
-                     const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, int* status) {
-  using S = Smem2;
+                     const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, int splits, float* ws,
+                     int* counters, int* status) {
+  constexpr int kStages2 = PairCfg<BN>::STAGES;
+  using S = Smem2<BN, kStages2>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
@@ -199,11 +212,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
   const int num_m = (M + 2 * kBM - 1) / (2 * kBM);
-  const int num_n = (N + kBN - 1) / kBN;
+  const int num_n = (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_k = (K + kBK - 1) / kBK;
-  constexpr uint32_t TMEM_COLS = 2 * kBN;
-  constexpr uint32_t IDESC = idesc_bf16(2 * kBM, kBN, A_MN, B_MN);
+  // split-K (splits = 1 or 2): work unit u = (tile u / splits, K half u % splits); the two halves of a tile are
+  // consecutive units, so they run in the same wave
+  const int num_units = num_tiles * splits;
+  const int k_chunk = (num_k + splits - 1) / splits;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t IDESC = idesc_bf16(2 * kBM, BN, A_MN, B_MN);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages2; ++s) {
@@ -234,11 +251,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int u = cluster_id; u < num_tiles && ok; u += num_clusters) {
-        const int mb = u % num_m, nb = u / num_m;
+      for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
+        const int t = u / splits;
+        const int mb = t % num_m, nb = t / num_m;
         const int m0 = mb * 2 * kBM + static_cast<int>(crank) * kBM;
-        const int n0 = nb * kBN + static_cast<int>(crank) * (kBN / 2);
-        for (int kb = 0; kb < num_k; ++kb) {
+        const int n0 = nb * BN + static_cast<int>(crank) * (BN / 2);
+        const int kb0 = (u % splits) * k_chunk, kb1 = min(num_k, kb0 + k_chunk);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, status, 21)) {
             ok = false;
             break;
@@ -257,7 +276,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
             tma_load_2d_pair(sb, &tmB, bar, kb * kBK, n0);
           } else {
 #pragma unroll
-            for (int j = 0; j < (kBN / 2) / 64; ++j) tma_load_2d_pair(sb + j * 8192, &tmB, bar, n0 + 64 * j, kb * kBK);
+            for (int j = 0; j < (BN / 2) / 64; ++j) tma_load_2d_pair(sb + j * 8192, &tmB, bar, n0 + 64 * j, kb * kBK);
           }
           if (++s == kStages2) {
             s = 0;
@@ -282,11 +301,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       int acc = 0;
       uint32_t acc_ph = 0;
       bool ok = true;
-      for (int u = cluster_id; u < num_tiles && ok; u += num_clusters) {
+      for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
         if (!mbar_wait_cluster(&tempty[acc], acc_ph ^ 1u, abort_flag, status, 23)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * kBN);
-        for (int kb = 0; kb < num_k; ++kb) {
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        const int kb0 = (u % splits) * k_chunk, kb1 = min(num_k, kb0 + k_chunk);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[s], ph, abort_flag, status, 24)) {
             ok = false;
             break;
@@ -298,7 +318,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t ad = A_MN ? sw128_desc(a0 + k * 2048, 8192, 1024) : sw128_desc(a0 + k * 32, 16, 1024);
             const uint64_t bd = B_MN ? sw128_desc(b0 + k * 2048, 8192, 1024) : sw128_desc(b0 + k * 32, 16, 1024);
-            umma_bf16_pair(d, ad, bd, IDESC, (kb != 0 || k != 0) ? 1u : 0u);
+            umma_bf16_pair(d, ad, bd, IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           // the stage may be refilled in both CTAs once these MMAs have read it
           umma_commit_pair(mapa_u32(&empty[s], 0));
@@ -320,18 +340,61 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     const int q = warp & 3;
     int acc = 0;
     uint32_t acc_ph = 0;
-    for (int u = cluster_id; u < num_tiles; u += num_clusters) {
-      const int mb = u % num_m, nb = u / num_m;
+    for (int u = cluster_id; u < num_units; u += num_clusters) {
+      const int t = u / splits;
+      const int mb = t % num_m, nb = t / num_m;
       if (!mbar_wait(&tfull[acc], acc_ph, abort_flag, status, 25)) break;
       tc_fence_after();
       const int row = mb * 2 * kBM + static_cast<int>(crank) * kBM + q * 32 + lane;
-      const uint32_t tb = tmem_base + static_cast<uint32_t>(acc * kBN) + (static_cast<uint32_t>(q * 32) << 16);
+      const uint32_t tb = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+      bool last = true;
+      const float* other = nullptr;
+      if (splits == 2) {
+        // publish this K half's partial (this warp's 32 rows x BN, fp32), then count the warp's arrival for the
+        // tile: the second of the two arrivals adds the first's partial and stores. a + b == b + a, so the
+        // result does not depend on which half arrives last
+        const int64_t lrow = (static_cast<int64_t>(u) * 2 + crank) * kBM + q * 32 + lane;
+        float* mine = ws + lrow * BN;
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tb + c * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(mine + c * 32 + j) = make_float4(
+                __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+        }
+        __threadfence();
+        __syncwarp();
+        int* cnt = counters + (static_cast<int64_t>(t) * 2 + crank) * 4 + q;
+        int prev = 0;
+        if (lane == 0) prev = atomicAdd(cnt, 1);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        last = prev == 1;
+        if (last) {
+          __threadfence();
+          if (lane == 0) *cnt = 0;                   // ready for the next GEMM that uses these counters
+          const int64_t orow = (static_cast<int64_t>(u ^ 1) * 2 + crank) * kBM + q * 32 + lane;
+          other = ws + orow * BN;
+        }
+      }
+#pragma unroll 1
+      for (int c = 0; last && c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tb + c * 32, r);        // warp-collective: every lane, whatever its row
         tmem_ld_wait();
-        const int col = nb * kBN + c * 32;
+        if (other != nullptr) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 o = *reinterpret_cast<const float4*>(other + c * 32 + j);
+            r[j] = __float_as_uint(__uint_as_float(r[j]) + o.x);
+            r[j + 1] = __float_as_uint(__uint_as_float(r[j + 1]) + o.y);
+            r[j + 2] = __float_as_uint(__uint_as_float(r[j + 2]) + o.z);
+            r[j + 3] = __float_as_uint(__uint_as_float(r[j + 3]) + o.w);
+          }
+        }
+        const int col = nb * BN + c * 32;
         if (row < M && col < N) store_row32<EPI>(r, Cv, R, row, col, N, ldc, ldr);
       }
       tc_fence_before();
@@ -350,35 +413,75 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   }
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+struct PairArgs {
+  int splits;
+  float* ws;
+  int* counters;
+};
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
 void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const __nv_bfloat16* R, int M, int N, int K,
-                 int64_t ldc, int64_t ldr, cudaStream_t stream) {
-  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
+                 int64_t ldc, int64_t ldr, const PairArgs& pa, cudaStream_t stream) {
+  using S = Smem2<BN, PairCfg<BN>::STAGES>;
+  auto kern = gemm_pair_kernel<BN, A_MN, B_MN, EPI>;
   static bool attr_set = false;
   if (!attr_set) {
-    FYB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem2::TOTAL));
+    FYB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
     attr_set = true;
   }
-  const int tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN - 1) / kBN);
-  const int clusters = std::max(1, std::min(tiles, num_sms() / 2));
-  kern<<<2 * clusters, kThreads2, Smem2::TOTAL, stream>>>(ta, tb, C, R, M, N, K, ldc, ldr, status_ptr());
+  const int units = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + BN - 1) / BN) * pa.splits;
+  const int clusters = std::max(1, std::min(units, num_sms() / 2));
+  kern<<<2 * clusters, kThreads2, S::TOTAL, stream>>>(ta, tb, C, R, M, N, K, ldc, ldr, pa.splits, pa.ws,
+                                                      pa.counters, status_ptr());
   check_launch("gemm_pair");
 }
 
-template <int EPI>
+template <int BN, int EPI>
 void dispatch_pair(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, void* C,
-                   const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, cudaStream_t st) {
-  if (!a_mn && !b_mn) launch_pair<false, false, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
-  else if (!a_mn && b_mn) launch_pair<false, true, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
-  else if (a_mn && b_mn) launch_pair<true, true, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
-  else launch_pair<true, false, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, st);
+                   const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, const PairArgs& pa,
+                   cudaStream_t st) {
+  if (!a_mn && !b_mn) launch_pair<BN, false, false, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, pa, st);
+  else if (!a_mn && b_mn) launch_pair<BN, false, true, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, pa, st);
+  else if (a_mn && b_mn) launch_pair<BN, true, true, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, pa, st);
+  else launch_pair<BN, true, false, EPI>(ta, tb, C, R, M, N, K, ldc, ldr, pa, st);
+}
+
+template <int EPI>
+void dispatch_pair_bn(int bn, bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, void* C,
+                      const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, const PairArgs& pa,
+                      cudaStream_t st) {
+  if (bn == 256) dispatch_pair<256, EPI>(a_mn, b_mn, ta, tb, C, R, M, N, K, ldc, ldr, pa, st);
+  else dispatch_pair<128, EPI>(a_mn, b_mn, ta, tb, C, R, M, N, K, ldc, ldr, pa, st);
+}
+
+// Arrival counters of the split-K epilogue, one per (tile, CTA of the pair, epilogue warp): zeroed once per device
+// and left zero by every GEMM (the second arrival resets its counter), so one buffer serves every call on the
+// stream. Sized for 16 Ki tiles.
+constexpr int kMaxPairTiles = 16384;
+int* pair_counters() {
+  static int* ptr[64] = {nullptr};
+  int dev = 0;
+  FYB_CUDA(cudaGetDevice(&dev));
+  FYB_CHECK(dev >= 0 && dev < 64, "gemm_pair: device index out of range");
+  if (ptr[dev] == nullptr) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    FYB_CUDA(cudaStreamIsCapturing(cur_stream(), &cs));
+    FYB_CHECK(cs == cudaStreamCaptureStatusNone,
+              "gemm_pair: the first split-K GEMM on a device must run before any stream capture");
+    FYB_CUDA(cudaMalloc(&ptr[dev], sizeof(int) * kMaxPairTiles * 8));
+    FYB_CUDA(cudaMemset(ptr[dev], 0, sizeof(int) * kMaxPairTiles * 8));
+    FYB_CUDA(cudaDeviceSynchronize());
+  }
+  return ptr[dev];
 }
 
 }  // namespace
 
-// C = A @ B^T on CTA pairs (operand conventions as gemm()); no split-K. C: bf16 or fp32 [M, N]; R: bf16 residual.
+// C = A @ B^T on CTA pairs (operand conventions as gemm()). C: bf16 or fp32 [M, N]; R: bf16 residual.
+// bn: output tile width, 256 or 128; splits: 1, or 2 (each tile's K range in two halves on two pairs, summed by the
+// epilogue of the later one; the fp32 workspace is allocated here).
 void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
-               const c10::optional<at::Tensor>& R) {
+               const c10::optional<at::Tensor>& R, int64_t bn, int64_t splits) {
   FYB_RANGE("fyb::gemm_pair");
   FYB_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "gemm_pair: CUDA tensors expected");
   FYB_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm_pair: bf16 operands expected");
@@ -403,19 +506,33 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_m
     Rp = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr());
     ldr = R->stride(0);
   }
+  FYB_CHECK(bn == 256 || bn == 128, "gemm_pair: tile width must be 256 or 128");
+  FYB_CHECK(splits == 1 || splits == 2, "gemm_pair: splits must be 1 or 2");
   if (M == 0 || N == 0) return;
   c10::cuda::CUDAGuard guard(A.device());
   cudaStream_t st = cur_stream();
+  const int64_t tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + bn - 1) / bn);
+  const int64_t num_k = (K + kBK - 1) / kBK;
+  PairArgs pa{static_cast<int>(splits), nullptr, nullptr};
+  at::Tensor ws;
+  if (splits == 2) {
+    FYB_CHECK(num_k >= 2, "gemm_pair: split-K needs at least two K blocks");
+    FYB_CHECK(tiles <= kMaxPairTiles, "gemm_pair: too many tiles for split-K");
+    ws = at::empty({tiles * 2 * 2 * kBM, bn}, A.options().dtype(at::kFloat));
+    pa.ws = ws.data_ptr<float>();
+    pa.counters = pair_counters();
+  }
   const CUtensorMap ta = a_mn ? make_tmap_2d(A.data_ptr(), K, M, A.stride(0), 64)
                               : make_tmap_2d(A.data_ptr(), M, K, A.stride(0), kBM);
   const CUtensorMap tb = b_mn ? make_tmap_2d(B.data_ptr(), K, N, B.stride(0), 64)
-                              : make_tmap_2d(B.data_ptr(), N, K, B.stride(0), kBN / 2);
+                              : make_tmap_2d(B.data_ptr(), N, K, B.stride(0), static_cast<int>(bn / 2));
   void* Cp = C.data_ptr();
   const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
   const int64_t ldc = C.stride(0);
-  if (f32) dispatch_pair<kE2F32>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
-  else if (Rp != nullptr) dispatch_pair<kE2Bf16Res>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
-  else dispatch_pair<kE2Bf16>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, st);
+  const int b = static_cast<int>(bn);
+  if (f32) dispatch_pair_bn<kE2F32>(b, a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, pa, st);
+  else if (Rp != nullptr) dispatch_pair_bn<kE2Bf16Res>(b, a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, pa, st);
+  else dispatch_pair_bn<kE2Bf16>(b, a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, pa, st);
 }
 
 }  // namespace fyb

@@ -96,13 +96,26 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn_major: bool = False, b_mn_maj
     N = b.shape[1] if b_mn_major else b.shape[0]
     if out is None:
         out = torch.empty(M, N, dtype=out_dtype or a.dtype, device=a.device)
-    if _GEMM_PAIR and ((M + 255) // 256) * ((N + 255) // 256) >= 64:
-        # opt-in: CTA-pair kernel (256 x 256 tiles) for shapes with at least about a wave of tiles; the skinny
-        # shapes that need split-K stay on the one-CTA kernel
-        _C().gemm_pair(a, b, out, a_mn_major, b_mn_major, residual)
+    K = a.shape[0] if a_mn_major else a.shape[1]
+    route = _gemm_route(M, N, K) if _GEMM_PAIR else (0, 1)
+    if route[0] == 1:
+        _C().gemm_pair(a, b, out, a_mn_major, b_mn_major, residual, 256, route[1])
     else:
         _C().gemm(a, b, out, a_mn_major, b_mn_major, residual)
     return out
+
+
+_ROUTES = {}
+
+
+def _gemm_route(M: int, N: int, K: int):
+    """(kernel, splits) for the shape: the CTA-pair kernel unless the one-CTA kernel's plan needs split-K (cached per
+    shape; csrc/gemm.cu::gemm_route)."""
+    key = (M, N, K)
+    r = _ROUTES.get(key)
+    if r is None:
+        r = _ROUTES[key] = tuple(_C().gemm_route(M, N, K))
+    return r
 
 
 class _NativeLinear(torch.autograd.Function):

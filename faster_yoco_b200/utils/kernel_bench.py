@@ -63,10 +63,15 @@ def bench_gemm(results, pair_too: bool = False):
             it[0] += 1
             ops._C().gemm(a, b, c, a_mn, b_mn, None)
 
-        def pair():
+        def pair(bn=256, splits=1):
             a, b = pool[it[0] % len(pool)]
             it[0] += 1
-            ops._C().gemm_pair(a, b, c, a_mn, b_mn, None)
+            ops._C().gemm_pair(a, b, c, a_mn, b_mn, None, bn, splits)
+
+        def routed():
+            a, b = pool[it[0] % len(pool)]
+            it[0] += 1
+            ops.gemm(a, b, a_mn_major=a_mn, b_mn_major=b_mn, out=c)
 
         def cublas():
             a, b = pool[it[0] % len(pool)]
@@ -81,7 +86,12 @@ def bench_gemm(results, pair_too: bool = False):
              "ours_tflops": fl / t_ours / 1e9, "cublas_tflops": fl / t_cub / 1e9}
         if pair_too:
             t_pair = _time(pair)
-            r.update(pair_ms=t_pair, pair_tflops=fl / t_pair / 1e9)
+            t_pair2 = _time(lambda: pair(256, 2)) if K >= 128 else float("nan")
+            r.update(pair_ms=t_pair, pair_tflops=fl / t_pair / 1e9, pair_split2_ms=t_pair2,
+                     pair_split2_tflops=fl / t_pair2 / 1e9)
+        t_routed = _time(routed)
+        r.update(routed_ms=t_routed, routed_tflops=fl / t_routed / 1e9,
+                 route=list(ops._gemm_route(M, N, K)))
         results.append(r)
 
 

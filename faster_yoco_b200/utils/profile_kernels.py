@@ -5,7 +5,8 @@ launches each). Used as:  ncu --set full --clock-control none -k regex:<kernel> 
 cases: attn, attn_bwd, swa, swa_bwd (sliding window 1024), ret, ret_bwd (parallel form), ret_chunk,
 ret_chunk_bwd (chunkwise kernels), gemm, gemm_dgrad, gemm_scatter (weight
 gradient stored at 4 emulated owners, block-cyclic map), adam, ce, ce_bwd, rms, rms_bwd, subln, subln_bwd, swiglu,
-swiglu_bwd, rope, embed, embed_bwd, reduce_compact.
+swiglu_bwd, rope, embed, embed_bwd, reduce_compact, reduce_owner, adam_push (eight ranks emulated in local memory),
+gate_cumsum (chunk-local), gemm_pair, gemm_pair128.
 """
 import argparse
 
@@ -166,6 +167,40 @@ def main():
                 C.gemm_scatter(dy, x, slot, False, grad, bases, seg, rank, chunk)
             else:
                 C.reduce_compact(grad, staging[rank], seg, world, rank, seg, chunk, part, 296)
+    elif a.what in ("reduce_owner", "adam_push"):
+        # eight ranks emulated in this GPU's memory (the kernels only see addresses), contiguous owner segments:
+        # rank 2's reduce-to-owner of a 16 Mi-element segment over 8 gradient buffers (fp32 rank-order sum), and
+        # its Adam step fused with the push of the new bf16 values into the 8 parameter buffers
+        world, rank, seg = 8, 2, 1 << 24
+        n = world * seg
+        if a.what == "reduce_owner":
+            grads = [torch.randn(n, device=dev).to(torch.bfloat16) for _ in range(world)]
+            ptrs = [t.data_ptr() for t in grads]
+            part = torch.zeros(296, device=dev)
+            sq = torch.zeros(1, device=dev)
+            for _ in range(a.reps):
+                C.reduce_owner(ptrs, grads[rank], rank * seg, seg, part, sq, 0, rank)
+        else:
+            p32 = torch.randn(seg, device=dev)
+            m = torch.zeros(seg, device=dev)
+            v = torch.zeros(seg, device=dev)
+            g16 = torch.randn(seg, device=dev).to(torch.bfloat16)
+            pb = [torch.zeros(n, dtype=torch.bfloat16, device=dev) for _ in range(world)]
+            hyper = torch.tensor([1e-4, 0.1, 0.001, 1.0], device=dev)
+            factor = torch.tensor([1.0], device=dev)
+            for _ in range(a.reps):
+                C.adam_push(p32, g16, m, v, pb[rank][rank * seg:(rank + 1) * seg], hyper, factor, 0.9, 0.95, 1e-6,
+                            0.05, True, [t.data_ptr() for t in pb], rank * seg, rank, 0)
+    elif a.what == "gate_cumsum":
+        y = torch.randn(2048, 12312, device=dev, dtype=torch.bfloat16)
+        for _ in range(a.reps):
+            C.gate_cumsum_fwd(y[:, 4 * 3072:4 * 3072 + 24], 1, 2048, 16.0, True)
+    elif a.what in ("gemm_pair", "gemm_pair128"):
+        x = torch.randn(2048, 3072, device=dev, dtype=torch.bfloat16)
+        w = torch.randn(16384, 3072, device=dev, dtype=torch.bfloat16)
+        y = torch.empty(2048, 16384, device=dev, dtype=torch.bfloat16)
+        for _ in range(a.reps):
+            C.gemm_pair(x, w, y, False, False, None, 128 if a.what == "gemm_pair128" else 256)
     else:
         raise SystemExit(f"unknown --what {a.what}")
     torch.cuda.synchronize()

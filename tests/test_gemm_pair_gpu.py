@@ -1,6 +1,7 @@
 """The CTA-pair GEMM (tcgen05.mma.cta_group::2, 256 x 256 tiles over two CTAs, gemm2.cu) against the one-CTA GEMM
 and an fp32 PyTorch oracle: every operand layout (forward, input gradient, weight gradient), M / N / K tails, the
-residual epilogue and fp32 output, two calls in a row."""
+residual epilogue and fp32 output, 256- and 128-wide tiles, whole-K and two-way split-K (the later half's epilogue
+adds the earlier half's partial), two calls in a row."""
 import pytest
 import torch
 
@@ -38,7 +39,8 @@ def _close_in_ulps(x, y, ulps, acc_mag=None):
     (520, 300, 136, True, False),
 ])
 @pytest.mark.parametrize("epi", ["bf16", "res", "f32"])
-def test_gemm_pair_matches_one_cta_and_fp32(M, N, K, a_mn, b_mn, epi):
+@pytest.mark.parametrize("bn,splits", [(256, 1), (128, 1), (256, 2), (128, 2)])
+def test_gemm_pair_matches_one_cta_and_fp32(M, N, K, a_mn, b_mn, epi, bn, splits):
     C = ops._C()
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
     a, b = _operands(M, N, K, a_mn, b_mn, g)
@@ -52,7 +54,7 @@ def test_gemm_pair_matches_one_cta_and_fp32(M, N, K, a_mn, b_mn, epi):
     prod = A32 @ B32
     for _ in range(2):
         pair = torch.full((M, N), float("nan"), dtype=dt, device=dev)
-        C.gemm_pair(a, b, pair, a_mn, b_mn, res)
+        C.gemm_pair(a, b, pair, a_mn, b_mn, res, bn, splits)
         torch.cuda.synchronize()
         assert int(C.status()[0].item()) == 0
         assert not bool(torch.isnan(pair.float()).any()), "unwritten output"
