@@ -42,6 +42,7 @@ void adam_push(at::Tensor& p32, const at::Tensor& g16, at::Tensor& m, at::Tensor
                const at::Tensor& hyper, const at::Tensor& factor, double b1, double b2, double eps, double wd,
                bool adamw, const std::vector<int64_t>& peer_params, int64_t peer_off, int64_t rank, int64_t chunk);
 at::Tensor sq_norm(const at::Tensor& x);
+at::Tensor sq_norm_ranges(const at::Tensor& x, const at::Tensor& chunks);
 std::vector<at::Tensor> attention_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, bool causal,
                                       int64_t window, double scale);
 std::vector<at::Tensor> attention_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
@@ -141,7 +142,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pair", &fyb::gemm_pair, "C = A @ B^T on CTA pairs (tcgen05.mma.cta_group::2, 256 x bn tiles)",
         py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn_major"), py::arg("b_mn_major"),
         py::arg("residual") = py::none(), py::arg("bn") = 256, py::arg("splits") = 1);
-  m.def("gemm_route", &fyb::gemm_route, "kernel choice {0 one-CTA / 1 CTA pair, splits} for an M x N x K GEMM");
+  m.def("gemm_route", &fyb::gemm_route, "kernel choice {0 one-CTA / 1 CTA pair, tile width, splits} for an M x N x K GEMM");
   m.def("gemm_sq", &fyb::gemm_sq,
         "weight gradient dW = A^T B (bf16, optionally accumulated) with fp32 sum-of-squares partials of the stored "
         "values; returns the number of partials", py::arg("A"), py::arg("B"), py::arg("C"), py::arg("accumulate"),
@@ -179,6 +180,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("p32"), py::arg("g16"), py::arg("m"), py::arg("v"), py::arg("p16"), py::arg("hyper"),
         py::arg("factor"), py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"), py::arg("adamw"),
         py::arg("peer_params"), py::arg("peer_off"), py::arg("rank"), py::arg("chunk") = 0);
+  m.def("sq_norm_ranges", &fyb::sq_norm_ranges, "sum of squares over chunks [n, 2] (start, len <= 65536) of a bf16 buffer");
   m.def("sq_norm", &fyb::sq_norm);
   m.def("attention_fwd", &fyb::attention_fwd);
   m.def("attention_bwd", &fyb::attention_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),

@@ -33,18 +33,18 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
       make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]), pack_bf16(f[6], f[7]));
 }
 
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// sigmoid with the hardware reciprocal (__frcp_rn: one correctly rounded reciprocal instead of a full division)
+__device__ __forceinline__ float sigmoidf_(float x) { return __frcp_rn(1.0f + __expf(-x)); }
 
 // ------------------------------------------------------------------------------------------------------------------
 // SwiGLU on [M, N] views with row strides (N % 8 == 0)
 
+// grid: (rows, column blocks of 8 x blockDim values); no integer division per thread
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ y,
                                   int64_t ldy, __nv_bfloat16* __restrict__ out, int64_t M, int N) {
-  const int per_row = N / 8;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= M * per_row) return;
-  const int64_t r = i / per_row;
-  const int c = static_cast<int>(i % per_row) * 8;
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (c >= N) return;
+  const int64_t r = blockIdx.x;
   float a[8], b[8], o[8];
   load8(x + r * ldx + c, a);
   load8(y + r * ldy + c, b);
@@ -56,11 +56,9 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t l
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ y,
                                   int64_t ldy, const __nv_bfloat16* __restrict__ g, __nv_bfloat16* __restrict__ dx,
                                   __nv_bfloat16* __restrict__ dy, int64_t M, int N, int64_t lddx, int64_t lddy) {
-  const int per_row = N / 8;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= M * per_row) return;
-  const int64_t r = i / per_row;
-  const int c = static_cast<int>(i % per_row) * 8;
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (c >= N) return;
+  const int64_t r = blockIdx.x;
   float a[8], b[8], gg[8], da[8], db[8];
   load8(x + r * ldx + c, a);
   load8(y + r * ldy + c, b);
@@ -78,32 +76,30 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t l
 // ------------------------------------------------------------------------------------------------------------------
 // rotary embedding, interleaved pairs. x: [B, L, H, D] strided (last dim contiguous); out contiguous.
 
+// one block per token (b * L + l); its threads walk the (head, 8-value chunk) items; per = D / 8 is a power of two
 __global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, int64_t sb, int64_t sl, int64_t sh,
                             const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t,
                             __nv_bfloat16* __restrict__ out, int B, int L, int H, int D, float sign) {
   const int per = D / 8;
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t total = static_cast<int64_t>(B) * L * H * per;
-  if (i >= total) return;
-  const int c8 = static_cast<int>(i % per) * 8;
-  int64_t rest = i / per;
-  const int h = static_cast<int>(rest % H);
-  rest /= H;
-  const int l = static_cast<int>(rest % L);
-  const int b = static_cast<int>(rest / L);
-  float f[8], o[8];
-  load8(x + b * sb + l * sl + h * sh + c8, f);
-  const __nv_bfloat16* cp = cos_t + static_cast<int64_t>(l) * (D / 2) + c8 / 2;
-  const __nv_bfloat16* spp = sin_t + static_cast<int64_t>(l) * (D / 2) + c8 / 2;
+  const int l = static_cast<int>(blockIdx.x % static_cast<unsigned>(L));
+  const int b = static_cast<int>(blockIdx.x / static_cast<unsigned>(L));
+  for (int j = threadIdx.x; j < H * per; j += blockDim.x) {
+    const int c8 = (j & (per - 1)) * 8;
+    const int h = j / per;
+    float f[8], o[8];
+    load8(x + b * sb + l * sl + h * sh + c8, f);
+    const __nv_bfloat16* cp = cos_t + static_cast<int64_t>(l) * (D / 2) + c8 / 2;
+    const __nv_bfloat16* spp = sin_t + static_cast<int64_t>(l) * (D / 2) + c8 / 2;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float cs = __bfloat162float(cp[k]);
-    const float sn = sign * __bfloat162float(spp[k]);
-    const float x0 = f[2 * k], x1 = f[2 * k + 1];
-    o[2 * k] = x0 * cs - x1 * sn;
-    o[2 * k + 1] = x0 * sn + x1 * cs;
+    for (int k = 0; k < 4; ++k) {
+      const float cs = __bfloat162float(cp[k]);
+      const float sn = sign * __bfloat162float(spp[k]);
+      const float x0 = f[2 * k], x1 = f[2 * k + 1];
+      o[2 * k] = x0 * cs - x1 * sn;
+      o[2 * k + 1] = x0 * sn + x1 * cs;
+    }
+    store8(out + ((static_cast<int64_t>(b) * L + l) * H + h) * D + c8, o);
   }
-  store8(out + ((static_cast<int64_t>(b) * L + l) * H + h) * D + c8, o);
 }
 
 // NeoX / non-interleaved rotary: pairs (x[i], x[i + D/2]); each thread rotates 8 pairs.
@@ -471,6 +467,43 @@ __global__ void sq_partial_kernel(const __nv_bfloat16* __restrict__ x, int64_t n
   }
 }
 
+// Sum of squares over many ranges of one bf16 buffer in one launch: block i sums chunk i ([start, start + len),
+// len <= 65,536, any alignment) into part[i]; the caller sums the partials in order (deterministic).
+__global__ void sq_ranges_kernel(const __nv_bfloat16* __restrict__ x, const int64_t* __restrict__ chunks,
+                                 float* __restrict__ part) {
+  const int64_t start = chunks[2 * blockIdx.x], len = chunks[2 * blockIdx.x + 1];
+  const __nv_bfloat16* p = x + start;
+  // scalar head up to a 16-byte boundary, then 8-wide loads, then a scalar tail
+  const int64_t mis = static_cast<int64_t>(((16 - (reinterpret_cast<uintptr_t>(p) & 15)) & 15) / 2);
+  const int64_t head = len < mis ? len : mis;
+  float s = 0.f;
+  for (int64_t j = threadIdx.x; j < head; j += blockDim.x) {
+    const float f = __bfloat162float(p[j]);
+    s += f * f;
+  }
+  const int64_t nvec = (len - head) / 8;
+  for (int64_t v = threadIdx.x; v < nvec; v += blockDim.x) {
+    float f[8];
+    load8(p + head + 8 * v, f);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += f[k] * f[k];
+  }
+  for (int64_t j = head + 8 * nvec + threadIdx.x; j < len; j += blockDim.x) {
+    const float f = __bfloat162float(p[j]);
+    s += f * f;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+    part[blockIdx.x] = t;
+  }
+}
+
 __global__ void sq_final_kernel(const float* __restrict__ part, int P, float* __restrict__ out) {
   __shared__ float red[1024];
   float s = 0.f;
@@ -655,7 +688,8 @@ at::Tensor swiglu_fwd(const at::Tensor& x, const at::Tensor& y) {
   auto out = at::empty({M, N}, x.options());
   const int64_t n = M * (N / 8);
   if (n > 0)
-    swiglu_fwd_kernel<<<(n + 255) / 256, 256, 0, cur_stream()>>>(
+    swiglu_fwd_kernel<<<dim3(static_cast<unsigned>(M), static_cast<unsigned>((N / 8 + 127) / 128)), 128, 0,
+                        cur_stream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
         reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
         reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), M, (int)N);
@@ -681,7 +715,8 @@ std::vector<at::Tensor> swiglu_bwd(const at::Tensor& x, const at::Tensor& y, con
   auto dy = pick(dy_out);
   const int64_t n = M * (N / 8);
   if (n > 0)
-    swiglu_bwd_kernel<<<(n + 255) / 256, 256, 0, cur_stream()>>>(
+    swiglu_bwd_kernel<<<dim3(static_cast<unsigned>(M), static_cast<unsigned>((N / 8 + 127) / 128)), 128, 0,
+                        cur_stream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
         reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
         reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()),
@@ -714,9 +749,10 @@ at::Tensor rope_fwd(const at::Tensor& x, const at::Tensor& cos_t, const at::Tens
     check_launch("rope_neox");
     return out;
   }
-  const int64_t n = static_cast<int64_t>(B) * L * H * (D / 8);
-  if (n > 0)
-    rope_kernel<<<(n + 255) / 256, 256, 0, cur_stream()>>>(
+  FYB_CHECK(((D / 8) & (D / 8 - 1)) == 0, "rope: head dim / 8 must be a power of two");
+  const int64_t n = static_cast<int64_t>(B) * L;
+  if (n > 0 && H > 0)
+    rope_kernel<<<static_cast<unsigned>(n), 128, 0, cur_stream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), x.stride(1), x.stride(2),
         reinterpret_cast<const __nv_bfloat16*>(cos_t.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(sin_t.data_ptr()),
         reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), B, L, H, D, conj ? -1.f : 1.f);
@@ -935,6 +971,28 @@ void sq_norm_into(const at::Tensor& x, float* part, int P, float* out) {
   check_launch("sq_partial");
   sq_final_kernel<<<1, 1024, 0, cur_stream()>>>(part, P, out);
   check_launch("sq_final");
+}
+
+// Sum of squares of x over the chunks [n, 2] (start, length <= 65,536) of a bf16 buffer: one launch for the partials
+// and one for their ordered sum. Returns fp32 [1].
+at::Tensor sq_norm_ranges(const at::Tensor& x, const at::Tensor& chunks) {
+  FYB_RANGE("fyb::sq_norm_ranges");
+  FYB_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "sq_norm_ranges: bf16 buffer");
+  FYB_CHECK(chunks.is_cuda() && chunks.scalar_type() == at::kLong && chunks.is_contiguous() && chunks.dim() == 2 &&
+                chunks.size(1) == 2,
+            "sq_norm_ranges: chunks must be int64 [n, 2] on the device");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t n = chunks.size(0);
+  auto out = at::zeros({1}, x.options().dtype(at::kFloat));
+  if (n == 0) return out;
+  FYB_CHECK(n < (1ll << 31), "sq_norm_ranges: too many chunks");
+  auto part = at::empty({n}, x.options().dtype(at::kFloat));
+  sq_ranges_kernel<<<static_cast<unsigned>(n), 256, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), chunks.data_ptr<int64_t>(), part.data_ptr<float>());
+  check_launch("sq_ranges");
+  sq_final_kernel<<<1, 1024, 0, cur_stream()>>>(part.data_ptr<float>(), static_cast<int>(n), out.data_ptr<float>());
+  check_launch("sq_final");
+  return out;
 }
 
 at::Tensor sq_norm(const at::Tensor& x) {

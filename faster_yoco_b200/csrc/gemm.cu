@@ -84,7 +84,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // split-K: work unit u = (tile u / splits, K slice u % splits); slices write fp32 partials to ws[slice, M, N]
   const int num_units = num_tiles * splits;
   const int k_chunk = (num_k + splits - 1) / splits;
-  constexpr uint32_t TMEM_COLS = 2 * BN;
+  // accumulator buffers at a power-of-two column stride (BN = 192 uses columns [0, 192) and [256, 448))
+  constexpr uint32_t ACC_STRIDE = BN <= 128 ? 128u : 256u;
+  constexpr uint32_t TMEM_COLS = 2 * ACC_STRIDE;
   constexpr uint32_t IDESC = idesc_bf16(BM, BN, A_MN, B_MN);
 
   if (threadIdx.x == 0) {
@@ -166,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
         if (!mbar_wait(&tempty[acc], acc_ph ^ 1u, abort_flag, status, 2)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc) * ACC_STRIDE;
         const int kb0 = (u % splits) * k_chunk, kb1 = min(num_k, kb0 + k_chunk);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[s], ph, abort_flag, status, 3)) {
@@ -207,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       float ss = 0.f;                       // sum of squares of this thread's stored values (epi_sq)
       const int row = mb * BM + q * 32 + lane;
-      const uint32_t tb = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+      const uint32_t tb = tmem_base + static_cast<uint32_t>(acc) * ACC_STRIDE + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -458,31 +460,37 @@ void dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorM
 
 struct Plan {
   int bn, splits;
+  double cost;
 };
 
 // Tile width and split-K factor: minimise (waves x per-unit work) + the fp32 split reduction, in tile-k-block
-// units. A unit of a BN-wide tile over kc k-blocks costs ~ BN * kc; the last partial wave costs a full wave.
+// units. A unit of a BN-wide tile over kc k-blocks costs ~ BN * kc (narrower tiles a little more per column: more
+// operand traffic per FLOP); the last partial wave costs a full wave. The 192-wide tile exists for the 3,072-wide
+// outputs at M = 2,048: 16 x 16 = 256 tiles fill two waves of 148 SMs, where 256-wide tiles leave the second wave
+// 30 % full.
 Plan pick_plan(int M, int N, int K) {
   const int sms = num_sms();
   const int tm = (M + BM - 1) / BM;
   const int nk = (K + BK - 1) / BK;
-  Plan best{256, 1};
-  double best_cost = 1e30;
-  for (int bn : {256, 128}) {
+  Plan best{256, 1, 1e30};
+  // three or more K slices only where the tiles alone leave most SMs idle or K dwarfs the output (measured: on the
+  // 3,072-wide outputs at M = 2,048 the fp32 partials of a 3-way split cost more than its balance gains)
+  const long tiles256 = static_cast<long>(tm) * ((N + 255) / 256);
+  const bool deep_split = 2 * tiles256 < sms || static_cast<long>(K) > 8l * std::max(M, N);
+  for (int bn : {256, 192, 128}) {
     const long tiles = static_cast<long>(tm) * ((N + bn - 1) / bn);
     for (int sp : {1, 2, 3, 4, 6, 8}) {
       if (sp > 1 && nk / sp < 8) break;                  // keep at least 8 k-blocks per slice
+      if (sp > 2 && !deep_split) break;
       const long units = tiles * sp;
       const long waves = (units + sms - 1) / sms;
       const int kc = (nk + sp - 1) / sp;
-      double cost = static_cast<double>(waves) * bn * kc * (bn == 128 ? 1.15 : 1.0);   // narrow tiles: more traffic
+      const double width = bn == 256 ? 1.0 : (bn == 192 ? 1.10 : 1.25);
+      double cost = static_cast<double>(waves) * bn * kc * width;
       // fp32 partials written and re-read once: ~ M*N*(sp+1)*4 bytes at HBM speed, in the same units
       // (one BN=256 k-block of one SM ~ 512 tensor cycles ~ 2 units per cycle)
       if (sp > 1) cost += static_cast<double>(M) * N * (sp + 1) * 6.0e-4;
-      if (cost < best_cost * 0.97) {
-        best_cost = cost;
-        best = Plan{bn, sp};
-      }
+      if (cost < best.cost * 0.97) best = Plan{bn, sp, cost};
     }
   }
   return best;
@@ -490,21 +498,34 @@ Plan pick_plan(int M, int N, int K) {
 
 }  // namespace
 
-// Kernel choice for C[M, N] = A B^T with K-deep products: {kernel (0 = one-CTA, 1 = CTA pair), splits}.
-// Measured on the YOCO-3B shapes (one B200): the CTA-pair kernel (256 x 256 tiles) is faster than the one-CTA kernel
-// on every shape whose one-CTA plan needs no split-K; shapes with a K far longer than M and N (the output
-// projection's input gradient, K = 100,288) keep the one-CTA kernel's split-K plan. On the pair kernel, a K split in
-// two halves pays when the tiles fill the last round of clusters poorly (96 tiles on 74 clusters: 2 rounds of whole
-// tiles against 3 of half tiles).
+// Kernel choice for C[M, N] = A B^T with K-deep products: {kernel (0 = one-CTA, 1 = CTA pair), tile width, splits}, by the
+// cost model of pick_plan (waves x tile width x K blocks) for both kernels. Measured on the YOCO-3B shapes (one
+// B200): the pair kernel with 256-wide tiles where they fill the rounds well (QKVG, fc1 / gate forward, fc2's input
+// gradient, the output projection's forward, the weight gradients); the one-CTA kernel with 192-wide tiles for the
+// 3,072-wide outputs at M = 2,048 (256 tiles in two waves of 148 SMs, where 256-wide ones leave the second wave 30 %
+// full); the output projection's input gradient (K = 100,288) on the one-CTA kernel's split-K plan. The pair
+// kernel's 192-wide tiles and its two-way split-K are not routed to: both measured slower on these shapes.
 std::vector<int64_t> gemm_route(int64_t M, int64_t N, int64_t K) {
   const Plan one = pick_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
-  if (one.splits > 1) return {0, one.splits};
+  // a K several times longer than the output needs the one-CTA kernel's split-K (no pair plan comes close)
+  if (one.splits > 2) return {0, one.bn, one.splits};
+  // the pair kernel's 256 x 256 tile = two one-CTA 128 x 256 tiles per round of clusters, at ~0.90 of the one-CTA
+  // kernel's time per unit (measured on the YOCO-3B shapes: half the B operand traffic per SM)
   const int64_t clusters = std::max(1, num_sms() / 2);
-  const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
   const int64_t nk = (K + BK - 1) / BK;
-  const double r1 = static_cast<double>((tiles + clusters - 1) / clusters);
-  const double r2 = static_cast<double>((2 * tiles + clusters - 1) / clusters) / 2.0 * 1.10;
-  return {1, (nk >= 8 && r2 < r1) ? 2 : 1};
+  int64_t best_bn = 0;
+  double best = one.cost;
+  {
+    const int64_t bn = 256;        // the pair kernel's 192-wide tiles measured slower than the one-CTA kernel's
+    const int64_t tiles = ((M + 255) / 256) * ((N + bn - 1) / bn);
+    const double cost = static_cast<double>((tiles + clusters - 1) / clusters) * bn * nk * 0.90;
+    if (cost < best) {
+      best = cost;
+      best_bn = bn;
+    }
+  }
+  if (best_bn == 0) return {0, one.bn, one.splits};
+  return {1, best_bn, 1};
 }
 
 // C = A @ B^T in the operand conventions above. C: bf16 or fp32 [M, N] (any row stride); R: optional bf16 residual.
@@ -564,6 +585,11 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bo
     else if (epi == kEpiBf16Res)
       dispatch_major<256, 4, kEpiBf16Res>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, sp, wsp, st);
     else dispatch_major<256, 4, kEpiF32>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, sp, wsp, st);
+  } else if (bn == 192) {
+    if (epi == kEpiBf16) dispatch_major<192, 5, kEpiBf16>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, sp, wsp, st);
+    else if (epi == kEpiBf16Res)
+      dispatch_major<192, 5, kEpiBf16Res>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, sp, wsp, st);
+    else dispatch_major<192, 5, kEpiF32>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, sp, wsp, st);
   } else {
     if (epi == kEpiBf16) dispatch_major<128, 6, kEpiBf16>(a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, sp, wsp, st);
     else if (epi == kEpiBf16Res)
@@ -627,6 +653,9 @@ void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
   if (plan.bn == 256) {
     if (accumulate) launch<256, 4, true, true, kEpiScatterRes>(ta, tb, Cp, Rp, m, n, k, ld, ld, plan.splits, wsp, st, sc);
     else launch<256, 4, true, true, kEpiScatter>(ta, tb, Cp, Rp, m, n, k, ld, ld, plan.splits, wsp, st, sc);
+  } else if (plan.bn == 192) {
+    if (accumulate) launch<192, 5, true, true, kEpiScatterRes>(ta, tb, Cp, Rp, m, n, k, ld, ld, plan.splits, wsp, st, sc);
+    else launch<192, 5, true, true, kEpiScatter>(ta, tb, Cp, Rp, m, n, k, ld, ld, plan.splits, wsp, st, sc);
   } else {
     if (accumulate) launch<128, 6, true, true, kEpiScatterRes>(ta, tb, Cp, Rp, m, n, k, ld, ld, plan.splits, wsp, st, sc);
     else launch<128, 6, true, true, kEpiScatter>(ta, tb, Cp, Rp, m, n, k, ld, ld, plan.splits, wsp, st, sc);
@@ -677,6 +706,11 @@ int64_t gemm_sq(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool ac
     if (accumulate) launch<256, 4, true, true, kEpiBf16ResSq>(ta, tb, Cp, Rp, m, n, k, ldc, ldc, plan.splits, wsp, st,
                                                               OwnerScatter{}, sp);
     else launch<256, 4, true, true, kEpiBf16Sq>(ta, tb, Cp, Rp, m, n, k, ldc, ldc, plan.splits, wsp, st,
+                                                OwnerScatter{}, sp);
+  } else if (plan.bn == 192) {
+    if (accumulate) launch<192, 5, true, true, kEpiBf16ResSq>(ta, tb, Cp, Rp, m, n, k, ldc, ldc, plan.splits, wsp, st,
+                                                              OwnerScatter{}, sp);
+    else launch<192, 5, true, true, kEpiBf16Sq>(ta, tb, Cp, Rp, m, n, k, ldc, ldc, plan.splits, wsp, st,
                                                 OwnerScatter{}, sp);
   } else {
     if (accumulate) launch<128, 6, true, true, kEpiBf16ResSq>(ta, tb, Cp, Rp, m, n, k, ldc, ldc, plan.splits, wsp, st,

@@ -31,12 +31,14 @@ constexpr int kThreads2 = 192;
 
 enum Epi2 : int { kE2Bf16 = 0, kE2Bf16Res = 1, kE2F32 = 2 };
 
-// BN: output columns per tile (256, or 128 for shapes whose 256-wide tiles leave a mostly empty last wave); each CTA
-// loads BN / 2 rows of B per K slab
+// BN: output columns per tile (256; 192 or 128 for shapes whose 256-wide tiles leave a mostly empty last round);
+// each CTA loads BN / 2 rows of B per K slab
 template <int BN, int STAGES>
 struct Smem2 {
   static constexpr int A_BYTES = kBM * kBK * 2;             // 16 KB
-  static constexpr int B_BYTES = (BN / 2) * kBK * 2;        // this CTA's half of the B slab
+  // this CTA's half of the B slab, in whole 64-wide swizzle atoms (BN = 192: 96 rows / columns, 2 atoms reserved)
+  static constexpr int B_ATOMS = (BN / 2 + 63) / 64;
+  static constexpr int B_BYTES = B_ATOMS * 64 * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;
@@ -46,6 +48,10 @@ template <int BN>
 struct PairCfg;
 template <>
 struct PairCfg<256> {
+  static constexpr int STAGES = 6;
+};
+template <>
+struct PairCfg<192> {
   static constexpr int STAGES = 6;
 };
 template <>
@@ -219,7 +225,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   // consecutive units, so they run in the same wave
   const int num_units = num_tiles * splits;
   const int k_chunk = (num_k + splits - 1) / splits;
-  constexpr uint32_t TMEM_COLS = 2 * BN;
+  // accumulator buffers at a power-of-two column stride (BN = 192 uses columns [0, 192) and [256, 448))
+  constexpr uint32_t ACC_STRIDE = BN <= 128 ? 128u : 256u;
+  constexpr uint32_t TMEM_COLS = 2 * ACC_STRIDE;
+  // bytes one CTA's loads deliver per stage: the K-major B half is BN / 2 rows of 128 bytes; the MN-major half is
+  // whole 64-wide atoms (BN = 192: 128 columns loaded, 96 used by the MMA)
+  constexpr uint32_t TX_BYTES = S::A_BYTES + (B_MN ? S::B_BYTES : (BN / 2) * kBK * 2);
   constexpr uint32_t IDESC = idesc_bf16(2 * kBM, BN, A_MN, B_MN);
 
   if (threadIdx.x == 0) {
@@ -265,7 +276,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
           uint8_t* sa = smem + s * S::STAGE_BYTES;
           uint8_t* sb = sa + S::A_BYTES;
           const uint32_t bar = mapa_u32(&full[s], 0);
-          if (crank == 0) mbar_arrive_expect_tx(&full[s], 2 * S::STAGE_BYTES);
+          if (crank == 0) mbar_arrive_expect_tx(&full[s], 2 * TX_BYTES);
           if (!A_MN) {
             tma_load_2d_pair(sa, &tmA, bar, kb * kBK, m0);
           } else {
@@ -276,7 +287,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
             tma_load_2d_pair(sb, &tmB, bar, kb * kBK, n0);
           } else {
 #pragma unroll
-            for (int j = 0; j < (BN / 2) / 64; ++j) tma_load_2d_pair(sb + j * 8192, &tmB, bar, n0 + 64 * j, kb * kBK);
+            for (int j = 0; j < S::B_ATOMS; ++j) tma_load_2d_pair(sb + j * 8192, &tmB, bar, n0 + 64 * j, kb * kBK);
           }
           if (++s == kStages2) {
             s = 0;
@@ -304,7 +315,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
         if (!mbar_wait_cluster(&tempty[acc], acc_ph ^ 1u, abort_flag, status, 23)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc) * ACC_STRIDE;
         const int kb0 = (u % splits) * k_chunk, kb1 = min(num_k, kb0 + k_chunk);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[s], ph, abort_flag, status, 24)) {
@@ -346,7 +357,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       if (!mbar_wait(&tfull[acc], acc_ph, abort_flag, status, 25)) break;
       tc_fence_after();
       const int row = mb * 2 * kBM + static_cast<int>(crank) * kBM + q * 32 + lane;
-      const uint32_t tb = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+      const uint32_t tb = tmem_base + static_cast<uint32_t>(acc) * ACC_STRIDE + (static_cast<uint32_t>(q * 32) << 16);
       bool last = true;
       const float* other = nullptr;
       if (splits == 2) {
@@ -451,6 +462,7 @@ void dispatch_pair_bn(int bn, bool a_mn, bool b_mn, const CUtensorMap& ta, const
                       const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, const PairArgs& pa,
                       cudaStream_t st) {
   if (bn == 256) dispatch_pair<256, EPI>(a_mn, b_mn, ta, tb, C, R, M, N, K, ldc, ldr, pa, st);
+  else if (bn == 192) dispatch_pair<192, EPI>(a_mn, b_mn, ta, tb, C, R, M, N, K, ldc, ldr, pa, st);
   else dispatch_pair<128, EPI>(a_mn, b_mn, ta, tb, C, R, M, N, K, ldc, ldr, pa, st);
 }
 
@@ -478,7 +490,7 @@ int* pair_counters() {
 }  // namespace
 
 // C = A @ B^T on CTA pairs (operand conventions as gemm()). C: bf16 or fp32 [M, N]; R: bf16 residual.
-// bn: output tile width, 256 or 128; splits: 1, or 2 (each tile's K range in two halves on two pairs, summed by the
+// bn: output tile width, 256, 192 or 128; splits: 1, or 2 (each tile's K range in two halves on two pairs, summed by the
 // epilogue of the later one; the fp32 workspace is allocated here).
 void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
                const c10::optional<at::Tensor>& R, int64_t bn, int64_t splits) {
@@ -506,7 +518,7 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_m
     Rp = reinterpret_cast<const __nv_bfloat16*>(R->data_ptr());
     ldr = R->stride(0);
   }
-  FYB_CHECK(bn == 256 || bn == 128, "gemm_pair: tile width must be 256 or 128");
+  FYB_CHECK(bn == 256 || bn == 192 || bn == 128, "gemm_pair: tile width must be 256, 192 or 128");
   FYB_CHECK(splits == 1 || splits == 2, "gemm_pair: splits must be 1 or 2");
   if (M == 0 || N == 0) return;
   c10::cuda::CUDAGuard guard(A.device());

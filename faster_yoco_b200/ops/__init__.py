@@ -97,9 +97,9 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn_major: bool = False, b_mn_maj
     if out is None:
         out = torch.empty(M, N, dtype=out_dtype or a.dtype, device=a.device)
     K = a.shape[0] if a_mn_major else a.shape[1]
-    route = _gemm_route(M, N, K) if _GEMM_PAIR else (0, 1)
+    route = _gemm_route(M, N, K) if _GEMM_PAIR else (0, 0, 1)
     if route[0] == 1:
-        _C().gemm_pair(a, b, out, a_mn_major, b_mn_major, residual, 256, route[1])
+        _C().gemm_pair(a, b, out, a_mn_major, b_mn_major, residual, route[1], route[2])
     else:
         _C().gemm(a, b, out, a_mn_major, b_mn_major, residual)
     return out
@@ -109,8 +109,8 @@ _ROUTES = {}
 
 
 def _gemm_route(M: int, N: int, K: int):
-    """(kernel, splits) for the shape: the CTA-pair kernel unless the one-CTA kernel's plan needs split-K (cached per
-    shape; csrc/gemm.cu::gemm_route)."""
+    """(kernel, tile width, splits) for the shape from the cost model of csrc/gemm.cu::gemm_route (cached per
+    shape)."""
     key = (M, N, K)
     r = _ROUTES.get(key)
     if r is None:

@@ -151,6 +151,7 @@ class FlatParams:
         self.sq_used = 0
         self._sq_covered = set()
         self._sq_region = {}               # id(p) -> (start, end) of p's partials in sq_buf this update
+        self._sq_chunks = {}               # covered set -> device table of the other gradients' chunks
 
     # ---------------------------------------------------------------------------------------------------------
     def owner_of(self, x: int) -> int:
@@ -270,11 +271,22 @@ class FlatParams:
         """Sum of squares of the whole (bf16) gradient buffer: the GEMM partials of this update plus one pass over
         every gradient no GEMM covered (device tensor [1])."""
         from .. import ops
-        parts = [self.sq_buf[:self.sq_used].sum().reshape(1)] if self.sq_used else []
-        for e in self.entries:
-            if id(e.param) not in self._sq_covered:
-                parts.append(ops._C().sq_norm(self.grad_flat[e.offset:e.offset + e.numel]))
-        return torch.stack(parts).sum().reshape(1)
+        key = frozenset(self._sq_covered)
+        chunks = self._sq_chunks.get(key)
+        if chunks is None:
+            if self.device.type == "cuda" and torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("gradient norm: the set of GEMM-covered weights changed under capture")
+            rows = []
+            for e in self.entries:
+                if id(e.param) not in key:
+                    for a in range(e.offset, e.offset + e.numel, 1 << 16):
+                        rows.append([a, min(1 << 16, e.offset + e.numel - a)])
+            chunks = torch.tensor(rows, dtype=torch.int64, device=self.device).view(-1, 2)
+            self._sq_chunks[key] = chunks
+        rest = ops._C().sq_norm_ranges(self.grad_flat, chunks)     # every gradient no GEMM covered, one launch
+        if self.sq_used:
+            return (self.sq_buf[:self.sq_used].sum().reshape(1) + rest).reshape(1)
+        return rest
 
     def sparse(self) -> frozenset:
         return frozenset(self._sparse)

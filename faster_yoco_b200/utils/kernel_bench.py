@@ -86,9 +86,9 @@ def bench_gemm(results, pair_too: bool = False):
              "ours_tflops": fl / t_ours / 1e9, "cublas_tflops": fl / t_cub / 1e9}
         if pair_too:
             t_pair = _time(pair)
-            t_pair2 = _time(lambda: pair(256, 2)) if K >= 128 else float("nan")
-            r.update(pair_ms=t_pair, pair_tflops=fl / t_pair / 1e9, pair_split2_ms=t_pair2,
-                     pair_split2_tflops=fl / t_pair2 / 1e9)
+            t_pair192 = _time(lambda: pair(192))
+            r.update(pair_ms=t_pair, pair_tflops=fl / t_pair / 1e9, pair192_ms=t_pair192,
+                     pair192_tflops=fl / t_pair192 / 1e9)
         t_routed = _time(routed)
         r.update(routed_ms=t_routed, routed_tflops=fl / t_routed / 1e9,
                  route=list(ops._gemm_route(M, N, K)))

@@ -1,6 +1,6 @@
 """The CTA-pair GEMM (tcgen05.mma.cta_group::2, 256 x 256 tiles over two CTAs, gemm2.cu) against the one-CTA GEMM
 and an fp32 PyTorch oracle: every operand layout (forward, input gradient, weight gradient), M / N / K tails, the
-residual epilogue and fp32 output, 256- and 128-wide tiles, whole-K and two-way split-K (the later half's epilogue
+residual epilogue and fp32 output, 256-, 192- and 128-wide tiles, whole-K and two-way split-K (the later half's epilogue
 adds the earlier half's partial), two calls in a row."""
 import pytest
 import torch
@@ -39,7 +39,7 @@ def _close_in_ulps(x, y, ulps, acc_mag=None):
     (520, 300, 136, True, False),
 ])
 @pytest.mark.parametrize("epi", ["bf16", "res", "f32"])
-@pytest.mark.parametrize("bn,splits", [(256, 1), (128, 1), (256, 2), (128, 2)])
+@pytest.mark.parametrize("bn,splits", [(256, 1), (192, 1), (128, 1), (256, 2), (192, 2)])
 def test_gemm_pair_matches_one_cta_and_fp32(M, N, K, a_mn, b_mn, epi, bn, splits):
     C = ops._C()
     g = torch.Generator(device="cuda").manual_seed(M + N + K)

@@ -231,3 +231,20 @@ def test_gemm_split_k_with_residual(M, N, K):
     out2 = torch.empty(M, N, device=dev(), dtype=torch.bfloat16)
     C().gemm(a, b, out2, False, False, None)
     assert rel(out2, ref) < 1e-2
+
+
+def test_sq_norm_ranges_any_alignment():
+    """Sum of squares over many ranges of one bf16 buffer (unaligned starts, lengths up to 65,536) in one launch,
+    against fp64 PyTorch; the order of the partials is fixed, so two calls agree bit for bit."""
+    lib = C()
+    dv = dev()
+    g = torch.Generator(device=dv).manual_seed(3)
+    x = torch.randn(1 << 20, generator=g, device=dv).to(torch.bfloat16)
+    rows = [[0, 65536], [3, 17], [70001, 65536], [200003, 1], [300000, 40000], [1048575, 1], [500001, 9]]
+    chunks = torch.tensor(rows, dtype=torch.int64, device=dv)
+    got = lib.sq_norm_ranges(x, chunks)
+    want = sum(x[a:a + n].double().pow(2).sum().item() for a, n in rows)
+    assert abs(got.item() - want) <= 1e-5 * want
+    assert torch.equal(got, lib.sq_norm_ranges(x, chunks))
+    empty = lib.sq_norm_ranges(x, torch.zeros(0, 2, dtype=torch.int64, device=dv))
+    assert empty.item() == 0.0
