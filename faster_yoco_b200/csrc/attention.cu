@@ -443,6 +443,232 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 }
 
+// ====================================================================================== forward, two CTAs per SM
+// Softmax attention forward sized so that two CTAs share an SM (the tensor core works on one CTA's MMAs while the
+// other's softmax runs): one query tile per CTA, 6 warps (producer, MMA issuer, 4 softmax warps with one thread per
+// query row), single-buffered K / V (96 KB of shared memory), 256 TMEM columns: S @ 0 with P written back over its
+// first 64 columns as bf16 pairs (the A operand of O += P V), O @ 128. The next key tile's S MMA is issued after the
+// PV MMA that reads P from the same columns (one CTA's MMAs run in issue order). Lazy rescaling as in attn_fwd_kernel.
+constexpr int kFwd2Threads = 192;
+constexpr int kSoftWarps = 4;
+
+__global__ void __launch_bounds__(kFwd2Threads, 2)
+    attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + kTileBytes;
+  uint8_t* sV = sK + kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + kTileBytes);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 2;
+  uint64_t* v_full = bars + 3;
+  uint64_t* v_empty = bars + 4;
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;    // kSoftWarps arrivals
+  uint64_t* pv_done = bars + 7;
+  uint64_t* o_full = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = (p.Lq + kT - 1) / kT;
+  const int units = p.B * p.Hq;
+  const int qt = nq - 1 - static_cast<int>(blockIdx.x / units);      // longest first
+  const int bh = static_cast<int>(blockIdx.x % units);
+  const int h = bh % p.Hq, b = bh / p.Hq;
+  const int hk = h / (p.Hq / p.Hk);
+  const int q0 = qt * kT;
+  const Range rg = kv_range(p, q0);
+  const int n = rg.j1 - rg.j0;
+  constexpr uint32_t IDESC_S = idesc_bf16(128, 128, false, false);
+  constexpr uint32_t IDESC_O = idesc_bf16(128, 128, false, true);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 9; ++i) mbar_init(&bars[i], 1);
+    mbar_init(p_full, kSoftWarps);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;   // S / P @ 0, O @ 128
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------------------------------------ producer
+    if (lane == 0 && n > 0) {
+      const int rowq = b * p.Lq + q0;
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      tma_load_3d(sQ, &tmQ, q_full, 0, h, rowq);
+      tma_load_3d(sQ + 16384, &tmQ, q_full, 64, h, rowq);
+      int issued_k = 0, issued_v = 0;
+      for (int it = 0; it < n; ++it) {
+        const uint32_t ph = it & 1;
+        const int rowk = b * p.Lk + (rg.j0 + it) * kT;
+        if (!mbar_wait(k_empty, ph ^ 1u, abort_flag, p.status, 60)) break;
+        mbar_arrive_expect_tx(k_full, kTileBytes);
+        tma_load_3d(sK, &tmK, k_full, 0, hk, rowk);
+        tma_load_3d(sK + 16384, &tmK, k_full, 64, hk, rowk);
+        issued_k = it + 1;
+        if (!mbar_wait(v_empty, ph ^ 1u, abort_flag, p.status, 61)) break;
+        mbar_arrive_expect_tx(v_full, kTileBytes);
+        tma_load_3d(sV, &tmV, v_full, 0, hk, rowk);
+        tma_load_3d(sV + 16384, &tmV, v_full, 64, hk, rowk);
+        issued_v = it + 1;
+      }
+      // drain: the last loads must have landed before the CTA ends
+      if (issued_k > 0) mbar_wait(k_full, (issued_k - 1) & 1, nullptr, p.status, 62);
+      if (issued_v > 0) mbar_wait(v_full, (issued_v - 1) & 1, nullptr, p.status, 63);
+      mbar_wait(q_full, 0, nullptr, p.status, 64);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n > 0) {
+      const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, 65);
+      for (int it = 0; ok && it < n; ++it) {
+        const uint32_t ph = it & 1;
+        if (!(ok = mbar_wait(k_full, ph, abort_flag, p.status, 66))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k)
+          umma_bf16(tmem, kmaj_desc(aQ, k), kmaj_desc(aK, k), IDESC_S, k > 0 ? 1u : 0u);
+        umma_commit(s_full);
+        umma_commit(k_empty);
+        if (!(ok = mbar_wait(p_full, ph, abort_flag, p.status, 67))) break;
+        if (!(ok = mbar_wait(v_full, ph, abort_flag, p.status, 68))) break;
+        tc_fence_after();
+        // O += P V, P (bf16 pairs) in TMEM columns 0..63: K step k = keys 16k..16k+15 in columns 8k..8k+7
+#pragma unroll
+        for (int k = 0; k < kT / 16; ++k)
+          umma_bf16_ts(tmem + 128, tmem + k * 8, mnmaj_desc(aV, k), IDESC_O, (it > 0 || k > 0) ? 1u : 0u);
+        umma_commit(pv_done);
+        umma_commit(v_empty);
+      }
+      if (ok) umma_commit(o_full);
+    }
+  } else {
+    // ------------------------------------------------------------------------------------------ softmax warps
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;                 // query row within the tile
+    const int qrow = q0 + r;
+    const bool rowvalid = qrow < p.Lq;
+    const int qa = qrow + p.q_offset;
+    const uint32_t trow = static_cast<uint32_t>(quad * 32) << 16;
+    const float sl2 = p.scale * kLog2e;
+    float m_ref = -INFINITY, l_sum = 0.f;
+    bool ok = true;
+    for (int it = 0; ok && it < n; ++it) {
+      const uint32_t ph = it & 1;
+      const int k0 = (rg.j0 + it) * kT;
+      const bool full_tile = rowvalid && (k0 + kT <= p.Lk) && (!p.causal || k0 + kT - 1 <= q0 + p.q_offset) &&
+                             (p.window <= 0 || k0 > min(q0 + kT, p.Lq) - 1 + p.q_offset - p.window);
+      if (!(ok = mbar_wait(s_full, ph, abort_flag, p.status, 69))) break;
+      tc_fence_after();
+      // row max over the tile (this thread owns the whole row)
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kT; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + trow + c, v);
+        tmem_ld_wait();
+        const uint32_t mk = full_tile ? 0xffffffffu : key_mask32(p, qa, k0 + c, rowvalid);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, ((mk >> i) & 1u) ? __uint_as_float(v[i]) : -INFINITY);
+      }
+      const float m_cand = fmaxf(m_ref, mx * sl2);
+      const bool need = m_cand > m_ref + kRescaleLog2;
+      const bool scale_o = need && m_ref != -INFINITY;
+      if (__any_sync(0xffffffffu, scale_o)) {
+        // O may be touched only after PV(it-1): PV(it-2) completed before S(it) was issued and PV(it) is not issued
+        // yet, so the parity of phase it - 1 names exactly one phase
+        if (!(ok = mbar_wait(pv_done, ph ^ 1u, abort_flag, p.status, 70))) break;
+        tc_fence_after();
+        const float f = scale_o ? fast_exp2(m_ref - m_cand) : 1.0f;
+#pragma unroll
+        for (int c = 0; c < kD; c += 32) {
+          uint32_t v[32];
+          tmem_ld32(tmem + 128 + trow + c, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * f);
+          tmem_st32(tmem + 128 + trow + c, v);
+        }
+        tmem_st_wait();
+        if (scale_o) l_sum *= f;
+      }
+      if (need) m_ref = m_cand;
+      const float mref = m_ref == -INFINITY ? 0.f : m_ref;
+      // P = exp2(S * scale * log2 e - m) as bf16 pairs over S's first 64 columns: the packed chunk of S columns
+      // c .. c + 31 lands in columns c / 2 .. c / 2 + 15, all of which this thread has already read
+#pragma unroll
+      for (int c = 0; c < kT; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + trow + c, v);
+        tmem_ld_wait();
+        const uint32_t mk = full_tile ? 0xffffffffu : key_mask32(p, qa, k0 + c, rowvalid);
+        uint32_t pp[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float x0 = fast_exp2(__uint_as_float(v[2 * i]) * sl2 - mref);
+          float x1 = fast_exp2(__uint_as_float(v[2 * i + 1]) * sl2 - mref);
+          x0 = ((mk >> (2 * i)) & 1u) ? x0 : 0.f;
+          x1 = ((mk >> (2 * i + 1)) & 1u) ? x1 : 0.f;
+          l_sum += x0 + x1;
+          pp[i] = pack_bf16(x0, x1);
+        }
+        tmem_st16(tmem + trow + c / 2, pp);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    // ------------------------------------------------------------------------------------------------ epilogue
+    const bool have = ok && n > 0 && mbar_wait(o_full, 0, abort_flag, p.status, 71);
+    if (have) tc_fence_after();
+    const float inv = l_sum > 0.f ? 1.0f / l_sum : 0.f;
+    if (rowvalid)
+      p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.Lq + qrow] =
+          l_sum > 0.f ? (m_ref + __log2f(l_sum)) * 0.6931471805599453f : -INFINITY;
+    __nv_bfloat16* orow = p.O + ((static_cast<int64_t>(b) * p.Lq + (rowvalid ? qrow : 0)) * p.Hq + h) * kD;
+#pragma unroll 1
+    for (int c = 0; c < kD; c += 32) {
+      uint32_t v[32];
+      if (have) {
+        tmem_ld32(tmem + 128 + trow + c, v);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0u;
+      }
+      if (rowvalid) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          *reinterpret_cast<uint4*>(orow + c + 8 * j) =
+              make_uint4(pack_bf16(__uint_as_float(v[8 * j]) * inv, __uint_as_float(v[8 * j + 1]) * inv),
+                         pack_bf16(__uint_as_float(v[8 * j + 2]) * inv, __uint_as_float(v[8 * j + 3]) * inv),
+                         pack_bf16(__uint_as_float(v[8 * j + 4]) * inv, __uint_as_float(v[8 * j + 5]) * inv),
+                         pack_bf16(__uint_as_float(v[8 * j + 6]) * inv, __uint_as_float(v[8 * j + 7]) * inv));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
 // ======================================================================================================= backward
 
 struct AttnBwdParams {
@@ -918,6 +1144,7 @@ __global__ void dq_out_kernel(const float* __restrict__ acc, __nv_bfloat16* __re
 }
 
 constexpr int kFwdSmem = 5 * kTileBytes + 6 * kT * 4 + 256 + 1024;
+constexpr int kFwd2Smem = 3 * kTileBytes + 128 + 1024;
 constexpr int kBwdSmem = 7 * kTileBytes + 2 * kT * 4 + 256 + 1024;
 static_assert(kBwdSmem <= 227 * 1024, "attention backward shared memory");
 
@@ -966,11 +1193,12 @@ std::vector<at::Tensor> attention_fwd(const at::Tensor& q, const at::Tensor& k, 
   const CUtensorMap tq = tmap_heads(q), tk = tmap_heads(k), tv = tmap_heads(v);
   static bool init = false;
   if (!init) {
-    set_smem(attn_fwd_kernel<kSoftmax>, kFwdSmem);
+    set_smem(attn_fwd2_kernel, kFwd2Smem);
+    FYB_CUDA(cudaFuncSetAttribute(attn_fwd2_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     init = true;
   }
   const int grid = B * Hq * ((Lq + kT - 1) / kT);
-  attn_fwd_kernel<kSoftmax><<<grid, kAttnThreads, kFwdSmem, cur_stream()>>>(tq, tk, tv, p);
+  attn_fwd2_kernel<<<grid, kFwd2Threads, kFwd2Smem, cur_stream()>>>(tq, tk, tv, p);
   check_launch("attn_fwd");
   return {o, lse};
 }
