@@ -15,6 +15,10 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_m
 int64_t gemm_sq(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, at::Tensor& sq_part);
 int64_t gemm_sq_slots(int64_t M, int64_t N, int64_t K);
 std::vector<int64_t> gemm_route(int64_t M, int64_t N, int64_t K);
+void gemm_rope(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const at::Tensor& cos_t,
+               const at::Tensor& sin_t, int64_t L, int64_t rot_cols);
+std::vector<at::Tensor> gemm_swiglu(const at::Tensor& A, const at::Tensor& B);
+void gemm_swiglu_bwd(const at::Tensor& G, const at::Tensor& W, bool w_mn, const at::Tensor& U, at::Tensor& dU);
 void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, const at::Tensor& grad_flat,
                   const at::Tensor& bases, int64_t seg, int64_t rank, int64_t chunk);
 std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps);
@@ -142,6 +146,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pair", &fyb::gemm_pair, "C = A @ B^T on CTA pairs (tcgen05.mma.cta_group::2, 256 x bn tiles)",
         py::arg("A"), py::arg("B"), py::arg("C"), py::arg("a_mn_major"), py::arg("b_mn_major"),
         py::arg("residual") = py::none(), py::arg("bn") = 256, py::arg("splits") = 1);
+  m.def("gemm_rope", &fyb::gemm_rope,
+        "C = A @ B^T with the interleaved rotary embedding of the leading rot_cols columns in the epilogue",
+        py::arg("A"), py::arg("B"), py::arg("C"), py::arg("cos"), py::arg("sin"), py::arg("L"), py::arg("rot_cols"));
+  m.def("gemm_swiglu", &fyb::gemm_swiglu,
+        "{u, h}: u = A @ [fc1; gate]^T and h = silu(u[:, :f]) * u[:, f:] from one GEMM (SwiGLU epilogue)");
+  m.def("gemm_swiglu_bwd", &fyb::gemm_swiglu_bwd,
+        "du = SwiGLU backward of (G @ W) against the saved u, computed in the GEMM epilogue", py::arg("G"),
+        py::arg("W"), py::arg("w_mn"), py::arg("u"), py::arg("du"));
   m.def("gemm_route", &fyb::gemm_route, "kernel choice {0 one-CTA / 1 CTA pair, tile width, splits} for an M x N x K GEMM");
   m.def("gemm_sq", &fyb::gemm_sq,
         "weight gradient dW = A^T B (bf16, optionally accumulated) with fp32 sum-of-squares partials of the stored "

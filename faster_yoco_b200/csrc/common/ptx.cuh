@@ -286,4 +286,27 @@ __device__ __forceinline__ float2 unpack_bf16(uint32_t u) {
 
 __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// ------------------------------------------------------------------------------------------------------------------
+// activation / rotary pieces shared by the elementwise kernels and the fused GEMM epilogues: one definition, so the
+// fused and the separate forms round identically
+
+// sigmoid with the hardware reciprocal (__frcp_rn: one correctly rounded reciprocal instead of a full division)
+__device__ __forceinline__ float sigmoidf_(float x) { return __frcp_rn(1.0f + __expf(-x)); }
+
+// SwiGLU value silu(a) * b (kernel/swiglu.py:4-17: silu of the first operand)
+__device__ __forceinline__ float swiglu_val(float a, float b) { return a * b * sigmoidf_(a); }
+
+// gradients of silu(a) * b for the output gradient g
+__device__ __forceinline__ void swiglu_grad(float a, float b, float g, float& da, float& db) {
+  const float s = sigmoidf_(a);
+  da = s * (1.0f + a * (1.0f - s)) * g * b;
+  db = a * s * g;
+}
+
+// one interleaved rotary pair (x0, x1) by the angle with cosine cs and sine sn
+__device__ __forceinline__ void rope_rot(float x0, float x1, float cs, float sn, float& o0, float& o1) {
+  o0 = x0 * cs - x1 * sn;
+  o1 = x0 * sn + x1 * cs;
+}
+
 }  // namespace fyb

@@ -33,8 +33,6 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
       make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]), pack_bf16(f[4], f[5]), pack_bf16(f[6], f[7]));
 }
 
-// sigmoid with the hardware reciprocal (__frcp_rn: one correctly rounded reciprocal instead of a full division)
-__device__ __forceinline__ float sigmoidf_(float x) { return __frcp_rn(1.0f + __expf(-x)); }
 
 // ------------------------------------------------------------------------------------------------------------------
 // SwiGLU on [M, N] views with row strides (N % 8 == 0)
@@ -49,7 +47,7 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t l
   load8(x + r * ldx + c, a);
   load8(y + r * ldy + c, b);
 #pragma unroll
-  for (int k = 0; k < 8; ++k) o[k] = a[k] * b[k] * sigmoidf_(a[k]);
+  for (int k = 0; k < 8; ++k) o[k] = swiglu_val(a[k], b[k]);
   store8(out + r * N + c, o);
 }
 
@@ -64,11 +62,7 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t l
   load8(y + r * ldy + c, b);
   load8(g + r * N + c, gg);
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const float s = sigmoidf_(a[k]);
-    da[k] = s * (1.0f + a[k] * (1.0f - s)) * gg[k] * b[k];
-    db[k] = a[k] * s * gg[k];
-  }
+  for (int k = 0; k < 8; ++k) swiglu_grad(a[k], b[k], gg[k], da[k], db[k]);
   store8(dx + r * lddx + c, da);
   store8(dy + r * lddy + c, db);
 }
@@ -94,9 +88,7 @@ __global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, int64_t sb, int
     for (int k = 0; k < 4; ++k) {
       const float cs = __bfloat162float(cp[k]);
       const float sn = sign * __bfloat162float(spp[k]);
-      const float x0 = f[2 * k], x1 = f[2 * k + 1];
-      o[2 * k] = x0 * cs - x1 * sn;
-      o[2 * k + 1] = x0 * sn + x1 * cs;
+      rope_rot(f[2 * k], f[2 * k + 1], cs, sn, o[2 * k], o[2 * k + 1]);
     }
     store8(out + ((static_cast<int64_t>(b) * L + l) * H + h) * D + c8, o);
   }

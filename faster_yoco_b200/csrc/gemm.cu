@@ -507,6 +507,11 @@ Plan pick_plan(int M, int N, int K) {
 // kernel's 192-wide tiles and its two-way split-K are not routed to: both measured slower on these shapes.
 std::vector<int64_t> gemm_route(int64_t M, int64_t N, int64_t K) {
   const Plan one = pick_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
+  static const bool pair_off = [] {
+    const char* e = std::getenv("FYB_GEMM_PAIR");
+    return e != nullptr && e[0] == '0';
+  }();
+  if (pair_off) return {0, one.bn, one.splits};          // FYB_GEMM_PAIR=0: the one-CTA kernel everywhere
   // a K several times longer than the output needs the one-CTA kernel's split-K (no pair plan comes close)
   if (one.splits > 2) return {0, one.bn, one.splits};
   // the pair kernel's 256 x 256 tile = two one-CTA 128 x 256 tiles per round of clusters, at ~0.90 of the one-CTA
@@ -522,6 +527,17 @@ std::vector<int64_t> gemm_route(int64_t M, int64_t N, int64_t K) {
     if (cost < best) {
       best = cost;
       best_bn = bn;
+    }
+  }
+  // long-K shapes whose 256 x 256 tiles leave the last round poorly filled: the pair kernel's in-kernel two-way
+  // split-K (each half publishes fp32 rows, the later one adds and stores) measured ahead of every other plan once a
+  // K half has at least 128 blocks (fc1 / gate input gradient, K = 16,384: 0.170 vs 0.186 ms)
+  {
+    const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
+    const int64_t r1 = (tiles + clusters - 1) / clusters, r2 = (2 * tiles + clusters - 1) / clusters;
+    if (nk >= 256 && 2 * r1 > r2 && tiles <= 16384) {
+      const double cost = static_cast<double>(r2) * 256.0 * (nk / 2) * 0.90 * 1.05;
+      if (cost < best) return {1, 256, 2};
     }
   }
   if (best_bn == 0) return {0, one.bn, one.splits};
@@ -666,7 +682,11 @@ void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool 
 // the earlier micro-batches) with the sum of squares of the stored values as fp32 partials in sq_part: one per
 // (tile, epilogue warp), or one per split-K reduction block. Returns the number of partials written (the first
 // entries of sq_part; the caller sums them). sq_part must hold at least gemm_sq_slots(...) floats.
+int64_t gemm_pair_sq_slots(int64_t M, int64_t N);
+int64_t gemm_pair_sq(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, at::Tensor& sq_part);
+
 int64_t gemm_sq_slots(int64_t M, int64_t N, int64_t K) {
+  if (gemm_route(M, N, K)[0] == 1) return gemm_pair_sq_slots(M, N);
   const Plan plan = pick_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
   return sq_slots(static_cast<int>(M), static_cast<int>(N), plan.bn, plan.splits);
 }
@@ -682,6 +702,8 @@ int64_t gemm_sq(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool ac
   const int64_t K = A.size(0), M = A.size(1), N = B.size(1);
   FYB_CHECK(B.size(0) == K && C.size(0) == M && C.size(1) == N && K > 0, "gemm_sq: shape mismatch");
   FYB_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm_sq: dimension too large");
+  // the shapes the cost model gives to the CTA-pair kernel run there (its epilogue writes every partial slot)
+  if (gemm_route(M, N, K)[0] == 1) return gemm_pair_sq(A, B, C, accumulate, sq_part);
   const Plan plan = pick_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
   const int64_t slots = sq_slots(static_cast<int>(M), static_cast<int>(N), plan.bn, plan.splits);
   FYB_CHECK(sq_part.numel() >= slots, "gemm_sq: partials buffer too small");

@@ -29,7 +29,34 @@ constexpr int kBM = 128;        // rows of A (and of the output) per CTA
 constexpr int kBK = 64;
 constexpr int kThreads2 = 192;
 
-enum Epi2 : int { kE2Bf16 = 0, kE2Bf16Res = 1, kE2F32 = 2 };
+// kE2Bf16Sq / kE2Bf16ResSq: the bf16 store plus the sum of squares of the stored values, one fp32 partial per
+// (tile, CTA of the pair, epilogue warp) -- the weight-gradient form behind the one-GPU clip norm.
+// Fused elementwise epilogues (operands in EpiAux):
+//   kE2Rope      : interleaved rotary embedding of the leading aux.i1 columns (the q / k blocks of a projection) at
+//                  position row % aux.i0, cos / sin tables aux.t0 / aux.t1 [L, 64] (kernel/rotary.py:20-141)
+//   kE2Swiglu    : the merged fc1 | gate projection: the pair's two B halves are rows [j0, j0 + 128) and
+//                  [f + j0, f + j0 + 128) of B (f = aux.i0), so one tile holds both operands of silu(a) * b for 128
+//                  columns; stores a and b (kept for the backward) and h = silu(a) * b into aux.out2
+//                  (kernel/swiglu.py:4-17)
+//   kE2SwigluBwd : the fc2 input gradient dh (N = f columns) is not stored: with a, b from aux.t0 (the saved
+//                  fc1 | gate output, row stride aux.ld2) the epilogue stores da at C[:, col] and db at C[:, f + col]
+// Every fused epilogue rounds the accumulator to bf16 first, as the separate kernels read it from memory.
+enum Epi2 : int {
+  kE2Bf16 = 0, kE2Bf16Res = 1, kE2F32 = 2, kE2Bf16Sq = 3, kE2Bf16ResSq = 4, kE2Rope = 5, kE2Swiglu = 6,
+  kE2SwigluBwd = 7
+};
+__host__ __device__ constexpr bool e2_res(int e) { return e == kE2Bf16Res || e == kE2Bf16ResSq; }
+__host__ __device__ constexpr bool e2_sq(int e) { return e == kE2Bf16Sq || e == kE2Bf16ResSq; }
+
+// operands of the fused epilogues (unused fields zero)
+struct EpiAux {
+  const __nv_bfloat16* t0;   // kE2Rope: cos [L, 64]; kE2SwigluBwd: fc1 | gate output [M, 2f]
+  const __nv_bfloat16* t1;   // kE2Rope: sin [L, 64]
+  __nv_bfloat16* out2;       // kE2Swiglu: h [M, f]
+  int64_t ld2;               // row stride of out2 (kE2Swiglu) / t0 (kE2SwigluBwd)
+  int i0;                    // kE2Rope: L; kE2Swiglu / kE2SwigluBwd: f
+  int i1;                    // kE2Rope: rotated leading columns (a multiple of 128)
+};
 
 // BN: output columns per tile (256; 192 or 128 for shapes whose 256-wide tiles leave a mostly empty last round);
 // each CTA loads BN / 2 rows of B per K slab
@@ -149,9 +176,10 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   }
 }
 
+// stores 32 values of one output row; returns the sum of squares of the stored bf16 values (sq epilogues)
 template <int EPI>
-__device__ __forceinline__ void store_row32(const uint32_t (&r)[32], void* Cv, const __nv_bfloat16* R, int row,
-                                            int col, int N, int64_t ldc, int64_t ldr) {
+__device__ __forceinline__ float store_row32(const uint32_t (&r)[32], void* Cv, const __nv_bfloat16* R, int row,
+                                             int col, int N, int64_t ldc, int64_t ldr) {
   if (EPI == kE2F32) {
     float* C = reinterpret_cast<float*>(Cv) + static_cast<int64_t>(row) * ldc + col;
     if (col + 32 <= N && (ldc % 4) == 0) {
@@ -164,11 +192,11 @@ __device__ __forceinline__ void store_row32(const uint32_t (&r)[32], void* Cv, c
       for (int j = 0; j < 32; ++j)
         if (col + j < N) C[j] = __uint_as_float(r[j]);
     }
-    return;
+    return 0.f;
   }
   __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(Cv) + static_cast<int64_t>(row) * ldc + col;
   uint32_t p[16];
-  if (EPI == kE2Bf16Res) {
+  if (e2_res(EPI)) {
     const __nv_bfloat16* Rr = R + static_cast<int64_t>(row) * ldr + col;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
@@ -194,13 +222,66 @@ __device__ __forceinline__ void store_row32(const uint32_t (&r)[32], void* Cv, c
       }
     }
   }
+  float sq = 0.f;
+  if (e2_sq(EPI)) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float2 x = unpack_bf16(p[j]);
+      if (col + 2 * j < N) sq = fmaf(x.x, x.x, sq);
+      if (col + 2 * j + 1 < N) sq = fmaf(x.y, x.y, sq);
+    }
+  }
+  return sq;
+}
+
+__device__ __forceinline__ void store16x2(__nv_bfloat16* p, const uint32_t (&w)[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(p + 8 * j) = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+}
+
+__device__ __forceinline__ void load16x2(const __nv_bfloat16* p, uint32_t (&w)[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint4 v = *reinterpret_cast<const uint4*>(p + 8 * j);
+    w[4 * j] = v.x;
+    w[4 * j + 1] = v.y;
+    w[4 * j + 2] = v.z;
+    w[4 * j + 3] = v.w;
+  }
+}
+
+// 32 columns of a rotated block (col within [0, aux.i1), 16-byte aligned rows): pairs (2i, 2i + 1) of the head's
+// 128 columns turned by the angle of position pos and frequency index i = (col mod 128) / 2 + pair
+__device__ __forceinline__ void rope_store32(const uint32_t (&r)[32], __nv_bfloat16* C, const EpiAux& aux, int pos,
+                                             int col) {
+  uint32_t cw[8], sw[8];
+  const int64_t t = static_cast<int64_t>(pos) * 64 + ((col & 127) >> 1);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const uint4 c4 = *reinterpret_cast<const uint4*>(aux.t0 + t + 8 * j);
+    const uint4 s4 = *reinterpret_cast<const uint4*>(aux.t1 + t + 8 * j);
+    cw[4 * j] = c4.x, cw[4 * j + 1] = c4.y, cw[4 * j + 2] = c4.z, cw[4 * j + 3] = c4.w;
+    sw[4 * j] = s4.x, sw[4 * j + 1] = s4.y, sw[4 * j + 2] = s4.z, sw[4 * j + 3] = s4.w;
+  }
+  uint32_t p[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    // pair k uses table entry k: entries 2m, 2m + 1 of the 16 sit in word m
+    const float2 cs2 = unpack_bf16(cw[k >> 1]), sn2 = unpack_bf16(sw[k >> 1]);
+    const float cs = (k & 1) ? cs2.y : cs2.x, sn = (k & 1) ? sn2.y : sn2.x;
+    float o0, o1;
+    rope_rot(bf16_round(__uint_as_float(r[2 * k])), bf16_round(__uint_as_float(r[2 * k + 1])), cs, sn, o0, o1);
+    p[k] = pack_bf16(o0, o1);
+  }
+  store16x2(C, p);
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* Cv,
                      const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, int splits, float* ws,
-                     int* counters, int* status) {
+                     int* counters, int* status, float* sq_part, const EpiAux aux) {
+  static_assert(EPI != kE2Swiglu || (BN == 256 && !B_MN), "the SwiGLU epilogue pairs two 128-row B halves");
   constexpr int kStages2 = PairCfg<BN>::STAGES;
   using S = Smem2<BN, kStages2>;
   extern __shared__ uint8_t smem_raw[];
@@ -218,7 +299,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
   const int num_m = (M + 2 * kBM - 1) / (2 * kBM);
-  const int num_n = (N + BN - 1) / BN;
+  // kE2Swiglu: tile nb covers columns [128 nb, 128 nb + 128) of both halves
+  const int num_n = EPI == kE2Swiglu ? (aux.i0 + 127) / 128 : (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_k = (K + kBK - 1) / kBK;
   // split-K (splits = 1 or 2): work unit u = (tile u / splits, K half u % splits); the two halves of a tile are
@@ -266,7 +348,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         const int t = u / splits;
         const int mb = t % num_m, nb = t / num_m;
         const int m0 = mb * 2 * kBM + static_cast<int>(crank) * kBM;
-        const int n0 = nb * BN + static_cast<int>(crank) * (BN / 2);
+        const int n0 = EPI == kE2Swiglu ? nb * 128 + static_cast<int>(crank) * aux.i0
+                                        : nb * BN + static_cast<int>(crank) * (BN / 2);
         const int kb0 = (u % splits) * k_chunk, kb1 = min(num_k, kb0 + k_chunk);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, status, 21)) {
@@ -390,11 +473,77 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
           other = ws + orow * BN;
         }
       }
+      float sq = 0.f;
+      if constexpr (EPI == kE2Swiglu) {
+        // TMEM columns [0, 128): a = fc1 columns j0.., [128, 256): b = gate columns f + j0..
+        const int f = aux.i0;
+        __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(Cv);
 #pragma unroll 1
-      for (int c = 0; last && c < BN / 32; ++c) {
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ra[32], rb[32];
+          tmem_ld32(tb + c * 32, ra);
+          tmem_ld32(tb + 128 + c * 32, rb);
+          tmem_ld_wait();
+          const int j = nb * 128 + c * 32;
+          if (row < M && j < f) {
+            uint32_t pa[16], pb[16], ph[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              pa[k] = pack_bf16(__uint_as_float(ra[2 * k]), __uint_as_float(ra[2 * k + 1]));
+              pb[k] = pack_bf16(__uint_as_float(rb[2 * k]), __uint_as_float(rb[2 * k + 1]));
+              const float2 a = unpack_bf16(pa[k]), b = unpack_bf16(pb[k]);
+              ph[k] = pack_bf16(swiglu_val(a.x, b.x), swiglu_val(a.y, b.y));
+            }
+            __nv_bfloat16* crow = C + static_cast<int64_t>(row) * ldc;
+            store16x2(crow + j, pa);
+            store16x2(crow + f + j, pb);
+            store16x2(aux.out2 + static_cast<int64_t>(row) * aux.ld2 + j, ph);
+          }
+        }
+      }
+      const int pos = EPI == kE2Rope && row < M ? row % aux.i0 : 0;
+#pragma unroll 1
+      for (int c = 0; EPI != kE2Swiglu && last && c < BN / 32; ++c) {
         uint32_t r[32];
+        uint32_t ua[16], ub[16];
+        const int col = nb * BN + c * 32;
+        if (EPI == kE2SwigluBwd && row < M && col < N) {
+          // the saved a, b of these columns, loaded ahead of the accumulator read
+          const __nv_bfloat16* u = aux.t0 + static_cast<int64_t>(row) * aux.ld2 + col;
+          load16x2(u, ua);
+          load16x2(u + aux.i0, ub);
+        }
         tmem_ld32(tb + c * 32, r);        // warp-collective: every lane, whatever its row
         tmem_ld_wait();
+        if constexpr (EPI == kE2SwigluBwd) {
+          if (row < M && col < N) {
+            uint32_t pa[16], pb[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              const float2 a = unpack_bf16(ua[k]), b = unpack_bf16(ub[k]);
+              const float g0 = bf16_round(__uint_as_float(r[2 * k])), g1 = bf16_round(__uint_as_float(r[2 * k + 1]));
+              float da0, db0, da1, db1;
+              swiglu_grad(a.x, b.x, g0, da0, db0);
+              swiglu_grad(a.y, b.y, g1, da1, db1);
+              pa[k] = pack_bf16(da0, da1);
+              pb[k] = pack_bf16(db0, db1);
+            }
+            __nv_bfloat16* crow = reinterpret_cast<__nv_bfloat16*>(Cv) + static_cast<int64_t>(row) * ldc;
+            store16x2(crow + col, pa);
+            store16x2(crow + aux.i0 + col, pb);
+          }
+          continue;
+        }
+        if constexpr (EPI == kE2Rope) {
+          if (row < M && col < N) {
+            if (col < aux.i1)
+              rope_store32(r, reinterpret_cast<__nv_bfloat16*>(Cv) + static_cast<int64_t>(row) * ldc + col, aux, pos,
+                           col);
+            else
+              store_row32<kE2Bf16>(r, Cv, R, row, col, N, ldc, ldr);
+          }
+          continue;
+        }
         if (other != nullptr) {
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
@@ -405,8 +554,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
             r[j + 3] = __float_as_uint(__uint_as_float(r[j + 3]) + o.w);
           }
         }
-        const int col = nb * BN + c * 32;
-        if (row < M && col < N) store_row32<EPI>(r, Cv, R, row, col, N, ldc, ldr);
+        if (row < M && col < N) sq += store_row32<EPI>(r, Cv, R, row, col, N, ldc, ldr);
+      }
+      if (e2_sq(EPI)) {
+        // one partial per (tile, CTA, epilogue warp), every slot written exactly once (no clearing needed)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        if (lane == 0) sq_part[(static_cast<int64_t>(t) * 2 + crank) * 4 + q] = sq;
       }
       tc_fence_before();
       __syncwarp();
@@ -428,11 +582,12 @@ struct PairArgs {
   int splits;
   float* ws;
   int* counters;
+  float* sq_part;
 };
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const __nv_bfloat16* R, int M, int N, int K,
-                 int64_t ldc, int64_t ldr, const PairArgs& pa, cudaStream_t stream) {
+                 int64_t ldc, int64_t ldr, const PairArgs& pa, cudaStream_t stream, const EpiAux& aux = EpiAux{}) {
   using S = Smem2<BN, PairCfg<BN>::STAGES>;
   auto kern = gemm_pair_kernel<BN, A_MN, B_MN, EPI>;
   static bool attr_set = false;
@@ -443,7 +598,7 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const __
   const int units = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + BN - 1) / BN) * pa.splits;
   const int clusters = std::max(1, std::min(units, num_sms() / 2));
   kern<<<2 * clusters, kThreads2, S::TOTAL, stream>>>(ta, tb, C, R, M, N, K, ldc, ldr, pa.splits, pa.ws,
-                                                      pa.counters, status_ptr());
+                                                      pa.counters, status_ptr(), pa.sq_part, aux);
   check_launch("gemm_pair");
 }
 
@@ -525,7 +680,7 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_m
   cudaStream_t st = cur_stream();
   const int64_t tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + bn - 1) / bn);
   const int64_t num_k = (K + kBK - 1) / kBK;
-  PairArgs pa{static_cast<int>(splits), nullptr, nullptr};
+  PairArgs pa{static_cast<int>(splits), nullptr, nullptr, nullptr};
   at::Tensor ws;
   if (splits == 2) {
     FYB_CHECK(num_k >= 2, "gemm_pair: split-K needs at least two K blocks");
@@ -545,6 +700,132 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_m
   if (f32) dispatch_pair_bn<kE2F32>(b, a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, pa, st);
   else if (Rp != nullptr) dispatch_pair_bn<kE2Bf16Res>(b, a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, pa, st);
   else dispatch_pair_bn<kE2Bf16>(b, a_mn, b_mn, ta, tb, Cp, Rp, m, n, k, ldc, ldr, pa, st);
+}
+
+// partials a gemm_pair_sq call writes: one per (256 x 256 tile, CTA of the pair, epilogue warp)
+int64_t gemm_pair_sq_slots(int64_t M, int64_t N) { return ((M + 255) / 256) * ((N + 255) / 256) * 8; }
+
+// Weight gradient on CTA pairs: C = A^T B (A = dy [K, M], B = x [K, N], both MN-major), bf16, optionally added to C's
+// current contents (earlier micro-batches), with the sum of squares of the stored values in sq_part (every one of
+// gemm_pair_sq_slots(M, N) partials written). Returns the number of partials.
+int64_t gemm_pair_sq(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, at::Tensor& sq_part) {
+  FYB_RANGE("fyb::gemm_pair_sq");
+  const int64_t K = A.size(0), M = A.size(1), N = B.size(1);
+  FYB_CHECK(B.size(0) == K && C.size(0) == M && C.size(1) == N && K > 0, "gemm_pair_sq: shape mismatch");
+  FYB_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm_pair_sq: contiguous rows expected");
+  FYB_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm_pair_sq: dimension too large");
+  const int64_t slots = gemm_pair_sq_slots(M, N);
+  FYB_CHECK(sq_part.scalar_type() == at::kFloat && sq_part.is_contiguous() && sq_part.numel() >= slots,
+            "gemm_pair_sq: partials buffer too small");
+  if (M == 0 || N == 0) return 0;
+  c10::cuda::CUDAGuard guard(A.device());
+  cudaStream_t st = cur_stream();
+  const CUtensorMap ta = make_tmap_2d(A.data_ptr(), K, M, A.stride(0), 64);
+  const CUtensorMap tb = make_tmap_2d(B.data_ptr(), K, N, B.stride(0), 64);
+  PairArgs pa{1, nullptr, nullptr, sq_part.data_ptr<float>()};
+  void* Cp = C.data_ptr();
+  const __nv_bfloat16* Rp = accumulate ? reinterpret_cast<const __nv_bfloat16*>(Cp) : nullptr;
+  const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
+  const int64_t ldc = C.stride(0);
+  if (accumulate) launch_pair<256, true, true, kE2Bf16ResSq>(ta, tb, Cp, Rp, m, n, k, ldc, ldc, pa, st);
+  else launch_pair<256, true, true, kE2Bf16Sq>(ta, tb, Cp, Rp, m, n, k, ldc, ldc, pa, st);
+  return slots;
+}
+
+namespace {
+// bf16 [rows, cols] with contiguous, 16-byte aligned rows (the fused epilogues store 16 bytes at a time)
+void check_rows16(const at::Tensor& t, const char* what) {
+  FYB_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 2 && t.stride(1) == 1 &&
+                t.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
+            what);
+}
+}  // namespace
+
+// C = A @ B^T (A [M, K], B [N, K], both K-major) with the interleaved rotary embedding applied in the epilogue to
+// the leading rot_cols columns (the q / k head blocks of a projection), token row r at position r mod L.
+// cos / sin: bf16 [>= L, 64] (head dim 128), the tables rope_fwd takes. Rounding as gemm() followed by rope_fwd.
+void gemm_rope(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const at::Tensor& cos_t,
+               const at::Tensor& sin_t, int64_t L, int64_t rot_cols) {
+  FYB_RANGE("fyb::gemm_rope");
+  check_rows16(A, "gemm_rope: A must be bf16 [M, K] with 16-byte aligned rows");
+  check_rows16(B, "gemm_rope: B must be bf16 [N, K] with 16-byte aligned rows");
+  check_rows16(C, "gemm_rope: C must be bf16 [M, N] with 16-byte aligned rows");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  FYB_CHECK(B.size(1) == K && K > 0 && C.size(0) == M && C.size(1) == N, "gemm_rope: shape mismatch");
+  FYB_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm_rope: dimension too large");
+  FYB_CHECK(L > 0 && M % L == 0, "gemm_rope: rows must be whole sequences of length L");
+  FYB_CHECK(rot_cols >= 0 && rot_cols % 128 == 0 && rot_cols <= N, "gemm_rope: rotated columns: whole 128 heads");
+  for (const at::Tensor* t : {&cos_t, &sin_t})
+    FYB_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->dim() == 2 &&
+                  t->size(0) >= L && t->size(1) == 64 && reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
+              "gemm_rope: cos / sin must be contiguous bf16 [>= L, 64]");
+  if (M == 0 || N == 0) return;
+  c10::cuda::CUDAGuard guard(A.device());
+  const CUtensorMap ta = make_tmap_2d(A.data_ptr(), M, K, A.stride(0), kBM);
+  const CUtensorMap tb = make_tmap_2d(B.data_ptr(), N, K, B.stride(0), 128);
+  const EpiAux aux{reinterpret_cast<const __nv_bfloat16*>(cos_t.data_ptr()),
+                   reinterpret_cast<const __nv_bfloat16*>(sin_t.data_ptr()), nullptr, 0, static_cast<int>(L),
+                   static_cast<int>(rot_cols)};
+  launch_pair<256, false, false, kE2Rope>(ta, tb, C.data_ptr(), nullptr, static_cast<int>(M), static_cast<int>(N),
+                                          static_cast<int>(K), C.stride(0), 0, PairArgs{1, nullptr, nullptr, nullptr},
+                                          cur_stream(), aux);
+}
+
+// The merged fc1 | gate projection with SwiGLU in the epilogue: u = A @ B^T (A [M, K], B = [fc1; gate] [2f, K], both
+// K-major) and h = silu(u[:, :f]) * u[:, f:]. Returns {u [M, 2f] (kept for the backward), h [M, f]}; the values
+// equal gemm() followed by swiglu_fwd.
+std::vector<at::Tensor> gemm_swiglu(const at::Tensor& A, const at::Tensor& B) {
+  FYB_RANGE("fyb::gemm_swiglu");
+  check_rows16(A, "gemm_swiglu: A must be bf16 [M, K] with 16-byte aligned rows");
+  check_rows16(B, "gemm_swiglu: B must be bf16 [2f, K] with 16-byte aligned rows");
+  const int64_t M = A.size(0), K = A.size(1), N2 = B.size(0);
+  FYB_CHECK(B.size(1) == K && K > 0 && N2 % 64 == 0, "gemm_swiglu: B must be [2f, K] with f a multiple of 32");
+  FYB_CHECK(M < (1ll << 31) && N2 < (1ll << 31) && K < (1ll << 31), "gemm_swiglu: dimension too large");
+  const int64_t f = N2 / 2;
+  at::Tensor u = at::empty({M, N2}, A.options());
+  at::Tensor h = at::empty({M, f}, A.options());
+  if (M == 0) return {u, h};
+  c10::cuda::CUDAGuard guard(A.device());
+  const CUtensorMap ta = make_tmap_2d(A.data_ptr(), M, K, A.stride(0), kBM);
+  const CUtensorMap tb = make_tmap_2d(B.data_ptr(), N2, K, B.stride(0), 128);
+  const EpiAux aux{nullptr, nullptr, reinterpret_cast<__nv_bfloat16*>(h.data_ptr()), f, static_cast<int>(f), 0};
+  launch_pair<256, false, false, kE2Swiglu>(ta, tb, u.data_ptr(), nullptr, static_cast<int>(M), static_cast<int>(N2),
+                                            static_cast<int>(K), N2, 0, PairArgs{1, nullptr, nullptr, nullptr},
+                                            cur_stream(), aux);
+  return {u, h};
+}
+
+// The fc2 input gradient with the SwiGLU backward in the epilogue: dh = G @ W (G [M, K]; W = fc2 weight [K, f]
+// (w_mn) or [f, K]) is not stored; with u = [a | b] the saved fc1 | gate output ([M, 2f], any 16-byte aligned row
+// stride) the epilogue writes dU[:, :f] = d silu(a) b / da and dU[:, f:] = d / db. Values equal gemm() followed by
+// swiglu_bwd.
+void gemm_swiglu_bwd(const at::Tensor& G, const at::Tensor& W, bool w_mn, const at::Tensor& U, at::Tensor& dU) {
+  FYB_RANGE("fyb::gemm_swiglu_bwd");
+  check_rows16(G, "gemm_swiglu_bwd: G must be bf16 [M, K] with 16-byte aligned rows");
+  check_rows16(W, "gemm_swiglu_bwd: W must be bf16 with 16-byte aligned rows");
+  check_rows16(U, "gemm_swiglu_bwd: u must be bf16 [M, 2f] with 16-byte aligned rows");
+  check_rows16(dU, "gemm_swiglu_bwd: du must be bf16 [M, 2f] with 16-byte aligned rows");
+  const int64_t M = G.size(0), K = G.size(1);
+  const int64_t f = w_mn ? W.size(1) : W.size(0);
+  FYB_CHECK((w_mn ? W.size(0) : W.size(1)) == K && K > 0, "gemm_swiglu_bwd: inner dimensions differ");
+  FYB_CHECK(f % 32 == 0 && U.size(0) == M && U.size(1) == 2 * f && dU.size(0) == M && dU.size(1) == 2 * f,
+            "gemm_swiglu_bwd: u / du must be [M, 2f] with f a multiple of 32");
+  FYB_CHECK(M < (1ll << 31) && f < (1ll << 30) && K < (1ll << 31), "gemm_swiglu_bwd: dimension too large");
+  if (M == 0) return;
+  c10::cuda::CUDAGuard guard(G.device());
+  const CUtensorMap ta = make_tmap_2d(G.data_ptr(), M, K, G.stride(0), kBM);
+  const CUtensorMap tb = w_mn ? make_tmap_2d(W.data_ptr(), K, f, W.stride(0), 64)
+                              : make_tmap_2d(W.data_ptr(), f, K, W.stride(0), 128);
+  const EpiAux aux{reinterpret_cast<const __nv_bfloat16*>(U.data_ptr()), nullptr, nullptr, U.stride(0),
+                   static_cast<int>(f), 0};
+  const PairArgs pa{1, nullptr, nullptr, nullptr};
+  const int m = static_cast<int>(M), n = static_cast<int>(f), k = static_cast<int>(K);
+  if (w_mn)
+    launch_pair<256, false, true, kE2SwigluBwd>(ta, tb, dU.data_ptr(), nullptr, m, n, k, dU.stride(0), 0, pa,
+                                                cur_stream(), aux);
+  else
+    launch_pair<256, false, false, kE2SwigluBwd>(ta, tb, dU.data_ptr(), nullptr, m, n, k, dU.stride(0), 0, pa,
+                                                 cur_stream(), aux);
 }
 
 }  // namespace fyb
