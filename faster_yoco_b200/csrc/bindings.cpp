@@ -16,7 +16,7 @@ int64_t gemm_sq(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool ac
 int64_t gemm_sq_slots(int64_t M, int64_t N, int64_t K);
 std::vector<int64_t> gemm_route(int64_t M, int64_t N, int64_t K);
 void gemm_rope(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const at::Tensor& cos_t,
-               const at::Tensor& sin_t, int64_t L, int64_t rot_cols);
+               const at::Tensor& sin_t, int64_t L, int64_t rot_cols, int64_t bn);
 std::vector<at::Tensor> gemm_swiglu(const at::Tensor& A, const at::Tensor& B);
 void gemm_swiglu_bwd(const at::Tensor& G, const at::Tensor& W, bool w_mn, const at::Tensor& U, at::Tensor& dU);
 void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, const at::Tensor& grad_flat,
@@ -148,7 +148,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("residual") = py::none(), py::arg("bn") = 256, py::arg("splits") = 1);
   m.def("gemm_rope", &fyb::gemm_rope,
         "C = A @ B^T with the interleaved rotary embedding of the leading rot_cols columns in the epilogue",
-        py::arg("A"), py::arg("B"), py::arg("C"), py::arg("cos"), py::arg("sin"), py::arg("L"), py::arg("rot_cols"));
+        py::arg("A"), py::arg("B"), py::arg("C"), py::arg("cos"), py::arg("sin"), py::arg("L"), py::arg("rot_cols"),
+        py::arg("bn") = 256);
   m.def("gemm_swiglu", &fyb::gemm_swiglu,
         "{u, h}: u = A @ [fc1; gate]^T and h = silu(u[:, :f]) * u[:, f:] from one GEMM (SwiGLU epilogue)");
   m.def("gemm_swiglu_bwd", &fyb::gemm_swiglu_bwd,

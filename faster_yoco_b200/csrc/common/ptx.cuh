@@ -86,6 +86,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // ------------------------------------------------------------------------------------------------------------------
 // TMA tensor loads: each CTA loads its own tiles from this GPU's memory
 
+// bring the 128-byte line holding p into L2 (no register result, no wait)
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -290,8 +295,10 @@ __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(_
 // activation / rotary pieces shared by the elementwise kernels and the fused GEMM epilogues: one definition, so the
 // fused and the separate forms round identically
 
-// sigmoid with the hardware reciprocal (__frcp_rn: one correctly rounded reciprocal instead of a full division)
-__device__ __forceinline__ float sigmoidf_(float x) { return __frcp_rn(1.0f + __expf(-x)); }
+// sigmoid as 1 / (1 + e^-x) with the fast division (__fdividef: an approximate reciprocal and a multiply, a couple of
+// fp32 ulps like the reference's Triton sigmoid; 0 once e^-x passes 2^126, the limit, with no slow path -- a
+// correctly rounded reciprocal branches to a long sequence for such inputs, which stalls a GEMM epilogue)
+__device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 // SwiGLU value silu(a) * b (kernel/swiglu.py:4-17: silu of the first operand)
 __device__ __forceinline__ float swiglu_val(float a, float b) { return a * b * sigmoidf_(a); }

@@ -437,6 +437,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     for (int u = cluster_id; u < num_units; u += num_clusters) {
       const int t = u / splits;
       const int mb = t % num_m, nb = t / num_m;
+      if constexpr (EPI == kE2SwigluBwd) {
+        // the saved a, b of this tile's rows into L2 while its mainloop still runs (the chunk loop below then
+        // waits for L2, not DRAM): per thread its row's BN columns of both halves, 128-byte lines
+        const int prow = mb * 2 * kBM + static_cast<int>(crank) * kBM + q * 32 + lane;
+        if (prow < M) {
+          const __nv_bfloat16* u = aux.t0 + static_cast<int64_t>(prow) * aux.ld2;
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) {
+            const int pc = nb * BN + 64 * j;
+            if (pc < N) {
+              prefetch_l2(u + pc);
+              prefetch_l2(u + aux.i0 + pc);
+            }
+          }
+        }
+      }
       if (!mbar_wait(&tfull[acc], acc_ph, abort_flag, status, 25)) break;
       tc_fence_after();
       const int row = mb * 2 * kBM + static_cast<int>(crank) * kBM + q * 32 + lane;
@@ -502,25 +518,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         }
       }
       const int pos = EPI == kE2Rope && row < M ? row % aux.i0 : 0;
+      // kE2SwigluBwd: the saved a, b of chunk c + 1 are loaded while chunk c is processed
+      uint32_t ua[16], ub[16];
+      if (EPI == kE2SwigluBwd && row < M && nb * BN < N) {
+        const __nv_bfloat16* u = aux.t0 + static_cast<int64_t>(row) * aux.ld2 + nb * BN;
+        load16x2(u, ua);
+        load16x2(u + aux.i0, ub);
+      }
 #pragma unroll 1
       for (int c = 0; EPI != kE2Swiglu && last && c < BN / 32; ++c) {
         uint32_t r[32];
-        uint32_t ua[16], ub[16];
         const int col = nb * BN + c * 32;
-        if (EPI == kE2SwigluBwd && row < M && col < N) {
-          // the saved a, b of these columns, loaded ahead of the accumulator read
-          const __nv_bfloat16* u = aux.t0 + static_cast<int64_t>(row) * aux.ld2 + col;
-          load16x2(u, ua);
-          load16x2(u + aux.i0, ub);
-        }
         tmem_ld32(tb + c * 32, r);        // warp-collective: every lane, whatever its row
         tmem_ld_wait();
         if constexpr (EPI == kE2SwigluBwd) {
           if (row < M && col < N) {
             uint32_t pa[16], pb[16];
+            uint32_t ca[16], cb[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) ca[k] = ua[k], cb[k] = ub[k];
+            if (c + 1 < BN / 32 && col + 32 < N) {
+              const __nv_bfloat16* u = aux.t0 + static_cast<int64_t>(row) * aux.ld2 + col + 32;
+              load16x2(u, ua);
+              load16x2(u + aux.i0, ub);
+            }
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
-              const float2 a = unpack_bf16(ua[k]), b = unpack_bf16(ub[k]);
+              const float2 a = unpack_bf16(ca[k]), b = unpack_bf16(cb[k]);
               const float g0 = bf16_round(__uint_as_float(r[2 * k])), g1 = bf16_round(__uint_as_float(r[2 * k + 1]));
               float da0, db0, da1, db1;
               swiglu_grad(a.x, b.x, g0, da0, db0);
@@ -744,8 +768,9 @@ void check_rows16(const at::Tensor& t, const char* what) {
 // C = A @ B^T (A [M, K], B [N, K], both K-major) with the interleaved rotary embedding applied in the epilogue to
 // the leading rot_cols columns (the q / k head blocks of a projection), token row r at position r mod L.
 // cos / sin: bf16 [>= L, 64] (head dim 128), the tables rope_fwd takes. Rounding as gemm() followed by rope_fwd.
+// bn: output tile width of the pair kernel (256, 192 or 128; the routed width of the plain GEMM of this shape).
 void gemm_rope(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const at::Tensor& cos_t,
-               const at::Tensor& sin_t, int64_t L, int64_t rot_cols) {
+               const at::Tensor& sin_t, int64_t L, int64_t rot_cols, int64_t bn) {
   FYB_RANGE("fyb::gemm_rope");
   check_rows16(A, "gemm_rope: A must be bf16 [M, K] with 16-byte aligned rows");
   check_rows16(B, "gemm_rope: B must be bf16 [N, K] with 16-byte aligned rows");
@@ -759,16 +784,22 @@ void gemm_rope(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const at
     FYB_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->dim() == 2 &&
                   t->size(0) >= L && t->size(1) == 64 && reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
               "gemm_rope: cos / sin must be contiguous bf16 [>= L, 64]");
+  FYB_CHECK(bn == 256 || bn == 192 || bn == 128, "gemm_rope: tile width must be 256, 192 or 128");
   if (M == 0 || N == 0) return;
   c10::cuda::CUDAGuard guard(A.device());
   const CUtensorMap ta = make_tmap_2d(A.data_ptr(), M, K, A.stride(0), kBM);
-  const CUtensorMap tb = make_tmap_2d(B.data_ptr(), N, K, B.stride(0), 128);
+  const CUtensorMap tb = make_tmap_2d(B.data_ptr(), N, K, B.stride(0), static_cast<int>(bn / 2));
   const EpiAux aux{reinterpret_cast<const __nv_bfloat16*>(cos_t.data_ptr()),
                    reinterpret_cast<const __nv_bfloat16*>(sin_t.data_ptr()), nullptr, 0, static_cast<int>(L),
                    static_cast<int>(rot_cols)};
-  launch_pair<256, false, false, kE2Rope>(ta, tb, C.data_ptr(), nullptr, static_cast<int>(M), static_cast<int>(N),
-                                          static_cast<int>(K), C.stride(0), 0, PairArgs{1, nullptr, nullptr, nullptr},
-                                          cur_stream(), aux);
+  const PairArgs pa{1, nullptr, nullptr, nullptr};
+  const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
+  if (bn == 256) launch_pair<256, false, false, kE2Rope>(ta, tb, C.data_ptr(), nullptr, m, n, k, C.stride(0), 0, pa,
+                                                         cur_stream(), aux);
+  else if (bn == 192) launch_pair<192, false, false, kE2Rope>(ta, tb, C.data_ptr(), nullptr, m, n, k, C.stride(0), 0,
+                                                              pa, cur_stream(), aux);
+  else launch_pair<128, false, false, kE2Rope>(ta, tb, C.data_ptr(), nullptr, m, n, k, C.stride(0), 0, pa,
+                                               cur_stream(), aux);
 }
 
 // The merged fc1 | gate projection with SwiGLU in the epilogue: u = A @ B^T (A [M, K], B = [fc1; gate] [2f, K], both

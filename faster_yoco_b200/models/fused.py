@@ -41,11 +41,19 @@ def _ngrad(w: torch.Tensor, dw: torch.Tensor):
     return dw
 
 
+def _fuse_ok(f: int) -> bool:
+    """The fused GEMM epilogues apply (FYB_GEMM_FUSE on, widths the 16-byte stores and 32-column chunks cover)."""
+    return ops.GEMM_FUSE and f % 32 == 0
+
+
 def _ffn_forward(x1, wn2, wfc1g, wfc2, eps, f):
     C = _C()
     h2, r2 = C.rms_norm_fwd(x1, wn2, eps)
-    u = ops.gemm(h2, wfc1g)
-    a = C.swiglu_fwd(u[:, :f], u[:, f:])
+    if _fuse_ok(f):
+        u, a = ops.gemm_swiglu(h2, wfc1g)          # SwiGLU in the fc1 | gate GEMM's epilogue
+    else:
+        u = ops.gemm(h2, wfc1g)
+        a = C.swiglu_fwd(u[:, :f], u[:, f:])
     xo = ops.gemm(a, wfc2, residual=x1)
     return xo, (h2, r2, u, a)
 
@@ -55,10 +63,13 @@ def _ffn_backward(dxo, x1, wn2, wfc1g, wfc2, saved, f):
     C = _C()
     h2, r2, u, a = saved
     T = dxo.shape[0]
-    da = ops.gemm(dxo, wfc2, b_mn_major=True)
-    g_fc2 = _wgrad(wfc2, dxo, a)
     du = torch.empty(T, 2 * f, dtype=dxo.dtype, device=dxo.device)
-    C.swiglu_bwd(u[:, :f], u[:, f:], da, du[:, :f], du[:, f:])
+    if _fuse_ok(f):
+        ops.gemm_swiglu_bwd(dxo, wfc2, u, du)       # the SwiGLU backward in the fc2 input-gradient epilogue
+    else:
+        da = ops.gemm(dxo, wfc2, b_mn_major=True)
+        C.swiglu_bwd(u[:, :f], u[:, f:], da, du[:, :f], du[:, f:])
+    g_fc2 = _wgrad(wfc2, dxo, a)
     dh2 = ops.gemm(du, wfc1g, b_mn_major=True)
     g_fc1g = _wgrad(wfc1g, du, h2)
     dx1, dwn2 = C.rms_norm_bwd(dh2, x1, wn2, r2, dxo)
@@ -77,10 +88,17 @@ class SelfRetentionLayerFn(torch.autograd.Function):
         R = wqkvg.shape[0]
         x2 = x.reshape(T, d)
         h1, r1 = C.rms_norm_fwd(x2, wn1, eps)
-        y = ops.gemm(h1, wqkvg)
-        y3 = y.view(B, L, R)
-        q = C.rope_fwd(y3[..., :d].view(B, L, H, D), cos, sin, False)
-        k = C.rope_fwd(y3[..., d:2 * d].view(B, L, H, D), cos, sin, False)
+        if _fuse_ok(d):
+            # q, k rotated in the projection's epilogue, read in place from y
+            y = ops.gemm_rope(h1, wqkvg, cos, sin, L, 2 * d)
+            y3 = y.view(B, L, R)
+            q = y3[..., :d].view(B, L, H, D)
+            k = y3[..., d:2 * d].view(B, L, H, D)
+        else:
+            y = ops.gemm(h1, wqkvg)
+            y3 = y.view(B, L, R)
+            q = C.rope_fwd(y3[..., :d].view(B, L, H, D), cos, sin, False)
+            k = C.rope_fwd(y3[..., d:2 * d].view(B, L, H, D), cos, sin, False)
         v = y3[..., 2 * d:3 * d].view(B, L, H, D)
         if ops.RETENTION_FORM == "parallel":
             gcum = C.gate_cumsum_fwd(y[:, 4 * d:4 * d + H], B, L, float(norm))
@@ -142,10 +160,16 @@ class SelfWindowLayerFn(torch.autograd.Function):
         T = B * L
         x2 = x.reshape(T, d)
         h1, r1 = C.rms_norm_fwd(x2, wn1, eps)
-        y = ops.gemm(h1, wqkv)
-        y3 = y.view(B, L, 3 * d)
-        q = C.rope_fwd(y3[..., :d].view(B, L, H, D), cos, sin, False)
-        k = C.rope_fwd(y3[..., d:2 * d].view(B, L, H, D), cos, sin, False)
+        if _fuse_ok(d):
+            y = ops.gemm_rope(h1, wqkv, cos, sin, L, 2 * d)
+            y3 = y.view(B, L, 3 * d)
+            q = y3[..., :d].view(B, L, H, D)
+            k = y3[..., d:2 * d].view(B, L, H, D)
+        else:
+            y = ops.gemm(h1, wqkv)
+            y3 = y.view(B, L, 3 * d)
+            q = C.rope_fwd(y3[..., :d].view(B, L, H, D), cos, sin, False)
+            k = C.rope_fwd(y3[..., d:2 * d].view(B, L, H, D), cos, sin, False)
         v = y3[..., 2 * d:].view(B, L, H, D)
         scale = D ** -0.5
         o, lse = C.attention_fwd(q, k, v, True, int(window), scale)
@@ -192,8 +216,10 @@ class CrossLayerFn(torch.autograd.Function):
         T = B * L
         x2 = x.reshape(T, d)
         h1, r1 = C.rms_norm_fwd(x2, wn1, eps)
-        qp = ops.gemm(h1, wq)
-        q = C.rope_fwd(qp.view(B, L, Hq, D), cos, sin, False)
+        if _fuse_ok(d):
+            q = ops.gemm_rope(h1, wq, cos, sin, L, Hq * D).view(B, L, Hq, D)
+        else:
+            q = C.rope_fwd(ops.gemm(h1, wq).view(B, L, Hq, D), cos, sin, False)
         o, lse = C.attention_fwd(q, K, V, True, 0, D ** -0.5)
         x1 = ops.gemm(o.view(T, d), wout, residual=x2)
         xo, ffn_saved = _ffn_forward(x1, wn2, wfc1g, wfc2, eps, f)

@@ -118,6 +118,61 @@ def _gemm_route(M: int, N: int, K: int):
     return r
 
 
+# Elementwise epilogues of the CTA-pair GEMM (csrc/gemm2.cu): the rotary embedding of the q / k blocks in the
+# projection that produces them, SwiGLU in the merged fc1 | gate projection and the SwiGLU backward in the fc2 input
+# gradient. Each saves one read + write of an activation and a launch per layer. FYB_GEMM_FUSE=0 runs the GEMM and
+# the elementwise kernel separately (same values; comparison switch).
+GEMM_FUSE = os.environ.get("FYB_GEMM_FUSE", "1") == "1"
+
+
+def gemm_rope(a: torch.Tensor, w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, seq_len: int, rot_cols: int,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = a @ w.T with the interleaved rotary embedding (head dim 128) applied to columns [0, rot_cols) of every
+    row, row r at position r mod seq_len -- the values of gemm() followed by rope() on those head blocks.
+    a: [T, K]; w: [N, K]; cos / sin: the [>= seq_len, 64] tables of ``rope``."""
+    T, N = a.shape[0], w.shape[0]
+    if out is None:
+        out = torch.empty(T, N, dtype=a.dtype, device=a.device)
+    if native_on(a):
+        route = _gemm_route(T, N, a.shape[1])
+        bn = route[1] if route[0] == 1 and route[2] == 1 else 256
+        _C().gemm_rope(a, w, out, cos, sin, seq_len, rot_cols, bn)
+        return out
+    y = gemm(a, w, out=out)
+    if rot_cols:
+        blk = y[:, :rot_cols].view(T // seq_len, seq_len, rot_cols // 128, 128)
+        blk.copy_(ref.apply_rope(blk, cos[:seq_len], sin[:seq_len]))
+    return out
+
+
+def gemm_swiglu(a: torch.Tensor, w: torch.Tensor):
+    """(u, h): u = a @ w.T for the merged [fc1; gate] weight w [2f, K], h = silu(u[:, :f]) * u[:, f:] -- one GEMM
+    whose epilogue also computes the activation (values of gemm() followed by swiglu())."""
+    if native_on(a):
+        u, h = _C().gemm_swiglu(a, w)
+        return u, h
+    u = gemm(a, w)
+    f = u.shape[1] // 2
+    return u, ref.swiglu(u[:, :f], u[:, f:])
+
+
+def gemm_swiglu_bwd(g: torch.Tensor, w2: torch.Tensor, u: torch.Tensor, du: Optional[torch.Tensor] = None):
+    """du = [da | db], the SwiGLU backward of dh = g @ w2 (w2: the fc2 weight [d, f], g: [T, d]) against the saved
+    fc1 | gate output u [T, 2f], with dh never stored (values of gemm() followed by the swiglu backward)."""
+    if du is None:
+        du = torch.empty_like(u)
+    if native_on(g):
+        _C().gemm_swiglu_bwd(g, w2, True, u, du)
+        return du
+    dh = gemm(g, w2, b_mn_major=True)
+    f = u.shape[1] // 2
+    a32, b32 = u[:, :f].float(), u[:, f:].float()
+    s = torch.sigmoid(a32)
+    du[:, :f] = (s * (1 + a32 * (1 - s)) * dh.float() * b32).to(du.dtype)
+    du[:, f:] = (a32 * s * dh.float()).to(du.dtype)
+    return du
+
+
 class _NativeLinear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, residual):

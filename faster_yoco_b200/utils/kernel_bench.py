@@ -1,7 +1,7 @@
 """Per-kernel microbenchmarks: the sm_100a kernels against the library baselines (cuBLAS, flash-attn) on the
 YOCO-3B shapes, timed with CUDA events after warm-up, inputs rotated through a pool larger than L2.
 
-    python -m faster_yoco_b200.utils.kernel_bench [--only gemm|attn|ret] [--pair 1]
+    python -m faster_yoco_b200.utils.kernel_bench [--only gemm|fused|attn|ret] [--pair 1]
 """
 from __future__ import annotations
 
@@ -95,6 +95,83 @@ def bench_gemm(results, pair_too: bool = False):
         results.append(r)
 
 
+def bench_gemm_fused(results):
+    """The fused elementwise epilogues against the routed GEMM followed by the separate kernel, YOCO-3B shapes:
+    RoPE on q / k in the retention layer's QKVG projection and on q in a cross layer's q projection, SwiGLU in the
+    fc1 | gate projection, the SwiGLU backward in the fc2 input gradient."""
+    from faster_yoco_b200 import ops
+    dev = torch.device("cuda")
+    C = ops._C()
+    T, L, d, f, H = 2048, 2048, 3072, 8192, 24
+    ang = torch.rand(L, 64, device=dev) * 6.283
+    cos, sin = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+    bf = dict(device=dev, dtype=torch.bfloat16)
+    # training-scale operands: activations ~ N(0, 1), weights ~ N(0, 0.02), output gradients ~ 1e-3 (the
+    # activation's cost depends on the value range, e.g. a sigmoid of |x| > 88 takes a slow reciprocal path)
+
+    def wt(*shape):
+        return (torch.randn(*shape, device=dev) * 0.02).to(torch.bfloat16)
+
+    for name, N, rot in [("qkvg.fwd+rope", 4 * d + H, 2 * d), ("q_proj.fwd+rope", d, d)]:
+        pool = _pool(lambda: (torch.randn(T, d, **bf), wt(N, d)), 2 * (T * d + N * d))
+        y = torch.empty(T, N, **bf)
+        it = [0]
+
+        def fused():
+            a, w = pool[it[0] % len(pool)]
+            it[0] += 1
+            ops.gemm_rope(a, w, cos, sin, L, rot, out=y)
+
+        def separate():
+            a, w = pool[it[0] % len(pool)]
+            it[0] += 1
+            ops.gemm(a, w, out=y)
+            for c0 in range(0, rot, d):
+                C.rope_fwd(y[:, c0:c0 + d].view(1, L, H, 128), cos, sin, False)
+
+        tf, ts = _time(fused), _time(separate)
+        results.append({"kernel": "gemm_fused", "shape": name, "fused_ms": tf, "separate_ms": ts,
+                        "fused_tflops": 2.0 * T * N * d / tf / 1e9})
+    # SwiGLU forward
+    pool = _pool(lambda: (torch.randn(T, d, **bf), wt(2 * f, d)), 2 * (T * d + 2 * f * d))
+    it = [0]
+
+    def sw_fused():
+        a, w = pool[it[0] % len(pool)]
+        it[0] += 1
+        ops.gemm_swiglu(a, w)
+
+    def sw_separate():
+        a, w = pool[it[0] % len(pool)]
+        it[0] += 1
+        u = ops.gemm(a, w)
+        C.swiglu_fwd(u[:, :f], u[:, f:])
+
+    tf, ts = _time(sw_fused), _time(sw_separate)
+    results.append({"kernel": "gemm_fused", "shape": "fc1_gate.fwd+swiglu", "fused_ms": tf, "separate_ms": ts,
+                    "fused_tflops": 2.0 * T * 2 * f * d / tf / 1e9})
+    # SwiGLU backward in the fc2 input gradient
+    pool = _pool(lambda: ((torch.randn(T, d, device=dev) * 1e-3).to(torch.bfloat16), wt(d, f),
+                          torch.randn(T, 2 * f, **bf)),
+                 2 * (T * d + d * f + 2 * T * f))
+    du = torch.empty(T, 2 * f, **bf)
+
+    def sb_fused():
+        g, w2, u = pool[it[0] % len(pool)]
+        it[0] += 1
+        ops.gemm_swiglu_bwd(g, w2, u, du)
+
+    def sb_separate():
+        g, w2, u = pool[it[0] % len(pool)]
+        it[0] += 1
+        dh = ops.gemm(g, w2, b_mn_major=True)
+        C.swiglu_bwd(u[:, :f], u[:, f:], dh, du[:, :f], du[:, f:])
+
+    tf, ts = _time(sb_fused), _time(sb_separate)
+    results.append({"kernel": "gemm_fused", "shape": "fc2.dgrad+swiglu_bwd", "fused_ms": tf, "separate_ms": ts,
+                    "fused_tflops": 2.0 * T * f * d / tf / 1e9})
+
+
 def bench_attention(results, L=2048, Hq=24, Hk=8, B=1):
     from faster_yoco_b200 import ops
     dev = torch.device("cuda")
@@ -161,6 +238,8 @@ def main():
     res = []
     if a.only in (None, "gemm"):
         bench_gemm(res, pair_too=bool(a.pair))
+    if a.only in (None, "gemm", "fused"):
+        bench_gemm_fused(res)
     if a.only in (None, "attn"):
         bench_attention(res)
     if a.only in (None, "ret"):

@@ -6,7 +6,7 @@ cases: attn, attn_bwd, swa, swa_bwd (sliding window 1024), ret, ret_bwd (paralle
 ret_chunk_bwd (chunkwise kernels), gemm, gemm_dgrad, gemm_scatter (weight
 gradient stored at 4 emulated owners, block-cyclic map), adam, ce, ce_bwd, rms, rms_bwd, subln, subln_bwd, swiglu,
 swiglu_bwd, rope, embed, embed_bwd, reduce_compact, reduce_owner, adam_push (eight ranks emulated in local memory),
-gate_cumsum (chunk-local), gemm_pair, gemm_pair128.
+gate_cumsum (chunk-local), gemm_pair, gemm_pair128, gemm_swiglu, gemm_swiglu_bwd (fused epilogues).
 """
 import argparse
 
@@ -195,12 +195,23 @@ def main():
         y = torch.randn(2048, 12312, device=dev, dtype=torch.bfloat16)
         for _ in range(a.reps):
             C.gate_cumsum_fwd(y[:, 4 * 3072:4 * 3072 + 24], 1, 2048, 16.0, True)
-    elif a.what in ("gemm_pair", "gemm_pair128"):
+    elif a.what in ("gemm_pair", "gemm_pair128", "gemm_swiglu"):
+        # the fc1 | gate projection at training scale (activations ~ N(0, 1), weights ~ N(0, 0.02))
         x = torch.randn(2048, 3072, device=dev, dtype=torch.bfloat16)
-        w = torch.randn(16384, 3072, device=dev, dtype=torch.bfloat16)
+        w = (torch.randn(16384, 3072, device=dev) * 0.02).to(torch.bfloat16)
         y = torch.empty(2048, 16384, device=dev, dtype=torch.bfloat16)
         for _ in range(a.reps):
-            C.gemm_pair(x, w, y, False, False, None, 128 if a.what == "gemm_pair128" else 256)
+            if a.what == "gemm_swiglu":
+                C.gemm_swiglu(x, w)
+            else:
+                C.gemm_pair(x, w, y, False, False, None, 128 if a.what == "gemm_pair128" else 256)
+    elif a.what == "gemm_swiglu_bwd":
+        g = (torch.randn(2048, 3072, device=dev) * 1e-3).to(torch.bfloat16)
+        w2 = (torch.randn(3072, 8192, device=dev) * 0.02).to(torch.bfloat16)
+        u = torch.randn(2048, 16384, device=dev, dtype=torch.bfloat16)
+        du = torch.empty_like(u)
+        for _ in range(a.reps):
+            C.gemm_swiglu_bwd(g, w2, True, u, du)
     else:
         raise SystemExit(f"unknown --what {a.what}")
     torch.cuda.synchronize()

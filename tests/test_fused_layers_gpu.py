@@ -15,8 +15,19 @@ def rel(x, r):
     return ((x - r).abs().max() / r.abs().max().clamp_min(1e-6)).item()
 
 
+@pytest.mark.parametrize("gemm_fuse", [True, False])
 @pytest.mark.parametrize("window", [None, 96])
-def test_fused_layers_match_module_path(window, monkeypatch):
+def test_fused_layers_match_module_path(window, gemm_fuse, monkeypatch):
+    """gemm_fuse: RoPE / SwiGLU in the GEMM epilogues (default) or as separate kernels."""
+    old_fuse = ops.GEMM_FUSE
+    ops.GEMM_FUSE = gemm_fuse
+    try:
+        _check_fused_layers(window, monkeypatch)
+    finally:
+        ops.GEMM_FUSE = old_fuse
+
+
+def _check_fused_layers(window, monkeypatch):
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
     args = build_args("yoco_small", max_seq_len=384, init_std=0.02, sliding_window=window)
