@@ -45,11 +45,13 @@ def parse():
                         "transport at 2 GPUs (one peer: the copy engines reach 766 GB/s and take no SM time), off "
                         "(serial P2P reduce + push all-gather after backward) at more GPUs, where the copy engines "
                         "deliver only ~210 GB/s in aggregate to 7 peers")
-    p.add_argument("--transport", default="auto", choices=["auto", "sm", "ce", "gemm"],
+    p.add_argument("--transport", default="auto", choices=["auto", "sm", "ce", "gemm", "pull"],
                    help="overlapped exchange: pushes by kernels (sm) or by the copy engines (ce); gemm: the "
                         "weight-gradient GEMMs store every element at its ZeRO owner over NVLink (GEMM fused with the "
                         "reduce-scatter), parameters pushed after the update (--overlap 0) or per layer ahead of "
-                        "the next forward (--overlap 1)")
+                        "the next forward (--overlap 1); pull: the parameter all-gather fused into the consuming "
+                        "forward GEMMs (gather warps pull each weight's rows from their owners ahead of the tiles; "
+                        "use with --partition cyclic), gradients by the serial P2P reduce")
     p.add_argument("--partition", default="even", choices=["even", "greedy", "cyclic"],
                    help="ZeRO owner map: even contiguous segments, the OSS greedy per-parameter rule, or block-cyclic "
                         "chunks (every weight spread over all owners)")
@@ -236,7 +238,7 @@ def main():
     dev = torch.device("cuda", dev_index)
     ops.set_backend(args.kernels)
     if args.overlap == "auto":
-        args.overlap = 1 if (world == 2 and args.comm == "fused" and args.transport != "gemm") else 0
+        args.overlap = 1 if (world == 2 and args.comm == "fused" and args.transport not in ("gemm", "pull")) else 0
     else:
         args.overlap = int(args.overlap)
     if args.transport == "auto":

@@ -132,10 +132,11 @@ def train_parser() -> argparse.ArgumentParser:
     g.add_argument("--overlap", default="auto",
                    help="overlap the ZeRO exchange with forward/backward: auto (copy-engine pushes at 2 GPUs, "
                         "serial exchange otherwise), 1 or 0")
-    g.add_argument("--transport", default="auto", choices=["auto", "sm", "ce", "gemm"],
+    g.add_argument("--transport", default="auto", choices=["auto", "sm", "ce", "gemm", "pull"],
                    help="overlapped pushes by kernels (sm) or by the copy engines (ce); gemm: serial schedule whose "
                         "weight-gradient GEMMs store each element at its ZeRO owner (GEMM fused with the "
-                        "reduce-scatter)")
+                        "reduce-scatter); pull: the parameter all-gather fused into the consuming forward GEMMs "
+                        "(use with --partition cyclic)")
     g.add_argument("--partition", default="even", choices=["even", "greedy", "cyclic"],
                    help="ZeRO owner map: even contiguous split, the fairscale OSS greedy per-parameter split, or "
                         "block-cyclic chunks (every weight spread over all owners)")

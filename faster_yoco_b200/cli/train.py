@@ -141,8 +141,10 @@ def main(argv=None) -> int:
     rep = cp if cp > 1 else tp                # consecutive ranks that hold one model replica
     dp = world // rep
     comm = args.comm if (dp > 1 and device.type == "cuda" and rep == 1) else "nccl"
-    overlap = (world == 2 and comm == "fused" and args.transport != "gemm") if str(args.overlap) == "auto" \
-        else bool(_flag(args.overlap))
+    if str(args.overlap) == "auto":
+        overlap = world == 2 and comm == "fused" and args.transport not in ("gemm", "pull")
+    else:
+        overlap = bool(_flag(args.overlap))
     if tp > 1:
         overlap = False
     transport = ("ce" if world == 2 else "sm") if args.transport == "auto" else args.transport
@@ -188,6 +190,7 @@ def main(argv=None) -> int:
                 print(line, flush=True)
         if (not args.disable_validation and args.validate_interval_updates > 0
                 and nu % args.validate_interval_updates == 0):
+            trainer.sync_params()          # lazily gathered parameters current before evaluating
             v = validate_lm(model, task, args, device, rank, world, rep, cp, tp)
             if v is not None and rank == 0:
                 print(f"valid on '{args.valid_subset}' subset | loss {v['loss']} | ppl {v['ppl']} | "
@@ -207,6 +210,7 @@ def main(argv=None) -> int:
                 prune_interval_checkpoints(args.save_dir, args.keep_interval_updates)
     trainer.pending.check(block=True)
     if not args.disable_validation and args.validate_interval_updates <= 0:
+        trainer.sync_params()
         v = validate_lm(model, task, args, device, rank, world, rep, cp, tp)
         if v is not None and rank == 0:
             print(f"valid on '{args.valid_subset}' subset | loss {v['loss']} | ppl {v['ppl']} | "

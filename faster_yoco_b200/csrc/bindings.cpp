@@ -19,6 +19,12 @@ void gemm_rope(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const at
                const at::Tensor& sin_t, int64_t L, int64_t rot_cols, int64_t bn);
 std::vector<at::Tensor> gemm_swiglu(const at::Tensor& A, const at::Tensor& B);
 void gemm_swiglu_bwd(const at::Tensor& G, const at::Tensor& W, bool w_mn, const at::Tensor& U, at::Tensor& dU);
+void gemm_gather(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const at::Tensor& flat,
+                 const at::Tensor& peers, int64_t seg, int64_t chunk, int64_t rank, int64_t bn,
+                 const c10::optional<at::Tensor>& cos_t, const c10::optional<at::Tensor>& sin_t, int64_t L,
+                 int64_t rot_cols, const c10::optional<at::Tensor>& residual);
+std::vector<at::Tensor> gemm_gather_swiglu(const at::Tensor& A, const at::Tensor& B, const at::Tensor& flat,
+                                           const at::Tensor& peers, int64_t seg, int64_t chunk, int64_t rank);
 void gemm_scatter(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool accumulate, const at::Tensor& grad_flat,
                   const at::Tensor& bases, int64_t seg, int64_t rank, int64_t chunk);
 std::vector<at::Tensor> rms_norm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps);
@@ -155,6 +161,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_swiglu_bwd", &fyb::gemm_swiglu_bwd,
         "du = SwiGLU backward of (G @ W) against the saved u, computed in the GEMM epilogue", py::arg("G"),
         py::arg("W"), py::arg("w_mn"), py::arg("u"), py::arg("du"));
+  m.def("gemm_gather", &fyb::gemm_gather,
+        "C = A @ B^T with the ZeRO all-gather of the weight B fused in: the GEMM's gather warps pull B's rows owned by "
+        "other ranks from their replicas (peer loads) ahead of the tiles that read them",
+        py::arg("A"), py::arg("B"), py::arg("C"), py::arg("flat"), py::arg("peers"), py::arg("seg"),
+        py::arg("chunk"), py::arg("rank"), py::arg("bn") = 256, py::arg("cos") = py::none(),
+        py::arg("sin") = py::none(), py::arg("L") = 0, py::arg("rot_cols") = 0, py::arg("residual") = py::none());
+  m.def("gemm_gather_swiglu", &fyb::gemm_gather_swiglu,
+        "{u, h} of the fc1 | gate projection with the weight's all-gather fused in and SwiGLU in the epilogue",
+        py::arg("A"), py::arg("B"), py::arg("flat"), py::arg("peers"), py::arg("seg"), py::arg("chunk"),
+        py::arg("rank"));
   m.def("gemm_route", &fyb::gemm_route, "kernel choice {0 one-CTA / 1 CTA pair, tile width, splits} for an M x N x K GEMM");
   m.def("gemm_sq", &fyb::gemm_sq,
         "weight gradient dW = A^T B (bf16, optionally accumulated) with fp32 sum-of-squares partials of the stored "

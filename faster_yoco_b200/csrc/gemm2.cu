@@ -28,6 +28,87 @@ namespace {
 constexpr int kBM = 128;        // rows of A (and of the output) per CTA
 constexpr int kBK = 64;
 constexpr int kThreads2 = 192;
+constexpr int kThreadsG = 320;  // the gather form: + 4 warps that pull the weight rows from their ZeRO owners
+constexpr int kGatherThreads = kThreadsG - kThreads2;
+
+// The ZeRO parameter all-gather fused into a forward GEMM (the consumer of the gathered weight). B is a contiguous
+// [N, K] weight inside this rank's flat parameter replica (element offset w_off); after the owners' optimizer
+// step only the rows this rank owns are current here. Every tile (mb, nb) of the GEMM is computed by one CTA pair,
+// and its two CTAs' gather warps pull shares 2 mb and 2 mb + 1 (of 2 num_m) of B's tile column nb -- the elements
+// [w_off + 256 nb K, w_off + 256 (nb + 1) K) -- from the owners' replicas into this one, with plain 16-byte loads of
+// peer memory, then count the share done on counters[nb] (release). Before loading tile column nb with TMA (from
+// this replica only) the producer waits (acquire, bounded) for all 2 num_m shares. The gather warps never wait, so
+// the column a producer waits for is always being copied; they run ahead of the MMAs through the CTA's tile list,
+// so the NVLink transfer of the next tiles overlaps the math of the current ones.
+// Owner of flat element x: (x / chunk) mod world (block-cyclic map) or x / seg (contiguous segments).
+struct GatherArgs {
+  const int64_t* peers;      // [world] base addresses of every rank's flat replica (this rank's entry unused)
+  __nv_bfloat16* local;      // this rank's flat replica
+  int64_t w_off;             // element offset of B[0, 0] in the flat buffer
+  int64_t seg;               // owner segment length (elements)
+  int64_t chunk;             // block-cyclic chunk (elements), 0: contiguous segments
+  int* counters;             // [num_n] shares done per tile column, zero at launch
+  int world, rank;
+};
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// generic-proxy writes of this thread (or ordered before it) vs. async-proxy (TMA) accesses of global memory
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// bounded wait until *p >= target (status word + abort flag on timeout, like the mbarrier waits)
+__device__ __forceinline__ bool wait_count(const int* p, int target, volatile int* abort, int* status, int site) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+#pragma unroll 1
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(32);
+    if (ld_acquire_gpu(p) >= target) return true;
+    if ((it & 63u) == 0u) {
+      if (abort != nullptr && *abort) return false;
+      if (globaltimer_ns() - t0 > FYB_WAIT_NS) {
+        record_status(status, kPeerTimeout, site);
+        if (abort != nullptr) *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// copy the elements [lo, hi) of the flat buffer that other ranks own from their replicas into this one; called by
+// the kGatherThreads gather threads (index gt), 8 loads of 16 bytes in flight per thread
+__device__ __forceinline__ void gather_range(const GatherArgs& ga, int64_t lo, int64_t hi, int gt) {
+  const int64_t step = ga.chunk ? ga.chunk : ga.seg;
+  int64_t x = lo;
+#pragma unroll 1
+  while (x < hi) {
+    const int64_t blk = x / step;
+    const int64_t end = min(hi, (blk + 1) * step);
+    const int owner = ga.chunk ? static_cast<int>(blk % ga.world) : static_cast<int>(blk);
+    if (owner != ga.rank) {
+      const uint4* src = reinterpret_cast<const uint4*>(ga.peers[owner] + x * 2);
+      uint4* dst = reinterpret_cast<uint4*>(ga.local + x);
+      const int64_t nv = (end - x) >> 3;
+#pragma unroll 1
+      for (int64_t i = gt; i < nv; i += 8 * kGatherThreads) {
+        uint4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (i + j * kGatherThreads < nv) v[j] = src[i + j * kGatherThreads];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (i + j * kGatherThreads < nv) dst[i + j * kGatherThreads] = v[j];
+      }
+    }
+    x = end;
+  }
+}
 
 // kE2Bf16Sq / kE2Bf16ResSq: the bf16 store plus the sum of squares of the stored values, one fp32 partial per
 // (tile, CTA of the pair, epilogue warp) -- the weight-gradient form behind the one-GPU clip norm.
@@ -276,11 +357,12 @@ __device__ __forceinline__ void rope_store32(const uint32_t (&r)[32], __nv_bfloa
   store16x2(C, p);
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
+template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER = false>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG : kThreads2, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* Cv,
                      const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, int splits, float* ws,
-                     int* counters, int* status, float* sq_part, const EpiAux aux) {
+                     int* counters, int* status, float* sq_part, const EpiAux aux, const GatherArgs ga) {
+  static_assert(!GATHER || !B_MN, "the gather form reads K-major weight rows");
   static_assert(EPI != kE2Swiglu || (BN == 256 && !B_MN), "the SwiGLU epilogue pairs two 128-row B halves");
   constexpr int kStages2 = PairCfg<BN>::STAGES;
   using S = Smem2<BN, kStages2>;
@@ -351,6 +433,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         const int n0 = EPI == kE2Swiglu ? nb * 128 + static_cast<int>(crank) * aux.i0
                                         : nb * BN + static_cast<int>(crank) * (BN / 2);
         const int kb0 = (u % splits) * k_chunk, kb1 = min(num_k, kb0 + k_chunk);
+        if constexpr (GATHER) {
+          // every share of tile column nb pulled into this replica (then visible to the TMA loads below)
+          if (!wait_count(ga.counters + nb, 2 * num_m, abort_flag, status, 27)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_global();
+        }
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, status, 21)) {
             ok = false;
@@ -427,6 +517,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         umma_commit_pair(mapa_u32(&tfull[acc], 1));
         acc ^= 1;
         if (acc == 0) acc_ph ^= 1u;
+      }
+    }
+  } else if (GATHER && warp >= kThreads2 / 32) {
+    // ---------------------------------------------------------------------------------------- gather (pull)
+    const int gt = threadIdx.x - kThreads2;
+    const int shares = 2 * num_m;
+#pragma unroll 1
+    for (int u = cluster_id; u < num_units; u += num_clusters) {
+      const int mb = u % num_m, nb = u / num_m;
+      int64_t lo_all, tot, per;
+      int share;
+      if constexpr (EPI == kE2Swiglu) {
+        // the tile reads rows [128 nb, 128 nb + 128) of the fc1 half (CTA 0's B half) and the same rows of the gate
+        // half (CTA 1's): each CTA pulls share mb of num_m of its own half
+        const int f = aux.i0;
+        const int r0 = static_cast<int>(crank) * f + nb * 128;
+        const int r1 = min(static_cast<int>(crank) * f + f, r0 + 128);
+        lo_all = ga.w_off + static_cast<int64_t>(r0) * K;
+        tot = static_cast<int64_t>(max(0, r1 - r0)) * K;
+        per = ((tot / 8 + num_m - 1) / num_m) * 8;
+        share = mb;
+      } else {
+        lo_all = ga.w_off + static_cast<int64_t>(nb) * BN * K;
+        tot = static_cast<int64_t>(min(N, (nb + 1) * BN) - nb * BN) * K;
+        per = ((tot / 8 + shares - 1) / shares) * 8;      // whole 16-byte vectors per share
+        share = mb * 2 + static_cast<int>(crank);
+      }
+      const int64_t lo = lo_all + min(tot, share * per), hi = lo_all + min(tot, (share + 1) * per);
+      gather_range(ga, lo, hi, gt);
+      asm volatile("bar.sync 1, %0;" ::"n"(kGatherThreads) : "memory");   // the gather warps only
+      if (gt == 0) {
+        fence_proxy_async_global();
+        asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(ga.counters + nb), "r"(1) : "memory");
       }
     }
   } else {
@@ -609,11 +732,12 @@ struct PairArgs {
   float* sq_part;
 };
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER = false>
 void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const __nv_bfloat16* R, int M, int N, int K,
-                 int64_t ldc, int64_t ldr, const PairArgs& pa, cudaStream_t stream, const EpiAux& aux = EpiAux{}) {
+                 int64_t ldc, int64_t ldr, const PairArgs& pa, cudaStream_t stream, const EpiAux& aux = EpiAux{},
+                 const GatherArgs& ga = GatherArgs{}) {
   using S = Smem2<BN, PairCfg<BN>::STAGES>;
-  auto kern = gemm_pair_kernel<BN, A_MN, B_MN, EPI>;
+  auto kern = gemm_pair_kernel<BN, A_MN, B_MN, EPI, GATHER>;
   static bool attr_set = false;
   if (!attr_set) {
     FYB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL));
@@ -621,8 +745,8 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const __
   }
   const int units = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + BN - 1) / BN) * pa.splits;
   const int clusters = std::max(1, std::min(units, num_sms() / 2));
-  kern<<<2 * clusters, kThreads2, S::TOTAL, stream>>>(ta, tb, C, R, M, N, K, ldc, ldr, pa.splits, pa.ws,
-                                                      pa.counters, status_ptr(), pa.sq_part, aux);
+  kern<<<2 * clusters, GATHER ? kThreadsG : kThreads2, S::TOTAL, stream>>>(
+      ta, tb, C, R, M, N, K, ldc, ldr, pa.splits, pa.ws, pa.counters, status_ptr(), pa.sq_part, aux, ga);
   check_launch("gemm_pair");
 }
 
@@ -857,6 +981,121 @@ void gemm_swiglu_bwd(const at::Tensor& G, const at::Tensor& W, bool w_mn, const 
   else
     launch_pair<256, false, false, kE2SwigluBwd>(ta, tb, dU.data_ptr(), nullptr, m, n, k, dU.stride(0), 0, pa,
                                                  cur_stream(), aux);
+}
+
+// C = A @ B^T with the ZeRO parameter all-gather of B fused in (GatherArgs): A [M, K] K-major activations; B a
+// contiguous [N, K] weight view of `flat`, this rank's parameter replica, whose rows owned by other ranks are stale;
+// peers: int64 [world] device tensor of every rank's replica base address (entry `rank` unused); seg / chunk: the
+// owner map (chunk 0: contiguous segments of seg elements). On return B's rows are every owner's current values and
+// C = A @ B^T. With cos / sin (the rope tables), the leading rot_cols columns are rotated as in gemm_rope (L: sequence
+// length). bn: 256 or 192.
+namespace {
+GatherArgs make_gather_args(const at::Tensor& A, const at::Tensor& B, const at::Tensor& flat, const at::Tensor& peers,
+                            int64_t seg, int64_t chunk, int64_t rank, int64_t num_n, at::Tensor& counters) {
+  const int64_t K = A.size(1), N = B.size(0);
+  FYB_CHECK(B.is_cuda() && B.scalar_type() == at::kBFloat16 && B.dim() == 2 && B.size(1) == K && B.is_contiguous(),
+            "gemm_gather: B must be a contiguous bf16 [N, K] weight");
+  FYB_CHECK(flat.is_cuda() && flat.scalar_type() == at::kBFloat16 && flat.is_contiguous(),
+            "gemm_gather: flat must be the contiguous bf16 replica");
+  const int64_t w_off = (reinterpret_cast<intptr_t>(B.data_ptr()) - reinterpret_cast<intptr_t>(flat.data_ptr())) / 2;
+  FYB_CHECK(w_off >= 0 && w_off + N * K <= flat.numel() && w_off % 8 == 0,
+            "gemm_gather: B must lie inside flat at a 16-byte aligned element offset");
+  FYB_CHECK(reinterpret_cast<uintptr_t>(flat.data_ptr()) % 16 == 0 && K % 8 == 0 && K > 0,
+            "gemm_gather: 16-byte aligned replica and K a multiple of 8");
+  FYB_CHECK(peers.is_cuda() && peers.scalar_type() == at::kLong && peers.is_contiguous() && peers.dim() == 1,
+            "gemm_gather: peers must be a device int64 [world] tensor");
+  const int64_t world = peers.numel();
+  FYB_CHECK(world >= 1 && rank >= 0 && rank < world, "gemm_gather: rank out of range");
+  FYB_CHECK(seg > 0 && seg % 8 == 0 && chunk >= 0 && chunk % 8 == 0,
+            "gemm_gather: owner map sizes must be multiples of 8 elements");
+  FYB_CHECK(flat.numel() <= world * seg, "gemm_gather: flat larger than world x seg");
+  counters = at::zeros({num_n}, A.options().dtype(at::kInt));
+  return GatherArgs{peers.data_ptr<int64_t>(), reinterpret_cast<__nv_bfloat16*>(flat.data_ptr()), w_off, seg, chunk,
+                    counters.data_ptr<int>(), static_cast<int>(world), static_cast<int>(rank)};
+}
+}  // namespace
+
+// The fc1 | gate projection with the all-gather of its merged weight fused in (gemm_gather) and SwiGLU in the
+// epilogue (gemm_swiglu): returns {u, h}.
+std::vector<at::Tensor> gemm_gather_swiglu(const at::Tensor& A, const at::Tensor& B, const at::Tensor& flat,
+                                           const at::Tensor& peers, int64_t seg, int64_t chunk, int64_t rank) {
+  FYB_RANGE("fyb::gemm_gather_swiglu");
+  check_rows16(A, "gemm_gather_swiglu: A must be bf16 [M, K] with 16-byte aligned rows");
+  const int64_t M = A.size(0), K = A.size(1), N2 = B.size(0);
+  FYB_CHECK(B.dim() == 2 && B.size(1) == K && N2 % 64 == 0, "gemm_gather_swiglu: B must be [2f, K], f % 32 == 0");
+  FYB_CHECK(M < (1ll << 31) && N2 < (1ll << 31) && K < (1ll << 31), "gemm_gather_swiglu: dimension too large");
+  const int64_t f = N2 / 2;
+  at::Tensor u = at::empty({M, N2}, A.options());
+  at::Tensor h = at::empty({M, f}, A.options());
+  c10::cuda::CUDAGuard guard(A.device());
+  at::Tensor counters;
+  const GatherArgs ga = make_gather_args(A, B, flat, peers, seg, chunk, rank, (f + 127) / 128, counters);
+  if (M == 0) return {u, h};
+  const CUtensorMap ta = make_tmap_2d(A.data_ptr(), M, K, A.stride(0), kBM);
+  const CUtensorMap tb = make_tmap_2d(B.data_ptr(), N2, K, K, 128);
+  const EpiAux aux{nullptr, nullptr, reinterpret_cast<__nv_bfloat16*>(h.data_ptr()), f, static_cast<int>(f), 0};
+  launch_pair<256, false, false, kE2Swiglu, true>(ta, tb, u.data_ptr(), nullptr, static_cast<int>(M),
+                                                  static_cast<int>(N2), static_cast<int>(K), N2, 0,
+                                                  PairArgs{1, nullptr, nullptr, nullptr}, cur_stream(), aux, ga);
+  return {u, h};
+}
+
+void gemm_gather(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, const at::Tensor& flat,
+                 const at::Tensor& peers, int64_t seg, int64_t chunk, int64_t rank, int64_t bn,
+                 const c10::optional<at::Tensor>& cos_t, const c10::optional<at::Tensor>& sin_t, int64_t L,
+                 int64_t rot_cols, const c10::optional<at::Tensor>& residual) {
+  FYB_RANGE("fyb::gemm_gather");
+  check_rows16(A, "gemm_gather: A must be bf16 [M, K] with 16-byte aligned rows");
+  check_rows16(C, "gemm_gather: C must be bf16 [M, N] with 16-byte aligned rows");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  FYB_CHECK(C.size(0) == M && C.size(1) == N, "gemm_gather: output shape mismatch");
+  FYB_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm_gather: dimension too large");
+  FYB_CHECK(bn == 256 || bn == 192, "gemm_gather: tile width must be 256 or 192");
+  const __nv_bfloat16* Rp = nullptr;
+  int64_t ldr = 0;
+  if (residual.has_value() && residual->defined()) {
+    FYB_CHECK(residual->scalar_type() == at::kBFloat16 && residual->dim() == 2 && residual->size(0) == M &&
+                  residual->size(1) == N && residual->stride(1) == 1,
+              "gemm_gather: residual must be bf16 [M, N] with contiguous rows");
+    Rp = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    ldr = residual->stride(0);
+  }
+  const bool rope = cos_t.has_value() && cos_t->defined();
+  if (rope) {
+    FYB_CHECK(sin_t.has_value() && sin_t->defined(), "gemm_gather: cos without sin");
+    FYB_CHECK(L > 0 && M % L == 0 && rot_cols >= 0 && rot_cols % 128 == 0 && rot_cols <= N,
+              "gemm_gather: rope rows / columns");
+    for (const at::Tensor* t : {&*cos_t, &*sin_t})
+      FYB_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->dim() == 2 &&
+                    t->size(0) >= L && t->size(1) == 64 && reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
+                "gemm_gather: cos / sin must be contiguous bf16 [>= L, 64]");
+  }
+  FYB_CHECK(!(rope && Rp != nullptr), "gemm_gather: rope and residual do not combine");
+  if (M == 0 || N == 0) return;
+  c10::cuda::CUDAGuard guard(A.device());
+  at::Tensor counters;
+  const GatherArgs ga = make_gather_args(A, B, flat, peers, seg, chunk, rank, (N + bn - 1) / bn, counters);
+  const CUtensorMap ta = make_tmap_2d(A.data_ptr(), M, K, A.stride(0), kBM);
+  const CUtensorMap tb = make_tmap_2d(B.data_ptr(), N, K, K, static_cast<int>(bn / 2));
+  EpiAux aux{};
+  if (rope)
+    aux = EpiAux{reinterpret_cast<const __nv_bfloat16*>(cos_t->data_ptr()),
+                 reinterpret_cast<const __nv_bfloat16*>(sin_t->data_ptr()), nullptr, 0, static_cast<int>(L),
+                 static_cast<int>(rot_cols)};
+  const PairArgs pa{1, nullptr, nullptr, nullptr};
+  const int m = static_cast<int>(M), n = static_cast<int>(N), k = static_cast<int>(K);
+  void* Cp = C.data_ptr();
+  const int64_t ldc = C.stride(0);
+  cudaStream_t st = cur_stream();
+  if (bn == 256) {
+    if (rope) launch_pair<256, false, false, kE2Rope, true>(ta, tb, Cp, nullptr, m, n, k, ldc, 0, pa, st, aux, ga);
+    else if (Rp) launch_pair<256, false, false, kE2Bf16Res, true>(ta, tb, Cp, Rp, m, n, k, ldc, ldr, pa, st, aux, ga);
+    else launch_pair<256, false, false, kE2Bf16, true>(ta, tb, Cp, nullptr, m, n, k, ldc, 0, pa, st, aux, ga);
+  } else {
+    if (rope) launch_pair<192, false, false, kE2Rope, true>(ta, tb, Cp, nullptr, m, n, k, ldc, 0, pa, st, aux, ga);
+    else if (Rp) launch_pair<192, false, false, kE2Bf16Res, true>(ta, tb, Cp, Rp, m, n, k, ldc, ldr, pa, st, aux, ga);
+    else launch_pair<192, false, false, kE2Bf16, true>(ta, tb, Cp, nullptr, m, n, k, ldc, 0, pa, st, aux, ga);
+  }
 }
 
 }  // namespace fyb

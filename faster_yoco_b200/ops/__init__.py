@@ -97,6 +97,12 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn_major: bool = False, b_mn_maj
     if out is None:
         out = torch.empty(M, N, dtype=out_dtype or a.dtype, device=a.device)
     K = a.shape[0] if a_mn_major else a.shape[1]
+    if not a_mn_major and not b_mn_major and out.dtype == torch.bfloat16:
+        pa = _pull_args(b)
+        if pa is not None:
+            # the weight's all-gather runs inside this (its first forward) GEMM
+            _C().gemm_gather(a, b, out, *pa, _gather_bn(M, N, K), None, None, 0, 0, residual)
+            return out
     route = _gemm_route(M, N, K) if _GEMM_PAIR else (0, 0, 1)
     if route[0] == 1:
         _C().gemm_pair(a, b, out, a_mn_major, b_mn_major, residual, route[1], route[2])
@@ -106,6 +112,19 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_mn_major: bool = False, b_mn_maj
 
 
 _ROUTES = {}
+
+
+def _pull_args(w: torch.Tensor):
+    """Gather-GEMM arguments when w's ZeRO all-gather runs inside the GEMM that first reads it this update."""
+    fp = getattr(w, "_fyb_flat", None)
+    if fp is None or fp.pull is None:
+        return None
+    return fp.pull_args(w)
+
+
+def _gather_bn(M: int, N: int, K: int) -> int:
+    route = _gemm_route(M, N, K)
+    return 192 if route[0] == 1 and route[1] == 192 and route[2] == 1 else 256
 
 
 def _gemm_route(M: int, N: int, K: int):
@@ -134,6 +153,10 @@ def gemm_rope(a: torch.Tensor, w: torch.Tensor, cos: torch.Tensor, sin: torch.Te
     if out is None:
         out = torch.empty(T, N, dtype=a.dtype, device=a.device)
     if native_on(a):
+        pa = _pull_args(w)
+        if pa is not None:
+            _C().gemm_gather(a, w, out, *pa, _gather_bn(T, N, a.shape[1]), cos, sin, seq_len, rot_cols)
+            return out
         route = _gemm_route(T, N, a.shape[1])
         bn = route[1] if route[0] == 1 and route[2] == 1 else 256
         _C().gemm_rope(a, w, out, cos, sin, seq_len, rot_cols, bn)
@@ -149,7 +172,11 @@ def gemm_swiglu(a: torch.Tensor, w: torch.Tensor):
     """(u, h): u = a @ w.T for the merged [fc1; gate] weight w [2f, K], h = silu(u[:, :f]) * u[:, f:] -- one GEMM
     whose epilogue also computes the activation (values of gemm() followed by swiglu())."""
     if native_on(a):
-        u, h = _C().gemm_swiglu(a, w)
+        pa = _pull_args(w)
+        if pa is not None:
+            u, h = _C().gemm_gather_swiglu(a, w, *pa)
+        else:
+            u, h = _C().gemm_swiglu(a, w)
         return u, h
     u = gemm(a, w)
     f = u.shape[1] // 2
@@ -171,6 +198,25 @@ def gemm_swiglu_bwd(g: torch.Tensor, w2: torch.Tensor, u: torch.Tensor, du: Opti
     du[:, :f] = (s * (1 + a32 * (1 - s)) * dh.float() * b32).to(du.dtype)
     du[:, f:] = (a32 * s * dh.float()).to(du.dtype)
     return du
+
+
+def gemm_gather(a: torch.Tensor, w: torch.Tensor, flat: torch.Tensor, peers: torch.Tensor, seg: int, chunk: int,
+                rank: int, out: Optional[torch.Tensor] = None, rope=None) -> torch.Tensor:
+    """y = a @ w.T with the ZeRO parameter all-gather of w fused into the GEMM: w is a contiguous weight inside this
+    rank's flat replica `flat`; its rows owned by other ranks (owner map seg / chunk) are pulled from the owners'
+    replicas (`peers`: device int64 [world] base addresses) by the GEMM's gather warps ahead of the tiles that read
+    them, so w is current in this replica on return. rope: optional (cos, sin, seq_len, rot_cols) as gemm_rope.
+    No torch form: the peer replicas are device memory of other GPUs."""
+    T, N = a.shape[0], w.shape[0]
+    if out is None:
+        out = torch.empty(T, N, dtype=a.dtype, device=a.device)
+    bn = _gather_bn(T, N, a.shape[1])
+    if rope is None:
+        _C().gemm_gather(a, w, out, flat, peers, seg, chunk, rank, bn)
+    else:
+        cos, sin, seq_len, rot_cols = rope
+        _C().gemm_gather(a, w, out, flat, peers, seg, chunk, rank, bn, cos, sin, seq_len, rot_cols)
+    return out
 
 
 class _NativeLinear(torch.autograd.Function):

@@ -248,6 +248,36 @@ class PeerComm:
             self.peer_streams = {q: torch.cuda.Stream(device=self.dev) for q in range(self.world) if q != self.rank}
             self.ce_done = torch.cuda.Event()
 
+    # ----------------------------------------------------------------- all-gather fused into the forward GEMMs
+    def setup_pull(self, flat, model):
+        """The parameter all-gather moves into the consumers: every 2-D weight except embeddings is pulled from its
+        owners by the first forward GEMM that reads it (gemm_gather: the GEMM's gather warps copy the rows ahead of
+        the tiles); after the optimizer step this rank pushes only the rest (embeddings, norm weights) and passes
+        one barrier, which also tells the pullers that its owned rows are final. Best with the block-cyclic owner
+        map: a tile column then spans several owners, and pulls from several peers at once run near link speed
+        where pulls from one peer do not."""
+        embed = {id(p) for n, p in model.named_parameters(remove_duplicate=False) if "embed" in n}
+        ids = set()
+        for e in flat.entries:
+            p = e.param
+            if p.dim() == 2 and id(p) not in embed and p.shape[1] % 8 == 0:
+                ids.add(id(p))
+        rest = [[o, c] for e in flat.entries if id(e.param) not in ids
+                for o, c, r in flat.owner_ranges(e) if r == self.rank]
+        self.rest_ranges = torch.tensor(rest, dtype=torch.int64, device=self.dev).view(-1, 2)
+        if not hasattr(self, "peer_arrive"):
+            self.arrive, self.peer_arrive = self.share_bytes(self.NSLOTS * 4)
+        flat.pull = {"peers": torch.tensor(self.peers["param"], dtype=torch.int64, device=self.dev), "ids": ids}
+        self.flat = flat
+
+    def push_rest(self):
+        """Pull mode, after the optimizer step: push this owner's parameters that no GEMM pulls, then barrier."""
+        sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
+        if self.rest_ranges.numel():
+            self.C.push_bucket(self.flat.flat, self.peers["param"], self.peer_arrive, self.rest_ranges,
+                               self.NSLOTS - 2, self.rank, sms)
+        self.barrier()
+
     def _slot_barrier(self, slot: int):
         self.C.flag_barrier(self.peer_flags, self.flags, self.counters, self.rank, slot)
 

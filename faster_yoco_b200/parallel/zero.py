@@ -152,6 +152,10 @@ class FlatParams:
         self._sq_covered = set()
         self._sq_region = {}               # id(p) -> (start, end) of p's partials in sq_buf this update
         self._sq_chunks = {}               # covered set -> device table of the other gradients' chunks
+        # parameter all-gather fused into the consuming forward GEMMs (PeerComm.setup_pull): the weights in
+        # pull["ids"] are pulled from their owners by the first K-major GEMM that reads them in an update
+        self.pull = None                   # {"peers": device int64 [world] replica addresses, "ids": set of id(p)}
+        self._pulled = set()
 
     # ---------------------------------------------------------------------------------------------------------
     def owner_of(self, x: int) -> int:
@@ -291,8 +295,17 @@ class FlatParams:
     def sparse(self) -> frozenset:
         return frozenset(self._sparse)
 
+    def pull_args(self, p):
+        """(flat, peers, seg, chunk, rank) for the gather-GEMM when p's all-gather runs inside the GEMM that consumes
+        it and this update has not pulled p yet (marks it pulled), else None."""
+        if self.pull is None or id(p) not in self.pull["ids"] or id(p) in self._pulled:
+            return None
+        self._pulled.add(id(p))
+        return self.flat, self.pull["peers"], self.seg, self.chunk, self.rank
+
     def begin_update(self):
         self.accumulate = False
+        self._pulled.clear()
         self._written.clear()
         self._scattered.clear()
         self._sparse.clear()
@@ -420,6 +433,11 @@ class ZeroOptimizer:
         if self.comm == "fused" and self.p2p is not None:
             if self.p2p.buckets is not None:
                 return          # pushed bucket by bucket ahead of the next update's forward (overlapped)
+            if fp.pull is not None:
+                # the GEMM weights are pulled by their consumers in the next forward; push the rest, then one
+                # barrier publishes this owner's update to the pullers
+                self.p2p.push_rest()
+                return
             self.p2p.all_gather(fp.flat, fp.seg, fp.used, chunk=fp.chunk)
             return
         if not fp.chunk:
@@ -478,7 +496,8 @@ class ZeroOptimizer:
         b1, b2 = self.cfg.betas
         seg = fp.param_segment()
         fused_push = (native and fp.world > 1 and self.comm == "fused" and self.p2p is not None
-                      and self.p2p.buckets is None and self.fuse_adam_push and not self.skip_exchange)
+                      and self.p2p.buckets is None and self.fuse_adam_push and not self.skip_exchange
+                      and fp.pull is None)
         # the kernels address this owner's bf16 gradients / parameters through the owner map: its segment views
         # (contiguous layouts) or the whole flat buffers + the chunk size (block-cyclic)
         g_arg, p_arg = (fp.grad_flat, fp.flat) if fp.chunk else (g16, seg)

@@ -83,6 +83,9 @@ def save_checkpoint(path: str, model, trainer, *, extra_state: Optional[dict] = 
     `path` (with tensor parallelism: one part file per TP rank, see part_path)."""
     rank = trainer.rank if rank is None else rank
     path = part_path(path)
+    # the overlapped and the pull exchanges gather parameters lazily (at the next forward): make them current first
+    if hasattr(trainer, "sync_params"):
+        trainer.sync_params()
     opt = trainer.zero.consolidated_state()            # {internal name: {master, exp_avg, exp_avg_sq}}
     if rank != 0:
         return None

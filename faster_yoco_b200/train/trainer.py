@@ -96,8 +96,10 @@ class Trainer:
         if self.tp > 1:
             self.zero.set_tensor_parallel(TP.tp_group(), TP.tp_rank(), TP.is_sharded)
         self.zero.p2p = p2p
-        if transport not in ("sm", "ce", "gemm"):
+        if transport not in ("sm", "ce", "gemm", "pull"):
             raise ValueError(f"unknown transport {transport!r}")
+        if transport == "pull":
+            overlap = False                  # the all-gather runs inside the forward GEMMs instead
         self.overlap = p2p is not None and overlap and hasattr(model, "param_buckets")
         if p2p is not None and transport == "gemm":
             # gradients: the weight-gradient GEMMs store at the owners; parameters: pushed per layer bucket ahead of
@@ -110,6 +112,12 @@ class Trainer:
             p2p.setup_scatter(self.flat)
             if self.overlap:
                 p2p.setup_buckets(self.flat, model.param_buckets(), transport="sm", grads="scatter")
+        elif p2p is not None and transport == "pull":
+            # parameters: the all-gather fused into the consuming forward GEMMs (gemm_gather); gradients: the
+            # serial P2P reduce-to-owner after backward
+            if not self.flat.direct_grads:
+                raise ValueError("transport 'pull' needs the native kernels (the gather-GEMM)")
+            p2p.setup_pull(self.flat, model)
         elif self.overlap:
             p2p.setup_buckets(self.flat, model.param_buckets(), transport=transport)
         self.sched = PolynomialDecaySchedule(optim_cfg.lr, optim_cfg.warmup_updates, optim_cfg.total_num_update,
@@ -187,12 +195,13 @@ class Trainer:
         self.release_graph()
         self.zero.skip_exchange = on
         if on:
-            self._saved_modes = (self.flat.scatter, self.check_consistency, self.overlap)
+            self._saved_modes = (self.flat.scatter, self.check_consistency, self.overlap, self.flat.pull)
             self.flat.scatter = None
+            self.flat.pull = None            # no pulls inside the GEMMs
             self.check_consistency = False
             self.overlap = False             # no per-bucket pushes or waits either
         elif getattr(self, "_saved_modes", None) is not None:
-            self.flat.scatter, self.check_consistency, self.overlap = self._saved_modes
+            self.flat.scatter, self.check_consistency, self.overlap, self.flat.pull = self._saved_modes
             self._saved_modes = None
 
     def _reduce_stats(self, loss_sum, sample_size):
@@ -293,6 +302,11 @@ class Trainer:
 
     def sync_params(self):
         """Make every rank's full parameter copy current (the overlapped path gathers lazily at the next update)."""
+        if getattr(self.flat, "pull", None) is not None and self.zero.p2p is not None:
+            # the pulled weights are current only where a GEMM read them: gather everything
+            fp = self.flat
+            self.zero.p2p.all_gather(fp.flat, fp.seg, fp.used, chunk=fp.chunk)
+            return
         if getattr(self, "overlap", False):
             p2p = self.zero.p2p
             p2p.start_gather()

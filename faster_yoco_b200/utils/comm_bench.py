@@ -10,6 +10,8 @@
   ([2048 x 12312]^T [2048 x 3072]) stored by the GEMM's epilogue at each element's owner (block-cyclic owner map)
   and summed by the owner from local memory -- against GEMM + NCCL reduce-scatter and GEMM + P2P reduce-to-owner;
   roofline = max(FLOPs / measured bf16 peak, bytes this rank sends over NVLink / 770 GB/s);
+* ``--fused-gather 1``: all-gather -> GEMM of a forward weight (1 MB .. 1 GB): the all-gather fused into the
+  consumer GEMM (gemm_gather) against NCCL all_gather_into_tensor + GEMM;
 * ``--fused-adam 1``: reduce-scatter + sharded Adam + parameter all-gather over per-rank segments of 1 MB .. 1 GB
   (gradients N(0, 1e-3)): P2P reduce-to-owner + Adam fused with the push all-gather, against NCCL reduce-scatter +
   Adam + NCCL all-gather; roofline = max(inbound NVLink bytes / 770 GB/s, Adam's HBM bytes / measured HBM bandwidth).
@@ -55,6 +57,7 @@ def main():
     ap.add_argument("--interference", type=int, default=1)
     ap.add_argument("--fused-gemm", type=int, default=0)
     ap.add_argument("--fused-adam", type=int, default=0)
+    ap.add_argument("--fused-gather", type=int, default=0)
     ap.add_argument("--skip-sweep", type=int, default=0, help="only the --fused-* sections")
     a = ap.parse_args()
     from faster_yoco_b200.parallel import dist as D
@@ -73,6 +76,8 @@ def main():
         fused_gemm_bench(comm, a.iters)
     if a.fused_adam:
         fused_adam_bench(comm, [int(x) for x in a.sizes_mb.split(",")], a.iters)
+    if a.fused_gather:
+        fused_gather_bench(comm, [int(x) for x in a.sizes_mb.split(",")], a.iters)
     if a.skip_sweep:
         comm.close()
         dist.barrier()
@@ -211,6 +216,49 @@ def fused_gemm_bench(comm, iters, T=2048, M=12312, N=3072, chunk=1 << 18):
         res[k.replace("_ms", "_frac_of_roofline")] = res["roofline_ms"] / res[k]
     if rank == 0:
         print(json.dumps(res), flush=True)
+
+
+def fused_gather_bench(comm, sizes_mb, iters, T=2048, K=3072, chunk=1 << 18):
+    """All-gather -> GEMM of a forward weight ([N, 3072] bf16, N from the weight size; x [2048, 3072]): the
+    all-gather fused into the consumer GEMM (gemm_gather: the GEMM's gather warps pull the rows other ranks own
+    from their replicas ahead of the tiles, block-cyclic owner map) against NCCL all_gather_into_tensor + the GEMM.
+    Sizes are the whole weight (1 MB .. 1 GB); roofline = max(FLOPs / measured bf16 peak, bytes this rank receives
+    ((world - 1) / world of the weight) / 770 GB/s)."""
+    from .. import ops
+    C = comm.C
+    rank, world = comm.rank, comm.world
+    g = torch.Generator(device="cuda").manual_seed(rank)
+    x = torch.randn(T, K, generator=g, device="cuda").to(torch.bfloat16)
+    nmax = max(sizes_mb) * 1024 * 1024 // (2 * K) // 8 * 8
+    span = chunk * world
+    seg_max = -(-nmax * K // span) * chunk
+    flat = comm.alloc("gg_param", world * seg_max, torch.bfloat16)
+    flat.normal_(0, 0.02)
+    peers = torch.tensor(comm.peers["gg_param"], dtype=torch.int64, device="cuda")
+    for mb in sizes_mb:
+        N = max(8, mb * 1024 * 1024 // (2 * K) // 8 * 8)
+        numel = N * K
+        seg_n = -(-numel // (world * 8)) * 8                  # NCCL: contiguous shards of the weight
+        w = flat[:numel].view(N, K)
+        y = torch.empty(T, N, dtype=torch.bfloat16, device="cuda")
+        full = torch.empty(world * seg_n, dtype=torch.bfloat16, device="cuda")
+        shard = flat[rank * seg_n:(rank + 1) * seg_n] if (rank + 1) * seg_n <= flat.numel() else full[:seg_n]
+        res = {"fused_gather": "all-gather + GEMM", "world": world, "weight_mb": mb, "T": T, "N": N, "K": K,
+               "chunk": chunk}
+        res["gemm_only_ms"] = _time(lambda: ops.gemm(x, w, out=y), iters)
+        res["fused_gather_gemm_ms"] = _time(
+            lambda: (comm.barrier(), ops.gemm_gather(x, w, flat, peers, seg_max, chunk, rank, out=y)), iters)
+        res["nccl_allgather_then_gemm_ms"] = _time(
+            lambda: (dist.all_gather_into_tensor(full, shard),
+                     ops.gemm(x, full[:numel].view(N, K), out=y)), iters)
+        t_compute = 2.0 * T * N * K / (BF16_TFLOPS * 1e12) * 1e3
+        t_link = (world - 1) / world * numel * 2 / (LINK_GBS * 1e9) * 1e3
+        res["roofline_ms"] = max(t_compute, t_link)
+        res["roofline_compute_ms"], res["roofline_link_ms"] = t_compute, t_link
+        for k in [k for k in res if k.endswith("_ms") and not k.startswith("roofline")]:
+            res[k.replace("_ms", "_frac_of_roofline")] = res["roofline_ms"] / res[k]
+        if rank == 0:
+            print(json.dumps(res), flush=True)
 
 
 def fused_adam_bench(comm, sizes_mb, iters):

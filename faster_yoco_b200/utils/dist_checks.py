@@ -138,7 +138,9 @@ def gemm_scatter_vs_serial_gpu(rank, world, outdir, steps):
             ("gemm_uf2", "gemm", False, 2, "even"), ("serial_cyclic", "sm", False, 1, "cyclic"),
             ("gemm_cyclic", "gemm", False, 1, "cyclic"), ("gemm_cyclic_graph", "gemm", True, 1, "cyclic"),
             ("gemm_overlap_cyclic", "gemm+overlap", True, 1, "cyclic"), ("sm_overlap_cyclic", "sm+overlap", False,
-                                                                          1, "cyclic")):
+                                                                          1, "cyclic"),
+            ("pull_cyclic", "pull", False, 1, "cyclic"), ("pull_cyclic_graph", "pull", True, 1, "cyclic"),
+            ("pull_even", "pull", False, 1, "even")):
         overlap = transport.endswith("+overlap")
         model, tr = _tiny_trainer(dev, comm="fused", arch="yoco_small", dtype=torch.bfloat16, overlap=overlap,
                                   transport=transport.split("+")[0], graph=graph, partition=part, chunk=1 << 14)
@@ -154,10 +156,51 @@ def gemm_scatter_vs_serial_gpu(rank, world, outdir, steps):
         tr.release_graph()
         torch.cuda.synchronize()
         status = int(ops._C().status()[0].item())
-        res[name] = {"losses": losses, "params": tr.flat.flat.float().cpu(), "status": status}
+        # parameters in model order (the padding of the flat buffer differs between owner maps)
+        params = torch.cat([p.detach().float().reshape(-1) for p in model.parameters()]).cpu()
+        res[name] = {"losses": losses, "params": params, "status": status}
         tr.zero.p2p.close()
     if rank == 0:
         torch.save(res, os.path.join(outdir, "gemm_scatter.pt"))
+
+
+def gemm_gather_gpu(rank, world, outdir, chunk):
+    """GPU, one rank per GPU over CUDA-IPC peer replicas: the ZeRO all-gather fused into the consumer GEMM
+    (gemm_gather). Every rank writes only the elements it owns (block-cyclic map of `chunk`, or contiguous segments
+    for chunk 0) and garbage elsewhere; after a barrier each rank's gather-GEMM must leave the weight current in its
+    replica and produce a @ w_true^T. Twice, so the second call also reads rows that the first one pulled."""
+    from .. import ops
+    from ..parallel.p2p import PeerComm
+    ops.set_backend("native")
+    dev = torch.device("cuda", rank)
+    comm = PeerComm()
+    K, N, M = 512, 1544, 512
+    span = (chunk or 1024) * world
+    seg = ((N * K + 65536 + span - 1) // span) * span // world
+    flat = comm.alloc("param", world * seg, torch.bfloat16)
+    g = torch.Generator(device=dev).manual_seed(7)
+    truth = (torch.randn(world * seg, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+    x = torch.arange(world * seg, device=dev)
+    own = (x // chunk) % world if chunk else x // seg
+    flat.copy_(torch.where(own == rank, truth, torch.full_like(truth, 7.0)))
+    torch.cuda.synchronize()
+    comm.barrier()
+    peers = torch.tensor(comm.peers["param"], dtype=torch.int64, device=dev)
+    a = (torch.randn(M, K, device=dev, generator=g)).to(torch.bfloat16)
+    w_off = 40960 + 16
+    w = flat[w_off:w_off + N * K].view(N, K)
+    ok = True
+    for _ in range(2):
+        y = ops.gemm_gather(a, w, flat, peers, seg, chunk, rank)
+        torch.cuda.synchronize()
+        ok = ok and torch.equal(flat[w_off:w_off + N * K], truth[w_off:w_off + N * K])
+    y0 = ops.gemm(a, truth[w_off:w_off + N * K].view(N, K).contiguous())
+    err = float(((y.float() - y0.float()).abs().max() / y0.float().abs().max()).item())
+    status = int(ops._C().status()[0].item())
+    comm.barrier()
+    torch.cuda.synchronize()
+    comm.close()
+    torch.save({"ok": ok, "err": err, "status": status}, os.path.join(outdir, f"gemm_gather_{rank}.pt"))
 
 
 def exchange_free_steps(rank, world, outdir, steps):

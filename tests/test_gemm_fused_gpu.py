@@ -119,3 +119,50 @@ def test_gemm_swiglu_bwd_matches_gemm_then_swiglu_bwd(M, K, f, pad):
     C().gemm_swiglu_bwd(g, w2.t().contiguous(), False, u, du2)
     close_ulps(du2, du0)
     assert int(C().status()[0].item()) == 0
+
+
+def _owner(x, seg, chunk, world):
+    return (x // chunk) % world if chunk else x // seg
+
+
+@pytest.mark.parametrize("world,chunk,bn,rope", [(4, 0, 256, False), (4, 4096, 256, False), (8, 2048, 192, True),
+                                                 (2, 0, 192, False), (3, 8192, 256, True)])
+def test_gemm_gather_pulls_owner_rows_and_multiplies(world, chunk, bn, rope):
+    """The all-gather fused into the consumer GEMM, owners emulated by replicas in this GPU's memory: the weight's
+    rows owned elsewhere are stale in this rank's replica before the call and current after it, the other elements
+    of the replica are untouched, and the product uses the current rows."""
+    ops.set_backend("native")
+    K, N, L, Bs = 256, 648, 128, 3
+    M = Bs * L
+    span = (chunk or 1024) * world
+    seg = ((N * K + 40960 + span - 1) // span) * span // world          # whole chunks / aligned segments
+    rank = 1
+    reps = [rnd(world * seg, seed=20 + r, scale=0.05) for r in range(world)]
+    x = torch.arange(world * seg, device=dev())
+    own = _owner(x, seg, chunk, world)
+    truth = reps[0].clone()
+    for r in range(world):
+        truth[own == r] = reps[r][own == r]
+    local = reps[rank]
+    before = local.clone()
+    peers = torch.tensor([t.data_ptr() for t in reps], dtype=torch.int64, device=dev())
+    w_off = 8192 + 8 * 3                                          # 16-byte aligned, not tile aligned
+    w = local[w_off:w_off + N * K].view(N, K)
+    a = rnd(M, K, seed=30)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=dev())
+    if rope:
+        cos, sin = tables(L)
+        C().gemm_gather(a, w, y, local, peers, seg, chunk, rank, bn, cos, sin, L, 256)
+    else:
+        C().gemm_gather(a, w, y, local, peers, seg, chunk, rank, bn)
+    torch.cuda.synchronize()
+    assert int(C().status()[0].item()) == 0
+    assert torch.equal(local[w_off:w_off + N * K], truth[w_off:w_off + N * K])
+    assert torch.equal(local[:w_off], before[:w_off]) and torch.equal(local[w_off + N * K:], before[w_off + N * K:])
+    wt = truth[w_off:w_off + N * K].view(N, K)
+    if rope:
+        y0 = torch.empty_like(y)
+        C().gemm_rope(a, wt.contiguous(), y0, cos, sin, L, 256, bn)
+    else:
+        y0 = ops.gemm(a, wt.contiguous())
+    close_ulps(y, y0)

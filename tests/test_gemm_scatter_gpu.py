@@ -173,7 +173,8 @@ def test_gemm_scatter_training_matches_serial_exchange(tmp_path):
     r = torch.load(os.path.join(tmp_path, "gemm_scatter.pt"))
     for name, base in (("gemm", "serial"), ("gemm_graph", "serial"), ("gemm_uf2", "serial_uf2"),
                        ("serial_cyclic", "serial"), ("gemm_cyclic", "serial"), ("gemm_cyclic_graph", "serial"),
-                       ("gemm_overlap_cyclic", "serial"), ("sm_overlap_cyclic", "serial")):
+                       ("gemm_overlap_cyclic", "serial"), ("sm_overlap_cyclic", "serial"),
+                       ("pull_cyclic", "serial"), ("pull_cyclic_graph", "serial"), ("pull_even", "serial")):
         assert r[name]["status"] == 0 and r[base]["status"] == 0
         for a, b in zip(r[name]["losses"], r[base]["losses"]):
             assert abs(a - b) / abs(b) < 2e-4, (name, r[name]["losses"], r[base]["losses"])

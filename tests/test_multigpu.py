@@ -28,3 +28,13 @@ def test_fused_p2p_matches_nccl(tmp_path):
             assert abs(a - b) / abs(b) < 2e-4, (name, r[name]["losses"], r["fused_serial"]["losses"])
         pf, ps = r[name]["params"], r["fused_serial"]["params"]
         assert ((pf - ps).abs().max() / ps.abs().max()).item() < 1e-2, name
+
+
+@pytest.mark.parametrize("chunk", [0, 1 << 14])
+def test_gemm_gather_two_ranks(tmp_path, chunk):
+    """The all-gather fused into the consumer GEMM over real peer replicas (2 GPUs)."""
+    run_ranks(dist_checks.gemm_gather_gpu, 2, str(tmp_path), chunk, backend="nccl", timeout_s=180)
+    for r in range(2):
+        res = torch.load(os.path.join(tmp_path, f"gemm_gather_{r}.pt"))
+        assert res["status"] == 0 and res["ok"], res
+        assert res["err"] < 1e-2, res
