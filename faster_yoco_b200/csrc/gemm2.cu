@@ -357,11 +357,68 @@ __device__ __forceinline__ void rope_store32(const uint32_t (&r)[32], __nv_bfloa
   store16x2(C, p);
 }
 
+// The work of one CTA pair, the same sequence for its producer, MMA and epilogue warps.
+//   uniform split-K (sk_per == 0): units u = cluster, cluster + clusters, ...: tile u / splits, K part u % splits of
+//     `splits` equal parts; a partial's workspace slot is u.
+//   stream-K (sk_per > 0): the pair's contiguous range [cluster sk_per, (cluster + 1) sk_per) of the tile-major K
+//     iterations (tile t covers [t nk, (t + 1) nk)), cut at tile boundaries: every pair does the same number of K
+//     blocks, and only the tiles cut by a range boundary are summed from parts. A pair has at most two partial
+//     segments (the first and the last of its range), workspace slots 2 cluster + {0: starts the range, 1: ends it}.
+struct Work {
+  int t, kb0, kb1;   // tile, K blocks [kb0, kb1)
+  int part, parts;   // this segment's index among the tile's K parts (in K order), their number
+  int slot;          // workspace slot of this part
+};
+
+struct Sched {
+  int cluster, clusters, splits, nk, k_chunk, num_units;
+  int64_t per, g0, g, g1;
+  int u;
+  __device__ __forceinline__ Sched(int cluster_, int clusters_, int splits_, int nk_, int num_tiles, int64_t per_)
+      : cluster(cluster_), clusters(clusters_), splits(splits_), nk(nk_), k_chunk((nk_ + splits_ - 1) / splits_),
+        num_units(num_tiles * splits_), per(per_), u(cluster_) {
+    const int64_t total = static_cast<int64_t>(num_tiles) * nk_;
+    g0 = g = per_ > 0 ? min(total, static_cast<int64_t>(cluster_) * per_) : 0;
+    g1 = per_ > 0 ? min(total, g0 + per_) : 0;
+  }
+  __device__ __forceinline__ bool next(Work& w) {
+    if (per == 0) {
+      if (u >= num_units) return false;
+      w.t = u / splits;
+      w.part = u % splits;
+      w.parts = splits;
+      w.kb0 = w.part * k_chunk;
+      w.kb1 = min(nk, w.kb0 + k_chunk);
+      w.slot = u;
+      u += clusters;
+      return true;
+    }
+    if (g >= g1) return false;
+    const int64_t t = g / nk;
+    w.t = static_cast<int>(t);
+    w.kb0 = static_cast<int>(g - t * nk);
+    w.kb1 = static_cast<int>(min(static_cast<int64_t>(nk), g1 - t * nk));
+    const int64_t fc = (t * nk) / per, lc = ((t + 1) * nk - 1) / per;
+    w.parts = static_cast<int>(lc - fc + 1);
+    w.part = static_cast<int>(cluster - fc);
+    w.slot = cluster * 2 + (g == g0 ? 0 : 1);
+    g = t * nk + w.kb1;
+    return true;
+  }
+  // workspace slot of part j of tile t
+  __device__ __forceinline__ int64_t part_slot(int t, int j) const {
+    if (per == 0) return static_cast<int64_t>(t) * splits + j;
+    const int64_t cj = (static_cast<int64_t>(t) * nk) / per + j;
+    const int64_t start = max(static_cast<int64_t>(t) * nk, cj * per);
+    return cj * 2 + (start == cj * per ? 0 : 1);
+  }
+};
+
 template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG : kThreads2, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, void* Cv,
-                     const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, int splits, float* ws,
-                     int* counters, int* status, float* sq_part, const EpiAux aux, const GatherArgs ga) {
+                     const __nv_bfloat16* R, int M, int N, int K, int64_t ldc, int64_t ldr, int splits, int64_t sk_per,
+                     float* ws, int* counters, int* status, float* sq_part, const EpiAux aux, const GatherArgs ga) {
   static_assert(!GATHER || !B_MN, "the gather form reads K-major weight rows");
   static_assert(EPI != kE2Swiglu || (BN == 256 && !B_MN), "the SwiGLU epilogue pairs two 128-row B halves");
   constexpr int kStages2 = PairCfg<BN>::STAGES;
@@ -385,10 +442,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
   const int num_n = EPI == kE2Swiglu ? (aux.i0 + 127) / 128 : (N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_k = (K + kBK - 1) / kBK;
-  // split-K (splits = 1 or 2): work unit u = (tile u / splits, K half u % splits); the two halves of a tile are
+  // split-K (splits = 1 .. 4): work unit u = (tile u / splits, K part u % splits); the parts of a tile are
   // consecutive units, so they run in the same wave
   const int num_units = num_tiles * splits;
-  const int k_chunk = (num_k + splits - 1) / splits;
   // accumulator buffers at a power-of-two column stride (BN = 192 uses columns [0, 192) and [256, 448))
   constexpr uint32_t ACC_STRIDE = BN <= 128 ? 128u : 256u;
   constexpr uint32_t TMEM_COLS = 2 * ACC_STRIDE;
@@ -426,13 +482,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
       int s = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
-        const int t = u / splits;
+      Sched sc(cluster_id, num_clusters, splits, num_k, num_tiles, sk_per);
+      Work w;
+      while (ok && sc.next(w)) {
+        const int t = w.t;
         const int mb = t % num_m, nb = t / num_m;
         const int m0 = mb * 2 * kBM + static_cast<int>(crank) * kBM;
         const int n0 = EPI == kE2Swiglu ? nb * 128 + static_cast<int>(crank) * aux.i0
                                         : nb * BN + static_cast<int>(crank) * (BN / 2);
-        const int kb0 = (u % splits) * k_chunk, kb1 = min(num_k, kb0 + k_chunk);
+        const int kb0 = w.kb0, kb1 = w.kb1;
         if constexpr (GATHER) {
           // every share of tile column nb pulled into this replica (then visible to the TMA loads below)
           if (!wait_count(ga.counters + nb, 2 * num_m, abort_flag, status, 27)) {
@@ -485,11 +543,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
       int acc = 0;
       uint32_t acc_ph = 0;
       bool ok = true;
-      for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
+      Sched sc(cluster_id, num_clusters, splits, num_k, num_tiles, sk_per);
+      Work w;
+      while (ok && sc.next(w)) {
         if (!mbar_wait_cluster(&tempty[acc], acc_ph ^ 1u, abort_flag, status, 23)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc) * ACC_STRIDE;
-        const int kb0 = (u % splits) * k_chunk, kb1 = min(num_k, kb0 + k_chunk);
+        const int kb0 = w.kb0, kb1 = w.kb1;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[s], ph, abort_flag, status, 24)) {
             ok = false;
@@ -557,8 +617,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
     const int q = warp & 3;
     int acc = 0;
     uint32_t acc_ph = 0;
-    for (int u = cluster_id; u < num_units; u += num_clusters) {
-      const int t = u / splits;
+    Sched sc(cluster_id, num_clusters, splits, num_k, num_tiles, sk_per);
+    Work w;
+    while (sc.next(w)) {
+      const int t = w.t;
       const int mb = t % num_m, nb = t / num_m;
       if constexpr (EPI == kE2SwigluBwd) {
         // the saved a, b of this tile's rows into L2 while its mainloop still runs (the chunk loop below then
@@ -581,13 +643,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
       const int row = mb * 2 * kBM + static_cast<int>(crank) * kBM + q * 32 + lane;
       const uint32_t tb = tmem_base + static_cast<uint32_t>(acc) * ACC_STRIDE + (static_cast<uint32_t>(q * 32) << 16);
       bool last = true;
-      const float* other = nullptr;
-      if (splits == 2) {
-        // publish this K half's partial (this warp's 32 rows x BN, fp32), then count the warp's arrival for the
-        // tile: the second of the two arrivals adds the first's partial and stores. a + b == b + a, so the
-        // result does not depend on which half arrives last
-        const int64_t lrow = (static_cast<int64_t>(u) * 2 + crank) * kBM + q * 32 + lane;
-        float* mine = ws + lrow * BN;
+      const float4* pp[4] = {nullptr, nullptr, nullptr, nullptr};   // the last arriver: every part's words of
+      int my_split = 0;                                                // this lane's row (its own read from TMEM)
+      const int nparts = w.parts;
+      if (nparts >= 2) {
+        // publish this K part's partial (this warp's 32 rows x BN, fp32), then count the warp's arrival for the
+        // tile: the last of the parts to arrive sums them in K order ((p0 + p1) + p2) + p3 -- its own from TMEM --
+        // and stores, so the result does not depend on the order of arrival.
+        // workspace layout per (slot, CTA): 16-byte word w = 4 consecutive columns of row r at float4 index
+        // w x 128 + r, so the 32 lanes of a warp (32 consecutive rows) store / load 512 contiguous bytes
+        float4* mine =
+            reinterpret_cast<float4*>(ws + (static_cast<int64_t>(w.slot) * 2 + crank) * kBM * BN) + q * 32 + lane;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
@@ -595,8 +661,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(mine + c * 32 + j) = make_float4(
-                __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+            mine[(c * 8 + j / 4) * kBM] = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                      __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
         }
         __threadfence();
         __syncwarp();
@@ -604,12 +670,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
         int prev = 0;
         if (lane == 0) prev = atomicAdd(cnt, 1);
         prev = __shfl_sync(0xffffffffu, prev, 0);
-        last = prev == 1;
+        last = prev == nparts - 1;
         if (last) {
           __threadfence();
           if (lane == 0) *cnt = 0;                   // ready for the next GEMM that uses these counters
-          const int64_t orow = (static_cast<int64_t>(u ^ 1) * 2 + crank) * kBM + q * 32 + lane;
-          other = ws + orow * BN;
+          my_split = w.part;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (j < nparts)
+              pp[j] = reinterpret_cast<const float4*>(ws + (sc.part_slot(t, j) * 2 + crank) * kBM * BN) + q * 32 +
+                      lane;
         }
       }
       float sq = 0.f;
@@ -691,19 +761,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GATHER ? kThreadsG :
           }
           continue;
         }
-        if (other != nullptr) {
+        if (pp[0] != nullptr) {
+          // sum of the K parts in K order; this unit's part is the accumulator just read
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
-            const float4 o = *reinterpret_cast<const float4*>(other + c * 32 + j);
-            r[j] = __float_as_uint(__uint_as_float(r[j]) + o.x);
-            r[j + 1] = __float_as_uint(__uint_as_float(r[j + 1]) + o.y);
-            r[j + 2] = __float_as_uint(__uint_as_float(r[j + 2]) + o.z);
-            r[j + 3] = __float_as_uint(__uint_as_float(r[j + 3]) + o.w);
+            float4 tot = my_split == 0 ? make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                     __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]))
+                                       : pp[0][(c * 8 + j / 4) * kBM];
+#pragma unroll
+            for (int sp = 1; sp < 4; ++sp) {
+              if (sp >= nparts) break;
+              const float4 o = sp == my_split
+                                   ? make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                 __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]))
+                                   : pp[sp][(c * 8 + j / 4) * kBM];
+              tot.x += o.x;
+              tot.y += o.y;
+              tot.z += o.z;
+              tot.w += o.w;
+            }
+            r[j] = __float_as_uint(tot.x);
+            r[j + 1] = __float_as_uint(tot.y);
+            r[j + 2] = __float_as_uint(tot.z);
+            r[j + 3] = __float_as_uint(tot.w);
           }
         }
         if (row < M && col < N) sq += store_row32<EPI>(r, Cv, R, row, col, N, ldc, ldr);
       }
-      if (e2_sq(EPI)) {
+      if (e2_sq(EPI) && last) {
         // one partial per (tile, CTA, epilogue warp), every slot written exactly once (no clearing needed)
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
@@ -730,6 +815,8 @@ struct PairArgs {
   float* ws;
   int* counters;
   float* sq_part;
+  int64_t sk_per = 0;       // stream-K: K iterations per CTA pair (0: uniform split-K / none)
+  int sk_clusters = 0;      // stream-K: CTA pairs launched
 };
 
 template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER = false>
@@ -744,9 +831,9 @@ void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const __
     attr_set = true;
   }
   const int units = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + BN - 1) / BN) * pa.splits;
-  const int clusters = std::max(1, std::min(units, num_sms() / 2));
+  const int clusters = pa.sk_per > 0 ? pa.sk_clusters : std::max(1, std::min(units, num_sms() / 2));
   kern<<<2 * clusters, GATHER ? kThreadsG : kThreads2, S::TOTAL, stream>>>(
-      ta, tb, C, R, M, N, K, ldc, ldr, pa.splits, pa.ws, pa.counters, status_ptr(), pa.sq_part, aux, ga);
+      ta, tb, C, R, M, N, K, ldc, ldr, pa.splits, pa.sk_per, pa.ws, pa.counters, status_ptr(), pa.sq_part, aux, ga);
   check_launch("gemm_pair");
 }
 
@@ -793,8 +880,10 @@ int* pair_counters() {
 }  // namespace
 
 // C = A @ B^T on CTA pairs (operand conventions as gemm()). C: bf16 or fp32 [M, N]; R: bf16 residual.
-// bn: output tile width, 256, 192 or 128; splits: 1, or 2 (each tile's K range in two halves on two pairs, summed by the
-// epilogue of the later one; the fp32 workspace is allocated here).
+// bn: output tile width, 256, 192 or 128; splits: 1 .. 4 (each tile's K range in `splits` parts on as many pairs,
+// summed in part order by the epilogue of the last to finish; the fp32 workspace is allocated here), or 0 for
+// stream-K (every pair takes an equal contiguous share of the tile-major K iterations; only the tiles cut by a share
+// boundary are summed from parts).
 void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_mn, bool b_mn,
                const c10::optional<at::Tensor>& R, int64_t bn, int64_t splits) {
   FYB_RANGE("fyb::gemm_pair");
@@ -822,7 +911,7 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_m
     ldr = R->stride(0);
   }
   FYB_CHECK(bn == 256 || bn == 192 || bn == 128, "gemm_pair: tile width must be 256, 192 or 128");
-  FYB_CHECK(splits == 1 || splits == 2, "gemm_pair: splits must be 1 or 2");
+  FYB_CHECK(splits >= 0 && splits <= 4, "gemm_pair: splits must be 0 (stream-K) or 1 .. 4");
   if (M == 0 || N == 0) return;
   c10::cuda::CUDAGuard guard(A.device());
   cudaStream_t st = cur_stream();
@@ -830,10 +919,25 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, bool a_m
   const int64_t num_k = (K + kBK - 1) / kBK;
   PairArgs pa{static_cast<int>(splits), nullptr, nullptr, nullptr};
   at::Tensor ws;
-  if (splits == 2) {
-    FYB_CHECK(num_k >= 2, "gemm_pair: split-K needs at least two K blocks");
+  if (splits == 0) {
+    // stream-K: every CTA pair takes the same number of the tile-major K iterations
+    const int64_t total = tiles * num_k;
+    const int64_t clusters = std::max<int64_t>(1, std::min<int64_t>(num_sms() / 2, total));
+    // at least a third of a tile's K blocks per pair, so a tile is cut into at most 4 parts
+    const int64_t per = std::max((total + clusters - 1) / clusters, (num_k + 2) / 3);
+    FYB_CHECK((num_k + per - 1) / per + 1 <= 4, "gemm_pair: stream-K would cut a tile into more than 4 parts");
+    FYB_CHECK(tiles <= kMaxPairTiles, "gemm_pair: too many tiles for stream-K");
+    pa.splits = 1;
+    pa.sk_per = per;
+    pa.sk_clusters = static_cast<int>((total + per - 1) / per);
+    ws = at::empty({static_cast<int64_t>(pa.sk_clusters) * 2 * 2 * kBM, bn}, A.options().dtype(at::kFloat));
+    pa.ws = ws.data_ptr<float>();
+    pa.counters = pair_counters();
+  } else if (splits >= 2) {
+    FYB_CHECK((splits - 1) * ((num_k + splits - 1) / splits) < num_k,
+              "gemm_pair: split-K needs at least one K block in every part");
     FYB_CHECK(tiles <= kMaxPairTiles, "gemm_pair: too many tiles for split-K");
-    ws = at::empty({tiles * 2 * 2 * kBM, bn}, A.options().dtype(at::kFloat));
+    ws = at::empty({tiles * splits * 2 * kBM, bn}, A.options().dtype(at::kFloat));
     pa.ws = ws.data_ptr<float>();
     pa.counters = pair_counters();
   }

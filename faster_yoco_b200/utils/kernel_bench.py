@@ -1,7 +1,7 @@
 """Per-kernel microbenchmarks: the sm_100a kernels against the library baselines (cuBLAS, flash-attn) on the
 YOCO-3B shapes, timed with CUDA events after warm-up, inputs rotated through a pool larger than L2.
 
-    python -m faster_yoco_b200.utils.kernel_bench [--only gemm|fused|attn|ret] [--pair 1]
+    python -m faster_yoco_b200.utils.kernel_bench [--only gemm|splits|fused|attn|ret] [--pair 1]
 """
 from __future__ import annotations
 
@@ -92,6 +92,38 @@ def bench_gemm(results, pair_too: bool = False):
         t_routed = _time(routed)
         r.update(routed_ms=t_routed, routed_tflops=fl / t_routed / 1e9,
                  route=list(ops._gemm_route(M, N, K)))
+        results.append(r)
+
+
+def bench_gemm_splits(results):
+    """The CTA-pair kernel's in-kernel split-K (1 .. 4 K parts per 256 x 256 tile, 0 = stream-K) on every YOCO-3B shape, next to
+    the routed GEMM: the data behind the routing rule for shapes whose tiles fill the last round poorly."""
+    from faster_yoco_b200 import ops
+    dev = torch.device("cuda")
+    for name, M, N, K, a_mn, b_mn in gemm_shapes():
+        a_shape = (K, M) if a_mn else (M, K)
+        b_shape = (K, N) if b_mn else (N, K)
+        pool = _pool(lambda: (torch.randn(a_shape, device=dev, dtype=torch.bfloat16),
+                              torch.randn(b_shape, device=dev, dtype=torch.bfloat16)), 2 * (M * K + N * K))
+        c = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        it = [0]
+
+        def pair(splits):
+            a, b = pool[it[0] % len(pool)]
+            it[0] += 1
+            ops._C().gemm_pair(a, b, c, a_mn, b_mn, None, 256, splits)
+
+        def routed():
+            a, b = pool[it[0] % len(pool)]
+            it[0] += 1
+            ops.gemm(a, b, a_mn_major=a_mn, b_mn_major=b_mn, out=c)
+
+        nk = (K + 63) // 64
+        r = {"kernel": "gemm_splits", "shape": name, "M": M, "N": N, "K": K, "routed_ms": _time(routed),
+             "route": list(ops._gemm_route(M, N, K))}
+        for sp in (0, 1, 2, 3, 4):         # 0: stream-K
+            if sp == 0 or (sp - 1) * ((nk + sp - 1) // sp) < nk:
+                r[f"pair_s{sp}_ms"] = _time(lambda: pair(sp))
         results.append(r)
 
 
@@ -238,6 +270,8 @@ def main():
     res = []
     if a.only in (None, "gemm"):
         bench_gemm(res, pair_too=bool(a.pair))
+    if a.only == "splits":
+        bench_gemm_splits(res)
     if a.only in (None, "gemm", "fused"):
         bench_gemm_fused(res)
     if a.only in (None, "attn"):

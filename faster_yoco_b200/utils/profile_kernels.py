@@ -6,7 +6,7 @@ cases: attn, attn_bwd, swa, swa_bwd (sliding window 1024), ret, ret_bwd (paralle
 ret_chunk_bwd (chunkwise kernels), gemm, gemm_dgrad, gemm_scatter (weight
 gradient stored at 4 emulated owners, block-cyclic map), adam, ce, ce_bwd, rms, rms_bwd, subln, subln_bwd, swiglu,
 swiglu_bwd, rope, embed, embed_bwd, reduce_compact, reduce_owner, adam_push (eight ranks emulated in local memory),
-gate_cumsum (chunk-local), gemm_pair, gemm_pair128, gemm_swiglu, gemm_swiglu_bwd (fused epilogues).
+gate_cumsum (chunk-local), gemm_pair, gemm_pair128, gemm_swiglu, gemm_swiglu_bwd (fused epilogues), gemm_pair_sk / gemm_pair_s1 (stream-K vs one part).
 """
 import argparse
 
@@ -205,6 +205,13 @@ def main():
                 C.gemm_swiglu(x, w)
             else:
                 C.gemm_pair(x, w, y, False, False, None, 128 if a.what == "gemm_pair128" else 256)
+    elif a.what in ("gemm_pair_sk", "gemm_pair_s1"):
+        # a 3,072-wide output (96 pair tiles on 74 CTA pairs): stream-K vs one K part per tile
+        x = torch.randn(2048, 3072, device=dev, dtype=torch.bfloat16)
+        w = (torch.randn(3072, 3072, device=dev) * 0.02).to(torch.bfloat16)
+        y = torch.empty(2048, 3072, device=dev, dtype=torch.bfloat16)
+        for _ in range(a.reps):
+            C.gemm_pair(x, w, y, False, False, None, 256, 0 if a.what == "gemm_pair_sk" else 1)
     elif a.what == "gemm_swiglu_bwd":
         g = (torch.randn(2048, 3072, device=dev) * 1e-3).to(torch.bfloat16)
         w2 = (torch.randn(3072, 8192, device=dev) * 0.02).to(torch.bfloat16)

@@ -39,8 +39,12 @@ def _close_in_ulps(x, y, ulps, acc_mag=None):
     (520, 300, 136, True, False),
 ])
 @pytest.mark.parametrize("epi", ["bf16", "res", "f32"])
-@pytest.mark.parametrize("bn,splits", [(256, 1), (192, 1), (128, 1), (256, 2), (192, 2)])
+@pytest.mark.parametrize("bn,splits", [(256, 1), (192, 1), (128, 1), (256, 2), (192, 2), (256, 3), (256, 4), (256, 0),
+                                       (192, 0)])
 def test_gemm_pair_matches_one_cta_and_fp32(M, N, K, a_mn, b_mn, epi, bn, splits):
+    nk = (K + 63) // 64
+    if splits and (splits - 1) * ((nk + splits - 1) // splits) >= nk:
+        pytest.skip("a K part would be empty")
     C = ops._C()
     g = torch.Generator(device="cuda").manual_seed(M + N + K)
     a, b = _operands(M, N, K, a_mn, b_mn, g)
@@ -52,6 +56,7 @@ def test_gemm_pair_matches_one_cta_and_fp32(M, N, K, a_mn, b_mn, epi, bn, splits
     A32 = (a.float().t() if a_mn else a.float())
     B32 = (b.float() if b_mn else b.float().t())
     prod = A32 @ B32
+    first = None
     for _ in range(2):
         pair = torch.full((M, N), float("nan"), dtype=dt, device=dev)
         C.gemm_pair(a, b, pair, a_mn, b_mn, res, bn, splits)
@@ -61,6 +66,10 @@ def test_gemm_pair_matches_one_cta_and_fp32(M, N, K, a_mn, b_mn, epi, bn, splits
         # same per-element K order in both kernels: equal up to the tensor cores' accumulation rounding, which can
         # move a bf16 output by one unit in the last place (two with the residual epilogue's second rounding)
         _close_in_ulps(pair.float(), one.float(), 2 if dt == torch.bfloat16 else 0, prod.abs())
+        # split-K parts are summed in part order whatever order they finish in: runs are bitwise identical
+        if first is not None:
+            assert torch.equal(pair, first)
+        first = pair
     ref = prod
     if res is not None:
         ref = ref + res.float()
