@@ -37,6 +37,15 @@ import torch.distributed as dist
 from .. import ops
 
 
+def pull_weight_ids(flat, model) -> set:
+    """The weights whose all-gather the consuming forward GEMM carries (pull exchange): every 2-D parameter whose rows
+    are whole 16-byte vectors, except embeddings (their forward is a row lookup, not a GEMM; a weight tied to one is
+    excluded with it)."""
+    embed = {id(p) for n, p in model.named_parameters(remove_duplicate=False) if "embed" in n}
+    return {id(e.param) for e in flat.entries
+            if e.param.dim() == 2 and id(e.param) not in embed and e.param.shape[1] % 8 == 0}
+
+
 class PeerComm:
     NSLOTS = 64          # flag slots: 0 = generic barrier, 1..61 = reduction buckets, 63 = gather barrier
     GATHER_SLOT = 63
@@ -256,12 +265,7 @@ class PeerComm:
         one barrier, which also tells the pullers that its owned rows are final. Best with the block-cyclic owner
         map: a tile column then spans several owners, and pulls from several peers at once run near link speed
         where pulls from one peer do not."""
-        embed = {id(p) for n, p in model.named_parameters(remove_duplicate=False) if "embed" in n}
-        ids = set()
-        for e in flat.entries:
-            p = e.param
-            if p.dim() == 2 and id(p) not in embed and p.shape[1] % 8 == 0:
-                ids.add(id(p))
+        ids = pull_weight_ids(flat, model)
         rest = [[o, c] for e in flat.entries if id(e.param) not in ids
                 for o, c, r in flat.owner_ranges(e) if r == self.rank]
         self.rest_ranges = torch.tensor(rest, dtype=torch.int64, device=self.dev).view(-1, 2)
