@@ -325,19 +325,20 @@ __global__ void adam_kernel(float* __restrict__ p32, const __nv_bfloat16* __rest
   for (int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < n; i += stride) {
     if (i + 4 <= n) {
       const int64_t x = zero_flat(z, i);   // the bf16 gradient / parameter of local element i (4 in one chunk)
-      float4 P = *reinterpret_cast<float4*>(p32 + i);
-      float4 Mv = *reinterpret_cast<float4*>(m + i);
-      float4 Vv = *reinterpret_cast<float4*>(v + i);
-      const uint2 gu = *reinterpret_cast<const uint2*>(g16 + x);
+      // every byte is touched once per update: streaming loads / stores (evict-first) keep the L2 for the rest
+      float4 P = __ldcs(reinterpret_cast<const float4*>(p32 + i));
+      float4 Mv = __ldcs(reinterpret_cast<const float4*>(m + i));
+      float4 Vv = __ldcs(reinterpret_cast<const float4*>(v + i));
+      const uint2 gu = __ldcs(reinterpret_cast<const uint2*>(g16 + x));
       const float2 g01 = unpack_bf16(gu.x), g23 = unpack_bf16(gu.y);
       adam_elem(P.x, Mv.x, Vv.x, g01.x * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
       adam_elem(P.y, Mv.y, Vv.y, g01.y * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
       adam_elem(P.z, Mv.z, Vv.z, g23.x * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
       adam_elem(P.w, Mv.w, Vv.w, g23.y * f, lr, b1, b2, eps, wd, bc1, bc2, adamw);
-      *reinterpret_cast<float4*>(p32 + i) = P;
-      *reinterpret_cast<float4*>(m + i) = Mv;
-      *reinterpret_cast<float4*>(v + i) = Vv;
-      *reinterpret_cast<uint2*>(p16 + x) = make_uint2(pack_bf16(P.x, P.y), pack_bf16(P.z, P.w));
+      __stcs(reinterpret_cast<float4*>(p32 + i), P);
+      __stcs(reinterpret_cast<float4*>(m + i), Mv);
+      __stcs(reinterpret_cast<float4*>(v + i), Vv);
+      __stcs(reinterpret_cast<uint2*>(p16 + x), make_uint2(pack_bf16(P.x, P.y), pack_bf16(P.z, P.w)));
     } else {
       for (int64_t j = i; j < n; ++j) {
         const int64_t x = zero_flat(z, j);

@@ -298,7 +298,8 @@ __device__ __forceinline__ float store_row32(const uint32_t (&r)[32], void* Cv, 
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       if (col + j < N) {
-        const uint16_t h = (j & 1) ? static_cast<uint16_t>(p[j >> 1] >> 16) : static_cast<uint16_t>(p[j >> 1] & 0xffffu);
+        const uint16_t h =
+            (j & 1) ? static_cast<uint16_t>(p[j >> 1] >> 16) : static_cast<uint16_t>(p[j >> 1] & 0xffffu);
         C[j] = __ushort_as_bfloat16(h);
       }
     }
@@ -317,7 +318,8 @@ __device__ __forceinline__ float store_row32(const uint32_t (&r)[32], void* Cv, 
 
 __device__ __forceinline__ void store16x2(__nv_bfloat16* p, const uint32_t (&w)[16]) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(p + 8 * j) = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4*>(p + 8 * j) = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
 }
 
 __device__ __forceinline__ void load16x2(const __nv_bfloat16* p, uint32_t (&w)[16]) {

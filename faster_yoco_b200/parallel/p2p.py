@@ -38,12 +38,14 @@ from .. import ops
 
 
 def pull_weight_ids(flat, model) -> set:
-    """The weights whose all-gather the consuming forward GEMM carries (pull exchange): every 2-D parameter whose rows
-    are whole 16-byte vectors, except embeddings (their forward is a row lookup, not a GEMM; a weight tied to one is
-    excluded with it)."""
+    """The weights whose all-gather the consuming forward GEMM carries (pull exchange): every 2-D parameter both of
+    whose dimensions are multiples of 8 (the shapes the native GEMM takes; others run on the library path, which
+    reads the local replica as it is), except embeddings (their forward is a row lookup, not a GEMM; a weight tied
+    to one is excluded with it)."""
     embed = {id(p) for n, p in model.named_parameters(remove_duplicate=False) if "embed" in n}
     return {id(e.param) for e in flat.entries
-            if e.param.dim() == 2 and id(e.param) not in embed and e.param.shape[1] % 8 == 0}
+            if e.param.dim() == 2 and id(e.param) not in embed and e.param.shape[0] % 8 == 0
+            and e.param.shape[1] % 8 == 0}
 
 
 class PeerComm:

@@ -1,7 +1,7 @@
 """Per-kernel microbenchmarks: the sm_100a kernels against the library baselines (cuBLAS, flash-attn) on the
 YOCO-3B shapes, timed with CUDA events after warm-up, inputs rotated through a pool larger than L2.
 
-    python -m faster_yoco_b200.utils.kernel_bench [--only gemm|splits|fused|attn|ret] [--pair 1]
+    python -m faster_yoco_b200.utils.kernel_bench [--only gemm|splits|fused|adam|attn|ret] [--pair 1]
 """
 from __future__ import annotations
 
@@ -96,8 +96,9 @@ def bench_gemm(results, pair_too: bool = False):
 
 
 def bench_gemm_splits(results):
-    """The CTA-pair kernel's in-kernel split-K (1 .. 4 K parts per 256 x 256 tile, 0 = stream-K) on every YOCO-3B shape, next to
-    the routed GEMM: the data behind the routing rule for shapes whose tiles fill the last round poorly."""
+    """The CTA-pair kernel's in-kernel split-K (1 .. 4 K parts per 256 x 256 tile, 0 = stream-K) on every YOCO-3B
+    shape, next to the routed GEMM: the data behind the routing rule for shapes whose tiles fill the last round
+    poorly."""
     from faster_yoco_b200 import ops
     dev = torch.device("cuda")
     for name, M, N, K, a_mn, b_mn in gemm_shapes():
@@ -204,6 +205,29 @@ def bench_gemm_fused(results):
                     "fused_tflops": 2.0 * T * f * d / tf / 1e9})
 
 
+def bench_adam(results, n=1 << 30):
+    """Adam (apex expression) + bf16 parameter copy over n elements (28 bytes each: fp32 master, m, v read + write,
+    bf16 gradient read, bf16 parameter write), the 4-per-thread kernel and the 8-per-thread form (the Adam + push
+    kernel with no peers); achieved bandwidth = algorithmic bytes / CUDA-event time."""
+    from faster_yoco_b200 import ops
+    dev = torch.device("cuda")
+    C = ops._C()
+    p32 = torch.randn(n, device=dev)
+    m = torch.zeros(n, device=dev)
+    v = torch.zeros(n, device=dev)
+    g16 = torch.randn(n, device=dev, dtype=torch.bfloat16)
+    p16 = torch.empty(n, device=dev, dtype=torch.bfloat16)
+    hyper = torch.tensor([1e-4, 0.1, 0.05, 1.0], device=dev)
+    factor = torch.tensor([1.0], device=dev)
+    t4 = _time(lambda: C.adam_step(p32, g16, m, v, p16, hyper, factor, 0.9, 0.95, 1e-6, 0.05, True), iters=10,
+               warmup=3)
+    t8 = _time(lambda: C.adam_push(p32, g16, m, v, p16, hyper, factor, 0.9, 0.95, 1e-6, 0.05, True,
+                                   [p16.data_ptr()], 0, 0, 0), iters=10, warmup=3)
+    gb = 28.0 * n / 1e9
+    results.append({"kernel": "adam", "n": n, "adam_ms": t4, "adam_tbs": gb / t4, "adam8_ms": t8,
+                    "adam8_tbs": gb / t8})
+
+
 def bench_attention(results, L=2048, Hq=24, Hk=8, B=1):
     from faster_yoco_b200 import ops
     dev = torch.device("cuda")
@@ -272,6 +296,8 @@ def main():
         bench_gemm(res, pair_too=bool(a.pair))
     if a.only == "splits":
         bench_gemm_splits(res)
+    if a.only == "adam":
+        bench_adam(res)
     if a.only in (None, "gemm", "fused"):
         bench_gemm_fused(res)
     if a.only in (None, "attn"):

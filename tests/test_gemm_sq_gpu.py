@@ -61,7 +61,8 @@ def test_one_gpu_training_norm_from_gemm_partials(graph, tied):
 
 
 def test_adam_eight_wide_matches_adam():
-    """FYB_ADAM8: the one-segment Adam through the 8-wide (Adam + push, no peers) kernel gives the same parameters."""
+    """The 8-wide Adam (the Adam + push kernel with no peers; default for contiguous owner maps) gives the same
+    parameters as the 4-wide kernel."""
     from faster_yoco_b200.utils import dist_checks
     ops.set_backend("native")
     dev = torch.device("cuda", 0)
