@@ -40,11 +40,12 @@ def parse():
     p.add_argument("--comm", default="fused", choices=["nccl", "fused"],
                    help="fused: NVLink peer-memory collectives overlapped with compute; nccl: the baseline path")
     p.add_argument("--graph", type=int, default=1, help="capture the whole update as one CUDA graph")
-    p.add_argument("--overlap", default="auto", choices=["auto", "0", "1"],
-                   help="fused comm: bucketed pushes overlapped with forward/backward. auto = on with the copy-engine "
-                        "transport at 2 GPUs (one peer: the copy engines reach 766 GB/s and take no SM time), off "
-                        "(serial P2P reduce + push all-gather after backward) at more GPUs, where the copy engines "
-                        "deliver only ~210 GB/s in aggregate to 7 peers")
+    p.add_argument("--overlap", default="auto", choices=["auto", "0", "1", "grads"],
+                   help="fused comm: 1 = gradients and parameters pushed per layer bucket, overlapped with "
+                        "backward / forward; grads = only the gradients per bucket during backward, the parameters "
+                        "by the fused Adam + push after it; 0 = the serial exchange (P2P reduce + fused Adam + push "
+                        "after backward); auto = the measured schedule of this GPU count "
+                        "(faster_yoco_b200.parallel.zero.AUTO_SCHEDULE)")
     p.add_argument("--transport", default="auto", choices=["auto", "sm", "ce", "gemm", "pull"],
                    help="overlapped exchange: pushes by kernels (sm) or by the copy engines (ce); gemm: the "
                         "weight-gradient GEMMs store every element at its ZeRO owner over NVLink (GEMM fused with the "
@@ -195,7 +196,8 @@ def result_line(args, world: int, ms: float, clocks, e2e, launches, exposed=None
                    "kernels": args.kernels, "comm": args.comm if world > 1 else "none",
                    "vs_baseline_basis": "tokens/s per GPU vs 138983/8 (8xH100 published)",
                    "cuda_graph": bool(args.graph),
-                   "comm_overlap": bool(args.overlap), "zero_partition": args.partition,
+                   "comm_overlap": args.overlap if args.overlap == "grads" else bool(int(args.overlap)),
+                   "zero_partition": args.partition,
                    "transport": (args.transport if (args.overlap or args.transport == "gemm") else None)
                    if world > 1 else None,
                    "l2": "working set (>=55 GB of params/grads/Adam state per update) >> 126 MB L2"},
@@ -229,6 +231,7 @@ def main():
     from faster_yoco_b200.data.synthetic import SyntheticLM
     from faster_yoco_b200.models.yoco import YOCO
     from faster_yoco_b200.parallel import dist as D
+    from faster_yoco_b200.parallel.zero import exchange_schedule
     from faster_yoco_b200.train.trainer import Trainer
 
     dev_index = D.init(timeout_s=300)
@@ -237,12 +240,7 @@ def main():
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     dev = torch.device("cuda", dev_index)
     ops.set_backend(args.kernels)
-    if args.overlap == "auto":
-        args.overlap = 1 if (world == 2 and args.comm == "fused" and args.transport not in ("gemm", "pull")) else 0
-    else:
-        args.overlap = int(args.overlap)
-    if args.transport == "auto":
-        args.transport = "ce" if world == 2 else "sm"
+    args.overlap, args.transport = exchange_schedule(world, args.comm, args.overlap, args.transport)
     torch.manual_seed(1234)
 
     margs = build_args(args.arch, max_seq_len=args.seq_len, max_batch_size=args.batch, init_std=0.02,
@@ -252,8 +250,7 @@ def main():
     model = model.to(torch.bfloat16)
     optim = OptimConfig()
     trainer = Trainer(model, optim, device=dev, comm=args.comm, graph_step=bool(args.graph),
-                      overlap=bool(args.overlap), transport=args.transport, partition=args.partition,
-                      chunk=args.zero_chunk)
+                      overlap=args.overlap, transport=args.transport, partition=args.partition, chunk=args.zero_chunk)
     data = SyntheticLM(margs.vocab_size, args.seq_len, args.batch, seed=1, rank=rank, pin=True)
     batches = [next(data) for _ in range(4)]
 

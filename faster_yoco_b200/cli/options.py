@@ -130,8 +130,9 @@ def train_parser() -> argparse.ArgumentParser:
                    help="fused: NVLink peer-memory reduce/all-gather kernels; nccl: the NCCL baseline path")
     g.add_argument("--cuda-graph", type=_bool_int, default=True, help="capture each update as one CUDA graph")
     g.add_argument("--overlap", default="auto",
-                   help="overlap the ZeRO exchange with forward/backward: auto (copy-engine pushes at 2 GPUs, "
-                        "serial exchange otherwise), 1 or 0")
+                   help="overlap the ZeRO exchange with forward/backward: auto (the measured schedule of the GPU "
+                        "count), 1 (gradients and parameters per layer bucket), grads (gradients per bucket during "
+                        "backward, parameters by the fused Adam + push) or 0 (serial)")
     g.add_argument("--transport", default="auto", choices=["auto", "sm", "ce", "gemm", "pull"],
                    help="overlapped pushes by kernels (sm) or by the copy engines (ce); gemm: serial schedule whose "
                         "weight-gradient GEMMs store each element at its ZeRO owner (GEMM fused with the "

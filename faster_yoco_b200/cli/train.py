@@ -22,6 +22,7 @@ import torch.distributed as dist
 
 from ..config import OptimConfig
 from ..parallel import dist as D
+from ..parallel.zero import exchange_schedule
 from ..train.checkpoint import load_checkpoint, part_path, prune_interval_checkpoints, save_checkpoint
 from ..train.metrics import format_log
 from ..train.trainer import Trainer
@@ -43,10 +44,6 @@ def _cp_slice(batch, cp: int):
     n = int(batch["ntokens"])
     out["ntokens"] = n // cp + (n % cp if r == cp - 1 else 0)
     return out
-
-
-def _flag(v) -> bool:
-    return str(v).lower() in ("1", "true", "yes", "on")
 
 
 def _gather_iterator_states(itr):
@@ -141,15 +138,9 @@ def main(argv=None) -> int:
     rep = cp if cp > 1 else tp                # consecutive ranks that hold one model replica
     dp = world // rep
     comm = args.comm if (dp > 1 and device.type == "cuda" and rep == 1) else "nccl"
-    if str(args.overlap) == "auto":
-        overlap = world == 2 and comm == "fused" and args.transport not in ("gemm", "pull")
-    else:
-        overlap = bool(_flag(args.overlap))
+    overlap, transport = exchange_schedule(dp, comm, args.overlap, args.transport)
     if tp > 1:
-        overlap = False
-    transport = ("ce" if world == 2 else "sm") if args.transport == "auto" else args.transport
-    if tp > 1:
-        transport = "sm"
+        overlap, transport = False, "sm"
     graph = bool(args.cuda_graph) and device.type == "cuda" and rep == 1
     trainer = Trainer(model, optim, device=device, comm=comm, graph_step=graph,
                       overlap=overlap, transport=transport, partition=args.partition, pad_idx=task.tokenizer.pad_id,

@@ -15,7 +15,9 @@ read and write peer memory directly over NVLink / NVSwitch:
 * bucketed overlap (``setup_buckets``): per layer bucket, gradient pieces are pushed to their owners during backward
   and parameters are pushed ahead of the next forward, either by kernels (``transport="sm"``) or by the copy
   engines (``transport="ce"``: one ``cudaMemcpyAsync`` per piece on one stream per peer, arrival published by a
-  one-thread release-add on the peer's counter); the owner sums the staged pieces from local memory;
+  one-thread release-add on the peer's counter); the owner sums the staged pieces from local memory. With
+  ``params="fused"`` only the gradients travel per bucket: the parameters go out with the fused Adam + push after
+  the update, as in the serial exchange;
 * GEMM-fused reduce-scatter (``setup_scatter`` / ``reduce_scattered``): the weight-gradient GEMMs and the embedding
   backward store their output at the owners' staging slots while backward runs; after it, one push of the remaining
   gradients, one barrier and the owner's local rank-order sum.
@@ -68,6 +70,7 @@ class PeerComm:
         # device-resident barrier epochs (one per flag slot) and mailbox call counter: graph replays stay correct
         self.counters = torch.zeros(self.NSLOTS + 1, dtype=torch.int32, device=self.dev)
         self.buckets = None
+        self.params_mode = "bucketed"
         self.peers: Dict[str, List[int]] = {}
         P = min(2 * torch.cuda.get_device_properties(self.dev).multi_processor_count, 1024)
         self.part = torch.zeros(P, dtype=torch.float32, device=self.dev)
@@ -205,18 +208,24 @@ class PeerComm:
 
     # ------------------------------------------------------------------------------------ overlapped (bucketed)
     def setup_buckets(self, flat, groups, reduce_ctas: Optional[int] = None, gather_ctas: Optional[int] = None,
-                      transport: str = "sm", grads: str = "push"):
+                      transport: str = "sm", grads: str = "push", params: str = "bucketed"):
         """groups: parameter lists in FORWARD order (bucket b = groups[b]). Precomputes, per bucket, the ranges this
         rank owns (reduced during backward) and the ranges it must pull from other owners (before forward).
 
         transport "sm": the pushes are kernels (remote stores from CTAs); "ce": the pushes are cudaMemcpyAsync
         transfers on one stream per peer (the copy engines move the data, so no SM time is taken from the GEMMs of
-        the overlapped forward / backward), each followed by a one-thread kernel that publishes the arrival."""
+        the overlapped forward / backward), each followed by a one-thread kernel that publishes the arrival.
+
+        params "bucketed": parameters are pushed bucket by bucket ahead of the next forward (start_gather /
+        wait_gather); "fused": only the gradients are exchanged per bucket, the parameters by the fused Adam + push
+        kernel after the update (its closing barrier also tells every owner that its staging slots may be written
+        again)."""
         if len(groups) > self.NSLOTS - 3:
             raise ValueError("too many buckets")
-        if transport not in ("sm", "ce") or grads not in ("push", "scatter"):
-            raise ValueError((transport, grads))
+        if transport not in ("sm", "ce") or grads not in ("push", "scatter") or params not in ("bucketed", "fused"):
+            raise ValueError((transport, grads, params))
         self.transport = transport
+        self.params_mode = params
         # grads "scatter": the weight-gradient GEMMs store at the owners (setup_scatter), so no bucket pushes
         # gradients; finish_reduce pushes the rest and sums (reduce_scattered)
         self.grads_mode = grads
@@ -344,6 +353,9 @@ class PeerComm:
         by bucket in forward order, into every peer's flat buffer on the communication stream; forward waits per
         bucket for the peers' pushes (wait_gather). Safe: a peer's previous reads of bucket b ended with its
         backward of b, which every owner's reduction of b (hence Adam) waited for."""
+        if self.params_mode == "fused":
+            self._reduced = [False] * self.nb        # parameters went out with the fused Adam + push
+            return
         if self.transport == "ce":
             return self._ce_start_gather()
         cur = torch.cuda.current_stream(self.dev)
@@ -357,6 +369,8 @@ class PeerComm:
         self._reduced = [False] * self.nb
 
     def wait_gather(self, b: int):
+        if self.params_mode == "fused":
+            return
         inc = (self.world - 1) * (1 if self.transport == "ce" else self.push_ctas)
         self.C.wait_arrivals(self.arrive, self.expected, b, inc)
 

@@ -35,6 +35,31 @@ ALIGN = 64          # elements (128 bytes of bf16): every parameter view starts 
 CYCLIC_CHUNK = 1 << 18   # elements per chunk of the block-cyclic owner map (512 KB of bf16)
 
 
+# Measured exchange schedule per GPU count (YOCO-3B, 2,048 tokens per GPU, one node), used by overlap / transport
+# "auto": world -> (overlap, transport). 2 GPUs: gradients pushed by the copy engines per layer bucket during
+# backward, parameters by the fused Adam + push (59.0 ms / update; copy-engine pushes of both 60.3 ms, serial 61.3 ms).
+# Other counts: the serial exchange (P2P reduce-to-owner after backward, then the fused Adam + push).
+AUTO_SCHEDULE = {2: ("grads", "ce")}
+
+
+def exchange_schedule(world: int, comm: str, overlap="auto", transport="auto"):
+    """(overlap, transport) for :class:`faster_yoco_b200.train.trainer.Trainer` from the command-line values.
+    overlap: "auto", "0" / "1" (or a bool) or "grads"; transport: "auto", "sm", "ce", "gemm" or "pull". "auto" picks
+    the measured schedule of this GPU count (AUTO_SCHEDULE) for the peer-memory exchange; an explicit transport
+    whose exchange is built differently (gemm, pull) keeps the serial schedule."""
+    plan = AUTO_SCHEDULE.get(world) if comm == "fused" else None
+    if str(overlap) == "auto":
+        if plan is not None and transport in ("auto", plan[1]):
+            overlap = plan[0]
+        else:
+            overlap = False
+    elif str(overlap) != "grads":
+        overlap = str(overlap).lower() in ("1", "true", "yes", "on")
+    if transport == "auto":
+        transport = plan[1] if plan is not None else "sm"
+    return overlap, transport
+
+
 def greedy_partition(sizes: Sequence[int], world: int) -> List[int]:
     """Owner of each parameter: next parameter to the rank with the smallest running total (ties: lowest rank)."""
     totals = [0] * world
@@ -433,7 +458,7 @@ class ZeroOptimizer:
         if fp.world == 1 or self.skip_exchange:
             return
         if self.comm == "fused" and self.p2p is not None:
-            if self.p2p.buckets is not None:
+            if self.p2p.buckets is not None and self.p2p.params_mode == "bucketed":
                 return          # pushed bucket by bucket ahead of the next update's forward (overlapped)
             if fp.pull is not None:
                 # the GEMM weights are pulled by their consumers in the next forward; push the rest, then one
@@ -498,8 +523,8 @@ class ZeroOptimizer:
         b1, b2 = self.cfg.betas
         seg = fp.param_segment()
         fused_push = (native and fp.world > 1 and self.comm == "fused" and self.p2p is not None
-                      and self.p2p.buckets is None and self.fuse_adam_push and not self.skip_exchange
-                      and fp.pull is None)
+                      and (self.p2p.buckets is None or self.p2p.params_mode == "fused") and self.fuse_adam_push
+                      and not self.skip_exchange and fp.pull is None)
         # the kernels address this owner's bf16 gradients / parameters through the owner map: its segment views
         # (contiguous layouts) or the whole flat buffers + the chunk size (block-cyclic)
         g_arg, p_arg = (fp.grad_flat, fp.flat) if fp.chunk else (g16, seg)

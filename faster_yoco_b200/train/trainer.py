@@ -45,9 +45,18 @@ class _CommHooks:
 class Trainer:
     def __init__(self, model: torch.nn.Module, optim_cfg, *, device, comm: str = "nccl",
                  pad_idx: int = 1, graph_step: bool = False, group=None, check_consistency: bool = True,
-                 overlap: bool = False, partition: str = "even", criterion=None, transport: str = "sm",
+                 overlap=False, partition: str = "even", criterion=None, transport: str = "sm",
                  chunk: Optional[int] = None, zero_sharding: str = "os"):
+        """overlap: False (the serial exchange after backward), True (gradients pushed to their owners per layer
+        bucket during backward and parameters per bucket ahead of the next forward) or "grads" (gradients per bucket
+        during backward, parameters by the fused Adam + push after the update)."""
         from ..parallel import tp as TP
+        overlap_params = "bucketed"
+        if overlap == "grads":
+            overlap, overlap_params = True, "fused"
+            if transport == "gemm":
+                overlap = False              # the GEMMs already deliver the gradients during backward
+        overlap = bool(overlap)
         self.tp = TP.tp_size()
         if self.tp > 1:
             # tensor x data parallelism: ZeRO shards over the data-parallel group (ranks holding the same TP slice);
@@ -119,7 +128,7 @@ class Trainer:
                 raise ValueError("transport 'pull' needs the native kernels (the gather-GEMM)")
             p2p.setup_pull(self.flat, model)
         elif self.overlap:
-            p2p.setup_buckets(self.flat, model.param_buckets(), transport=transport)
+            p2p.setup_buckets(self.flat, model.param_buckets(), transport=transport, params=overlap_params)
         self.sched = PolynomialDecaySchedule(optim_cfg.lr, optim_cfg.warmup_updates, optim_cfg.total_num_update,
                                              optim_cfg.end_learning_rate, optim_cfg.power)
         self.pending = PendingChecks(self.device.type == "cuda")

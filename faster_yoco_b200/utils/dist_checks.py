@@ -98,10 +98,13 @@ def fused_vs_nccl_gpu(rank, world, outdir, steps):
     ops.set_backend("native")
     dev = torch.device("cuda", rank)
     res = {}
+    # overlap "grads": gradients per bucket during backward, parameters by the fused Adam + push after the update
+    # (copy-engine pushes eager; kernel pushes inside the captured update)
     for name, comm, overlap, transport, graph in (
             ("nccl", "nccl", False, "sm", False), ("fused", "fused", True, "sm", False),
             ("fused_serial", "fused", False, "sm", False), ("fused_ce", "fused", True, "ce", False),
-            ("fused_ce_graph", "fused", True, "ce", True), ("fused_serial_two_pass", "fused", False, "sm", False)):
+            ("fused_ce_graph", "fused", True, "ce", True), ("fused_serial_two_pass", "fused", False, "sm", False),
+            ("fused_grads_ce", "fused", "grads", "ce", False), ("fused_grads_sm_graph", "fused", "grads", "sm", True)):
         model, tr = _tiny_trainer(dev, comm=comm, arch="yoco_small", dtype=torch.bfloat16, overlap=overlap,
                                   transport=transport, graph=graph)
         # the serial variants differ only in Adam + all-gather: one fused kernel, or Adam then the push kernel

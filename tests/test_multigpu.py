@@ -1,6 +1,7 @@
 """2-GPU data parallelism: the NVLink peer-memory collectives (fused reduce-to-owner, all-gather, mailbox
 all-reduce; serial, overlapped with kernel pushes, overlapped with copy-engine pushes, and the latter inside the
-whole-update CUDA graph) against the NCCL path on the same training run."""
+whole-update CUDA graph; gradients overlapped with parameters by the fused Adam + push) against the NCCL path on the
+same training run."""
 import os
 
 import pytest
@@ -15,7 +16,8 @@ pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 def test_fused_p2p_matches_nccl(tmp_path):
     run_ranks(dist_checks.fused_vs_nccl_gpu, 2, str(tmp_path), 4, backend="nccl", timeout_s=300)
     r = torch.load(os.path.join(tmp_path, "fused_vs_nccl.pt"))
-    for name in ("fused", "fused_serial", "fused_ce", "fused_ce_graph", "fused_serial_two_pass"):
+    for name in ("fused", "fused_serial", "fused_ce", "fused_ce_graph", "fused_serial_two_pass", "fused_grads_ce",
+                 "fused_grads_sm_graph"):
         assert r[name]["status"] == 0 and r["nccl"]["status"] == 0
         for a, b in zip(r[name]["losses"], r["nccl"]["losses"]):
             assert abs(a - b) / abs(b) < 2e-3, (name, r[name]["losses"], r["nccl"]["losses"])
@@ -23,7 +25,8 @@ def test_fused_p2p_matches_nccl(tmp_path):
         assert ((pf - pn).abs().max() / pn.abs().max()).item() < 2e-2, name
     # the overlapped and the serial peer-memory paths reduce in the same order; what differs run to run is only the
     # order of the fp32 atomics of the attention dQ accumulation
-    for name in ("fused", "fused_ce", "fused_ce_graph", "fused_serial_two_pass"):
+    for name in ("fused", "fused_ce", "fused_ce_graph", "fused_serial_two_pass", "fused_grads_ce",
+                 "fused_grads_sm_graph"):
         for a, b in zip(r[name]["losses"], r["fused_serial"]["losses"]):
             assert abs(a - b) / abs(b) < 2e-4, (name, r[name]["losses"], r["fused_serial"]["losses"])
         pf, ps = r[name]["params"], r["fused_serial"]["params"]
