@@ -320,16 +320,3 @@ def test_every_preset_parses():
         a = parse_with_preset(train_parser(), ["--preset", n, "DATA"])
         assert a.comm in ("fused", "nccl") and a.partition in ("even", "greedy", "cyclic"), n
 
-
-def test_exchange_schedule_auto_and_explicit():
-    """The measured exchange schedule behind overlap / transport "auto", and explicit values passed through."""
-    from faster_yoco_b200.parallel.zero import AUTO_SCHEDULE, exchange_schedule
-    for world, (ov, tr) in AUTO_SCHEDULE.items():
-        assert exchange_schedule(world, "fused") == (ov, tr)
-        assert exchange_schedule(world, "nccl") == (False, "sm")        # the library path has no peer pushes
-    assert exchange_schedule(1, "fused") == (False, "sm")
-    assert exchange_schedule(2, "fused", "0", "auto")[0] is False
-    assert exchange_schedule(8, "fused", "1", "ce") == (True, "ce")
-    assert exchange_schedule(8, "fused", "grads", "ce") == ("grads", "ce")
-    assert exchange_schedule(2, "fused", "auto", "pull") == (False, "pull")   # pull carries its own all-gather
-    assert exchange_schedule(2, "fused", "auto", "gemm") == (False, "gemm")
