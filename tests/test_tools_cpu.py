@@ -319,4 +319,3 @@ def test_every_preset_parses():
     for n in names:
         a = parse_with_preset(train_parser(), ["--preset", n, "DATA"])
         assert a.comm in ("fused", "nccl") and a.partition in ("even", "greedy", "cyclic"), n
-
