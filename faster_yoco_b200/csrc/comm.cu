@@ -591,7 +591,17 @@ void push_grads(const at::Tensor& grad, const std::vector<int64_t>& peer_staging
 void reduce_staged(at::Tensor& grad, const at::Tensor& staging, const at::Tensor& ranges, int64_t world, int64_t rank,
                    int64_t seg, at::Tensor& part, int64_t ctas, int64_t chunk) {
   FYB_RANGE("fyb::reduce_staged");
-  FYB_CHECK(part.numel() >= ctas, "reduce_staged: partials buffer too small");
+  // ranges: flat (offset, count) pieces of this owner's elements, offsets multiples of 8 elements (16-byte loads);
+  // every range of the ZeRO bucket tables is (parameters start 64-element aligned, owner cuts are multiples of 64)
+  FYB_CHECK(ranges.is_cuda() && ranges.scalar_type() == at::kLong && ranges.dim() == 2 && ranges.size(1) == 2,
+            "reduce_staged: ranges must be a device int64 [n, 2]");
+  FYB_CHECK(grad.scalar_type() == at::kBFloat16 && staging.scalar_type() == at::kBFloat16 &&
+                grad.numel() == world * seg && staging.numel() == world * seg && seg % 8 == 0,
+            "reduce_staged: bf16 gradient buffer and staging of world x seg elements");
+  FYB_CHECK(reinterpret_cast<uintptr_t>(grad.data_ptr()) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(staging.data_ptr()) % 16 == 0,
+            "reduce_staged: 16-byte aligned buffers");
+  FYB_CHECK(ctas >= 1 && part.numel() >= ctas, "reduce_staged: partials buffer too small");
   if (ranges.size(0) == 0) {
     part.zero_();
     return;

@@ -6,6 +6,7 @@ cases: attn, attn_bwd, swa, swa_bwd (sliding window 1024), ret, ret_bwd (paralle
 ret_chunk_bwd (chunkwise kernels), gemm, gemm_dgrad, gemm_scatter (weight
 gradient stored at 4 emulated owners, block-cyclic map), adam, ce, ce_bwd, rms, rms_bwd, subln, subln_bwd, swiglu,
 swiglu_bwd, rope, embed, embed_bwd, reduce_compact, reduce_owner, adam_push (eight ranks emulated in local memory),
+reduce_staged (four ranks emulated),
 gate_cumsum (chunk-local), gemm_pair, gemm_pair128, gemm_swiglu, gemm_swiglu_bwd (fused epilogues), gemm_pair_sk / gemm_pair_s1 (stream-K vs one part).
 """
 import argparse
@@ -191,6 +192,18 @@ def main():
             for _ in range(a.reps):
                 C.adam_push(p32, g16, m, v, pb[rank][rank * seg:(rank + 1) * seg], hyper, factor, 0.9, 0.95, 1e-6,
                             0.05, True, [t.data_ptr() for t in pb], rank * seg, rank, 0)
+    elif a.what == "reduce_staged":
+        # four ranks emulated in this GPU's memory: rank 1's owner-side sum after the copy engines delivered the
+        # other ranks' gradient pieces into its staging slots (the 4-GPU default exchange), over a 32 Mi-element
+        # segment cut into 26 bucket pieces as in the training step
+        world, rank, seg = 4, 1, 1 << 25
+        grad = torch.randn(world * seg, device=dev).to(torch.bfloat16)
+        staging = torch.randn(world * seg, device=dev).to(torch.bfloat16)
+        cuts = [rank * seg + (seg * k // 26) // 64 * 64 for k in range(26)] + [(rank + 1) * seg]
+        ranges = torch.tensor([[a0, b0 - a0] for a0, b0 in zip(cuts, cuts[1:])], dtype=torch.int64, device=dev)
+        part = torch.zeros(296, device=dev)
+        for _ in range(a.reps):
+            C.reduce_staged(grad, staging, ranges, world, rank, seg, part, 296, 0)
     elif a.what == "gate_cumsum":
         y = torch.randn(2048, 12312, device=dev, dtype=torch.bfloat16)
         for _ in range(a.reps):

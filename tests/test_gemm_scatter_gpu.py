@@ -62,7 +62,7 @@ def _ptrs(ts):
 def test_zero_kernels_owner_map_one_gpu(chunk):
     """The exchange kernels under both owner maps, with every rank's buffer emulated in this GPU's memory (a kernel
     sees only addresses): reduce-to-owner, push all-gather, Adam, Adam + push, the gradient push to staging slots
-    and the staged owner sum, each against a PyTorch oracle."""
+    and the staged owner sum (whole segment, and over a table of owned pieces), each against a PyTorch oracle."""
     ops.set_backend("native")
     C = ops._C()
     dev = torch.device("cuda", 0)
@@ -158,6 +158,17 @@ def test_zero_kernels_owner_map_one_gpu(chunk):
     want = (acc * (1.0 / world)).to(torch.bfloat16)
     keep = own_grad.clone()
     C.reduce_compact(own_grad, staging, seg, world, rank, seg, chunk, part, 296)
+    C.sum_partials(part, sq)
+    torch.cuda.synchronize()
+    assert torch.equal(own_grad[flat_of_local], want) and torch.equal(own_grad[~mine], keep[~mine])
+    assert abs(sq.item() - want.float().pow(2).sum().item()) <= 1e-3 * max(1.0, sq.item())
+    # the same sum over a table of owned pieces (flat offset, count), as the bucketed exchange runs it after the
+    # copy engines delivered the other ranks' pieces
+    own_grad = keep.clone()
+    mine_pieces = [[o, min(step, n - o)] for o in range(0, n, step) if int(owner[o]) == rank]
+    part.zero_()
+    C.reduce_staged(own_grad, staging, torch.tensor(mine_pieces, dtype=torch.int64, device=dev), world, rank, seg,
+                    part, 64, chunk)
     C.sum_partials(part, sq)
     torch.cuda.synchronize()
     assert torch.equal(own_grad[flat_of_local], want) and torch.equal(own_grad[~mine], keep[~mine])
