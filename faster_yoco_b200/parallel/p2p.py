@@ -345,7 +345,9 @@ class PeerComm:
                 torch.zeros(0, 2, dtype=torch.int64, device=self.dev)
             self._owned_all_t = rows.contiguous()
             sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
-            self.red_ctas_all = min(2 * sms, self.bucket_part.numel())
+            # three CTAs per SM (the staged-sum kernel's register budget): it is latency-bound with fewer loads in
+            # flight
+            self.red_ctas_all = min(3 * sms, self.bucket_part.numel())
         return self._owned_all_t
 
     def start_gather(self):

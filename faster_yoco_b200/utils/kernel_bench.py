@@ -1,7 +1,7 @@
 """Per-kernel microbenchmarks: the sm_100a kernels against the library baselines (cuBLAS, flash-attn) on the
 YOCO-3B shapes, timed with CUDA events after warm-up, inputs rotated through a pool larger than L2.
 
-    python -m faster_yoco_b200.utils.kernel_bench [--only gemm|splits|fused|adam|attn|ret] [--pair 1]
+    python -m faster_yoco_b200.utils.kernel_bench [--only gemm|splits|fused|adam|staged|attn|ret] [--pair 1]
 """
 from __future__ import annotations
 
@@ -228,6 +228,32 @@ def bench_adam(results, n=1 << 30):
                     "adam8_tbs": gb / t8})
 
 
+def bench_staged(results, seg=1 << 25):
+    """The owner's staged sum (ZeRO exchange with copy-engine gradient pushes): one owner's segment of `seg` bf16
+    elements summed over its own gradient buffer and world - 1 staging slots in rank order, bf16 result written back,
+    over a table of 26 bucket pieces; world ranks emulated in local memory. Achieved bandwidth = (world reads + one
+    write) x 2 bytes x seg / CUDA-event time; inputs (>= 256 MB) exceed L2."""
+    from faster_yoco_b200 import ops
+    dev = torch.device("cuda")
+    C = ops._C()
+    for world in (2, 4, 8):
+        rank = 1
+        grad = torch.randn(world * seg, device=dev).to(torch.bfloat16)
+        staging = torch.randn(world * seg, device=dev).to(torch.bfloat16)
+        cuts = [rank * seg + (seg * k // 26) // 64 * 64 for k in range(26)] + [(rank + 1) * seg]
+        ranges = torch.tensor([[a, b - a] for a, b in zip(cuts, cuts[1:])], dtype=torch.int64, device=dev)
+        gb = (world + 1) * 2.0 * seg / 1e9
+        row = {"kernel": "reduce_staged", "world": world, "seg": seg}
+        for ctas in (296, 444, 592):
+            part = torch.zeros(ctas, device=dev)
+            t = _time(lambda: C.reduce_staged(grad, staging, ranges, world, rank, seg, part, ctas, 0), iters=10,
+                      warmup=3)
+            row[f"ctas{ctas}_ms"] = t
+            row[f"ctas{ctas}_tbs"] = gb / t
+        results.append(row)
+        del grad, staging
+
+
 def bench_attention(results, L=2048, Hq=24, Hk=8, B=1):
     from faster_yoco_b200 import ops
     dev = torch.device("cuda")
@@ -298,6 +324,8 @@ def main():
         bench_gemm_splits(res)
     if a.only == "adam":
         bench_adam(res)
+    if a.only == "staged":
+        bench_staged(res)
     if a.only in (None, "gemm", "fused"):
         bench_gemm_fused(res)
     if a.only in (None, "attn"):

@@ -201,9 +201,9 @@ def main():
         staging = torch.randn(world * seg, device=dev).to(torch.bfloat16)
         cuts = [rank * seg + (seg * k // 26) // 64 * 64 for k in range(26)] + [(rank + 1) * seg]
         ranges = torch.tensor([[a0, b0 - a0] for a0, b0 in zip(cuts, cuts[1:])], dtype=torch.int64, device=dev)
-        part = torch.zeros(296, device=dev)
+        part = torch.zeros(444, device=dev)
         for _ in range(a.reps):
-            C.reduce_staged(grad, staging, ranges, world, rank, seg, part, 296, 0)
+            C.reduce_staged(grad, staging, ranges, world, rank, seg, part, 444, 0)
     elif a.what == "gate_cumsum":
         y = torch.randn(2048, 12312, device=dev, dtype=torch.bfloat16)
         for _ in range(a.reps):
