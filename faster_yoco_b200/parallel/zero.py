@@ -37,8 +37,8 @@ CYCLIC_CHUNK = 1 << 18   # elements per chunk of the block-cyclic owner map (512
 
 # Measured exchange schedule per GPU count (YOCO-3B, 2,048 tokens per GPU, one node), used by overlap / transport
 # "auto": world -> (overlap, transport). 2 and 4 GPUs: gradients pushed by the copy engines per layer bucket during
-# backward, parameters by the fused Adam + push (2 GPUs 59.0 ms / update against 60.3 ms with copy-engine pushes of
-# both and 61.3 ms serial; 4 GPUs 57.9 against 59.5 ms serial). 8 GPUs and other counts: the serial exchange (P2P
+# backward, parameters by the fused Adam + push (2 GPUs 58.5 ms / update against 60.3 ms with copy-engine pushes of
+# both and 61.2 ms serial; 4 GPUs 57.9 against 59.5 ms serial). 8 GPUs and other counts: the serial exchange (P2P
 # reduce-to-owner after backward, then the fused Adam + push; 61.5 ms at 8 GPUs against 65.0 ms for the copy-engine
 # gradient pushes, which reach only ~210 GB/s in aggregate to 7 peers).
 AUTO_SCHEDULE = {2: ("grads", "ce"), 4: ("grads", "ce")}
