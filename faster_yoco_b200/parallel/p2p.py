@@ -31,6 +31,7 @@ epoch serves every barrier. All waits are bounded on the device (a timeout sets 
 """
 from __future__ import annotations
 
+import os
 from typing import Dict, List, Optional, Tuple
 
 import torch
@@ -229,7 +230,6 @@ class PeerComm:
         # grads "scatter": the weight-gradient GEMMs store at the owners (setup_scatter), so no bucket pushes
         # gradients; finish_reduce pushes the rest and sums (reduce_scattered)
         self.grads_mode = grads
-        import os
         reduce_ctas = int(os.environ.get("FYB_REDUCE_CTAS", reduce_ctas or 128))
         gather_ctas = int(os.environ.get("FYB_PUSH_CTAS", gather_ctas or 128))
         self.flat = flat
@@ -260,6 +260,9 @@ class PeerComm:
         self.gather_ev = [torch.cuda.Event() for _ in range(self.nb)]
         self.start_ev = torch.cuda.Event()
         self._reduced = [False] * self.nb
+        # copy-engine transport: FYB_CE_BUCKET_SUM=1 sums each bucket's staged pieces on the communication stream as
+        # soon as every peer's pieces of it have arrived (during backward) instead of all buckets after backward
+        self.ce_bucket_sum = transport == "ce" and os.environ.get("FYB_CE_BUCKET_SUM", "0") == "1"
         if transport == "ce":
             # host-side piece lists (byte offsets) and one copy stream per peer
             esz = flat.flat.element_size()
@@ -324,11 +327,24 @@ class PeerComm:
                     if owner == q:
                         self.C.peer_copy(slot + self.flat.local_of(o // esz) * esz, grad + o, c)
                 self.C.signal_peer(self.peer_garrive[q], b)
+        if self.ce_bucket_sum:
+            # this owner's part of bucket b: wait (bounded) for every peer's pieces, then sum them with its own
+            # values, which are final once the bucket's backward is
+            owned, _ = self.buckets
+            with torch.cuda.stream(self.stream):
+                self.stream.wait_event(self.ready_ev[b])
+                self.C.wait_arrivals(self.garrive, self.gexpected, b, self.world - 1)
+                self.C.reduce_staged(self.flat.grad_flat, self.staging, owned[b], self.world, self.rank,
+                                     self.flat.seg, self.bucket_part[b], self.red_ctas, self.flat.chunk)
 
     def _ce_finish_reduce(self) -> torch.Tensor:
         cur = torch.cuda.current_stream(self.dev)
         for st in self.peer_streams.values():
             cur.wait_stream(st)                    # my pushes are done (staging of peers, gradient buffer reusable)
+        if self.ce_bucket_sum:                     # every bucket was summed on the communication stream
+            cur.wait_stream(self.stream)
+            self.C.sum_partials(self.bucket_part.view(-1), self.sq)
+            return self.sq
         for b in range(self.nb):
             self.C.wait_arrivals(self.garrive, self.gexpected, b, self.world - 1)
         owned_all = self._owned_all()
