@@ -51,6 +51,19 @@ def pull_weight_ids(flat, model) -> set:
             and e.param.shape[1] % 8 == 0}
 
 
+def bucket_pieces(flat, groups, rank: int):
+    """Per bucket (parameter groups in forward order), the pieces of its parameters cut at owner boundaries:
+    (owned, other) with owned[b] = [[flat offset, count], ...] of the pieces `rank` owns (it sums them) and
+    other[b] = [[flat offset, count, owner], ...] of the pieces it sends to their owners."""
+    owned, other = [], []
+    for grp in groups:
+        ents = [flat.by_param[id(p)] for p in grp if id(p) in flat.by_param]
+        pieces = [pc for e in ents for pc in flat.owner_ranges(e)]
+        owned.append([[o, c] for o, c, r in pieces if r == rank])
+        other.append([[o, c, r] for o, c, r in pieces if r != rank])
+    return owned, other
+
+
 class PeerComm:
     NSLOTS = 64          # flag slots: 0 = generic barrier, 1..61 = reduction buckets, 63 = gather barrier
     GATHER_SLOT = 63
@@ -233,14 +246,9 @@ class PeerComm:
         reduce_ctas = int(os.environ.get("FYB_REDUCE_CTAS", reduce_ctas or 128))
         gather_ctas = int(os.environ.get("FYB_PUSH_CTAS", gather_ctas or 128))
         self.flat = flat
-        owned, other = [], []
-        for grp in groups:
-            ents = [flat.by_param[id(p)] for p in grp if id(p) in flat.by_param]
-            pieces = [pc for e in ents for pc in flat.owner_ranges(e)]
-            own = [[o, c] for o, c, r in pieces if r == self.rank]
-            oth = [[o, c, r] for o, c, r in pieces if r != self.rank]
-            owned.append(torch.tensor(own, dtype=torch.int64, device=self.dev).view(-1, 2))
-            other.append(torch.tensor(oth, dtype=torch.int64, device=self.dev).view(-1, 3))
+        own_l, oth_l = bucket_pieces(flat, groups, self.rank)
+        owned = [torch.tensor(t, dtype=torch.int64, device=self.dev).view(-1, 2) for t in own_l]
+        other = [torch.tensor(t, dtype=torch.int64, device=self.dev).view(-1, 3) for t in oth_l]
         self.buckets = (owned, other)
         self.nb = len(groups)
         # push-based parameter exchange: per-bucket arrival counters (peers add into ours) + local expectations

@@ -47,3 +47,54 @@ def test_parameter_exchange_follows_the_overlap_form():
     zero.p2p = _FakeBuckets("fused")
     zero.all_gather_params()
     assert zero.p2p.calls == ["all_gather"]
+
+
+def _model(tied=False):
+    torch.manual_seed(0)
+    return YOCO(build_args("yoco_tiny", max_seq_len=64, share_input_output_embed=tied))
+
+
+def test_param_buckets_cover_every_parameter_once():
+    """The overlap units (embedding, each layer, shared K/V projection, head) hold every trainable parameter exactly
+    once, tied weights included."""
+    for tied in (False, True):
+        model = _model(tied)
+        groups = model.param_buckets()
+        ids = [id(p) for g in groups for p in g]
+        assert len(ids) == len(set(ids))
+        assert set(ids) == {id(p) for p in model.parameters() if p.requires_grad}
+        assert groups[0] == [model.embed_tokens.weight]
+
+
+def test_bucket_pieces_partition_the_flat_buffer():
+    """Per bucket, one rank's owned pieces and the pieces it sends cover the bucket's parameters exactly once, every
+    piece lies inside one owner's range, and over all ranks every element is summed by exactly one owner."""
+    from faster_yoco_b200.parallel.p2p import bucket_pieces
+    for partition, chunk in (("even", None), ("greedy", None), ("cyclic", 512)):
+        for world in (2, 4):
+            model = _model()
+            groups = model.param_buckets()
+            fps = [FlatParams(model.named_parameters(), world, r, "cpu", dtype=torch.float32, partition=partition,
+                              chunk=chunk) for r in range(world)]
+            summed = torch.zeros(world * fps[0].seg, dtype=torch.int32)
+            for rank, fp in enumerate(fps):
+                owned, other = bucket_pieces(fp, groups, rank)
+                assert len(owned) == len(other) == len(groups)
+                for b, grp in enumerate(groups):
+                    cover = torch.zeros(world * fp.seg, dtype=torch.int32)
+                    for o, c in owned[b]:
+                        assert fp.owner_of(o) == rank and fp.owner_of(o + c - 1) == rank
+                        cover[o:o + c] += 1
+                        summed[o:o + c] += 1
+                    for o, c, q in other[b]:
+                        assert q != rank and fp.owner_of(o) == q and fp.owner_of(o + c - 1) == q
+                        cover[o:o + c] += 1
+                    want = torch.zeros_like(cover)
+                    for p in grp:
+                        e = fp.by_param[id(p)]
+                        want[e.offset:e.offset + e.numel] = 1
+                    assert torch.equal(cover, want), (partition, world, rank, b)
+            used = torch.zeros_like(summed)
+            for e in fps[0].entries:
+                used[e.offset:e.offset + e.numel] = 1
+            assert torch.equal(summed, used), (partition, world)
