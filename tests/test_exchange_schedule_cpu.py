@@ -88,6 +88,8 @@ def test_bucket_pieces_partition_the_flat_buffer():
                         summed[o:o + c] += 1
                     for o, c, q in other[b]:
                         assert q != rank and fp.owner_of(o) == q and fp.owner_of(o + c - 1) == q
+                        # a sent piece lands contiguously in the owner's staging slot (at its local offsets)
+                        assert fp.local_of(o + c - 1) - fp.local_of(o) == c - 1
                         cover[o:o + c] += 1
                     want = torch.zeros_like(cover)
                     for p in grp:
