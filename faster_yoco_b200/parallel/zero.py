@@ -49,14 +49,21 @@ def exchange_schedule(world: int, comm: str, overlap="auto", transport="auto"):
     overlap: "auto", "0" / "1" (or a bool) or "grads"; transport: "auto", "sm", "ce", "gemm" or "pull". "auto" picks
     the measured schedule of this GPU count (AUTO_SCHEDULE) for the peer-memory exchange; an explicit transport
     whose exchange is built differently (gemm, pull) keeps the serial schedule."""
+    flag = str(overlap).lower()
+    if flag not in ("auto", "grads", "0", "1", "true", "false", "yes", "no", "on", "off"):
+        raise ValueError(f"overlap must be auto, 0, 1 or grads, not {overlap!r}")
+    if transport not in ("auto", "sm", "ce", "gemm", "pull"):
+        raise ValueError(f"unknown transport {transport!r}")
     plan = AUTO_SCHEDULE.get(world) if comm == "fused" else None
-    if str(overlap) == "auto":
+    if flag == "auto":
         if plan is not None and transport in ("auto", plan[1]):
             overlap = plan[0]
         else:
             overlap = False
-    elif str(overlap) != "grads":
-        overlap = str(overlap).lower() in ("1", "true", "yes", "on")
+    elif flag == "grads":
+        overlap = "grads"
+    else:
+        overlap = flag in ("1", "true", "yes", "on")
     if transport == "auto":
         transport = plan[1] if plan is not None else "sm"
     return overlap, transport

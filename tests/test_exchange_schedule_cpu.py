@@ -1,5 +1,6 @@
 """Host logic of the exchange schedule: the measured per-GPU-count choice behind overlap / transport "auto", and
 which exchange the optimizer step runs for the parameters under each overlap form (CPU, fake peer transport)."""
+import pytest
 import torch
 
 from faster_yoco_b200.config import OptimConfig, build_args
@@ -19,6 +20,12 @@ def test_exchange_schedule_auto_and_explicit():
     assert exchange_schedule(8, "fused", "grads", "ce") == ("grads", "ce")
     assert exchange_schedule(2, "fused", "auto", "pull") == (False, "pull")   # pull carries its own all-gather
     assert exchange_schedule(2, "fused", "auto", "gemm") == (False, "gemm")
+    assert exchange_schedule(2, "fused", True, "ce") == (True, "ce")
+    for bad in ("grad", "2"):
+        with pytest.raises(ValueError):
+            exchange_schedule(2, "fused", bad)
+    with pytest.raises(ValueError):
+        exchange_schedule(2, "fused", "auto", "copy")
 
 
 class _FakeBuckets:
