@@ -107,3 +107,65 @@ def test_bucket_pieces_partition_the_flat_buffer():
             for e in fps[0].entries:
                 used[e.offset:e.offset + e.numel] = 1
             assert torch.equal(summed, used), (partition, world)
+
+
+class _RecordingPeers:
+    """Stand-in for PeerComm in the overlapped schedule on one CPU process: records the calls the trainer and the
+    model's communication hooks make; the vector all-reduce adds a second rank with the same values."""
+
+    def __init__(self, nb, params_mode):
+        self.buckets = ([None] * nb, [None] * nb)
+        self.nb = nb
+        self.params_mode = params_mode
+        self.calls = []
+
+    def start_gather(self):
+        self.calls.append(("start_gather",))
+
+    def wait_gather(self, b):
+        self.calls.append(("before", b))
+
+    def bucket_ready(self, b):
+        self.calls.append(("ready", b))
+
+    def finish_reduce(self):
+        self.calls.append(("finish_reduce",))
+        return None
+
+    def all_reduce_vector(self, v):
+        return v.reshape(-1).float() * 2
+
+    def all_gather(self, *a, **k):
+        self.calls.append(("all_gather",))
+
+
+def test_overlapped_schedule_call_order():
+    """One update of the overlapped exchange (host side): the forward waits for each bucket's parameters in forward
+    order, every bucket but the embedding reports its gradients from a hook in reverse order during backward, the
+    reduction finishes after the last report, and the parameters are exchanged after Adam only in the gradient-only
+    form (the bucketed form pushes them ahead of the next forward instead)."""
+    from faster_yoco_b200.train.trainer import Trainer
+    cfg = OptimConfig(lr=3e-4, warmup_updates=0, total_num_update=10)
+    for params_mode in ("fused", "bucketed"):
+        model = _model()
+        nb = len(model.param_buckets())
+        tr = Trainer(model, cfg, device="cpu")
+        fp = FlatParams(model.named_parameters(), 2, 0, "cpu", dtype=torch.float32)     # rank 0 of 2
+        tr.flat, tr.zero = fp, ZeroOptimizer(fp, cfg, comm="fused")
+        peers = _RecordingPeers(nb, params_mode)
+        tr.zero.p2p, tr.overlap, tr.world, tr.check_consistency = peers, True, 2, False
+        ids = torch.randint(0, 1024, (2, 65), generator=torch.Generator().manual_seed(0))
+        loss = tr.train_step({"src_tokens": ids[:, :-1].contiguous(), "target": ids[:, 1:].contiguous(),
+                              "ntokens": 128, "nsentences": 2})
+        assert torch.isfinite(loss)
+        calls = peers.calls
+        assert calls[0] == ("start_gather",)
+        before = [c[1] for c in calls if c[0] == "before"]
+        ready = [c[1] for c in calls if c[0] == "ready"]
+        assert before == list(range(nb))
+        assert ready == list(range(nb - 1, 0, -1))          # the head first; the embedding (bucket 0) has no hook
+        fin = calls.index(("finish_reduce",))
+        assert fin > max(i for i, c in enumerate(calls) if c[0] == "ready")
+        gathers = [i for i, c in enumerate(calls) if c == ("all_gather",)]
+        assert gathers == ([len(calls) - 1] if params_mode == "fused" else [])
+        assert gathers == [] or gathers[0] > fin
