@@ -198,7 +198,7 @@ def result_line(args, world: int, ms: float, clocks, e2e, launches, exposed=None
                    "cuda_graph": bool(args.graph),
                    "comm_overlap": args.overlap if args.overlap == "grads" else bool(int(args.overlap)),
                    "zero_partition": args.partition,
-                   "transport": (args.transport if (args.overlap or args.transport == "gemm") else None)
+                   "transport": (args.transport if (args.overlap or args.transport in ("gemm", "pull")) else "serial")
                    if world > 1 else None,
                    "l2": "working set (>=55 GB of params/grads/Adam state per update) >> 126 MB L2"},
         "clocks": clocks, "e2e": e2e, "gpu_launches": launches,

@@ -249,6 +249,9 @@ def test_bench_result_line_contract(monkeypatch):
     one = bench.result_line(args, 1, 70.0, clocks, e2e, 8000)             # N = 1: per GPU vs per GPU
     assert abs(one["vs_baseline"] - one["value"] / (138983.0 / 8)) < 1e-9
     assert one["config"]["comm"] == "none" and one["config"]["transport"] is None
+    assert line["config"]["transport"] == "serial"                         # N = 8, no overlap: the serial exchange
+    args.transport = "pull"
+    assert bench.result_line(args, 8, 70.0, clocks, e2e, 8000)["config"]["transport"] == "pull"
     for k in ("model", "global_batch", "seq_len", "parallelism", "l2"):
         assert k in line["config"], k
     assert line["config"]["model"] == "yoco_3b" and line["config"]["global_batch"] == 8
